@@ -1,0 +1,16 @@
+"""CPU oracle for LSRM's variable-block native sparse attention.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the shipped package imports this
+directory: only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` use it, and only
+as the checker or as the timed CPU restatement of the reference.
+
+Parity status: pinned.  ``tests/golden/make_golden.py`` runs the reference's
+own code (``sparse.ops.get_block_score``, ``SparseResBlock``,
+``torch.segment_reduce``, ``SpatialSparseAttentionOut`` and the Triton
+``native_sparse_attend`` under ``TRITON_INTERPRET=1`` in fp16) and stores its
+outputs as fixtures; ``tests/test_oracle_golden.py`` checks this oracle
+against them.
+"""
+
+from .nsa_oracle import *  # noqa: F401,F403

@@ -1,0 +1,577 @@
+"""CPU restatement of LSRM's variable-block native sparse attention.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``): never imported by the
+shipped package.  Floating-point math runs in float64 torch on the CPU unless
+a function says otherwise; the block scorer runs in numpy float32 with a fixed
+operation order so that its indices can be compared bit for bit with the CUDA
+scorer.
+
+Every function cites the reference lines it restates (paths are relative to
+the root of chenxiex/Large-Sparse-Reconstruction-Model).
+
+Selection semantics shared by every function here and by the CUDA kernels:
+
+* ``block_topk[h, i, :]`` holds sequence-local block ids.  An entry is valid
+  when ``0 <= id < blocks_in_sequence``; other entries (the reference pads with
+  ``-1`` at the tail) are ignored.  For tail padding this is exactly the
+  reference's ``valid_sel_count`` rule
+  (sparse/ops/triton_native_sparse_attention_impl_kvcentric.py:151-166).
+* A block listed twice is attended twice (multiplicity weight), as the
+  reference's loops do (kvcentric.py:166-226 forward, :494-572 reverse map).
+* A query with no valid block gets a NaN output row and ``-inf`` LSE
+  (0/0 at kvcentric.py:229).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+LOG2E = 1.44269504  # the constant the reference uses (block_score.py:59-60)
+
+__all__ = [
+    "LOG2E",
+    "segment_mean",
+    "res_block",
+    "compress_kv",
+    "selection_attention",
+    "compressed_attention",
+    "window_attention_intra_block",
+    "sliding_window_attention",
+    "gate_merge",
+    "exp2_fixed",
+    "token_block_scores_exact",
+    "get_block_score_exact",
+    "get_block_score_qblock_exact",
+    "block_score_reference_formula",
+    "build_query_tiles",
+    "build_tile_unions",
+    "selection_flops",
+    "dense_attention_flops",
+]
+
+
+def _i(x) -> List[int]:
+    return [int(v) for v in torch.as_tensor(x).reshape(-1).tolist()]
+
+
+# ---------------------------------------------------------------------------
+# Compression (SpatialSparseAttentionIn)
+# ---------------------------------------------------------------------------
+
+
+def segment_mean(x: torch.Tensor, cu: torch.Tensor) -> torch.Tensor:
+    """Mean of ``x`` rows over each segment ``[cu[b], cu[b+1])``.
+
+    Restates ``torch.segment_reduce(reduce="mean")`` as used at
+    sparse/module/spatial_sparse_attention.py:27-37.  Empty segments give NaN,
+    as ``segment_reduce`` does.
+    """
+    xs = x.to(torch.float64)
+    offs = _i(cu)
+    out = torch.empty((len(offs) - 1,) + tuple(xs.shape[1:]), dtype=torch.float64)
+    for b in range(len(offs) - 1):
+        s, e = offs[b], offs[b + 1]
+        out[b] = xs[s:e].mean(dim=0) if e > s else float("nan")
+    return out
+
+
+def res_block(x, w1, b1, w2, b2, eps: float = 1e-5) -> torch.Tensor:
+    """``SparseResBlock``: LN_fp32(x + W2·SiLU(W1·x + b1) + b2), no affine.
+
+    Restates sparse/module/residual_block.py:11-34 (LayerNorm32 with
+    ``elementwise_affine=False`` and the default eps 1e-5).
+    """
+    xd = x.to(torch.float64)
+    h = torch.nn.functional.linear(xd, w1.double(), b1.double())
+    h = torch.nn.functional.silu(h)
+    h = torch.nn.functional.linear(h, w2.double(), b2.double())
+    y = xd + h
+    return torch.nn.functional.layer_norm(y, (y.shape[-1],), eps=eps)
+
+
+def compress_kv(x, cu_block_include_tokens, weights=None) -> torch.Tensor:
+    """One branch of ``SpatialSparseAttentionIn.forward``.
+
+    spatial_sparse_attention.py:46-66: the ResBlock runs token-wise, then the
+    block mean.  ``weights=None`` is the pure block-mean compression.
+    """
+    if weights is not None:
+        x = res_block(x, *weights)
+    return segment_mean(x, cu_block_include_tokens)
+
+
+# ---------------------------------------------------------------------------
+# Attention branches
+# ---------------------------------------------------------------------------
+
+
+def _block_counts(block_topk_h: torch.Tensor, nb: int) -> torch.Tensor:
+    """[nq, k] sequence-local ids -> [nq, nb] multiplicity counts (valid ids)."""
+    sel = block_topk_h.long()
+    valid = (sel >= 0) & (sel < nb)
+    counts = torch.zeros(sel.shape[0], max(nb, 1), dtype=torch.float64)
+    if nb > 0:
+        counts.scatter_add_(1, sel.clamp(0, nb - 1), valid.to(torch.float64))
+    return counts[:, :nb]
+
+
+def _masked_softmax_attend(qh, kh, vh, log_weight, scale):
+    """o = softmax(scale·q·kᵀ + log_weight)·v, lse (natural log)."""
+    logits = (qh @ kh.transpose(0, 1)) * scale + log_weight
+    lse = torch.logsumexp(logits, dim=-1)
+    p = torch.softmax(logits, dim=-1)
+    return p @ vh, lse
+
+
+def selection_attention(
+    q,
+    k,
+    v,
+    block_topk,
+    cu_seqblocks,
+    cu_block_include_tokens,
+    cu_seqlens_q,
+    cu_seqlens_k,
+    softmax_scale: Optional[float] = None,
+    dtype=torch.float64,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Selected-block attention forward; returns ``(o, lse_log2)``.
+
+    Restates ``forward_kernel_varblock``
+    (sparse/ops/triton_native_sparse_attention_impl_kvcentric.py:55-247):
+    query ``i`` of sequence ``b`` attends to the union (with multiplicity) of
+    the token ranges ``cu_block_include_tokens[cu_seqblocks[b] + id]`` of its
+    valid selected blocks, keys restricted to ``[cu_seqlens_k[b],
+    cu_seqlens_k[b+1])`` (the ``c + tile + offs_n < seqlen_k`` mask, :181).
+    LSE is returned in log2 units, ``[Hq, Nq]`` (:240-245).  Differentiable
+    when the inputs require grad (the backward of the same formula is what
+    kvcentric.py:262-478 and :687-923 compute).
+    """
+    Nq, Hq, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    qd, kd, vd = q.to(dtype), k.to(dtype), v.to(dtype)
+    cq, ck, cs, cb = _i(cu_seqlens_q), _i(cu_seqlens_k), _i(cu_seqblocks), _i(cu_block_include_tokens)
+    outs = []
+    lses = []
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], ck[b], ck[b + 1]
+        bs, be = cs[b], cs[b + 1]
+        nb = be - bs
+        # key token -> sequence-local block id (tokens outside any block: -1)
+        key_block = torch.full((ke - ks,), -1, dtype=torch.long)
+        for j in range(nb):
+            t0, t1 = cb[bs + j], cb[bs + j + 1]
+            lo, hi = max(t0, ks), min(t1, ke)
+            if hi > lo:
+                key_block[lo - ks : hi - ks] = j
+        o_seq = []
+        l_seq = []
+        for hq in range(Hq):
+            h = hq // G
+            cnt = _block_counts(block_topk[h, qs:qe], nb)  # [nq, nb]
+            if ke > ks:
+                w = torch.zeros(qe - qs, ke - ks, dtype=torch.float64)
+                inb = key_block >= 0
+                w[:, inb] = cnt[:, key_block[inb]]
+            else:
+                w = torch.zeros(qe - qs, 0, dtype=torch.float64)
+            logw = torch.where(w > 0, w.log(), torch.full_like(w, -math.inf)).to(dtype)
+            empty = (w > 0).sum(dim=1) == 0  # rows with no attended key
+            logw = torch.where(empty[:, None], torch.zeros_like(logw), logw)
+            o_h, lse_h = _masked_softmax_attend(
+                qd[qs:qe, hq], kd[ks:ke, h], vd[ks:ke, h], logw, scale
+            )
+            # 0/0 in the reference: NaN output, -inf LSE, no gradient path
+            o_h = torch.where(empty[:, None], torch.full_like(o_h, math.nan), o_h)
+            lse_h = torch.where(empty, torch.full_like(lse_h, -math.inf), lse_h)
+            if ke == ks:
+                o_h = torch.full((qe - qs, D), math.nan, dtype=dtype)
+                lse_h = torch.full((qe - qs,), -math.inf, dtype=dtype)
+            o_seq.append(o_h)
+            l_seq.append(lse_h / math.log(2.0))
+        if qe > qs:
+            outs.append(torch.stack(o_seq, dim=1))
+            lses.append(torch.stack(l_seq, dim=0))
+    o = torch.cat(outs, 0) if outs else torch.zeros(0, Hq, D, dtype=dtype)
+    lse = torch.cat(lses, 1) if lses else torch.zeros(Hq, 0, dtype=dtype)
+    return o, lse
+
+
+def compressed_attention(
+    q, ck, cv, cu_seqlens_q, cu_seqblocks, softmax_scale=None, dtype=torch.float64
+):
+    """Compressed branch: every query attends to all compressed blocks of its
+    sequence.  Returns ``(o, lse_ln)`` with the natural-log LSE ``[Hq, Nq]``.
+
+    Restates the ``flash_attn_varlen_func(q, compressed_k, compressed_v,
+    cu_seqlens_q, compressed_cu_seqlens, ..., causal=False,
+    return_attn_probs=True)`` call at spatial_sparse_attention.py:121-143.
+    """
+    Nq, Hq, D = q.shape
+    Hkv = ck.shape[1]
+    G = Hq // Hkv
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    qd, kd, vd = q.to(dtype), ck.to(dtype), cv.to(dtype)
+    cq, cs = _i(cu_seqlens_q), _i(cu_seqblocks)
+    outs, lses = [], []
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], cs[b], cs[b + 1]
+        if qe == qs:
+            continue
+        o_seq, l_seq = [], []
+        for hq in range(Hq):
+            h = hq // G
+            zero = torch.zeros(qe - qs, ke - ks, dtype=dtype)
+            o_h, l_h = _masked_softmax_attend(qd[qs:qe, hq], kd[ks:ke, h], vd[ks:ke, h], zero, scale)
+            o_seq.append(o_h)
+            l_seq.append(l_h)
+        outs.append(torch.stack(o_seq, 1))
+        lses.append(torch.stack(l_seq, 0))
+    o = torch.cat(outs, 0) if outs else torch.zeros(0, Hq, D, dtype=dtype)
+    lse = torch.cat(lses, 1) if lses else torch.zeros(Hq, 0, dtype=dtype)
+    return o, lse
+
+
+def _dense_segments_attention(q, k, v, segments, scale, band=None, dtype=torch.float64):
+    Nq, Hq, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    qd, kd, vd = q.to(dtype), k.to(dtype), v.to(dtype)
+    out = torch.zeros(Nq, Hq, D, dtype=dtype)
+    rows = []
+    for (s, e) in segments:
+        if e <= s:
+            continue
+        idx = torch.arange(s, e)
+        logw = torch.zeros(e - s, e - s, dtype=dtype)
+        if band is not None:
+            dist = (idx[:, None] - idx[None, :]).abs()
+            logw = torch.where(dist <= band, logw, torch.full_like(logw, -math.inf))
+        o_seg = []
+        for hq in range(Hq):
+            h = hq // G
+            o_h, _ = _masked_softmax_attend(qd[s:e, hq], kd[s:e, h], vd[s:e, h], logw, scale)
+            o_seg.append(o_h)
+        rows.append((s, e, torch.stack(o_seg, 1)))
+    for s, e, o in rows:
+        out = out.index_copy(0, torch.arange(s, e), o)
+    return out
+
+
+def window_attention_intra_block(q, k, v, cu_block_include_tokens, softmax_scale=None, dtype=torch.float64):
+    """Reference window branch: full attention inside each variable block.
+
+    Restates ``sparse_window_attention`` (sparse/ops/block_window_attention.py:
+    14-31), i.e. ``flash_attn_varlen_func`` with ``cu_seqlens_q = cu_seqlens_k
+    = cu_block_include_tokens`` and the default scale 1/sqrt(d).
+    """
+    D = q.shape[-1]
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    cb = _i(cu_block_include_tokens)
+    return _dense_segments_attention(q, k, v, list(zip(cb[:-1], cb[1:])), scale, dtype=dtype)
+
+
+def sliding_window_attention(q, k, v, cu_seqlens, window: int, softmax_scale=None, dtype=torch.float64):
+    """Extension (not in the reference): band attention ``|i - j| <= window // 2``
+    inside each sequence, in token (Morton) order."""
+    D = q.shape[-1]
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    cs = _i(cu_seqlens)
+    return _dense_segments_attention(q, k, v, list(zip(cs[:-1], cs[1:])), scale, band=window // 2, dtype=dtype)
+
+
+def gate_merge(x, gate_weight, branches: Sequence[torch.Tensor], mode: str = "per_channel", num_heads: int = 1):
+    """Sigmoid-gated merge of the attention branches.
+
+    ``per_channel`` restates ``SpatialSparseAttentionOut.forward``
+    (spatial_sparse_attention.py:215-224, 257-269): ``g = sigmoid(x·Wgᵀ)`` with
+    ``Wg`` of shape ``[n·C, C]`` and ``out = Σ g[:, i·C:(i+1)·C] ⊙ branch_i``
+    (branch order: compressed, selection, window).  ``per_head`` is the
+    extension where ``Wg`` is ``[n·H, hidden]`` and each gate value is
+    broadcast over the ``head_dim`` channels of its head.
+    """
+    g = torch.sigmoid(x.double() @ gate_weight.double().t())
+    out = 0
+    n = len(branches)
+    C = branches[0].shape[-1]
+    for i, br in enumerate(branches):
+        if mode == "per_channel":
+            gi = g[:, i * C : (i + 1) * C]
+        else:
+            d = C // num_heads
+            gi = g[:, i * num_heads : (i + 1) * num_heads].repeat_interleave(d, dim=1)
+        out = out + gi * br.double()
+    assert g.shape[1] == (n * C if mode == "per_channel" else n * num_heads)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Block scoring + top-k with a fixed float32 operation order (bit-exact)
+# ---------------------------------------------------------------------------
+
+_F32 = np.float32
+# Taylor coefficients of 2^f = exp(f·ln2) around 0, rounded to float32.
+_EXP2_COEF = [_F32(math.log(2.0) ** i / math.factorial(i)) for i in range(8)]
+
+
+def exp2_fixed(t: np.ndarray) -> np.ndarray:
+    """2^t in float32 with a fixed, portable operation order.
+
+    Range reduction ``n = rint(t)``, ``f = t - n`` (exact), degree-7 Taylor
+    polynomial of ``exp(f ln 2)`` by Horner's rule with separately rounded
+    multiplies and adds, then an exact scale by ``2^n``.  ``t < -125.5`` flushes
+    to 0 (no subnormals), ``t >= 127.5`` gives inf.  The CUDA scorer evaluates
+    the same sequence with ``__fmul_rn``/``__fadd_rn``, so both sides agree bit
+    for bit.
+    """
+    t = np.asarray(t, dtype=_F32)
+    n = np.rint(t)
+    f = (t - n).astype(_F32)
+    r = np.full_like(f, _EXP2_COEF[7])
+    for c in _EXP2_COEF[6::-1]:
+        r = (r * f).astype(_F32)
+        r = (r + c).astype(_F32)
+    n_cl = np.clip(n, -125, 127).astype(np.int32)
+    scale = ((n_cl + 127).astype(np.uint32) << np.uint32(23)).view(_F32)
+    with np.errstate(over="ignore"):
+        out = (r * scale).astype(_F32)
+    out = np.where(n < -125, _F32(0.0), out)
+    out = np.where(n > 127, _F32(np.inf), out)
+    return out.astype(_F32)
+
+
+def _to_f32_np(x) -> np.ndarray:
+    return torch.as_tensor(x).detach().to(torch.float32).cpu().numpy()
+
+
+def token_block_scores_exact(q, ck, lse_ln, cu_seqlens_q, compressed_cu_seqlens, sm_scale=None):
+    """Per-token block scores in fixed-order float32.
+
+    score[h, i, b] = Σ_{g<G} exp2_fixed(dot(q[i, hG+g], ck[b, h]) · qk_scale
+    − lse[hG+g, i]·1.44269504), where ``dot`` accumulates the products in
+    ascending channel order with separately rounded multiply and add, and
+    ``qk_scale = float32(sm_scale · 1.44269504)``.  This is the arithmetic of
+    ``get_block_score`` (sparse/ops/block_score.py:57-92) with its summation
+    order fixed.  Returns a list (one entry per sequence) of ``[Hkv, nq, nb]``
+    float32 arrays.
+    """
+    qn = _to_f32_np(q)
+    cn = _to_f32_np(ck)
+    ln = _to_f32_np(lse_ln)
+    Nq, Hq, D = qn.shape
+    Hkv = cn.shape[1]
+    G = Hq // Hkv
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    qk_scale = _F32(sm_scale * LOG2E)
+    lse2 = (ln * _F32(LOG2E)).astype(_F32)
+    cq, cc = _i(cu_seqlens_q), _i(compressed_cu_seqlens)
+    res = []
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], cc[b], cc[b + 1]
+        sc = np.zeros((Hkv, qe - qs, ke - ks), dtype=_F32)
+        for h in range(Hkv):
+            for g in range(G):
+                hq = h * G + g
+                qh = qn[qs:qe, hq, :]
+                kh = cn[ks:ke, h, :]
+                acc = np.zeros((qe - qs, ke - ks), dtype=_F32)
+                for j in range(D):
+                    acc = (acc + (qh[:, j : j + 1] * kh[None, :, j]).astype(_F32)).astype(_F32)
+                t = ((acc * qk_scale).astype(_F32) - lse2[hq, qs:qe, None]).astype(_F32)
+                sc[h] = (sc[h] + exp2_fixed(t)).astype(_F32)
+        res.append(sc)
+    return res
+
+
+def _topk_lowest_id(scores: np.ndarray, k: int, force: Optional[np.ndarray] = None) -> np.ndarray:
+    """Rows of ``scores`` [n, nb] -> ascending ids of the k best blocks.
+
+    Order: larger score first, ties broken by the lower block id; then the
+    chosen ids are sorted ascending and padded with -1 (block_score.py:85-96).
+    ``force[i]`` (optional) is a block id that is always selected first.
+    """
+    n, nb = scores.shape
+    out = np.full((n, k), -1, dtype=np.int32)
+    kk = min(k, nb)
+    if kk == 0:
+        return out
+    ids = np.arange(nb)
+    for i in range(n):
+        s = scores[i].astype(np.float64)
+        chosen = []
+        if force is not None and 0 <= force[i] < nb:
+            chosen.append(int(force[i]))
+        order = np.lexsort((ids, -s))  # primary: -score, secondary: id
+        for b in order:
+            if len(chosen) >= kk:
+                break
+            if force is not None and b == force[i]:
+                continue
+            chosen.append(int(b))
+        out[i, :kk] = np.sort(np.array(chosen, dtype=np.int32))
+    return out
+
+
+def get_block_score_exact(q, compressed_k, lse, topk, cu_seqlens_q, compressed_cu_seqlens, sm_scale=None):
+    """Bit-exact restatement of ``get_block_score`` (block_score.py:16-98).
+
+    Returns ``[Hkv, Nq, topk]`` int32 of sequence-local block ids, ascending,
+    ``-1``-padded when a sequence has fewer than ``topk`` blocks.  Ties go to
+    the lowest block id.
+    """
+    Hkv = compressed_k.shape[1]
+    Nq = q.shape[0]
+    out = np.full((Hkv, Nq, topk), -1, dtype=np.int32)
+    scores = token_block_scores_exact(q, compressed_k, lse, cu_seqlens_q, compressed_cu_seqlens, sm_scale)
+    cq = _i(cu_seqlens_q)
+    for b, sc in enumerate(scores):
+        for h in range(Hkv):
+            out[h, cq[b] : cq[b + 1]] = _topk_lowest_id(sc[h], topk)
+    return torch.from_numpy(out)
+
+
+def get_block_score_qblock_exact(
+    q, compressed_k, lse, topk, cu_seqlens_q, compressed_cu_seqlens, cu_qblocks, sm_scale=None, force_self=False
+):
+    """Extension: one selection per query block.
+
+    The score of block ``b`` for query block ``Q`` is the float32 sum, in
+    ascending token order, of the per-token scores of
+    ``token_block_scores_exact``.  ``cu_qblocks`` are global token offsets of
+    the query blocks (each lies inside one sequence).  With ``force_self`` the
+    query block's own index (sequence-local, query block ``j`` of a sequence
+    maps to KV block ``j``) is always selected.  Returns ``[Hkv, n_qblocks,
+    topk]`` int32.
+    """
+    Hkv = compressed_k.shape[1]
+    cqb = _i(cu_qblocks)
+    nqb = len(cqb) - 1
+    out = np.full((Hkv, nqb, topk), -1, dtype=np.int32)
+    scores = token_block_scores_exact(q, compressed_k, lse, cu_seqlens_q, compressed_cu_seqlens, sm_scale)
+    cq = _i(cu_seqlens_q)
+    qb = 0
+    for b, sc in enumerate(scores):
+        qs, qe = cq[b], cq[b + 1]
+        first = qb
+        rows = []
+        while qb < nqb and cqb[qb] < qe:
+            rows.append((cqb[qb] - qs, cqb[qb + 1] - qs))
+            qb += 1
+        for h in range(Hkv):
+            agg = np.zeros((len(rows), sc.shape[2]), dtype=_F32)
+            for r, (s, e) in enumerate(rows):
+                acc = np.zeros(sc.shape[2], dtype=_F32)
+                for t in range(s, e):
+                    acc = (acc + sc[h, t]).astype(_F32)
+                agg[r] = acc
+            force = np.arange(len(rows)) if force_self else None
+            out[h, first : first + len(rows)] = _topk_lowest_id(agg, topk, force)
+    return torch.from_numpy(out)
+
+
+def block_score_reference_formula(q, compressed_k, lse, cu_seqlens_q, compressed_cu_seqlens, sm_scale=None):
+    """float64 scores of block_score.py:57-92 (for tolerance checks only)."""
+    Nq, Hq, D = q.shape
+    Hkv = compressed_k.shape[1]
+    G = Hq // Hkv
+    sm_scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(D)
+    cq, cc = _i(cu_seqlens_q), _i(compressed_cu_seqlens)
+    res = []
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], cc[b], cc[b + 1]
+        sc = torch.zeros(Hkv, qe - qs, ke - ks, dtype=torch.float64)
+        for h in range(Hkv):
+            ckh = compressed_k[ks:ke, h].double()
+            for g in range(G):
+                hq = h * G + g
+                qk = (q[qs:qe, hq].double() @ ckh.t()) * sm_scale * LOG2E
+                sc[h] += torch.exp2(qk - lse[hq, qs:qe, None].double() * LOG2E)
+        res.append(sc)
+    return res
+
+
+# ---------------------------------------------------------------------------
+# Work decomposition (restated so that the CUDA builders can be checked)
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class QueryTile:
+    seq: int
+    q_start: int  # global query index of the first query
+    n_q: int  # queries in the tile (<= rows // G)
+
+
+def build_query_tiles(cu_seqlens_q, queries_per_tile: int, cu_qblocks=None) -> List[QueryTile]:
+    """Split each sequence's queries into tiles of ``queries_per_tile``.
+
+    With ``cu_qblocks`` (global offsets of query blocks) no tile straddles a
+    query-block boundary.
+    """
+    cq = _i(cu_seqlens_q)
+    cuts = set(_i(cu_qblocks)) if cu_qblocks is not None else set()
+    tiles = []
+    for b in range(len(cq) - 1):
+        s, e = cq[b], cq[b + 1]
+        i = s
+        while i < e:
+            j = min(i + queries_per_tile, e)
+            if cuts:
+                nxt = [c for c in cuts if i < c < j]
+                if nxt:
+                    j = min(nxt)
+            tiles.append(QueryTile(b, i, j - i))
+            i = j
+    return tiles
+
+
+def build_tile_unions(block_topk_h: torch.Tensor, tiles: List[QueryTile], cu_seqblocks) -> List[Tuple[List[int], List[int]]]:
+    """For each tile: ascending unique valid sequence-local block ids and,
+    per id, the bitmask of tile queries that selected it."""
+    cs = _i(cu_seqblocks)
+    out = []
+    for t in tiles:
+        nb = cs[t.seq + 1] - cs[t.seq]
+        masks = {}
+        for r in range(t.n_q):
+            for e in _i(block_topk_h[t.q_start + r]):
+                if 0 <= e < nb:
+                    masks[e] = masks.get(e, 0) | (1 << r)
+        ids = sorted(masks)
+        out.append((ids, [masks[i] for i in ids]))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic FLOP accounting (valid pairs only)
+# ---------------------------------------------------------------------------
+
+
+def selection_flops(block_topk, cu_seqblocks, cu_block_include_tokens, cu_seqlens_q, num_q_heads, head_dim) -> float:
+    """4·d per (query head, attended key) for the forward pass.  Keys are
+    counted with multiplicity, as the reference attends them."""
+    G = num_q_heads // block_topk.shape[0]
+    cs, cb, cq = _i(cu_seqblocks), _i(cu_block_include_tokens), _i(cu_seqlens_q)
+    lens = np.diff(np.array(cb, dtype=np.int64))
+    total = 0
+    bt = block_topk.numpy() if isinstance(block_topk, torch.Tensor) else block_topk
+    for b in range(len(cq) - 1):
+        nb = cs[b + 1] - cs[b]
+        sel = bt[:, cq[b] : cq[b + 1]].astype(np.int64)
+        valid = (sel >= 0) & (sel < nb)
+        seg = lens[cs[b] : cs[b + 1]]
+        if nb:
+            total += int(np.where(valid, seg[np.clip(sel, 0, nb - 1)], 0).sum())
+    return 4.0 * head_dim * G * total
+
+
+def dense_attention_flops(pairs: int, num_q_heads: int, head_dim: int) -> float:
+    return 4.0 * head_dim * num_q_heads * pairs

@@ -1,0 +1,215 @@
+"""Generate golden fixtures by running the REFERENCE implementation on the CPU.
+
+Run once in a container that holds the reference checkout (read-only is fine):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --ref /path/to/reference
+
+What runs, all unmodified reference code:
+
+* ``native_sparse_attend`` (sparse/ops/triton_native_sparse_attention_impl_kvcentric.py
+  :1382-1435) through ``TRITON_INTERPRET=1``, forward (output, log2 LSE) and
+  backward (dQ, dK, dV).  fp16 only: the interpreter mis-computes bf16.
+* ``get_block_score`` (sparse/ops/block_score.py:16-98), fp32.
+* ``SpatialSparseAttentionIn`` (ResBlock compression + segment mean,
+  sparse/module/spatial_sparse_attention.py:16-67) with its own random init.
+* ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
+  without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
+  for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
+  plain restatement of flash-attn's varlen contract); the gate math that the
+  fixture pins is the reference's.
+
+Fixtures are small ``.npz`` files next to this script.  Nothing at test time
+reads the reference checkout.
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _cpu_varlen_attention(q, k, v, cu_q, cu_k, max_q, max_k, dropout_p=0.0, softmax_scale=None,
+                          causal=False, return_attn_probs=False, **_):
+    """flash_attn_varlen_func contract on the CPU: per-sequence softmax
+    attention, GQA by head grouping, natural-log LSE ``[Hq, total_q]``."""
+    assert not causal
+    Hq, Hkv, D = q.shape[1], k.shape[1], q.shape[2]
+    G = Hq // Hkv
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    out = torch.zeros_like(q, dtype=torch.float32)
+    lse = torch.zeros(Hq, q.shape[0], dtype=torch.float32)
+    cq, ck = cu_q.tolist(), cu_k.tolist()
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], ck[b], ck[b + 1]
+        for h in range(Hq):
+            s = (q[qs:qe, h].float() @ k[ks:ke, h // G].float().t()) * scale
+            lse[h, qs:qe] = torch.logsumexp(s, -1)
+            out[qs:qe, h] = torch.softmax(s, -1) @ v[ks:ke, h // G].float()
+    out = out.to(q.dtype)
+    if return_attn_probs:
+        return out, lse, None
+    return out
+
+
+def _blocks(lengths):
+    return torch.tensor([0] + list(np.cumsum(lengths)), dtype=torch.int32)
+
+
+def _unique_topk(gen, n, nb, k, pad_tail=0):
+    """[n, k] ascending unique ids in [0, nb); the last ``pad_tail`` of every
+    row replaced by -1 (the reference's tail padding)."""
+    rows = []
+    kk = min(k, nb)
+    for _ in range(n):
+        sel = torch.randperm(nb, generator=gen)[:kk].sort().values
+        row = torch.full((k,), -1, dtype=torch.int32)
+        row[:kk] = sel.to(torch.int32)
+        if pad_tail:
+            row[kk - pad_tail:kk] = -1
+        rows.append(row)
+    return torch.stack(rows)
+
+
+def selection_cases():
+    """(name, seq_block_lengths, Hq, Hkv, D, k, special)."""
+    return [
+        ("sel_g2_d32", [[7, 8, 5, 13, 7]], 4, 2, 32, 3, None),
+        ("sel_mha_d64_2seq_pad", [[20, 33, 12, 9], [40, 16]], 2, 2, 64, 3, "pad"),
+        ("sel_g2_long_blocks", [[150, 70, 5]], 2, 1, 32, 2, None),
+        ("sel_dup_and_empty", [[10, 0, 12, 9, 17]], 2, 1, 32, 3, "dup_empty"),
+        ("sel_g4_d64", [[16, 24, 8, 40, 12, 28]], 8, 2, 64, 4, None),
+    ]
+
+
+def make_selection(native_sparse_attend, name, seq_blocks, Hq, Hkv, D, k, special, seed):
+    gen = torch.Generator().manual_seed(seed)
+    lens = [l for s in seq_blocks for l in s]
+    cu_blk = _blocks(lens)
+    cu_seqblocks = _blocks([len(s) for s in seq_blocks])
+    cu_seqlens = _blocks([sum(s) for s in seq_blocks])
+    N = int(cu_seqlens[-1])
+    q = (torch.randn(N, Hq, D, generator=gen) * 0.5).half()
+    kk = (torch.randn(N, Hkv, D, generator=gen) * 0.5).half()
+    v = (torch.randn(N, Hkv, D, generator=gen) * 0.5).half()
+    do = (torch.randn(N, Hq, D, generator=gen) * 0.1).half()
+    topk = torch.full((Hkv, N, k), -1, dtype=torch.int32)
+    for b, blocks in enumerate(seq_blocks):
+        qs, qe = int(cu_seqlens[b]), int(cu_seqlens[b + 1])
+        for h in range(Hkv):
+            topk[h, qs:qe] = _unique_topk(gen, qe - qs, len(blocks), k, pad_tail=1 if special == "pad" and b == 1 else 0)
+    if special == "dup_empty":
+        # a duplicated block id (attended twice) and a row with no selection
+        topk[0, 3] = torch.tensor([2, 2, 4], dtype=torch.int32)
+        topk[0, 5] = torch.tensor([1, 1, -1], dtype=torch.int32)  # block 1 is empty
+        topk[0, 7] = torch.tensor([-1, -1, -1], dtype=torch.int32)
+    qr, kr, vr = (t.clone().requires_grad_() for t in (q, kk, v))
+    o, lse = native_sparse_attend(qr, kr, vr, topk, cu_seqblocks, cu_blk, cu_seqlens, cu_seqlens, return_lse=True)
+    o.backward(do)
+    return dict(
+        q=q.float().numpy(), k=kk.float().numpy(), v=v.float().numpy(), do=do.float().numpy(),
+        block_topk=topk.numpy(), cu_seqblocks=cu_seqblocks.numpy(), cu_block_include_tokens=cu_blk.numpy(),
+        cu_seqlens=cu_seqlens.numpy(), o=o.detach().float().numpy(), lse_log2=lse.detach().float().numpy(),
+        dq=qr.grad.float().numpy(), dk=kr.grad.float().numpy(), dv=vr.grad.float().numpy(),
+        dtype=np.array("float16"),
+    )
+
+
+def make_block_score(get_block_score, seed, seq_q, seq_nb, Hq, Hkv, D, topk):
+    gen = torch.Generator().manual_seed(seed)
+    cu_q = _blocks(seq_q)
+    cu_c = _blocks(seq_nb)
+    N, NB = int(cu_q[-1]), int(cu_c[-1])
+    q = torch.randn(N, Hq, D, generator=gen).bfloat16().float()
+    ck = torch.randn(NB, Hkv, D, generator=gen).bfloat16().float()
+    # a consistent LSE: the compressed attention's own natural-log LSE
+    _, lse, _ = _cpu_varlen_attention(q, ck, ck, cu_q, cu_c, 0, 0, return_attn_probs=True)
+    out = get_block_score(q, ck, lse, topk, cu_q, cu_c, cu_q[1:] - cu_q[:-1], cu_c[1:] - cu_c[:-1], None)
+    return dict(q=q.numpy(), ck=ck.numpy(), lse=lse.numpy(), cu_seqlens_q=cu_q.numpy(),
+                compressed_cu_seqlens=cu_c.numpy(), topk=np.array(topk), block_topk=out.numpy())
+
+
+def make_compress(SpatialSparseAttentionIn, seed):
+    torch.manual_seed(seed)
+    D, Hkv = 32, 2
+    mod = SpatialSparseAttentionIn(head_dim=D, num_kv_heads=Hkv)
+    lens = [5, 9, 1, 14, 3, 8]
+    cu = _blocks(lens)
+    N = int(cu[-1])
+    k = torch.randn(N, Hkv * D)
+    v = torch.randn(N, Hkv * D)
+    with torch.no_grad():
+        ck, cv = mod(k, v, {"cu_block_include_tokens": cu})
+    sd = {n: p.detach().numpy() for n, p in mod.state_dict().items()}
+    out = dict(k=k.numpy(), v=v.numpy(), cu_block_include_tokens=cu.numpy(), ck=ck.numpy(), cv=cv.numpy())
+    out.update({"w:" + n: a for n, a in sd.items()})
+    return out
+
+
+def make_gate(SpatialSparseAttentionOut, ssa_module, seed, window):
+    torch.manual_seed(seed)
+    hidden, Hq, Hkv = 64, 4, 2
+    D = hidden // Hq
+    mod = SpatialSparseAttentionOut(hidden_dim=hidden, num_q_heads=Hq, num_kv_heads=Hkv, is_window_attn=window)
+    lens = [6, 10, 4, 12]
+    cu = _blocks(lens)
+    N = int(cu[-1])
+    x = torch.randn(N, hidden)
+    q = torch.randn(N, Hq * D)
+    k = torch.randn(N, Hkv * D)
+    v = torch.randn(N, Hkv * D)
+    sel = torch.randn(N, hidden)
+    comp = torch.randn(N, hidden)
+    with torch.no_grad():
+        out = mod(x, q, k, v, {"cu_block_include_tokens": cu}, {"selection_attn": sel, "compressed_attn": comp})
+    return dict(x=x.numpy(), q=q.numpy(), k=k.numpy(), v=v.numpy(), selection=sel.numpy(),
+                compressed=comp.numpy(), cu_block_include_tokens=cu.numpy(), out=out.numpy(),
+                gate_weight=mod.gate[0].weight.detach().numpy(), window=np.array(window))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    args = ap.parse_args()
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, args.ref)
+    import flash_attn  # noqa: F401  (import check only; no CPU kernel)
+
+    from sparse.ops import block_window_attention as bwa
+    from sparse.ops.block_score import get_block_score
+    from sparse.ops.triton_native_sparse_attention_impl_kvcentric import native_sparse_attend
+    from sparse.module import spatial_sparse_attention as ssa
+
+    bwa.flash_attn_varlen_func = _cpu_varlen_attention
+    ssa.flash_attn_varlen_func = _cpu_varlen_attention
+
+    for i, (name, seq_blocks, Hq, Hkv, D, k, special) in enumerate(selection_cases()):
+        data = make_selection(native_sparse_attend, name, seq_blocks, Hq, Hkv, D, k, special, seed=100 + i)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **data)
+        print("wrote", name)
+    bs_cases = [
+        ("score_g1", 11, [37, 21], [9, 5], 4, 4, 32, 4),
+        ("score_g4", 12, [50], [12], 8, 2, 64, 5),
+        ("score_few_blocks", 13, [19, 23], [3, 7], 2, 1, 16, 4),
+    ]
+    for name, seed, sq, snb, Hq, Hkv, D, topk in bs_cases:
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"),
+                            **make_block_score(get_block_score, seed, sq, snb, Hq, Hkv, D, topk))
+        print("wrote", name)
+    np.savez_compressed(os.path.join(HERE, "compress_resblock.npz"), **make_compress(ssa.SpatialSparseAttentionIn, 21))
+    print("wrote compress_resblock")
+    for window in (False, True):
+        nm = "gate_window" if window else "gate_nowindow"
+        np.savez_compressed(os.path.join(HERE, f"{nm}.npz"), **make_gate(ssa.SpatialSparseAttentionOut, ssa, 31, window))
+        print("wrote", nm)
+
+
+if __name__ == "__main__":
+    main()
