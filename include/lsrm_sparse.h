@@ -1,0 +1,227 @@
+/*
+ * lsrm_sparse.h — C ABI of the B200 (sm_100a) variable-block native sparse
+ * attention library (liblsrm_sparse.so).
+ *
+ * The library replaces the hot path of LSRM's sparse volume decoder
+ * (chenxiex/Large-Sparse-Reconstruction-Model): the Triton kernels of
+ * sparse/ops/triton_native_sparse_attention_impl_kvcentric.py, the pure-torch
+ * scorer sparse/ops/block_score.py, the flash-attn calls of the compressed
+ * and window branches, the segment-mean compression and the gated merge of
+ * sparse/module/spatial_sparse_attention.py.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers, sizes and element strides; no framework types;
+ *   - `stream` is a cudaStream_t passed as void*; nothing synchronises the
+ *     host; work is enqueued on `stream` only;
+ *   - return 0 on success or a negative LSRM_ERR_* code; a message for the
+ *     last failure of the calling thread is returned by lsrm_last_error();
+ *   - device-side problems (bad indices, timeouts) are OR-ed into the int
+ *     pointed to by `err_flags` (device memory, may be NULL) as LSRM_ERR_*
+ *     bits; callers that want them read the word after the stream completes;
+ *   - `workspace` is caller-owned device memory of at least the size reported
+ *     by the matching *_workspace_bytes() query; the library never allocates.
+ *   - token-major layouts: q/o/dq [total_q, Hq, D], k/v/dk/dv [total_k, Hkv, D]
+ *     (head stride D, token stride given), LSE [Hq, total_q] fp32.
+ *   - dtype: LSRM_DTYPE_BF16 or LSRM_DTYPE_F16 for q/k/v/o and grads.
+ */
+#ifndef LSRM_SPARSE_H_
+#define LSRM_SPARSE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSRM_ABI_VERSION 1
+
+/* return codes (negative) and device error bits (positive) */
+#define LSRM_OK 0
+#define LSRM_ERR_INVALID_ARG (-1)
+#define LSRM_ERR_UNSUPPORTED (-2)
+#define LSRM_ERR_ALIGNMENT (-3)
+#define LSRM_ERR_CUDA (-4)
+#define LSRM_ERR_WORKSPACE (-5)
+/* device error-word bits */
+#define LSRM_ERR_TIMEOUT 0x1          /* a bounded wait ran out (kernel tore down) */
+#define LSRM_ERR_DUPLICATE_BLOCK 0x2  /* a query listed one block twice */
+#define LSRM_ERR_CAPACITY 0x4         /* a work list exceeded its capacity */
+#define LSRM_ERR_BAD_INDEX 0x8        /* metadata out of range */
+
+#define LSRM_DTYPE_F16 0
+#define LSRM_DTYPE_BF16 1
+
+/* Variable-length metadata shared by the attention entry points (device
+ * pointers, int32).  Mirrors the arguments of native_sparse_attend
+ * (sparse/ops/triton_native_sparse_attention_impl_kvcentric.py:1382-1393). */
+typedef struct lsrm_varlen {
+  int32_t num_seqs;                       /* B */
+  int32_t total_q;                        /* Nq */
+  int32_t total_k;                        /* Nk */
+  int32_t num_blocks;                     /* total KV blocks (len(cu_block_include_tokens) - 1) */
+  const int32_t* cu_seqlens_q;            /* [B+1] */
+  const int32_t* cu_seqlens_k;            /* [B+1] */
+  const int32_t* cu_seqblocks;            /* [B+1] block offsets per sequence */
+  const int32_t* cu_block_include_tokens; /* [num_blocks+1] global token offsets */
+} lsrm_varlen;
+
+/* Attention problem shape and operand layout. */
+typedef struct lsrm_attn_shape {
+  int32_t num_q_heads;   /* Hq */
+  int32_t num_kv_heads;  /* Hkv; Hq % Hkv == 0, G = Hq/Hkv a power of two <= 128 */
+  int32_t head_dim;      /* D: 32 or 64 */
+  int32_t dtype;         /* LSRM_DTYPE_* */
+  int64_t q_token_stride;  /* elements between consecutive tokens of q/o/do/dq */
+  int64_t kv_token_stride; /* elements between consecutive tokens of k/v/dk/dv */
+  float softmax_scale;     /* <= 0 selects 1/sqrt(D) */
+} lsrm_attn_shape;
+
+/* ---------------------------------------------------------------------- */
+/* Library information                                                      */
+/* ---------------------------------------------------------------------- */
+int lsrm_abi_version(void);
+const char* lsrm_last_error(void);
+/* Returns the number of kernels this library launched since load (all
+ * entry points, all threads); used by benchmarks to count launches. */
+uint64_t lsrm_launch_count(void);
+
+/* ---------------------------------------------------------------------- */
+/* Selected-block attention (the reference's NSA op)                        */
+/* ---------------------------------------------------------------------- */
+
+/* Workspace needed by lsrm_select_attn_fwd/_bwd for `topk` selections per
+ * row.  `selection_rows` is total_q for per-token selection or the number of
+ * query blocks when `cu_query_blocks` is used (see below). */
+size_t lsrm_select_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t topk,
+                                   int32_t num_query_blocks);
+
+/* Forward of sparse/ops/triton_native_sparse_attention.py:17-41 /
+ * native_sparse_attn_forward (kvcentric.py:931-1010):
+ *   out [Nq,Hq,D], lse_log2 [Hq,Nq] (log2 units, as the reference's Lse).
+ * block_topk: [Hkv, rows, topk] int32 sequence-local block ids (-1 = none);
+ * rows = Nq (per-token selection, the reference) or the number of query blocks
+ * when `cu_query_blocks` (global token offsets of query blocks, [nqb+1]) is
+ * non-NULL (one selection per query block, an extension).
+ * A query whose list has no valid id gets a NaN row and -inf LSE, as in the
+ * reference.  A block id listed twice for one query is rejected
+ * (LSRM_ERR_DUPLICATE_BLOCK in err_flags). */
+int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* k,
+                         const void* v, const int32_t* block_topk, int32_t topk, const int32_t* cu_query_blocks,
+                         int32_t num_query_blocks, void* out, float* lse_log2, void* workspace,
+                         size_t workspace_bytes, int* err_flags, void* stream);
+
+/* Backward of NSA (kvcentric.py:1018-1263): dq, dk, dv (same dtype as q).
+ * `workspace` must be the one the forward used (its selection plan is
+ * reused) or freshly sized; `delta` receives rowsum(o*do) [Hq,Nq] fp32.
+ * Accumulation order is fixed: dK/dV sum query tiles in ascending order. */
+int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* k,
+                         const void* v, const void* out, const float* lse_log2, const void* dout,
+                         const int32_t* block_topk, int32_t topk, const int32_t* cu_query_blocks,
+                         int32_t num_query_blocks, void* dq, void* dk, void* dv, float* delta, void* workspace,
+                         size_t workspace_bytes, int* err_flags, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Dense-range branches                                                     */
+/* ---------------------------------------------------------------------- */
+
+/* Workspace for the compressed / window / sliding-window entries. */
+size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode);
+
+#define LSRM_DENSE_COMPRESSED 0 /* q vs all compressed blocks of its sequence */
+#define LSRM_DENSE_INTRA_BLOCK 1 /* full attention inside each block */
+#define LSRM_DENSE_SLIDING 2     /* |i-j| <= window/2 inside each sequence */
+
+/* Compressed branch (replaces flash_attn_varlen_func(q, ck, cv,
+ * cu_seqlens_q, cu_seqblocks, ..., return_attn_probs=True) at
+ * sparse/module/spatial_sparse_attention.py:121-143): k/v are the compressed
+ * tokens [num_blocks, Hkv, D]; keys of sequence b are rows
+ * [cu_seqblocks[b], cu_seqblocks[b+1]).  lse_ln: natural-log LSE [Hq,Nq].
+ * Intra-block window (sparse/ops/block_window_attention.py:14-31): q, k, v
+ * are the same token sequence, segments = cu_block_include_tokens.
+ * Sliding window (extension): segments = sequences, band |i-j| <= window/2. */
+int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode, int32_t window,
+                        const void* q, const void* k, const void* v, void* out, float* lse, void* workspace,
+                        size_t workspace_bytes, int* err_flags, void* stream);
+
+/* Backward of the above; `lse` is what the forward returned (natural log for
+ * LSRM_DENSE_COMPRESSED, log2 otherwise). */
+int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode, int32_t window,
+                        const void* q, const void* k, const void* v, const void* out, const float* lse,
+                        const void* dout, void* dq, void* dk, void* dv, float* delta, void* workspace,
+                        size_t workspace_bytes, int* err_flags, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Block scoring + deterministic top-k (sparse/ops/block_score.py:16-98)    */
+/* ---------------------------------------------------------------------- */
+
+/* score[h,i,b] = sum_g exp2(dot(q[i,hG+g], ck[b,h]) * float(sm_scale*1.44269504)
+ *                          - lse_ln[hG+g,i] * 1.44269504f)
+ * evaluated in float32 with a fixed operation order (the dot product
+ * accumulates channel 0..D-1 with separately rounded multiply and add; exp2 is
+ * a fixed range-reduction + degree-7 Taylor evaluation), so results are
+ * reproducible bit for bit.  Top-k keeps the largest scores, ties to the
+ * lowest block id, then sorts ids ascending and pads with -1.
+ * Per-token: out [Hkv, Nq, topk].  With cu_query_blocks: out [Hkv, nqb,
+ * topk], the score of a query block being the float32 sum of its tokens'
+ * scores in ascending token order; force_self always selects block j for
+ * query block j of a sequence.  `q` may be fp16/bf16 (shape->dtype); ck has
+ * the same dtype; lse_ln fp32. */
+int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
+                    const float* lse_ln, int32_t topk, const int32_t* cu_query_blocks, int32_t num_query_blocks,
+                    int32_t force_self, float sm_scale, int32_t* block_topk, int* err_flags, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Compression (SpatialSparseAttentionIn, spatial_sparse_attention.py:27-67) */
+/* ---------------------------------------------------------------------- */
+
+/* out[b, c] = mean_{t in block b} x[t, c]; x [Nk, C] row stride `x_stride`,
+ * out [num_blocks, C] contiguous; empty blocks give NaN (segment_reduce). */
+int lsrm_block_mean_fwd(int32_t num_blocks, int32_t channels, int32_t dtype, const int32_t* cu_block_include_tokens,
+                        const void* x, int64_t x_stride, void* out, void* stream);
+/* dx[t, c] = dout[block(t), c] / len(block); dx [Nk, C] contiguous. */
+int lsrm_block_mean_bwd(int32_t num_blocks, int32_t channels, int32_t dtype, const int32_t* cu_block_include_tokens,
+                        int32_t total_tokens, const void* dout, void* dx, void* stream);
+
+/* Non-affine LayerNorm (fp32 math) of r = x + h, the epilogue of
+ * SparseResBlock (sparse/module/residual_block.py:31-34), fused with the
+ * block mean: y[t] = LN(x[t]+h[t]) (optional, may be NULL) and
+ * out[b] = mean_{t in b} y[t].  mean/rstd [Nk] fp32 are saved for backward. */
+int lsrm_resnorm_mean_fwd(int32_t num_blocks, int32_t total_tokens, int32_t channels, int32_t dtype,
+                          const int32_t* cu_block_include_tokens, const void* x, const void* h, float eps, void* y,
+                          void* out, float* mean, float* rstd, void* stream);
+/* Backward: given dout [nb, C] (grad of the block mean) -> dr [Nk, C] (grad
+ * of x + h, same for both). */
+int lsrm_resnorm_mean_bwd(int32_t num_blocks, int32_t total_tokens, int32_t channels, int32_t dtype,
+                          const int32_t* cu_block_include_tokens, const void* x, const void* h, const float* mean,
+                          const float* rstd, const void* dout, void* dr, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Gated merge (SpatialSparseAttentionOut, spatial_sparse_attention.py:226-270) */
+/* ---------------------------------------------------------------------- */
+
+/* out[t, c] = sum_i sigmoid(z[t, gate_col(i, c)]) * branch_i[t, c], where z are
+ * the gate logits [N, n_branch*G_w] (G_w = C for per-channel gates, Hq for
+ * per-head gates whose value is shared by the D channels of a head).
+ * branches: array of n_branch device pointers, each [N, C] contiguous. */
+int lsrm_gate_merge_fwd(int32_t total_tokens, int32_t channels, int32_t n_branch, int32_t per_head,
+                        int32_t head_dim, int32_t dtype, const void* z, const void* const* branches, void* out,
+                        void* stream);
+/* dz [N, n_branch*G_w] and dbranch_i [N, C]. */
+int lsrm_gate_merge_bwd(int32_t total_tokens, int32_t channels, int32_t n_branch, int32_t per_head,
+                        int32_t head_dim, int32_t dtype, const void* z, const void* const* branches,
+                        const void* dout, void* dz, void* const* dbranches, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Self-test of the tcgen05 / TMA building blocks (used by the GPU tests)   */
+/* ---------------------------------------------------------------------- */
+/* a, b, v: [128, D] bf16; p: [128, 128] bf16; c1 = a @ b^T [128,128] fp32,
+ * c2 = p @ v [128, D] fp32.  D = 32 or 64. */
+int lsrm_umma_selftest(int32_t head_dim, const void* a, const void* b, const void* p, const void* v, float* c1,
+                       float* c2, int* err_flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSRM_SPARSE_H_ */

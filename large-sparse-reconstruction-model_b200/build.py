@@ -1,0 +1,91 @@
+"""Build liblsrm_sparse.so (sm_100a) in-tree with nvcc.
+
+    python large-sparse-reconstruction-model_b200/build.py [--jobs N] [--force]
+
+Each ``csrc/*.cu`` compiles to an object under ``_build/`` (skipped when up to
+date), then all objects link into ``lsrm_sparse/liblsrm_sparse.so``.  The
+library links the CUDA runtime statically and resolves the driver's tensor-map
+encoder at run time, so it loads next to any PyTorch build.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_ROOT = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(PKG_ROOT)
+CSRC = os.path.join(PKG_ROOT, "csrc")
+INCLUDE = os.path.join(REPO, "include")
+BUILD = os.path.join(PKG_ROOT, "_build")
+LIB = os.path.join(PKG_ROOT, "lsrm_sparse", "liblsrm_sparse.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "-Xcompiler",
+    "-fPIC,-O3",
+    "--expt-relaxed-constexpr",
+    "-I" + INCLUDE,
+    "-I" + CSRC,
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _deps_mtime(src: str) -> float:
+    m = os.path.getmtime(src)
+    for d in (CSRC, INCLUDE):
+        for f in os.listdir(d):
+            if f.endswith((".cuh", ".h")):
+                m = max(m, os.path.getmtime(os.path.join(d, f)))
+    return m
+
+
+def compile_one(src: str, force: bool, verbose_ptxas: bool) -> str:
+    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+    if not force and os.path.exists(obj) and os.path.getmtime(obj) >= _deps_mtime(src):
+        return obj
+    cmd = [nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
+    if verbose_ptxas:
+        cmd.insert(1, "-Xptxas=-v")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    if verbose_ptxas:
+        sys.stderr.write(r.stderr)
+    return obj
+
+
+def build(force: bool = False, jobs: int = 0, verbose_ptxas: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    jobs = jobs or min(len(srcs), os.cpu_count() or 4)
+    with cf.ThreadPoolExecutor(jobs) as ex:
+        objs = list(ex.map(lambda s: compile_one(s, force, verbose_ptxas), srcs))
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-Xcompiler", "-fPIC"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--jobs", type=int, default=0)
+    ap.add_argument("--ptxas-v", action="store_true", help="print register / shared-memory usage")
+    a = ap.parse_args()
+    print(build(a.force, a.jobs, a.ptxas_v))

@@ -1,0 +1,186 @@
+// Host entry points of the forward attention paths.
+#include <cmath>
+
+#include "attn_fwd.cuh"
+#include "attn_host.h"
+#include "host_util.h"
+
+namespace lsrm {
+
+template <int D, bool BF16, int MODE>
+static int launch_fwd_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdParams& p,
+                        int grid_x, int hkv, cudaStream_t s) {
+  constexpr int STAGES = 3;
+  using L = FwdSmem<D, STAGES>;
+  auto kern = attn_fwd_kernel<D, BF16, MODE, STAGES>;
+  LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  kern<<<dim3(grid_x, hkv), 192, L::ALLOC, s>>>(mq, mk, mv, p);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+template <int MODE>
+static int launch_fwd(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                      const FwdParams& p, int grid_x, int hkv, cudaStream_t s) {
+  if (grid_x <= 0) return LSRM_OK;
+  if (D == 64) {
+    return bf16 ? launch_fwd_t<64, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
+                : launch_fwd_t<64, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
+  }
+  return bf16 ? launch_fwd_t<32, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
+              : launch_fwd_t<32, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
+}
+
+int check_shape(const lsrm_varlen* m, const lsrm_attn_shape* sh, int& G) {
+  LSRM_CHECK_ARG(m && sh, "null metadata / shape");
+  LSRM_CHECK_ARG(sh->head_dim == 32 || sh->head_dim == 64, "head_dim must be 32 or 64 (got %d)", sh->head_dim);
+  LSRM_CHECK_ARG(sh->dtype == LSRM_DTYPE_BF16 || sh->dtype == LSRM_DTYPE_F16, "dtype must be bf16 or fp16");
+  LSRM_CHECK_ARG(sh->num_kv_heads > 0 && sh->num_q_heads % sh->num_kv_heads == 0,
+                 "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", sh->num_q_heads, sh->num_kv_heads);
+  G = sh->num_q_heads / sh->num_kv_heads;
+  LSRM_CHECK_ARG(G <= 128 && (G & (G - 1)) == 0, "query heads per kv head (%d) must be a power of two <= 128", G);
+  LSRM_CHECK_ARG(m->num_seqs >= 1 && m->total_q >= 0 && m->total_k >= 0 && m->num_blocks >= 0, "bad varlen sizes");
+  LSRM_CHECK_ARG(sh->q_token_stride >= (int64_t)sh->num_q_heads * sh->head_dim, "q token stride too small");
+  LSRM_CHECK_ARG(sh->kv_token_stride >= (int64_t)sh->num_kv_heads * sh->head_dim, "kv token stride too small");
+  return LSRM_OK;
+}
+
+float softmax_scale_of(const lsrm_attn_shape* sh) {
+  return sh->softmax_scale > 0.f ? sh->softmax_scale : 1.0f / std::sqrt((float)sh->head_dim);
+}
+
+}  // namespace lsrm
+
+using namespace lsrm;
+
+extern "C" size_t lsrm_select_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t topk,
+                                              int32_t num_query_blocks) {
+  int G = 1;
+  if (check_shape(meta, shape, G) != LSRM_OK || topk < 1) return 0;
+  SelectPlan p = make_select_plan(meta, G, shape->num_kv_heads, topk, num_query_blocks, nullptr);
+  return p.bytes + 256;  // + internal error word
+}
+
+extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q,
+                                    const void* k, const void* v, const int32_t* block_topk, int32_t topk,
+                                    const int32_t* cu_query_blocks, int32_t num_query_blocks, void* out,
+                                    float* lse_log2, void* workspace, size_t workspace_bytes, int* err_flags,
+                                    void* stream) {
+  int G = 1, rc;
+  if ((rc = check_shape(meta, shape, G))) return rc;
+  LSRM_CHECK_ARG(topk >= 1 && topk <= 64, "topk must be in [1, 64] (got %d)", topk);
+  LSRM_CHECK_ARG(num_query_blocks == 0 || cu_query_blocks, "num_query_blocks > 0 needs cu_query_blocks");
+  const size_t need = lsrm_select_workspace_bytes(meta, shape, topk, num_query_blocks);
+  if (workspace_bytes < need || !workspace) {
+    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    return LSRM_ERR_WORKSPACE;
+  }
+  if (meta->total_q == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SelectPlan plan = make_select_plan(meta, G, shape->num_kv_heads, topk, num_query_blocks, workspace);
+  int* err = err_flags ? err_flags : reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + plan.bytes);
+  const int qpt = kRows / G;
+  const bool qblock = num_query_blocks > 0;
+  if ((rc = launch_build_tiles(plan.tiles, plan.n_tiles, plan.tiles_ub, qblock ? kTilesQBlock : kTilesSeq, qpt, meta,
+                               cu_query_blocks, qblock ? num_query_blocks : meta->num_seqs, 0, err, s)))
+    return rc;
+  if ((rc = launch_build_unions(plan, meta, block_topk, topk, qblock ? num_query_blocks : meta->total_q, G, err, s)))
+    return rc;
+  const int D = shape->head_dim;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
+  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+    return rc;
+  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+    return rc;
+  FwdParams p{};
+  p.tiles = plan.tiles;
+  p.n_tiles = plan.n_tiles;
+  p.union_cnt = plan.union_cnt;
+  p.union_nchunk = plan.union_nchunk;
+  p.union_blk = plan.union_blk;
+  p.union_mask = plan.union_mask;
+  p.tiles_ub = plan.tiles_ub;
+  p.union_cap = plan.union_cap;
+  p.cu_block_include_tokens = meta->cu_block_include_tokens;
+  p.out = out;
+  p.lse = lse_log2;
+  p.q_tok_stride = shape->q_token_stride;
+  p.num_q_heads = shape->num_q_heads;
+  p.total_q = meta->total_q;
+  p.total_k = meta->total_k;
+  p.G = G;
+  p.scale_log2 = softmax_scale_of(shape) * 1.44269504f;
+  p.half_window = 0;
+  p.lse_natural = 0;
+  p.err = err;
+  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+}
+
+extern "C" size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode) {
+  int G = 1;
+  if (check_shape(meta, shape, G) != LSRM_OK) return 0;
+  DensePlan p = make_dense_plan(meta, G, mode, nullptr);
+  return p.bytes + dense_bwd_extra_bytes(meta, shape, mode) + 256;
+}
+
+namespace lsrm {
+
+int dense_fwd_tiles(const lsrm_varlen* meta, int G, int mode, int window, DensePlan& plan, int* err, cudaStream_t s) {
+  const int qpt = kRows / G;
+  if (mode == LSRM_DENSE_COMPRESSED)
+    return launch_build_tiles(plan.tiles, plan.n_tiles, plan.tiles_ub, 5 /*seq rows, compressed kv*/, qpt, meta,
+                              nullptr, meta->num_seqs, 0, err, s);
+  if (mode == LSRM_DENSE_INTRA_BLOCK)
+    return launch_build_tiles(plan.tiles, plan.n_tiles, plan.tiles_ub, kTilesKVBlock, qpt, meta, nullptr,
+                              meta->num_blocks, 0, err, s);
+  return launch_build_tiles(plan.tiles, plan.n_tiles, plan.tiles_ub, kTilesSeq, qpt, meta, nullptr, meta->num_seqs,
+                            window, err, s);
+}
+
+}  // namespace lsrm
+
+extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode,
+                                   int32_t window, const void* q, const void* k, const void* v, void* out, float* lse,
+                                   void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
+  int G = 1, rc;
+  if ((rc = check_shape(meta, shape, G))) return rc;
+  LSRM_CHECK_ARG(mode >= 0 && mode <= 2, "unknown dense mode %d", mode);
+  LSRM_CHECK_ARG(mode != LSRM_DENSE_SLIDING || window >= 0, "window must be >= 0");
+  LSRM_CHECK_ARG(mode == LSRM_DENSE_COMPRESSED || meta->total_q == meta->total_k,
+                 "window branches attend inside one token sequence (total_q == total_k)");
+  const size_t need = lsrm_dense_workspace_bytes(meta, shape, mode);
+  if (workspace_bytes < need || !workspace) {
+    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    return LSRM_ERR_WORKSPACE;
+  }
+  if (meta->total_q == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DensePlan plan = make_dense_plan(meta, G, mode, workspace);
+  int* err = err_flags ? err_flags : reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + need - 256);
+  if ((rc = dense_fwd_tiles(meta, G, mode, window, plan, err, s))) return rc;
+  const int D = shape->head_dim, qpt = kRows / G;
+  const long long nk = (mode == LSRM_DENSE_COMPRESSED) ? meta->num_blocks : meta->total_k;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
+  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, nk, shape->kv_token_stride, 1, kKVChunk))) return rc;
+  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, nk, shape->kv_token_stride, 1, kKVChunk))) return rc;
+  FwdParams p{};
+  p.tiles = plan.tiles;
+  p.n_tiles = plan.n_tiles;
+  p.out = out;
+  p.lse = lse;
+  p.q_tok_stride = shape->q_token_stride;
+  p.num_q_heads = shape->num_q_heads;
+  p.total_q = meta->total_q;
+  p.total_k = (int)nk;
+  p.G = G;
+  p.scale_log2 = softmax_scale_of(shape) * 1.44269504f;
+  p.half_window = window / 2;
+  p.lse_natural = (mode == LSRM_DENSE_COMPRESSED) ? 1 : 0;
+  p.err = err;
+  const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
+  if (mode == LSRM_DENSE_SLIDING)
+    return launch_fwd<kBand>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+  return launch_fwd<kRange>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+}

@@ -1,0 +1,422 @@
+// Forward attention kernel for sm_100a: one CTA per (query tile, kv head).
+//
+// Roles (192 threads):
+//   warps 0-3  softmax: thread r owns MMA row r (query r/G, head r%G); reads
+//              S = Q K^T from TMEM, applies the row's key mask, online softmax
+//              in log2 units, writes P (bf16/fp16) to shared memory, folds
+//              P V from TMEM into fp32 registers, writes O and the LSE.
+//   warp 4     producer: TMA loads of the Q tile and of K/V chunks (128 keys)
+//              into a STAGES-deep ring.
+//   warp 5     MMA issuer (lane 0): S_j = Q K_j^T (M=128, N=128), then
+//              O_j = P_j V_j (M=128, N=D); S and PV double-buffered in TMEM.
+//
+// KV chunk sources:
+//   kSelect : the union of the blocks selected by the tile's queries, walked
+//             in 8-token groups (one TMA box per group); a per-group query
+//             bitmask tells each row which groups it may attend.
+//   kRange  : a contiguous key range (compressed keys of the sequence, or the
+//             tokens of one block), 128-key TMA boxes.
+//   kBand   : a contiguous range with the band |i - j| <= half.
+#pragma once
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace lsrm {
+
+enum AttnMode : int { kSelect = 0, kRange = 1, kBand = 2 };
+
+struct FwdParams {
+  const QTile* tiles;
+  const int* n_tiles;
+  // select mode
+  const int* union_cnt;
+  const int* union_nchunk;
+  const int* union_blk;
+  const uint4* union_mask;
+  int tiles_ub;
+  int union_cap;
+  const int32_t* cu_block_include_tokens;
+  // outputs
+  void* out;
+  float* lse;
+  long long q_tok_stride;
+  int num_q_heads;
+  int total_q;
+  int total_k;
+  int G;
+  float scale_log2;
+  int half_window;
+  int lse_natural;  // write ln-based LSE (compressed branch) instead of log2
+  int* err;
+};
+
+struct ChunkMeta {
+  uint32_t colmask[4];     // select: columns holding a key of the chunk
+  uint32_t qmask[16][4];   // select: per group, the tile queries that may attend it
+  int row0[16];            // select: first key token of each group (-1 = unused)
+  int kv_start;            // range modes: first key token of the chunk
+  int n_valid;             // range modes: keys in the chunk
+  int pad[2];
+};
+
+template <int D, int STAGES>
+struct FwdSmem {
+  static constexpr int RB = 2 * D;
+  static constexpr int TILE = 128 * RB;
+  static constexpr int P_BYTES = 2 * 128 * 128;  // two 64-key regions, 128B rows
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + TILE;
+  static constexpr int OFF_V = OFF_K + STAGES * TILE;
+  static constexpr int OFF_P = OFF_V + STAGES * TILE;
+  static constexpr int OFF_META = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(ChunkMeta);
+  // barriers: kv_full[S], kv_empty[S], q_full, s_full[2], s_free[2], p_full[2],
+  // p_free[2], pv_full[2], pv_free[2], mma_done
+  static constexpr int NBAR = 2 * STAGES + 1 + 12 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;  // alignment slack
+};
+
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_test(bar, parity)) {
+    if (globaltimer() - t0 > 200000000ull) return false;
+  }
+  return true;
+}
+
+template <int D, bool BF16, int MODE, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
+  using L = FwdSmem<D, STAGES>;
+  constexpr int RB = L::RB;
+  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint32_t AB = BF16 ? 1u : 0u;
+
+  const int tile_idx = blockIdx.x, h = blockIdx.y;
+  if (tile_idx >= *prm.n_tiles) return;
+  const QTile tile = prm.tiles[tile_idx];
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sP = smem + L::OFF_P;
+  ChunkMeta* meta = reinterpret_cast<ChunkMeta*>(smem + L::OFF_META);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + STAGES;
+  uint64_t* q_full = bars + 2 * STAGES;
+  uint64_t* s_full = q_full + 1;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* p_free = p_full + 2;
+  uint64_t* pv_full = p_free + 2;
+  uint64_t* pv_free = pv_full + 2;
+  uint64_t* mma_done = pv_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = prm.G;
+  const int qpt = 128 / G;
+
+  // number of KV chunks for this (tile, head)
+  int n_chunks;
+  int U = 0;
+  size_t ubase = 0;
+  if constexpr (MODE == kSelect) {
+    ubase = ((size_t)h * prm.tiles_ub + tile_idx) * prm.union_cap;
+    U = prm.union_cnt[(size_t)h * prm.tiles_ub + tile_idx];
+    n_chunks = prm.union_nchunk[(size_t)h * prm.tiles_ub + tile_idx];
+  } else {
+    n_chunks = tile.kv_hi > tile.kv_lo ? (tile.kv_hi - tile.kv_lo + kKVChunk - 1) / kKVChunk : 0;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+      mbar_init(&pv_full[i], 1);
+      mbar_init(&pv_free[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S0 [0,128), S1 [128,256), PV0 [256,256+D), PV1 [256+D, 256+2D)
+  const uint32_t tm_s0 = tmem, tm_pv0 = tmem + 256;
+
+  if (warp == 4) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(q_full, L::TILE);
+      tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, q_full);
+      int u = -1, tcur = 0, tend = 0;  // select-mode walk state
+      int issued = 0;
+      for (int j = 0; j < n_chunks; ++j) {
+        const int s = j % STAGES;
+        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+        ChunkMeta& mt = meta[s];
+        uint8_t* dK = sK + s * L::TILE;
+        uint8_t* dV = sV + s * L::TILE;
+        if constexpr (MODE == kSelect) {
+          uint32_t cm[4] = {0u, 0u, 0u, 0u};
+          for (int g = 0; g < kGroupsPerChunk; ++g) {
+            while (tcur >= tend && u + 1 < U) {
+              ++u;
+              const int gb = prm.union_blk[ubase + u];
+              tcur = max(prm.cu_block_include_tokens[gb], tile.kv_lo);
+              tend = min(prm.cu_block_include_tokens[gb + 1], tile.kv_hi);
+            }
+            if (tcur < tend) {
+              const int cnt = min(kGroupRows, tend - tcur);
+              mt.row0[g] = tcur;
+              const uint4 qm = prm.union_mask[ubase + u];
+              mt.qmask[g][0] = qm.x;
+              mt.qmask[g][1] = qm.y;
+              mt.qmask[g][2] = qm.z;
+              mt.qmask[g][3] = qm.w;
+              cm[g >> 2] |= ((1u << cnt) - 1u) << ((g & 3) * 8);
+              tcur += cnt;
+            } else {
+              mt.row0[g] = -1;
+              mt.qmask[g][0] = mt.qmask[g][1] = mt.qmask[g][2] = mt.qmask[g][3] = 0u;
+            }
+          }
+          for (int w = 0; w < 4; ++w) mt.colmask[w] = cm[w];
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+          for (int g = 0; g < kGroupsPerChunk; ++g) {
+            // unused groups read past the end of the tensor: zero fill
+            const int row = mt.row0[g] >= 0 ? mt.row0[g] : prm.total_k;
+            tma_load_3d(dK + g * kGroupRows * RB, &tm_k, 0, h, row, &kv_full[s]);
+            tma_load_3d(dV + g * kGroupRows * RB, &tm_v, 0, h, row, &kv_full[s]);
+          }
+        } else {
+          const int k0 = tile.kv_lo + j * kKVChunk;
+          mt.kv_start = k0;
+          mt.n_valid = min(kKVChunk, tile.kv_hi - k0);
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+          tma_load_3d(dK, &tm_k, 0, h, k0, &kv_full[s]);
+          tma_load_3d(dV, &tm_v, 0, h, k0, &kv_full[s]);
+        }
+        issued = j + 1;
+      }
+      // Teardown after an abort: let issued copies land before the CTA exits.
+      if (*abort_flag) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer -----------------------------
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc(AB, 0, 0, 128, 128);
+      const uint32_t idesc_pv = make_idesc(AB, 0, 1, 128, D);
+      bool ok = mbar_wait(q_full, 0, abort_flag, prm.err);
+      auto issue_pv = [&](int i) -> bool {
+        const int pb = i & 1, s = i % STAGES;
+        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
+        if (!mbar_wait(&pv_free[pb], ((i >> 1) & 1) ^ 1, abort_flag, prm.err)) return false;
+        tc_fence_after();
+        const uint32_t p_base = smem_u32(sP + pb * L::P_BYTES);
+        const uint32_t v_base = smem_u32(sV + s * L::TILE);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t da = make_sdesc(p_base + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSw128);
+          const uint64_t db = make_sdesc(v_base + ks * 16 * RB, L::TILE, 8 * RB, SWZ);
+          umma_f16(tm_pv0 + pb * D, da, db, idesc_pv, ks > 0);
+        }
+        umma_commit(&pv_full[pb]);
+        umma_commit(&p_free[pb]);
+        umma_commit(&kv_empty[s]);
+        return true;
+      };
+      if (ok) {
+        for (int j = 0; j < n_chunks && ok; ++j) {
+          const int s = j % STAGES, sb = j & 1;
+          if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sQ);
+          const uint32_t k_base = smem_u32(sK + s * L::TILE);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint64_t da = make_sdesc(q_base + ks * 32, 16, 8 * RB, SWZ);
+            const uint64_t db = make_sdesc(k_base + ks * 32, 16, 8 * RB, SWZ);
+            umma_f16(tm_s0 + sb * 128, da, db, idesc_qk, ks > 0);
+          }
+          umma_commit(&s_full[sb]);
+          if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        }
+        if (ok && n_chunks > 0) issue_pv(n_chunks - 1);
+      }
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ softmax -------------------------------
+    const int r = threadIdx.x;  // MMA row
+    const int qloc = r / G;
+    const int hq = h * G + (r % G);
+    const int qi = tile.q_start + qloc;
+    const bool row_valid = qloc < tile.n_q;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = prm.scale_log2;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    float o[D];
+#pragma unroll
+    for (int c = 0; c < D; ++c) o[c] = 0.f;
+    bool ok = true;
+
+    auto fold_pv = [&](int i) -> bool {
+      const int pb = i & 1;
+      if (!mbar_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        float pv[32];
+        tmem_ld32(tm_pv0 + pb * D + lane_base + c0, pv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c0 + c] = fmaf(o[c0 + c], alpha_prev, pv[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pv_free[pb]);
+      return true;
+    };
+
+    for (int j = 0; j < n_chunks; ++j) {
+      const int s = j % STAGES, sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      // key-validity mask of this row for the 128 columns of the chunk
+      uint32_t vm[4];
+      const ChunkMeta& mt = meta[s];
+      if constexpr (MODE == kSelect) {
+        const int w = qloc >> 5, b = qloc & 31;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          uint32_t e = 0u;
+#pragma unroll
+          for (int y = 0; y < 4; ++y)
+            if ((mt.qmask[x * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
+          vm[x] = e & mt.colmask[x];
+        }
+      } else {
+        int lo = 0, hi = mt.n_valid;  // valid columns [lo, hi)
+        if constexpr (MODE == kBand) {
+          lo = max(lo, qi - prm.half_window - mt.kv_start);
+          hi = min(hi, qi + prm.half_window + 1 - mt.kv_start);
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int a = max(lo - 32 * x, 0), bnd = min(hi - 32 * x, 32);
+          uint32_t e = 0u;
+          if (bnd > a) e = ((bnd - a) == 32 ? 0xffffffffu : ((1u << (bnd - a)) - 1u)) << a;
+          vm[x] = e;
+        }
+      }
+      const uint32_t tm_s = tm_s0 + sb * 128 + lane_base;
+      // pass 1: row max over valid columns
+      float mx = -INFINITY;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        float sv[32];
+        tmem_ld32(tm_s + x * 32, sv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if ((vm[x] >> c) & 1u) mx = fmaxf(mx, sv[c]);
+      }
+      const float m_new = fmaxf(m, mx * sl2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2(m - m_use);
+      // pass 2: probabilities -> P (shared, K-major 128B swizzle)
+      if (!mbar_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      float rowsum = 0.f;
+      const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES);
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        float sv[32];
+        tmem_ld32(tm_s + x * 32, sv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float pv = ((vm[x] >> c) & 1u) ? ex2(fmaf(sv[c], sl2, -m_use)) : 0.f;
+          sv[c] = pv;
+          rowsum += pv;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int ch = x * 4 + q8;  // 16-byte chunk index along the 128 keys
+          const uint32_t addr = p_base + (ch >> 3) * 16384 + swz_offset<128>(r, ch & 7);
+          st_shared_v4(addr, pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]), pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]),
+                       pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]), pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[sb]);
+        mbar_arrive(&p_full[sb]);
+      }
+      l = l * alpha + rowsum;
+      if (j >= 1 && !fold_pv(j - 1)) { ok = false; break; }
+      alpha_prev = alpha;
+      m = m_new;
+    }
+    if (ok && n_chunks > 0) ok = fold_pv(n_chunks - 1);
+    if (ok && row_valid) {
+      const float inv = (l > 0.f) ? 1.f / l : __int_as_float(0x7fc00000);
+      uint8_t* orow = static_cast<uint8_t*>(prm.out) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
+#pragma unroll
+      for (int c = 0; c < D; c += 8) {
+        uint4 pk;
+        pk.x = pack2<BF16>(o[c] * inv, o[c + 1] * inv);
+        pk.y = pack2<BF16>(o[c + 2] * inv, o[c + 3] * inv);
+        pk.z = pack2<BF16>(o[c + 4] * inv, o[c + 5] * inv);
+        pk.w = pack2<BF16>(o[c + 6] * inv, o[c + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + c * 2) = pk;
+      }
+      float lse = (l > 0.f) ? m + __log2f(l) : -INFINITY;
+      if (prm.lse_natural) lse *= 0.69314718055994531f;
+      prm.lse[(size_t)hq * prm.total_q + qi] = lse;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace lsrm

@@ -1,0 +1,471 @@
+// Plan-building kernels: tile lists, per-tile selection unions, reverse map.
+// All integer work; deterministic outputs (the reverse map is sorted).
+#include <cuda_runtime.h>
+
+#include "host_util.h"
+#include "plan.cuh"
+
+namespace lsrm {
+
+// ---------------------------------------------------------------------------
+// Block-wide exclusive scan (blockDim.x a multiple of 32, <= 1024).
+// ---------------------------------------------------------------------------
+__device__ int block_exclusive_scan(int v, int* total, int* scratch /* >= 33 ints */) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? scratch[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) scratch[lane] = w;  // inclusive warp totals
+    if (lane == nw - 1) scratch[32] = w;
+  }
+  __syncthreads();
+  const int base = warp > 0 ? scratch[warp - 1] : 0;
+  *total = scratch[32];
+  const int res = base + x - v;
+  __syncthreads();
+  return res;
+}
+
+__device__ __forceinline__ int upper_bound_i32(const int32_t* a, int n, int x) {
+  // first index i in [0, n) with a[i] > x
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (lo + hi) >> 1;
+    if (a[mid] > x) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo;
+}
+
+// Segment i -> [row_lo, row_hi) (the tile rows), [oth_lo, oth_hi) (the range
+// the tile iterates over), sequence index, selection row.
+__device__ void segment_info(int kind, int i, const lsrm_varlen& m, const int32_t* cu_seg, int window, int& row_lo,
+                             int& row_hi, int& oth_lo, int& oth_hi, int& seq, int& sel_row) {
+  sel_row = -1;
+  switch (kind) {
+    case kTilesSeq:
+      row_lo = m.cu_seqlens_q[i];
+      row_hi = m.cu_seqlens_q[i + 1];
+      oth_lo = m.cu_seqlens_k[i];
+      oth_hi = m.cu_seqlens_k[i + 1];
+      seq = i;
+      break;
+    case kTilesQBlock:
+      row_lo = cu_seg[i];
+      row_hi = cu_seg[i + 1];
+      seq = upper_bound_i32(m.cu_seqlens_q, m.num_seqs + 1, row_lo) - 1;
+      oth_lo = m.cu_seqlens_k[seq];
+      oth_hi = m.cu_seqlens_k[seq + 1];
+      sel_row = i;
+      break;
+    case kTilesKVBlock:
+      row_lo = m.cu_block_include_tokens[i];
+      row_hi = m.cu_block_include_tokens[i + 1];
+      oth_lo = row_lo;
+      oth_hi = row_hi;
+      seq = upper_bound_i32(m.cu_seqblocks, m.num_seqs + 1, i) - 1;
+      break;
+    case kTilesCompressed:  // rows = compressed keys of sequence i, other = its queries
+      row_lo = m.cu_seqblocks[i];
+      row_hi = m.cu_seqblocks[i + 1];
+      oth_lo = m.cu_seqlens_q[i];
+      oth_hi = m.cu_seqlens_q[i + 1];
+      seq = i;
+      break;
+    default:  // kTilesKVSeq: rows = keys of sequence i, other = its queries
+      row_lo = m.cu_seqlens_k[i];
+      row_hi = m.cu_seqlens_k[i + 1];
+      oth_lo = m.cu_seqlens_q[i];
+      oth_hi = m.cu_seqlens_q[i + 1];
+      seq = i;
+      break;
+  }
+  (void)window;
+}
+
+// Forward tiles of the compressed branch: rows = queries of sequence i,
+// other = compressed keys of sequence i.  Encoded as kind 5 internally.
+constexpr int kTilesSeqCompressedKV = 5;
+
+__global__ void build_tiles_kernel(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int rows_per_tile,
+                                   lsrm_varlen m, const int32_t* cu_seg, int n_seg, int window, int* err) {
+  __shared__ int scratch[40];
+  int base = 0;
+  const int half = window / 2;
+  for (int c0 = 0; c0 < n_seg; c0 += blockDim.x) {
+    const int i = c0 + threadIdx.x;
+    int row_lo = 0, row_hi = 0, oth_lo = 0, oth_hi = 0, seq = 0, sel_row = -1;
+    int cnt = 0;
+    if (i < n_seg) {
+      const int k = (kind == kTilesSeqCompressedKV) ? kTilesSeq : kind;
+      segment_info(k, i, m, cu_seg, window, row_lo, row_hi, oth_lo, oth_hi, seq, sel_row);
+      if (kind == kTilesSeqCompressedKV) {
+        oth_lo = m.cu_seqblocks[i];
+        oth_hi = m.cu_seqblocks[i + 1];
+      }
+      if (row_hi > row_lo) cnt = (row_hi - row_lo + rows_per_tile - 1) / rows_per_tile;
+    }
+    int total;
+    const int off = base + block_exclusive_scan(cnt, &total, scratch);
+    for (int t = 0; t < cnt; ++t) {
+      const int idx = off + t;
+      if (idx >= tiles_ub) {
+        atomicOr(err, LSRM_ERR_CAPACITY);
+        break;
+      }
+      QTile q;
+      q.q_start = row_lo + t * rows_per_tile;
+      q.n_q = min(rows_per_tile, row_hi - q.q_start);
+      q.kv_lo = oth_lo;
+      q.kv_hi = oth_hi;
+      if (window > 0) {
+        // band |i - j| <= window/2 (query and key token indices of one sequence)
+        q.kv_lo = max(oth_lo, q.q_start - half);
+        q.kv_hi = min(oth_hi, q.q_start + q.n_q + half);
+      }
+      q.seq = seq;
+      q.sel_row = sel_row;
+      q.seg = i;
+      q.pad = 0;
+      tiles[idx] = q;
+    }
+    base += total;
+  }
+  if (threadIdx.x == 0) *n_tiles = min(base, tiles_ub);
+}
+
+// ---------------------------------------------------------------------------
+// Unions of selected blocks per (tile, kv head)
+// ---------------------------------------------------------------------------
+constexpr int kUnionThreads = 256;
+constexpr int kMaxUnionEntries = 8192;
+
+__global__ void __launch_bounds__(kUnionThreads)
+    build_unions_kernel(SelectPlan p, lsrm_varlen m, const int32_t* __restrict__ block_topk, int topk, int sel_rows,
+                        int G, int* err) {
+  extern __shared__ int sm[];
+  const int t = blockIdx.x, h = blockIdx.y;
+  if (t >= *p.n_tiles) return;
+  const QTile tile = p.tiles[t];
+  const int blk0 = m.cu_seqblocks[tile.seq];
+  const int nb_seq = m.cu_seqblocks[tile.seq + 1] - blk0;
+  const bool per_block = tile.sel_row >= 0;
+  const int E = per_block ? topk : tile.n_q * topk;
+  int P = 1;
+  while (P < E) P <<= 1;
+  int* keys = sm;                  // [P]
+  int* ids = sm + P;               // [P] unique ids
+  uint32_t* masks = reinterpret_cast<uint32_t*>(sm + 2 * P);  // [cap][4]
+  __shared__ int scratch[40];
+  __shared__ int s_count, s_dup;
+  const int32_t* sel = block_topk + (size_t)h * sel_rows * topk;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    int v = INT32_MAX;
+    if (i < E) {
+      const int row = per_block ? tile.sel_row : tile.q_start + i / topk;
+      const int id = sel[(size_t)row * topk + (i % topk)];
+      if (id >= 0 && id < nb_seq) v = id;
+    }
+    keys[i] = v;
+  }
+  if (threadIdx.x == 0) s_dup = 0;
+  __syncthreads();
+  // bitonic sort, ascending
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const int a = keys[i], b = keys[ixj];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // unique: each thread owns a contiguous run of the sorted keys
+  const int per = (P + blockDim.x - 1) / blockDim.x;
+  const int i0 = threadIdx.x * per, i1 = min(P, i0 + per);
+  int cnt = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int v = keys[i];
+    if (v == INT32_MAX) continue;
+    if (i == 0 || keys[i - 1] != v) ++cnt;
+    else if (per_block) s_dup = 1;  // one selection row listing a block twice
+  }
+  int total;
+  int pos = block_exclusive_scan(cnt, &total, scratch);
+  for (int i = i0; i < i1; ++i) {
+    const int v = keys[i];
+    if (v == INT32_MAX) continue;
+    if (i == 0 || keys[i - 1] != v) ids[pos++] = v;
+  }
+  if (threadIdx.x == 0) s_count = total;
+  __syncthreads();
+  const int U = s_count;
+  if (U > p.union_cap) {
+    if (threadIdx.x == 0) atomicOr(err, LSRM_ERR_CAPACITY);
+    return;
+  }
+  for (int i = threadIdx.x; i < U * 4; i += blockDim.x) masks[i] = 0u;
+  __syncthreads();
+  if (per_block) {
+    for (int u = threadIdx.x; u < U; u += blockDim.x)
+      for (int w = 0; w < 4; ++w) {
+        const int lo = w * 32;
+        uint32_t bits = 0;
+        if (tile.n_q > lo) bits = (tile.n_q - lo >= 32) ? 0xffffffffu : ((1u << (tile.n_q - lo)) - 1u);
+        masks[u * 4 + w] = bits;
+      }
+  } else {
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+      const int r = i / topk;
+      const int id = sel[(size_t)(tile.q_start + r) * topk + (i % topk)];
+      if (id < 0 || id >= nb_seq) continue;
+      int lo = 0, hi = U;  // lower bound of id in ids[0..U)
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (ids[mid] < id) lo = mid + 1;
+        else hi = mid;
+      }
+      const uint32_t bit = 1u << (r & 31);
+      const uint32_t old = atomicOr(&masks[lo * 4 + (r >> 5)], bit);
+      if (old & bit) s_dup = 1;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && s_dup) atomicOr(err, LSRM_ERR_DUPLICATE_BLOCK);
+  // write the union, count 8-row groups for the chunk count
+  const size_t base = ((size_t)h * p.tiles_ub + t) * p.union_cap;
+  int groups = 0;
+  for (int u = threadIdx.x; u < U; u += blockDim.x) {
+    const int gb = blk0 + ids[u];
+    p.union_blk[base + u] = gb;
+    p.union_mask[base + u] = make_uint4(masks[u * 4], masks[u * 4 + 1], masks[u * 4 + 2], masks[u * 4 + 3]);
+    const int t0 = max(m.cu_block_include_tokens[gb], tile.kv_lo);
+    const int t1 = min(m.cu_block_include_tokens[gb + 1], tile.kv_hi);
+    if (t1 > t0) groups += (t1 - t0 + kGroupRows - 1) / kGroupRows;
+  }
+  int gtotal;
+  block_exclusive_scan(groups, &gtotal, scratch);
+  if (threadIdx.x == 0) {
+    p.union_cnt[(size_t)h * p.tiles_ub + t] = U;
+    p.union_nchunk[(size_t)h * p.tiles_ub + t] = (gtotal + kGroupsPerChunk - 1) / kGroupsPerChunk;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reverse map: (kv head, block) -> ascending list of (tile, union entry)
+// ---------------------------------------------------------------------------
+__global__ void rev_count_kernel(SelectPlan p) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  if (t >= *p.n_tiles) return;
+  const size_t base = ((size_t)h * p.tiles_ub + t) * p.union_cap;
+  const int U = p.union_cnt[(size_t)h * p.tiles_ub + t];
+  for (int u = threadIdx.x; u < U; u += blockDim.x)
+    atomicAdd(&p.rev_off[(size_t)h * (p.num_blocks + 1) + p.union_blk[base + u] + 1], 1);
+}
+
+__global__ void rev_scan_kernel(SelectPlan p) {
+  __shared__ int scratch[40];
+  const int h = blockIdx.x;
+  int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
+  int* cur = p.rev_cursor + (size_t)h * p.num_blocks;
+  int run = 0;
+  for (int c0 = 0; c0 < p.num_blocks; c0 += blockDim.x) {
+    const int b = c0 + threadIdx.x;
+    const int v = b < p.num_blocks ? off[b + 1] : 0;
+    int total;
+    const int ex = run + block_exclusive_scan(v, &total, scratch);
+    if (b < p.num_blocks) {
+      off[b + 1] = ex + v;
+      cur[b] = ex;
+    }
+    run += total;
+  }
+  if (threadIdx.x == 0) off[0] = 0;
+}
+
+__global__ void rev_fill_kernel(SelectPlan p) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  if (t >= *p.n_tiles) return;
+  const size_t base = ((size_t)h * p.tiles_ub + t) * p.union_cap;
+  const int U = p.union_cnt[(size_t)h * p.tiles_ub + t];
+  for (int u = threadIdx.x; u < U; u += blockDim.x) {
+    const int b = p.union_blk[base + u];
+    const int pos = atomicAdd(&p.rev_cursor[(size_t)h * p.num_blocks + b], 1);
+    p.rev_entries[(size_t)h * p.tiles_ub * p.union_cap + pos] = make_int2(t, u);
+  }
+}
+
+constexpr int kRevSortMax = 8192;
+
+__global__ void __launch_bounds__(256) rev_sort_kernel(SelectPlan p, int* err) {
+  extern __shared__ long long keys[];  // [kRevSortMax]
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
+  const int s = off[b], e = off[b + 1], n = e - s;
+  if (n <= 1) return;
+  if (n > kRevSortMax) {
+    if (threadIdx.x == 0) atomicOr(err, LSRM_ERR_CAPACITY);
+    return;
+  }
+  int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap + s;
+  int P = 1;
+  while (P < n) P <<= 1;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    long long k = LLONG_MAX;
+    if (i < n) {
+      const int2 x = ent[i];
+      k = ((long long)x.x << 32) | (unsigned)x.y;
+    }
+    keys[i] = k;
+  }
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const long long a = keys[i], c = keys[ixj];
+          const bool up = (i & k) == 0;
+          if ((a > c) == up) {
+            keys[i] = c;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    ent[i] = make_int2((int)(keys[i] >> 32), (int)(keys[i] & 0xffffffffll));
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static size_t carve(uint8_t*& cur, size_t bytes) {
+  size_t a = align_up(bytes, 256);
+  cur += a;
+  return a;
+}
+
+SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int num_qblocks, void* ws) {
+  SelectPlan p{};
+  const int qpt = kRows / G;
+  const long long nq = m->total_q, nk = m->total_k;
+  const bool qblock = num_qblocks > 0;
+  p.tiles_ub = (int)(ceil_div<long long>(nq, qpt) + m->num_seqs + (qblock ? num_qblocks : 0) + 1);
+  p.union_cap = (int)std::min<long long>(qblock ? topk : (long long)qpt * topk, std::max(m->num_blocks, 1));
+  p.kvtiles_ub = (int)(ceil_div<long long>(nk, kRows) + m->num_blocks + 1);
+  p.hkv = hkv;
+  p.num_blocks = m->num_blocks;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  uint8_t* cur = base;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = cur;
+    carve(cur, bytes);
+    return r;
+  };
+  const size_t ent = (size_t)hkv * p.tiles_ub * p.union_cap;
+  p.tiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.tiles_ub));
+  p.n_tiles = reinterpret_cast<int*>(take(16));
+  p.union_cnt = reinterpret_cast<int*>(take(sizeof(int) * hkv * p.tiles_ub));
+  p.union_nchunk = reinterpret_cast<int*>(take(sizeof(int) * hkv * p.tiles_ub));
+  p.union_blk = reinterpret_cast<int*>(take(sizeof(int) * ent));
+  p.union_mask = reinterpret_cast<uint4*>(take(sizeof(uint4) * ent));
+  p.kvtiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.kvtiles_ub));
+  p.n_kvtiles = reinterpret_cast<int*>(take(16));
+  p.rev_off = reinterpret_cast<int*>(take(sizeof(int) * hkv * ((size_t)m->num_blocks + 1)));
+  p.rev_cursor = reinterpret_cast<int*>(take(sizeof(int) * hkv * (size_t)std::max(m->num_blocks, 1)));
+  p.rev_entries = reinterpret_cast<int2*>(take(sizeof(int2) * ent));
+  p.bytes = (size_t)(cur - base);
+  return p;
+}
+
+DensePlan make_dense_plan(const lsrm_varlen* m, int G, int mode, void* ws) {
+  DensePlan p{};
+  const int qpt = kRows / G;
+  const long long nq = m->total_q, nk = m->total_k;
+  long long nseg_q = (mode == LSRM_DENSE_INTRA_BLOCK) ? m->num_blocks : m->num_seqs;
+  p.tiles_ub = (int)(ceil_div<long long>(nq, qpt) + nseg_q + 1);
+  long long nrows_k = (mode == LSRM_DENSE_COMPRESSED) ? m->num_blocks : nk;
+  long long nseg_k = (mode == LSRM_DENSE_INTRA_BLOCK) ? m->num_blocks : m->num_seqs;
+  p.kvtiles_ub = (int)(ceil_div<long long>(nrows_k, kRows) + nseg_k + 1);
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  uint8_t* cur = base;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = cur;
+    carve(cur, bytes);
+    return r;
+  };
+  p.tiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.tiles_ub));
+  p.n_tiles = reinterpret_cast<int*>(take(16));
+  p.kvtiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.kvtiles_ub));
+  p.n_kvtiles = reinterpret_cast<int*>(take(16));
+  p.bytes = (size_t)(cur - base);
+  return p;
+}
+
+int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int rows_per_tile, const lsrm_varlen* m,
+                       const int32_t* cu_segments, int n_segments, int window, int* err, cudaStream_t s) {
+  build_tiles_kernel<<<1, 1024, 0, s>>>(tiles, n_tiles, tiles_ub, kind, rows_per_tile, *m, cu_segments, n_segments,
+                                        window, err);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t* block_topk, int topk, int sel_rows,
+                        int G, int* err, cudaStream_t s) {
+  const int qpt = kRows / G;
+  const int E = (sel_rows == m->total_q) ? qpt * topk : topk;
+  int P = 1;
+  while (P < std::max(E, 1)) P <<= 1;
+  if (P > kMaxUnionEntries) {
+    set_error("queries per tile (%d) x topk (%d) exceeds %d", qpt, topk, kMaxUnionEntries);
+    return LSRM_ERR_UNSUPPORTED;
+  }
+  const size_t smem = sizeof(int) * 2 * P + sizeof(uint32_t) * 4 * (size_t)p.union_cap;
+  if (smem > 200 * 1024) {
+    set_error("union builder needs %zu bytes of shared memory", smem);
+    return LSRM_ERR_UNSUPPORTED;
+  }
+  LSRM_CUDA_TRY(cudaFuncSetAttribute(build_unions_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid(p.tiles_ub, p.hkv);
+  build_unions_kernel<<<grid, kUnionThreads, smem, s>>>(p, *m, block_topk, topk, sel_rows, G, err);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s) {
+  LSRM_CUDA_TRY(cudaMemsetAsync(p.rev_off, 0, sizeof(int) * p.hkv * ((size_t)p.num_blocks + 1), s));
+  dim3 grid(p.tiles_ub, p.hkv);
+  rev_count_kernel<<<grid, 128, 0, s>>>(p);
+  LSRM_LAUNCH_CHECK();
+  rev_scan_kernel<<<p.hkv, 1024, 0, s>>>(p);
+  LSRM_LAUNCH_CHECK();
+  rev_fill_kernel<<<grid, 128, 0, s>>>(p);
+  LSRM_LAUNCH_CHECK();
+  const int sort_smem = kRevSortMax * (int)sizeof(long long);
+  LSRM_CUDA_TRY(cudaFuncSetAttribute(rev_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sort_smem));
+  rev_sort_kernel<<<dim3(std::max(p.num_blocks, 1), p.hkv), 256, sort_smem, s>>>(p, err);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+}  // namespace lsrm

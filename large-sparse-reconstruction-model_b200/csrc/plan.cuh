@@ -1,0 +1,87 @@
+// Work decomposition shared by the attention kernels.
+//
+// A query tile is up to 128 MMA rows: QPT = 128 / G queries x G query heads
+// of one KV head.  Query tiles never straddle a sequence (and, when query
+// blocks are given, never straddle a query block).  For selected-block
+// attention each (tile, kv head) carries the ascending union of the blocks its
+// queries selected and, per union entry, the bitmask of tile queries that
+// selected it; the KV side of the kernels walks that union in 8-token groups.
+// The backward's reverse map lists, per (kv head, block), the (tile, entry)
+// pairs in ascending tile order, so dK/dV accumulate in a fixed order.
+#pragma once
+
+#include <cstdint>
+
+#include "lsrm_sparse.h"
+
+namespace lsrm {
+
+struct QTile {
+  int q_start;  // first query (global token index)
+  int n_q;      // queries in the tile
+  int kv_lo;    // KV token range the tile may read (sequence or block range)
+  int kv_hi;
+  int seq;      // sequence index
+  int sel_row;  // selection row for per-query-block selection, else -1
+  int seg;      // segment index the tile came from (block / query block / sequence)
+  int pad;
+};
+
+// Tile-list builder modes.
+enum TileKind : int {
+  kTilesSeq = 0,        // segments = sequences of the query side
+  kTilesQBlock = 1,     // segments = query blocks (selection per query block)
+  kTilesKVBlock = 2,    // segments = KV blocks (intra-block window; dK/dV tiles)
+  kTilesCompressed = 3, // segments = compressed-key ranges of sequences (dK/dV)
+  kTilesKVSeq = 4,      // segments = KV sequences (sliding-window dK/dV)
+};
+
+constexpr int kRows = 128;     // MMA M (rows of a query or KV tile)
+constexpr int kKVChunk = 128;  // keys per KV chunk (MMA N of S = Q K^T)
+constexpr int kGroupRows = 8;  // rows per TMA gather group in select mode
+constexpr int kGroupsPerChunk = kKVChunk / kGroupRows;
+
+// Workspace layout for selected-block attention.
+struct SelectPlan {
+  int tiles_ub;      // capacity of the tile list
+  int union_cap;     // union entries per (tile, head)
+  int kvtiles_ub;    // capacity of the KV tile list
+  int hkv;
+  int num_blocks;
+  // device pointers into the workspace
+  QTile* tiles;
+  int* n_tiles;            // [1]
+  int* union_cnt;          // [hkv][tiles_ub]
+  int* union_nchunk;       // [hkv][tiles_ub]
+  int* union_blk;          // [hkv][tiles_ub][cap] global block ids
+  uint4* union_mask;       // [hkv][tiles_ub][cap] query bits within the tile
+  QTile* kvtiles;          // dK/dV tiles (one block's keys, <= 128)
+  int* n_kvtiles;          // [1]
+  int* rev_off;            // [hkv][num_blocks+1]
+  int* rev_cursor;         // [hkv][num_blocks]
+  int2* rev_entries;       // [hkv][tiles_ub*cap] (tile, union entry index)
+  size_t bytes;
+};
+
+struct DensePlan {
+  int tiles_ub;
+  int kvtiles_ub;
+  QTile* tiles;
+  int* n_tiles;
+  QTile* kvtiles;
+  int* n_kvtiles;
+  size_t bytes;
+};
+
+// Host helpers (plan.cu).
+SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int num_qblocks, void* ws);
+DensePlan make_dense_plan(const lsrm_varlen* m, int G, int mode, void* ws);
+
+// Enqueue the plan-building kernels.  Return 0 or an LSRM error code.
+int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int rows_per_tile, const lsrm_varlen* m,
+                       const int32_t* cu_segments, int n_segments, int window, int* err, cudaStream_t s);
+int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t* block_topk, int topk,
+                        int sel_rows, int G, int* err, cudaStream_t s);
+int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s);
+
+}  // namespace lsrm

@@ -1,0 +1,212 @@
+"""Thin torch-tensor wrappers over the C ABI (include/lsrm_sparse.h).
+
+Tensors must live on a CUDA device; every call enqueues on the current torch
+stream and never synchronises, except where a function says so.  Device-side
+error bits accumulate in a per-device word that ``read_errors()`` returns and
+clears (with a synchronisation).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import AttnShape, Varlen, check
+
+_ERR_WORDS = {}
+
+
+def _err_word(device: torch.device) -> torch.Tensor:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    w = _ERR_WORDS.get(key)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR_WORDS[key] = w
+    return w
+
+
+def read_errors(device=None, clear: bool = True) -> int:
+    """Synchronise and return the OR of device error bits (LSRM_ERR_*)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    w = _err_word(dev)
+    v = int(w.item())
+    if clear and v:
+        w.zero_()
+    return v
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return 1
+    if t.dtype == torch.float16:
+        return 0
+    raise TypeError(f"only bf16/fp16 are supported, got {t.dtype}")
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        t = t.to(torch.int32)
+    return t.contiguous()
+
+
+class Meta:
+    """Device int32 metadata of one varlen problem (keeps the tensors alive)."""
+
+    def __init__(self, cu_seqlens_q, cu_seqlens_k, cu_seqblocks, cu_block_include_tokens, total_q=None, total_k=None):
+        self.cu_seqlens_q = _i32(cu_seqlens_q)
+        self.cu_seqlens_k = _i32(cu_seqlens_k)
+        self.cu_seqblocks = _i32(cu_seqblocks)
+        self.cu_block_include_tokens = _i32(cu_block_include_tokens)
+        self.num_seqs = self.cu_seqlens_q.numel() - 1
+        self.num_blocks = self.cu_block_include_tokens.numel() - 1
+        self.total_q = int(total_q) if total_q is not None else None
+        self.total_k = int(total_k) if total_k is not None else None
+
+    def struct(self, total_q: int, total_k: int) -> Varlen:
+        return Varlen(
+            self.num_seqs, int(total_q), int(total_k), self.num_blocks,
+            self.cu_seqlens_q.data_ptr(), self.cu_seqlens_k.data_ptr(), self.cu_seqblocks.data_ptr(),
+            self.cu_block_include_tokens.data_ptr(),
+        )
+
+
+def _shape(q: torch.Tensor, k: torch.Tensor, softmax_scale: Optional[float]) -> AttnShape:
+    assert q.dim() == 3 and k.dim() == 3, "q/k must be [tokens, heads, head_dim]"
+    assert q.stride(-1) == 1 and q.stride(-2) == q.shape[-1], "q must have contiguous [heads, head_dim]"
+    assert k.stride(-1) == 1 and k.stride(-2) == k.shape[-1], "k must have contiguous [heads, head_dim]"
+    return AttnShape(
+        q.shape[1], k.shape[1], q.shape[2], _dtype_code(q), q.stride(0), k.stride(0),
+        float(softmax_scale) if softmax_scale else 0.0,
+    )
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# ---------------------------------------------------------------------------
+# Selected-block attention
+# ---------------------------------------------------------------------------
+
+
+def select_attn_fwd(q, k, v, block_topk, meta: Meta, softmax_scale=None, cu_query_blocks=None,
+                    workspace: Optional[torch.Tensor] = None):
+    """Returns (out [Nq,Hq,D], lse_log2 [Hq,Nq] fp32, workspace)."""
+    L = _lib.lib()
+    assert q.dtype == k.dtype == v.dtype
+    assert k.stride() == v.stride(), "k and v must share a layout"
+    block_topk = _i32(block_topk)
+    topk = block_topk.shape[-1]
+    nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
+    cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
+    vl = meta.struct(q.shape[0], k.shape[0])
+    sh = _shape(q, k, softmax_scale)
+    need = L.lsrm_select_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), topk, nqb)
+    if need == 0:
+        raise _lib.LsrmError("invalid selection problem: " + L.lsrm_last_error().decode())
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, q.device)
+    out = torch.empty_like(q) if q.is_contiguous() else torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    assert out.stride(0) == q.stride(0)
+    lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+    rc = L.lsrm_select_attn_fwd(
+        ctypes.byref(vl), ctypes.byref(sh), _ptr(q), _ptr(k), _ptr(v), _ptr(block_topk), topk, _ptr(cqb), nqb,
+        _ptr(out), _ptr(lse), _ptr(workspace), workspace.numel(), _ptr(_err_word(q.device)), _stream(),
+    )
+    check(rc, "lsrm_select_attn_fwd")
+    return out, lse, workspace
+
+
+def select_attn_bwd(q, k, v, out, lse, dout, block_topk, meta: Meta, softmax_scale=None, cu_query_blocks=None,
+                    workspace: Optional[torch.Tensor] = None):
+    """Returns (dq, dk, dv)."""
+    L = _lib.lib()
+    block_topk = _i32(block_topk)
+    topk = block_topk.shape[-1]
+    nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
+    cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
+    vl = meta.struct(q.shape[0], k.shape[0])
+    sh = _shape(q, k, softmax_scale)
+    need = L.lsrm_select_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), topk, nqb)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, q.device)
+    dout = dout.contiguous() if dout.stride() != q.stride() else dout
+    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+    dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    delta = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+    rc = L.lsrm_select_attn_bwd(
+        ctypes.byref(vl), ctypes.byref(sh), _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse), _ptr(dout),
+        _ptr(block_topk), topk, _ptr(cqb), nqb, _ptr(dq), _ptr(dk), _ptr(dv), _ptr(delta), _ptr(workspace),
+        workspace.numel(), _ptr(_err_word(q.device)), _stream(),
+    )
+    check(rc, "lsrm_select_attn_bwd")
+    return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# Dense-range branches
+# ---------------------------------------------------------------------------
+
+DENSE_COMPRESSED = _lib.DENSE_COMPRESSED
+DENSE_INTRA_BLOCK = _lib.DENSE_INTRA_BLOCK
+DENSE_SLIDING = _lib.DENSE_SLIDING
+
+
+def dense_attn_fwd(q, k, v, meta: Meta, mode: int, window: int = 0, softmax_scale=None):
+    """Returns (out, lse).  lse is natural-log for DENSE_COMPRESSED, log2
+    otherwise; [Hq, Nq] fp32."""
+    L = _lib.lib()
+    vl = meta.struct(q.shape[0], k.shape[0])
+    sh = _shape(q, k, softmax_scale)
+    need = L.lsrm_dense_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), mode)
+    if need == 0:
+        raise _lib.LsrmError("invalid dense problem: " + L.lsrm_last_error().decode())
+    ws = _workspace(need, q.device)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+    rc = L.lsrm_dense_attn_fwd(ctypes.byref(vl), ctypes.byref(sh), mode, int(window), _ptr(q), _ptr(k), _ptr(v),
+                               _ptr(out), _ptr(lse), _ptr(ws), ws.numel(), _ptr(_err_word(q.device)), _stream())
+    check(rc, "lsrm_dense_attn_fwd")
+    return out, lse
+
+
+def dense_attn_bwd(q, k, v, out, lse, dout, meta: Meta, mode: int, window: int = 0, softmax_scale=None):
+    L = _lib.lib()
+    vl = meta.struct(q.shape[0], k.shape[0])
+    sh = _shape(q, k, softmax_scale)
+    need = L.lsrm_dense_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), mode)
+    ws = _workspace(need, q.device)
+    dout = dout.contiguous() if dout.stride() != q.stride() else dout
+    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+    dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    delta = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+    rc = L.lsrm_dense_attn_bwd(ctypes.byref(vl), ctypes.byref(sh), mode, int(window), _ptr(q), _ptr(k), _ptr(v),
+                               _ptr(out), _ptr(lse), _ptr(dout), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(delta), _ptr(ws),
+                               ws.numel(), _ptr(_err_word(q.device)), _stream())
+    check(rc, "lsrm_dense_attn_bwd")
+    return dq, dk, dv
+
+
+def umma_selftest(a, b, p, v):
+    L = _lib.lib()
+    D = a.shape[1]
+    c1 = torch.empty(128, 128, dtype=torch.float32, device=a.device)
+    c2 = torch.empty(128, D, dtype=torch.float32, device=a.device)
+    rc = L.lsrm_umma_selftest(D, _ptr(a), _ptr(b), _ptr(p), _ptr(v), _ptr(c1), _ptr(c2), _ptr(_err_word(a.device)),
+                              _stream())
+    check(rc, "lsrm_umma_selftest")
+    return c1, c2
