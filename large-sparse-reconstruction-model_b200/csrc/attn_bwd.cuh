@@ -1,0 +1,834 @@
+// Backward attention kernels for sm_100a.
+//
+// attn_dq_kernel — one CTA per (query tile, kv head), 64-key chunks:
+//   S_j = Q K_j^T, dP_j = dO V_j^T (TMEM, double-buffered); the 4 compute
+//   warps form dS = P (dP - delta) * scale with P = exp2(S*scale*log2e - lse)
+//   and the row's key mask, write dS to shared memory; dQ += dS K_j
+//   accumulates in TMEM and is written once.  Row r also computes
+//   delta = rowsum(O * dO) in its prologue and stores it for dK/dV.
+//
+// attn_dkdv_kernel — one CTA per (KV tile of <= 128 keys, kv head[, split]):
+//   the queries attending the tile are gathered 64 MMA rows at a time (for
+//   selected-block attention: the tiles listed by the sorted reverse map and
+//   their query bitmasks; for dense branches: a contiguous query range);
+//   S^T = K Q_c^T, dP^T = V dO_c^T; the compute warps (row = key) form P^T and
+//   dS^T; dV += P^T dO_c and dK += dS^T Q_c accumulate in TMEM.  Single writer
+//   per KV tile, query chunks in ascending order: deterministic.
+#pragma once
+
+#include "attn_fwd.cuh"
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace lsrm {
+
+constexpr int kDqChunk = 64;     // keys per dQ chunk
+constexpr int kDqGroups = kDqChunk / kGroupRows;
+constexpr int kKvQRows = 64;     // query rows per dK/dV chunk
+
+struct DqParams {
+  const QTile* tiles;
+  const int* n_tiles;
+  const int* union_cnt;
+  const int* union_ngroups;
+  const int* union_blk;
+  const uint4* union_mask;
+  int tiles_ub;
+  int union_cap;
+  const int32_t* cu_block_include_tokens;
+  const void* out;
+  const void* dout;
+  const float* lse;
+  float* delta;
+  void* dq;
+  long long q_tok_stride;
+  int total_q;
+  int total_k;
+  int G;
+  float scale_log2;
+  float scale;
+  int half_window;
+  int lse_natural;
+  int* err;
+};
+
+struct DqMeta {
+  uint32_t colmask[2];
+  uint32_t qmask[kDqGroups][4];
+  int row0[kDqGroups];
+  int kv_start;
+  int n_valid;
+};
+
+template <int D, int STAGES>
+struct DqSmem {
+  static constexpr int RB = 2 * D;
+  static constexpr int QTILE = 128 * RB;
+  static constexpr int KTILE = kDqChunk * RB;
+  static constexpr int DS_BYTES = 128 * 128;  // 128 rows x 64 keys x 2 B
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = QTILE;
+  static constexpr int OFF_K = 2 * QTILE;
+  static constexpr int OFF_V = OFF_K + STAGES * KTILE;
+  static constexpr int OFF_DS = OFF_V + STAGES * KTILE;
+  static constexpr int OFF_META = OFF_DS + 2 * DS_BYTES;
+  static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(DqMeta);
+  static constexpr int NBAR = 2 * STAGES + 1 + 8 + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+};
+
+// Fills the groups of one select-mode chunk by walking the union.
+template <int NG>
+__device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, int U, const int* union_blk,
+                                                  const uint4* union_mask, size_t ubase, const int32_t* cu_blk,
+                                                  int kv_lo, int kv_hi, int* row0, uint32_t (*qmask)[4],
+                                                  uint32_t* colmask) {
+  uint32_t cm[NG / 4];
+#pragma unroll
+  for (int w = 0; w < NG / 4; ++w) cm[w] = 0u;
+  for (int g = 0; g < NG; ++g) {
+    while (tcur >= tend && u + 1 < U) {
+      ++u;
+      const int gb = union_blk[ubase + u];
+      tcur = max(cu_blk[gb], kv_lo);
+      tend = min(cu_blk[gb + 1], kv_hi);
+    }
+    if (tcur < tend) {
+      const int cnt = min(kGroupRows, tend - tcur);
+      row0[g] = tcur;
+      const uint4 qm = union_mask[ubase + u];
+      qmask[g][0] = qm.x;
+      qmask[g][1] = qm.y;
+      qmask[g][2] = qm.z;
+      qmask[g][3] = qm.w;
+      cm[g >> 2] |= ((1u << cnt) - 1u) << ((g & 3) * 8);
+      tcur += cnt;
+    } else {
+      row0[g] = -1;
+      qmask[g][0] = qmask[g][1] = qmask[g][2] = qmask[g][3] = 0u;
+    }
+  }
+#pragma unroll
+  for (int w = 0; w < NG / 4; ++w) colmask[w] = cm[w];
+}
+
+template <int D, bool BF16, int MODE, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    attn_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                   const DqParams prm) {
+  using L = DqSmem<D, STAGES>;
+  constexpr int RB = L::RB;
+  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint32_t AB = BF16 ? 1u : 0u;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+
+  const int tile_idx = blockIdx.x, h = blockIdx.y;
+  if (tile_idx >= *prm.n_tiles) return;
+  const QTile tile = prm.tiles[tile_idx];
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sDS = smem + L::OFF_DS;
+  DqMeta* meta = reinterpret_cast<DqMeta*>(smem + L::OFF_META);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + STAGES;
+  uint64_t* qdo_full = bars + 2 * STAGES;
+  uint64_t* sd_full = qdo_full + 1;
+  uint64_t* sd_free = sd_full + 2;
+  uint64_t* ds_full = sd_free + 2;
+  uint64_t* ds_free = ds_full + 2;
+  uint64_t* dq_done = ds_free + 2;
+  uint64_t* mma_done = dq_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = prm.G;
+
+  int n_chunks, U = 0;
+  size_t ubase = 0;
+  if constexpr (MODE == kSelect) {
+    ubase = ((size_t)h * prm.tiles_ub + tile_idx) * prm.union_cap;
+    U = prm.union_cnt[(size_t)h * prm.tiles_ub + tile_idx];
+    n_chunks = (prm.union_ngroups[(size_t)h * prm.tiles_ub + tile_idx] + kDqGroups - 1) / kDqGroups;
+  } else {
+    n_chunks = tile.kv_hi > tile.kv_lo ? (tile.kv_hi - tile.kv_lo + kDqChunk - 1) / kDqChunk : 0;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(qdo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sd_full[i], 1);
+      mbar_init(&sd_free[i], 4);
+      mbar_init(&ds_full[i], 4);
+      mbar_init(&ds_free[i], 1);
+    }
+    mbar_init(dq_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: S0 [0,64) S1 [64,128) dP0 [128,192) dP1 [192,256) dQ [256, 256+D)
+  const uint32_t tm_s0 = tmem, tm_dp0 = tmem + 128, tm_dq = tmem + 256;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const int qpt = 128 / G;
+      mbar_arrive_expect_tx(qdo_full, 2 * L::QTILE);
+      tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, qdo_full);
+      tma_load_3d(sDO, &tm_do, 0, h * G, tile.q_start, qdo_full);
+      (void)qpt;
+      int u = -1, tcur = 0, tend = 0, issued = 0;
+      for (int j = 0; j < n_chunks; ++j) {
+        const int s = j % STAGES;
+        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+        DqMeta& mt = meta[s];
+        uint8_t* dK = sK + s * L::KTILE;
+        uint8_t* dV = sV + s * L::KTILE;
+        if constexpr (MODE == kSelect) {
+          walk_union_groups<kDqGroups>(u, tcur, tend, U, prm.union_blk, prm.union_mask, ubase,
+                                       prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
+                                       mt.colmask);
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+          for (int g = 0; g < kDqGroups; ++g) {
+            const int row = mt.row0[g] >= 0 ? mt.row0[g] : prm.total_k;
+            tma_load_3d(dK + g * kGroupRows * RB, &tm_k, 0, h, row, &kv_full[s]);
+            tma_load_3d(dV + g * kGroupRows * RB, &tm_v, 0, h, row, &kv_full[s]);
+          }
+        } else {
+          const int k0 = tile.kv_lo + j * kDqChunk;
+          mt.kv_start = k0;
+          mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+          tma_load_3d(dK, &tm_k, 0, h, k0, &kv_full[s]);
+          tma_load_3d(dV, &tm_v, 0, h, k0, &kv_full[s]);
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_drain(qdo_full, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc(AB, 0, 0, 128, kDqChunk);
+      const uint32_t idesc_dq = make_idesc(AB, 0, 1, 128, D);
+      bool ok = mbar_wait(qdo_full, 0, abort_flag, prm.err);
+      auto issue_dq = [&](int i) -> bool {
+        const int pb = i & 1, s = i % STAGES;
+        if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sDS + pb * L::DS_BYTES);
+        const uint32_t k_base = smem_u32(sK + s * L::KTILE);
+#pragma unroll
+        for (int ks = 0; ks < kDqChunk / 16; ++ks) {
+          const uint64_t da = make_sdesc(a_base + ks * 32, 16, 1024, kSw128);
+          const uint64_t db = make_sdesc(k_base + ks * 16 * RB, L::KTILE, 8 * RB, SWZ);
+          umma_f16(tm_dq, da, db, idesc_dq, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(&ds_free[pb]);
+        umma_commit(&kv_empty[s]);
+        return true;
+      };
+      if (ok) {
+        for (int j = 0; j < n_chunks && ok; ++j) {
+          const int s = j % STAGES, sb = j & 1;
+          if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&sd_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
+          const uint32_t k_base = smem_u32(sK + s * L::KTILE), v_base = smem_u32(sV + s * L::KTILE);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            umma_f16(tm_s0 + sb * kDqChunk, make_sdesc(q_base + ks * 32, 16, 8 * RB, SWZ),
+                     make_sdesc(k_base + ks * 32, 16, 8 * RB, SWZ), idesc_s, ks > 0);
+          }
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            umma_f16(tm_dp0 + sb * kDqChunk, make_sdesc(do_base + ks * 32, 16, 8 * RB, SWZ),
+                     make_sdesc(v_base + ks * 32, 16, 8 * RB, SWZ), idesc_s, ks > 0);
+          }
+          umma_commit(&sd_full[sb]);
+          if (j >= 1 && !issue_dq(j - 1)) { ok = false; break; }
+        }
+        if (ok && n_chunks > 0) issue_dq(n_chunks - 1);
+      }
+      umma_commit(dq_done);
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    const int r = threadIdx.x;
+    const int qloc = r / G;
+    const int hq = h * G + (r % G);
+    const int qi = tile.q_start + qloc;
+    const bool row_valid = qloc < tile.n_q;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = prm.scale_log2, scale = prm.scale;
+    float lse2 = 0.f, delta = 0.f;
+    if (row_valid) {
+      lse2 = prm.lse[(size_t)hq * prm.total_q + qi];
+      if (prm.lse_natural) lse2 *= 1.4426950408889634f;
+      const size_t off = ((size_t)qi * prm.q_tok_stride + (size_t)hq * D);
+      const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const T*>(prm.out) + off);
+      const uint4* grow = reinterpret_cast<const uint4*>(static_cast<const T*>(prm.dout) + off);
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 a = orow[c], b = grow[c];
+        const T* ae = reinterpret_cast<const T*>(&a);
+        const T* be = reinterpret_cast<const T*>(&b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) delta = fmaf((float)ae[e], (float)be[e], delta);
+      }
+      prm.delta[(size_t)hq * prm.total_q + qi] = delta;
+    }
+    bool ok = true;
+    for (int j = 0; j < n_chunks; ++j) {
+      const int s = j % STAGES, sb = j & 1;
+      if (!mbar_wait(&sd_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      const DqMeta& mt = meta[s];
+      uint32_t vm[2];
+      if constexpr (MODE == kSelect) {
+        const int w = qloc >> 5, b = qloc & 31;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          uint32_t e = 0u;
+#pragma unroll
+          for (int y = 0; y < 4; ++y)
+            if ((mt.qmask[x * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
+          vm[x] = e & mt.colmask[x];
+        }
+      } else {
+        int lo = 0, hi = mt.n_valid;
+        if constexpr (MODE == kBand) {
+          lo = max(lo, qi - prm.half_window - mt.kv_start);
+          hi = min(hi, qi + prm.half_window + 1 - mt.kv_start);
+        }
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int a = max(lo - 32 * x, 0), bnd = min(hi - 32 * x, 32);
+          uint32_t e = 0u;
+          if (bnd > a) e = ((bnd - a) == 32 ? 0xffffffffu : ((1u << (bnd - a)) - 1u)) << a;
+          vm[x] = e;
+        }
+      }
+      if (!mbar_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float sv[32], dp[32];
+        tmem_ld32(tm_s0 + sb * kDqChunk + lane_base + x * 32, sv);
+        tmem_ld32(tm_dp0 + sb * kDqChunk + lane_base + x * 32, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const bool valid = (vm[x] >> c) & 1u;
+          const float p = ex2(fmaf(sv[c], sl2, -lse2));
+          sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int ch = x * 4 + q8;
+          st_shared_v4(ds_base + swz_offset<128>(r, ch), pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]),
+                       pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]), pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]),
+                       pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sd_free[sb]);
+        mbar_arrive(&ds_full[sb]);
+      }
+    }
+    // every lane takes part in the warp-collective TMEM loads; only valid rows store
+    bool have = ok;
+    if (ok && n_chunks > 0) have = mbar_wait(dq_done, 0, abort_flag, prm.err);
+    if (have) {
+      tc_fence_after();
+      uint8_t* drow = static_cast<uint8_t*>(prm.dq) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        float v[32];
+        if (n_chunks > 0) {
+          tmem_ld32(tm_dq + lane_base + c0, v);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = 0.f;
+        }
+        if (!row_valid) continue;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 pk;
+          pk.x = pack2<BF16>(v[c], v[c + 1]);
+          pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
+          pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
+          pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
+          *reinterpret_cast<uint4*>(drow + (c0 + c) * 2) = pk;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dK / dV
+// ---------------------------------------------------------------------------
+
+struct DkvParams {
+  const QTile* kvtiles;
+  const int* n_kvtiles;
+  int kvtiles_ub;
+  // select mode: reverse map
+  const QTile* qtiles;
+  const int* rev_off;
+  const int2* rev_entries;
+  const uint4* union_mask;
+  int tiles_ub;
+  int union_cap;
+  int num_blocks;
+  // per-row statistics [Hq, Nq]
+  const float* lse;
+  const float* delta;
+  void* dk;
+  void* dv;
+  float* partial;  // [split][hkv][kvtiles_ub][128][D] x 2 when n_split > 1
+  int n_split;
+  long long kv_tok_stride;
+  int total_q;
+  int G;
+  int hkv;
+  float scale_log2;
+  float scale;
+  int half_window;
+  int lse_natural;
+  int* err;
+};
+
+struct KvMeta {
+  float lse2[kKvQRows];
+  float delta[kKvQRows];
+  int qidx[kKvQRows];  // query token of each row (-1: padding)
+  int n_rows;
+  int pad[3];
+};
+
+template <int D, int STAGES>
+struct DkvSmem {
+  static constexpr int RB = 2 * D;
+  static constexpr int KTILE = 128 * RB;
+  static constexpr int QTILE = kKvQRows * RB;
+  static constexpr int PT_BYTES = 128 * 128;  // 128 keys x 64 query rows x 2 B
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = KTILE;
+  static constexpr int OFF_Q = 2 * KTILE;
+  static constexpr int OFF_DO = OFF_Q + STAGES * QTILE;
+  static constexpr int OFF_PT = OFF_DO + STAGES * QTILE;
+  static constexpr int OFF_DST = OFF_PT + 2 * PT_BYTES;
+  static constexpr int OFF_META = OFF_DST + 2 * PT_BYTES;
+  static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(KvMeta);
+  // kv_full, q_full[S], q_empty[S], st_full[2], st_free[2], pds_full[2], pds_free[2], acc_done, mma_done
+  static constexpr int NBAR = 1 + 2 * STAGES + 8 + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 32;
+  static constexpr int ALLOC = BYTES + 1024;
+};
+
+// Number of query rows (queries x G) gathered for one KV tile (select mode).
+__device__ __forceinline__ int count_select_queries(const DkvParams& prm, int h, int blk) {
+  const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
+  const int e0 = off[blk], e1 = off[blk + 1];
+  const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
+  int n = 0;
+  for (int e = e0 + (threadIdx.x & 31); e < e1; e += 32) {
+    const int2 x = ent[e];
+    const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+    n += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  return n;
+}
+
+template <int D, bool BF16, int MODE, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    attn_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                     const DkvParams prm) {
+  using L = DkvSmem<D, STAGES>;
+  constexpr int RB = L::RB;
+  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint32_t AB = BF16 ? 1u : 0u;
+
+  const int split = blockIdx.x % prm.n_split;
+  const int kt_idx = blockIdx.x / prm.n_split;
+  const int h = blockIdx.y;
+  if (kt_idx >= *prm.n_kvtiles) return;
+  const QTile kt = prm.kvtiles[kt_idx];  // rows = keys [q_start, q_start + n_q)
+  const int G = prm.G;
+  const int qpc = kKvQRows / G;  // queries per chunk
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sPT = smem + L::OFF_PT;
+  uint8_t* sDST = smem + L::OFF_DST;
+  KvMeta* meta = reinterpret_cast<KvMeta*>(smem + L::OFF_META);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = q_full + STAGES;
+  uint64_t* st_full = q_empty + STAGES;
+  uint64_t* st_free = st_full + 2;
+  uint64_t* pds_full = st_free + 2;
+  uint64_t* pds_free = pds_full + 2;
+  uint64_t* acc_done = pds_free + 2;
+  uint64_t* mma_done = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  int* s_nchunks = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // query range of this split (dense modes) / number of gathered queries (select)
+  int q_lo = kt.kv_lo, q_hi = kt.kv_hi;
+  if constexpr (MODE != kSelect) {
+    const int nq = max(q_hi - q_lo, 0);
+    const int per = ((nq + prm.n_split - 1) / prm.n_split + qpc - 1) / qpc * qpc;
+    q_lo = min(kt.kv_lo + split * per, kt.kv_hi);
+    q_hi = min(q_lo + per, kt.kv_hi);
+  }
+  if (warp == 4) {
+    int nqueries;
+    if constexpr (MODE == kSelect) nqueries = count_select_queries(prm, h, kt.seg);
+    else nqueries = max(q_hi - q_lo, 0);
+    if (lane == 0) *s_nchunks = (nqueries + qpc - 1) / qpc;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&st_full[i], 1);
+      mbar_init(&st_free[i], 4);
+      mbar_init(&pds_full[i], 4);
+      mbar_init(&pds_free[i], 1);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_chunks = *s_nchunks;
+  // TMEM: St0 [0,64) St1 [64,128) dPt0 [128,192) dPt1 [192,256) dK [256,256+D) dV [256+D, 256+2D)
+  const uint32_t tm_st0 = tmem, tm_dpt0 = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 256 + D;
+
+  if (warp == 4) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+      tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
+      tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+    }
+    // select-mode walk state (lane 0 walks, all lanes issue the gathers)
+    const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
+    const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
+    int e = 0, e_end = 0, tq0 = 0;
+    uint32_t wbits[4] = {0u, 0u, 0u, 0u};
+    if constexpr (MODE == kSelect) {
+      e = off[kt.seg] - 1;
+      e_end = off[kt.seg + 1];
+    }
+    int issued = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int s = c % STAGES;
+      if (!mbar_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+      KvMeta& mt = meta[s];
+      uint8_t* dQ = sQ + s * L::QTILE;
+      uint8_t* dDO = sDO + s * L::QTILE;
+      if constexpr (MODE == kSelect) {
+        if (lane == 0) {
+          int n = 0;
+          while (n < qpc) {
+            if ((wbits[0] | wbits[1] | wbits[2] | wbits[3]) == 0u) {
+              if (e + 1 >= e_end) break;
+              ++e;
+              const int2 x = ent[e];
+              const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+              wbits[0] = m.x;
+              wbits[1] = m.y;
+              wbits[2] = m.z;
+              wbits[3] = m.w;
+              tq0 = prm.qtiles[x.x].q_start;
+              continue;
+            }
+            int w = 0;
+            while (wbits[w] == 0u) ++w;
+            const int b = __ffs(wbits[w]) - 1;
+            wbits[w] &= wbits[w] - 1u;
+            mt.qidx[n] = tq0 + w * 32 + b;  // per query for now; expanded below
+            ++n;
+          }
+          mt.n_rows = n * G;
+          for (int i = n; i < qpc; ++i) mt.qidx[i] = -1;
+        }
+        __syncwarp();
+        // expand per-query entries to rows, gather Q / dO, lse / delta
+        int myq[2];
+        for (int i = 0; i < 2; ++i) {
+          const int slot = lane + 32 * i;
+          myq[i] = slot < qpc ? mt.qidx[slot] : -1;
+        }
+        __syncwarp();
+        for (int i = 0; i < 2; ++i) {
+          const int slot = lane + 32 * i;
+          if (slot < qpc) {
+            const int q = myq[i];
+            for (int g = 0; g < G; ++g) {
+              const int row = slot * G + g;
+              mt.qidx[row] = q;
+              mt.lse2[row] = q >= 0 ? prm.lse[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
+              mt.delta[row] = q >= 0 ? prm.delta[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
+            }
+          }
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&q_full[s], 2 * L::QTILE);
+        __syncwarp();
+        for (int i = 0; i < 2; ++i) {
+          const int slot = lane + 32 * i;
+          if (slot < qpc) {
+            const int q = myq[i] >= 0 ? myq[i] : prm.total_q;  // padding rows read zeros
+            tma_load_3d(dQ + slot * G * RB, &tm_q, 0, h * G, q, &q_full[s]);
+            tma_load_3d(dDO + slot * G * RB, &tm_do, 0, h * G, q, &q_full[s]);
+          }
+        }
+      } else {
+        const int q0 = q_lo + c * qpc;
+        const int nq = min(qpc, q_hi - q0);
+        for (int row = lane; row < kKvQRows; row += 32) {
+          const int ql = row / G, g = row % G;
+          const int q = ql < nq ? q0 + ql : -1;
+          mt.qidx[row] = q;
+          mt.lse2[row] = q >= 0 ? prm.lse[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
+          mt.delta[row] = q >= 0 ? prm.delta[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
+        }
+        if (lane == 0) mt.n_rows = nq * G;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[s], 2 * L::QTILE);
+          tma_load_3d(dQ, &tm_q, 0, h * G, q0, &q_full[s]);
+          tma_load_3d(dDO, &tm_do, 0, h * G, q0, &q_full[s]);
+        }
+      }
+      issued = c + 1;
+    }
+    if (lane == 0 && *abort_flag) {
+      mbar_wait_drain(kv_full, 0);
+      for (int c = max(0, issued - STAGES); c < issued; ++c) mbar_wait_drain(&q_full[c % STAGES], (c / STAGES) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer -----------------------------
+    if (lane == 0) {
+      const uint32_t idesc_st = make_idesc(AB, 0, 0, 128, kKvQRows);
+      const uint32_t idesc_acc = make_idesc(AB, 0, 1, 128, D);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, prm.err);
+      auto issue_acc = [&](int i) -> bool {
+        const int pb = i & 1, s = i % STAGES;
+        if (!mbar_wait(&pds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
+        tc_fence_after();
+        const uint32_t pt = smem_u32(sPT + pb * L::PT_BYTES), dst = smem_u32(sDST + pb * L::PT_BYTES);
+        const uint32_t qb = smem_u32(sQ + s * L::QTILE), dob = smem_u32(sDO + s * L::QTILE);
+#pragma unroll
+        for (int ks = 0; ks < kKvQRows / 16; ++ks) {
+          umma_f16(tm_dv, make_sdesc(pt + ks * 32, 16, 1024, kSw128),
+                   make_sdesc(dob + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < kKvQRows / 16; ++ks) {
+          umma_f16(tm_dk, make_sdesc(dst + ks * 32, 16, 1024, kSw128),
+                   make_sdesc(qb + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(&pds_free[pb]);
+        umma_commit(&q_empty[s]);
+        return true;
+      };
+      if (ok) {
+        for (int c = 0; c < n_chunks && ok; ++c) {
+          const int s = c % STAGES, sb = c & 1;
+          if (!mbar_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&st_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t kb = smem_u32(sK), vb = smem_u32(sV);
+          const uint32_t qb = smem_u32(sQ + s * L::QTILE), dob = smem_u32(sDO + s * L::QTILE);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_f16(tm_st0 + sb * kKvQRows, make_sdesc(kb + ks * 32, 16, 8 * RB, SWZ),
+                     make_sdesc(qb + ks * 32, 16, 8 * RB, SWZ), idesc_st, ks > 0);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_f16(tm_dpt0 + sb * kKvQRows, make_sdesc(vb + ks * 32, 16, 8 * RB, SWZ),
+                     make_sdesc(dob + ks * 32, 16, 8 * RB, SWZ), idesc_st, ks > 0);
+          umma_commit(&st_full[sb]);
+          if (c >= 1 && !issue_acc(c - 1)) { ok = false; break; }
+        }
+        if (ok && n_chunks > 0) issue_acc(n_chunks - 1);
+      }
+      umma_commit(acc_done);
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ P^T / dS^T -----------------------------
+    const int r = threadIdx.x;  // key row
+    const bool row_valid = r < kt.n_q;
+    const int kidx = kt.q_start + r;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = prm.scale_log2, scale = prm.scale;
+    const float lse_mul = prm.lse_natural ? 1.4426950408889634f : 1.f;
+    bool ok = true;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int s = c % STAGES, sb = c & 1;
+      if (!mbar_wait(&st_full[sb], (c >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!mbar_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      const KvMeta& mt = meta[s];
+      if (!mbar_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float st[32], dpt[32];
+        tmem_ld32(tm_st0 + sb * kKvQRows + lane_base + x * 32, st);
+        tmem_ld32(tm_dpt0 + sb * kKvQRows + lane_base + x * 32, dpt);
+        tmem_wait_ld();
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const int col = x * 32 + cc;
+          bool valid = row_valid && col < mt.n_rows;
+          if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
+          const float p = valid ? ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul)) : 0.f;
+          st[cc] = p;
+          dpt[cc] = valid ? p * (dpt[cc] - mt.delta[col]) * scale : 0.f;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int ch = x * 4 + q8;
+          const uint32_t o = swz_offset<128>(r, ch);
+          st_shared_v4(pt + o, pack2<BF16>(st[q8 * 8], st[q8 * 8 + 1]), pack2<BF16>(st[q8 * 8 + 2], st[q8 * 8 + 3]),
+                       pack2<BF16>(st[q8 * 8 + 4], st[q8 * 8 + 5]), pack2<BF16>(st[q8 * 8 + 6], st[q8 * 8 + 7]));
+          st_shared_v4(dst + o, pack2<BF16>(dpt[q8 * 8], dpt[q8 * 8 + 1]),
+                       pack2<BF16>(dpt[q8 * 8 + 2], dpt[q8 * 8 + 3]), pack2<BF16>(dpt[q8 * 8 + 4], dpt[q8 * 8 + 5]),
+                       pack2<BF16>(dpt[q8 * 8 + 6], dpt[q8 * 8 + 7]));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&st_free[sb]);
+        mbar_arrive(&pds_full[sb]);
+      }
+    }
+    // epilogue: dK, dV of this key row
+    bool have = ok;
+    if (ok && n_chunks > 0) have = mbar_wait(acc_done, 0, abort_flag, prm.err);
+    if (have) {
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tm_acc = which == 0 ? tm_dk : tm_dv;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float v[32];
+          if (n_chunks > 0) {
+            tmem_ld32(tm_acc + lane_base + c0, v);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = 0.f;
+          }
+          if (!row_valid) continue;
+          if (prm.n_split > 1) {
+            float* dst_p = prm.partial +
+                           ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +
+                           (size_t)r * D + c0;
+#pragma unroll
+            for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst_p + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+          } else {
+            uint8_t* drow = static_cast<uint8_t*>(which == 0 ? prm.dk : prm.dv) +
+                            ((size_t)kidx * prm.kv_tok_stride + (size_t)h * D) * 2;
+#pragma unroll
+            for (int c = 0; c < 32; c += 8) {
+              uint4 pk;
+              pk.x = pack2<BF16>(v[c], v[c + 1]);
+              pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
+              pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
+              pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
+              *reinterpret_cast<uint4*>(drow + (c0 + c) * 2) = pk;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace lsrm

@@ -97,7 +97,7 @@ extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_sha
   p.tiles = plan.tiles;
   p.n_tiles = plan.n_tiles;
   p.union_cnt = plan.union_cnt;
-  p.union_nchunk = plan.union_nchunk;
+  p.union_ngroups = plan.union_ngroups;
   p.union_blk = plan.union_blk;
   p.union_mask = plan.union_mask;
   p.tiles_ub = plan.tiles_ub;

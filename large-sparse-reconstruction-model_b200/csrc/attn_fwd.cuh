@@ -31,7 +31,7 @@ struct FwdParams {
   const int* n_tiles;
   // select mode
   const int* union_cnt;
-  const int* union_nchunk;
+  const int* union_ngroups;
   const int* union_blk;
   const uint4* union_mask;
   int tiles_ub;
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (MODE == kSelect) {
     ubase = ((size_t)h * prm.tiles_ub + tile_idx) * prm.union_cap;
     U = prm.union_cnt[(size_t)h * prm.tiles_ub + tile_idx];
-    n_chunks = prm.union_nchunk[(size_t)h * prm.tiles_ub + tile_idx];
+    n_chunks = (prm.union_ngroups[(size_t)h * prm.tiles_ub + tile_idx] + kGroupsPerChunk - 1) / kGroupsPerChunk;
   } else {
     n_chunks = tile.kv_hi > tile.kv_lo ? (tile.kv_hi - tile.kv_lo + kKVChunk - 1) / kKVChunk : 0;
   }

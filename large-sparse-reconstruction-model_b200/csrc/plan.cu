@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kUnionThreads)
   block_exclusive_scan(groups, &gtotal, scratch);
   if (threadIdx.x == 0) {
     p.union_cnt[(size_t)h * p.tiles_ub + t] = U;
-    p.union_nchunk[(size_t)h * p.tiles_ub + t] = (gtotal + kGroupsPerChunk - 1) / kGroupsPerChunk;
+    p.union_ngroups[(size_t)h * p.tiles_ub + t] = gtotal;
   }
 }
 
@@ -386,7 +386,7 @@ SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int 
   p.tiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.tiles_ub));
   p.n_tiles = reinterpret_cast<int*>(take(16));
   p.union_cnt = reinterpret_cast<int*>(take(sizeof(int) * hkv * p.tiles_ub));
-  p.union_nchunk = reinterpret_cast<int*>(take(sizeof(int) * hkv * p.tiles_ub));
+  p.union_ngroups = reinterpret_cast<int*>(take(sizeof(int) * hkv * p.tiles_ub));
   p.union_blk = reinterpret_cast<int*>(take(sizeof(int) * ent));
   p.union_mask = reinterpret_cast<uint4*>(take(sizeof(uint4) * ent));
   p.kvtiles = reinterpret_cast<QTile*>(take(sizeof(QTile) * p.kvtiles_ub));

@@ -52,7 +52,7 @@ struct SelectPlan {
   QTile* tiles;
   int* n_tiles;            // [1]
   int* union_cnt;          // [hkv][tiles_ub]
-  int* union_nchunk;       // [hkv][tiles_ub]
+  int* union_ngroups;       // [hkv][tiles_ub] 8-token groups of the union
   int* union_blk;          // [hkv][tiles_ub][cap] global block ids
   uint4* union_mask;       // [hkv][tiles_ub][cap] query bits within the tile
   QTile* kvtiles;          // dK/dV tiles (one block's keys, <= 128)

@@ -2,21 +2,12 @@
 #include "attn_host.h"
 #include "host_util.h"
 
-namespace lsrm {
-size_t dense_bwd_extra_bytes(const lsrm_varlen*, const lsrm_attn_shape*, int) { return 0; }
-}  // namespace lsrm
 
 #define LSRM_STUB(name) \
   ::lsrm::set_error(#name " is not implemented in this build"); \
   return LSRM_ERR_UNSUPPORTED;
 
 extern "C" {
-int lsrm_select_attn_bwd(const lsrm_varlen*, const lsrm_attn_shape*, const void*, const void*, const void*,
-                         const void*, const float*, const void*, const int32_t*, int32_t, const int32_t*, int32_t,
-                         void*, void*, void*, float*, void*, size_t, int*, void*) { LSRM_STUB(lsrm_select_attn_bwd) }
-int lsrm_dense_attn_bwd(const lsrm_varlen*, const lsrm_attn_shape*, int32_t, int32_t, const void*, const void*,
-                        const void*, const void*, const float*, const void*, void*, void*, void*, float*, void*,
-                        size_t, int*, void*) { LSRM_STUB(lsrm_dense_attn_bwd) }
 int lsrm_block_topk(const lsrm_varlen*, const lsrm_attn_shape*, const void*, const void*, const float*, int32_t,
                     const int32_t*, int32_t, int32_t, float, int32_t*, int*, void*) { LSRM_STUB(lsrm_block_topk) }
 int lsrm_block_mean_fwd(int32_t, int32_t, int32_t, const int32_t*, const void*, int64_t, void*, void*) {
