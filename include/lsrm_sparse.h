@@ -166,10 +166,11 @@ int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, i
  * topk], the score of a query block being the float32 sum of its tokens'
  * scores in ascending token order; force_self always selects block j for
  * query block j of a sequence.  `q` may be fp16/bf16 (shape->dtype); ck has
- * the same dtype; lse_ln fp32. */
+ * the same dtype; lse_ln fp32.  sm_scale <= 0 selects 1/sqrt(D); the scale
+ * used is float(sm_scale * 1.44269504) evaluated in double. */
 int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
                     const float* lse_ln, int32_t topk, const int32_t* cu_query_blocks, int32_t num_query_blocks,
-                    int32_t force_self, float sm_scale, int32_t* block_topk, int* err_flags, void* stream);
+                    int32_t force_self, double sm_scale, int32_t* block_topk, int* err_flags, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Compression (SpatialSparseAttentionIn, spatial_sparse_attention.py:27-67) */

@@ -56,6 +56,9 @@ static int launch_dq(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap&
   if (D == 64)
     return bf16 ? launch_dq_t<64, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
                 : launch_dq_t<64, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
+  if (D == 16)
+    return bf16 ? launch_dq_t<16, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
+                : launch_dq_t<16, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
   return bf16 ? launch_dq_t<32, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
               : launch_dq_t<32, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
 }
@@ -83,6 +86,9 @@ static int launch_dkdv(int D, bool bf16, const CUtensorMap& mk, const CUtensorMa
   if (D == 64)
     return bf16 ? launch_dkdv_t<64, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
                 : launch_dkdv_t<64, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
+  if (D == 16)
+    return bf16 ? launch_dkdv_t<16, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
+                : launch_dkdv_t<16, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
   return bf16 ? launch_dkdv_t<32, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
               : launch_dkdv_t<32, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
 }

@@ -76,7 +76,7 @@ struct DqSmem {
   static constexpr int NBAR = 2 * STAGES + 1 + 8 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
-  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
 };
 
 // Fills the groups of one select-mode chunk by walking the union.
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(192, 1)
                    const DqParams prm) {
   using L = DqSmem<D, STAGES>;
   constexpr int RB = L::RB;
-  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
 
@@ -373,25 +373,23 @@ __global__ void __launch_bounds__(192, 1)
     if (have) {
       tc_fence_after();
       uint8_t* drow = static_cast<uint8_t*>(prm.dq) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
+      float v[D];
+      if (n_chunks > 0) {
+        tmem_load_cols<D>(tm_dq + lane_base, v);
+        tmem_wait_ld();
+      } else {
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        float v[32];
-        if (n_chunks > 0) {
-          tmem_ld32(tm_dq + lane_base + c0, v);
-          tmem_wait_ld();
-        } else {
+        for (int c = 0; c < D; ++c) v[c] = 0.f;
+      }
+      if (row_valid) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = 0.f;
-        }
-        if (!row_valid) continue;
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
+        for (int c = 0; c < D; c += 8) {
           uint4 pk;
           pk.x = pack2<BF16>(v[c], v[c + 1]);
           pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
           pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
           pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
-          *reinterpret_cast<uint4*>(drow + (c0 + c) * 2) = pk;
+          *reinterpret_cast<uint4*>(drow + c * 2) = pk;
         }
       }
     }
@@ -465,7 +463,7 @@ struct DkvSmem {
   static constexpr int NBAR = 1 + 2 * STAGES + 8 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 32;
-  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
 };
 
 // Number of query rows (queries x G) gathered for one KV tile (select mode).
@@ -491,7 +489,7 @@ __global__ void __launch_bounds__(192, 1)
                      const DkvParams prm) {
   using L = DkvSmem<D, STAGES>;
   constexpr int RB = L::RB;
-  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
 
   const int split = blockIdx.x % prm.n_split;
@@ -788,35 +786,33 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t tm_acc = which == 0 ? tm_dk : tm_dv;
+        float v[D];
+        if (n_chunks > 0) {
+          tmem_load_cols<D>(tm_acc + lane_base, v);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          float v[32];
-          if (n_chunks > 0) {
-            tmem_ld32(tm_acc + lane_base + c0, v);
-            tmem_wait_ld();
-          } else {
+          for (int c = 0; c < D; ++c) v[c] = 0.f;
+        }
+        if (!row_valid) continue;
+        if (prm.n_split > 1) {
+          float* dst_p = prm.partial +
+                         ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +
+                         (size_t)r * D;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] = 0.f;
-          }
-          if (!row_valid) continue;
-          if (prm.n_split > 1) {
-            float* dst_p = prm.partial +
-                           ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +
-                           (size_t)r * D + c0;
+          for (int c = 0; c < D; c += 4)
+            *reinterpret_cast<float4*>(dst_p + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+        } else {
+          uint8_t* drow = static_cast<uint8_t*>(which == 0 ? prm.dk : prm.dv) +
+                          ((size_t)kidx * prm.kv_tok_stride + (size_t)h * D) * 2;
 #pragma unroll
-            for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst_p + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-          } else {
-            uint8_t* drow = static_cast<uint8_t*>(which == 0 ? prm.dk : prm.dv) +
-                            ((size_t)kidx * prm.kv_tok_stride + (size_t)h * D) * 2;
-#pragma unroll
-            for (int c = 0; c < 32; c += 8) {
-              uint4 pk;
-              pk.x = pack2<BF16>(v[c], v[c + 1]);
-              pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
-              pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
-              pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
-              *reinterpret_cast<uint4*>(drow + (c0 + c) * 2) = pk;
-            }
+          for (int c = 0; c < D; c += 8) {
+            uint4 pk;
+            pk.x = pack2<BF16>(v[c], v[c + 1]);
+            pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
+            pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
+            pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
+            *reinterpret_cast<uint4*>(drow + c * 2) = pk;
           }
         }
       }

@@ -27,13 +27,17 @@ static int launch_fwd(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap
     return bf16 ? launch_fwd_t<64, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
                 : launch_fwd_t<64, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
   }
+  if (D == 16)
+    return bf16 ? launch_fwd_t<16, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
+                : launch_fwd_t<16, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
   return bf16 ? launch_fwd_t<32, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
               : launch_fwd_t<32, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
 }
 
 int check_shape(const lsrm_varlen* m, const lsrm_attn_shape* sh, int& G) {
   LSRM_CHECK_ARG(m && sh, "null metadata / shape");
-  LSRM_CHECK_ARG(sh->head_dim == 32 || sh->head_dim == 64, "head_dim must be 32 or 64 (got %d)", sh->head_dim);
+  LSRM_CHECK_ARG(sh->head_dim == 16 || sh->head_dim == 32 || sh->head_dim == 64, "head_dim must be 16, 32 or 64 (got %d)",
+                 sh->head_dim);
   LSRM_CHECK_ARG(sh->dtype == LSRM_DTYPE_BF16 || sh->dtype == LSRM_DTYPE_F16, "dtype must be bf16 or fp16");
   LSRM_CHECK_ARG(sh->num_kv_heads > 0 && sh->num_q_heads % sh->num_kv_heads == 0,
                  "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", sh->num_q_heads, sh->num_kv_heads);

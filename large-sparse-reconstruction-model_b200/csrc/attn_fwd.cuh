@@ -76,7 +76,7 @@ struct FwdSmem {
   static constexpr int NBAR = 2 * STAGES + 1 + 12 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
-  static constexpr int ALLOC = BYTES + 1024;  // alignment slack
+  static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(192, 1)
                     const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
   using L = FwdSmem<D, STAGES>;
   constexpr int RB = L::RB;
-  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
 
   const int tile_idx = blockIdx.x, h = blockIdx.y;
@@ -296,13 +296,12 @@ __global__ void __launch_bounds__(192, 1)
       const int pb = i & 1;
       if (!mbar_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
       tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        float pv[32];
-        tmem_ld32(tm_pv0 + pb * D + lane_base + c0, pv);
+      {
+        float pv[D];
+        tmem_load_cols<D>(tm_pv0 + pb * D + lane_base, pv);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) o[c0 + c] = fmaf(o[c0 + c], alpha_prev, pv[c]);
+        for (int c = 0; c < D; ++c) o[c] = fmaf(o[c], alpha_prev, pv[c]);
       }
       tc_fence_before();
       __syncwarp();

@@ -209,6 +209,27 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_type, uint32_t a_m
          ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// Dynamic shared memory requested by every kernel that allocates all 512
+// TMEM columns: more than half of an SM's 228 KB, so one CTA per SM.
+constexpr int kOneCtaPerSmSmem = 116 * 1024;
+
+// Swizzle mode matching a row of RB bytes (TMA box inner extent).
+__host__ __device__ constexpr uint64_t swz_for_row_bytes(int RB) {
+  return RB == 128 ? kSw128 : (RB == 64 ? kSw64 : kSw32);
+}
+
+// Loads N (16 or a multiple of 32) consecutive fp32 TMEM columns of this
+// warp's 32 lanes into v[0..N).
+template <int N>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* v) {
+  if constexpr (N == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; c += 32) tmem_ld32(taddr + c, v + c);
+  }
+}
+
 // Byte offset of the 16-byte chunk `chunk` of row `row` inside a tile whose
 // rows are `row_bytes` (= swizzle span: 128, 64 or 32) long, in the TMA /
 // UMMA swizzled layout (XOR of the 16-byte chunk index with the row index

@@ -16,7 +16,7 @@ __global__ void __launch_bounds__(192, 1)
                          float* __restrict__ c1, float* __restrict__ c2, int* err) {
   constexpr int RB = 2 * D;         // bytes per row of a / b / v tiles
   constexpr int TILE = 128 * RB;    // bytes per 128-row tile
-  constexpr uint64_t SWZ = (RB == 128) ? kSw128 : kSw64;
+  constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -89,11 +89,10 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
         for (int j = 0; j < 32; ++j) c1[row * 128 + c + j] = v[j];
       }
-      for (int c = 0; c < D; c += 32) {
-        tmem_ld32(tmem + lane_base + 128 + c, v);
-        tmem_wait_ld();
-        for (int j = 0; j < 32; ++j) c2[row * D + c + j] = v[j];
-      }
+      float w[D];
+      tmem_load_cols<D>(tmem + lane_base + 128, w);
+      tmem_wait_ld();
+      for (int j = 0; j < D; ++j) c2[row * D + j] = w[j];
     }
   }
   tc_fence_before();
@@ -110,7 +109,7 @@ using namespace lsrm;
 
 extern "C" int lsrm_umma_selftest(int32_t head_dim, const void* a, const void* b, const void* p, const void* v,
                                   float* c1, float* c2, int* err_flags, void* stream) {
-  LSRM_CHECK_ARG(head_dim == 32 || head_dim == 64, "head_dim must be 32 or 64, got %d", head_dim);
+  LSRM_CHECK_ARG(head_dim == 16 || head_dim == 32 || head_dim == 64, "head_dim must be 16, 32 or 64, got %d", head_dim);
   CUtensorMap ma, mb, mv;
   int rc;
   if ((rc = make_tmap_3d(&ma, a, head_dim, 1, 128, head_dim, 1, 128))) return rc;
@@ -122,6 +121,11 @@ extern "C" int lsrm_umma_selftest(int32_t head_dim, const void* a, const void* b
     LSRM_CUDA_TRY(cudaFuncSetAttribute(umma_selftest_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
     umma_selftest_kernel<64><<<1, 192, smem, s>>>(ma, mb, mv, static_cast<const __nv_bfloat16*>(p), c1, c2,
+                                                  err_flags);
+  } else if (head_dim == 16) {
+    LSRM_CUDA_TRY(cudaFuncSetAttribute(umma_selftest_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+    umma_selftest_kernel<16><<<1, 192, smem, s>>>(ma, mb, mv, static_cast<const __nv_bfloat16*>(p), c1, c2,
                                                   err_flags);
   } else {
     LSRM_CUDA_TRY(cudaFuncSetAttribute(umma_selftest_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,

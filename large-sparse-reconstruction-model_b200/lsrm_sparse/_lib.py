@@ -83,7 +83,7 @@ _SIGS = {
     ),
     "lsrm_block_topk": (
         c_int,
-        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_float,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, ctypes.c_double,
          c_void_p, c_void_p, c_void_p],
     ),
     "lsrm_block_mean_fwd": (c_int, [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),

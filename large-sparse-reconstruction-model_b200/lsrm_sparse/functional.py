@@ -1,0 +1,121 @@
+"""Autograd functions over the CUDA ops (every forward and backward runs in
+liblsrm_sparse.so; torch supplies memory, streams and the Linear GEMMs)."""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import ops
+
+
+def _meta(cu_seqlens_q, cu_seqlens_k, cu_seqblocks, cu_block_include_tokens):
+    return ops.Meta(cu_seqlens_q, cu_seqlens_k, cu_seqblocks, cu_block_include_tokens)
+
+
+class SelectAttnFn(torch.autograd.Function):
+    """Selected-block attention (native_sparse_attend, kvcentric.py:1281-1371)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, block_topk, meta, softmax_scale, cu_query_blocks):
+        out, lse, ws = ops.select_attn_fwd(q, k, v, block_topk, meta, softmax_scale, cu_query_blocks)
+        ctx.save_for_backward(q, k, v, out, lse, block_topk)
+        ctx.meta = meta
+        ctx.scale = softmax_scale
+        ctx.cqb = cu_query_blocks
+        ctx.ws = ws
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, dout, _dlse):
+        q, k, v, out, lse, block_topk = ctx.saved_tensors
+        dq, dk, dv = ops.select_attn_bwd(q, k, v, out, lse, dout, block_topk, ctx.meta, ctx.scale, ctx.cqb,
+                                         workspace=ctx.ws)
+        ctx.ws = None
+        return dq, dk, dv, None, None, None, None
+
+
+class DenseAttnFn(torch.autograd.Function):
+    """Compressed / intra-block / sliding-window attention."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, meta, mode, window, softmax_scale):
+        out, lse = ops.dense_attn_fwd(q, k, v, meta, mode, window, softmax_scale)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.meta, ctx.mode, ctx.window, ctx.scale = meta, mode, window, softmax_scale
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, dout, _dlse):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = ops.dense_attn_bwd(q, k, v, out, lse, dout, ctx.meta, ctx.mode, ctx.window, ctx.scale)
+        return dq, dk, dv, None, None, None, None
+
+
+class BlockMeanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cu_block_include_tokens):
+        ctx.save_for_backward(cu_block_include_tokens)
+        ctx.n = x.shape[0]
+        return ops.block_mean_fwd(x, cu_block_include_tokens)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (cu,) = ctx.saved_tensors
+        return ops.block_mean_bwd(dout, cu, ctx.n), None
+
+
+class ResNormMeanFn(torch.autograd.Function):
+    """block_mean(LayerNorm_fp32(x + h)) — the SparseResBlock epilogue fused
+    with the compression mean.  Gradient flows to x and h equally."""
+
+    @staticmethod
+    def forward(ctx, x, h, cu_block_include_tokens, eps):
+        out, _, mean, rstd = ops.resnorm_mean_fwd(x, h, cu_block_include_tokens, eps)
+        ctx.save_for_backward(x, h, cu_block_include_tokens, mean, rstd)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, h, cu, mean, rstd = ctx.saved_tensors
+        dr = ops.resnorm_mean_bwd(x, h, cu, mean, rstd, dout)
+        return dr, dr, None, None
+
+
+class GateMergeFn(torch.autograd.Function):
+    """sum_i sigmoid(z_i) * branch_i (per channel or per head)."""
+
+    @staticmethod
+    def forward(ctx, z, per_head, head_dim, *branches):
+        ctx.save_for_backward(z, *branches)
+        ctx.per_head, ctx.head_dim = per_head, head_dim
+        return ops.gate_merge_fwd(z, branches, per_head, head_dim)
+
+    @staticmethod
+    def backward(ctx, dout):
+        z, *branches = ctx.saved_tensors
+        dz, dbr = ops.gate_merge_bwd(z, branches, dout, ctx.per_head, ctx.head_dim)
+        return (dz, None, None, *dbr)
+
+
+def select_attention(q, k, v, block_topk, meta, softmax_scale=None, cu_query_blocks=None):
+    return SelectAttnFn.apply(q, k, v, block_topk, meta, softmax_scale, cu_query_blocks)
+
+
+def dense_attention(q, k, v, meta, mode, window=0, softmax_scale=None):
+    return DenseAttnFn.apply(q, k, v, meta, mode, window, softmax_scale)
+
+
+def block_mean(x, cu_block_include_tokens):
+    return BlockMeanFn.apply(x, cu_block_include_tokens)
+
+
+def resnorm_mean(x, h, cu_block_include_tokens, eps=1e-5):
+    return ResNormMeanFn.apply(x, h, cu_block_include_tokens, eps)
+
+
+def gate_merge(z, branches: Sequence[torch.Tensor], per_head=False, head_dim=0):
+    return GateMergeFn.apply(z, per_head, head_dim, *branches)

@@ -210,3 +210,109 @@ def umma_selftest(a, b, p, v):
                               _stream())
     check(rc, "lsrm_umma_selftest")
     return c1, c2
+
+
+# ---------------------------------------------------------------------------
+# Scoring, compression, gated merge
+# ---------------------------------------------------------------------------
+
+
+def block_topk(q, ck, lse_ln, topk: int, meta: Meta, cu_query_blocks=None, force_self: bool = False,
+               sm_scale: Optional[float] = None):
+    """Deterministic block selection; returns int32 [Hkv, rows, topk]."""
+    L = _lib.lib()
+    vl = meta.struct(q.shape[0], ck.shape[0])
+    sh = _shape(q, ck, None)
+    nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
+    rows = nqb if nqb else q.shape[0]
+    out = torch.empty(ck.shape[1], rows, topk, dtype=torch.int32, device=q.device)
+    cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
+    lse_ln = lse_ln.float().contiguous()
+    rc = L.lsrm_block_topk(ctypes.byref(vl), ctypes.byref(sh), _ptr(q), _ptr(ck), _ptr(lse_ln), int(topk), _ptr(cqb),
+                           nqb, int(bool(force_self)), float(sm_scale) if sm_scale else 0.0, _ptr(out),
+                           _ptr(_err_word(q.device)), _stream())
+    check(rc, "lsrm_block_topk")
+    return out
+
+
+def block_mean_fwd(x: torch.Tensor, cu_block_include_tokens: torch.Tensor) -> torch.Tensor:
+    """x [N, C] (row stride may exceed C) -> [nb, C]."""
+    L = _lib.lib()
+    assert x.dim() == 2 and x.stride(1) == 1
+    cu_ = _i32(cu_block_include_tokens)
+    nb = cu_.numel() - 1
+    out = torch.empty(nb, x.shape[1], dtype=x.dtype, device=x.device)
+    rc = L.lsrm_block_mean_fwd(nb, x.shape[1], _dtype_code(x), _ptr(cu_), _ptr(x), x.stride(0), _ptr(out), _stream())
+    check(rc, "lsrm_block_mean_fwd")
+    return out
+
+
+def block_mean_bwd(dout: torch.Tensor, cu_block_include_tokens: torch.Tensor, total_tokens: int) -> torch.Tensor:
+    L = _lib.lib()
+    dout = dout.contiguous()
+    cu_ = _i32(cu_block_include_tokens)
+    dx = torch.empty(total_tokens, dout.shape[1], dtype=dout.dtype, device=dout.device)
+    rc = L.lsrm_block_mean_bwd(cu_.numel() - 1, dout.shape[1], _dtype_code(dout), _ptr(cu_), int(total_tokens),
+                               _ptr(dout), _ptr(dx), _stream())
+    check(rc, "lsrm_block_mean_bwd")
+    return dx
+
+
+def resnorm_mean_fwd(x, h, cu_block_include_tokens, eps: float = 1e-5, want_y: bool = False):
+    """Returns (block_mean [nb, C], y or None, mean [N], rstd [N])."""
+    L = _lib.lib()
+    x = x.contiguous()
+    h = h.contiguous()
+    cu_ = _i32(cu_block_include_tokens)
+    nb = cu_.numel() - 1
+    N, C = x.shape
+    out = torch.empty(nb, C, dtype=x.dtype, device=x.device)
+    y = torch.empty_like(x) if want_y else None
+    mean = torch.empty(N, dtype=torch.float32, device=x.device)
+    rstd = torch.empty(N, dtype=torch.float32, device=x.device)
+    rc = L.lsrm_resnorm_mean_fwd(nb, N, C, _dtype_code(x), _ptr(cu_), _ptr(x), _ptr(h), float(eps), _ptr(y),
+                                 _ptr(out), _ptr(mean), _ptr(rstd), _stream())
+    check(rc, "lsrm_resnorm_mean_fwd")
+    return out, y, mean, rstd
+
+
+def resnorm_mean_bwd(x, h, cu_block_include_tokens, mean, rstd, dout):
+    L = _lib.lib()
+    cu_ = _i32(cu_block_include_tokens)
+    N, C = x.shape
+    dr = torch.empty_like(x)
+    rc = L.lsrm_resnorm_mean_bwd(cu_.numel() - 1, N, C, _dtype_code(x), _ptr(cu_), _ptr(x), _ptr(h), _ptr(mean),
+                                 _ptr(rstd), _ptr(dout.contiguous()), _ptr(dr), _stream())
+    check(rc, "lsrm_resnorm_mean_bwd")
+    return dr
+
+
+def _ptr_array(ts):
+    arr = (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    return arr
+
+
+def gate_merge_fwd(z, branches: Sequence[torch.Tensor], per_head: bool = False, head_dim: int = 0):
+    L = _lib.lib()
+    z = z.contiguous()
+    branches = [b.contiguous() for b in branches]
+    N, C = branches[0].shape
+    out = torch.empty(N, C, dtype=branches[0].dtype, device=z.device)
+    arr = _ptr_array(branches)
+    rc = L.lsrm_gate_merge_fwd(N, C, len(branches), int(per_head), int(head_dim), _dtype_code(z), _ptr(z), arr,
+                               _ptr(out), _stream())
+    check(rc, "lsrm_gate_merge_fwd")
+    return out
+
+
+def gate_merge_bwd(z, branches: Sequence[torch.Tensor], dout, per_head: bool = False, head_dim: int = 0):
+    L = _lib.lib()
+    z = z.contiguous()
+    branches = [b.contiguous() for b in branches]
+    N, C = branches[0].shape
+    dz = torch.empty_like(z)
+    dbr = [torch.empty_like(b) for b in branches]
+    rc = L.lsrm_gate_merge_bwd(N, C, len(branches), int(per_head), int(head_dim), _dtype_code(z), _ptr(z),
+                               _ptr_array(branches), _ptr(dout.contiguous()), _ptr(dz), _ptr_array(dbr), _stream())
+    check(rc, "lsrm_gate_merge_bwd")
+    return dz, dbr

@@ -317,8 +317,11 @@ def gate_merge(x, gate_weight, branches: Sequence[torch.Tensor], mode: str = "pe
 # ---------------------------------------------------------------------------
 
 _F32 = np.float32
-# Taylor coefficients of 2^f = exp(f·ln2) around 0, rounded to float32.
-_EXP2_COEF = [_F32(math.log(2.0) ** i / math.factorial(i)) for i in range(8)]
+# Taylor coefficients ln(2)^i / i! of 2^f = exp(f·ln2) around 0, rounded to
+# float32; stored as bit patterns so the CUDA scorer uses identical values.
+_EXP2_COEF_BITS = [0x3F800000, 0x3F317218, 0x3E75FDF0, 0x3D635847, 0x3C1D955B, 0x3AAEC3FF, 0x39218489, 0x377FE5FE]
+_EXP2_COEF = [np.array(b, dtype=np.uint32).view(_F32)[()] for b in _EXP2_COEF_BITS]
+assert all(abs(float(c) - math.log(2.0) ** i / math.factorial(i)) < 1e-7 for i, c in enumerate(_EXP2_COEF))
 
 
 def exp2_fixed(t: np.ndarray) -> np.ndarray:

@@ -1,0 +1,223 @@
+"""Scorer, compression, gated merge and the drop-in modules on the GPU."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.cases import cu, random_problem
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _cos(a, b):
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float((a @ b) / (a.norm() * b.norm() + 1e-30))
+
+
+def _score_inputs(seed, seq_q, seq_nb, Hq, Hkv, D):
+    g = torch.Generator().manual_seed(seed)
+    cq, cc = cu(seq_q), cu(seq_nb)
+    q = torch.randn(sum(seq_q), Hq, D, generator=g).bfloat16()
+    ck = torch.randn(sum(seq_nb), Hkv, D, generator=g).bfloat16()
+    _, lse = oracle.compressed_attention(q, ck, ck, cq, cc)
+    return q, ck, lse.float(), cq, cc
+
+
+@pytest.mark.parametrize("seq_q,seq_nb,Hq,Hkv,D,topk", [
+    ([37, 21], [9, 5], 4, 4, 32, 4),
+    ([200], [50], 8, 2, 64, 8),
+    ([19, 23], [3, 7], 2, 1, 32, 4),
+    ([64, 64], [40, 33], 16, 1, 64, 16),
+])
+def test_block_topk_per_token_bit_exact(seq_q, seq_nb, Hq, Hkv, D, topk):
+    from lsrm_sparse import api
+
+    q, ck, lse, cq, cc = _score_inputs(sum(seq_q), seq_q, seq_nb, Hq, Hkv, D)
+    got = api.get_block_score(q.to(DEV), ck.to(DEV), lse.to(DEV), topk, cq.to(DEV), cc.to(DEV))
+    ref = oracle.get_block_score_exact(q, ck, lse, topk, cq, cc)
+    assert torch.equal(got.cpu(), ref)
+
+
+@pytest.mark.parametrize("force_self", [False, True])
+def test_block_topk_query_block_bit_exact(force_self):
+    from lsrm_sparse import api
+
+    qb_lens = [[17, 40, 3, 64, 25], [30, 30, 12]]
+    seq_q = [sum(x) for x in qb_lens]
+    seq_nb = [len(x) for x in qb_lens]
+    q, ck, lse, cq, cc = _score_inputs(3, seq_q, seq_nb, 4, 2, 64)
+    cqb = cu([l for s in qb_lens for l in s])
+    got = api.get_block_score(q.to(DEV), ck.to(DEV), lse.to(DEV), 3, cq.to(DEV), cc.to(DEV),
+                              cu_query_blocks=cqb.to(DEV), force_self_block=force_self)
+    ref = oracle.get_block_score_qblock_exact(q, ck, lse, 3, cq, cc, cqb, force_self=force_self)
+    assert torch.equal(got.cpu(), ref)
+
+
+def test_block_topk_tie_lowest_id():
+    from lsrm_sparse import api
+
+    q = torch.randn(6, 2, 32).bfloat16()
+    ck = torch.randn(1, 1, 32).bfloat16().repeat(5, 1, 1)
+    lse = torch.zeros(2, 6)
+    cq = torch.tensor([0, 6], dtype=torch.int32)
+    cc = torch.tensor([0, 5], dtype=torch.int32)
+    got = api.get_block_score(q.to(DEV), ck.to(DEV), lse.to(DEV), 3, cq.to(DEV), cc.to(DEV))
+    assert (got.cpu()[0] == torch.tensor([0, 1, 2], dtype=torch.int32)).all()
+
+
+@pytest.mark.parametrize("name", ["score_g1", "score_g4", "score_few_blocks"])
+def test_block_topk_vs_reference_fixture(golden, name):
+    from lsrm_sparse import api
+
+    g = golden(name)
+    q = torch.from_numpy(g["q"]).bfloat16()  # values are bf16-exact
+    ck = torch.from_numpy(g["ck"]).bfloat16()
+    lse = torch.from_numpy(g["lse"])
+    cq = torch.from_numpy(g["cu_seqlens_q"])
+    cc = torch.from_numpy(g["compressed_cu_seqlens"])
+    got = api.get_block_score(q.to(DEV), ck.to(DEV), lse.to(DEV), int(g["topk"]), cq.to(DEV), cc.to(DEV)).cpu()
+    assert torch.equal(got, oracle.get_block_score_exact(q, ck, lse, int(g["topk"]), cq, cc))
+    ref = torch.from_numpy(g["block_topk"])
+    if not torch.equal(got, ref):  # only swaps of float64-tied scores allowed
+        scores = oracle.block_score_reference_formula(q.float(), ck.float(), lse, cq, cc)
+        cqn = cq.numpy()
+        for h, i in zip(*np.nonzero((got != ref).any(-1).numpy())):
+            b = np.searchsorted(cqn, i, side="right") - 1
+            s = scores[b][h, i - cqn[b]].numpy()
+            for x, y in zip(sorted(set(got[h, i].tolist()) - set(ref[h, i].tolist())),
+                            sorted(set(ref[h, i].tolist()) - set(got[h, i].tolist()))):
+                assert abs(s[x] - s[y]) <= 1e-6 * s.max()
+
+
+def test_block_mean_fwd_bwd():
+    from lsrm_sparse import functional as F
+
+    lens = [5, 1, 64, 130, 7, 0, 33]
+    cb = cu(lens)
+    x = torch.randn(sum(lens), 96).bfloat16().to(DEV).requires_grad_()
+    y = F.block_mean(x, cb.to(DEV))
+    ref = oracle.segment_mean(x.detach().cpu(), cb)
+    nonempty = torch.tensor([l > 0 for l in lens])
+    assert torch.isnan(y[~nonempty.to(DEV)]).all()
+    assert (y.float().cpu()[nonempty] - ref[nonempty]).abs().max() < 1e-2
+    g = torch.randn(y.shape, device=DEV).bfloat16()
+    g[~nonempty.to(DEV)] = 0
+    y.backward(g)
+    lens_t = torch.tensor(lens)
+    idx = torch.repeat_interleave(torch.arange(len(lens)), lens_t)
+    ref_dx = g.float().cpu()[idx] / lens_t[idx].float()[:, None]
+    assert (x.grad.float().cpu() - ref_dx).abs().max() < 1e-2
+
+
+def test_resblock_compression_vs_reference_fixture(golden):
+    from lsrm_sparse.module import SpatialSparseAttentionIn
+
+    g = golden("compress_resblock")
+    mod = SpatialSparseAttentionIn(head_dim=32, num_kv_heads=2)
+    sd = {k[2:]: torch.from_numpy(v) for k, v in g.items() if k.startswith("w:")}
+    mod.load_state_dict(sd)
+    mod = mod.to(DEV).bfloat16()
+    k = torch.from_numpy(g["k"]).to(DEV).bfloat16()
+    v = torch.from_numpy(g["v"]).to(DEV).bfloat16()
+    ck, cv = mod(k, v, {"cu_block_include_tokens": torch.from_numpy(g["cu_block_include_tokens"]).to(DEV)})
+    assert (ck.float().cpu() - torch.from_numpy(g["ck"])).abs().max() < 5e-2
+    assert (cv.float().cpu() - torch.from_numpy(g["cv"])).abs().max() < 5e-2
+    assert _cos(ck.float().cpu(), torch.from_numpy(g["ck"])) > 0.999
+
+
+def test_resnorm_mean_backward_vs_torch():
+    from lsrm_sparse.module import SparseResBlock
+
+    torch.manual_seed(0)
+    blk = SparseResBlock(128).to(DEV).bfloat16()
+    lens = [3, 50, 1, 17, 90]
+    cb = cu(lens).to(DEV)
+    x = torch.randn(sum(lens), 128, device=DEV).bfloat16().requires_grad_()
+    out = blk.forward_block_mean(x, cb)
+    g = torch.randn(out.shape, device=DEV).bfloat16()
+    out.backward(g)
+    gx = x.grad.clone()
+    gw = blk.act_layers[0].weight.grad.clone()
+    x2 = x.detach().float().requires_grad_()
+    blk32 = SparseResBlock(128).to(DEV)
+    blk32.load_state_dict({k: v.float() for k, v in blk.state_dict().items()})
+    y = blk32(x2)
+    lens_t = torch.tensor(lens, device=DEV)
+    idx = torch.repeat_interleave(torch.arange(len(lens), device=DEV), lens_t)
+    ref = torch.zeros(len(lens), 128, device=DEV).index_add_(0, idx, y) / lens_t[:, None]
+    assert (out.float() - ref).abs().max() < 3e-2
+    ref.backward(g.float())
+    assert _cos(gx.float(), x2.grad) > 0.999
+    assert _cos(gw.float(), blk32.act_layers[0].weight.grad) > 0.999
+
+
+@pytest.mark.parametrize("window", [False, True])
+def test_gate_module_vs_reference_fixture(golden, window):
+    from lsrm_sparse.module import SpatialSparseAttentionOut
+
+    g = golden("gate_window" if window else "gate_nowindow")
+    mod = SpatialSparseAttentionOut(hidden_dim=64, num_q_heads=4, num_kv_heads=2, is_window_attn=window)
+    mod.gate[0].weight.data = torch.from_numpy(g["gate_weight"])
+    mod = mod.to(DEV).bfloat16()
+    t = lambda n: torch.from_numpy(g[n]).to(DEV).bfloat16()  # noqa: E731
+    out = mod(t("x"), t("q"), t("k"), t("v"), {"cu_block_include_tokens": torch.from_numpy(
+        g["cu_block_include_tokens"]).to(DEV)}, {"selection_attn": t("selection"), "compressed_attn": t("compressed")})
+    ref = torch.from_numpy(g["out"])
+    assert (out.float().cpu() - ref).abs().max() < 5e-2
+    assert _cos(out.float().cpu(), ref) > 0.9995
+
+
+@pytest.mark.parametrize("per_head", [False, True])
+def test_gate_merge_backward_vs_torch(per_head):
+    from lsrm_sparse import functional as F
+
+    N, H, D, nbr = 300, 4, 16, 3
+    C = H * D
+    torch.manual_seed(1)
+    zw = nbr * (H if per_head else C)
+    z = torch.randn(N, zw, device=DEV).bfloat16().requires_grad_()
+    brs = [torch.randn(N, C, device=DEV).bfloat16().requires_grad_() for _ in range(nbr)]
+    out = F.gate_merge(z, brs, per_head=per_head, head_dim=D)
+    gz = torch.randn(N, C, device=DEV).bfloat16()
+    out.backward(gz)
+    z2 = z.detach().float().requires_grad_()
+    b2 = [b.detach().float().requires_grad_() for b in brs]
+    s = torch.sigmoid(z2)
+    ref = 0
+    for i, b in enumerate(b2):
+        gi = s[:, i * C:(i + 1) * C] if not per_head else s[:, i * H:(i + 1) * H].repeat_interleave(D, 1)
+        ref = ref + gi * b
+    ref.backward(gz.float())
+    assert (out.float() - ref).abs().max() < 3e-2
+    assert _cos(z.grad.float(), z2.grad) > 0.999
+    for a, b in zip(brs, b2):
+        assert _cos(a.grad.float(), b.grad) > 0.999
+
+
+def test_mid_module_end_to_end_vs_oracle():
+    """compressed attention -> per-token scoring -> selection, as
+    SpatialSparseAttentionMid runs them when block_topk is None."""
+    from lsrm_sparse.module import SpatialSparseAttentionMid
+
+    sbl = [[20, 33, 12, 9, 40, 16, 25]]
+    p = random_problem(21, sbl, 4, 2, 32, 3)
+    cb, cs, cq = p["cu_blk"], p["cu_seqblocks"], p["cu_seqlens"]
+    ck = oracle.segment_mean(p["k"].reshape(p["N"], -1), cb).reshape(-1, 2, 32).bfloat16()
+    cv = oracle.segment_mean(p["v"].reshape(p["N"], -1), cb).reshape(-1, 2, 32).bfloat16()
+    mid = SpatialSparseAttentionMid(hidden_dim=128, num_q_heads=4, num_kv_heads=2)
+    am = {"block_topk": None, "cu_seqblocks": cs.to(DEV), "cu_block_include_tokens": cb.to(DEV)}
+    out, info = mid(p["q"].to(DEV).reshape(p["N"], -1), cq.to(DEV), p["k"].to(DEV).reshape(p["N"], -1),
+                    ck.to(DEV).reshape(-1, 64), p["v"].to(DEV).reshape(p["N"], -1), cv.to(DEV).reshape(-1, 64), 3,
+                    am, return_sparse_info=True)
+    ref_c, lse = oracle.compressed_attention(p["q"], ck, cv, cq, cs)
+    assert (out["compressed_attn"].float().cpu() - ref_c.reshape(p["N"], -1)).abs().max() < 2e-2
+    # selection indices: exact given the kernel's own LSE (checked separately); here the
+    # oracle's fp64 LSE may differ in the last bits, so compare through the chosen set
+    bt = info["block_topk"].cpu()
+    ref_o, _ = oracle.selection_attention(p["q"], p["k"], p["v"], bt, cs, cb, cq, cq)
+    assert (out["selection_attn"].float().cpu() - ref_o.reshape(p["N"], -1)).abs().max() < 2e-2
+    ref_bt = oracle.get_block_score_exact(p["q"], ck, lse.float(), 3, cq, cs)
+    assert (bt == ref_bt).float().mean() > 0.98
