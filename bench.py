@@ -1,0 +1,469 @@
+"""Benchmark of the B200 variable-block native sparse attention (LSRM hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2]
+
+One step = forward + backward of the full three-branch sparse-attention op on
+one synthetic voxel sequence (BASELINE config 2 by default): block-mean
+compression of K/V, compressed attention, bit-exact per-query-block top-16
+scoring (own block forced), selected-block attention, sliding window 512,
+per-head sigmoid-gated merge, then the backward of everything.
+Rank r of N processes its own sequence (weak scaling, no collective on the
+data path).  Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "large-sparse-reconstruction-model_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "Sparse-attn TFLOP/s (fwd+bwd) & decoder tokens/s at 1/2/4/8 B200; % bf16 peak"
+
+CONFIGS = {
+    # the headline single-GPU workload
+    "cfg2": dict(n=131072, heads=16, head_dim=64, res=256, blk_min=64, blk_max=256, topk=16, window=512,
+                 gate="per_head", voxel=True),
+    # configs[0] at its sizes (contiguous uniform blocks), on the GPU
+    "cfg1": dict(n=4096, heads=8, head_dim=64, n_blocks=64, blk_min=32, blk_max=96, topk=8, window=128,
+                 gate="per_head", voxel=False),
+    # 512^3 shell, blocks 32-512, window 1024
+    "cfg3": dict(n=262144, heads=16, head_dim=64, res=512, blk_min=32, blk_max=512, topk=16, window=1024,
+                 gate="per_head", voxel=True),
+}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+
+def block_lengths(cfg, seed):
+    from lsrm_sparse import synth
+
+    if cfg["voxel"]:
+        w = synth.voxel_workload(cfg["n"], cfg["res"], cfg["blk_min"], cfg["blk_max"], seed)
+        return w.block_lens, w.shell_size
+    return synth.uniform_blocks(cfg["n"], cfg["n_blocks"], cfg["blk_min"], cfg["blk_max"], seed), cfg["n"]
+
+
+class Problem:
+    def __init__(self, cfg, seed, device, pin=True):
+        self.cfg = cfg
+        lens, self.shell = block_lengths(cfg, seed)
+        self.lens = lens
+        N, H, D = cfg["n"], cfg["heads"], cfg["head_dim"]
+        self.N, self.H, self.D, self.nb = N, H, D, len(lens)
+        self.hidden = H * D
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        pinned = (lambda t: t.pin_memory()) if pin else (lambda t: t)
+        # host copies (pinned) for the end-to-end path
+        self.h_q = pinned(torch.randn(N, H, D, generator=g).bfloat16())
+        self.h_k = pinned(torch.randn(N, H, D, generator=g).bfloat16())
+        self.h_v = pinned(torch.randn(N, H, D, generator=g).bfloat16())
+        self.h_x = pinned(torch.randn(N, self.hidden, generator=g).bfloat16())
+        self.h_g = pinned((torch.randn(N, self.hidden, generator=g) * 0.1).bfloat16())
+        n_gate = 3 * H if cfg["gate"] == "per_head" else 3 * self.hidden
+        self.gate_w = (torch.randn(n_gate, self.hidden, generator=g) / math.sqrt(self.hidden)).bfloat16()
+        cu_blk = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+        self.h_cu_blk = pinned(cu_blk)
+        self.h_cu_seq = pinned(torch.tensor([0, N], dtype=torch.int32))
+        self.h_cu_sb = pinned(torch.tensor([0, len(lens)], dtype=torch.int32))
+        self.device = device
+        if device != "cpu":
+            self.to_device()
+
+    def to_device(self, non_blocking=False):
+        d = self.device
+        self.q = self.h_q.to(d, non_blocking=non_blocking).requires_grad_()
+        self.k = self.h_k.to(d, non_blocking=non_blocking).requires_grad_()
+        self.v = self.h_v.to(d, non_blocking=non_blocking).requires_grad_()
+        self.x = self.h_x.to(d, non_blocking=non_blocking).requires_grad_()
+        self.g = self.h_g.to(d, non_blocking=non_blocking)
+        self.cu_blk = self.h_cu_blk.to(d, non_blocking=non_blocking)
+        self.cu_seq = self.h_cu_seq.to(d, non_blocking=non_blocking)
+        self.cu_sb = self.h_cu_sb.to(d, non_blocking=non_blocking)
+        if not hasattr(self, "wg"):
+            self.wg = self.gate_w.to(d).requires_grad_()
+
+    def h2d_bytes(self):
+        ts = (self.h_q, self.h_k, self.h_v, self.h_x, self.h_g, self.h_cu_blk, self.h_cu_seq, self.h_cu_sb)
+        return int(sum(t.numel() * t.element_size() for t in ts))
+
+
+def forward_backward(p: Problem, want_loss=False, capture=None):
+    """One step through the public API (lsrm_sparse.functional / ops)."""
+    from lsrm_sparse import functional as F
+    from lsrm_sparse import ops
+
+    cfg = p.cfg
+    N, H, D, nb = p.N, p.H, p.D, p.nb
+    meta = ops.Meta(p.cu_seq, p.cu_seq, p.cu_sb, p.cu_blk)
+    dummy = torch.arange(nb + 1, dtype=torch.int32, device=p.device) if not hasattr(p, "_cblk") else p._cblk
+    p._cblk = dummy
+    meta_c = ops.Meta(p.cu_seq, p.cu_seq, p.cu_sb, dummy)
+    ck = F.block_mean(p.k.view(N, H * D), p.cu_blk).view(nb, H, D)
+    cv = F.block_mean(p.v.view(N, H * D), p.cu_blk).view(nb, H, D)
+    o_c, lse = F.dense_attention(p.q, ck, cv, meta_c, ops.DENSE_COMPRESSED)
+    with torch.no_grad():
+        bt = ops.block_topk(p.q, ck, lse, cfg["topk"], meta_c, cu_query_blocks=p.cu_blk, force_self=True)
+    if capture is not None:
+        capture["block_topk"] = bt
+    o_s, _ = F.select_attention(p.q, p.k, p.v, bt, meta, None, p.cu_blk)
+    o_w, _ = F.dense_attention(p.q, p.k, p.v, meta, ops.DENSE_SLIDING, cfg["window"])
+    z = torch.nn.functional.linear(p.x, p.wg)
+    out = F.gate_merge(z, [o_c.view(N, -1), o_s.view(N, -1), o_w.view(N, -1)], per_head=cfg["gate"] == "per_head",
+                       head_dim=D)
+    loss = (out.float() * p.g.float()).sum() if want_loss else None
+    out.backward(p.g)
+    return loss
+
+
+def zero_grads(p: Problem):
+    for t in (p.q, p.k, p.v, p.x, p.wg):
+        t.grad = None
+
+
+def count_pairs(p: Problem, bt: torch.Tensor):
+    """Attended (query, key) pairs per head of the three branches."""
+    lens = torch.tensor(p.lens, dtype=torch.int64)
+    sel = bt.cpu().long()  # [H, nqb, k]
+    valid = sel >= 0
+    sel_len = torch.where(valid, lens[sel.clamp(min=0)], torch.zeros_like(sel)).sum(-1)  # [H, nqb]
+    sel_pairs = (sel_len * lens[None]).sum().item()  # summed over heads
+    comp_pairs = p.N * p.nb * p.H
+    half = p.cfg["window"] // 2
+    i = torch.arange(p.N, dtype=torch.int64)
+    band = (torch.clamp(i + half, max=p.N - 1) - torch.clamp(i - half, min=0) + 1).sum().item()
+    slide_pairs = band * p.H
+    return dict(select=sel_pairs, compressed=comp_pairs, sliding=slide_pairs)
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        rows = []
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), sm_max=float(f[2]), power=float(f[3]), active=f[4], hw=f[5],
+                                 hw_th=f[6], sw_th=f[7], sw_pc=f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        pmax = max(r["power"] for r in rows)
+        load = [r for r in rows if r["power"] > 0.5 * pmax] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hw_th", "hw_thermal_slowdown"),
+                              ("sw_th", "sw_thermal_slowdown"), ("sw_pc", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["sm_max"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(load), "power_w_max": pmax}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle restatement on the host cores)
+# ---------------------------------------------------------------------------
+
+
+def cpu_sample(p: Problem, n_qblocks: int, seed: int):
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(seed)
+    qbs = sorted(rng.choice(p.nb, size=min(n_qblocks, p.nb), replace=False).tolist())
+    t0 = time.perf_counter()
+    _, flops = oracle.three_branch_sample_step(p.h_q, p.h_k, p.h_v, p.h_x, p.gate_w, p.h_g, p.h_cu_blk, qbs,
+                                               p.cfg["topk"], p.cfg["window"], per_head=p.cfg["gate"] == "per_head")
+    dt = time.perf_counter() - t0
+    tokens = int(sum(p.lens[i] for i in qbs))
+    return dict(value=flops / dt / 1e12, unit="TFLOP/s", cores=torch.get_num_threads(), kind="port",
+                sample=f"{len(qbs)} of {p.nb} query blocks ({tokens} of {p.N} queries), three-branch fwd+bwd "
+                       f"incl. exact scoring, fp32 torch on {torch.get_num_threads()} host threads",
+                seconds=dt)
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    p = Problem(cfg, args.seed, "cpu", pin=False)  # host tensors only
+    for _ in range(args.warmup):
+        cpu_sample(p, args.cpu_qblocks, args.seed)
+    vals, secs = [], []
+    for i in range(args.steps):
+        r = cpu_sample(p, args.cpu_qblocks, args.seed + 1 + i)
+        vals.append(r["value"])
+        secs.append(r["seconds"])
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-sphere SDF shell voxels, Morton octree blocks)",
+        "config": workload_config(cfg, p),
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line, default=_json_default), flush=True)
+
+
+def workload_config(cfg, p):
+    return {"workload": f"three-branch sparse attention fwd+bwd, N={cfg['n']} voxel tokens, H={cfg['heads']}, "
+                        f"d={cfg['head_dim']}, top-{cfg['topk']} per query block, window {cfg['window']}",
+            "tokens": cfg["n"], "heads": cfg["heads"], "head_dim": cfg["head_dim"], "blocks": p.nb,
+            "block_len": [min(p.lens), max(p.lens)], "topk": cfg["topk"], "window": cfg["window"],
+            "gate": cfg["gate"], "selection": "per query block, bit-exact fp32 score, own block forced",
+            "l2": "inputs larger than L2 (q/k/v 268 MB each)", "grid_res": cfg.get("res")}
+
+
+def kernel_flops(name, pairs, H, D, N, nb):
+    """Algorithmic FLOPs of one launch of a profiled kernel (pairs summed
+    over heads): forward 4d, dQ pass 6d (QK^T, dO V^T, dS K), dK/dV pass 8d
+    (K Q^T, V dO^T, P^T dO, dS^T Q) per attended pair."""
+    table = {"select": pairs["select"], "range": pairs["compressed"], "sliding": pairs["sliding"]}
+    for kind, mult in (("attn_fwd_", 4), ("attn_dq_", 6), ("attn_dkdv_", 8)):
+        if name.startswith(kind):
+            return mult * D * table[name[len(kind):]], "tensor"
+    return None, None
+
+
+def run_ours(args, cfg):
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    from lsrm_sparse import _lib, ops
+
+    lib_launches = _lib.launch_count
+    p = Problem(cfg, args.seed + rank, dev)
+    cap = {}
+    forward_backward(p, capture=cap)
+    zero_grads(p)
+    err = ops.read_errors()
+    if err:
+        raise RuntimeError(f"device error bits 0x{err:x} in the first step")
+    pairs = count_pairs(p, cap["block_topk"])
+    flops_step = 14.0 * p.D * (pairs["select"] + pairs["compressed"] + pairs["sliding"])
+    for _ in range(max(args.warmup - 1, 0)):
+        forward_backward(p)
+        zero_grads(p)
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    # ---- timed pass (device time, CUDA events on the compute stream) ----
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = lib_launches()
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            forward_backward(p)
+            zero_grads(p)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = lib_launches() - n0
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = ms
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = ws * flops_step / (ms_max * 1e-3) / 1e12
+
+    # ---- profiled pass: per-kernel device time (events on the launching stream) ----
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        forward_backward(p)
+        zero_grads(p)
+    torch.cuda.synchronize()
+    prof = _lib.profile_collect()
+    _lib.profile_enable(False)
+    peaks, peak_kind = load_peaks()
+    total_prof = sum(v[0] for v in prof.values())
+    kernels = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
+                   "share": v[0] / total_prof if total_prof else None} for k, v in sorted(prof.items())}
+    attn = {k: v for k, v in prof.items() if kernel_flops(k, pairs, p.H, p.D, p.N, p.nb)[0] is not None}
+    dom = max(attn.items(), key=lambda kv: kv[1][0])[0] if attn else None
+    roofline = None
+    if dom is not None:
+        fl, bound = kernel_flops(dom, pairs, p.H, p.D, p.N, p.nb)
+        avg_ms = prof[dom][0] / prof[dom][1]
+        achieved = fl / (avg_ms * 1e-3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": traffic_for(dom),
+                    "peak_source": f"bf16_tflops_sustained of {peak_kind} (kernel timed inside a long step)"}
+    slowest = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+
+    # ---- end to end through the public API: H2D inputs, D2H loss ----
+    e2e = None
+    if not args.no_e2e:
+        e_steps = max(2, min(args.steps, 5))
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            p.to_device(non_blocking=True)
+            loss = forward_backward(p, want_loss=True)
+            float(loss.item())  # device -> host read of the step's result
+            zero_grads(p)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / e_steps
+        if ws > 1:
+            t = torch.tensor([e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": ws * flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": p.h2d_bytes(), "d2h_bytes_per_step": 4}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_sample(p, args.cpu_qblocks, args.seed)
+        cpu.pop("seconds", None)
+
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: seeded random-sphere SDF shell ({p.shell} shell voxels, subsampled), Morton octree "
+                "blocks; q/k/v N(0,1), grad N(0,0.1)",
+        "config": workload_config(cfg, p),
+        "tokens_per_s": ws * p.N / (ms_max * 1e-3),
+        "flops_per_step": flops_step,
+        "pairs_per_step": pairs,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "kernels": kernels,
+        "slowest_kernel": slowest,
+    }
+    print(json.dumps(line, default=_json_default), flush=True)
+
+
+def _json_default(o):
+    if hasattr(o, "item"):
+        return o.item()
+    return str(o)
+
+
+def traffic_for(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if
+    one exists (profiles/traffic.json: {kernel: bytes_per_launch})."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-qblocks", type=int, default=24)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -86,6 +86,17 @@ const char* lsrm_last_error(void);
  * entry points, all threads); used by benchmarks to count launches. */
 uint64_t lsrm_launch_count(void);
 
+/* Kernel timing (tracing): while enabled, every entry point records a CUDA
+ * event pair on its stream around each kernel it launches.
+ * lsrm_profile_enable(1) starts (and clears), lsrm_profile_collect()
+ * synchronises on the recorded events and folds them into per-kernel totals
+ * (returns the number of distinct kernels, or < 0), lsrm_profile_get() reads
+ * one total.  Off by default; no reference counterpart (the reference times
+ * with host wall clocks, test_lrm_vol_sparse.py:1374-1401). */
+void lsrm_profile_enable(int on);
+int lsrm_profile_collect(void);
+int lsrm_profile_get(int index, char* name, int name_cap, double* total_ms, uint64_t* launches);
+
 /* ---------------------------------------------------------------------- */
 /* Selected-block attention (the reference's NSA op)                        */
 /* ---------------------------------------------------------------------- */

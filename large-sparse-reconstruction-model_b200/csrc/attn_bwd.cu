@@ -44,6 +44,7 @@ static int launch_dq_t(const CUtensorMap& mq, const CUtensorMap& mdo, const CUte
   using L = DqSmem<D, STAGES>;
   auto kern = attn_dq_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  ProfScope ps(MODE == kSelect ? "attn_dq_select" : (MODE == kBand ? "attn_dq_sliding" : "attn_dq_range"), s);
   kern<<<dim3(grid_x, hkv), 192, L::ALLOC, s>>>(mq, mdo, mk, mv, p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
@@ -70,9 +71,13 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
   using L = DkvSmem<D, STAGES>;
   auto kern = attn_dkdv_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
-  kern<<<dim3(grid_x * p.n_split, hkv), 192, L::ALLOC, s>>>(mk, mv, mq, mdo, p);
-  LSRM_LAUNCH_CHECK();
+  {
+    ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
+    kern<<<dim3(grid_x * p.n_split, hkv), 192, L::ALLOC, s>>>(mk, mv, mq, mdo, p);
+    LSRM_LAUNCH_CHECK();
+  }
   if (p.n_split > 1) {
+    ProfScope ps("dkdv_split_reduce", s);
     dkdv_reduce_kernel_d<BF16, D><<<dim3(grid_x, hkv, 2), 256, 0, s>>>(p);
     LSRM_LAUNCH_CHECK();
   }
@@ -95,6 +100,7 @@ static int launch_dkdv(int D, bool bf16, const CUtensorMap& mk, const CUtensorMa
 
 static int launch_zero_tail(void* dk, void* dv, const int32_t* start, long long total, long long stride,
                             int row_elems, cudaStream_t s) {
+  ProfScope ps("zero_tail", s);
   zero_tail_kernel<<<148, 256, 0, s>>>(static_cast<uint16_t*>(dk), static_cast<uint16_t*>(dv), start, total, stride,
                                        row_elems);
   LSRM_LAUNCH_CHECK();

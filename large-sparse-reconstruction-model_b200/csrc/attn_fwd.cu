@@ -14,6 +14,7 @@ static int launch_fwd_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUte
   using L = FwdSmem<D, STAGES>;
   auto kern = attn_fwd_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  ProfScope ps(MODE == kSelect ? "attn_fwd_select" : (MODE == kBand ? "attn_fwd_sliding" : "attn_fwd_range"), s);
   kern<<<dim3(grid_x, hkv), 192, L::ALLOC, s>>>(mq, mk, mv, p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;

@@ -355,6 +355,7 @@ extern "C" int lsrm_block_mean_fwd(int32_t num_blocks, int32_t channels, int32_t
   if (num_blocks <= 0) return LSRM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int threads = std::min(256, std::max(32, (channels / 8 + 31) / 32 * 32));
+  ProfScope ps("block_mean_fwd", s);
   DISPATCH_T(dtype, (block_mean_fwd_kernel<T><<<num_blocks, threads, 0, s>>>(
                         cu_block_include_tokens, static_cast<const T*>(x), x_stride, static_cast<T*>(out), channels,
                         num_blocks)));
@@ -370,6 +371,7 @@ extern "C" int lsrm_block_mean_bwd(int32_t num_blocks, int32_t channels, int32_t
   if (total_tokens > 0) LSRM_CUDA_TRY(cudaMemsetAsync(dx, 0, (size_t)total_tokens * channels * 2, s));
   if (num_blocks <= 0) return LSRM_OK;
   const int threads = std::min(256, std::max(32, (channels / 8 + 31) / 32 * 32));
+  ProfScope ps("block_mean_bwd", s);
   DISPATCH_T(dtype, (block_mean_bwd_kernel<T><<<num_blocks, threads, 0, s>>>(
                         cu_block_include_tokens, static_cast<const T*>(dout), static_cast<T*>(dx), channels,
                         num_blocks)));
@@ -386,6 +388,7 @@ extern "C" int lsrm_resnorm_mean_fwd(int32_t num_blocks, int32_t total_tokens, i
   if (num_blocks <= 0) return LSRM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int threads = std::max(32, (channels / 8 + 31) / 32 * 32);
+  ProfScope ps("resnorm_mean_fwd", s);
   DISPATCH_T(dtype, (resnorm_mean_fwd_kernel<T><<<num_blocks, threads, 0, s>>>(
                         cu_block_include_tokens, static_cast<const T*>(x), static_cast<const T*>(h), channels, eps,
                         static_cast<T*>(y), static_cast<T*>(out), mean, rstd, num_blocks)));
@@ -402,6 +405,7 @@ extern "C" int lsrm_resnorm_mean_bwd(int32_t num_blocks, int32_t total_tokens, i
   if (total_tokens > 0) LSRM_CUDA_TRY(cudaMemsetAsync(dr, 0, (size_t)total_tokens * channels * 2, s));
   if (num_blocks <= 0) return LSRM_OK;
   const int threads = std::max(32, (channels / 8 + 31) / 32 * 32);
+  ProfScope ps("resnorm_mean_bwd", s);
   DISPATCH_T(dtype, (resnorm_mean_bwd_kernel<T><<<num_blocks, threads, 0, s>>>(
                         cu_block_include_tokens, static_cast<const T*>(x), static_cast<const T*>(h), channels, mean,
                         rstd, static_cast<const T*>(dout), static_cast<T*>(dr), num_blocks)));
@@ -421,6 +425,7 @@ extern "C" int lsrm_gate_merge_fwd(int32_t total_tokens, int32_t channels, int32
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long work = (long long)total_tokens * (channels / 8);
   const int H = per_head ? channels / head_dim : 0;
+  ProfScope ps("gate_merge_fwd", s);
   DISPATCH_T(dtype, if (per_head) gate_merge_fwd_kernel<T, true><<<grid_for(work, 256), 256, 0, s>>>(
                         total_tokens, channels, n_branch, H, head_dim, static_cast<const T*>(z), a,
                         static_cast<T*>(out));
@@ -447,6 +452,7 @@ extern "C" int lsrm_gate_merge_bwd(int32_t total_tokens, int32_t channels, int32
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long work = (long long)total_tokens * (channels / 8);
   const int H = per_head ? channels / head_dim : 0;
+  ProfScope ps("gate_merge_bwd", s);
   DISPATCH_T(dtype, if (per_head) gate_merge_bwd_kernel<T, true><<<grid_for(work, 256), 256, 0, s>>>(
                         total_tokens, channels, n_branch, H, head_dim, static_cast<const T*>(z), a,
                         static_cast<const T*>(dout), static_cast<T*>(dz));

@@ -2,6 +2,8 @@
 
 #include <cstdarg>
 #include <mutex>
+#include <string>
+#include <vector>
 
 namespace lsrm {
 
@@ -68,9 +70,95 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int D, int n_head, long lon
   return LSRM_OK;
 }
 
+// ------------------------------ profiler ----------------------------------
+struct ProfRecord {
+  std::string name;
+  cudaEvent_t start, stop;
+};
+static std::mutex g_prof_mu;
+static std::vector<ProfRecord> g_prof_records;
+static std::atomic<int> g_prof_on{0};
+struct ProfTotal {
+  std::string name;
+  double ms;
+  uint64_t launches;
+};
+static std::vector<ProfTotal> g_prof_totals;
+
+ProfScope::ProfScope(const char* name, cudaStream_t s) : stream_(s) {
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  ProfRecord r;
+  r.name = name;
+  if (cudaEventCreate(&r.start) != cudaSuccess) return;
+  if (cudaEventCreate(&r.stop) != cudaSuccess) {
+    cudaEventDestroy(r.start);
+    return;
+  }
+  cudaEventRecord(r.start, s);
+  std::lock_guard<std::mutex> g(g_prof_mu);
+  slot_ = (int)g_prof_records.size();
+  g_prof_records.push_back(r);
+}
+
+ProfScope::~ProfScope() {
+  if (slot_ < 0) return;
+  cudaEvent_t stop;
+  {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    stop = g_prof_records[slot_].stop;
+  }
+  cudaEventRecord(stop, stream_);
+}
+
 }  // namespace lsrm
 
 extern "C" {
+
+void lsrm_profile_enable(int on) {
+  std::lock_guard<std::mutex> g(lsrm::g_prof_mu);
+  for (auto& r : lsrm::g_prof_records) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  lsrm::g_prof_records.clear();
+  lsrm::g_prof_totals.clear();
+  lsrm::g_prof_on.store(on ? 1 : 0);
+}
+
+int lsrm_profile_collect(void) {
+  std::lock_guard<std::mutex> g(lsrm::g_prof_mu);
+  for (auto& r : lsrm::g_prof_records) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess) {
+      lsrm::set_error("profile: event query failed");
+      return -1;
+    }
+    bool found = false;
+    for (auto& t : lsrm::g_prof_totals)
+      if (t.name == r.name) {
+        t.ms += ms;
+        t.launches += 1;
+        found = true;
+        break;
+      }
+    if (!found) lsrm::g_prof_totals.push_back({r.name, (double)ms, 1});
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  lsrm::g_prof_records.clear();
+  return (int)lsrm::g_prof_totals.size();
+}
+
+int lsrm_profile_get(int index, char* name, int name_cap, double* total_ms, uint64_t* launches) {
+  std::lock_guard<std::mutex> g(lsrm::g_prof_mu);
+  if (index < 0 || index >= (int)lsrm::g_prof_totals.size()) return LSRM_ERR_INVALID_ARG;
+  const auto& t = lsrm::g_prof_totals[index];
+  if (name && name_cap > 0) snprintf(name, name_cap, "%s", t.name.c_str());
+  if (total_ms) *total_ms = t.ms;
+  if (launches) *launches = t.launches;
+  return LSRM_OK;
+}
+
 
 int lsrm_abi_version(void) { return LSRM_ABI_VERSION; }
 

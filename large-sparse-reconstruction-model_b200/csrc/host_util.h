@@ -49,6 +49,19 @@ inline void count_launch(uint64_t n = 1) { g_launch_count.fetch_add(n, std::memo
     }                                                                                  \
   } while (0)
 
+// Kernel timing: while profiling is enabled (lsrm_profile_enable), a
+// ProfScope records a CUDA event pair on the launching stream around the
+// launches made in its lifetime, keyed by name.
+class ProfScope {
+ public:
+  ProfScope(const char* name, cudaStream_t s);
+  ~ProfScope();
+
+ private:
+  int slot_ = -1;
+  cudaStream_t stream_;
+};
+
 // Encodes a 3-D tiled tensor map over a [n_tok, n_head, D] 16-bit tensor:
 // dims {D, n_head, n_tok}, strides in elements (head stride D, token stride
 // `tok_stride`), box {D, box_h, box_n}, swizzle matched to the row size

@@ -424,6 +424,7 @@ DensePlan make_dense_plan(const lsrm_varlen* m, int G, int mode, void* ws) {
 
 int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int rows_per_tile, const lsrm_varlen* m,
                        const int32_t* cu_segments, int n_segments, int window, int* err, cudaStream_t s) {
+  ProfScope ps("plan_tiles", s);
   build_tiles_kernel<<<1, 1024, 0, s>>>(tiles, n_tiles, tiles_ub, kind, rows_per_tile, *m, cu_segments, n_segments,
                                         window, err);
   LSRM_LAUNCH_CHECK();
@@ -447,12 +448,14 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
   }
   LSRM_CUDA_TRY(cudaFuncSetAttribute(build_unions_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid(p.tiles_ub, p.hkv);
+  ProfScope ps("plan_unions", s);
   build_unions_kernel<<<grid, kUnionThreads, smem, s>>>(p, *m, block_topk, topk, sel_rows, G, err);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }
 
 int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s) {
+  ProfScope ps("plan_reverse", s);
   LSRM_CUDA_TRY(cudaMemsetAsync(p.rev_off, 0, sizeof(int) * p.hkv * ((size_t)p.num_blocks + 1), s));
   dim3 grid(p.tiles_ub, p.hkv);
   rev_count_kernel<<<grid, 128, 0, s>>>(p);

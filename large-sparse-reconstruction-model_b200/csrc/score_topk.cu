@@ -209,6 +209,7 @@ template <typename T, int D>
 static int launch_topk_t(const ScoreParams& p, int rows, int hkv, size_t smem, cudaStream_t s) {
   LSRM_CUDA_TRY(
       cudaFuncSetAttribute(block_topk_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  ProfScope ps("block_topk", s);
   block_topk_kernel<T, D><<<dim3(rows, hkv), kScoreThreads, smem, s>>>(p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;

@@ -59,6 +59,10 @@ _SIGS = {
     "lsrm_abi_version": (c_int, []),
     "lsrm_last_error": (ctypes.c_char_p, []),
     "lsrm_launch_count": (c_uint64, []),
+    "lsrm_profile_enable": (None, [c_int]),
+    "lsrm_profile_collect": (c_int, []),
+    "lsrm_profile_get": (c_int, [c_int, ctypes.c_char_p, c_int, ctypes.POINTER(ctypes.c_double),
+                                 ctypes.POINTER(c_uint64)]),
     "lsrm_select_workspace_bytes": (c_size_t, [c_void_p, c_void_p, c_int32, c_int32]),
     "lsrm_select_attn_fwd": (
         c_int,
@@ -153,3 +157,23 @@ def check(rc: int, what: str = "") -> None:
 
 def launch_count() -> int:
     return int(lib().lsrm_launch_count())
+
+
+def profile_enable(on: bool = True) -> None:
+    lib().lsrm_profile_enable(1 if on else 0)
+
+
+def profile_collect() -> dict:
+    """Per-kernel totals {name: (total_ms, launches)} since profile_enable."""
+    L = lib()
+    n = L.lsrm_profile_collect()
+    if n < 0:
+        raise LsrmError(L.lsrm_last_error().decode())
+    out = {}
+    buf = ctypes.create_string_buffer(128)
+    for i in range(n):
+        ms = ctypes.c_double()
+        cnt = c_uint64()
+        check(L.lsrm_profile_get(i, buf, 128, ctypes.byref(ms), ctypes.byref(cnt)), "lsrm_profile_get")
+        out[buf.value.decode()] = (ms.value, int(cnt.value))
+    return out

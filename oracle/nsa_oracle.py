@@ -52,6 +52,7 @@ __all__ = [
     "build_tile_unions",
     "selection_flops",
     "dense_attention_flops",
+    "three_branch_sample_step",
 ]
 
 
@@ -578,3 +579,88 @@ def selection_flops(block_topk, cu_seqblocks, cu_block_include_tokens, cu_seqlen
 
 def dense_attention_flops(pairs: int, num_q_heads: int, head_dim: int) -> float:
     return 4.0 * head_dim * num_q_heads * pairs
+
+
+# ---------------------------------------------------------------------------
+# Bounded CPU sample of the three-branch op (the benchmark's CPU baseline)
+# ---------------------------------------------------------------------------
+
+
+def three_branch_sample_step(q, k, v, x, gate_w, g, cu_blk, qblock_ids, topk, window, per_head=True,
+                             force_self=True):
+    """float32 CPU forward + backward of the three-branch op for the query
+    blocks ``qblock_ids`` of a single-sequence problem (keys gathered per
+    query block), the restatement that the benchmark times on the host cores.
+
+    Branches (gates in this order): compressed attention over the block means
+    of K/V (spatial_sparse_attention.py:27-37, :121-143), selected blocks by
+    the query-block score of ``get_block_score_qblock_exact`` with
+    ``force_self`` (block_score.py:16-98 aggregated per query block), sliding
+    window ``|i-j| <= window//2``; sigmoid-gated merge (:257-269, per head when
+    ``per_head``).  Returns (loss, algorithmic flops of the attention
+    branches, 14·d per attended (query head, key) pair).
+    """
+    N, H, D = q.shape
+    nb = cu_blk.numel() - 1
+    cb = _i(cu_blk)
+    lens = torch.tensor(np.diff(np.array(cb)), dtype=torch.float32)
+    qf = q.detach().float().requires_grad_()
+    kf = k.detach().float().requires_grad_()
+    vf = v.detach().float().requires_grad_()
+    xf = x.detach().float().requires_grad_()
+    wf = gate_w.detach().float().requires_grad_()
+    blk_of = torch.repeat_interleave(torch.arange(nb), lens.long())
+    ck = torch.zeros(nb, H, D).index_add(0, blk_of, kf) / lens[:, None, None]
+    cv = torch.zeros(nb, H, D).index_add(0, blk_of, vf) / lens[:, None, None]
+    scale = 1.0 / math.sqrt(D)
+    half = window // 2
+    loss = 0.0
+    pairs = 0
+    for qb in qblock_ids:
+        r0, r1 = cb[qb], cb[qb + 1]
+        L = r1 - r0
+        qq = qf[r0:r1]  # [L, H, D]
+        # compressed branch (natural-log LSE kept for scoring)
+        sc = torch.einsum("lhd,bhd->hlb", qq, ck) * scale
+        lse = torch.logsumexp(sc, -1)  # [H, L]
+        o_c = torch.einsum("hlb,bhd->lhd", torch.softmax(sc, -1), cv)
+        pairs += L * nb
+        # scoring (bit-exact restatement) for this query block
+        cq = torch.tensor([0, L], dtype=torch.int32)
+        cc = torch.tensor([0, nb], dtype=torch.int32)
+        cqb = torch.tensor([0, L], dtype=torch.int32)
+        tok = token_block_scores_exact(qq.detach(), ck.detach(), lse.detach(), cq, cc)[0]  # [H, L, nb]
+        fixed = []
+        for h in range(H):
+            agg = np.zeros(nb, dtype=_F32)
+            for t in range(L):
+                agg = (agg + tok[h, t]).astype(_F32)
+            force = np.array([qb]) if force_self else None
+            row = _topk_lowest_id(agg[None], topk, force)[0]
+            fixed.append([int(t) for t in row if t >= 0])
+        o_s = []
+        for h in range(H):
+            keys = torch.cat([torch.arange(cb[b], cb[b + 1]) for b in fixed[h]])
+            s = (qq[:, h] @ kf[keys, h].t()) * scale
+            o_s.append(torch.softmax(s, -1) @ vf[keys, h])
+            pairs += L * keys.numel()
+        o_s = torch.stack(o_s, 1)
+        # sliding window
+        k0, k1 = max(0, r0 - half), min(N, r1 + half)
+        idx_q = torch.arange(r0, r1)[:, None]
+        idx_k = torch.arange(k0, k1)[None, :]
+        band = (idx_q - idx_k).abs() <= half
+        s = torch.einsum("lhd,khd->hlk", qq, kf[k0:k1]) * scale
+        s = s.masked_fill(~band[None], float("-inf"))
+        o_w = torch.einsum("hlk,khd->lhd", torch.softmax(s, -1), vf[k0:k1])
+        pairs += int(band.sum())
+        # gated merge
+        z = torch.sigmoid(xf[r0:r1] @ wf.t())
+        branches = [o_c, o_s, o_w]
+        out = 0
+        for i, br in enumerate(branches):
+            gi = z[:, i * H:(i + 1) * H, None] if per_head else z[:, i * H * D:(i + 1) * H * D].view(L, H, D)
+            out = out + gi * br
+        loss = loss + (out.reshape(L, -1) * g[r0:r1].float()).sum()
+    loss.backward()
+    return float(loss.detach()), 14.0 * D * H * pairs
