@@ -132,6 +132,25 @@ int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, 
                          int32_t num_query_blocks, void* dq, void* dk, void* dv, float* delta, void* workspace,
                          size_t workspace_bytes, int* err_flags, void* stream);
 
+/* Scratch size of lsrm_select_attn_fwd_noalloc: 16 MiB of device memory that
+ * every GPU loading this library holds until the process exits. */
+#define LSRM_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* lsrm_select_attn_fwd without allocation or caller workspace.  No
+ * counterpart in the reference: it exists for callers that may not allocate
+ * device memory (plugin hosts that own every device allocation, latency-bound
+ * loops that must not enter the driver allocator).  Same inputs, outputs and
+ * results as lsrm_select_attn_fwd; the selection plan lives in a fixed
+ * LSRM_NOALLOC_SCRATCH_BYTES device array inside the library.  Problems whose
+ * plan exceeds it are rejected with LSRM_ERR_WORKSPACE and a message.  The
+ * first call on each device resolves the array's device address (make that
+ * first call before any stream capture); all calls share the array, so calls
+ * that overlap on the GPU race on it. */
+int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q,
+                                 const void* k, const void* v, const int32_t* block_topk, int32_t topk,
+                                 const int32_t* cu_query_blocks, int32_t num_query_blocks, void* out,
+                                 float* lse_log2, int* err_flags, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Dense-range branches                                                     */
 /* ---------------------------------------------------------------------- */

@@ -1,5 +1,6 @@
 // Host entry points of the forward attention paths.
 #include <cmath>
+#include <mutex>
 
 #include "attn_fwd.cuh"
 #include "attn_host.h"
@@ -188,4 +189,136 @@ extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shap
   if (mode == LSRM_DENSE_SLIDING)
     return launch_fwd<kBand>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
   return launch_fwd<kRange>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+}
+
+// ---------------------------------------------------------------------------
+// Selected-block forward without any allocation
+//
+// For callers that may not allocate device memory themselves: plugin hosts
+// that own every device allocation (an inference server's fixed arena, another
+// framework's operator interface), and latency-critical loops that must not
+// call the driver allocator (cudaMalloc can synchronise the device and stall).
+// The plan scratch (query tiles and per-tile block unions) lives in one
+// file-scope device array that every GPU loading this library holds until the
+// process exits.  Every call shares it and it keeps the previous call's
+// contents; calls that overlap on the GPU (different streams, different host
+// threads) race on it.
+// ---------------------------------------------------------------------------
+
+namespace lsrm {
+
+static __device__ __align__(256) uint8_t g_select_fwd_scratch[LSRM_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the scratch array, resolved once per device on the first
+// call made with that device current (host code cannot use the symbol itself:
+// on the host it names a stand-in, not device memory).
+static int noalloc_scratch_ptr(void** out) {
+  static std::mutex mu;
+  static void* cache[128] = {};
+  int dev = 0;
+  LSRM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 128) {
+    set_error("device ordinal %d out of range", dev);
+    return LSRM_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    LSRM_CUDA_TRY(cudaGetSymbolAddress(&p, g_select_fwd_scratch));
+    cache[dev] = p;
+  }
+  *out = cache[dev];
+  return LSRM_OK;
+}
+
+}  // namespace lsrm
+
+extern "C" int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q,
+                                            const void* k, const void* v, const int32_t* block_topk, int32_t topk,
+                                            const int32_t* cu_query_blocks, int32_t num_query_blocks, void* out,
+                                            float* lse_log2, int* err_flags, void* stream) {
+  int G = 1, rc;
+  if ((rc = check_shape(meta, shape, G))) return rc;
+  LSRM_CHECK_ARG(topk >= 1 && topk <= 64, "topk must be in [1, 64] (got %d)", topk);
+  LSRM_CHECK_ARG(num_query_blocks == 0 || cu_query_blocks, "num_query_blocks > 0 needs cu_query_blocks");
+  // forward-only carve of the selection plan: tiles, tile count, unions
+  SelectPlan plan = make_select_plan(meta, G, shape->num_kv_heads, topk, num_query_blocks, nullptr);
+  const size_t hkv = (size_t)shape->num_kv_heads;
+  const size_t ent = hkv * plan.tiles_ub * plan.union_cap;
+  size_t need = 0;
+  auto carve_off = [&](size_t bytes) {
+    const size_t off = need;
+    need += align_up(bytes, 256);
+    return off;
+  };
+  const size_t o_tiles = carve_off(sizeof(QTile) * plan.tiles_ub);
+  const size_t o_ntiles = carve_off(16);
+  const size_t o_cnt = carve_off(sizeof(int) * hkv * plan.tiles_ub);
+  const size_t o_ngroups = carve_off(sizeof(int) * hkv * plan.tiles_ub);
+  const size_t o_blk = carve_off(sizeof(int) * ent);
+  const size_t o_mask = carve_off(sizeof(uint4) * ent);
+  const size_t o_err = carve_off(sizeof(int));
+  if (need > (size_t)LSRM_NOALLOC_SCRATCH_BYTES) {
+    set_error("lsrm_select_attn_fwd_noalloc: this problem needs %zu bytes of plan scratch, more than the fixed %zu; "
+              "use lsrm_select_attn_fwd with a caller-provided workspace",
+              need, (size_t)LSRM_NOALLOC_SCRATCH_BYTES);
+    return LSRM_ERR_WORKSPACE;
+  }
+  if (meta->total_q == 0) return LSRM_OK;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch_ptr(&scratch))) return rc;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  plan.tiles = reinterpret_cast<QTile*>(base + o_tiles);
+  plan.n_tiles = reinterpret_cast<int*>(base + o_ntiles);
+  plan.union_cnt = reinterpret_cast<int*>(base + o_cnt);
+  plan.union_ngroups = reinterpret_cast<int*>(base + o_ngroups);
+  plan.union_blk = reinterpret_cast<int*>(base + o_blk);
+  plan.union_mask = reinterpret_cast<uint4*>(base + o_mask);
+  plan.kvtiles = nullptr;
+  plan.n_kvtiles = nullptr;
+  plan.rev_off = nullptr;
+  plan.rev_cursor = nullptr;
+  plan.rev_entries = nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* err = err_flags;
+  if (!err) {  // the internal error word must start clear on every call
+    err = reinterpret_cast<int*>(base + o_err);
+    LSRM_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+  }
+  const int qpt = kRows / G;
+  const bool qblock = num_query_blocks > 0;
+  if ((rc = launch_build_tiles(plan.tiles, plan.n_tiles, plan.tiles_ub, qblock ? kTilesQBlock : kTilesSeq, qpt, meta,
+                               cu_query_blocks, qblock ? num_query_blocks : meta->num_seqs, 0, err, s)))
+    return rc;
+  if ((rc = launch_build_unions(plan, meta, block_topk, topk, qblock ? num_query_blocks : meta->total_q, G, err, s)))
+    return rc;
+  const int D = shape->head_dim;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
+  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+    return rc;
+  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+    return rc;
+  FwdParams p{};
+  p.tiles = plan.tiles;
+  p.n_tiles = plan.n_tiles;
+  p.union_cnt = plan.union_cnt;
+  p.union_ngroups = plan.union_ngroups;
+  p.union_blk = plan.union_blk;
+  p.union_mask = plan.union_mask;
+  p.tiles_ub = plan.tiles_ub;
+  p.union_cap = plan.union_cap;
+  p.cu_block_include_tokens = meta->cu_block_include_tokens;
+  p.out = out;
+  p.lse = lse_log2;
+  p.q_tok_stride = shape->q_token_stride;
+  p.num_q_heads = shape->num_q_heads;
+  p.total_q = meta->total_q;
+  p.total_k = meta->total_k;
+  p.G = G;
+  p.scale_log2 = softmax_scale_of(shape) * 1.44269504f;
+  p.half_window = 0;
+  p.lse_natural = 0;
+  p.err = err;
+  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
 }

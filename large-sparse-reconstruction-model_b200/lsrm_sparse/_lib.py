@@ -74,6 +74,11 @@ _SIGS = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
          c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "lsrm_select_attn_fwd_noalloc": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p,
+         c_void_p, c_void_p, c_void_p],
+    ),
     "lsrm_dense_workspace_bytes": (c_size_t, [c_void_p, c_void_p, c_int32]),
     "lsrm_dense_attn_fwd": (
         c_int,
