@@ -308,8 +308,8 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int j = 0; j < n_chunks; ++j) {
       const int s = j % STAGES, sb = j & 1;
-      if (!mbar_wait(&sd_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&sd_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       const DqMeta& mt = meta[s];
       uint32_t vm[2];
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(192, 1)
           vm[x] = e;
         }
       }
-      if (!mbar_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     // every lane takes part in the warp-collective TMEM loads; only valid rows store
     bool have = ok;
-    if (ok && n_chunks > 0) have = mbar_wait(dq_done, 0, abort_flag, prm.err);
+    if (ok && n_chunks > 0) have = warp_wait(dq_done, 0, abort_flag, prm.err);
     if (have) {
       tc_fence_after();
       uint8_t* drow = static_cast<uint8_t*>(prm.dq) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
@@ -419,6 +419,10 @@ struct DkvParams {
   int tiles_ub;
   int union_cap;
   int num_blocks;
+  // query-side operands, gathered row by row with cp.async
+  const void* q;
+  const void* dout;
+  long long q_tok_stride;
   // per-row statistics [Hq, Nq]
   const float* lse;
   const float* delta;
@@ -440,7 +444,8 @@ struct DkvParams {
 struct KvMeta {
   float lse2[kKvQRows];
   float delta[kKvQRows];
-  int qidx[kKvQRows];  // query token of each row (-1: padding)
+  int qidx[kKvQRows];   // query token of each row (-1: padding)
+  int qlist[kKvQRows];  // query tokens of the chunk (G rows each)
   int n_rows;
   int pad[3];
 };
@@ -485,7 +490,6 @@ __device__ __forceinline__ int count_select_queries(const DkvParams& prm, int h,
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const DkvParams prm) {
   using L = DkvSmem<D, STAGES>;
   constexpr int RB = L::RB;
@@ -570,110 +574,110 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 4) {
     // ------------------------------ producer ------------------------------
+    // K/V tile by TMA; query rows gathered with 16-byte cp.async by all 32
+    // lanes (any row pattern at full LSU rate), lse/delta with 4-byte
+    // cp.async; chunk c is published LAG chunks later, after wait_group and a
+    // generic->async proxy fence.
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
       tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
       tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
     }
-    // select-mode walk state (lane 0 walks, all lanes issue the gathers)
+    constexpr int CPR = RB / 16;  // 16-byte chunks per row
+    constexpr int LAG = STAGES - 2;
+    const uint8_t* qbase = static_cast<const uint8_t*>(prm.q);
+    const uint8_t* dobase = static_cast<const uint8_t*>(prm.dout);
     const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
     const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
     int e = 0, e_end = 0, tq0 = 0;
-    uint32_t wbits[4] = {0u, 0u, 0u, 0u};
+    uint32_t w0 = 0u, w1 = 0u, w2 = 0u, w3 = 0u;  // uniform across the warp
     if constexpr (MODE == kSelect) {
       e = off[kt.seg] - 1;
       e_end = off[kt.seg + 1];
     }
-    int issued = 0;
+    auto publish = [&](int cc) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_full[cc % STAGES]);
+    };
+    int issued = 0, published = 0;
     for (int c = 0; c < n_chunks; ++c) {
       const int s = c % STAGES;
-      if (!mbar_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+      if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
       KvMeta& mt = meta[s];
-      uint8_t* dQ = sQ + s * L::QTILE;
-      uint8_t* dDO = sDO + s * L::QTILE;
+      int n = 0;
       if constexpr (MODE == kSelect) {
-        if (lane == 0) {
-          int n = 0;
-          while (n < qpc) {
-            if ((wbits[0] | wbits[1] | wbits[2] | wbits[3]) == 0u) {
-              if (e + 1 >= e_end) break;
-              ++e;
-              const int2 x = ent[e];
-              const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-              wbits[0] = m.x;
-              wbits[1] = m.y;
-              wbits[2] = m.z;
-              wbits[3] = m.w;
-              tq0 = prm.qtiles[x.x].q_start;
-              continue;
-            }
-            int w = 0;
-            while (wbits[w] == 0u) ++w;
-            const int b = __ffs(wbits[w]) - 1;
-            wbits[w] &= wbits[w] - 1u;
-            mt.qidx[n] = tq0 + w * 32 + b;  // per query for now; expanded below
-            ++n;
+        while (n < qpc) {
+          if ((w0 | w1 | w2 | w3) == 0u) {
+            if (e + 1 >= e_end) break;
+            ++e;
+            const int2 x = ent[e];
+            const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+            w0 = m.x;
+            w1 = m.y;
+            w2 = m.z;
+            w3 = m.w;
+            tq0 = prm.qtiles[x.x].q_start;
+            continue;
           }
-          mt.n_rows = n * G;
-          for (int i = n; i < qpc; ++i) mt.qidx[i] = -1;
+          const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
+          const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
+          const bool bit = (word >> lane) & 1u;
+          const int rank = __popc(word & ((1u << lane) - 1u));
+          const bool take = bit && rank < qpc - n;
+          if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
+          const uint32_t taken = __ballot_sync(0xffffffffu, take);
+          n += __popc(taken);
+          if (wi == 0) w0 &= ~taken;
+          else if (wi == 1) w1 &= ~taken;
+          else if (wi == 2) w2 &= ~taken;
+          else w3 &= ~taken;
         }
-        __syncwarp();
-        // expand per-query entries to rows, gather Q / dO, lse / delta
-        int myq[2];
-        for (int i = 0; i < 2; ++i) {
-          const int slot = lane + 32 * i;
-          myq[i] = slot < qpc ? mt.qidx[slot] : -1;
-        }
-        __syncwarp();
-        for (int i = 0; i < 2; ++i) {
-          const int slot = lane + 32 * i;
-          if (slot < qpc) {
-            const int q = myq[i];
-            for (int g = 0; g < G; ++g) {
-              const int row = slot * G + g;
-              mt.qidx[row] = q;
-              mt.lse2[row] = q >= 0 ? prm.lse[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
-              mt.delta[row] = q >= 0 ? prm.delta[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
-            }
-          }
-        }
-        __threadfence_block();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&q_full[s], 2 * L::QTILE);
-        __syncwarp();
-        for (int i = 0; i < 2; ++i) {
-          const int slot = lane + 32 * i;
-          if (slot < qpc) {
-            const int q = myq[i] >= 0 ? myq[i] : prm.total_q;  // padding rows read zeros
-            tma_load_3d(dQ + slot * G * RB, &tm_q, 0, h * G, q, &q_full[s]);
-            tma_load_3d(dDO + slot * G * RB, &tm_do, 0, h * G, q, &q_full[s]);
-          }
-        }
+        for (int i = n + lane; i < qpc; i += 32) mt.qlist[i] = -1;
       } else {
         const int q0 = q_lo + c * qpc;
-        const int nq = min(qpc, q_hi - q0);
-        for (int row = lane; row < kKvQRows; row += 32) {
-          const int ql = row / G, g = row % G;
-          const int q = ql < nq ? q0 + ql : -1;
-          mt.qidx[row] = q;
-          mt.lse2[row] = q >= 0 ? prm.lse[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
-          mt.delta[row] = q >= 0 ? prm.delta[(size_t)(h * G + g) * prm.total_q + q] : 0.f;
-        }
-        if (lane == 0) mt.n_rows = nq * G;
-        __threadfence_block();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&q_full[s], 2 * L::QTILE);
-          tma_load_3d(dQ, &tm_q, 0, h * G, q0, &q_full[s]);
-          tma_load_3d(dDO, &tm_do, 0, h * G, q0, &q_full[s]);
+        n = max(0, min(qpc, q_hi - q0));
+        for (int i = lane; i < qpc; i += 32) mt.qlist[i] = i < n ? q0 + i : -1;
+      }
+      if (lane == 0) mt.n_rows = n * G;
+      __syncwarp();
+      for (int row = lane; row < kKvQRows; row += 32) {
+        const int q = mt.qlist[row / G], g = row % G;
+        mt.qidx[row] = q;
+        if (q >= 0) {
+          const size_t si = (size_t)(h * G + g) * prm.total_q + q;
+          cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
+          cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+        } else {
+          mt.lse2[row] = 0.f;
+          mt.delta[row] = 0.f;
         }
       }
+      const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
+      for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
+        const int row = idx / CPR, j = idx % CPR;
+        const int q = mt.qlist[row / G], g = row % G;
+        const uint32_t o = swz_offset<RB>(row, j);
+        if (q >= 0) {
+          const size_t src = ((size_t)q * prm.q_tok_stride + (size_t)(h * G + g) * D) * 2 + (size_t)j * 16;
+          cp_async_16(dq_s + o, qbase + src);
+          cp_async_16(ddo_s + o, dobase + src);
+        } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
+          st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
+          st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+        }
+      }
+      cp_async_commit();
       issued = c + 1;
+      if (c >= LAG) {
+        cp_async_wait<LAG>();
+        publish(c - LAG);
+        published = c - LAG + 1;
+      }
     }
-    if (lane == 0 && *abort_flag) {
-      mbar_wait_drain(kv_full, 0);
-      for (int c = max(0, issued - STAGES); c < issued; ++c) mbar_wait_drain(&q_full[c % STAGES], (c / STAGES) & 1);
-    }
+    cp_async_wait<0>();
+    for (int cc = published; cc < issued; ++cc) publish(cc);
+    if (lane == 0 && *abort_flag) mbar_wait_drain(kv_full, 0);
     __syncwarp();
   } else if (warp == 5) {
     // ------------------------------ MMA issuer -----------------------------
@@ -738,11 +742,12 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int c = 0; c < n_chunks; ++c) {
       const int s = c % STAGES, sb = c & 1;
-      if (!mbar_wait(&st_full[sb], (c >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!mbar_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&st_full[sb], (c >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       const KvMeta& mt = meta[s];
-      if (!mbar_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      const int n_rows = mt.n_rows;
+      if (!warp_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
@@ -753,9 +758,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int cc = 0; cc < 32; ++cc) {
           const int col = x * 32 + cc;
-          bool valid = row_valid && col < mt.n_rows;
+          bool valid = row_valid && col < n_rows;
           if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
-          const float p = valid ? ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul)) : 0.f;
+          // unconditional ex2, then select: a conditional asm call becomes a branch per element
+          const float e = ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul));
+          const float p = valid ? e : 0.f;
           st[cc] = p;
           dpt[cc] = valid ? p * (dpt[cc] - mt.delta[col]) * scale : 0.f;
         }
@@ -780,7 +787,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     // epilogue: dK, dV of this key row
     bool have = ok;
-    if (ok && n_chunks > 0) have = mbar_wait(acc_done, 0, abort_flag, prm.err);
+    if (ok && n_chunks > 0) have = warp_wait(acc_done, 0, abort_flag, prm.err);
     if (have) {
       tc_fence_after();
 #pragma unroll

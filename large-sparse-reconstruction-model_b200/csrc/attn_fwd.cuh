@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(192, 1)
 
     auto fold_pv = [&](int i) -> bool {
       const int pb = i & 1;
-      if (!mbar_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
+      if (!warp_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
       tc_fence_after();
       {
         float pv[D];
@@ -311,8 +311,8 @@ __global__ void __launch_bounds__(192, 1)
 
     for (int j = 0; j < n_chunks; ++j) {
       const int s = j % STAGES, sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       // key-validity mask of this row for the 128 columns of the chunk
       uint32_t vm[4];
@@ -350,14 +350,13 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld32(tm_s + x * 32, sv);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if ((vm[x] >> c) & 1u) mx = fmaxf(mx, sv[c]);
+        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[x] >> c) & 1u) ? sv[c] : -INFINITY);
       }
       const float m_new = fmaxf(m, mx * sl2);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
       // pass 2: probabilities -> P (shared, K-major 128B swizzle)
-      if (!mbar_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       float rowsum = 0.f;
       const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES);
 #pragma unroll
@@ -367,7 +366,8 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float pv = ((vm[x] >> c) & 1u) ? ex2(fmaf(sv[c], sl2, -m_use)) : 0.f;
+          const float e = ex2(fmaf(sv[c], sl2, -m_use));  // unconditional: no branch per element
+          const float pv = ((vm[x] >> c) & 1u) ? e : 0.f;
           sv[c] = pv;
           rowsum += pv;
         }

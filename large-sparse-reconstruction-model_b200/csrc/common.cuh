@@ -94,6 +94,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform wait: every lane polls, the warp proceeds only if all lanes
+// saw the phase complete (so warp-collective instructions that follow never
+// run with lanes diverged on an abort path).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err));
+}
+
 // ------------------------------- TMA ----------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -263,6 +270,19 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
+}
+
+// Ampere-style asynchronous copies (global -> shared, through L2).
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ float ex2(float x) {
