@@ -73,7 +73,7 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const Dkv
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   {
     ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
-    kern<<<dim3(grid_x * p.n_split, hkv), 192, L::ALLOC, s>>>(mk, mv, p);
+    kern<<<dim3(grid_x * p.n_split, hkv), kDkvThreads, L::ALLOC, s>>>(mk, mv, p);
     LSRM_LAUNCH_CHECK();
   }
   if (p.n_split > 1) {

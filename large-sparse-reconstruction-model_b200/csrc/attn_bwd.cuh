@@ -487,8 +487,14 @@ __device__ __forceinline__ int count_select_queries(const DkvParams& prm, int h,
   return n;
 }
 
+// Threads of the dK/dV kernel: 8 compute warps (two per TMEM lane quarter,
+// splitting the 64 query columns of a chunk), a producer warp, an MMA warp.
+constexpr int kDkvThreads = 320;
+constexpr int kDkvProducerWarp = 8;
+constexpr int kDkvMmaWarp = 9;
+
 template <int D, bool BF16, int MODE, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kDkvThreads, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const DkvParams prm) {
   using L = DkvSmem<D, STAGES>;
@@ -537,7 +543,7 @@ __global__ void __launch_bounds__(192, 1)
     q_lo = min(kt.kv_lo + split * per, kt.kv_hi);
     q_hi = min(q_lo + per, kt.kv_hi);
   }
-  if (warp == 4) {
+  if (warp == kDkvProducerWarp) {
     int nqueries;
     if constexpr (MODE == kSelect) nqueries = count_select_queries(prm, h, kt.seg);
     else nqueries = max(q_hi - q_lo, 0);
@@ -551,8 +557,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 1);
-      mbar_init(&st_free[i], 4);
-      mbar_init(&pds_full[i], 4);
+      mbar_init(&st_free[i], 8);
+      mbar_init(&pds_full[i], 8);
       mbar_init(&pds_free[i], 1);
     }
     mbar_init(acc_done, 1);
@@ -569,10 +575,11 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_chunks = *s_nchunks;
+  const int lg_g = __ffs(G) - 1;  // G is a power of two
   // TMEM: St0 [0,64) St1 [64,128) dPt0 [128,192) dPt1 [192,256) dK [256,256+D) dV [256+D, 256+2D)
   const uint32_t tm_st0 = tmem, tm_dpt0 = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 256 + D;
 
-  if (warp == 4) {
+  if (warp == kDkvProducerWarp) {
     // ------------------------------ producer ------------------------------
     // K/V tile by TMA; query rows gathered with 16-byte cp.async by all 32
     // lanes (any row pattern at full LSU rate), lse/delta with 4-byte
@@ -642,7 +649,7 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mt.n_rows = n * G;
       __syncwarp();
       for (int row = lane; row < kKvQRows; row += 32) {
-        const int q = mt.qlist[row / G], g = row % G;
+        const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
         mt.qidx[row] = q;
         if (q >= 0) {
           const size_t si = (size_t)(h * G + g) * prm.total_q + q;
@@ -653,10 +660,12 @@ __global__ void __launch_bounds__(192, 1)
           mt.delta[row] = 0.f;
         }
       }
+      __syncwarp();
       const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
+#pragma unroll 4
       for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
-        const int row = idx / CPR, j = idx % CPR;
-        const int q = mt.qlist[row / G], g = row % G;
+        const int row = idx / CPR, j = idx % CPR;  // CPR is a power of two
+        const int q = mt.qidx[row], g = row & (G - 1);
         const uint32_t o = swz_offset<RB>(row, j);
         if (q >= 0) {
           const size_t src = ((size_t)q * prm.q_tok_stride + (size_t)(h * G + g) * D) * 2 + (size_t)j * 16;
@@ -679,7 +688,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int cc = published; cc < issued; ++cc) publish(cc);
     if (lane == 0 && *abort_flag) mbar_wait_drain(kv_full, 0);
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kDkvMmaWarp) {
     // ------------------------------ MMA issuer -----------------------------
     if (lane == 0) {
       const uint32_t idesc_st = make_idesc(AB, 0, 0, 128, kKvQRows);
@@ -733,10 +742,12 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------ P^T / dS^T -----------------------------
-    const int r = threadIdx.x;  // key row
+    // warp w: key rows 32*(w%4).., query columns 32*(w/4).. of each chunk
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;  // key row
     const bool row_valid = r < kt.n_q;
     const int kidx = kt.q_start + r;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2, scale = prm.scale;
     const float lse_mul = prm.lse_natural ? 1.4426950408889634f : 1.f;
     bool ok = true;
@@ -747,79 +758,74 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const KvMeta& mt = meta[s];
       const int n_rows = mt.n_rows;
+      float st[32], dpt[32];
+      tmem_ld32(tm_st0 + sb * kKvQRows + lane_base + half * 32, st);
+      tmem_ld32(tm_dpt0 + sb * kKvQRows + lane_base + half * 32, dpt);
+      tmem_wait_ld();
+      // S^T / dP^T of this chunk are in registers: release the TMEM buffer early
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st_free[sb]);
+#pragma unroll
+      for (int cc = 0; cc < 32; ++cc) {
+        const int col = half * 32 + cc;
+        bool valid = row_valid && col < n_rows;
+        if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
+        // unconditional ex2, then select: a conditional asm call becomes a branch per element
+        const float e = ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul));
+        const float p = valid ? e : 0.f;
+        st[cc] = p;
+        dpt[cc] = valid ? p * (dpt[cc] - mt.delta[col]) * scale : 0.f;
+      }
       if (!warp_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        float st[32], dpt[32];
-        tmem_ld32(tm_st0 + sb * kKvQRows + lane_base + x * 32, st);
-        tmem_ld32(tm_dpt0 + sb * kKvQRows + lane_base + x * 32, dpt);
-        tmem_wait_ld();
-#pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          const int col = x * 32 + cc;
-          bool valid = row_valid && col < n_rows;
-          if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
-          // unconditional ex2, then select: a conditional asm call becomes a branch per element
-          const float e = ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul));
-          const float p = valid ? e : 0.f;
-          st[cc] = p;
-          dpt[cc] = valid ? p * (dpt[cc] - mt.delta[col]) * scale : 0.f;
-        }
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = x * 4 + q8;
-          const uint32_t o = swz_offset<128>(r, ch);
-          st_shared_v4(pt + o, pack2<BF16>(st[q8 * 8], st[q8 * 8 + 1]), pack2<BF16>(st[q8 * 8 + 2], st[q8 * 8 + 3]),
-                       pack2<BF16>(st[q8 * 8 + 4], st[q8 * 8 + 5]), pack2<BF16>(st[q8 * 8 + 6], st[q8 * 8 + 7]));
-          st_shared_v4(dst + o, pack2<BF16>(dpt[q8 * 8], dpt[q8 * 8 + 1]),
-                       pack2<BF16>(dpt[q8 * 8 + 2], dpt[q8 * 8 + 3]), pack2<BF16>(dpt[q8 * 8 + 4], dpt[q8 * 8 + 5]),
-                       pack2<BF16>(dpt[q8 * 8 + 6], dpt[q8 * 8 + 7]));
-        }
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int ch = half * 4 + q8;
+        const uint32_t o = swz_offset<128>(r, ch);
+        st_shared_v4(pt + o, pack2<BF16>(st[q8 * 8], st[q8 * 8 + 1]), pack2<BF16>(st[q8 * 8 + 2], st[q8 * 8 + 3]),
+                     pack2<BF16>(st[q8 * 8 + 4], st[q8 * 8 + 5]), pack2<BF16>(st[q8 * 8 + 6], st[q8 * 8 + 7]));
+        st_shared_v4(dst + o, pack2<BF16>(dpt[q8 * 8], dpt[q8 * 8 + 1]), pack2<BF16>(dpt[q8 * 8 + 2], dpt[q8 * 8 + 3]),
+                     pack2<BF16>(dpt[q8 * 8 + 4], dpt[q8 * 8 + 5]), pack2<BF16>(dpt[q8 * 8 + 6], dpt[q8 * 8 + 7]));
       }
-      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&st_free[sb]);
-        mbar_arrive(&pds_full[sb]);
-      }
+      if (lane == 0) mbar_arrive(&pds_full[sb]);
     }
-    // epilogue: dK, dV of this key row
+    // epilogue: warps of half 0 write dK, of half 1 write dV (key row r)
     bool have = ok;
     if (ok && n_chunks > 0) have = warp_wait(acc_done, 0, abort_flag, prm.err);
     if (have) {
       tc_fence_after();
+      const int which = half;
+      const uint32_t tm_acc = which == 0 ? tm_dk : tm_dv;
+      float v[D];
+      if (n_chunks > 0) {
+        tmem_load_cols<D>(tm_acc + lane_base, v);
+        tmem_wait_ld();
+      } else {
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t tm_acc = which == 0 ? tm_dk : tm_dv;
-        float v[D];
-        if (n_chunks > 0) {
-          tmem_load_cols<D>(tm_acc + lane_base, v);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int c = 0; c < D; ++c) v[c] = 0.f;
-        }
-        if (!row_valid) continue;
+        for (int cc = 0; cc < D; ++cc) v[cc] = 0.f;
+      }
+      if (row_valid) {
         if (prm.n_split > 1) {
           float* dst_p = prm.partial +
                          ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +
                          (size_t)r * D;
 #pragma unroll
-          for (int c = 0; c < D; c += 4)
-            *reinterpret_cast<float4*>(dst_p + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+          for (int cc = 0; cc < D; cc += 4)
+            *reinterpret_cast<float4*>(dst_p + cc) = make_float4(v[cc], v[cc + 1], v[cc + 2], v[cc + 3]);
         } else {
           uint8_t* drow = static_cast<uint8_t*>(which == 0 ? prm.dk : prm.dv) +
                           ((size_t)kidx * prm.kv_tok_stride + (size_t)h * D) * 2;
 #pragma unroll
-          for (int c = 0; c < D; c += 8) {
+          for (int cc = 0; cc < D; cc += 8) {
             uint4 pk;
-            pk.x = pack2<BF16>(v[c], v[c + 1]);
-            pk.y = pack2<BF16>(v[c + 2], v[c + 3]);
-            pk.z = pack2<BF16>(v[c + 4], v[c + 5]);
-            pk.w = pack2<BF16>(v[c + 6], v[c + 7]);
-            *reinterpret_cast<uint4*>(drow + c * 2) = pk;
+            pk.x = pack2<BF16>(v[cc], v[cc + 1]);
+            pk.y = pack2<BF16>(v[cc + 2], v[cc + 3]);
+            pk.z = pack2<BF16>(v[cc + 4], v[cc + 5]);
+            pk.w = pack2<BF16>(v[cc + 6], v[cc + 7]);
+            *reinterpret_cast<uint4*>(drow + cc * 2) = pk;
           }
         }
       }
