@@ -79,14 +79,6 @@ struct FwdSmem {
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
 };
 
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
-  while (!mbar_test(bar, parity)) {
-    if (globaltimer() - t0 > 200000000ull) return false;
-  }
-  return true;
-}
-
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,

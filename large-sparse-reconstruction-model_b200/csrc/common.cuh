@@ -94,6 +94,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Teardown wait (ignores the abort flag): lets copies or MMAs already in
+// flight finish before the CTA exits; gives up after 200 ms.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_test(bar, parity)) {
+    if (globaltimer() - t0 > 200000000ull) return false;
+  }
+  return true;
+}
+
 // Warp-uniform wait: every lane polls, the warp proceeds only if all lanes
 // saw the phase complete (so warp-collective instructions that follow never
 // run with lanes diverged on an abort path).

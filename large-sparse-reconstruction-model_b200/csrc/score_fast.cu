@@ -1,0 +1,553 @@
+// Per-query-block block selection with tensor-core scores and exact
+// refinement.  One CTA per (query block, kv head); 320 threads: 8 reduce
+// warps, a TMA producer warp, an MMA warp.
+//
+// 1. Fast scores.  For each chunk of 128 compressed blocks of the sequence,
+//    S^T = CK_chunk . Q^T (M = 128 blocks, N <= 256 query rows of the query
+//    block, tcgen05, fp32 accumulators in TMEM, double-buffered).  Reduce warp
+//    w owns block row 32*(w%4)+lane and half of the columns; each element
+//    adds e = exp2(s*qk_scale - lse2) to the block's fast score, plus the
+//    terms of a rigorous error bound (below).
+// 2. Certified selection.  With U = fast + bound and L = fast - bound, let T
+//    be the k'-th largest L (k' = k minus the forced own block).  Blocks with
+//    U < T are certainly outside the top-k; the rest (the candidates) get
+//    their score recomputed with the exact fixed-order arithmetic of
+//    score_exact.cuh, and the top k' of the candidates by (exact score desc,
+//    block id asc) are the answer.  This is the same set the exact scorer
+//    selects, so the indices stay bit-exact.
+//
+// Error bound per block (generous by construction):
+//   |fast dot - exact dot| <= 2^-16 |q| |ck|       (fp32 accumulation of 64
+//                                                    exact bf16 products, both
+//                                                    sides, 4x margin)
+//   |t error| <= qk_scale 2^-16 |q||ck| + 2^-20 (2|t| + 2|lse2| + 1)
+//   |e error| <= e (0.7 |t error| + 2^-19)          (ex2 vs exp2_fixed)
+//   sum error <= 2 (n + 1) 2^-23 sum e + n 2^-120   (both accumulations; flush)
+// and the whole bound is doubled.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "attn_host.h"
+#include "common.cuh"
+#include "host_util.h"
+#include "score_exact.cuh"
+
+namespace lsrm {
+
+constexpr int kSfThreads = 320;
+constexpr int kSfReduceThreads = 256;
+constexpr int kSfCols = 256;
+constexpr int kSfStages = 3;
+constexpr int kSfCandCap = 1024;
+
+struct FastScoreParams {
+  const void* q;
+  const void* ck;
+  const float* lse;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_cblocks;
+  const int32_t* cu_qblocks;
+  int32_t* out;
+  long long q_tok_stride;
+  long long ck_tok_stride;
+  int num_seqs;
+  int total_q;
+  int G;
+  int topk;
+  int force_self;
+  int nb_cap;
+  float qk_scale;
+  int* err;
+};
+
+template <int D>
+struct SfLayout {
+  static constexpr int RB = 2 * D;
+  static constexpr int QT = kSfCols * RB;
+  static constexpr int CKT = 128 * RB;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_CK = QT;
+  static constexpr int OFF_COLS = OFF_CK + kSfStages * CKT;  // lse2[256], qn[256]
+  static constexpr int OFF_PART = OFF_COLS + 2 * kSfCols * 4;  // [2][128][3]
+  static constexpr int OFF_BAR = OFF_PART + 2 * 128 * 3 * 4;
+  static constexpr int NBAR = 2 * kSfStages + 2 + 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_CAND = OFF_MISC + 64;  // cand ids [cap], exact [cap], chosen[64]
+  static constexpr int OFF_ARR = OFF_CAND + kSfCandCap * 8 + 64 * 4;
+  // per-block arrays (nb_cap each): fast score, weighted sum, t-term sum
+  static size_t bytes(int nb_cap) { return (size_t)OFF_ARR + 3ull * 4 * nb_cap + 1024; }
+};
+
+// Row of D 16-bit values -> fp32 (exact conversion), 16-byte loads.
+template <typename T, int D>
+__device__ __forceinline__ void load_row_f32(const T* __restrict__ row, float* out) {
+  const uint4* r4 = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    const uint4 u = r4[c];
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[c * 8 + i] = (float)e[i];
+  }
+}
+
+__device__ __forceinline__ void reduce_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kSfReduceThreads) : "memory"); }
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kSfThreads, 1)
+    qblock_topk_fast_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck,
+                            const FastScoreParams p) {
+  using L = SfLayout<D>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int RB = L::RB;
+  constexpr uint64_t SWZ = swz_for_row_bytes(RB);
+  constexpr uint32_t AB = BF16 ? 1u : 0u;
+  const int qb = blockIdx.x, h = blockIdx.y;
+  const int G = p.G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int r0 = p.cu_qblocks[qb], r1 = p.cu_qblocks[qb + 1];
+  int lo = 0, hi = p.num_seqs + 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (p.cu_seqlens_q[mid] > r0) hi = mid;
+    else lo = mid + 1;
+  }
+  const int seq = max(lo - 1, 0);
+  const int blk0 = p.cu_cblocks[seq];
+  const int nb = p.cu_cblocks[seq + 1] - blk0;
+  const int ncols_total = max(r1 - r0, 0) * G;
+  const int tpp = kSfCols / G;  // tokens per pass
+  const int n_pass = (ncols_total + kSfCols - 1) / kSfCols;
+  const int n_ck = (nb + 127) / 128;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sCK = smem + L::OFF_CK;
+  float* col_lse2 = reinterpret_cast<float*>(smem + L::OFF_COLS);
+  float* col_qn = col_lse2 + kSfCols;
+  float* part = reinterpret_cast<float*>(smem + L::OFF_PART);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* ck_full = bars;
+  uint64_t* ck_empty = bars + kSfStages;
+  uint64_t* q_full = bars + 2 * kSfStages;
+  uint64_t* q_free = q_full + 1;
+  uint64_t* s_full = q_free + 1;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* mma_done = s_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  int* s_misc = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);  // [0]=n_cand [1]=fallback
+  int* cand = reinterpret_cast<int*>(smem + L::OFF_CAND);
+  float* cand_exact = reinterpret_cast<float*>(cand + kSfCandCap);
+  int* chosen = reinterpret_cast<int*>(cand_exact + kSfCandCap);
+  float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);
+  float* WS = SF + p.nb_cap;
+  float* TS = WS + p.nb_cap;
+
+  if (nb > p.nb_cap) {  // the host sizes nb_cap from the total block count
+    if (threadIdx.x == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
+    return;
+  }
+  for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+    SF[b] = 0.f;
+    WS[b] = 0.f;
+    TS[b] = 0.f;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSfStages; ++i) {
+      mbar_init(&ck_full[i], 1);
+      mbar_init(&ck_empty[i], 1);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const float sl2 = p.qk_scale;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      for (int ps = 0; ps < n_pass; ++ps) {
+        if (ps > 0 && !mbar_wait(q_free, (ps - 1) & 1, abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(q_full, L::QT);
+        tma_load_3d(sQ, &tm_q, 0, h * G, r0 + ps * tpp, q_full);
+        bool ok = true;
+        for (int c = 0; c < n_ck; ++c) {
+          const int j = ps * n_ck + c, s = j % kSfStages;
+          if (!mbar_wait(&ck_empty[s], ((j / kSfStages) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&ck_full[s], L::CKT);
+          tma_load_3d(sCK + s * L::CKT, &tm_ck, 0, h, blk0 + c * 128, &ck_full[s]);
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int ps = 0; ps < n_pass && ok; ++ps) {
+        const int ncols = min(kSfCols, ncols_total - ps * kSfCols);
+        const uint32_t n_mma = (uint32_t)((ncols + 15) / 16 * 16);
+        const uint32_t idesc = make_idesc(AB, 0, 0, 128, n_mma);
+        if (!mbar_wait(q_full, ps & 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        for (int c = 0; c < n_ck; ++c) {
+          const int j = ps * n_ck + c, s = j % kSfStages, sb = j & 1;
+          if (!mbar_wait(&ck_full[s], (j / kSfStages) & 1, abort_flag, p.err)) { ok = false; break; }
+          if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ckb = smem_u32(sCK + s * L::CKT), qb_s = smem_u32(sQ);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_f16(tmem + sb * kSfCols, make_sdesc(ckb + ks * 32, 16, 8 * RB, SWZ),
+                     make_sdesc(qb_s + ks * 32, 16, 8 * RB, SWZ), idesc, ks > 0);
+          umma_commit(&s_full[sb]);
+          umma_commit(&ck_empty[s]);
+        }
+        umma_commit(q_free);
+      }
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ reduce warps ---------------------------
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float l2e = __uint_as_float(0x3FB8AA3Bu);
+    bool ok = true;
+    for (int ps = 0; ps < n_pass && ok; ++ps) {
+      const int ncols = min(kSfCols, ncols_total - ps * kSfCols);
+      reduce_bar();
+      {
+        const int t = threadIdx.x;  // column of this pass
+        float l2 = 0.f, qn = 0.f;
+        if (t < ncols) {
+          const int tok = r0 + ps * tpp + t / G, g = t % G;
+          l2 = p.lse[(size_t)(h * G + g) * p.total_q + tok] * l2e;
+          float qv[D];
+          load_row_f32<T, D>(static_cast<const T*>(p.q) + (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D, qv);
+#pragma unroll
+          for (int j = 0; j < D; ++j) qn = fmaf(qv[j], qv[j], qn);
+          qn = sqrtf(qn);
+        }
+        col_lse2[t] = l2;
+        col_qn[t] = qn;
+      }
+      reduce_bar();
+      for (int c = 0; c < n_ck; ++c) {
+        const int j = ps * n_ck + c, sb = j & 1;
+        if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        float acc_e = 0.f, acc_w = 0.f, acc_t = 0.f;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int col0 = (2 * x + half) * 32;  // halves interleave 32-column slices
+          if (col0 < ncols) {
+            float sv[32];
+            tmem_ld32(tmem + sb * kSfCols + lane_base + col0, sv);
+            tmem_wait_ld();
+#pragma unroll
+            for (int cc = 0; cc < 32; ++cc) {
+              const int col = col0 + cc;
+              const float l2 = col_lse2[col];
+              const float t = fmaf(sv[cc], sl2, -l2);
+              const float e = col < ncols ? ex2(t) : 0.f;
+              acc_e += e;
+              acc_w = fmaf(e, col_qn[col], acc_w);
+              acc_t = fmaf(e, 2.f * fabsf(t) + 2.f * fabsf(l2) + 1.f, acc_t);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        float* pt = part + (size_t)sb * 128 * 3;
+        if (half == 1) {
+          pt[row * 3 + 0] = acc_e;
+          pt[row * 3 + 1] = acc_w;
+          pt[row * 3 + 2] = acc_t;
+        }
+        reduce_bar();
+        const int b = c * 128 + row;
+        if (half == 0 && b < nb) {
+          SF[b] += acc_e + pt[row * 3 + 0];
+          WS[b] += acc_w + pt[row * 3 + 1];
+          TS[b] += acc_t + pt[row * 3 + 2];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (*abort_flag) return;
+
+  // ------------------------------ selection --------------------------------
+  const int kk = min(p.topk, nb);
+  int self = -1;
+  if (p.force_self && kk > 0) {
+    int qb_lo = 0, qb_hi = qb + 1;
+    while (qb_lo < qb_hi) {
+      const int mid = (qb_lo + qb_hi) >> 1;
+      if (p.cu_qblocks[mid] >= p.cu_seqlens_q[seq]) qb_hi = mid;
+      else qb_lo = mid + 1;
+    }
+    const int sidx = qb - qb_lo;
+    if (sidx >= 0 && sidx < nb) self = sidx;
+  }
+  const int kp = kk - (self >= 0 ? 1 : 0);
+  // bounds: WS <- lower, TS <- upper
+  const float n_f = (float)ncols_total;
+  for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+    float kv[D];
+    load_row_f32<T, D>(static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D, kv);
+    float ckn = 0.f;
+#pragma unroll
+    for (int j = 0; j < D; ++j) ckn = fmaf(kv[j], kv[j], ckn);
+    ckn = sqrtf(ckn);
+    const float sf = SF[b];
+    const float e = 2.f * (0.7f * (sl2 * 0x1p-16f * ckn * WS[b] + 0x1p-20f * TS[b]) +
+                           (0x1p-19f + (n_f + 1.f) * 0x1p-22f) * sf + n_f * 0x1p-120f);
+    WS[b] = (b == self) ? -INFINITY : sf - e;
+    TS[b] = (b == self) ? -INFINITY : sf + e;
+  }
+  __syncthreads();
+  // threshold: the kp-th largest lower bound (ties counted), by kp arg-max rounds
+  float thr = -INFINITY;
+  {
+    __shared__ float red_v[kSfThreads / 32];
+    __shared__ int red_i[kSfThreads / 32];
+    // copy of the lower bounds lives in SF (fast scores are no longer needed)
+    for (int b = threadIdx.x; b < nb; b += kSfThreads) SF[b] = WS[b];
+    __syncthreads();
+    for (int round = 0; round < kp; ++round) {
+      float best = -INFINITY;
+      int bid = INT_MAX;
+      for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+        const float v = SF[b];
+        if (v > best || (v == best && b < bid)) {
+          best = v;
+          bid = b;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
+        if (ov > best || (ov == best && oi < bid)) {
+          best = ov;
+          bid = oi;
+        }
+      }
+      if (lane == 0) {
+        red_v[warp] = best;
+        red_i[warp] = bid;
+      }
+      __syncthreads();
+      float bv = red_v[0];
+      int bi = red_i[0];
+      for (int i = 1; i < kSfThreads / 32; ++i)
+        if (red_v[i] > bv || (red_v[i] == bv && red_i[i] < bi)) {
+          bv = red_v[i];
+          bi = red_i[i];
+        }
+      thr = bv;
+      __syncthreads();
+      if (threadIdx.x == 0 && bi != INT_MAX) SF[bi] = -INFINITY;
+      __syncthreads();
+    }
+  }
+  // candidates: upper bound reaches the threshold
+  if (threadIdx.x == 0) {
+    s_misc[0] = 0;
+    s_misc[1] = 0;
+  }
+  __syncthreads();
+  if (kp > 0) {
+    for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+      if (b != self && TS[b] >= thr) {
+        const int slot = atomicAdd(&s_misc[0], 1);
+        if (slot < kSfCandCap) cand[slot] = b;
+        else s_misc[1] = 1;
+      }
+    }
+  }
+  __syncthreads();
+  const int n_cand_raw = s_misc[0];
+  const bool fallback = s_misc[1] != 0;
+  // Exact scores of the candidates (every block on the fallback path):
+  // stage A, all threads: per (candidate, column) the fixed-order score term;
+  // stage B, one thread per candidate: ordered sums (heads, then tokens).
+  // Scratch for stage A: the per-block arrays (3 * nb_cap floats).
+  const int n_exact = fallback ? nb : (n_cand_raw > kp ? n_cand_raw : 0);
+  if (n_exact > 0) {
+    float* escore = cand_exact;  // [kSfCandCap] (fallback: SF, sized nb)
+    float* eterm = WS;           // [batch][ncols_total], spans WS and TS
+    const int cap_terms = 2 * p.nb_cap;
+    const int batch = max(1, min(n_exact, cap_terms / max(ncols_total, 1)));
+    const float l2e = __uint_as_float(0x3FB8AA3Bu);
+    for (int c0 = 0; c0 < n_exact; c0 += batch) {
+      const int nbat = min(batch, n_exact - c0);
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < nbat * ncols_total; idx += kSfThreads) {
+        const int ci = idx / ncols_total, col = idx % ncols_total;
+        const int b = fallback ? (c0 + ci) : cand[c0 + ci];
+        const int tok = r0 + col / G, g = col % G;
+        float kv[D], qv[D];
+        load_row_f32<T, D>(static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D, kv);
+        load_row_f32<T, D>(static_cast<const T*>(p.q) + (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D, qv);
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(qv[j], kv[j]));
+        const float lse2 = __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
+        eterm[idx] = exp2_fixed(__fsub_rn(__fmul_rn(dot, p.qk_scale), lse2));
+      }
+      __syncthreads();
+      for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) {
+        const float* e = eterm + (size_t)ci * ncols_total;
+        float agg = 0.f;
+        for (int t = 0; t < ncols_total / G; ++t) {
+          float st = 0.f;
+          for (int g = 0; g < G; ++g) st = __fadd_rn(st, e[t * G + g]);
+          agg = __fadd_rn(agg, st);
+        }
+        const int b = fallback ? (c0 + ci) : cand[c0 + ci];
+        if (fallback) SF[b] = (b == self) ? -INFINITY : agg;
+        else escore[c0 + ci] = agg;
+      }
+    }
+    __syncthreads();
+  }
+  const int n_cand = n_cand_raw;
+  // choose kp blocks: (exact desc, id asc) among candidates (or all blocks)
+  if (threadIdx.x == 0) {
+    int n_ch = 0;
+    if (self >= 0) chosen[n_ch++] = self;
+    if (fallback) {
+      for (int r = 0; r < kp; ++r) {
+        float bv = -INFINITY;
+        int bi = -1;
+        for (int b = 0; b < nb; ++b)  // ascending ids: ties keep the lowest id
+          if (SF[b] > bv) {
+            bv = SF[b];
+            bi = b;
+          }
+        if (bi < 0) break;
+        chosen[n_ch++] = bi;
+        SF[bi] = -INFINITY;
+      }
+    } else if (n_cand <= kp) {
+      for (int i = 0; i < n_cand; ++i) chosen[n_ch++] = cand[i];
+    } else {
+      for (int r = 0; r < kp; ++r) {
+        float bv = -INFINITY;
+        int bi = -1, bslot = -1;
+        for (int i = 0; i < n_cand; ++i) {
+          if (cand[i] < 0) continue;
+          const float v = cand_exact[i];
+          if (bi < 0 || v > bv || (v == bv && cand[i] < bi)) {
+            bv = v;
+            bi = cand[i];
+            bslot = i;
+          }
+        }
+        if (bi < 0) break;
+        chosen[n_ch++] = bi;
+        cand[bslot] = -1;
+      }
+    }
+    s_misc[2] = n_ch;
+  }
+  __syncthreads();
+  const int n_ch = s_misc[2];
+  int32_t* dst = p.out + ((size_t)h * gridDim.x + qb) * p.topk;
+  for (int i = threadIdx.x; i < p.topk; i += kSfThreads) {
+    if (i < n_ch) {
+      const int id = chosen[i];
+      int rank = 0;
+      for (int j = 0; j < n_ch; ++j) rank += chosen[j] < id;
+      dst[rank] = id;
+    } else {
+      dst[i] = -1;
+    }
+  }
+}
+
+template <int D, bool BF16>
+static int launch_fast_t(const CUtensorMap& mq, const CUtensorMap& mck, const FastScoreParams& p, int nqb, int hkv,
+                         size_t smem, cudaStream_t s) {
+  LSRM_CUDA_TRY(cudaFuncSetAttribute(qblock_topk_fast_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+  ProfScope ps("block_topk_fast", s);
+  qblock_topk_fast_kernel<D, BF16><<<dim3(nqb, hkv), kSfThreads, smem, s>>>(mq, mck, p);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+// Returns LSRM_ERR_UNSUPPORTED (without launching) when the problem does not
+// fit the fast path; the caller then uses the exact scorer.
+int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
+                            const float* lse_ln, int topk, const int32_t* cu_query_blocks, int num_query_blocks,
+                            int force_self, double qk_scale, int32_t* out, int* err, cudaStream_t s) {
+  const int D = shape->head_dim;
+  const int G = shape->num_q_heads / shape->num_kv_heads;
+  if (G > kSfCols) return LSRM_ERR_UNSUPPORTED;
+  const int nb_cap = std::max(meta->num_blocks, 1);
+  size_t smem = D == 64 ? SfLayout<64>::bytes(nb_cap) : D == 32 ? SfLayout<32>::bytes(nb_cap) : SfLayout<16>::bytes(nb_cap);
+  if (smem > 220 * 1024) return LSRM_ERR_UNSUPPORTED;
+  if (smem < (size_t)kOneCtaPerSmSmem) smem = kOneCtaPerSmSmem;  // all 512 TMEM columns per CTA
+  CUtensorMap mq, mck;
+  int rc;
+  if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, kSfCols / G)))
+    return rc;
+  if ((rc = make_tmap_3d(&mck, ck, D, shape->num_kv_heads, meta->num_blocks, shape->kv_token_stride, 1, 128))) return rc;
+  FastScoreParams p{};
+  p.q = q;
+  p.ck = ck;
+  p.lse = lse_ln;
+  p.cu_seqlens_q = meta->cu_seqlens_q;
+  p.cu_cblocks = meta->cu_seqblocks;
+  p.cu_qblocks = cu_query_blocks;
+  p.out = out;
+  p.q_tok_stride = shape->q_token_stride;
+  p.ck_tok_stride = shape->kv_token_stride;
+  p.num_seqs = meta->num_seqs;
+  p.total_q = meta->total_q;
+  p.G = G;
+  p.topk = topk;
+  p.force_self = force_self;
+  p.nb_cap = nb_cap;
+  p.qk_scale = (float)qk_scale;
+  p.err = err;
+  const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
+  if (D == 64) return bf16 ? launch_fast_t<64, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
+                           : launch_fast_t<64, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
+  if (D == 32) return bf16 ? launch_fast_t<32, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
+                           : launch_fast_t<32, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
+  return bf16 ? launch_fast_t<16, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
+              : launch_fast_t<16, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
+}
+
+}  // namespace lsrm

@@ -16,28 +16,18 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "attn_host.h"
 #include "host_util.h"
+#include "score_exact.cuh"
 
 namespace lsrm {
 
-__device__ __forceinline__ float exp2_fixed(float t) {
-  const float n = rintf(t);
-  if (n < -125.f) return 0.f;
-  if (n > 127.f) return INFINITY;
-  const float f = __fsub_rn(t, n);
-  float r = __uint_as_float(0x377FE5FEu);
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x39218489u));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3AAEC3FFu));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3C1D955Bu));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3D635847u));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3E75FDF0u));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3F317218u));
-  r = __fadd_rn(__fmul_rn(r, f), __uint_as_float(0x3F800000u));
-  const float sc = __int_as_float(((int)n + 127) << 23);
-  return __fmul_rn(r, sc);
-}
+int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
+                            const float* lse_ln, int topk, const int32_t* cu_query_blocks, int num_query_blocks,
+                            int force_self, double qk_scale, int32_t* out, int* err, cudaStream_t s);
 
 struct ScoreParams {
   const void* q;
@@ -225,7 +215,6 @@ extern "C" int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* s
                                int* err_flags, void* stream) {
   int G = 1, rc;
   if ((rc = check_shape(meta, shape, G))) return rc;
-  (void)err_flags;
   LSRM_CHECK_ARG(topk >= 1 && topk <= 64, "topk must be in [1, 64] (got %d)", topk);
   LSRM_CHECK_ARG(num_query_blocks == 0 || cu_query_blocks, "num_query_blocks > 0 needs cu_query_blocks");
   LSRM_CHECK_ARG(!force_self || cu_query_blocks, "force_self needs query blocks");
@@ -251,13 +240,22 @@ extern "C" int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* s
   p.qk_scale = (float)(scale * 1.44269504);
   const int rows = num_query_blocks > 0 ? num_query_blocks : meta->total_q;
   if (rows == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Per-query-block selection: tensor-core scores with exact refinement
+  // (same indices); LSRM_SCORER=exact forces the exact scorer everywhere.
+  const char* mode = getenv("LSRM_SCORER");
+  if (num_query_blocks > 0 && !(mode && strcmp(mode, "exact") == 0)) {
+    int* err = err_flags;
+    rc = launch_qblock_topk_fast(meta, shape, q, ck, lse_ln, topk, cu_query_blocks, num_query_blocks, force_self,
+                                 scale * 1.44269504, block_topk, err, s);
+    if (rc != LSRM_ERR_UNSUPPORTED) return rc;
+  }
   const size_t nb_cap = ((size_t)std::max(meta->num_blocks, 1) + 3) & ~size_t(3);
   const size_t smem = (nb_cap + (size_t)p.tq * G * D + (size_t)p.tq * G) * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("block_topk: %d compressed blocks do not fit the on-chip score buffer", meta->num_blocks);
     return LSRM_ERR_UNSUPPORTED;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
   if (D == 64)
     return bf16 ? launch_topk_t<__nv_bfloat16, 64>(p, rows, shape->num_kv_heads, smem, s)
