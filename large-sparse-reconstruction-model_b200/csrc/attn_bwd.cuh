@@ -496,6 +496,7 @@ constexpr int kDkvMmaWarp = 9;
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kDkvThreads, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const DkvParams prm) {
   using L = DkvSmem<D, STAGES>;
   constexpr int RB = L::RB;
@@ -662,6 +663,16 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       }
       __syncwarp();
       const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
+      if constexpr (MODE != kSelect) {
+        // contiguous queries: one TMA box per operand; rows past the range are
+        // other tokens' data (finite, masked) or zero fill past the tensor
+        if (lane == 0) {
+          const int q0 = q_lo + c * qpc;
+          mbar_expect_tx(&q_full[s], 2 * L::QTILE);
+          tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
+          tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
+        }
+      } else
 #pragma unroll 4
       for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
         const int row = idx / CPR, j = idx % CPR;  // CPR is a power of two
@@ -766,16 +777,30 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&st_free[sb]);
+      float lse_c[32], dl_c[32];
+#pragma unroll
+      for (int v4 = 0; v4 < 8; ++v4) {  // per-column statistics, 16-byte broadcast loads
+        const float4 a = *reinterpret_cast<const float4*>(&mt.lse2[half * 32 + v4 * 4]);
+        const float4 b = *reinterpret_cast<const float4*>(&mt.delta[half * 32 + v4 * 4]);
+        lse_c[v4 * 4 + 0] = a.x * lse_mul;
+        lse_c[v4 * 4 + 1] = a.y * lse_mul;
+        lse_c[v4 * 4 + 2] = a.z * lse_mul;
+        lse_c[v4 * 4 + 3] = a.w * lse_mul;
+        dl_c[v4 * 4 + 0] = b.x;
+        dl_c[v4 * 4 + 1] = b.y;
+        dl_c[v4 * 4 + 2] = b.z;
+        dl_c[v4 * 4 + 3] = b.w;
+      }
 #pragma unroll
       for (int cc = 0; cc < 32; ++cc) {
         const int col = half * 32 + cc;
         bool valid = row_valid && col < n_rows;
         if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
         // unconditional ex2, then select: a conditional asm call becomes a branch per element
-        const float e = ex2(fmaf(st[cc], sl2, -mt.lse2[col] * lse_mul));
+        const float e = ex2(fmaf(st[cc], sl2, -lse_c[cc]));
         const float p = valid ? e : 0.f;
         st[cc] = p;
-        dpt[cc] = valid ? p * (dpt[cc] - mt.delta[col]) * scale : 0.f;
+        dpt[cc] = valid ? p * (dpt[cc] - dl_c[cc]) * scale : 0.f;
       }
       if (!warp_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
