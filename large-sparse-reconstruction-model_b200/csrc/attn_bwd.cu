@@ -38,30 +38,30 @@ __global__ void zero_tail_kernel(uint16_t* dk, uint16_t* dv, const int32_t* star
 }
 
 template <int D, bool BF16, int MODE>
-static int launch_dq_t(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk, const CUtensorMap& mv,
-                       const DqParams& p, int grid_x, int hkv, cudaStream_t s) {
+static int launch_dq_t(const CUtensorMap& mq, const CUtensorMap& mdo, const KVMaps& kv, const DqParams& p, int grid_x,
+                       int hkv, cudaStream_t s) {
   constexpr int STAGES = 4;
   using L = DqSmem<D, STAGES>;
   auto kern = attn_dq_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   ProfScope ps(MODE == kSelect ? "attn_dq_select" : (MODE == kBand ? "attn_dq_sliding" : "attn_dq_range"), s);
-  kern<<<dim3(grid_x, hkv), 192, L::ALLOC, s>>>(mq, mdo, mk, mv, p);
+  kern<<<dim3(grid_x, hkv), kDqThreads, L::ALLOC, s>>>(mq, mdo, kv, p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }
 
 template <int MODE>
-static int launch_dq(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
-                     const CUtensorMap& mv, const DqParams& p, int grid_x, int hkv, cudaStream_t s) {
+static int launch_dq(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mdo, const KVMaps& kv,
+                     const DqParams& p, int grid_x, int hkv, cudaStream_t s) {
   if (grid_x <= 0) return LSRM_OK;
   if (D == 64)
-    return bf16 ? launch_dq_t<64, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
-                : launch_dq_t<64, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
+    return bf16 ? launch_dq_t<64, true, MODE>(mq, mdo, kv, p, grid_x, hkv, s)
+                : launch_dq_t<64, false, MODE>(mq, mdo, kv, p, grid_x, hkv, s);
   if (D == 16)
-    return bf16 ? launch_dq_t<16, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
-                : launch_dq_t<16, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
-  return bf16 ? launch_dq_t<32, true, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s)
-              : launch_dq_t<32, false, MODE>(mq, mdo, mk, mv, p, grid_x, hkv, s);
+    return bf16 ? launch_dq_t<16, true, MODE>(mq, mdo, kv, p, grid_x, hkv, s)
+                : launch_dq_t<16, false, MODE>(mq, mdo, kv, p, grid_x, hkv, s);
+  return bf16 ? launch_dq_t<32, true, MODE>(mq, mdo, kv, p, grid_x, hkv, s)
+              : launch_dq_t<32, false, MODE>(mq, mdo, kv, p, grid_x, hkv, s);
 }
 
 template <int D, bool BF16, int MODE>
@@ -176,12 +176,12 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
   const float scale = softmax_scale_of(shape);
   // dQ (+ delta)
   {
-    CUtensorMap mq, mdo, mk, mv;
+    CUtensorMap mq, mdo;
+    KVMaps kv;
     if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
     if ((rc = make_tmap_3d(&mdo, dout, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt)))
       return rc;
-    if ((rc = make_tmap_3d(&mk, k, D, hkv, meta->total_k, shape->kv_token_stride, 1, kGroupRows))) return rc;
-    if ((rc = make_tmap_3d(&mv, v, D, hkv, meta->total_k, shape->kv_token_stride, 1, kGroupRows))) return rc;
+    if ((rc = make_kv_maps(kv.k, kv.v, kNumBoxes, k, v, D, hkv, meta->total_k, shape->kv_token_stride))) return rc;
     DqParams p{};
     p.tiles = plan.tiles;
     p.n_tiles = plan.n_tiles;
@@ -204,7 +204,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.scale_log2 = scale * 1.44269504f;
     p.scale = scale;
     p.err = err;
-    if ((rc = launch_dq<kSelect>(D, bf16, mq, mdo, mk, mv, p, plan.tiles_ub, hkv, s))) return rc;
+    if ((rc = launch_dq<kSelect>(D, bf16, mq, mdo, kv, p, plan.tiles_ub, hkv, s))) return rc;
   }
   // dK, dV
   {
@@ -286,12 +286,12 @@ extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shap
   const float scale = softmax_scale_of(shape);
   const int qpt = kRows / G;
   {
-    CUtensorMap mq, mdo, mk, mv;
+    CUtensorMap mq, mdo;
+    KVMaps kv;
     if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
     if ((rc = make_tmap_3d(&mdo, dout, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt)))
       return rc;
-    if ((rc = make_tmap_3d(&mk, k, D, hkv, nk, shape->kv_token_stride, 1, kDqChunk))) return rc;
-    if ((rc = make_tmap_3d(&mv, v, D, hkv, nk, shape->kv_token_stride, 1, kDqChunk))) return rc;
+    if ((rc = make_kv_maps(kv.k, kv.v, kNumBoxes, k, v, D, hkv, nk, shape->kv_token_stride))) return rc;
     DqParams p{};
     p.tiles = plan.tiles;
     p.n_tiles = plan.n_tiles;
@@ -309,8 +309,8 @@ extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shap
     p.half_window = window / 2;
     p.lse_natural = mode == LSRM_DENSE_COMPRESSED;
     p.err = err;
-    rc = (mode == LSRM_DENSE_SLIDING) ? launch_dq<kBand>(D, bf16, mq, mdo, mk, mv, p, plan.tiles_ub, hkv, s)
-                                      : launch_dq<kRange>(D, bf16, mq, mdo, mk, mv, p, plan.tiles_ub, hkv, s);
+    rc = (mode == LSRM_DENSE_SLIDING) ? launch_dq<kBand>(D, bf16, mq, mdo, kv, p, plan.tiles_ub, hkv, s)
+                                      : launch_dq<kRange>(D, bf16, mq, mdo, kv, p, plan.tiles_ub, hkv, s);
     if (rc) return rc;
   }
   {

@@ -114,11 +114,14 @@ __device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, 
   for (int w = 0; w < NG / 4; ++w) colmask[w] = cm[w];
 }
 
+// Threads of the dQ kernel: 8 compute warps (two per TMEM lane quarter,
+// splitting the 64 key columns of a chunk), a producer warp, an MMA warp.
+constexpr int kDqThreads = 320;
+
 template <int D, bool BF16, int MODE, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kDqThreads, 1)
     attn_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                   const DqParams prm) {
+                   const __grid_constant__ KVMaps kv, const DqParams prm) {
   using L = DqSmem<D, STAGES>;
   constexpr int RB = L::RB;
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
@@ -171,8 +174,8 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(qdo_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sd_full[i], 1);
-      mbar_init(&sd_free[i], 4);
-      mbar_init(&ds_full[i], 4);
+      mbar_init(&sd_free[i], 8);
+      mbar_init(&ds_full[i], 8);
       mbar_init(&ds_free[i], 1);
     }
     mbar_init(dq_done, 1);
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(192, 1)
   // TMEM: S0 [0,64) S1 [64,128) dP0 [128,192) dP1 [192,256) dQ [256, 256+D)
   const uint32_t tm_s0 = tmem, tm_dp0 = tmem + 128, tm_dq = tmem + 256;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       const int qpt = 128 / G;
       mbar_arrive_expect_tx(qdo_full, 2 * L::QTILE);
@@ -210,18 +213,14 @@ __global__ void __launch_bounds__(192, 1)
                                        prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
                                        mt.colmask);
           mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-          for (int g = 0; g < kDqGroups; ++g) {
-            const int row = mt.row0[g] >= 0 ? mt.row0[g] : prm.total_k;
-            tma_load_3d(dK + g * kGroupRows * RB, &tm_k, 0, h, row, &kv_full[s]);
-            tma_load_3d(dV + g * kGroupRows * RB, &tm_v, 0, h, row, &kv_full[s]);
-          }
+          load_group_runs<kDqGroups, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
         } else {
           const int k0 = tile.kv_lo + j * kDqChunk;
           mt.kv_start = k0;
           mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
           mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-          tma_load_3d(dK, &tm_k, 0, h, k0, &kv_full[s]);
-          tma_load_3d(dV, &tm_v, 0, h, k0, &kv_full[s]);
+          tma_load_3d(dK, &kv.k[3], 0, h, k0, &kv_full[s]);  // 64-row box
+          tma_load_3d(dV, &kv.v[3], 0, h, k0, &kv_full[s]);
         }
         issued = j + 1;
       }
@@ -231,7 +230,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc(AB, 0, 0, 128, kDqChunk);
       const uint32_t idesc_dq = make_idesc(AB, 0, 1, 128, D);
@@ -281,12 +280,14 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    const int r = threadIdx.x;
+    // warp w: rows 32*(w%4).., key columns 32*(w/4).. of each chunk
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int qloc = r / G;
     const int hq = h * G + (r % G);
     const int qi = tile.q_start + qloc;
     const bool row_valid = qloc < tile.n_q;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2, scale = prm.scale;
     float lse2 = 0.f, delta = 0.f;
     if (row_valid) {
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) delta = fmaf((float)ae[e], (float)be[e], delta);
       }
-      prm.delta[(size_t)hq * prm.total_q + qi] = delta;
+      if (half == 0) prm.delta[(size_t)hq * prm.total_q + qi] = delta;
     }
     bool ok = true;
     for (int j = 0; j < n_chunks; ++j) {
@@ -312,65 +313,56 @@ __global__ void __launch_bounds__(192, 1)
       if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       const DqMeta& mt = meta[s];
-      uint32_t vm[2];
+      uint32_t vm;  // valid columns of this warp's 32-column slice
       if constexpr (MODE == kSelect) {
         const int w = qloc >> 5, b = qloc & 31;
+        uint32_t e = 0u;
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          uint32_t e = 0u;
-#pragma unroll
-          for (int y = 0; y < 4; ++y)
-            if ((mt.qmask[x * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
-          vm[x] = e & mt.colmask[x];
-        }
+        for (int y = 0; y < 4; ++y)
+          if ((mt.qmask[half * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
+        vm = e & mt.colmask[half];
       } else {
         int lo = 0, hi = mt.n_valid;
         if constexpr (MODE == kBand) {
           lo = max(lo, qi - prm.half_window - mt.kv_start);
           hi = min(hi, qi + prm.half_window + 1 - mt.kv_start);
         }
+        const int a = max(lo - 32 * half, 0), bnd = min(hi - 32 * half, 32);
+        vm = 0u;
+        if (bnd > a) vm = ((bnd - a) == 32 ? 0xffffffffu : ((1u << (bnd - a)) - 1u)) << a;
+      }
+      float sv[32], dp[32];
+      tmem_ld32(tm_s0 + sb * kDqChunk + lane_base + half * 32, sv);
+      tmem_ld32(tm_dp0 + sb * kDqChunk + lane_base + half * 32, dp);
+      tmem_wait_ld();
+      // S / dP of this chunk are in registers: release the TMEM buffers early
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sd_free[sb]);
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int a = max(lo - 32 * x, 0), bnd = min(hi - 32 * x, 32);
-          uint32_t e = 0u;
-          if (bnd > a) e = ((bnd - a) == 32 ? 0xffffffffu : ((1u << (bnd - a)) - 1u)) << a;
-          vm[x] = e;
-        }
+      for (int c = 0; c < 32; ++c) {
+        const bool valid = (vm >> c) & 1u;
+        const float p = ex2(fmaf(sv[c], sl2, -lse2));
+        sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
       }
       if (!warp_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        float sv[32], dp[32];
-        tmem_ld32(tm_s0 + sb * kDqChunk + lane_base + x * 32, sv);
-        tmem_ld32(tm_dp0 + sb * kDqChunk + lane_base + x * 32, dp);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const bool valid = (vm[x] >> c) & 1u;
-          const float p = ex2(fmaf(sv[c], sl2, -lse2));
-          sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
-        }
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = x * 4 + q8;
-          st_shared_v4(ds_base + swz_offset<128>(r, ch), pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]),
-                       pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]), pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]),
-                       pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
-        }
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int ch = half * 4 + q8;
+        st_shared_v4(ds_base + swz_offset<128>(r, ch), pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]),
+                     pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]), pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]),
+                     pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
       }
-      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sd_free[sb]);
-        mbar_arrive(&ds_full[sb]);
-      }
+      if (lane == 0) mbar_arrive(&ds_full[sb]);
     }
-    // every lane takes part in the warp-collective TMEM loads; only valid rows store
+    // warps of half 0 write dQ; every lane of such a warp takes part in the
+    // warp-collective TMEM load, only valid rows store
     bool have = ok;
     if (ok && n_chunks > 0) have = warp_wait(dq_done, 0, abort_flag, prm.err);
-    if (have) {
+    if (have && half == 0) {
       tc_fence_after();
       uint8_t* drow = static_cast<uint8_t*>(prm.dq) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
       float v[D];

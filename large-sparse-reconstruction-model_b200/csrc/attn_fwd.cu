@@ -9,31 +9,31 @@
 namespace lsrm {
 
 template <int D, bool BF16, int MODE>
-static int launch_fwd_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdParams& p,
-                        int grid_x, int hkv, cudaStream_t s) {
+static int launch_fwd_t(const CUtensorMap& mq, const KVMaps& kv, const FwdParams& p, int grid_x, int hkv,
+                        cudaStream_t s) {
   constexpr int STAGES = 3;
   using L = FwdSmem<D, STAGES>;
   auto kern = attn_fwd_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   ProfScope ps(MODE == kSelect ? "attn_fwd_select" : (MODE == kBand ? "attn_fwd_sliding" : "attn_fwd_range"), s);
-  kern<<<dim3(grid_x, hkv), 192, L::ALLOC, s>>>(mq, mk, mv, p);
+  kern<<<dim3(grid_x, hkv), kFwdThreads, L::ALLOC, s>>>(mq, kv, p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }
 
 template <int MODE>
-static int launch_fwd(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                      const FwdParams& p, int grid_x, int hkv, cudaStream_t s) {
+static int launch_fwd(int D, bool bf16, const CUtensorMap& mq, const KVMaps& kv, const FwdParams& p, int grid_x,
+                      int hkv, cudaStream_t s) {
   if (grid_x <= 0) return LSRM_OK;
   if (D == 64) {
-    return bf16 ? launch_fwd_t<64, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
-                : launch_fwd_t<64, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
+    return bf16 ? launch_fwd_t<64, true, MODE>(mq, kv, p, grid_x, hkv, s)
+                : launch_fwd_t<64, false, MODE>(mq, kv, p, grid_x, hkv, s);
   }
   if (D == 16)
-    return bf16 ? launch_fwd_t<16, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
-                : launch_fwd_t<16, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
-  return bf16 ? launch_fwd_t<32, true, MODE>(mq, mk, mv, p, grid_x, hkv, s)
-              : launch_fwd_t<32, false, MODE>(mq, mk, mv, p, grid_x, hkv, s);
+    return bf16 ? launch_fwd_t<16, true, MODE>(mq, kv, p, grid_x, hkv, s)
+                : launch_fwd_t<16, false, MODE>(mq, kv, p, grid_x, hkv, s);
+  return bf16 ? launch_fwd_t<32, true, MODE>(mq, kv, p, grid_x, hkv, s)
+              : launch_fwd_t<32, false, MODE>(mq, kv, p, grid_x, hkv, s);
 }
 
 int check_shape(const lsrm_varlen* m, const lsrm_attn_shape* sh, int& G) {
@@ -93,11 +93,10 @@ extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_sha
   if ((rc = launch_build_unions(plan, meta, block_topk, topk, qblock ? num_query_blocks : meta->total_q, G, err, s)))
     return rc;
   const int D = shape->head_dim;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq;
+  KVMaps kv;
   if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
-  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
-    return rc;
-  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+  if ((rc = make_kv_maps(kv.k, kv.v, kNumBoxes, k, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride)))
     return rc;
   FwdParams p{};
   p.tiles = plan.tiles;
@@ -120,7 +119,7 @@ extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_sha
   p.half_window = 0;
   p.lse_natural = 0;
   p.err = err;
-  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
 }
 
 extern "C" size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode) {
@@ -167,10 +166,10 @@ extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shap
   if ((rc = dense_fwd_tiles(meta, G, mode, window, plan, err, s))) return rc;
   const int D = shape->head_dim, qpt = kRows / G;
   const long long nk = (mode == LSRM_DENSE_COMPRESSED) ? meta->num_blocks : meta->total_k;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq;
+  KVMaps kv;
   if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
-  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, nk, shape->kv_token_stride, 1, kKVChunk))) return rc;
-  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, nk, shape->kv_token_stride, 1, kKVChunk))) return rc;
+  if ((rc = make_kv_maps(kv.k, kv.v, kNumBoxes, k, v, D, shape->num_kv_heads, nk, shape->kv_token_stride))) return rc;
   FwdParams p{};
   p.tiles = plan.tiles;
   p.n_tiles = plan.n_tiles;
@@ -187,8 +186,8 @@ extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shap
   p.err = err;
   const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
   if (mode == LSRM_DENSE_SLIDING)
-    return launch_fwd<kBand>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
-  return launch_fwd<kRange>(D, bf16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+    return launch_fwd<kBand>(D, bf16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
+  return launch_fwd<kRange>(D, bf16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -293,11 +292,10 @@ extern "C" int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_
   if ((rc = launch_build_unions(plan, meta, block_topk, topk, qblock ? num_query_blocks : meta->total_q, G, err, s)))
     return rc;
   const int D = shape->head_dim;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq;
+  KVMaps kv;
   if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, qpt))) return rc;
-  if ((rc = make_tmap_3d(&mk, k, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
-    return rc;
-  if ((rc = make_tmap_3d(&mv, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride, 1, kGroupRows)))
+  if ((rc = make_kv_maps(kv.k, kv.v, kNumBoxes, k, v, D, shape->num_kv_heads, meta->total_k, shape->kv_token_stride)))
     return rc;
   FwdParams p{};
   p.tiles = plan.tiles;
@@ -320,5 +318,5 @@ extern "C" int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_
   p.half_window = 0;
   p.lse_natural = 0;
   p.err = err;
-  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, mk, mv, p, plan.tiles_ub, shape->num_kv_heads, s);
+  return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
 }

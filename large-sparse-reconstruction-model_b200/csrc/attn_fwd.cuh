@@ -1,13 +1,16 @@
 // Forward attention kernel for sm_100a: one CTA per (query tile, kv head).
 //
-// Roles (192 threads):
-//   warps 0-3  softmax: thread r owns MMA row r (query r/G, head r%G); reads
-//              S = Q K^T from TMEM, applies the row's key mask, online softmax
-//              in log2 units, writes P (bf16/fp16) to shared memory, folds
-//              P V from TMEM into fp32 registers, writes O and the LSE.
-//   warp 4     producer: TMA loads of the Q tile and of K/V chunks (128 keys)
+// Roles (320 threads):
+//   warps 0-7  softmax: warps w and w+4 own MMA rows 32*(w%4).. (row r =
+//              query r/G, head r%G) and split each 128-key chunk into two
+//              64-key halves; they read S = Q K^T from TMEM, apply the row's
+//              key mask, exchange partial row max / row sum through shared
+//              memory (online softmax in log2 units), write their half of P
+//              (bf16/fp16) to shared memory, and each folds half of O's
+//              columns of P V from TMEM into fp32 registers.
+//   warp 8     producer: TMA loads of the Q tile and of K/V chunks (128 keys)
 //              into a STAGES-deep ring.
-//   warp 5     MMA issuer (lane 0): S_j = Q K_j^T (M=128, N=128), then
+//   warp 9     MMA issuer (lane 0): S_j = Q K_j^T (M=128, N=128), then
 //              O_j = P_j V_j (M=128, N=D); S and PV double-buffered in TMEM.
 //
 // KV chunk sources:
@@ -69,7 +72,8 @@ struct FwdSmem {
   static constexpr int OFF_K = OFF_Q + TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
   static constexpr int OFF_P = OFF_V + STAGES * TILE;
-  static constexpr int OFF_META = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_XCH = OFF_P + 2 * P_BYTES;  // row max / row sum exchange [2][2][128]
+  static constexpr int OFF_META = OFF_XCH + 4 * 128 * 4;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(ChunkMeta);
   // barriers: kv_full[S], kv_empty[S], q_full, s_full[2], s_free[2], p_full[2],
   // p_free[2], pv_full[2], pv_free[2], mma_done
@@ -79,10 +83,16 @@ struct FwdSmem {
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
 };
 
+constexpr int kFwdThreads = 320;
+
+__device__ __forceinline__ void pair_bar(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
+
 template <int D, bool BF16, int MODE, int STAGES>
-__global__ void __launch_bounds__(192, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const FwdParams prm) {
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ KVMaps kv,
+                    const FwdParams prm) {
   using L = FwdSmem<D, STAGES>;
   constexpr int RB = L::RB;
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
@@ -137,11 +147,11 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_free[i], 8);
+      mbar_init(&p_full[i], 8);
       mbar_init(&p_free[i], 1);
       mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_free[i], 4);
+      mbar_init(&pv_free[i], 8);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -158,11 +168,9 @@ __global__ void __launch_bounds__(192, 1)
   // TMEM columns: S0 [0,128), S1 [128,256), PV0 [256,256+D), PV1 [256+D, 256+2D)
   const uint32_t tm_s0 = tmem, tm_pv0 = tmem + 256;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(q_full, L::TILE);
       tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, q_full);
       int u = -1, tcur = 0, tend = 0;  // select-mode walk state
@@ -199,19 +207,15 @@ __global__ void __launch_bounds__(192, 1)
           }
           for (int w = 0; w < 4; ++w) mt.colmask[w] = cm[w];
           mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
-          for (int g = 0; g < kGroupsPerChunk; ++g) {
-            // unused groups read past the end of the tensor: zero fill
-            const int row = mt.row0[g] >= 0 ? mt.row0[g] : prm.total_k;
-            tma_load_3d(dK + g * kGroupRows * RB, &tm_k, 0, h, row, &kv_full[s]);
-            tma_load_3d(dV + g * kGroupRows * RB, &tm_v, 0, h, row, &kv_full[s]);
-          }
+          // unused groups read past the end of the tensor: zero fill
+          load_group_runs<kGroupsPerChunk, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
         } else {
           const int k0 = tile.kv_lo + j * kKVChunk;
           mt.kv_start = k0;
           mt.n_valid = min(kKVChunk, tile.kv_hi - k0);
           mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
-          tma_load_3d(dK, &tm_k, 0, h, k0, &kv_full[s]);
-          tma_load_3d(dV, &tm_v, 0, h, k0, &kv_full[s]);
+          tma_load_3d(dK, &kv.k[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
+          tma_load_3d(dV, &kv.v[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
         }
         issued = j + 1;
       }
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------ MMA issuer -----------------------------
     if (lane == 0) {
       const uint32_t idesc_qk = make_idesc(AB, 0, 0, 128, 128);
@@ -271,17 +275,20 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------ softmax -------------------------------
-    const int r = threadIdx.x;  // MMA row
+    constexpr int DH = D / 2;  // output columns folded by each warp of a pair
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;  // MMA row
     const int qloc = r / G;
     const int hq = h * G + (r % G);
     const int qi = tile.q_start + qloc;
     const bool row_valid = qloc < tile.n_q;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2;
+    float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);  // [max|sum][half][128]
     float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    float o[D];
+    float o[DH];
 #pragma unroll
-    for (int c = 0; c < D; ++c) o[c] = 0.f;
+    for (int c = 0; c < DH; ++c) o[c] = 0.f;
     bool ok = true;
 
     auto fold_pv = [&](int i) -> bool {
@@ -289,11 +296,11 @@ __global__ void __launch_bounds__(192, 1)
       if (!warp_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
       tc_fence_after();
       {
-        float pv[D];
-        tmem_load_cols<D>(tm_pv0 + pb * D + lane_base, pv);
+        float pv[DH];
+        tmem_load_cols<DH>(tm_pv0 + pb * D + half * DH + lane_base, pv);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < D; ++c) o[c] = fmaf(o[c], alpha_prev, pv[c]);
+        for (int c = 0; c < DH; ++c) o[c] = fmaf(o[c], alpha_prev, pv[c]);
       }
       tc_fence_before();
       __syncwarp();
@@ -306,18 +313,19 @@ __global__ void __launch_bounds__(192, 1)
       if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
       if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
-      // key-validity mask of this row for the 128 columns of the chunk
-      uint32_t vm[4];
+      // key-validity mask of this row for the warp's 64 columns (2 words)
+      uint32_t vm[2];
       const ChunkMeta& mt = meta[s];
       if constexpr (MODE == kSelect) {
         const int w = qloc >> 5, b = qloc & 31;
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int xx = 0; xx < 2; ++xx) {
+          const int x = 2 * half + xx;
           uint32_t e = 0u;
 #pragma unroll
           for (int y = 0; y < 4; ++y)
             if ((mt.qmask[x * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
-          vm[x] = e & mt.colmask[x];
+          vm[xx] = e & mt.colmask[x];
         }
       } else {
         int lo = 0, hi = mt.n_valid;  // valid columns [lo, hi)
@@ -326,58 +334,63 @@ __global__ void __launch_bounds__(192, 1)
           hi = min(hi, qi + prm.half_window + 1 - mt.kv_start);
         }
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int xx = 0; xx < 2; ++xx) {
+          const int x = 2 * half + xx;
           const int a = max(lo - 32 * x, 0), bnd = min(hi - 32 * x, 32);
           uint32_t e = 0u;
           if (bnd > a) e = ((bnd - a) == 32 ? 0xffffffffu : ((1u << (bnd - a)) - 1u)) << a;
-          vm[x] = e;
+          vm[xx] = e;
         }
       }
-      const uint32_t tm_s = tm_s0 + sb * 128 + lane_base;
-      // pass 1: row max over valid columns
+      const uint32_t tm_s = tm_s0 + sb * 128 + lane_base + half * 64;
+      float sv[2][32];
+      tmem_ld32(tm_s, sv[0]);
+      tmem_ld32(tm_s + 32, sv[1]);
+      tmem_wait_ld();
+      // S of this chunk is in registers: the TMEM buffer can be refilled
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      // row max over this half, then over the pair
       float mx = -INFINITY;
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        float sv[32];
-        tmem_ld32(tm_s + x * 32, sv);
-        tmem_wait_ld();
+      for (int xx = 0; xx < 2; ++xx)
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[x] >> c) & 1u) ? sv[c] : -INFINITY);
-      }
+        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[xx] >> c) & 1u) ? sv[xx][c] : -INFINITY);
+      xch[half * 128 + r] = mx;
+      pair_bar(quarter);
+      mx = fmaxf(xch[r], xch[128 + r]);
       const float m_new = fmaxf(m, mx * sl2);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      // pass 2: probabilities -> P (shared, K-major 128B swizzle)
+      // probabilities -> P (shared, K-major 128B swizzle; this half = region `half`)
       if (!warp_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-      float rowsum = 0.f;
-      const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES);
+      float rs = 0.f;
+      const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES) + half * 16384;
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        float sv[32];
-        tmem_ld32(tm_s + x * 32, sv);
-        tmem_wait_ld();
+      for (int xx = 0; xx < 2; ++xx) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float e = ex2(fmaf(sv[c], sl2, -m_use));  // unconditional: no branch per element
-          const float pv = ((vm[x] >> c) & 1u) ? e : 0.f;
-          sv[c] = pv;
-          rowsum += pv;
+          const float e = ex2(fmaf(sv[xx][c], sl2, -m_use));  // unconditional: no branch per element
+          const float pv = ((vm[xx] >> c) & 1u) ? e : 0.f;
+          sv[xx][c] = pv;
+          rs += pv;
         }
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = x * 4 + q8;  // 16-byte chunk index along the 128 keys
-          const uint32_t addr = p_base + (ch >> 3) * 16384 + swz_offset<128>(r, ch & 7);
-          st_shared_v4(addr, pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]), pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]),
-                       pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]), pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
+          const int ch = xx * 4 + q8;  // 16-byte chunk inside this half's 64-key region
+          st_shared_v4(p_base + swz_offset<128>(r, ch), pack2<BF16>(sv[xx][q8 * 8 + 0], sv[xx][q8 * 8 + 1]),
+                       pack2<BF16>(sv[xx][q8 * 8 + 2], sv[xx][q8 * 8 + 3]),
+                       pack2<BF16>(sv[xx][q8 * 8 + 4], sv[xx][q8 * 8 + 5]),
+                       pack2<BF16>(sv[xx][q8 * 8 + 6], sv[xx][q8 * 8 + 7]));
         }
       }
-      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[sb]);
-        mbar_arrive(&p_full[sb]);
-      }
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+      xch[256 + half * 128 + r] = rs;
+      pair_bar(quarter);
+      const float rowsum = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps
       l = l * alpha + rowsum;
       if (j >= 1 && !fold_pv(j - 1)) { ok = false; break; }
       alpha_prev = alpha;
@@ -386,9 +399,10 @@ __global__ void __launch_bounds__(192, 1)
     if (ok && n_chunks > 0) ok = fold_pv(n_chunks - 1);
     if (ok && row_valid) {
       const float inv = (l > 0.f) ? 1.f / l : __int_as_float(0x7fc00000);
-      uint8_t* orow = static_cast<uint8_t*>(prm.out) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
+      uint8_t* orow =
+          static_cast<uint8_t*>(prm.out) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D + half * DH) * 2;
 #pragma unroll
-      for (int c = 0; c < D; c += 8) {
+      for (int c = 0; c < DH; c += 8) {
         uint4 pk;
         pk.x = pack2<BF16>(o[c] * inv, o[c + 1] * inv);
         pk.y = pack2<BF16>(o[c + 2] * inv, o[c + 3] * inv);
@@ -396,9 +410,11 @@ __global__ void __launch_bounds__(192, 1)
         pk.w = pack2<BF16>(o[c + 6] * inv, o[c + 7] * inv);
         *reinterpret_cast<uint4*>(orow + c * 2) = pk;
       }
-      float lse = (l > 0.f) ? m + __log2f(l) : -INFINITY;
-      if (prm.lse_natural) lse *= 0.69314718055994531f;
-      prm.lse[(size_t)hq * prm.total_q + qi] = lse;
+      if (half == 0) {
+        float lse = (l > 0.f) ? m + __log2f(l) : -INFINITY;
+        if (prm.lse_natural) lse *= 0.69314718055994531f;
+        prm.lse[(size_t)hq * prm.total_q + qi] = lse;
+      }
     }
   }
 

@@ -194,6 +194,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
   asm volatile(
@@ -240,11 +247,13 @@ __host__ __device__ constexpr uint64_t swz_for_row_bytes(int RB) {
   return RB == 128 ? kSw128 : (RB == 64 ? kSw64 : kSw32);
 }
 
-// Loads N (16 or a multiple of 32) consecutive fp32 TMEM columns of this
+// Loads N (8, 16 or a multiple of 32) consecutive fp32 TMEM columns of this
 // warp's 32 lanes into v[0..N).
 template <int N>
 __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* v) {
-  if constexpr (N == 16) {
+  if constexpr (N == 8) {
+    tmem_ld8(taddr, v);
+  } else if constexpr (N == 16) {
     tmem_ld16(taddr, v);
   } else {
 #pragma unroll
@@ -304,6 +313,138 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+}  // namespace lsrm
+
+namespace lsrm {
+
+// Loads the groups of a select-mode chunk: row0[g] is the first key token of
+// 8-row group g (-1: unused, zero filled).  Runs of groups that are
+// contiguous in memory are split into power-of-two boxes (8..128 rows) of the
+// maps in `maps_k`/`maps_v` (box heights 8 << i).  Destinations stay aligned
+// to 8 rows (the swizzle atom).
+template <int NG, int RB>
+__device__ __forceinline__ void load_group_runs(const int* row0, uint8_t* dK, uint8_t* dV, const CUtensorMap* maps_k,
+                                                const CUtensorMap* maps_v, int h, int oob_row, uint64_t* bar) {
+  int g = 0;
+  while (g < NG) {
+    const int r = row0[g];
+    int n = 1;
+    if (r >= 0) {
+      while (g + n < NG && row0[g + n] == r + 8 * n) ++n;
+    } else {
+      while (g + n < NG && row0[g + n] < 0) ++n;
+    }
+    int done = 0;
+    while (done < n) {
+      const int rem = n - done;
+      const int mi = 31 - __clz(rem);  // largest power of two <= rem
+      const int piece = 1 << mi;
+      const int row = r >= 0 ? r + 8 * done : oob_row;
+      tma_load_3d(dK + (g + done) * 8 * RB, &maps_k[mi], 0, h, row, bar);
+      tma_load_3d(dV + (g + done) * 8 * RB, &maps_v[mi], 0, h, row, bar);
+      done += piece;
+    }
+    g += n;
+  }
+}
+
+}  // namespace lsrm
+
+namespace lsrm {
+
+// ---------------------------------------------------------------------------
+// Union cache: a tile's selected blocks in shared memory, so a producer warp
+// can lay out the 8-token groups of any KV chunk with one lane per group.
+// ---------------------------------------------------------------------------
+constexpr int kUnionCacheCap = 512;
+
+struct UnionCache {
+  int t0[kUnionCacheCap];     // first token (clipped to the tile's KV range)
+  int t1[kUnionCacheCap];     // end token
+  int gstart[kUnionCacheCap]; // first group index (exclusive prefix of group counts)
+  uint4 mask[kUnionCacheCap]; // queries of the tile that selected the block
+  int n;                      // entries cached (== U when the union fits)
+  int groups;                 // total groups
+};
+
+// Warp-wide fill (all 32 lanes).  Returns false when the union does not fit.
+__device__ __forceinline__ bool union_cache_fill(UnionCache& uc, int U, const int* union_blk, const uint4* union_mask,
+                                                 size_t ubase, const int32_t* cu_blk, int kv_lo, int kv_hi) {
+  const int lane = threadIdx.x & 31;
+  if (U > kUnionCacheCap) return false;
+  int carry = 0;
+  for (int b0 = 0; b0 < U; b0 += 32) {
+    const int e = b0 + lane;
+    int t0 = 0, t1 = 0, g = 0;
+    uint4 m = make_uint4(0u, 0u, 0u, 0u);
+    if (e < U) {
+      const int gb = union_blk[ubase + e];
+      t0 = max(cu_blk[gb], kv_lo);
+      t1 = min(cu_blk[gb + 1], kv_hi);
+      if (t1 < t0) t1 = t0;
+      g = (t1 - t0 + 7) >> 3;
+      m = union_mask[ubase + e];
+    }
+    int incl = g;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (e < U) {
+      uc.t0[e] = t0;
+      uc.t1[e] = t1;
+      uc.gstart[e] = carry + incl - g;
+      uc.mask[e] = m;
+    }
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) {
+    uc.n = U;
+    uc.groups = carry;
+  }
+  __syncwarp();
+  return true;
+}
+
+// Lays out groups [NG*j, NG*j+NG) of the union into row0 / qmask / colmask
+// (one lane per group, lanes >= NG idle).  Warp-wide.
+template <int NG>
+__device__ __forceinline__ void union_cache_chunk(const UnionCache& uc, int j, int* row0, uint32_t (*qmask)[4],
+                                                  uint32_t* colmask) {
+  const int lane = threadIdx.x & 31;
+  uint32_t bits = 0u;
+  if (lane < NG) {
+    const int g = NG * j + lane;
+    if (g < uc.groups) {
+      int lo = 0, hi = uc.n;  // last entry with gstart <= g (entries with no group share a start)
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (uc.gstart[mid] <= g) lo = mid;
+        else hi = mid;
+      }
+      while (lo + 1 < uc.n && uc.gstart[lo + 1] <= g) ++lo;
+      const int r = uc.t0[lo] + 8 * (g - uc.gstart[lo]);
+      const int cnt = min(8, uc.t1[lo] - r);
+      row0[lane] = r;
+      const uint4 m = uc.mask[lo];
+      qmask[lane][0] = m.x;
+      qmask[lane][1] = m.y;
+      qmask[lane][2] = m.z;
+      qmask[lane][3] = m.w;
+      bits = ((1u << cnt) - 1u) << ((lane & 3) * 8);
+    } else {
+      row0[lane] = -1;
+      qmask[lane][0] = qmask[lane][1] = qmask[lane][2] = qmask[lane][3] = 0u;
+    }
+  }
+  // colmask word w collects the bytes of groups 4w..4w+3
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
+  if (lane < NG && (lane & 3) == 0) colmask[lane >> 2] = bits;
+  __syncwarp();
 }
 
 }  // namespace lsrm

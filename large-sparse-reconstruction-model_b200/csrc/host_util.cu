@@ -70,6 +70,16 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int D, int n_head, long lon
   return LSRM_OK;
 }
 
+int make_kv_maps(CUtensorMap* maps_k, CUtensorMap* maps_v, int n, const void* k, const void* v, int D, int n_head,
+                 long long n_tok, long long tok_stride) {
+  for (int i = 0; i < n; ++i) {
+    int rc;
+    if ((rc = make_tmap_3d(&maps_k[i], k, D, n_head, n_tok, tok_stride, 1, 8 << i))) return rc;
+    if ((rc = make_tmap_3d(&maps_v[i], v, D, n_head, n_tok, tok_stride, 1, 8 << i))) return rc;
+  }
+  return LSRM_OK;
+}
+
 // ------------------------------ profiler ----------------------------------
 struct ProfRecord {
   std::string name;

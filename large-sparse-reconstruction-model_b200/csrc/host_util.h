@@ -70,6 +70,10 @@ class ProfScope {
 int make_tmap_3d(CUtensorMap* map, const void* base, int D, int n_head, long long n_tok, long long tok_stride,
                  int box_h, int box_n);
 
+// Fills maps_k/maps_v (box heights 8 << i rows, i < n) over k and v.
+int make_kv_maps(CUtensorMap* maps_k, CUtensorMap* maps_v, int n, const void* k, const void* v, int D, int n_head,
+                 long long n_tok, long long tok_stride);
+
 template <typename T>
 inline T ceil_div(T a, T b) {
   return (a + b - 1) / b;

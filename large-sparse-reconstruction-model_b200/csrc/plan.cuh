@@ -11,6 +11,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 
 #include "lsrm_sparse.h"
 
@@ -40,6 +41,14 @@ constexpr int kRows = 128;     // MMA M (rows of a query or KV tile)
 constexpr int kKVChunk = 128;  // keys per KV chunk (MMA N of S = Q K^T)
 constexpr int kGroupRows = 8;  // rows per TMA gather group in select mode
 constexpr int kGroupsPerChunk = kKVChunk / kGroupRows;
+
+// TMA maps over K and V with box heights 8, 16, 32, 64, 128 rows; used to
+// load runs of consecutive 8-token groups with as few copies as possible.
+constexpr int kNumBoxes = 5;
+struct KVMaps {
+  CUtensorMap k[kNumBoxes];
+  CUtensorMap v[kNumBoxes];
+};
 
 // Workspace layout for selected-block attention.
 struct SelectPlan {
