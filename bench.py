@@ -38,6 +38,9 @@ CONFIGS = {
     # configs[0] at its sizes (contiguous uniform blocks), on the GPU
     "cfg1": dict(n=4096, heads=8, head_dim=64, n_blocks=64, blk_min=32, blk_max=96, topk=8, window=128,
                  gate="per_head", voxel=False),
+    # half-size cfg2 (same grid, block sizes, top-k, window) for full ncu captures
+    "cfg2s": dict(n=65536, heads=16, head_dim=64, res=256, blk_min=64, blk_max=256, topk=16, window=512,
+                  gate="per_head", voxel=True),
     # 512^3 shell, blocks 32-512, window 1024
     "cfg3": dict(n=262144, heads=16, head_dim=64, res=512, blk_min=32, blk_max=512, topk=16, window=1024,
                  gate="per_head", voxel=True),
@@ -134,6 +137,53 @@ def forward_backward(p: Problem, want_loss=False, capture=None):
     z = torch.nn.functional.linear(p.x, p.wg)
     out = F.gate_merge(z, [o_c.view(N, -1), o_s.view(N, -1), o_w.view(N, -1)], per_head=cfg["gate"] == "per_head",
                        head_dim=D)
+    loss = (out.float() * p.g.float()).sum() if want_loss else None
+    out.backward(p.g)
+    return loss
+
+
+class ShardedProblem:
+    """One rank's view of the whole cfg problem under Ulysses sequence
+    parallelism: its token shard on the device (whole blocks, token-balanced),
+    the whole block table, the gate weight."""
+
+    def __init__(self, full: Problem, plan, device):
+        self.full, self.plan, self.device = full, plan, device
+        self.cfg, self.lens = full.cfg, full.lens
+        self.N, self.H, self.D, self.nb = full.N, full.H, full.D, full.nb
+        s, e = plan.local
+        self.h_local = [t[s:e] for t in (full.h_q, full.h_k, full.h_v, full.h_x, full.h_g)]
+        self.h_cu_blk = full.h_cu_blk
+        self.to_device()
+        self.wg = full.gate_w.to(device).requires_grad_()
+
+    def to_device(self, non_blocking=False):
+        d = self.device
+        q, k, v, x, g = (t.to(d, non_blocking=non_blocking) for t in self.h_local)
+        self.q, self.k, self.v, self.x = (t.requires_grad_() for t in (q, k, v, x))
+        self.g = g
+        self.cu_blk = self.h_cu_blk.to(d, non_blocking=non_blocking)
+
+    def h2d_bytes(self):
+        return int(sum(t.numel() * t.element_size() for t in self.h_local + [self.h_cu_blk]))
+
+
+def forward_backward_sp(p: ShardedProblem, want_loss=False, capture=None):
+    """One sequence-parallel step: gate logits on the local tokens, Ulysses
+    exchange, whole-sequence three-branch op for this rank's heads, exchange
+    back, backward through the same path."""
+    from lsrm_sparse import ulysses
+
+    cfg = p.cfg
+    n = p.q.shape[0]
+    z = torch.nn.functional.linear(p.x, p.wg)
+    fn = None
+    if capture is not None:
+        def fn(*a):
+            return ulysses.whole_sequence_branches(*a, capture=capture)
+    out = ulysses.three_branch_attention(p.q, p.k, p.v, z, p.plan, p.cu_blk, cfg["topk"], cfg["window"],
+                                         branch_fn=fn)
+    out = out.view(n, -1)
     loss = (out.float() * p.g.float()).sum() if want_loss else None
     out.backward(p.g)
     return loss
@@ -269,22 +319,24 @@ def run_reference(args, cfg):
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(secs),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-sphere SDF shell voxels, Morton octree blocks)",
-        "config": workload_config(cfg, p),
+        "config": workload_config(cfg, p, ws),
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line, default=_json_default), flush=True)
 
 
-def workload_config(cfg, p):
-    return {"workload": f"three-branch sparse attention fwd+bwd, N={cfg['n']} voxel tokens, H={cfg['heads']}, "
+def workload_config(cfg, p, world=1):
+    return {"parallelism": f"ulysses sequence parallel over {world} GPUs (strong scaling)" if world > 1
+            else "single GPU","workload": f"three-branch sparse attention fwd+bwd, N={cfg['n']} voxel tokens, H={cfg['heads']}, "
                         f"d={cfg['head_dim']}, top-{cfg['topk']} per query block, window {cfg['window']}",
             "tokens": cfg["n"], "heads": cfg["heads"], "head_dim": cfg["head_dim"], "blocks": p.nb,
             "block_len": [min(p.lens), max(p.lens)], "topk": cfg["topk"], "window": cfg["window"],
             "gate": cfg["gate"], "selection": "per query block, bit-exact fp32 score, own block forced",
-            "l2": "inputs larger than L2 (q/k/v 268 MB each)", "grid_res": cfg.get("res")}
+            "l2": f"inputs larger than L2 (q/k/v {cfg['n'] * cfg['heads'] * cfg['head_dim'] * 2 / 1e6:.0f} MB each), no flush",
+            "grid_res": cfg.get("res")}
 
 
 def kernel_flops(name, pairs, H, D, N, nb):
@@ -310,17 +362,33 @@ def run_ours(args, cfg):
     from lsrm_sparse import _lib, ops
 
     lib_launches = _lib.launch_count
-    p = Problem(cfg, args.seed + rank, dev)
+    if ws > 1:
+        # Ulysses sequence parallelism: every rank builds the same whole
+        # problem on the host and keeps its token shard on the device
+        from lsrm_sparse import ulysses
+
+        full = Problem(cfg, args.seed, "cpu", pin=True)
+        plan = ulysses.ShardPlan(full.h_cu_blk.tolist(), ws, rank)
+        p = ShardedProblem(full, plan, dev)
+        step = forward_backward_sp
+    else:
+        p = Problem(cfg, args.seed, dev)
+        step = forward_backward
     cap = {}
-    forward_backward(p, capture=cap)
+    step(p, capture=cap)
     zero_grads(p)
     err = ops.read_errors()
     if err:
         raise RuntimeError(f"device error bits 0x{err:x} in the first step")
     pairs = count_pairs(p, cap["block_topk"])
+    if ws > 1:
+        # each rank selected for its own heads: the whole job's pairs are the sum
+        t = torch.tensor([float(pairs["select"])], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t)
+        pairs["select"] = int(t.item())
     flops_step = 14.0 * p.D * (pairs["select"] + pairs["compressed"] + pairs["sliding"])
     for _ in range(max(args.warmup - 1, 0)):
-        forward_backward(p)
+        step(p)
         zero_grads(p)
 
     def barrier():
@@ -336,24 +404,27 @@ def run_ours(args, cfg):
     with ClockSampler(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            forward_backward(p)
+            step(p)
             zero_grads(p)
         ev1.record(stream)
         torch.cuda.synchronize()
     launches = lib_launches() - n0
     barrier()
+    if rank == 0:
+        print(f"device memory: {torch.cuda.max_memory_allocated(dev) / 2**30:.2f} GiB allocated at peak",
+              file=sys.stderr, flush=True)
     ms = ev0.elapsed_time(ev1) / args.steps
     ms_max = ms
     if ws > 1:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = ws * flops_step / (ms_max * 1e-3) / 1e12
+    value = flops_step / (ms_max * 1e-3) / 1e12  # whole job: one problem (N=1) or one sharded problem (N>1)
 
     # ---- profiled pass: per-kernel device time (events on the launching stream) ----
     _lib.profile_enable(True)
     for _ in range(args.steps):
-        forward_backward(p)
+        step(p)
         zero_grads(p)
     torch.cuda.synchronize()
     prof = _lib.profile_collect()
@@ -385,7 +456,7 @@ def run_ours(args, cfg):
         e0.record(stream)
         for _ in range(e_steps):
             p.to_device(non_blocking=True)
-            loss = forward_backward(p, want_loss=True)
+            loss = step(p, want_loss=True)
             float(loss.item())  # device -> host read of the step's result
             zero_grads(p)
         e1.record(stream)
@@ -395,7 +466,7 @@ def run_ours(args, cfg):
             t = torch.tensor([e_ms], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e_ms = float(t.item())
-        e2e = {"value": ws * flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
+        e2e = {"value": flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": p.h2d_bytes(), "d2h_bytes_per_step": 4}
 
     cpu = None
@@ -410,12 +481,12 @@ def run_ours(args, cfg):
         return
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": f"synthetic: seeded random-sphere SDF shell ({p.shell} shell voxels, subsampled), Morton octree "
                 "blocks; q/k/v N(0,1), grad N(0,0.1)",
-        "config": workload_config(cfg, p),
-        "tokens_per_s": ws * p.N / (ms_max * 1e-3),
+        "config": workload_config(cfg, p, ws),
+        "tokens_per_s": p.N / (ms_max * 1e-3),
         "flops_per_step": flops_step,
         "pairs_per_step": pairs,
         "roofline": roofline,

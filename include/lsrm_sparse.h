@@ -70,7 +70,7 @@ typedef struct lsrm_varlen {
 typedef struct lsrm_attn_shape {
   int32_t num_q_heads;   /* Hq */
   int32_t num_kv_heads;  /* Hkv; Hq % Hkv == 0, G = Hq/Hkv a power of two <= 128 */
-  int32_t head_dim;      /* D: 32 or 64 */
+  int32_t head_dim;      /* D: 16, 32 or 64 */
   int32_t dtype;         /* LSRM_DTYPE_* */
   int64_t q_token_stride;  /* elements between consecutive tokens of q/o/do/dq */
   int64_t kv_token_stride; /* elements between consecutive tokens of k/v/dk/dv */
@@ -242,6 +242,25 @@ int lsrm_gate_merge_fwd(int32_t total_tokens, int32_t channels, int32_t n_branch
 int lsrm_gate_merge_bwd(int32_t total_tokens, int32_t channels, int32_t n_branch, int32_t per_head,
                         int32_t head_dim, int32_t dtype, const void* z, const void* const* branches,
                         const void* dout, void* dz, void* const* dbranches, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Ulysses sequence <-> head exchange (sequence parallelism over W ranks)   */
+/* ---------------------------------------------------------------------- */
+/* Replaces the layout side of the reference's sequence-parallel exchange
+ * (models_sparse/utils.py:326-474 all-gathers its KV tokens; here queries,
+ * keys, values and gate logits are moved once by all_to_all_single).  A
+ * rank's head slice holds hp = H/W heads (H >= W) or one head shared by
+ * W/H ranks (H < W, grouped-query kv heads).  Both calls need 16-byte
+ * aligned buffers and hp*D*2 a multiple of 16 bytes.
+ *
+ * pack:   src [n, H, D] (token stride given) -> dst [W, n, hp, D] contiguous;
+ *         rank p's slice holds heads starting at (p / rep) * hp.
+ * unpack: src [W, n, hp, D] -> dst [n, H, D]; the rep replicas of a head
+ *         are summed in rank order in fp32 (the backward of pack). */
+int lsrm_ulysses_pack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int32_t world, int32_t dtype,
+                      int64_t src_token_stride, const void* src, void* dst, void* stream);
+int lsrm_ulysses_unpack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int32_t world, int32_t dtype,
+                        const void* src, int64_t dst_token_stride, void* dst, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Self-test of the tcgen05 / TMA building blocks (used by the GPU tests)   */

@@ -115,6 +115,10 @@ _SIGS = {
         [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p],
     ),
+    "lsrm_ulysses_pack": (c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_void_p]),
+    "lsrm_ulysses_unpack": (
+        c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
+    ),
     "lsrm_umma_selftest": (
         c_int, [c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     ),

@@ -316,3 +316,29 @@ def gate_merge_bwd(z, branches: Sequence[torch.Tensor], dout, per_head: bool = F
                                _ptr_array(branches), _ptr(dout.contiguous()), _ptr(dz), _ptr_array(dbr), _stream())
     check(rc, "lsrm_gate_merge_bwd")
     return dz, dbr
+
+
+def ulysses_pack(x: torch.Tensor, world: int) -> torch.Tensor:
+    """[n, H, D] -> [W, n, hp, D]: the head slice of every rank, rank-major
+    (hp = H/W, or one replicated head when H < W)."""
+    L = _lib.lib()
+    n, H, D = x.shape
+    if x.stride(2) != 1 or x.stride(1) != D:
+        x = x.contiguous()
+    hp = H // world if H >= world else 1
+    out = torch.empty(world, n, hp, D, dtype=x.dtype, device=x.device)
+    rc = L.lsrm_ulysses_pack(n, H, D, world, _dtype_code(x), x.stride(0), _ptr(x), _ptr(out), _stream())
+    check(rc, "lsrm_ulysses_pack")
+    return out
+
+
+def ulysses_unpack(y: torch.Tensor, num_heads: int) -> torch.Tensor:
+    """[W, n, hp, D] -> [n, H, D]; replicas of one head are summed in rank
+    order (fp32)."""
+    L = _lib.lib()
+    world, n, hp, D = y.shape
+    y = y.contiguous()
+    out = torch.empty(n, num_heads, D, dtype=y.dtype, device=y.device)
+    rc = L.lsrm_ulysses_unpack(n, num_heads, D, world, _dtype_code(y), _ptr(y), out.stride(0), _ptr(out), _stream())
+    check(rc, "lsrm_ulysses_unpack")
+    return out

@@ -1,0 +1,263 @@
+"""Ulysses sequence parallelism for the three-branch sparse attention.
+
+The voxel sequence is split across the W ranks of a process group into
+contiguous runs of whole blocks (Morton order), balanced by token count with
+the same greedy rule as the reference (models_sparse/seqparallel_utils.py:
+547-601), so a caller that already holds the reference's shards keeps them.
+
+Every branch of the op (compression, scoring, top-k, selected, sliding and
+compressed attention, per-head gates) factors over heads, so one exchange
+each way suffices: ``seq_to_head`` moves every rank's tokens of the heads
+that rank computes (one ``all_to_all_single``; the CUDA pack kernel lays the
+slices out rank-major and the received buffer is already token-major), the
+rank runs the whole-sequence op for its H/W heads, and ``head_to_seq`` brings
+the merged output back.  The backward is the same exchange in reverse.  The
+reference instead all-gathers all K/V tokens on every rank
+(models_sparse/utils.py:326-474); for H = Hkv the Ulysses exchange moves about
+a quarter of those bytes.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+__all__ = ["shard_blocks", "ShardPlan", "seq_to_head", "head_to_seq", "exchange_gate_logits",
+           "three_branch_attention"]
+
+
+def shard_blocks(cu_block_include_tokens: Sequence[int], world: int) -> List[Tuple[int, int]]:
+    """Per rank ``(first_block, end_block)``: contiguous runs of whole blocks
+    with balanced token counts.
+
+    Restates the greedy of seqparallel_utils.py:547-601: rank r aims at
+    (tokens left) / (ranks left), takes at least one block, and keeps taking
+    the next block while that brings its count at least as close to the aim;
+    the last rank takes what remains."""
+    cu = [int(x) for x in cu_block_include_tokens]
+    nb = len(cu) - 1
+    if world < 1:
+        raise ValueError("world size must be >= 1")
+    out = []
+    b = 0
+    for r in range(world):
+        if r == world - 1:
+            out.append((b, nb))
+            break
+        aim = (cu[nb] - cu[b]) / (world - r)
+        start, count = b, 0
+        while b < nb:
+            ln = cu[b + 1] - cu[b]
+            if b == start or abs(count + ln - aim) <= abs(count - aim):
+                count += ln
+                b += 1
+            else:
+                break
+        out.append((start, b))
+    return out
+
+
+class ShardPlan:
+    """Token ranges of every rank (host ints) and the split sizes of the
+    exchange."""
+
+    def __init__(self, cu_block_include_tokens: Sequence[int], world: int, rank: int):
+        cu = [int(x) for x in cu_block_include_tokens]
+        self.world, self.rank = world, rank
+        self.blocks = shard_blocks(cu, world)
+        self.tokens = [(cu[a], cu[b]) for a, b in self.blocks]
+        self.counts = [e - s for s, e in self.tokens]
+        self.total = cu[-1]
+
+    @property
+    def local(self) -> Tuple[int, int]:
+        return self.tokens[self.rank]
+
+    def heads_of(self, num_heads: int) -> Tuple[int, int]:
+        """Head range this rank computes (H >= W), or its replicated head."""
+        if num_heads >= self.world:
+            hp = num_heads // self.world
+            return self.rank * hp, (self.rank + 1) * hp
+        h = self.rank // (self.world // num_heads)
+        return h, h + 1
+
+
+def _check_heads(H: int, W: int):
+    if H % W and W % H:
+        raise ValueError(f"heads ({H}) and world size ({W}) must divide one another")
+
+
+class _SeqToHead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, plan: ShardPlan, group, pack: Callable, unpack: Callable):
+        n, H, D = x.shape
+        W = plan.world
+        _check_heads(H, W)
+        hp = H // W if H >= W else 1
+        send = pack(x, W)  # [W, n, hp, D]
+        recv = torch.empty(plan.total, hp, D, dtype=x.dtype, device=x.device)
+        row = hp * D
+        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W,
+                               group=group)
+        ctx.plan, ctx.group, ctx.unpack, ctx.H = plan, group, unpack, H
+        return recv
+
+    @staticmethod
+    def backward(ctx, g):
+        plan = ctx.plan
+        N, hp, D = g.shape
+        n = plan.counts[plan.rank]
+        back = torch.empty(plan.world, n, hp, D, dtype=g.dtype, device=g.device)
+        row = hp * D
+        dist.all_to_all_single(back.view(-1), g.contiguous().view(-1), [n * row] * plan.world,
+                               [c * row for c in plan.counts], group=ctx.group)
+        return ctx.unpack(back, ctx.H), None, None, None, None
+
+
+class _HeadToSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, plan: ShardPlan, num_heads: int, group, pack: Callable, unpack: Callable):
+        N, hp, D = y.shape
+        if num_heads < plan.world:
+            raise ValueError("head_to_seq needs at least one head per rank")
+        n = plan.counts[plan.rank]
+        back = torch.empty(plan.world, n, hp, D, dtype=y.dtype, device=y.device)
+        row = hp * D
+        dist.all_to_all_single(back.view(-1), y.contiguous().view(-1), [n * row] * plan.world,
+                               [c * row for c in plan.counts], group=group)
+        ctx.plan, ctx.group, ctx.pack = plan, group, pack
+        return unpack(back, num_heads)
+
+    @staticmethod
+    def backward(ctx, g):
+        plan = ctx.plan
+        n, H, D = g.shape
+        hp = H // plan.world
+        send = ctx.pack(g, plan.world)
+        recv = torch.empty(plan.total, hp, D, dtype=g.dtype, device=g.device)
+        row = hp * D
+        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * plan.world,
+                               group=ctx.group)
+        return recv, None, None, None, None, None
+
+
+def seq_to_head(x: torch.Tensor, plan: ShardPlan, group=None, pack: Callable = ops.ulysses_pack,
+                unpack: Callable = ops.ulysses_unpack) -> torch.Tensor:
+    """[n_local, H, D] (this rank's tokens, all heads) -> [N, hp, D] (all
+    tokens, this rank's heads).  Differentiable."""
+    return _SeqToHead.apply(x, plan, group, pack, unpack)
+
+
+def head_to_seq(y: torch.Tensor, plan: ShardPlan, num_heads: int, group=None, pack: Callable = ops.ulysses_pack,
+                unpack: Callable = ops.ulysses_unpack) -> torch.Tensor:
+    """[N, hp, D] -> [n_local, H, D].  Differentiable."""
+    return _HeadToSeq.apply(y, plan, num_heads, group, pack, unpack)
+
+
+def _pack_small(x: torch.Tensor, world: int) -> torch.Tensor:
+    # [n, B, H] -> [W, n, B, hp]: gate logits are a few bytes per head, below
+    # the 16-byte slices of the CUDA pack; a strided torch copy moves them.
+    n, B, H = x.shape
+    return x.view(n, B, world, H // world).permute(2, 0, 1, 3).contiguous()
+
+
+def _unpack_small(y: torch.Tensor, B: int, H: int) -> torch.Tensor:
+    W, n, _, hp = y.shape
+    return y.permute(1, 2, 0, 3).reshape(n, B, H)
+
+
+class _GateExchange(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, plan: ShardPlan, n_branch: int, group):
+        n, C = z.shape
+        H = C // n_branch
+        W = plan.world
+        if H % W:
+            raise ValueError("per-head gates need the heads to split evenly across ranks")
+        send = _pack_small(z.view(n, n_branch, H), W)
+        hp = H // W
+        recv = torch.empty(plan.total, n_branch, hp, dtype=z.dtype, device=z.device)
+        row = n_branch * hp
+        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W,
+                               group=group)
+        ctx.plan, ctx.group, ctx.B, ctx.H = plan, group, n_branch, H
+        return recv.view(plan.total, n_branch * hp)
+
+    @staticmethod
+    def backward(ctx, g):
+        plan = ctx.plan
+        W, B, H = plan.world, ctx.B, ctx.H
+        hp = H // W
+        n = plan.counts[plan.rank]
+        back = torch.empty(W, n, B, hp, dtype=g.dtype, device=g.device)
+        row = B * hp
+        dist.all_to_all_single(back.view(-1), g.contiguous().view(-1), [n * row] * W, [c * row for c in plan.counts],
+                               group=ctx.group)
+        return _unpack_small(back, B, H).reshape(n, B * H), None, None, None
+
+
+def exchange_gate_logits(z: torch.Tensor, plan: ShardPlan, n_branch: int, group=None) -> torch.Tensor:
+    """Per-head gate logits [n_local, n_branch*H] (column ``b*H + h``) ->
+    [N, n_branch*hp] for this rank's heads, same column rule.  Differentiable."""
+    return _GateExchange.apply(z, plan, n_branch, group)
+
+
+def three_branch_attention(q, k, v, z, plan: ShardPlan, cu_block_include_tokens: torch.Tensor, topk: int,
+                           window: int, group=None, branch_fn: Optional[Callable] = None,
+                           pack: Callable = ops.ulysses_pack, unpack: Callable = ops.ulysses_unpack,
+                           softmax_scale=None):
+    """Sequence-parallel compressed + selected + sliding-window attention with
+    per-head gates.
+
+    q [n_local, Hq, D], k/v [n_local, Hkv, D], z [n_local, 3*Hq] per-head gate
+    logits, all for this rank's tokens; ``cu_block_include_tokens`` is the
+    whole sequence's block table (every rank holds it).  Returns the merged
+    output [n_local, Hq, D].  ``branch_fn(q, k, v, z, cu_blk, topk, window,
+    scale)`` computes the merged output of the whole sequence for the heads it
+    is given; the default is :func:`whole_sequence_branches` (CUDA)."""
+    Hq, Hkv = q.shape[1], k.shape[1]
+    if Hkv % plan.world:
+        # the block score of a kv head sums over all q heads of its group
+        # (block_score.py:47-96); a group split across ranks would select
+        # differently, so every rank must own whole groups
+        raise ValueError(f"Ulysses needs the kv heads ({Hkv}) to split evenly over {plan.world} ranks")
+    fn = branch_fn or whole_sequence_branches
+    qh = seq_to_head(q, plan, group, pack, unpack)
+    kh = seq_to_head(k, plan, group, pack, unpack)
+    vh = seq_to_head(v, plan, group, pack, unpack)
+    zh = exchange_gate_logits(z, plan, 3, group)
+    oh = fn(qh, kh, vh, zh, cu_block_include_tokens, topk, window, softmax_scale)
+    return head_to_seq(oh, plan, Hq, group, pack, unpack)
+
+
+def whole_sequence_branches(q, k, v, z, cu_blk, topk: int, window: int, softmax_scale=None, capture=None):
+    """The single-rank op on one whole sequence: block-mean compression,
+    compressed attention, per-query-block top-k (own block forced), selected
+    and sliding-window attention, per-head sigmoid gates.  q [N, H, D],
+    k/v [N, Hkv, D], z [N, 3*H]."""
+    from . import functional as F
+
+    N, H, D = q.shape
+    Hkv = k.shape[1]
+    nb = cu_blk.numel() - 1
+    dev = q.device
+    cu_seq = torch.tensor([0, N], dtype=torch.int32, device=dev)
+    cu_sb = torch.tensor([0, nb], dtype=torch.int32, device=dev)
+    meta = ops.Meta(cu_seq, cu_seq, cu_sb, cu_blk)
+    meta_c = ops.Meta(cu_seq, cu_seq, cu_sb, torch.arange(nb + 1, dtype=torch.int32, device=dev))
+    ck = F.block_mean(k.reshape(N, Hkv * D), cu_blk).view(nb, Hkv, D)
+    cv = F.block_mean(v.reshape(N, Hkv * D), cu_blk).view(nb, Hkv, D)
+    o_c, lse = F.dense_attention(q, ck, cv, meta_c, ops.DENSE_COMPRESSED, 0, softmax_scale)
+    with torch.no_grad():
+        bt = ops.block_topk(q, ck, lse, topk, meta_c, cu_query_blocks=cu_blk, force_self=True,
+                            sm_scale=softmax_scale)
+    if capture is not None:
+        capture["block_topk"] = bt
+    o_s, _ = F.select_attention(q, k, v, bt, meta, softmax_scale, cu_blk)
+    o_w, _ = F.dense_attention(q, k, v, meta, ops.DENSE_SLIDING, window, softmax_scale)
+    out = F.gate_merge(z, [o_c.reshape(N, -1), o_s.reshape(N, -1), o_w.reshape(N, -1)], per_head=True, head_dim=D)
+    return out.view(N, H, D)

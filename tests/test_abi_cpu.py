@@ -1,0 +1,135 @@
+"""The C-ABI library on a host without a GPU: it loads, exports every entry
+point the header declares, and rejects bad arguments on the host (before any
+CUDA call) with the documented return codes and a message."""
+
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "lsrm_sparse.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^[A-Za-z_][\w \*]*?\b(lsrm_\w+)\s*\(", text, flags=re.M)))
+
+
+def _header_define(name):
+    m = re.search(rf"#define\s+{name}\s+\(?(-?\w+)\)?", open(HEADER).read())
+    return int(m.group(1), 0)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from lsrm_sparse import _lib
+
+    if not os.path.exists(_lib.LIB_PATH):
+        if shutil.which("nvcc") is None and not os.path.exists("/usr/local/cuda/bin/nvcc"):
+            pytest.skip("library not built and nvcc absent")
+        subprocess.run(["python", os.path.join(ROOT, "large-sparse-reconstruction-model_b200", "build.py")],
+                       check=True)
+    return _lib
+
+
+def test_header_declares_the_expected_entry_points():
+    names = _declared()
+    assert len(names) >= 21
+    for must in ("lsrm_select_attn_fwd", "lsrm_select_attn_bwd", "lsrm_select_attn_fwd_noalloc", "lsrm_block_topk",
+                 "lsrm_dense_attn_fwd", "lsrm_dense_attn_bwd", "lsrm_block_mean_fwd", "lsrm_gate_merge_fwd"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    declared = _declared()
+    h = lib.lib()
+    missing = [n for n in declared if not hasattr(h, n)]
+    assert not missing, missing
+    # the ctypes table binds exactly the header's entry points
+    assert sorted(lib.EXPORTED) == declared
+    nm = shutil.which("nm")
+    if nm:
+        out = subprocess.run([nm, "-D", "--defined-only", lib.LIB_PATH], capture_output=True, text=True).stdout
+        exported = {l.split()[-1] for l in out.splitlines() if l.strip()}
+        assert set(declared) <= exported
+
+
+def test_abi_version_matches_header(lib):
+    assert lib.lib().lsrm_abi_version() == _header_define("LSRM_ABI_VERSION")
+
+
+def _meta(total=256, blocks=4):
+    return lib_mod().Varlen(1, total, total, blocks, None, None, None, None)
+
+
+def lib_mod():
+    from lsrm_sparse import _lib
+
+    return _lib
+
+
+def _shape(Hq=4, Hkv=2, D=64, dtype=1):
+    L = lib_mod()
+    return L.AttnShape(Hq, Hkv, D, dtype, Hq * D, Hkv * D, 0.0)
+
+
+def _fwd(lib, meta, shape, topk=4, ws=None, ws_bytes=0):
+    h = lib.lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: every case fails host validation first
+    return h.lsrm_select_attn_fwd(ctypes.byref(meta), ctypes.byref(shape), p, p, p, p, topk, None, 0, p, p, ws,
+                                  ws_bytes, None, None)
+
+
+@pytest.mark.parametrize("bad,code,msg", [
+    (dict(D=48), "LSRM_ERR_INVALID_ARG", "head_dim"),
+    (dict(dtype=7), "LSRM_ERR_INVALID_ARG", "dtype"),
+    (dict(Hq=6, Hkv=2), "LSRM_ERR_INVALID_ARG", "power of two"),
+    (dict(Hq=5, Hkv=2), "LSRM_ERR_INVALID_ARG", "multiple"),
+])
+def test_select_fwd_rejects_bad_shapes_on_host(lib, bad, code, msg):
+    rc = _fwd(lib, _meta(), _shape(**bad))
+    assert rc == _header_define(code)
+    assert msg in lib.lib().lsrm_last_error().decode()
+
+
+def test_select_fwd_rejects_topk_and_small_workspace(lib):
+    rc = _fwd(lib, _meta(), _shape(), topk=0)
+    assert rc == _header_define("LSRM_ERR_INVALID_ARG")
+    assert "topk" in lib.lib().lsrm_last_error().decode()
+    rc = _fwd(lib, _meta(), _shape(), topk=4, ws=ctypes.c_void_p(256), ws_bytes=8)
+    assert rc == _header_define("LSRM_ERR_WORKSPACE")
+    assert "workspace" in lib.lib().lsrm_last_error().decode()
+
+
+def test_workspace_queries_are_host_only_and_grow_with_the_problem(lib):
+    h = lib.lib()
+    small = h.lsrm_select_workspace_bytes(ctypes.byref(_meta(1024, 8)), ctypes.byref(_shape()), 8, 0)
+    big = h.lsrm_select_workspace_bytes(ctypes.byref(_meta(65536, 400)), ctypes.byref(_shape()), 16, 0)
+    assert 0 < small < big
+    assert h.lsrm_select_workspace_bytes(ctypes.byref(_meta()), ctypes.byref(_shape(D=48)), 8, 0) == 0
+    for mode in (0, 1, 2):
+        assert h.lsrm_dense_workspace_bytes(ctypes.byref(_meta(4096, 32)), ctypes.byref(_shape()), mode) > 0
+
+
+def test_noalloc_scratch_bound_is_the_header_constant(lib):
+    m = re.search(r"#define\s+LSRM_NOALLOC_SCRATCH_BYTES\s+\((\d+)u\s*<<\s*(\d+)\)", open(HEADER).read())
+    assert m and int(m.group(1)) << int(m.group(2)) == 16 << 20
+
+
+def test_ops_fail_loudly_without_a_device():
+    import torch
+
+    from lsrm_sparse import ops
+
+    if torch.cuda.is_available():
+        pytest.skip("host-only check")
+    q = torch.zeros(8, 2, 64, dtype=torch.bfloat16)
+    cu = torch.tensor([0, 8], dtype=torch.int32)
+    meta = ops.Meta(cu, cu, torch.tensor([0, 1], dtype=torch.int32), cu)
+    with pytest.raises(Exception):
+        ops.select_attn_fwd(q, q, q, torch.zeros(2, 8, 1, dtype=torch.int32), meta)
