@@ -149,7 +149,7 @@ class ShardedProblem:
 
     def __init__(self, full: Problem, plan, device):
         self.full, self.plan, self.device = full, plan, device
-        self.cfg, self.lens = full.cfg, full.lens
+        self.cfg, self.lens, self.shell = full.cfg, full.lens, full.shell
         self.N, self.H, self.D, self.nb = full.N, full.H, full.D, full.nb
         s, e = plan.local
         self.h_local = [t[s:e] for t in (full.h_q, full.h_k, full.h_v, full.h_x, full.h_g)]

@@ -244,6 +244,32 @@ int lsrm_gate_merge_bwd(int32_t total_tokens, int32_t channels, int32_t n_branch
                         const void* dout, void* dz, void* const* dbranches, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Block metadata of sparse voxel sequences                                 */
+/* ---------------------------------------------------------------------- */
+/* Sort key of sort_volume_blocks (misc/sparse_utils.py:126-152): coords
+ * [n, 4] int32 (batch, z, y, x), 16-byte aligned; keys[i] int64 orders the
+ * voxels by batch, block cell (z, y, x) and position inside the cell.  The
+ * caller sorts by the key (a library sort) and permutes its tensors. */
+int lsrm_volume_sort_keys(int64_t n_tokens, const int32_t* coords, int32_t volume_res, int32_t block_size,
+                          int64_t* keys, void* stream);
+
+/* compute_block_separation (misc/sparse_utils.py:592-641): coords
+ * [n, dim+1] int32 (batch, then dim coordinates), grouped by batch; host
+ * arrays block_size[dim], resolution[dim] (cells per dimension =
+ * resolution / block_size).  Writes cu_seqlens [batch+1], cu_seqblocks
+ * [batch+1], cu_block_include_tokens [num_blocks+1] (capacity n+1) and the
+ * device scalar num_blocks: per batch element, the token count of every
+ * non-empty cell in cell order (first coordinate most significant); cells
+ * outside the grid are not counted.  Batch ids out of range set
+ * LSRM_ERR_BAD_INDEX in err_flags (required). */
+size_t lsrm_block_separation_workspace_bytes(int32_t dim, const int32_t* block_size, const int32_t* resolution,
+                                             int32_t batch);
+int lsrm_block_separation(int64_t n_tokens, const int32_t* coords, int32_t dim, const int32_t* block_size,
+                          const int32_t* resolution, int32_t batch, int32_t* cu_seqlens, int32_t* cu_seqblocks,
+                          int32_t* cu_block_include_tokens, int32_t* num_blocks, void* workspace,
+                          size_t workspace_bytes, int* err_flags, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Ulysses sequence <-> head exchange (sequence parallelism over W ranks)   */
 /* ---------------------------------------------------------------------- */
 /* Replaces the layout side of the reference's sequence-parallel exchange

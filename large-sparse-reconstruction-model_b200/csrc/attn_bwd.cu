@@ -73,7 +73,8 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   {
     ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
-    kern<<<dim3(grid_x * p.n_split, hkv), kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, p);
+    const dim3 grid = p.kv_sched ? dim3(grid_x * hkv, 1) : dim3(grid_x * p.n_split, hkv);
+    kern<<<grid, kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, p);
     LSRM_LAUNCH_CHECK();
   }
   if (p.n_split > 1) {
@@ -173,6 +174,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
   if ((rc = launch_build_tiles(plan.kvtiles, plan.n_kvtiles, plan.kvtiles_ub, kTilesKVBlock, kRows, meta, nullptr,
                                meta->num_blocks, 0, err, s)))
     return rc;
+  if ((rc = launch_build_kv_schedule(plan, kKvQRows / G, s))) return rc;
   const float scale = softmax_scale_of(shape);
   // dQ (+ delta)
   {
@@ -231,6 +233,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.dv = dv;
     p.partial = nullptr;
     p.n_split = 1;
+    p.kv_sched = plan.kv_sched;
     p.kv_tok_stride = shape->kv_token_stride;
     p.total_q = meta->total_q;
     p.G = G;

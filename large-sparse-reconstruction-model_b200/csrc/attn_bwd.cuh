@@ -75,8 +75,10 @@ struct DqSmem {
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(DqMeta);
   static constexpr int NBAR = 2 * STAGES + 1 + 8 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
+  static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
+  static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
 // Fills the groups of one select-mode chunk by walking the union.
@@ -196,11 +198,42 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 
   if (warp == 8) {
     if (lane == 0) {
-      const int qpt = 128 / G;
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_do);
+    }
+    if (lane < kNumBoxes) {
+      tma_prefetch_desc(&kv.k[lane]);
+      tma_prefetch_desc(&kv.v[lane]);
+    }
+    if (lane == 0) {
       mbar_arrive_expect_tx(qdo_full, 2 * L::QTILE);
       tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, qdo_full);
       tma_load_3d(sDO, &tm_do, 0, h * G, tile.q_start, qdo_full);
-      (void)qpt;
+    }
+    UnionCache& uc = *reinterpret_cast<UnionCache*>(smem + L::OFF_UC);
+    bool cached = false;
+    if constexpr (MODE == kSelect)
+      cached = union_cache_fill(uc, U, prm.union_blk, prm.union_mask, ubase, prm.cu_block_include_tokens, tile.kv_lo,
+                                tile.kv_hi);
+    if (cached) {
+      int issued = 0;
+      for (int j = 0; j < n_chunks; ++j) {
+        const int s = j % STAGES;
+        if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+        DqMeta& mt = meta[s];
+        const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+        __syncwarp();
+        issue_group_runs<kDqGroups, RB>(r, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
+                                        &kv_full[s]);
+        issued = j + 1;
+      }
+      if (lane == 0 && *abort_flag) {
+        mbar_wait_drain(qdo_full, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
+      }
+    } else if (lane == 0) {
       int u = -1, tcur = 0, tend = 0, issued = 0;
       for (int j = 0; j < n_chunks; ++j) {
         const int s = j % STAGES;
@@ -422,6 +455,7 @@ struct DkvParams {
   void* dv;
   float* partial;  // [split][hkv][kvtiles_ub][128][D] x 2 when n_split > 1
   int n_split;
+  const int* kv_sched;  // select mode: work items (h * kvtiles_ub + tile) in launch order; grid is 1-D
   long long kv_tok_stride;
   int total_q;
   int G;
@@ -442,6 +476,39 @@ struct KvMeta {
   int pad[3];
 };
 
+// The reverse map of one KV block in shared memory: the (query tile, union
+// slot) entries that selected it, as the tile's first query token, the
+// 128-bit mask of its queries and the exclusive prefix of the masks' bit
+// counts, so the queries of any chunk are found without a sequential walk.
+constexpr int kRevCacheCap = 1024;
+
+struct RevCache {
+  int tq0[kRevCacheCap];
+  int prefix[kRevCacheCap];
+  uint4 mask[kRevCacheCap];
+  int n;      // entries (-1: the block's list did not fit)
+  int total;  // queries
+  int pad[2];
+};
+
+// Position of the n-th (0-based) set bit of `word` (n < popc(word)).
+__device__ __forceinline__ int nth_set_bit(uint32_t word, int n) {
+  int pos = 0;
+#pragma unroll
+  for (int width = 16; width >= 1; width >>= 1) {
+    const uint32_t low = word & ((1u << width) - 1u);
+    const int c = __popc(low);
+    if (n >= c) {
+      n -= c;
+      word >>= width;
+      pos += width;
+    } else {
+      word = low;
+    }
+  }
+  return pos;
+}
+
 template <int D, int STAGES>
 struct DkvSmem {
   static constexpr int RB = 2 * D;
@@ -459,8 +526,10 @@ struct DkvSmem {
   // kv_full, q_full[S], q_empty[S], st_full[2], st_free[2], pds_full[2], pds_free[2], acc_done, mma_done
   static constexpr int NBAR = 1 + 2 * STAGES + 8 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 32;
+  static constexpr int OFF_RC = (OFF_MISC + 32 + 15) / 16 * 16;  // select mode: the block's reverse map
+  static constexpr int BYTES = OFF_RC + (int)sizeof(RevCache);
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
+  static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
 // Number of query rows (queries x G) gathered for one KV tile (select mode).
@@ -481,9 +550,93 @@ __device__ __forceinline__ int count_select_queries(const DkvParams& prm, int h,
 
 // Threads of the dK/dV kernel: 8 compute warps (two per TMEM lane quarter,
 // splitting the 64 query columns of a chunk), a producer warp, an MMA warp.
-constexpr int kDkvThreads = 320;
+constexpr int kDkvThreads = 352;
 constexpr int kDkvProducerWarp = 8;
 constexpr int kDkvMmaWarp = 9;
+constexpr int kDkvProducer2Warp = 10;  // select mode: gathers every other chunk
+
+// Warp-wide fill of the reverse cache for block `blk` of kv head `h`.
+__device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& prm, int h, int blk) {
+  const int lane = threadIdx.x & 31;
+  const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
+  const int e0 = off[blk], n = off[blk + 1] - e0;
+  if (n > kRevCacheCap) {
+    if (lane == 0) rc.n = -1;
+    __syncwarp();
+    return;
+  }
+  const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
+  int carry = 0;
+  for (int b0 = 0; b0 < n; b0 += 32) {
+    const int i = b0 + lane;
+    int cnt = 0;
+    if (i < n) {
+      const int2 x = ent[e0 + i];
+      const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+      rc.tq0[i] = prm.qtiles[x.x].q_start;
+      rc.mask[i] = m;
+      cnt = __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (i < n) rc.prefix[i] = carry + incl - cnt;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) {
+    rc.n = n;
+    rc.total = carry;
+  }
+  __syncwarp();
+}
+
+// Queries c*qpc .. c*qpc+qpc-1 of the cached list into qlist (-1 past the
+// end); returns how many are real.  Warp-wide.
+__device__ __forceinline__ int rev_cache_chunk(const RevCache& rc, int c, int qpc, int* qlist) {
+  const int lane = threadIdx.x & 31;
+  const int base = c * qpc;
+  const int n = max(0, min(qpc, rc.total - base));
+  for (int i = lane; i < qpc; i += 32) {
+    int q = -1;
+    if (i < n) {
+      const int t = base + i;
+      int lo = 0, hi = rc.n;  // last entry with prefix <= t (entries with no query never are)
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (rc.prefix[mid] <= t) lo = mid;
+        else hi = mid;
+      }
+      int rank = t - rc.prefix[lo];
+      const uint4 m = rc.mask[lo];
+      int w = 0;
+      uint32_t word = m.x;
+      int cw = __popc(m.x);
+      if (rank >= cw) {
+        rank -= cw;
+        w = 1;
+        word = m.y;
+        cw = __popc(m.y);
+        if (rank >= cw) {
+          rank -= cw;
+          w = 2;
+          word = m.z;
+          cw = __popc(m.z);
+          if (rank >= cw) {
+            rank -= cw;
+            w = 3;
+            word = m.w;
+          }
+        }
+      }
+      q = rc.tq0[lo] + 32 * w + nth_set_bit(word, rank);
+    }
+    qlist[i] = q;
+  }
+  return n;
+}
 
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kDkvThreads, 1)
@@ -495,9 +648,16 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
 
-  const int split = blockIdx.x % prm.n_split;
-  const int kt_idx = blockIdx.x / prm.n_split;
-  const int h = blockIdx.y;
+  int split = 0, kt_idx, h;
+  if (prm.kv_sched) {
+    const int item = prm.kv_sched[blockIdx.x];
+    h = item / prm.kvtiles_ub;
+    kt_idx = item - h * prm.kvtiles_ub;
+  } else {
+    split = blockIdx.x % prm.n_split;
+    kt_idx = blockIdx.x / prm.n_split;
+    h = blockIdx.y;
+  }
   if (kt_idx >= *prm.n_kvtiles) return;
   const QTile kt = prm.kvtiles[kt_idx];  // rows = keys [q_start, q_start + n_q)
   const int G = prm.G;
@@ -536,10 +696,16 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     q_lo = min(kt.kv_lo + split * per, kt.kv_hi);
     q_hi = min(q_lo + per, kt.kv_hi);
   }
+  RevCache& rc = *reinterpret_cast<RevCache*>(smem + L::OFF_RC);
   if (warp == kDkvProducerWarp) {
     int nqueries;
-    if constexpr (MODE == kSelect) nqueries = count_select_queries(prm, h, kt.seg);
-    else nqueries = max(q_hi - q_lo, 0);
+    if constexpr (MODE == kSelect) {
+      rev_cache_fill(rc, prm, h, kt.seg);
+      nqueries = rc.n >= 0 ? rc.total : count_select_queries(prm, h, kt.seg);
+    } else {
+      nqueries = max(q_hi - q_lo, 0);
+      if (lane == 0) rc.n = -1;
+    }
     if (lane == 0) *s_nchunks = (nqueries + qpc - 1) / qpc;
   }
   if (threadIdx.x == 0) {
@@ -572,124 +738,139 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   // TMEM: St0 [0,64) St1 [64,128) dPt0 [128,192) dPt1 [192,256) dK [256,256+D) dV [256+D, 256+2D)
   const uint32_t tm_st0 = tmem, tm_dpt0 = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 256 + D;
 
-  if (warp == kDkvProducerWarp) {
-    // ------------------------------ producer ------------------------------
+  if (warp == kDkvProducerWarp || warp == kDkvProducer2Warp) {
+    // ------------------------------ producers -----------------------------
     // K/V tile by TMA; query rows gathered with 16-byte cp.async by all 32
     // lanes (any row pattern at full LSU rate), lse/delta with 4-byte
-    // cp.async; chunk c is published LAG chunks later, after wait_group and a
-    // generic->async proxy fence.
-    if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
-      tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
-      tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
-    }
-    constexpr int CPR = RB / 16;  // 16-byte chunks per row
-    constexpr int LAG = STAGES - 2;
-    const uint8_t* qbase = static_cast<const uint8_t*>(prm.q);
-    const uint8_t* dobase = static_cast<const uint8_t*>(prm.dout);
-    const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
-    const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
-    int e = 0, e_end = 0, tq0 = 0;
-    uint32_t w0 = 0u, w1 = 0u, w2 = 0u, w3 = 0u;  // uniform across the warp
-    if constexpr (MODE == kSelect) {
-      e = off[kt.seg] - 1;
-      e_end = off[kt.seg + 1];
-    }
-    auto publish = [&](int cc) {
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&q_full[cc % STAGES]);
-    };
-    int issued = 0, published = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int s = c % STAGES;
-      if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-      KvMeta& mt = meta[s];
-      int n = 0;
+    // cp.async.  Two warps take alternate chunks (in select mode each
+    // chunk's queries come straight from the cached reverse map) and publish
+    // a chunk as soon as its copies have landed (wait_group, generic->async
+    // proxy fence, arrive).  When the map did not fit in shared memory,
+    // warp 8 alone walks it and publishes two chunks behind.
+    const bool cached = MODE == kSelect && rc.n >= 0;
+    const int nprod = (MODE == kSelect && !cached) ? 1 : 2;  // the sequential walk needs one warp
+    const int pw = warp == kDkvProducerWarp ? 0 : 1;
+    if (pw < nprod) {
+      if (pw == 0 && lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+        tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
+        tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+      }
+      constexpr int CPR = RB / 16;  // 16-byte chunks per row
+      // two warps: publish each chunk as soon as its copies land (the other
+      // warp keeps the pipe busy meanwhile); one warp: publish LAG chunks later
+      const int LAG = nprod == 2 ? 0 : STAGES - 2;
+      const uint8_t* qbase = static_cast<const uint8_t*>(prm.q);
+      const uint8_t* dobase = static_cast<const uint8_t*>(prm.dout);
+      const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
+      const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
+      int e = 0, e_end = 0, tq0 = 0;
+      uint32_t w0 = 0u, w1 = 0u, w2 = 0u, w3 = 0u;  // uniform across the warp
       if constexpr (MODE == kSelect) {
-        while (n < qpc) {
-          if ((w0 | w1 | w2 | w3) == 0u) {
-            if (e + 1 >= e_end) break;
-            ++e;
-            const int2 x = ent[e];
-            const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-            w0 = m.x;
-            w1 = m.y;
-            w2 = m.z;
-            w3 = m.w;
-            tq0 = prm.qtiles[x.x].q_start;
-            continue;
+        e = off[kt.seg] - 1;
+        e_end = off[kt.seg + 1];
+      }
+      auto publish = [&](int cc) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[cc % STAGES]);
+      };
+      int issued = 0, published = 0;  // in this warp's own chunk sequence
+      for (int c = pw; c < n_chunks; c += nprod) {
+        const int s = c % STAGES;
+        if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+        KvMeta& mt = meta[s];
+        int n = 0;
+        if constexpr (MODE == kSelect) {
+          if (cached) {
+            n = rev_cache_chunk(rc, c, qpc, mt.qlist);
+          } else {
+            while (n < qpc) {
+              if ((w0 | w1 | w2 | w3) == 0u) {
+                if (e + 1 >= e_end) break;
+                ++e;
+                const int2 x = ent[e];
+                const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+                w0 = m.x;
+                w1 = m.y;
+                w2 = m.z;
+                w3 = m.w;
+                tq0 = prm.qtiles[x.x].q_start;
+                continue;
+              }
+              const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
+              const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
+              const bool bit = (word >> lane) & 1u;
+              const int rank = __popc(word & ((1u << lane) - 1u));
+              const bool take = bit && rank < qpc - n;
+              if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
+              const uint32_t taken = __ballot_sync(0xffffffffu, take);
+              n += __popc(taken);
+              if (wi == 0) w0 &= ~taken;
+              else if (wi == 1) w1 &= ~taken;
+              else if (wi == 2) w2 &= ~taken;
+              else w3 &= ~taken;
+            }
+            for (int i = n + lane; i < qpc; i += 32) mt.qlist[i] = -1;
           }
-          const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
-          const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
-          const bool bit = (word >> lane) & 1u;
-          const int rank = __popc(word & ((1u << lane) - 1u));
-          const bool take = bit && rank < qpc - n;
-          if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
-          const uint32_t taken = __ballot_sync(0xffffffffu, take);
-          n += __popc(taken);
-          if (wi == 0) w0 &= ~taken;
-          else if (wi == 1) w1 &= ~taken;
-          else if (wi == 2) w2 &= ~taken;
-          else w3 &= ~taken;
-        }
-        for (int i = n + lane; i < qpc; i += 32) mt.qlist[i] = -1;
-      } else {
-        const int q0 = q_lo + c * qpc;
-        n = max(0, min(qpc, q_hi - q0));
-        for (int i = lane; i < qpc; i += 32) mt.qlist[i] = i < n ? q0 + i : -1;
-      }
-      if (lane == 0) mt.n_rows = n * G;
-      __syncwarp();
-      for (int row = lane; row < kKvQRows; row += 32) {
-        const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
-        mt.qidx[row] = q;
-        if (q >= 0) {
-          const size_t si = (size_t)(h * G + g) * prm.total_q + q;
-          cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
-          cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
         } else {
-          mt.lse2[row] = 0.f;
-          mt.delta[row] = 0.f;
-        }
-      }
-      __syncwarp();
-      const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
-      if constexpr (MODE != kSelect) {
-        // contiguous queries: one TMA box per operand; rows past the range are
-        // other tokens' data (finite, masked) or zero fill past the tensor
-        if (lane == 0) {
           const int q0 = q_lo + c * qpc;
-          mbar_expect_tx(&q_full[s], 2 * L::QTILE);
-          tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
-          tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
+          n = max(0, min(qpc, q_hi - q0));
+          for (int i = lane; i < qpc; i += 32) mt.qlist[i] = i < n ? q0 + i : -1;
         }
-      } else
+        if (lane == 0) mt.n_rows = n * G;
+        __syncwarp();
+        for (int row = lane; row < kKvQRows; row += 32) {
+          const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
+          mt.qidx[row] = q;
+          if (q >= 0) {
+            const size_t si = (size_t)(h * G + g) * prm.total_q + q;
+            cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
+            cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+          } else {
+            mt.lse2[row] = 0.f;
+            mt.delta[row] = 0.f;
+          }
+        }
+        __syncwarp();
+        const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
+        if constexpr (MODE != kSelect) {
+          // contiguous queries: one TMA box per operand; rows past the range are
+          // other tokens' data (finite, masked) or zero fill past the tensor
+          if (lane == 0) {
+            const int q0 = q_lo + c * qpc;
+            mbar_expect_tx(&q_full[s], 2 * L::QTILE);
+            tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
+            tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
+          }
+        } else
 #pragma unroll 4
-      for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
-        const int row = idx / CPR, j = idx % CPR;  // CPR is a power of two
-        const int q = mt.qidx[row], g = row & (G - 1);
-        const uint32_t o = swz_offset<RB>(row, j);
-        if (q >= 0) {
-          const size_t src = ((size_t)q * prm.q_tok_stride + (size_t)(h * G + g) * D) * 2 + (size_t)j * 16;
-          cp_async_16(dq_s + o, qbase + src);
-          cp_async_16(ddo_s + o, dobase + src);
-        } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
-          st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
-          st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+        for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
+          const int row = idx / CPR, j = idx % CPR;  // CPR is a power of two
+          const int q = mt.qidx[row], g = row & (G - 1);
+          const uint32_t o = swz_offset<RB>(row, j);
+          if (q >= 0) {
+            const size_t src = ((size_t)q * prm.q_tok_stride + (size_t)(h * G + g) * D) * 2 + (size_t)j * 16;
+            cp_async_16(dq_s + o, qbase + src);
+            cp_async_16(ddo_s + o, dobase + src);
+          } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
+            st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
+            st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+          }
+        }
+        cp_async_commit();
+        ++issued;
+        if (issued > LAG) {
+          if (LAG == 0) cp_async_wait<0>();
+          else cp_async_wait<STAGES - 2>();
+          publish(pw + nprod * published);
+          ++published;
         }
       }
-      cp_async_commit();
-      issued = c + 1;
-      if (c >= LAG) {
-        cp_async_wait<LAG>();
-        publish(c - LAG);
-        published = c - LAG + 1;
-      }
+      cp_async_wait<0>();
+      for (; published < issued; ++published) publish(pw + nprod * published);
+      if (pw == 0 && lane == 0 && *abort_flag) mbar_wait_drain(kv_full, 0);
     }
-    cp_async_wait<0>();
-    for (int cc = published; cc < issued; ++cc) publish(cc);
-    if (lane == 0 && *abort_flag) mbar_wait_drain(kv_full, 0);
     __syncwarp();
   } else if (warp == kDkvMmaWarp) {
     // ------------------------------ MMA issuer -----------------------------
@@ -743,7 +924,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       mbar_wait_drain(mma_done, 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // ------------------------------ P^T / dS^T -----------------------------
     // warp w: key rows 32*(w%4).., query columns 32*(w/4).. of each chunk
     const int quarter = warp & 3, half = warp >> 2;

@@ -79,8 +79,11 @@ struct FwdSmem {
   // p_free[2], pv_full[2], pv_free[2], mma_done
   static constexpr int NBAR = 2 * STAGES + 1 + 12 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int OFF_UC = OFF_MISC + 16;  // select mode: the tile's union (16-byte aligned)
+  static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
+  static_assert(OFF_UC % 16 == 0, "union cache must be 16-byte aligned");
+  static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
 constexpr int kFwdThreads = 320;
@@ -125,7 +128,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = prm.G;
-  const int qpt = 128 / G;
 
   // number of KV chunks for this (tile, head)
   int n_chunks;
@@ -170,10 +172,41 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == 8) {
     // ------------------------------ producer ------------------------------
+    if (lane == 0) tma_prefetch_desc(&tm_q);
+    if (lane < kNumBoxes) {
+      tma_prefetch_desc(&kv.k[lane]);
+      tma_prefetch_desc(&kv.v[lane]);
+    }
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, L::TILE);
       tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, q_full);
-      int u = -1, tcur = 0, tend = 0;  // select-mode walk state
+    }
+    UnionCache& uc = *reinterpret_cast<UnionCache*>(smem + L::OFF_UC);
+    bool cached = false;
+    if constexpr (MODE == kSelect)
+      cached = union_cache_fill(uc, U, prm.union_blk, prm.union_mask, ubase, prm.cu_block_include_tokens, tile.kv_lo,
+                                tile.kv_hi);
+    if (cached) {
+      // the whole warp lays out each chunk (one lane per group) and issues its boxes
+      int issued = 0;
+      for (int j = 0; j < n_chunks; ++j) {
+        const int s = j % STAGES;
+        if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
+        ChunkMeta& mt = meta[s];
+        const int r = union_cache_chunk<kGroupsPerChunk>(uc, j, mt.row0, mt.qmask, mt.colmask);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+        __syncwarp();
+        issue_group_runs<kGroupsPerChunk, RB>(r, sK + s * L::TILE, sV + s * L::TILE, kv.k, kv.v, h, prm.total_k,
+                                              &kv_full[s]);
+        issued = j + 1;
+      }
+      if (lane == 0 && *abort_flag) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
+      }
+    } else if (lane == 0) {
+      int u = -1, tcur = 0, tend = 0;  // select-mode walk state (unions too large for the cache)
       int issued = 0;
       for (int j = 0; j < n_chunks; ++j) {
         const int s = j % STAGES;

@@ -410,25 +410,25 @@ __device__ __forceinline__ bool union_cache_fill(UnionCache& uc, int U, const in
 }
 
 // Lays out groups [NG*j, NG*j+NG) of the union into row0 / qmask / colmask
-// (one lane per group, lanes >= NG idle).  Warp-wide.
+// (one lane per group, lanes >= NG idle).  Warp-wide.  Returns the lane's
+// group's first token (-1: no group).
 template <int NG>
-__device__ __forceinline__ void union_cache_chunk(const UnionCache& uc, int j, int* row0, uint32_t (*qmask)[4],
-                                                  uint32_t* colmask) {
+__device__ __forceinline__ int union_cache_chunk(const UnionCache& uc, int j, int* row0, uint32_t (*qmask)[4],
+                                                 uint32_t* colmask) {
   const int lane = threadIdx.x & 31;
   uint32_t bits = 0u;
+  int r = -1;
   if (lane < NG) {
     const int g = NG * j + lane;
     if (g < uc.groups) {
-      int lo = 0, hi = uc.n;  // last entry with gstart <= g (entries with no group share a start)
+      int lo = 0, hi = uc.n;  // last entry with gstart <= g (empty entries never are)
       while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
         if (uc.gstart[mid] <= g) lo = mid;
         else hi = mid;
       }
-      while (lo + 1 < uc.n && uc.gstart[lo + 1] <= g) ++lo;
-      const int r = uc.t0[lo] + 8 * (g - uc.gstart[lo]);
+      r = uc.t0[lo] + 8 * (g - uc.gstart[lo]);
       const int cnt = min(8, uc.t1[lo] - r);
-      row0[lane] = r;
       const uint4 m = uc.mask[lo];
       qmask[lane][0] = m.x;
       qmask[lane][1] = m.y;
@@ -436,15 +436,41 @@ __device__ __forceinline__ void union_cache_chunk(const UnionCache& uc, int j, i
       qmask[lane][3] = m.w;
       bits = ((1u << cnt) - 1u) << ((lane & 3) * 8);
     } else {
-      row0[lane] = -1;
       qmask[lane][0] = qmask[lane][1] = qmask[lane][2] = qmask[lane][3] = 0u;
     }
+    row0[lane] = r;
   }
   // colmask word w collects the bytes of groups 4w..4w+3
-#pragma unroll
-  for (int o = 1; o < 4; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
   if (lane < NG && (lane & 3) == 0) colmask[lane >> 2] = bits;
-  __syncwarp();
+  return r;
+}
+
+// Issues the TMA loads of one chunk's groups, lanes in parallel.  Runs of
+// groups contiguous in memory (or runs of unused groups, read past the end of
+// the tensor: zero fill) are split greedily into power-of-two boxes
+// (8 << i rows, maps[i]); the lane of each box's first group issues it.
+// `r` is the lane's group's first token (-1 unused).  Warp-wide; the caller
+// has armed `bar` with the chunk's bytes.
+template <int NG, int RB>
+__device__ __forceinline__ void issue_group_runs(int r, uint8_t* dK, uint8_t* dV, const CUtensorMap* maps_k,
+                                                 const CUtensorMap* maps_v, int h, int oob_row, uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  const int prev = __shfl_up_sync(0xffffffffu, r, 1);
+  const bool cont = lane > 0 && lane < NG && ((r >= 0 && prev == r - 8) || (r < 0 && prev < 0));
+  const uint32_t starts = __ballot_sync(0xffffffffu, lane < NG && !cont) | (1u << NG);
+  if (lane < NG) {
+    const int s0 = 31 - __clz(starts & ((2u << lane) - 1u));        // this run's first group
+    const int s1 = __ffs(starts & ~((2u << lane) - 1u)) - 1;         // next run's first group
+    const int n = s1 - s0, d = lane - s0;
+    const int hb = 31 - __clz(n - d);                                // largest box that fits
+    if (d == ((n >> (hb + 1)) << (hb + 1))) {
+      const int row = r >= 0 ? r : oob_row;
+      tma_load_3d(dK + lane * 8 * RB, &maps_k[hb], 0, h, row, bar);
+      tma_load_3d(dV + lane * 8 * RB, &maps_v[hb], 0, h, row, bar);
+    }
+  }
 }
 
 }  // namespace lsrm

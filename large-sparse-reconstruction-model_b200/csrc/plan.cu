@@ -394,6 +394,9 @@ SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int 
   p.rev_off = reinterpret_cast<int*>(take(sizeof(int) * hkv * ((size_t)m->num_blocks + 1)));
   p.rev_cursor = reinterpret_cast<int*>(take(sizeof(int) * hkv * (size_t)std::max(m->num_blocks, 1)));
   p.rev_entries = reinterpret_cast<int2*>(take(sizeof(int2) * ent));
+  p.kv_sched = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
+  p.sched_key = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
+  p.sched_bins = reinterpret_cast<int*>(take(sizeof(int) * 2 * kSchedBins));
   p.bytes = (size_t)(cur - base);
   return p;
 }
@@ -450,6 +453,84 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
   dim3 grid(p.tiles_ub, p.hkv);
   ProfScope ps("plan_unions", s);
   build_unions_kernel<<<grid, kUnionThreads, smem, s>>>(p, *m, block_topk, topk, sel_rows, G, err);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+// dK/dV schedule: every (kv head, KV tile) item gets a bucket by its number
+// of 64-query chunks (the queries that selected the tile's block), and the
+// items are listed heaviest bucket first, so the longest CTAs start early
+// instead of trailing the launch.  Order inside a bucket is arbitrary; it
+// does not change any result.
+__global__ void sched_key_kernel(SelectPlan p, int qpc) {
+  const int items = p.hkv * p.kvtiles_ub;
+  const int n_kv = *p.n_kvtiles;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
+    const int h = i / p.kvtiles_ub, kt = i - h * p.kvtiles_ub;
+    int bin = kSchedBins - 1;  // empty / unused items last
+    if (kt < n_kv) {
+      const int blk = p.kvtiles[kt].seg;
+      const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
+      const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
+      int nq = 0;
+      for (int e = off[blk]; e < off[blk + 1]; ++e) {
+        const int2 x = ent[e];
+        const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
+        nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+      }
+      const int chunks = (nq + qpc - 1) / qpc;
+      bin = kSchedBins - 1 - min(chunks, kSchedBins - 1);
+    }
+    p.sched_key[i] = bin;
+    atomicAdd(&p.sched_bins[bin], 1);
+  }
+}
+
+__global__ void sched_scan_kernel(SelectPlan p) {
+  // one warp per 32 bins, serial over warps (1024 bins)
+  __shared__ int wsum[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int v = p.sched_bins[threadIdx.x];
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int x = wsum[lane];
+    int xi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += y;
+    }
+    wsum[lane] = xi - x;
+  }
+  __syncthreads();
+  p.sched_bins[kSchedBins + threadIdx.x] = wsum[w] + incl - v;
+}
+
+__global__ void sched_scatter_kernel(SelectPlan p) {
+  const int items = p.hkv * p.kvtiles_ub;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
+    const int pos = atomicAdd(&p.sched_bins[kSchedBins + p.sched_key[i]], 1);
+    p.kv_sched[pos] = i;
+  }
+}
+
+int launch_build_kv_schedule(const SelectPlan& p, int qpc, cudaStream_t s) {
+  ProfScope ps("plan_schedule", s);
+  LSRM_CUDA_TRY(cudaMemsetAsync(p.sched_bins, 0, sizeof(int) * kSchedBins, s));
+  const int items = p.hkv * p.kvtiles_ub;
+  const int grid = std::min((items + 255) / 256, 148 * 8);
+  sched_key_kernel<<<grid, 256, 0, s>>>(p, qpc);
+  LSRM_LAUNCH_CHECK();
+  sched_scan_kernel<<<1, kSchedBins, 0, s>>>(p);
+  LSRM_LAUNCH_CHECK();
+  sched_scatter_kernel<<<grid, 256, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }

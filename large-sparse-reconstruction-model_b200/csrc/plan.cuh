@@ -69,8 +69,13 @@ struct SelectPlan {
   int* rev_off;            // [hkv][num_blocks+1]
   int* rev_cursor;         // [hkv][num_blocks]
   int2* rev_entries;       // [hkv][tiles_ub*cap] (tile, union entry index)
+  int* kv_sched;           // [hkv*kvtiles_ub] dK/dV work items (h*kvtiles_ub + tile), heaviest first
+  int* sched_key;          // [hkv*kvtiles_ub] bucket of each item
+  int* sched_bins;         // [2*kSchedBins] bucket counts, then cursors
   size_t bytes;
 };
+
+constexpr int kSchedBins = 1024;  // dK/dV schedule buckets (query chunks, capped)
 
 struct DensePlan {
   int tiles_ub;
@@ -92,5 +97,6 @@ int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int r
 int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t* block_topk, int topk,
                         int sel_rows, int G, int* err, cudaStream_t s);
 int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s);
+int launch_build_kv_schedule(const SelectPlan& p, int qpc, cudaStream_t s);
 
 }  // namespace lsrm

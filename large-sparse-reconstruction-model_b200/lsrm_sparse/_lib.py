@@ -115,6 +115,13 @@ _SIGS = {
         [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p],
     ),
+    "lsrm_volume_sort_keys": (c_int, [c_int64, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "lsrm_block_separation_workspace_bytes": (c_size_t, [c_int32, c_void_p, c_void_p, c_int32]),
+    "lsrm_block_separation": (
+        c_int,
+        [c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_size_t, c_void_p, c_void_p],
+    ),
     "lsrm_ulysses_pack": (c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_void_p]),
     "lsrm_ulysses_unpack": (
         c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]

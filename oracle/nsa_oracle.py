@@ -53,6 +53,8 @@ __all__ = [
     "selection_flops",
     "dense_attention_flops",
     "three_branch_sample_step",
+    "volume_sort_keys",
+    "block_separation",
 ]
 
 
@@ -664,3 +666,46 @@ def three_branch_sample_step(q, k, v, x, gate_w, g, cu_blk, qblock_ids, topk, wi
         loss = loss + (out.reshape(L, -1) * g[r0:r1].float()).sum()
     loss.backward()
     return float(loss.detach()), 14.0 * D * H * pairs
+
+
+# ---------------------------------------------------------------------------
+# block metadata
+# ---------------------------------------------------------------------------
+
+
+def volume_sort_keys(coords, volume_res: int, block_size: int) -> np.ndarray:
+    """Key of ``sort_volume_blocks`` (misc/sparse_utils.py:126-152): batch,
+    block cell (z, y, x) and position inside the cell, most significant
+    first; int64."""
+    c = np.asarray(coords, dtype=np.int64)
+    r, b = int(volume_res), int(block_size)
+    blk, inb = c[:, 1:] // b, c[:, 1:] % b
+    return (r ** 3 * c[:, 0] + r * r * b * blk[:, 0] + r * b * b * blk[:, 1] + b ** 3 * blk[:, 2]
+            + b * b * inb[:, 0] + b * inb[:, 1] + inb[:, 2])
+
+
+def block_separation(coords, dim: int, block_size, batch: int, resolution):
+    """``compute_block_separation`` (misc/sparse_utils.py:592-641): per batch
+    element, the token count of every non-empty cell (histogram over
+    [0, cells), flattened with the first coordinate most significant; ids
+    outside the range are not counted, as torch.histc ignores them).
+    Returns ``(cu_seqblocks, cu_block_include_tokens)`` int32."""
+    c = np.asarray(coords, dtype=np.int64)
+    cells_per = [int(resolution[d]) // int(block_size[d]) for d in range(dim)]
+    cells = int(np.prod(cells_per))
+    mult = [int(np.prod(cells_per[d + 1:])) for d in range(dim)]
+    counts, seqblocks = [], []
+    for b in range(batch):
+        cb = c[c[:, 0] == b]
+        flat = np.zeros(cb.shape[0], dtype=np.int64)
+        for d in range(dim):
+            flat += (cb[:, 1 + d] // int(block_size[d])) * mult[d]
+        flat = flat[(flat >= 0) & (flat < cells)]
+        h = np.bincount(flat, minlength=cells)
+        nz = h[h > 0]
+        counts.append(nz)
+        seqblocks.append(len(nz))
+    cu_sb = np.concatenate([[0], np.cumsum(seqblocks)]).astype(np.int32)
+    allc = np.concatenate(counts) if counts else np.zeros(0, np.int64)
+    cu_blk = np.concatenate([[0], np.cumsum(allc)]).astype(np.int32)
+    return cu_sb, cu_blk

@@ -12,6 +12,9 @@ What runs, all unmodified reference code:
 * ``get_block_score`` (sparse/ops/block_score.py:16-98), fp32.
 * ``SpatialSparseAttentionIn`` (ResBlock compression + segment mean,
   sparse/module/spatial_sparse_attention.py:16-67) with its own random init.
+* ``sort_volume_blocks`` / ``compute_block_separation``
+  (misc/sparse_utils.py:126-152, 592-641): block metadata of voxel and
+  image-patch coordinates.
 * ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
   without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
   for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
@@ -173,13 +176,64 @@ def make_gate(SpatialSparseAttentionOut, ssa_module, seed, window):
                 gate_weight=mod.gate[0].weight.detach().numpy(), window=np.array(window))
 
 
+def _unique_coords(gen, n, batch, res):
+    """n distinct voxels per batch element of a res^3 grid, grouped by batch."""
+    out = []
+    for b in range(batch):
+        flat = torch.randperm(res ** 3, generator=gen)[:n]
+        z, y, x = flat // (res * res), (flat // res) % res, flat % res
+        out.append(torch.stack([torch.full_like(z, b), z, y, x], 1))
+    return torch.cat(out).to(torch.int32)
+
+
+def make_block_metadata(sparse_utils, seed):
+    """sort_volume_blocks (misc/sparse_utils.py:126-152) and
+    compute_block_separation (:592-641) on a volume case and an image-patch
+    case.  compute_block_separation runs on float coordinates (integral
+    values): its torch.histc has no CPU kernel for integer tensors; the
+    arithmetic is the same."""
+    import types
+
+    gen = torch.Generator().manual_seed(seed)
+    res, bs, batch = 32, 8, 3
+    coords = _unique_coords(gen, 700, batch, res)
+    coords = coords[torch.randperm(coords.shape[0], generator=gen)]
+    coords = coords[torch.argsort(coords[:, 0], stable=True)]  # grouped by batch, voxel order shuffled
+    feats = torch.arange(coords.shape[0], dtype=torch.float32)[:, None]
+    args = types.SimpleNamespace(block_size=bs, volume_res=res)
+    _, sorted_coords, idx = sparse_utils.sort_volume_blocks(feats, coords.clone(), args)
+    cu_sb, cu_blk = sparse_utils.compute_block_separation(sorted_coords.clone().float(), 3, [bs, bs, bs], batch,
+                                                          [res, res, res])
+    # image patches: [view, row, col], blocks of 1 x 4 x 4 over a (views, 8, 8) grid
+    img = []
+    for b in range(2):
+        v, r, c = torch.meshgrid(torch.arange(3), torch.arange(8), torch.arange(8), indexing="ij")
+        keep = torch.rand(v.numel(), generator=gen) < 0.7
+        img.append(torch.stack([torch.full((int(keep.sum()),), b), v.flatten()[keep], r.flatten()[keep],
+                                c.flatten()[keep]], 1))
+    img = torch.cat(img).to(torch.int32)
+    img_sb, img_blk = sparse_utils.compute_block_separation(img.clone().float(), 3, [1, 4, 4], 2, [3, 8, 8])
+    return dict(coords=coords.numpy(), volume_res=np.int32(res), block_size=np.int32(bs), batch=np.int32(batch),
+                sort_idx=idx.numpy().astype(np.int64), cu_seqblocks=cu_sb.numpy().astype(np.int32),
+                cu_block_include_tokens=cu_blk.numpy().astype(np.int32), img_coords=img.numpy(),
+                img_cu_seqblocks=img_sb.numpy().astype(np.int32),
+                img_cu_block_include_tokens=img_blk.numpy().astype(np.int32))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", choices=["blocks"], default=None, help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.ref)
+    from misc import sparse_utils
+
+    np.savez_compressed(os.path.join(HERE, "block_metadata.npz"), **make_block_metadata(sparse_utils, 41))
+    print("wrote block_metadata")
+    if args.only == "blocks":
+        return
     import flash_attn  # noqa: F401  (import check only; no CPU kernel)
 
     from sparse.ops import block_window_attention as bwa

@@ -148,3 +148,17 @@ def test_tiles_and_unions():
     bt = torch.tensor([[1, 3, -1], [3, 0, 9], [2, 2, 1]], dtype=torch.int32)
     un = oracle.build_tile_unions(bt, [oracle.nsa_oracle.QueryTile(0, 0, 3)], torch.tensor([0, 4]))
     assert un[0] == ([0, 1, 2, 3], [0b010, 0b101, 0b100, 0b011])
+
+
+def test_block_metadata_matches_reference(golden):
+    g = golden("block_metadata")
+    keys = oracle.volume_sort_keys(g["coords"], int(g["volume_res"]), int(g["block_size"]))
+    assert np.array_equal(np.argsort(keys, kind="stable"), g["sort_idx"])
+    sorted_coords = g["coords"][g["sort_idx"]]
+    bs = int(g["block_size"])
+    cu_sb, cu_blk = oracle.block_separation(sorted_coords, 3, [bs] * 3, int(g["batch"]), [int(g["volume_res"])] * 3)
+    assert np.array_equal(cu_sb, g["cu_seqblocks"])
+    assert np.array_equal(cu_blk, g["cu_block_include_tokens"])
+    cu_sb, cu_blk = oracle.block_separation(g["img_coords"], 3, [1, 4, 4], 2, [3, 8, 8])
+    assert np.array_equal(cu_sb, g["img_cu_seqblocks"])
+    assert np.array_equal(cu_blk, g["img_cu_block_include_tokens"])
