@@ -372,11 +372,19 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sd_free[sb]);
+      if (__all_sync(0xffffffffu, !row_valid || vm == 0xffffffffu)) {  // no masking needed
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const bool valid = (vm >> c) & 1u;
-        const float p = ex2(fmaf(sv[c], sl2, -lse2));
-        sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
+        for (int c = 0; c < 32; ++c) {
+          const float p = ex2(fmaf(sv[c], sl2, -lse2));
+          sv[c] = p * (dp[c] - delta) * scale;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const bool valid = (vm >> c) & 1u;
+          const float p = ex2(fmaf(sv[c], sl2, -lse2));
+          sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
+        }
       }
       if (!warp_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
@@ -964,16 +972,29 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         dl_c[v4 * 4 + 2] = b.z;
         dl_c[v4 * 4 + 3] = b.w;
       }
+      // Select mode needs no mask: padding columns hold zero Q / dO rows with
+      // zero LSE and delta, so P^T dO and dS^T Q get nothing from them, and
+      // key rows past the tile are never stored.  Range mode: full chunks
+      // need none either.
+      if (MODE == kSelect || (MODE == kRange && n_rows >= half * 32 + 32)) {
 #pragma unroll
-      for (int cc = 0; cc < 32; ++cc) {
-        const int col = half * 32 + cc;
-        bool valid = row_valid && col < n_rows;
-        if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
-        // unconditional ex2, then select: a conditional asm call becomes a branch per element
-        const float e = ex2(fmaf(st[cc], sl2, -lse_c[cc]));
-        const float p = valid ? e : 0.f;
-        st[cc] = p;
-        dpt[cc] = valid ? p * (dpt[cc] - dl_c[cc]) * scale : 0.f;
+        for (int cc = 0; cc < 32; ++cc) {
+          const float p = ex2(fmaf(st[cc], sl2, -lse_c[cc]));
+          st[cc] = p;
+          dpt[cc] = p * (dpt[cc] - dl_c[cc]) * scale;
+        }
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const int col = half * 32 + cc;
+          bool valid = row_valid && col < n_rows;
+          if constexpr (MODE == kBand) valid = valid && abs(mt.qidx[col] - kidx) <= prm.half_window;
+          // unconditional ex2, then select: a conditional asm call becomes a branch per element
+          const float e = ex2(fmaf(st[cc], sl2, -lse_c[cc]));
+          const float p = valid ? e : 0.f;
+          st[cc] = p;
+          dpt[cc] = valid ? p * (dpt[cc] - dl_c[cc]) * scale : 0.f;
+        }
       }
       if (!warp_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);

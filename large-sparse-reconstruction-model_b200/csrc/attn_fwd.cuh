@@ -384,12 +384,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
+      // every row of the warp attends all 64 columns (rows past the tile do
+      // not matter): no per-element masking
+      const bool full = __all_sync(0xffffffffu, !row_valid || (vm[0] & vm[1]) == 0xffffffffu);
       // row max over this half, then over the pair
       float mx = -INFINITY;
+      if (full) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int xx = 0; xx < 2; ++xx)
+        for (int xx = 0; xx < 2; ++xx)
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[xx] >> c) & 1u) ? sv[xx][c] : -INFINITY);
+          for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[xx][c]);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      } else {
+#pragma unroll
+        for (int xx = 0; xx < 2; ++xx)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[xx] >> c) & 1u) ? sv[xx][c] : -INFINITY);
+      }
       xch[half * 128 + r] = mx;
       pair_bar(quarter);
       mx = fmaxf(xch[r], xch[128 + r]);
@@ -398,16 +410,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float alpha = ex2(m - m_use);
       // probabilities -> P (shared, K-major 128B swizzle; this half = region `half`)
       if (!warp_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES) + half * 16384;
 #pragma unroll
       for (int xx = 0; xx < 2; ++xx) {
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e = ex2(fmaf(sv[xx][c], sl2, -m_use));  // unconditional: no branch per element
-          const float pv = ((vm[xx] >> c) & 1u) ? e : 0.f;
-          sv[xx][c] = pv;
-          rs += pv;
+          for (int c = 0; c < 32; ++c) {
+            const float e = ex2(fmaf(sv[xx][c], sl2, -m_use));
+            sv[xx][c] = e;
+            rs4[c & 3] += e;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float e = ex2(fmaf(sv[xx][c], sl2, -m_use));  // unconditional: no branch per element
+            const float pv = ((vm[xx] >> c) & 1u) ? e : 0.f;
+            sv[xx][c] = pv;
+            rs4[c & 3] += pv;
+          }
         }
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
@@ -421,6 +442,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       xch[256 + half * 128 + r] = rs;
       pair_bar(quarter);
       const float rowsum = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps

@@ -3,8 +3,10 @@
 // warps, a TMA producer warp, an MMA warp.
 //
 // 1. Fast scores.  For each chunk of 128 compressed blocks of the sequence,
-//    S^T = CK_chunk . Q^T (M = 128 blocks, N <= 256 query rows of the query
-//    block, tcgen05, fp32 accumulators in TMEM, double-buffered).  Reduce warp
+//    S^T = CK_chunk . Q^T (M = 128 blocks, N <= 128 query rows of the query
+//    block per pass, tcgen05, fp32 accumulators in TMEM, double-buffered in
+//    256 columns so that two CTAs share an SM and one's selection phase
+//    overlaps the other's tensor-core phase).  Reduce warp
 //    w owns block row 32*(w%4)+lane and half of the columns; each element
 //    adds e = exp2(s*qk_scale - lse2) to the block's fast score, plus the
 //    terms of a rigorous error bound (below).
@@ -13,7 +15,7 @@
 //    U < T are certainly outside the top-k; the rest (the candidates) get
 //    their score recomputed with the exact fixed-order arithmetic of
 //    score_exact.cuh, and the top k' of the candidates by (exact score desc,
-//    block id asc) are the answer.  This is the same set the exact scorer
+//    block id asc) are the answer.  T comes from an exact radix select.  This is the same set the exact scorer
 //    selects, so the indices stay bit-exact.
 //
 // Error bound per block (generous by construction):
@@ -38,9 +40,10 @@ namespace lsrm {
 
 constexpr int kSfThreads = 320;
 constexpr int kSfReduceThreads = 256;
-constexpr int kSfCols = 256;
+constexpr int kSfCols = 128;  // query rows per pass: 2 x 128 TMEM columns, so two CTAs share an SM
 constexpr int kSfStages = 3;
 constexpr int kSfCandCap = 1024;
+constexpr int kSfMinScratch = 1024;  // exact-stage terms: >= 2048 floats, more than one token's G <= 256 heads
 
 struct FastScoreParams {
   const void* q;
@@ -75,9 +78,14 @@ struct SfLayout {
   static constexpr int NBAR = 2 * kSfStages + 2 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_CAND = OFF_MISC + 64;  // cand ids [cap], exact [cap], chosen[64]
-  static constexpr int OFF_ARR = OFF_CAND + kSfCandCap * 8 + 64 * 4;
-  // per-block arrays (nb_cap each): fast score, weighted sum, t-term sum
-  static size_t bytes(int nb_cap) { return (size_t)OFF_ARR + 3ull * 4 * nb_cap + 1024; }
+  static constexpr int OFF_HIST = OFF_CAND + kSfCandCap * 8 + 64 * 4;  // radix-select histogram [256]
+  static constexpr int OFF_ARR = OFF_HIST + 256 * 4;
+  // per-block arrays: fast score SF [nb_cap], then weighted sum WS and t-term
+  // sum TS [nb_cap each] inside a scratch of 2 * max(nb_cap, kSfMinScratch)
+  // floats that the exact stage reuses for its terms
+  static size_t bytes(int nb_cap) {
+    return (size_t)OFF_ARR + 4ull * nb_cap + 8ull * (size_t)(nb_cap > kSfMinScratch ? nb_cap : kSfMinScratch) + 1024;
+  }
 };
 
 // Row of D 16-bit values -> fp32 (exact conversion), 16-byte loads.
@@ -95,8 +103,76 @@ __device__ __forceinline__ void load_row_f32(const T* __restrict__ row, float* o
 
 __device__ __forceinline__ void reduce_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kSfReduceThreads) : "memory"); }
 
+// Order-preserving map of a float to uint32, descending: larger floats give
+// smaller keys (-inf and +inf included; no NaN reaches it).
+__device__ __forceinline__ uint32_t desc_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t asc = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ~asc;
+}
+
+// The k-th largest of vals[0..n) (1 <= k <= n), exactly, by an MSB-first
+// 8-bit radix select.  Block-wide: every thread of the CTA calls it.
+__device__ float kth_largest(const float* vals, int n, int k, uint32_t* hist, int* misc) {
+  uint32_t prefix = 0u, mask = 0u;
+  int kk = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+    __syncthreads();
+    // warp-aggregated counts: the keys crowd into few bins (similar magnitudes)
+    const int lane = threadIdx.x & 31;
+    for (int b0 = threadIdx.x - lane; b0 < n; b0 += blockDim.x) {
+      const int b = b0 + lane;
+      const uint32_t key = b < n ? desc_key(vals[b]) : 0u;
+      const bool m = b < n && (key & mask) == prefix;
+      const uint32_t bin = m ? ((key >> shift) & 255u) : 256u + lane;
+      const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+      if (m && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      uint32_t c[8], tot = 0u;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        c[i] = hist[lane * 8 + i];
+        tot += c[i];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - tot;
+      // the lane whose range of 8 bins holds the kk-th key
+      if (excl < (uint32_t)kk && (uint32_t)kk <= incl) {
+        uint32_t run = excl;
+        int d = lane * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (run + c[i] >= (uint32_t)kk) {
+            d = lane * 8 + i;
+            break;
+          }
+          run += c[i];
+        }
+        misc[0] = d;
+        misc[1] = kk - (int)run;
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)misc[0] << shift;
+    mask |= 255u << shift;
+    kk = misc[1];
+    __syncthreads();
+  }
+  const uint32_t asc = ~prefix;
+  return __uint_as_float((asc & 0x80000000u) ? (asc & 0x7fffffffu) : ~asc);
+}
+
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kSfThreads, 1)
+__global__ void __launch_bounds__(kSfThreads, 2)
     qblock_topk_fast_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck,
                             const FastScoreParams p) {
   using L = SfLayout<D>;
@@ -173,7 +249,7 @@ __global__ void __launch_bounds__(kSfThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 2 * kSfCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -249,8 +325,10 @@ __global__ void __launch_bounds__(kSfThreads, 1)
           for (int j = 0; j < D; ++j) qn = fmaf(qv[j], qv[j], qn);
           qn = sqrtf(qn);
         }
-        col_lse2[t] = l2;
-        col_qn[t] = qn;
+        if (t < kSfCols) {
+          col_lse2[t] = l2;
+          col_qn[t] = qn;
+        }
       }
       reduce_bar();
       for (int c = 0; c < n_ck; ++c) {
@@ -300,7 +378,7 @@ __global__ void __launch_bounds__(kSfThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 2 * kSfCols);
   }
   if (*abort_flag) return;
 
@@ -334,51 +412,9 @@ __global__ void __launch_bounds__(kSfThreads, 1)
     TS[b] = (b == self) ? -INFINITY : sf + e;
   }
   __syncthreads();
-  // threshold: the kp-th largest lower bound (ties counted), by kp arg-max rounds
+  // threshold: the kp-th largest lower bound (ties counted), radix select
   float thr = -INFINITY;
-  {
-    __shared__ float red_v[kSfThreads / 32];
-    __shared__ int red_i[kSfThreads / 32];
-    // copy of the lower bounds lives in SF (fast scores are no longer needed)
-    for (int b = threadIdx.x; b < nb; b += kSfThreads) SF[b] = WS[b];
-    __syncthreads();
-    for (int round = 0; round < kp; ++round) {
-      float best = -INFINITY;
-      int bid = INT_MAX;
-      for (int b = threadIdx.x; b < nb; b += kSfThreads) {
-        const float v = SF[b];
-        if (v > best || (v == best && b < bid)) {
-          best = v;
-          bid = b;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
-        if (ov > best || (ov == best && oi < bid)) {
-          best = ov;
-          bid = oi;
-        }
-      }
-      if (lane == 0) {
-        red_v[warp] = best;
-        red_i[warp] = bid;
-      }
-      __syncthreads();
-      float bv = red_v[0];
-      int bi = red_i[0];
-      for (int i = 1; i < kSfThreads / 32; ++i)
-        if (red_v[i] > bv || (red_v[i] == bv && red_i[i] < bi)) {
-          bv = red_v[i];
-          bi = red_i[i];
-        }
-      thr = bv;
-      __syncthreads();
-      if (threadIdx.x == 0 && bi != INT_MAX) SF[bi] = -INFINITY;
-      __syncthreads();
-    }
-  }
+  if (kp > 0) thr = kth_largest(WS, nb, kp, reinterpret_cast<uint32_t*>(smem + L::OFF_HIST), s_misc + 4);
   // candidates: upper bound reaches the threshold
   if (threadIdx.x == 0) {
     s_misc[0] = 0;
@@ -403,49 +439,104 @@ __global__ void __launch_bounds__(kSfThreads, 1)
   // Scratch for stage A: the per-block arrays (3 * nb_cap floats).
   const int n_exact = fallback ? nb : (n_cand_raw > kp ? n_cand_raw : 0);
   if (n_exact > 0) {
+    // Stage A, all threads: per (candidate, column) the fixed-order score
+    // term, from the candidates' key rows staged in shared memory (the CK
+    // ring is free now) and the query rows of the tile (still in sQ when the
+    // query block took one pass; else read from global memory).
+    // Stage B, one thread per candidate: ordered sums (heads, then tokens).
+    // Scratch for stage A: the per-block arrays WS and TS (2 * nb_cap floats).
     float* escore = cand_exact;  // [kSfCandCap] (fallback: SF, sized nb)
-    float* eterm = WS;           // [batch][ncols_total], spans WS and TS
-    const int cap_terms = 2 * p.nb_cap;
-    const int batch = max(1, min(n_exact, cap_terms / max(ncols_total, 1)));
+    float* eterm = WS;           // scratch of cap_terms floats (spans WS and TS)
+    const int cap_terms = 2 * max(p.nb_cap, kSfMinScratch);
+    constexpr int kRowsStaged = kSfStages * 128;
     const float l2e = __uint_as_float(0x3FB8AA3Bu);
-    for (int c0 = 0; c0 < n_exact; c0 += batch) {
-      const int nbat = min(batch, n_exact - c0);
+    const bool q_in_smem = n_pass == 1;
+    const T* ckrows = reinterpret_cast<const T*>(sCK);
+    // candidates per batch: staged key rows fit the CK ring, and one token's
+    // G terms per candidate fit the scratch (cap_terms >= 2048 >= G * 16)
+    const int nbat_max = min(kRowsStaged, cap_terms / G);
+    for (int c0 = 0; c0 < n_exact; c0 += nbat_max) {
+      const int nbat = min(nbat_max, n_exact - c0);
+      // token-aligned column chunks whose terms fit the scratch: nbat * cchunk <= cap_terms
+      const int cchunk = min(ncols_total, cap_terms / nbat / G * G);
       __syncthreads();
-      for (int idx = threadIdx.x; idx < nbat * ncols_total; idx += kSfThreads) {
-        const int ci = idx / ncols_total, col = idx % ncols_total;
+      for (int idx = threadIdx.x; idx < nbat * (D / 8); idx += kSfThreads) {
+        const int ci = idx / (D / 8), v = idx % (D / 8);
         const int b = fallback ? (c0 + ci) : cand[c0 + ci];
-        const int tok = r0 + col / G, g = col % G;
-        float kv[D], qv[D];
-        load_row_f32<T, D>(static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D, kv);
-        load_row_f32<T, D>(static_cast<const T*>(p.q) + (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D, qv);
-        float dot = 0.f;
-#pragma unroll
-        for (int j = 0; j < D; ++j) dot = __fadd_rn(dot, __fmul_rn(qv[j], kv[j]));
-        const float lse2 = __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
-        eterm[idx] = exp2_fixed(__fsub_rn(__fmul_rn(dot, p.qk_scale), lse2));
+        reinterpret_cast<uint4*>(sCK)[ci * (D / 8) + v] = reinterpret_cast<const uint4*>(
+            static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D)[v];
       }
-      __syncthreads();
-      for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) {
-        const float* e = eterm + (size_t)ci * ncols_total;
-        float agg = 0.f;
-        for (int t = 0; t < ncols_total / G; ++t) {
-          float st = 0.f;
-          for (int g = 0; g < G; ++g) st = __fadd_rn(st, e[t * G + g]);
-          agg = __fadd_rn(agg, st);
+      for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) (fallback ? SF[c0 + ci] : escore[c0 + ci]) = 0.f;
+      for (int cc0 = 0; cc0 < ncols_total; cc0 += cchunk) {
+        const int nc = min(cchunk, ncols_total - cc0);
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < nbat * nc; idx += kSfThreads) {
+          const int ci = idx / nc, col = cc0 + idx % nc;
+          const int tok = r0 + col / G, g = col % G;
+          const T* kr = ckrows + (size_t)ci * D;
+          float dot = 0.f;
+          if (q_in_smem) {
+#pragma unroll
+            for (int c8 = 0; c8 < D / 8; ++c8) {
+              const uint4 qu = *reinterpret_cast<const uint4*>(sQ + swz_offset<RB>(col, c8));
+              const uint4 ku = *reinterpret_cast<const uint4*>(kr + c8 * 8);
+              const T* qe = reinterpret_cast<const T*>(&qu);
+              const T* ke = reinterpret_cast<const T*>(&ku);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dot = __fadd_rn(dot, __fmul_rn((float)qe[i], (float)ke[i]));
+            }
+          } else {
+            const uint4* qr = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
+                                                             (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D);
+#pragma unroll
+            for (int c8 = 0; c8 < D / 8; ++c8) {
+              const uint4 qu = qr[c8];
+              const uint4 ku = *reinterpret_cast<const uint4*>(kr + c8 * 8);
+              const T* qe = reinterpret_cast<const T*>(&qu);
+              const T* ke = reinterpret_cast<const T*>(&ku);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dot = __fadd_rn(dot, __fmul_rn((float)qe[i], (float)ke[i]));
+            }
+          }
+          const float lse2 =
+              q_in_smem ? col_lse2[col] : __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
+          eterm[idx] = exp2_fixed(__fsub_rn(__fmul_rn(dot, p.qk_scale), lse2));
         }
-        const int b = fallback ? (c0 + ci) : cand[c0 + ci];
-        if (fallback) SF[b] = (b == self) ? -INFINITY : agg;
-        else escore[c0 + ci] = agg;
+        __syncthreads();
+        // ordered sums continue across chunks: heads of a token, then tokens
+        for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) {
+          const float* e = eterm + (size_t)ci * nc;
+          float& run = fallback ? SF[c0 + ci] : escore[c0 + ci];
+          float agg = run;
+          if (G == 1) {
+#pragma unroll 8
+            for (int t = 0; t < nc; ++t) agg = __fadd_rn(agg, __fadd_rn(0.f, e[t]));
+          } else {
+            for (int t = 0; t < nc / G; ++t) {
+              float st = 0.f;
+              for (int g = 0; g < G; ++g) st = __fadd_rn(st, e[t * G + g]);
+              agg = __fadd_rn(agg, st);
+            }
+          }
+          run = agg;
+        }
+      }
+      if (fallback) {
+        __syncthreads();
+        for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads)
+          if (c0 + ci == self) SF[c0 + ci] = -INFINITY;
       }
     }
     __syncthreads();
   }
   const int n_cand = n_cand_raw;
   // choose kp blocks: (exact desc, id asc) among candidates (or all blocks)
-  if (threadIdx.x == 0) {
-    int n_ch = 0;
-    if (self >= 0) chosen[n_ch++] = self;
-    if (fallback) {
+  if (threadIdx.x == 0) s_misc[2] = 0;
+  __syncthreads();
+  if (fallback) {
+    if (threadIdx.x == 0) {
+      int n_ch = 0;
+      if (self >= 0) chosen[n_ch++] = self;
       for (int r = 0; r < kp; ++r) {
         float bv = -INFINITY;
         int bi = -1;
@@ -458,27 +549,34 @@ __global__ void __launch_bounds__(kSfThreads, 1)
         chosen[n_ch++] = bi;
         SF[bi] = -INFINITY;
       }
-    } else if (n_cand <= kp) {
-      for (int i = 0; i < n_cand; ++i) chosen[n_ch++] = cand[i];
-    } else {
-      for (int r = 0; r < kp; ++r) {
-        float bv = -INFINITY;
-        int bi = -1, bslot = -1;
-        for (int i = 0; i < n_cand; ++i) {
-          if (cand[i] < 0) continue;
-          const float v = cand_exact[i];
-          if (bi < 0 || v > bv || (v == bv && cand[i] < bi)) {
-            bv = v;
-            bi = cand[i];
-            bslot = i;
-          }
+      s_misc[2] = n_ch;
+    }
+  } else {
+    // a candidate is chosen when fewer than kp candidates beat it; the
+    // order of `chosen` does not matter (the output is sorted by id)
+    if (threadIdx.x == 0 && self >= 0) chosen[atomicAdd(&s_misc[2], 1)] = self;
+    for (int i = threadIdx.x; i < n_cand; i += kSfThreads) {
+      bool take = n_cand <= kp;
+      if (!take) {
+        const float v = cand_exact[i];
+        const int id = cand[i];
+        int beat = 0;
+        for (int j = 0; j < n_cand; ++j) {
+          const float w = cand_exact[j];
+          beat += (w > v) || (w == v && cand[j] < id);
         }
-        if (bi < 0) break;
-        chosen[n_ch++] = bi;
-        cand[bslot] = -1;
+        take = beat < kp;
+      }
+      if (take) {
+        const int slot = atomicAdd(&s_misc[2], 1);
+        if (slot < 64) chosen[slot] = cand[i];
       }
     }
-    s_misc[2] = n_ch;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && s_misc[2] > kk) {  // only reachable with non-finite scores
+    s_misc[2] = kk;
+    atomicOr(p.err, LSRM_ERR_CAPACITY);
   }
   __syncthreads();
   const int n_ch = s_misc[2];
@@ -488,7 +586,7 @@ __global__ void __launch_bounds__(kSfThreads, 1)
       const int id = chosen[i];
       int rank = 0;
       for (int j = 0; j < n_ch; ++j) rank += chosen[j] < id;
-      dst[rank] = id;
+      if (rank < p.topk) dst[rank] = id;
     } else {
       dst[i] = -1;
     }
@@ -517,7 +615,7 @@ int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shap
   const int nb_cap = std::max(meta->num_blocks, 1);
   size_t smem = D == 64 ? SfLayout<64>::bytes(nb_cap) : D == 32 ? SfLayout<32>::bytes(nb_cap) : SfLayout<16>::bytes(nb_cap);
   if (smem > 220 * 1024) return LSRM_ERR_UNSUPPORTED;
-  if (smem < (size_t)kOneCtaPerSmSmem) smem = kOneCtaPerSmSmem;  // all 512 TMEM columns per CTA
+  // 256 TMEM columns per CTA: two CTAs may share an SM (their 512 columns fit)
   CUtensorMap mq, mck;
   int rc;
   if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, kSfCols / G)))
