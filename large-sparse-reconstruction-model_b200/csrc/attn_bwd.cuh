@@ -216,12 +216,12 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       cached = union_cache_fill(uc, U, prm.union_blk, prm.union_mask, ubase, prm.cu_block_include_tokens, tile.kv_lo,
                                 tile.kv_hi);
     if (cached) {
-      int issued = 0;
+      int issued = 0, ucur = 0;
       for (int j = 0; j < n_chunks; ++j) {
         const int s = j % STAGES;
         if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
         DqMeta& mt = meta[s];
-        const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask);
+        const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
         __syncwarp();
@@ -602,21 +602,23 @@ __device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& pr
 }
 
 // Queries c*qpc .. c*qpc+qpc-1 of the cached list into qlist (-1 past the
-// end); returns how many are real.  Warp-wide.
-__device__ __forceinline__ int rev_cache_chunk(const RevCache& rc, int c, int qpc, int* qlist) {
+// end); returns how many are real.  Warp-wide.  cursor[k] (per lane, start
+// at 0) keeps the entry of the lane's k-th slot between calls with
+// increasing c: it only moves forward, so a short scan replaces a search.
+__device__ __forceinline__ int rev_cache_chunk(const RevCache& rc, int c, int qpc, int* qlist, int* cursor) {
   const int lane = threadIdx.x & 31;
   const int base = c * qpc;
   const int n = max(0, min(qpc, rc.total - base));
-  for (int i = lane; i < qpc; i += 32) {
+#pragma unroll
+  for (int k = 0; k < kKvQRows / 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i >= qpc) break;
     int q = -1;
     if (i < n) {
       const int t = base + i;
-      int lo = 0, hi = rc.n;  // last entry with prefix <= t (entries with no query never are)
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (rc.prefix[mid] <= t) lo = mid;
-        else hi = mid;
-      }
+      int lo = cursor[k];  // last entry with prefix <= t (entries with no query never are)
+      while (lo + 1 < rc.n && rc.prefix[lo + 1] <= t) ++lo;
+      cursor[k] = lo;
       int rank = t - rc.prefix[lo];
       const uint4 m = rc.mask[lo];
       int w = 0;
@@ -784,6 +786,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         if (lane == 0) mbar_arrive(&q_full[cc % STAGES]);
       };
       int issued = 0, published = 0;  // in this warp's own chunk sequence
+      int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
       for (int c = pw; c < n_chunks; c += nprod) {
         const int s = c % STAGES;
         if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
@@ -791,7 +794,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         int n = 0;
         if constexpr (MODE == kSelect) {
           if (cached) {
-            n = rev_cache_chunk(rc, c, qpc, mt.qlist);
+            n = rev_cache_chunk(rc, c, qpc, mt.qlist, rcur);
           } else {
             while (n < qpc) {
               if ((w0 | w1 | w2 | w3) == 0u) {
@@ -851,19 +854,25 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
             tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
           }
-        } else
-#pragma unroll 4
-        for (int idx = lane; idx < kKvQRows * CPR; idx += 32) {
-          const int row = idx / CPR, j = idx % CPR;  // CPR is a power of two
-          const int q = mt.qidx[row], g = row & (G - 1);
-          const uint32_t o = swz_offset<RB>(row, j);
-          if (q >= 0) {
-            const size_t src = ((size_t)q * prm.q_tok_stride + (size_t)(h * G + g) * D) * 2 + (size_t)j * 16;
-            cp_async_16(dq_s + o, qbase + src);
-            cp_async_16(ddo_s + o, dobase + src);
-          } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
-            st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
-            st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+        } else {
+          // lane: 16-byte column j of rows r0, r0 + 32/CPR, ...; the head and
+          // column offsets are folded into the lane's base pointers
+          const int j = lane % CPR, r0 = lane / CPR;
+          const uint8_t* qb = qbase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
+          const uint8_t* db = dobase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
+          const size_t tok_bytes = (size_t)prm.q_tok_stride * 2;
+#pragma unroll
+          for (int row = r0; row < kKvQRows; row += 32 / CPR) {
+            const int q = mt.qidx[row];
+            const uint32_t o = swz_offset<RB>(row, j);
+            if (q >= 0) {
+              const size_t off = (size_t)q * tok_bytes + (size_t)(row & (G - 1)) * (D * 2);
+              cp_async_16(dq_s + o, qb + off);
+              cp_async_16(ddo_s + o, db + off);
+            } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
+              st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
+              st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+            }
           }
         }
         cp_async_commit();

@@ -188,12 +188,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                                 tile.kv_hi);
     if (cached) {
       // the whole warp lays out each chunk (one lane per group) and issues its boxes
-      int issued = 0;
+      int issued = 0, ucur = 0;
       for (int j = 0; j < n_chunks; ++j) {
         const int s = j % STAGES;
         if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
         ChunkMeta& mt = meta[s];
-        const int r = union_cache_chunk<kGroupsPerChunk>(uc, j, mt.row0, mt.qmask, mt.colmask);
+        const int r = union_cache_chunk<kGroupsPerChunk>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
         __syncwarp();

@@ -412,21 +412,22 @@ __device__ __forceinline__ bool union_cache_fill(UnionCache& uc, int U, const in
 // Lays out groups [NG*j, NG*j+NG) of the union into row0 / qmask / colmask
 // (one lane per group, lanes >= NG idle).  Warp-wide.  Returns the lane's
 // group's first token (-1: no group).
+//
+// `cursor` (per lane, start at 0) remembers the lane's entry between calls
+// with increasing j: the lane's group only moves forward, so the entry is
+// found by a short forward scan instead of a search.
 template <int NG>
 __device__ __forceinline__ int union_cache_chunk(const UnionCache& uc, int j, int* row0, uint32_t (*qmask)[4],
-                                                 uint32_t* colmask) {
+                                                 uint32_t* colmask, int& cursor) {
   const int lane = threadIdx.x & 31;
   uint32_t bits = 0u;
   int r = -1;
   if (lane < NG) {
     const int g = NG * j + lane;
     if (g < uc.groups) {
-      int lo = 0, hi = uc.n;  // last entry with gstart <= g (empty entries never are)
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (uc.gstart[mid] <= g) lo = mid;
-        else hi = mid;
-      }
+      int lo = cursor;  // last entry with gstart <= g (empty entries never are)
+      while (lo + 1 < uc.n && uc.gstart[lo + 1] <= g) ++lo;
+      cursor = lo;
       r = uc.t0[lo] + 8 * (g - uc.gstart[lo]);
       const int cnt = min(8, uc.t1[lo] - r);
       const uint4 m = uc.mask[lo];
