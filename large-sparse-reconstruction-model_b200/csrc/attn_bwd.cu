@@ -66,7 +66,7 @@ static int launch_dq(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap&
 
 template <int D, bool BF16, int MODE>
 static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const CUtensorMap& mdo,
-                         const DkvParams& p, int grid_x, int hkv, cudaStream_t s) {
+                         const QMaps& qm, const DkvParams& p, int grid_x, int hkv, cudaStream_t s) {
   constexpr int STAGES = 4;
   using L = DkvSmem<D, STAGES>;
   auto kern = attn_dkdv_kernel<D, BF16, MODE, STAGES>;
@@ -74,7 +74,7 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
   {
     ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
     const dim3 grid = p.kv_sched ? dim3(grid_x * hkv, 1) : dim3(grid_x * p.n_split, hkv);
-    kern<<<grid, kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, p);
+    kern<<<grid, kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, qm, p);
     LSRM_LAUNCH_CHECK();
   }
   if (p.n_split > 1) {
@@ -87,16 +87,17 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
 
 template <int MODE>
 static int launch_dkdv(int D, bool bf16, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq,
-                       const CUtensorMap& mdo, const DkvParams& p, int grid_x, int hkv, cudaStream_t s) {
+                       const CUtensorMap& mdo, const QMaps& qm, const DkvParams& p, int grid_x, int hkv,
+                       cudaStream_t s) {
   if (grid_x <= 0) return LSRM_OK;
   if (D == 64)
-    return bf16 ? launch_dkdv_t<64, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
-                : launch_dkdv_t<64, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
+    return bf16 ? launch_dkdv_t<64, true, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s)
+                : launch_dkdv_t<64, false, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s);
   if (D == 16)
-    return bf16 ? launch_dkdv_t<16, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
-                : launch_dkdv_t<16, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
-  return bf16 ? launch_dkdv_t<32, true, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s)
-              : launch_dkdv_t<32, false, MODE>(mk, mv, mq, mdo, p, grid_x, hkv, s);
+    return bf16 ? launch_dkdv_t<16, true, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s)
+                : launch_dkdv_t<16, false, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s);
+  return bf16 ? launch_dkdv_t<32, true, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s)
+              : launch_dkdv_t<32, false, MODE>(mk, mv, mq, mdo, qm, p, grid_x, hkv, s);
 }
 
 static int launch_zero_tail(void* dk, void* dv, const int32_t* start, long long total, long long stride,
@@ -241,8 +242,22 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.scale_log2 = scale * 1.44269504f;
     p.scale = scale;
     p.err = err;
-    // the query rows are gathered with cp.async; the query maps are unused here
-    if ((rc = launch_dkdv<kSelect>(D, bf16, mk, mv, mk, mv, p, plan.kvtiles_ub, hkv, s))) return rc;
+    // query rows: TMA boxes of whole query windows (G <= 8), else cp.async gathers
+    QMaps qm;
+    for (int i = 0; i < 4; ++i) {
+      if (G <= 8) {
+        if ((rc = make_tmap_3d(&qm.q[i], q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G,
+                               (8 / G) << i)))
+          return rc;
+        if ((rc = make_tmap_3d(&qm.dout[i], dout, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G,
+                               (8 / G) << i)))
+          return rc;
+      } else {
+        qm.q[i] = mk;
+        qm.dout[i] = mv;
+      }
+    }
+    if ((rc = launch_dkdv<kSelect>(D, bf16, mk, mv, mk, mv, qm, p, plan.kvtiles_ub, hkv, s))) return rc;
   }
   return launch_zero_tail(dk, dv, meta->cu_block_include_tokens + meta->num_blocks, meta->total_k,
                           shape->kv_token_stride, row_elems, s);
@@ -346,8 +361,13 @@ extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shap
     p.half_window = window / 2;
     p.lse_natural = mode == LSRM_DENSE_COMPRESSED;
     p.err = err;
-    rc = (mode == LSRM_DENSE_SLIDING) ? launch_dkdv<kBand>(D, bf16, mk, mv, mq, mdo, p, plan.kvtiles_ub, hkv, s)
-                                      : launch_dkdv<kRange>(D, bf16, mk, mv, mq, mdo, p, plan.kvtiles_ub, hkv, s);
+    QMaps qm;  // unused by the dense branches
+    for (int i = 0; i < 4; ++i) {
+      qm.q[i] = mq;
+      qm.dout[i] = mdo;
+    }
+    rc = (mode == LSRM_DENSE_SLIDING) ? launch_dkdv<kBand>(D, bf16, mk, mv, mq, mdo, qm, p, plan.kvtiles_ub, hkv, s)
+                                      : launch_dkdv<kRange>(D, bf16, mk, mv, mq, mdo, qm, p, plan.kvtiles_ub, hkv, s);
     if (rc) return rc;
   }
   const int32_t* start = mode == LSRM_DENSE_COMPRESSED   ? meta->cu_seqblocks + meta->num_seqs

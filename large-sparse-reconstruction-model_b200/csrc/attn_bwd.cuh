@@ -492,12 +492,25 @@ constexpr int kRevCacheCap = 1024;
 
 struct RevCache {
   int tq0[kRevCacheCap];
-  int prefix[kRevCacheCap];
+  int prefix[kRevCacheCap];  // queries before the entry
+  int gstart[kRevCacheCap];  // query groups before the entry (G <= 8)
+  int wmask[kRevCacheCap];   // the entry's non-empty query windows (16 bits)
   uint4 mask[kRevCacheCap];
-  int n;      // entries (-1: the block's list did not fit)
-  int total;  // queries
-  int pad[2];
+  int n;       // entries (-1: the block's list did not fit)
+  int total;   // queries
+  int groups;  // query groups (G <= 8): 8 rows = 8/G queries of one window
+  int pad;
 };
+
+// Query groups (G <= 8): a tile's 128 MMA rows are 16 windows of 8 rows,
+// window w = queries [w*W, w*W + W) of the tile, W = 8/G.  A group is one
+// non-empty window of one reverse-map entry; its bits say which of its W
+// queries selected the block.
+__device__ __forceinline__ uint32_t window_bits(const uint4& m, int w, int W) {
+  const int o = w * W;
+  const uint32_t word = (o >> 5) == 0 ? m.x : (o >> 5) == 1 ? m.y : (o >> 5) == 2 ? m.z : m.w;
+  return (word >> (o & 31)) & ((1u << W) - 1u);
+}
 
 // Position of the n-th (0-based) set bit of `word` (n < popc(word)).
 __device__ __forceinline__ int nth_set_bit(uint32_t word, int n) {
@@ -574,29 +587,45 @@ __device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& pr
     return;
   }
   const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
-  int carry = 0;
+  int carry = 0, gcarry = 0;
   for (int b0 = 0; b0 < n; b0 += 32) {
     const int i = b0 + lane;
-    int cnt = 0;
+    int cnt = 0, gcnt = 0;
     if (i < n) {
       const int2 x = ent[e0 + i];
       const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
       rc.tq0[i] = prm.qtiles[x.x].q_start;
       rc.mask[i] = m;
       cnt = __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+      if (prm.G <= 8) {
+        const int W = 8 / prm.G;
+        uint32_t wm = 0u;
+#pragma unroll
+        for (int w = 0; w < 16; ++w) wm |= (window_bits(m, w, W) != 0u ? 1u : 0u) << w;
+        rc.wmask[i] = (int)wm;
+        gcnt = __popc(wm);
+      }
     }
-    int incl = cnt;
+    int incl = cnt, gincl = gcnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      const int y = __shfl_up_sync(0xffffffffu, incl, o), gy = __shfl_up_sync(0xffffffffu, gincl, o);
+      if (lane >= o) {
+        incl += y;
+        gincl += gy;
+      }
     }
-    if (i < n) rc.prefix[i] = carry + incl - cnt;
+    if (i < n) {
+      rc.prefix[i] = carry + incl - cnt;
+      rc.gstart[i] = gcarry + gincl - gcnt;
+    }
     carry += __shfl_sync(0xffffffffu, incl, 31);
+    gcarry += __shfl_sync(0xffffffffu, gincl, 31);
   }
   if (lane == 0) {
     rc.n = n;
     rc.total = carry;
+    rc.groups = gcarry;
   }
   __syncwarp();
 }
@@ -648,11 +677,18 @@ __device__ __forceinline__ int rev_cache_chunk(const RevCache& rc, int c, int qp
   return n;
 }
 
+// Query-window boxes of the select-mode producer: box heights 8 << i rows
+// ((8/G) << i tokens of G heads), i = 0..3.
+struct QMaps {
+  CUtensorMap q[4];
+  CUtensorMap dout[4];
+};
+
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kDkvThreads, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                     const DkvParams prm) {
+                     const __grid_constant__ QMaps qm, const DkvParams prm) {
   using L = DkvSmem<D, STAGES>;
   constexpr int RB = L::RB;
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
@@ -709,14 +745,17 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   RevCache& rc = *reinterpret_cast<RevCache*>(smem + L::OFF_RC);
   if (warp == kDkvProducerWarp) {
     int nqueries;
+    int nch;
     if constexpr (MODE == kSelect) {
       rev_cache_fill(rc, prm, h, kt.seg);
       nqueries = rc.n >= 0 ? rc.total : count_select_queries(prm, h, kt.seg);
+      nch = (rc.n >= 0 && G <= 8) ? (rc.groups + 7) / 8 : (nqueries + qpc - 1) / qpc;
     } else {
       nqueries = max(q_hi - q_lo, 0);
+      nch = (nqueries + qpc - 1) / qpc;
       if (lane == 0) rc.n = -1;
     }
-    if (lane == 0) *s_nchunks = (nqueries + qpc - 1) / qpc;
+    if (lane == 0) *s_nchunks = nch;
   }
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -761,6 +800,10 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     const int nprod = (MODE == kSelect && !cached) ? 1 : 2;  // the sequential walk needs one warp
     const int pw = warp == kDkvProducerWarp ? 0 : 1;
     if (pw < nprod) {
+      if (MODE == kSelect && lane < 4) {
+        tma_prefetch_desc(&qm.q[lane]);
+        tma_prefetch_desc(&qm.dout[lane]);
+      }
       if (pw == 0 && lane == 0) {
         mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
         tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
@@ -787,10 +830,65 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       };
       int issued = 0, published = 0;  // in this warp's own chunk sequence
       int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
+      int gcur = 0;                   // group cursor (grouped path)
+      const bool grouped = cached && G <= 8;
+      const int W = G <= 8 ? 8 / G : 1;  // queries per 8-row window
       for (int c = pw; c < n_chunks; c += nprod) {
         const int s = c % STAGES;
         if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
         KvMeta& mt = meta[s];
+        if (grouped) {
+          // 8 groups of 8 rows: lane g < 8 finds its group's window; each
+          // group lands by TMA at an 8-row boundary (boxes of whole windows,
+          // merged when adjacent); rows whose query did not select the block
+          // get lse = +inf, so their P and dS are exactly zero
+          int tok = -1;
+          uint32_t bits = 0u;
+          if (lane < 8) {
+            const int gg = 8 * c + lane;
+            if (gg < rc.groups) {
+              int lo = gcur;
+              while (lo + 1 < rc.n && rc.gstart[lo + 1] <= gg) ++lo;
+              gcur = lo;
+              const int w = nth_set_bit((uint32_t)rc.wmask[lo], gg - rc.gstart[lo]);
+              tok = rc.tq0[lo] + w * W;
+              bits = window_bits(rc.mask[lo], w, W);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < kKvQRows / 32; ++k) {
+            const int row = lane + 32 * k, grp = row >> 3, rr = row & 7;
+            const int t = __shfl_sync(0xffffffffu, tok, grp);
+            const uint32_t bb = __shfl_sync(0xffffffffu, bits, grp);
+            const int qq = rr >> lg_g, g = rr & (G - 1);
+            const bool valid = t >= 0 && ((bb >> qq) & 1u);
+            mt.qidx[row] = valid ? t + qq : -1;
+            if (valid) {
+              const size_t si = (size_t)(h * G + g) * prm.total_q + (t + qq);
+              cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
+              cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+            } else {
+              mt.lse2[row] = INFINITY;
+              mt.delta[row] = 0.f;
+            }
+          }
+          if (lane == 0) {
+            mt.n_rows = kKvQRows;
+            mbar_expect_tx(&q_full[s], 2 * L::QTILE);
+          }
+          __syncwarp();
+          issue_group_runs<8, RB>(tok, sQ + s * L::QTILE, sDO + s * L::QTILE, qm.q, qm.dout, h * G, prm.total_q,
+                                  &q_full[s], W);
+          cp_async_commit();
+          ++issued;
+          if (issued > LAG) {
+            if (LAG == 0) cp_async_wait<0>();
+            else cp_async_wait<STAGES - 2>();
+            publish(pw + nprod * published);
+            ++published;
+          }
+          continue;
+        }
         int n = 0;
         if constexpr (MODE == kSelect) {
           if (cached) {

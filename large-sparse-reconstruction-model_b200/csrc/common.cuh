@@ -452,14 +452,17 @@ __device__ __forceinline__ int union_cache_chunk(const UnionCache& uc, int j, in
 // groups contiguous in memory (or runs of unused groups, read past the end of
 // the tensor: zero fill) are split greedily into power-of-two boxes
 // (8 << i rows, maps[i]); the lane of each box's first group issues it.
-// `r` is the lane's group's first token (-1 unused).  Warp-wide; the caller
-// has armed `bar` with the chunk's bytes.
+// `r` is the lane's group's first token (-1 unused); consecutive groups of a
+// run are `step` tokens apart (a group is 8 rows: 8 tokens of one head, or
+// 8/G tokens of G heads).  Warp-wide; the caller has armed `bar` with the
+// chunk's bytes.
 template <int NG, int RB>
 __device__ __forceinline__ void issue_group_runs(int r, uint8_t* dK, uint8_t* dV, const CUtensorMap* maps_k,
-                                                 const CUtensorMap* maps_v, int h, int oob_row, uint64_t* bar) {
+                                                 const CUtensorMap* maps_v, int h, int oob_row, uint64_t* bar,
+                                                 int step = 8) {
   const int lane = threadIdx.x & 31;
   const int prev = __shfl_up_sync(0xffffffffu, r, 1);
-  const bool cont = lane > 0 && lane < NG && ((r >= 0 && prev == r - 8) || (r < 0 && prev < 0));
+  const bool cont = lane > 0 && lane < NG && ((r >= 0 && prev == r - step) || (r < 0 && prev < 0));
   const uint32_t starts = __ballot_sync(0xffffffffu, lane < NG && !cont) | (1u << NG);
   if (lane < NG) {
     const int s0 = 31 - __clz(starts & ((2u << lane) - 1u));        // this run's first group
