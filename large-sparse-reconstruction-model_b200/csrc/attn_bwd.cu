@@ -115,8 +115,11 @@ static int dense_split(const lsrm_varlen* m, const lsrm_attn_shape* sh, int mode
   if (mode != LSRM_DENSE_COMPRESSED) return 1;
   const int G = sh->num_q_heads / sh->num_kv_heads;
   const int qpc = kKvQRows / G;
+  // compressed keys are few (one per block): split every KV tile's queries
+  // so that the grid is ~16 waves of 148 SMs (balanced), partial sums are
+  // reduced in a fixed order afterwards
   const long long ctas = (long long)std::max(m->num_blocks / kRows + m->num_seqs, 1) * sh->num_kv_heads;
-  int n = (int)std::min<long long>(32, (2 * 148 + ctas - 1) / ctas);
+  int n = (int)std::min<long long>(32, (16 * 148 + ctas - 1) / ctas);
   const long long chunks_per_seq = std::max<long long>(1, (long long)m->total_q / std::max(m->num_seqs, 1) / qpc);
   n = (int)std::max<long long>(1, std::min<long long>(n, chunks_per_seq / 16));
   (void)kvtiles_ub;
