@@ -1,4 +1,5 @@
 // Host entry points of the forward attention paths.
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 
@@ -16,7 +17,12 @@ static int launch_fwd_t(const CUtensorMap& mq, const KVMaps& kv, const FwdParams
   auto kern = attn_fwd_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   ProfScope ps(MODE == kSelect ? "attn_fwd_select" : (MODE == kBand ? "attn_fwd_sliding" : "attn_fwd_range"), s);
-  kern<<<dim3(grid_x, hkv), kFwdThreads, L::ALLOC, s>>>(mq, kv, p);
+  // persistent: one CTA per SM walks the (tile, head) items
+  FwdParams pp = p;
+  pp.hkv = hkv;
+  const long long items_ub = (long long)grid_x * hkv;
+  const int grid = (int)std::min<long long>(items_ub, num_sms());
+  kern<<<dim3(grid, 1), kFwdThreads, L::ALLOC, s>>>(mq, kv, pp);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }

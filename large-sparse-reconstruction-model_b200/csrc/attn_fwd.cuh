@@ -51,6 +51,7 @@ struct FwdParams {
   float scale_log2;
   int half_window;
   int lse_natural;  // write ln-based LSE (compressed branch) instead of log2
+  int hkv;          // kv heads (work items are tile x head)
   int* err;
 };
 
@@ -68,18 +69,18 @@ struct FwdSmem {
   static constexpr int RB = 2 * D;
   static constexpr int TILE = 128 * RB;
   static constexpr int P_BYTES = 2 * 128 * 128;  // two 64-key regions, 128B rows
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + TILE;
+  static constexpr int OFF_Q = 0;                 // two Q tiles (persistent CTAs prefetch the next)
+  static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
   static constexpr int OFF_P = OFF_V + STAGES * TILE;
   static constexpr int OFF_XCH = OFF_P + 2 * P_BYTES;  // row max / row sum exchange [2][2][128]
   static constexpr int OFF_META = OFF_XCH + 4 * 128 * 4;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(ChunkMeta);
-  // barriers: kv_full[S], kv_empty[S], q_full, s_full[2], s_free[2], p_full[2],
-  // p_free[2], pv_full[2], pv_free[2], mma_done
-  static constexpr int NBAR = 2 * STAGES + 1 + 12 + 1;
+  // barriers: kv_full[S], kv_empty[S], q_full[2], q_empty[2], s_full[2], s_free[2],
+  // p_full[2], p_free[2], pv_full[2], pv_free[2], mma_done
+  static constexpr int NBAR = 2 * STAGES + 4 + 12 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_UC = OFF_MISC + 16;  // select mode: the tile's union (16-byte aligned)
+  static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
   static constexpr int ALLOC = (BYTES + 1024 > kOneCtaPerSmSmem) ? BYTES + 1024 : kOneCtaPerSmSmem;
   static_assert(OFF_UC % 16 == 0, "union cache must be 16-byte aligned");
@@ -101,9 +102,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
 
-  const int tile_idx = blockIdx.x, h = blockIdx.y;
-  if (tile_idx >= *prm.n_tiles) return;
-  const QTile tile = prm.tiles[tile_idx];
+  // Persistent CTAs: work item i = (tile i / Hkv, kv head i % Hkv) for
+  // i = blockIdx.x, blockIdx.x + gridDim.x, ...  Every role walks the same
+  // items; chunk counters J run on across items, so the ring barriers'
+  // phases continue, and the producer fetches the next item's Q tile and
+  // KV chunks while the softmax warps finish the current one.
+  const int hkv_n = gridDim.y;  // 1: heads are folded into the item index
+  (void)hkv_n;
+  const int n_items = (*prm.n_tiles) * prm.hkv;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -116,7 +122,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + STAGES;
   uint64_t* q_full = bars + 2 * STAGES;
-  uint64_t* s_full = q_full + 1;
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* s_full = q_empty + 2;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* p_free = p_full + 2;
@@ -129,25 +136,38 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = prm.G;
 
-  // number of KV chunks for this (tile, head)
-  int n_chunks;
-  int U = 0;
-  size_t ubase = 0;
-  if constexpr (MODE == kSelect) {
-    ubase = ((size_t)h * prm.tiles_ub + tile_idx) * prm.union_cap;
-    U = prm.union_cnt[(size_t)h * prm.tiles_ub + tile_idx];
-    n_chunks = (prm.union_ngroups[(size_t)h * prm.tiles_ub + tile_idx] + kGroupsPerChunk - 1) / kGroupsPerChunk;
-  } else {
-    n_chunks = tile.kv_hi > tile.kv_lo ? (tile.kv_hi - tile.kv_lo + kKVChunk - 1) / kKVChunk : 0;
-  }
+  // per-item decode: tile, head, KV chunks (select: union size and base)
+  struct Item {
+    QTile tile;
+    int tile_idx, h, n_chunks, U;
+    size_t ubase;
+  };
+  auto item_of = [&](int i) {
+    Item it;
+    it.tile_idx = i / prm.hkv;
+    it.h = i - it.tile_idx * prm.hkv;
+    it.tile = prm.tiles[it.tile_idx];
+    it.U = 0;
+    it.ubase = 0;
+    if constexpr (MODE == kSelect) {
+      const size_t th = (size_t)it.h * prm.tiles_ub + it.tile_idx;
+      it.ubase = th * prm.union_cap;
+      it.U = prm.union_cnt[th];
+      it.n_chunks = (prm.union_ngroups[th] + kGroupsPerChunk - 1) / kGroupsPerChunk;
+    } else {
+      it.n_chunks = it.tile.kv_hi > it.tile.kv_lo ? (it.tile.kv_hi - it.tile.kv_lo + kKVChunk - 1) / kKVChunk : 0;
+    }
+    return it;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 8);
       mbar_init(&p_full[i], 8);
@@ -177,86 +197,96 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&kv.k[lane]);
       tma_prefetch_desc(&kv.v[lane]);
     }
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, L::TILE);
-      tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, q_full);
-    }
     UnionCache& uc = *reinterpret_cast<UnionCache*>(smem + L::OFF_UC);
-    bool cached = false;
-    if constexpr (MODE == kSelect)
-      cached = union_cache_fill(uc, U, prm.union_blk, prm.union_mask, ubase, prm.cu_block_include_tokens, tile.kv_lo,
-                                tile.kv_hi);
-    if (cached) {
-      // the whole warp lays out each chunk (one lane per group) and issues its boxes
-      int issued = 0, ucur = 0;
-      for (int j = 0; j < n_chunks; ++j) {
-        const int s = j % STAGES;
-        if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-        ChunkMeta& mt = meta[s];
-        const int r = union_cache_chunk<kGroupsPerChunk>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
-        __syncwarp();
-        issue_group_runs<kGroupsPerChunk, RB>(r, sK + s * L::TILE, sV + s * L::TILE, kv.k, kv.v, h, prm.total_k,
-                                              &kv_full[s]);
-        issued = j + 1;
+    int J = 0, issued = 0, it_n = 0, q_loads = 0;  // chunks issued (all items), items started, Q tiles issued
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
+      const Item w = item_of(i);
+      const QTile& tile = w.tile;
+      const int h = w.h, qb = it_n & 1;
+      if (!warp_wait(&q_empty[qb], ((it_n >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&q_full[qb], L::TILE);
+        tma_load_3d(sQ + qb * L::TILE, &tm_q, 0, h * G, tile.q_start, &q_full[qb]);
       }
-      if (lane == 0 && *abort_flag) {
-        mbar_wait_drain(q_full, 0);
-        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
-      }
-    } else if (lane == 0) {
-      int u = -1, tcur = 0, tend = 0;  // select-mode walk state (unions too large for the cache)
-      int issued = 0;
-      for (int j = 0; j < n_chunks; ++j) {
-        const int s = j % STAGES;
-        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-        ChunkMeta& mt = meta[s];
-        uint8_t* dK = sK + s * L::TILE;
-        uint8_t* dV = sV + s * L::TILE;
-        if constexpr (MODE == kSelect) {
-          uint32_t cm[4] = {0u, 0u, 0u, 0u};
-          for (int g = 0; g < kGroupsPerChunk; ++g) {
-            while (tcur >= tend && u + 1 < U) {
-              ++u;
-              const int gb = prm.union_blk[ubase + u];
-              tcur = max(prm.cu_block_include_tokens[gb], tile.kv_lo);
-              tend = min(prm.cu_block_include_tokens[gb + 1], tile.kv_hi);
-            }
-            if (tcur < tend) {
-              const int cnt = min(kGroupRows, tend - tcur);
-              mt.row0[g] = tcur;
-              const uint4 qm = prm.union_mask[ubase + u];
-              mt.qmask[g][0] = qm.x;
-              mt.qmask[g][1] = qm.y;
-              mt.qmask[g][2] = qm.z;
-              mt.qmask[g][3] = qm.w;
-              cm[g >> 2] |= ((1u << cnt) - 1u) << ((g & 3) * 8);
-              tcur += cnt;
-            } else {
-              mt.row0[g] = -1;
-              mt.qmask[g][0] = mt.qmask[g][1] = mt.qmask[g][2] = mt.qmask[g][3] = 0u;
-            }
-          }
-          for (int w = 0; w < 4; ++w) mt.colmask[w] = cm[w];
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
-          // unused groups read past the end of the tensor: zero fill
-          load_group_runs<kGroupsPerChunk, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
-        } else {
-          const int k0 = tile.kv_lo + j * kKVChunk;
-          mt.kv_start = k0;
-          mt.n_valid = min(kKVChunk, tile.kv_hi - k0);
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
-          tma_load_3d(dK, &kv.k[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
-          tma_load_3d(dV, &kv.v[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
+      q_loads = it_n + 1;
+      bool cached = false;
+      if constexpr (MODE == kSelect)
+        cached = union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens,
+                                  tile.kv_lo, tile.kv_hi);
+      if (cached) {
+        // the whole warp lays out each chunk (one lane per group) and issues its boxes
+        int ucur = 0;
+        for (int j = 0; j < w.n_chunks; ++j, ++J) {
+          const int s = J % STAGES;
+          if (!warp_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          ChunkMeta& mt = meta[s];
+          const int r = union_cache_chunk<kGroupsPerChunk>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+          __syncwarp();
+          issue_group_runs<kGroupsPerChunk, RB>(r, sK + s * L::TILE, sV + s * L::TILE, kv.k, kv.v, h, prm.total_k,
+                                                &kv_full[s]);
+          issued = J + 1;
         }
-        issued = j + 1;
+      } else {
+        if (lane == 0) {
+          int u = -1, tcur = 0, tend = 0;  // select-mode walk state (unions too large for the cache)
+          for (int j = 0; j < w.n_chunks; ++j, ++J) {
+            const int s = J % STAGES;
+            if (!mbar_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+            ChunkMeta& mt = meta[s];
+            uint8_t* dK = sK + s * L::TILE;
+            uint8_t* dV = sV + s * L::TILE;
+            if constexpr (MODE == kSelect) {
+              uint32_t cm[4] = {0u, 0u, 0u, 0u};
+              for (int g = 0; g < kGroupsPerChunk; ++g) {
+                while (tcur >= tend && u + 1 < w.U) {
+                  ++u;
+                  const int gb = prm.union_blk[w.ubase + u];
+                  tcur = max(prm.cu_block_include_tokens[gb], tile.kv_lo);
+                  tend = min(prm.cu_block_include_tokens[gb + 1], tile.kv_hi);
+                }
+                if (tcur < tend) {
+                  const int cnt = min(kGroupRows, tend - tcur);
+                  mt.row0[g] = tcur;
+                  const uint4 qm = prm.union_mask[w.ubase + u];
+                  mt.qmask[g][0] = qm.x;
+                  mt.qmask[g][1] = qm.y;
+                  mt.qmask[g][2] = qm.z;
+                  mt.qmask[g][3] = qm.w;
+                  cm[g >> 2] |= ((1u << cnt) - 1u) << ((g & 3) * 8);
+                  tcur += cnt;
+                } else {
+                  mt.row0[g] = -1;
+                  mt.qmask[g][0] = mt.qmask[g][1] = mt.qmask[g][2] = mt.qmask[g][3] = 0u;
+                }
+              }
+              for (int x = 0; x < 4; ++x) mt.colmask[x] = cm[x];
+              mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+              // unused groups read past the end of the tensor: zero fill
+              load_group_runs<kGroupsPerChunk, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
+            } else {
+              const int k0 = tile.kv_lo + j * kKVChunk;
+              mt.kv_start = k0;
+              mt.n_valid = min(kKVChunk, tile.kv_hi - k0);
+              mbar_arrive_expect_tx(&kv_full[s], 2 * L::TILE);
+              tma_load_3d(dK, &kv.k[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
+              tma_load_3d(dV, &kv.v[kNumBoxes - 1], 0, h, k0, &kv_full[s]);
+            }
+            issued = J + 1;
+          }
+        }
+        // lane 0 advanced J and may have hit an abort: share both
+        J = __shfl_sync(0xffffffffu, J, 0);
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+        ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
       }
-      // Teardown after an abort: let issued copies land before the CTA exits.
-      if (*abort_flag) {
-        mbar_wait_drain(q_full, 0);
-        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
-      }
+    }
+    // Teardown after an abort: let issued copies land before the CTA exits.
+    if (lane == 0 && *abort_flag) {
+      for (int k = max(0, q_loads - 2); k < q_loads; ++k) mbar_wait_drain(&q_full[k & 1], (k >> 1) & 1);
+      for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
     }
     __syncwarp();
   } else if (warp == 9) {
@@ -264,7 +294,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = make_idesc(AB, 0, 0, 128, 128);
       const uint32_t idesc_pv = make_idesc(AB, 0, 1, 128, D);
-      bool ok = mbar_wait(q_full, 0, abort_flag, prm.err);
       auto issue_pv = [&](int i) -> bool {
         const int pb = i & 1, s = i % STAGES;
         if (!mbar_wait(&p_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
@@ -283,13 +312,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         umma_commit(&kv_empty[s]);
         return true;
       };
-      if (ok) {
-        for (int j = 0; j < n_chunks && ok; ++j) {
-          const int s = j % STAGES, sb = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
-          if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      bool ok = true;
+      int J = 0, it_n = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
+        const int n_chunks = item_of(i).n_chunks, qb = it_n & 1;
+        if (!mbar_wait(&q_full[qb], (it_n >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+        const uint32_t q_base = smem_u32(sQ + qb * L::TILE);
+        for (int j = 0; j < n_chunks; ++j, ++J) {
+          const int s = J % STAGES, sb = J & 1;
+          if (!mbar_wait(&kv_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&s_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t q_base = smem_u32(sQ);
           const uint32_t k_base = smem_u32(sK + s * L::TILE);
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
@@ -298,9 +331,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             umma_f16(tm_s0 + sb * 128, da, db, idesc_qk, ks > 0);
           }
           umma_commit(&s_full[sb]);
-          if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+          if (j >= 1 && !issue_pv(J - 1)) { ok = false; break; }
         }
-        if (ok && n_chunks > 0) issue_pv(n_chunks - 1);
+        if (!ok) break;
+        umma_commit(&q_empty[qb]);  // the item's Q tile is free once its S products are done
+        if (n_chunks > 0 && !issue_pv(J - 1)) { ok = false; break; }
       }
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
@@ -312,17 +347,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;  // MMA row
     const int qloc = r / G;
-    const int hq = h * G + (r % G);
-    const int qi = tile.q_start + qloc;
-    const bool row_valid = qloc < tile.n_q;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2;
     float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);  // [max|sum][half][128]
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
     float o[DH];
-#pragma unroll
-    for (int c = 0; c < DH; ++c) o[c] = 0.f;
     bool ok = true;
+    float alpha_prev = 1.f;
 
     auto fold_pv = [&](int i) -> bool {
       const int pb = i & 1;
@@ -341,10 +371,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       return true;
     };
 
-    for (int j = 0; j < n_chunks; ++j) {
-      const int s = j % STAGES, sb = j & 1;
-      if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+    int J = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    const Item w = item_of(it);
+    const QTile& tile = w.tile;
+    const int n_chunks = w.n_chunks;
+    const int hq = w.h * G + (r % G);
+    const int qi = tile.q_start + qloc;
+    const bool row_valid = qloc < tile.n_q;
+    float m = -INFINITY, l = 0.f;
+    alpha_prev = 1.f;
+#pragma unroll
+    for (int c = 0; c < DH; ++c) o[c] = 0.f;
+    for (int j = 0; j < n_chunks; ++j, ++J) {
+      const int s = J % STAGES, sb = J & 1;
+      if (!warp_wait(&s_full[sb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&kv_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       // key-validity mask of this row for the warp's 64 columns (2 words)
       uint32_t vm[2];
@@ -409,7 +451,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
       // probabilities -> P (shared, K-major 128B swizzle; this half = region `half`)
-      if (!warp_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&p_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES) + half * 16384;
 #pragma unroll
@@ -447,11 +489,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       pair_bar(quarter);
       const float rowsum = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps
       l = l * alpha + rowsum;
-      if (j >= 1 && !fold_pv(j - 1)) { ok = false; break; }
+      if (j >= 1 && !fold_pv(J - 1)) { ok = false; break; }
       alpha_prev = alpha;
       m = m_new;
     }
-    if (ok && n_chunks > 0) ok = fold_pv(n_chunks - 1);
+    if (ok && n_chunks > 0) ok = fold_pv(J - 1);
     if (ok && row_valid) {
       const float inv = (l > 0.f) ? 1.f / l : __int_as_float(0x7fc00000);
       uint8_t* orow =
@@ -471,6 +513,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         prm.lse[(size_t)hq * prm.total_q + qi] = lse;
       }
     }
+    }  // items
   }
 
   tc_fence_before();

@@ -80,6 +80,18 @@ int make_kv_maps(CUtensorMap* maps_k, CUtensorMap* maps_v, int n, const void* k,
   return LSRM_OK;
 }
 
+int num_sms() {
+  static int cache[128] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 // ------------------------------ profiler ----------------------------------
 struct ProfRecord {
   std::string name;

@@ -15,6 +15,9 @@
 namespace lsrm {
 
 void set_error(const char* fmt, ...);
+
+// Streaming multiprocessors of the current device (cached per device).
+int num_sms();
 extern std::atomic<uint64_t> g_launch_count;
 
 inline void count_launch(uint64_t n = 1) { g_launch_count.fetch_add(n, std::memory_order_relaxed); }
