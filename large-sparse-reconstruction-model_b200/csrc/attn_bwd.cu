@@ -45,7 +45,11 @@ static int launch_dq_t(const CUtensorMap& mq, const CUtensorMap& mdo, const KVMa
   auto kern = attn_dq_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   ProfScope ps(MODE == kSelect ? "attn_dq_select" : (MODE == kBand ? "attn_dq_sliding" : "attn_dq_range"), s);
-  kern<<<dim3(grid_x, hkv), kDqThreads, L::ALLOC, s>>>(mq, mdo, kv, p);
+  // persistent: one CTA per SM walks the (tile, head) items
+  DqParams pp = p;
+  pp.hkv = hkv;
+  const int grid = (int)std::min<long long>((long long)grid_x * hkv, num_sms());
+  kern<<<dim3(grid, 1), kDqThreads, L::ALLOC, s>>>(mq, mdo, kv, pp);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }
@@ -178,7 +182,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
   if ((rc = launch_build_tiles(plan.kvtiles, plan.n_kvtiles, plan.kvtiles_ub, kTilesKVBlock, kRows, meta, nullptr,
                                meta->num_blocks, 0, err, s)))
     return rc;
-  if ((rc = launch_build_kv_schedule(plan, kKvQRows / G, s))) return rc;
+  if ((rc = launch_build_kv_schedule(plan, G, s))) return rc;
   const float scale = softmax_scale_of(shape);
   // dQ (+ delta)
   {
@@ -238,6 +242,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.partial = nullptr;
     p.n_split = 1;
     p.kv_sched = plan.kv_sched;
+    p.item_nch = plan.item_nch;
     p.kv_tok_stride = shape->kv_token_stride;
     p.total_q = meta->total_q;
     p.G = G;

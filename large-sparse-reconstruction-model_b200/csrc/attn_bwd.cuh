@@ -49,6 +49,7 @@ struct DqParams {
   float scale;
   int half_window;
   int lse_natural;
+  int hkv;  // kv heads (work items are tile x head)
   int* err;
 };
 
@@ -66,14 +67,16 @@ struct DqSmem {
   static constexpr int QTILE = 128 * RB;
   static constexpr int KTILE = kDqChunk * RB;
   static constexpr int DS_BYTES = 128 * 128;  // 128 rows x 64 keys x 2 B
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = QTILE;
-  static constexpr int OFF_K = 2 * QTILE;
+  static constexpr int OFF_Q = 0;            // two Q tiles and two dO tiles (the next item's prefetch)
+  static constexpr int OFF_DO = 2 * QTILE;
+  static constexpr int OFF_K = 4 * QTILE;
   static constexpr int OFF_V = OFF_K + STAGES * KTILE;
   static constexpr int OFF_DS = OFF_V + STAGES * KTILE;
   static constexpr int OFF_META = OFF_DS + 2 * DS_BYTES;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(DqMeta);
-  static constexpr int NBAR = 2 * STAGES + 1 + 8 + 2;
+  // kv_full[S], kv_empty[S], qdo_full[2], qdo_empty[2], sd_full[2], sd_free[2],
+  // ds_full[2], ds_free[2], dq_done, dq_free, mma_done
+  static constexpr int NBAR = 2 * STAGES + 4 + 8 + 3;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
@@ -130,9 +133,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   constexpr uint32_t AB = BF16 ? 1u : 0u;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
 
-  const int tile_idx = blockIdx.x, h = blockIdx.y;
-  if (tile_idx >= *prm.n_tiles) return;
-  const QTile tile = prm.tiles[tile_idx];
+  // Persistent CTAs over (tile, kv head) items; see attn_fwd_kernel.
+  const int n_items = (*prm.n_tiles) * prm.hkv;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -146,41 +148,58 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + STAGES;
   uint64_t* qdo_full = bars + 2 * STAGES;
-  uint64_t* sd_full = qdo_full + 1;
+  uint64_t* qdo_empty = qdo_full + 2;
+  uint64_t* sd_full = qdo_empty + 2;
   uint64_t* sd_free = sd_full + 2;
   uint64_t* ds_full = sd_free + 2;
   uint64_t* ds_free = ds_full + 2;
   uint64_t* dq_done = ds_free + 2;
-  uint64_t* mma_done = dq_done + 1;
+  uint64_t* dq_free = dq_done + 1;
+  uint64_t* mma_done = dq_free + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = prm.G;
 
-  int n_chunks, U = 0;
-  size_t ubase = 0;
-  if constexpr (MODE == kSelect) {
-    ubase = ((size_t)h * prm.tiles_ub + tile_idx) * prm.union_cap;
-    U = prm.union_cnt[(size_t)h * prm.tiles_ub + tile_idx];
-    n_chunks = (prm.union_ngroups[(size_t)h * prm.tiles_ub + tile_idx] + kDqGroups - 1) / kDqGroups;
-  } else {
-    n_chunks = tile.kv_hi > tile.kv_lo ? (tile.kv_hi - tile.kv_lo + kDqChunk - 1) / kDqChunk : 0;
-  }
+  struct Item {
+    QTile tile;
+    int tile_idx, h, n_chunks, U;
+    size_t ubase;
+  };
+  auto item_of = [&](int i) {
+    Item it;
+    it.tile_idx = i / prm.hkv;
+    it.h = i - it.tile_idx * prm.hkv;
+    it.tile = prm.tiles[it.tile_idx];
+    it.U = 0;
+    it.ubase = 0;
+    if constexpr (MODE == kSelect) {
+      const size_t th = (size_t)it.h * prm.tiles_ub + it.tile_idx;
+      it.ubase = th * prm.union_cap;
+      it.U = prm.union_cnt[th];
+      it.n_chunks = (prm.union_ngroups[th] + kDqGroups - 1) / kDqGroups;
+    } else {
+      it.n_chunks = it.tile.kv_hi > it.tile.kv_lo ? (it.tile.kv_hi - it.tile.kv_lo + kDqChunk - 1) / kDqChunk : 0;
+    }
+    return it;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(qdo_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
       mbar_init(&sd_full[i], 1);
       mbar_init(&sd_free[i], 8);
       mbar_init(&ds_full[i], 8);
       mbar_init(&ds_free[i], 1);
     }
     mbar_init(dq_done, 1);
+    mbar_init(dq_free, 8);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -205,70 +224,80 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tma_prefetch_desc(&kv.k[lane]);
       tma_prefetch_desc(&kv.v[lane]);
     }
-    if (lane == 0) {
-      mbar_arrive_expect_tx(qdo_full, 2 * L::QTILE);
-      tma_load_3d(sQ, &tm_q, 0, h * G, tile.q_start, qdo_full);
-      tma_load_3d(sDO, &tm_do, 0, h * G, tile.q_start, qdo_full);
-    }
     UnionCache& uc = *reinterpret_cast<UnionCache*>(smem + L::OFF_UC);
-    bool cached = false;
-    if constexpr (MODE == kSelect)
-      cached = union_cache_fill(uc, U, prm.union_blk, prm.union_mask, ubase, prm.cu_block_include_tokens, tile.kv_lo,
-                                tile.kv_hi);
-    if (cached) {
-      int issued = 0, ucur = 0;
-      for (int j = 0; j < n_chunks; ++j) {
-        const int s = j % STAGES;
-        if (!warp_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-        DqMeta& mt = meta[s];
-        const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-        __syncwarp();
-        issue_group_runs<kDqGroups, RB>(r, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
-                                        &kv_full[s]);
-        issued = j + 1;
+    int J = 0, issued = 0, it_n = 0, q_loads = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
+      const Item w = item_of(i);
+      const QTile& tile = w.tile;
+      const int h = w.h, qb = it_n & 1;
+      if (!warp_wait(&qdo_empty[qb], ((it_n >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&qdo_full[qb], 2 * L::QTILE);
+        tma_load_3d(sQ + qb * L::QTILE, &tm_q, 0, h * G, tile.q_start, &qdo_full[qb]);
+        tma_load_3d(sDO + qb * L::QTILE, &tm_do, 0, h * G, tile.q_start, &qdo_full[qb]);
       }
-      if (lane == 0 && *abort_flag) {
-        mbar_wait_drain(qdo_full, 0);
-        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
-      }
-    } else if (lane == 0) {
-      int u = -1, tcur = 0, tend = 0, issued = 0;
-      for (int j = 0; j < n_chunks; ++j) {
-        const int s = j % STAGES;
-        if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-        DqMeta& mt = meta[s];
-        uint8_t* dK = sK + s * L::KTILE;
-        uint8_t* dV = sV + s * L::KTILE;
-        if constexpr (MODE == kSelect) {
-          walk_union_groups<kDqGroups>(u, tcur, tend, U, prm.union_blk, prm.union_mask, ubase,
-                                       prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
-                                       mt.colmask);
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-          load_group_runs<kDqGroups, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
-        } else {
-          const int k0 = tile.kv_lo + j * kDqChunk;
-          mt.kv_start = k0;
-          mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-          tma_load_3d(dK, &kv.k[3], 0, h, k0, &kv_full[s]);  // 64-row box
-          tma_load_3d(dV, &kv.v[3], 0, h, k0, &kv_full[s]);
+      q_loads = it_n + 1;
+      bool cached = false;
+      if constexpr (MODE == kSelect)
+        cached = union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens,
+                                  tile.kv_lo, tile.kv_hi);
+      if (cached) {
+        int ucur = 0;
+        for (int j = 0; j < w.n_chunks; ++j, ++J) {
+          const int s = J % STAGES;
+          if (!warp_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          DqMeta& mt = meta[s];
+          const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+          __syncwarp();
+          issue_group_runs<kDqGroups, RB>(r, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
+                                          &kv_full[s]);
+          issued = J + 1;
         }
-        issued = j + 1;
+      } else {
+        if (lane == 0) {
+          int u = -1, tcur = 0, tend = 0;
+          for (int j = 0; j < w.n_chunks; ++j, ++J) {
+            const int s = J % STAGES;
+            if (!mbar_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+            DqMeta& mt = meta[s];
+            uint8_t* dK = sK + s * L::KTILE;
+            uint8_t* dV = sV + s * L::KTILE;
+            if constexpr (MODE == kSelect) {
+              walk_union_groups<kDqGroups>(u, tcur, tend, w.U, prm.union_blk, prm.union_mask, w.ubase,
+                                           prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
+                                           mt.colmask);
+              mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+              load_group_runs<kDqGroups, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
+            } else {
+              const int k0 = tile.kv_lo + j * kDqChunk;
+              mt.kv_start = k0;
+              mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
+              mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+              tma_load_3d(dK, &kv.k[3], 0, h, k0, &kv_full[s]);  // 64-row box
+              tma_load_3d(dV, &kv.v[3], 0, h, k0, &kv_full[s]);
+            }
+            issued = J + 1;
+          }
+        }
+        J = __shfl_sync(0xffffffffu, J, 0);
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+        ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
       }
-      if (*abort_flag) {
-        mbar_wait_drain(qdo_full, 0);
-        for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
-      }
+    }
+    if (lane == 0 && *abort_flag) {
+      for (int k = max(0, q_loads - 2); k < q_loads; ++k) mbar_wait_drain(&qdo_full[k & 1], (k >> 1) & 1);
+      for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
     }
     __syncwarp();
   } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc(AB, 0, 0, 128, kDqChunk);
       const uint32_t idesc_dq = make_idesc(AB, 0, 1, 128, D);
-      bool ok = mbar_wait(qdo_full, 0, abort_flag, prm.err);
-      auto issue_dq = [&](int i) -> bool {
+      // dQ(i) += dS(i) K(i); `first` starts the item's accumulator
+      auto issue_dq = [&](int i, bool first) -> bool {
         const int pb = i & 1, s = i % STAGES;
         if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
         tc_fence_after();
@@ -278,19 +307,30 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         for (int ks = 0; ks < kDqChunk / 16; ++ks) {
           const uint64_t da = make_sdesc(a_base + ks * 32, 16, 1024, kSw128);
           const uint64_t db = make_sdesc(k_base + ks * 16 * RB, L::KTILE, 8 * RB, SWZ);
-          umma_f16(tm_dq, da, db, idesc_dq, (i > 0 || ks > 0) ? 1u : 0u);
+          umma_f16(tm_dq, da, db, idesc_dq, (!first || ks > 0) ? 1u : 0u);
         }
         umma_commit(&ds_free[pb]);
         umma_commit(&kv_empty[s]);
         return true;
       };
-      if (ok) {
-        for (int j = 0; j < n_chunks && ok; ++j) {
-          const int s = j % STAGES, sb = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
-          if (!mbar_wait(&sd_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      bool ok = true;
+      int J = 0, it_n = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
+        const int n_chunks = item_of(i).n_chunks, qb = it_n & 1;
+        if (!mbar_wait(&qdo_full[qb], (it_n >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+        // the previous item's dQ accumulator must have been read out before this item's first dQ product
+        bool waited_free = false;
+        auto wait_free = [&]() -> bool {
+          if (waited_free) return true;
+          waited_free = true;
+          return mbar_wait(dq_free, (it_n & 1) ^ 1, abort_flag, prm.err);
+        };
+        const uint32_t q_base = smem_u32(sQ + qb * L::QTILE), do_base = smem_u32(sDO + qb * L::QTILE);
+        for (int j = 0; j < n_chunks; ++j, ++J) {
+          const int s = J % STAGES, sb = J & 1;
+          if (!mbar_wait(&kv_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&sd_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
           const uint32_t k_base = smem_u32(sK + s * L::KTILE), v_base = smem_u32(sV + s * L::KTILE);
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
@@ -303,11 +343,17 @@ __global__ void __launch_bounds__(kDqThreads, 1)
                      make_sdesc(v_base + ks * 32, 16, 8 * RB, SWZ), idesc_s, ks > 0);
           }
           umma_commit(&sd_full[sb]);
-          if (j >= 1 && !issue_dq(j - 1)) { ok = false; break; }
+          if (j >= 1) {
+            if (j == 1 && !wait_free()) { ok = false; break; }
+            if (!issue_dq(J - 1, j == 1)) { ok = false; break; }
+          }
         }
-        if (ok && n_chunks > 0) issue_dq(n_chunks - 1);
+        if (!ok) break;
+        umma_commit(&qdo_empty[qb]);  // Q / dO tiles free once the item's S and dP products are done
+        if (!wait_free()) { ok = false; break; }
+        if (n_chunks > 0 && !issue_dq(J - 1, n_chunks == 1)) { ok = false; break; }
+        umma_commit(dq_done);  // one completion per item
       }
-      umma_commit(dq_done);
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
     }
@@ -317,11 +363,17 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const int qloc = r / G;
-    const int hq = h * G + (r % G);
-    const int qi = tile.q_start + qloc;
-    const bool row_valid = qloc < tile.n_q;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2, scale = prm.scale;
+    bool ok = true;
+    int J = 0, it_n = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++it_n) {
+    const Item w = item_of(it);
+    const QTile& tile = w.tile;
+    const int n_chunks = w.n_chunks;
+    const int hq = w.h * G + (r % G);
+    const int qi = tile.q_start + qloc;
+    const bool row_valid = qloc < tile.n_q;
     float lse2 = 0.f, delta = 0.f;
     if (row_valid) {
       lse2 = prm.lse[(size_t)hq * prm.total_q + qi];
@@ -339,20 +391,19 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       }
       if (half == 0) prm.delta[(size_t)hq * prm.total_q + qi] = delta;
     }
-    bool ok = true;
-    for (int j = 0; j < n_chunks; ++j) {
-      const int s = j % STAGES, sb = j & 1;
-      if (!warp_wait(&sd_full[sb], (j >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!warp_wait(&kv_full[s], (j / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+    for (int j = 0; j < n_chunks; ++j, ++J) {
+      const int s = J % STAGES, sb = J & 1;
+      if (!warp_wait(&sd_full[sb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&kv_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       const DqMeta& mt = meta[s];
       uint32_t vm;  // valid columns of this warp's 32-column slice
       if constexpr (MODE == kSelect) {
-        const int w = qloc >> 5, b = qloc & 31;
+        const int wq = qloc >> 5, b = qloc & 31;
         uint32_t e = 0u;
 #pragma unroll
         for (int y = 0; y < 4; ++y)
-          if ((mt.qmask[half * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
+          if ((mt.qmask[half * 4 + y][wq] >> b) & 1u) e |= 0xffu << (y * 8);
         vm = e & mt.colmask[half];
       } else {
         int lo = 0, hi = mt.n_valid;
@@ -386,7 +437,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
         }
       }
-      if (!warp_wait(&ds_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&ds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
 #pragma unroll
       for (int q8 = 0; q8 < 4; ++q8) {
@@ -399,11 +450,12 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[sb]);
     }
-    // warps of half 0 write dQ; every lane of such a warp takes part in the
-    // warp-collective TMEM load, only valid rows store
-    bool have = ok;
-    if (ok && n_chunks > 0) have = warp_wait(dq_done, 0, abort_flag, prm.err);
-    if (have && half == 0) {
+    if (!ok) break;
+    // warps of half 0 write dQ (every lane takes part in the warp-collective
+    // TMEM load, only valid rows store); then all eight warps release the
+    // accumulator for the next item
+    if (!warp_wait(dq_done, it_n & 1, abort_flag, prm.err)) { ok = false; break; }
+    if (half == 0) {
       tc_fence_after();
       uint8_t* drow = static_cast<uint8_t*>(prm.dq) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D) * 2;
       float v[D];
@@ -426,6 +478,10 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         }
       }
     }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(dq_free);
+    }  // items
   }
 
   tc_fence_before();
@@ -463,7 +519,8 @@ struct DkvParams {
   void* dv;
   float* partial;  // [split][hkv][kvtiles_ub][128][D] x 2 when n_split > 1
   int n_split;
-  const int* kv_sched;  // select mode: work items (h * kvtiles_ub + tile) in launch order; grid is 1-D
+  const int* kv_sched;  // select mode: work items (h * kvtiles_ub + tile), heaviest first
+  const int* item_nch;  // select mode: query chunks of each work item
   long long kv_tok_stride;
   int total_q;
   int G;
@@ -487,8 +544,8 @@ struct KvMeta {
 // The reverse map of one KV block in shared memory: the (query tile, union
 // slot) entries that selected it, as the tile's first query token, the
 // 128-bit mask of its queries and the exclusive prefix of the masks' bit
-// counts, so the queries of any chunk are found without a sequential walk.
-constexpr int kRevCacheCap = 1024;
+// counts, so the queries of any chunk are found without a sequential walk
+// (capacity kRevCacheCap entries).
 
 struct RevCache {
   int tq0[kRevCacheCap];
@@ -502,15 +559,6 @@ struct RevCache {
   int pad;
 };
 
-// Query groups (G <= 8): a tile's 128 MMA rows are 16 windows of 8 rows,
-// window w = queries [w*W, w*W + W) of the tile, W = 8/G.  A group is one
-// non-empty window of one reverse-map entry; its bits say which of its W
-// queries selected the block.
-__device__ __forceinline__ uint32_t window_bits(const uint4& m, int w, int W) {
-  const int o = w * W;
-  const uint32_t word = (o >> 5) == 0 ? m.x : (o >> 5) == 1 ? m.y : (o >> 5) == 2 ? m.z : m.w;
-  return (word >> (o & 31)) & ((1u << W) - 1u);
-}
 
 // Position of the n-th (0-based) set bit of `word` (n < popc(word)).
 __device__ __forceinline__ int nth_set_bit(uint32_t word, int n) {
@@ -598,10 +646,7 @@ __device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& pr
       rc.mask[i] = m;
       cnt = __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
       if (prm.G <= 8) {
-        const int W = 8 / prm.G;
-        uint32_t wm = 0u;
-#pragma unroll
-        for (int w = 0; w < 16; ++w) wm |= (window_bits(m, w, W) != 0u ? 1u : 0u) << w;
+        const uint32_t wm = window_mask(m, 8 / prm.G);
         rc.wmask[i] = (int)wm;
         gcnt = __popc(wm);
       }

@@ -396,6 +396,7 @@ SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int 
   p.rev_entries = reinterpret_cast<int2*>(take(sizeof(int2) * ent));
   p.kv_sched = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
   p.sched_key = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
+  p.item_nch = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
   p.sched_bins = reinterpret_cast<int*>(take(sizeof(int) * 2 * kSchedBins));
   p.bytes = (size_t)(cur - base);
   return p;
@@ -462,26 +463,34 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
 // items are listed heaviest bucket first, so the longest CTAs start early
 // instead of trailing the launch.  Order inside a bucket is arbitrary; it
 // does not change any result.
-__global__ void sched_key_kernel(SelectPlan p, int qpc) {
+// The chunk count follows the dK/dV kernel's rule: a block whose reverse
+// list fits the shared-memory cache and G <= 8 runs in 8-row query groups
+// (chunks of 8 groups), otherwise in chunks of 64/G gathered queries.
+__global__ void sched_key_kernel(SelectPlan p, int G) {
   const int items = p.hkv * p.kvtiles_ub;
   const int n_kv = *p.n_kvtiles;
+  const int qpc = 64 / G, W = G <= 8 ? 8 / G : 1;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
     const int h = i / p.kvtiles_ub, kt = i - h * p.kvtiles_ub;
     int bin = kSchedBins - 1;  // empty / unused items last
+    int chunks = 0;
     if (kt < n_kv) {
       const int blk = p.kvtiles[kt].seg;
       const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
       const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
-      int nq = 0;
+      const bool grouped = off[blk + 1] - off[blk] <= kRevCacheCap && G <= 8;
+      int nq = 0, ng = 0;
       for (int e = off[blk]; e < off[blk + 1]; ++e) {
         const int2 x = ent[e];
         const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
         nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+        if (grouped) ng += __popc(window_mask(m, W));
       }
-      const int chunks = (nq + qpc - 1) / qpc;
+      chunks = grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
       bin = kSchedBins - 1 - min(chunks, kSchedBins - 1);
     }
     p.sched_key[i] = bin;
+    p.item_nch[i] = chunks;
     atomicAdd(&p.sched_bins[bin], 1);
   }
 }
@@ -521,12 +530,12 @@ __global__ void sched_scatter_kernel(SelectPlan p) {
   }
 }
 
-int launch_build_kv_schedule(const SelectPlan& p, int qpc, cudaStream_t s) {
+int launch_build_kv_schedule(const SelectPlan& p, int G, cudaStream_t s) {
   ProfScope ps("plan_schedule", s);
   LSRM_CUDA_TRY(cudaMemsetAsync(p.sched_bins, 0, sizeof(int) * kSchedBins, s));
   const int items = p.hkv * p.kvtiles_ub;
   const int grid = std::min((items + 255) / 256, 148 * 8);
-  sched_key_kernel<<<grid, 256, 0, s>>>(p, qpc);
+  sched_key_kernel<<<grid, 256, 0, s>>>(p, G);
   LSRM_LAUNCH_CHECK();
   sched_scan_kernel<<<1, kSchedBins, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();

@@ -70,12 +70,33 @@ struct SelectPlan {
   int* rev_cursor;         // [hkv][num_blocks]
   int2* rev_entries;       // [hkv][tiles_ub*cap] (tile, union entry index)
   int* kv_sched;           // [hkv*kvtiles_ub] dK/dV work items (h*kvtiles_ub + tile), heaviest first
+  int* item_nch;           // [hkv*kvtiles_ub] query chunks of each dK/dV work item
   int* sched_key;          // [hkv*kvtiles_ub] bucket of each item
   int* sched_bins;         // [2*kSchedBins] bucket counts, then cursors
   size_t bytes;
 };
 
 constexpr int kSchedBins = 1024;  // dK/dV schedule buckets (query chunks, capped)
+
+// dK/dV reverse-map cache capacity (entries of one block kept in shared memory)
+constexpr int kRevCacheCap = 1024;
+
+// Query groups (G <= 8): a tile's 128 MMA rows are 16 windows of 8 rows,
+// window w = queries [w*W, w*W + W) of the tile, W = 8/G.  A group is one
+// non-empty window of one reverse-map entry; its bits say which of its W
+// queries selected the block.
+__device__ __forceinline__ uint32_t window_bits(const uint4& m, int w, int W) {
+  const int o = w * W;
+  const uint32_t word = (o >> 5) == 0 ? m.x : (o >> 5) == 1 ? m.y : (o >> 5) == 2 ? m.z : m.w;
+  return (word >> (o & 31)) & ((1u << W) - 1u);
+}
+
+__device__ __forceinline__ uint32_t window_mask(const uint4& m, int W) {
+  uint32_t wm = 0u;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) wm |= (window_bits(m, w, W) != 0u ? 1u : 0u) << w;
+  return wm;
+}
 
 struct DensePlan {
   int tiles_ub;
@@ -97,6 +118,6 @@ int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int r
 int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t* block_topk, int topk,
                         int sel_rows, int G, int* err, cudaStream_t s);
 int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s);
-int launch_build_kv_schedule(const SelectPlan& p, int qpc, cudaStream_t s);
+int launch_build_kv_schedule(const SelectPlan& p, int G, cudaStream_t s);
 
 }  // namespace lsrm
