@@ -77,8 +77,12 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
   {
     ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
-    const dim3 grid = p.kv_sched ? dim3(grid_x * hkv, 1) : dim3(grid_x * p.n_split, hkv);
-    kern<<<grid, kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, qm, p);
+    // persistent: one CTA per SM walks the work items
+    DkvParams pp = p;
+    pp.hkv = hkv;
+    const long long items = (long long)grid_x * hkv * (p.kv_sched ? 1 : p.n_split);
+    const int grid = (int)std::min<long long>(items, num_sms());
+    kern<<<dim3(grid, 1), kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, qm, pp);
     LSRM_LAUNCH_CHECK();
   }
   if (p.n_split > 1) {

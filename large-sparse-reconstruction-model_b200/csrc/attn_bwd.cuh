@@ -592,8 +592,9 @@ struct DkvSmem {
   static constexpr int OFF_DST = OFF_PT + 2 * PT_BYTES;
   static constexpr int OFF_META = OFF_DST + 2 * PT_BYTES;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(KvMeta);
-  // kv_full, q_full[S], q_empty[S], st_full[2], st_free[2], pds_full[2], pds_free[2], acc_done, mma_done
-  static constexpr int NBAR = 1 + 2 * STAGES + 8 + 2;
+  // kv_full, kv_empty, q_full[S], q_empty[S], st_full[2], st_free[2], pds_full[2], pds_free[2],
+  // acc_done, acc_free, mma_done, rc_empty, rc_full
+  static constexpr int NBAR = 2 + 2 * STAGES + 8 + 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_RC = (OFF_MISC + 32 + 15) / 16 * 16;  // select mode: the block's reverse map
   static constexpr int BYTES = OFF_RC + (int)sizeof(RevCache);
@@ -601,21 +602,6 @@ struct DkvSmem {
   static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
-// Number of query rows (queries x G) gathered for one KV tile (select mode).
-__device__ __forceinline__ int count_select_queries(const DkvParams& prm, int h, int blk) {
-  const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
-  const int e0 = off[blk], e1 = off[blk + 1];
-  const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
-  int n = 0;
-  for (int e = e0 + (threadIdx.x & 31); e < e1; e += 32) {
-    const int2 x = ent[e];
-    const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-    n += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-  return n;
-}
 
 // Threads of the dK/dV kernel: 8 compute warps (two per TMEM lane quarter,
 // splitting the 64 query columns of a chunk), a producer warp, an MMA warp.
@@ -739,20 +725,16 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   constexpr uint64_t SWZ = swz_for_row_bytes(RB);
   constexpr uint32_t AB = BF16 ? 1u : 0u;
 
-  int split = 0, kt_idx, h;
-  if (prm.kv_sched) {
-    const int item = prm.kv_sched[blockIdx.x];
-    h = item / prm.kvtiles_ub;
-    kt_idx = item - h * prm.kvtiles_ub;
-  } else {
-    split = blockIdx.x % prm.n_split;
-    kt_idx = blockIdx.x / prm.n_split;
-    h = blockIdx.y;
-  }
-  if (kt_idx >= *prm.n_kvtiles) return;
-  const QTile kt = prm.kvtiles[kt_idx];  // rows = keys [q_start, q_start + n_q)
+  // Persistent CTAs walk the work items: select mode the heaviest-first
+  // schedule (kv head, KV tile); dense modes (kv head, KV tile, query
+  // split).  Every role decodes the same items in the same order; per-chunk
+  // ring phases run on across items and the K/V tile, the reverse-map cache
+  // and the dK/dV accumulators are handed from item to item by barriers, so
+  // the next item's loads overlap the current item's tail.
   const int G = prm.G;
-  const int qpc = kKvQRows / G;  // queries per chunk
+  const int qpc = kKvQRows / G;  // queries per chunk (gather path)
+  const int n_items = prm.kv_sched ? prm.hkv * prm.kvtiles_ub : prm.hkv * prm.kvtiles_ub * prm.n_split;
+  const int n_kv = *prm.n_kvtiles;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -765,45 +747,76 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   KvMeta* meta = reinterpret_cast<KvMeta*>(smem + L::OFF_META);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* q_full = bars + 2;
   uint64_t* q_empty = q_full + STAGES;
   uint64_t* st_full = q_empty + STAGES;
   uint64_t* st_free = st_full + 2;
   uint64_t* pds_full = st_free + 2;
   uint64_t* pds_free = pds_full + 2;
   uint64_t* acc_done = pds_free + 2;
-  uint64_t* mma_done = acc_done + 1;
+  uint64_t* acc_free = acc_done + 1;
+  uint64_t* mma_done = acc_free + 1;
+  uint64_t* rc_empty = mma_done + 1;  // both producer warps are done with the cache (count 2)
+  uint64_t* rc_full = rc_empty + 1;   // warp 8 has filled it for the next item (count 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  int* s_nchunks = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // query range of this split (dense modes) / number of gathered queries (select)
-  int q_lo = kt.kv_lo, q_hi = kt.kv_hi;
-  if constexpr (MODE != kSelect) {
-    const int nq = max(q_hi - q_lo, 0);
-    const int per = ((nq + prm.n_split - 1) / prm.n_split + qpc - 1) / qpc * qpc;
-    q_lo = min(kt.kv_lo + split * per, kt.kv_hi);
-    q_hi = min(q_lo + per, kt.kv_hi);
-  }
-  RevCache& rc = *reinterpret_cast<RevCache*>(smem + L::OFF_RC);
-  if (warp == kDkvProducerWarp) {
-    int nqueries;
-    int nch;
-    if constexpr (MODE == kSelect) {
-      rev_cache_fill(rc, prm, h, kt.seg);
-      nqueries = rc.n >= 0 ? rc.total : count_select_queries(prm, h, kt.seg);
-      nch = (rc.n >= 0 && G <= 8) ? (rc.groups + 7) / 8 : (nqueries + qpc - 1) / qpc;
+  struct KvItem {
+    QTile kt;
+    int kt_idx, h, split, n_chunks, q_lo, q_hi;
+    bool skip, cached;  // cached: the block's reverse list fits the shared-memory cache
+  };
+  auto item_of = [&](int i) {
+    KvItem it;
+    it.split = 0;
+    if (prm.kv_sched) {
+      const int e = prm.kv_sched[i];
+      it.h = e / prm.kvtiles_ub;
+      it.kt_idx = e - it.h * prm.kvtiles_ub;
     } else {
-      nqueries = max(q_hi - q_lo, 0);
-      nch = (nqueries + qpc - 1) / qpc;
-      if (lane == 0) rc.n = -1;
+      const int per_h = prm.kvtiles_ub * prm.n_split;
+      it.h = i / per_h;
+      const int rem = i - it.h * per_h;
+      it.kt_idx = rem / prm.n_split;
+      it.split = rem - it.kt_idx * prm.n_split;
     }
-    if (lane == 0) *s_nchunks = nch;
-  }
+    it.skip = it.kt_idx >= n_kv;
+    it.n_chunks = 0;
+    it.cached = false;
+    it.q_lo = it.q_hi = 0;
+    if (it.skip) return it;
+    it.kt = prm.kvtiles[it.kt_idx];  // rows = keys [q_start, q_start + n_q)
+    it.q_lo = it.kt.kv_lo;
+    it.q_hi = it.kt.kv_hi;
+    if constexpr (MODE == kSelect) {
+      const int* off = prm.rev_off + (size_t)it.h * (prm.num_blocks + 1);
+      it.cached = off[it.kt.seg + 1] - off[it.kt.seg] <= kRevCacheCap;
+      it.n_chunks = prm.item_nch[(size_t)it.h * prm.kvtiles_ub + it.kt_idx];
+    } else {
+      const int nq = max(it.q_hi - it.q_lo, 0);
+      const int per = ((nq + prm.n_split - 1) / prm.n_split + qpc - 1) / qpc * qpc;
+      it.q_lo = min(it.kt.kv_lo + it.split * per, it.kt.kv_hi);
+      it.q_hi = min(it.q_lo + per, it.kt.kv_hi);
+      it.n_chunks = (max(it.q_hi - it.q_lo, 0) + qpc - 1) / qpc;
+    }
+    return it;
+  };
+
+  // round k of the walk: items in snake order (k odd: reversed), so a CTA
+  // that drew a heavy item of the heaviest-first list draws a light one next
+  // (select mode; the dense modes' items are uniform and walk in order)
+  auto item_at = [&](int k) {
+    const bool rev = prm.kv_sched && (k & 1);
+    return k * (int)gridDim.x + (rev ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  };
+
+  RevCache& rc = *reinterpret_cast<RevCache*>(smem + L::OFF_RC);
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
@@ -815,7 +828,10 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       mbar_init(&pds_free[i], 1);
     }
     mbar_init(acc_done, 1);
+    mbar_init(acc_free, 8);
     mbar_init(mma_done, 1);
+    mbar_init(rc_empty, 2);
+    mbar_init(rc_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -827,39 +843,67 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_chunks = *s_nchunks;
   const int lg_g = __ffs(G) - 1;  // G is a power of two
   // TMEM: St0 [0,64) St1 [64,128) dPt0 [128,192) dPt1 [192,256) dK [256,256+D) dV [256+D, 256+2D)
   const uint32_t tm_st0 = tmem, tm_dpt0 = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 256 + D;
 
   if (warp == kDkvProducerWarp || warp == kDkvProducer2Warp) {
     // ------------------------------ producers -----------------------------
-    // K/V tile by TMA; query rows gathered with 16-byte cp.async by all 32
-    // lanes (any row pattern at full LSU rate), lse/delta with 4-byte
-    // cp.async.  Two warps take alternate chunks (in select mode each
-    // chunk's queries come straight from the cached reverse map) and publish
-    // a chunk as soon as its copies have landed (wait_group, generic->async
-    // proxy fence, arrive).  When the map did not fit in shared memory,
-    // warp 8 alone walks it and publishes two chunks behind.
-    const bool cached = MODE == kSelect && rc.n >= 0;
-    const int nprod = (MODE == kSelect && !cached) ? 1 : 2;  // the sequential walk needs one warp
+    // Per item: warp 8 fills the reverse-map cache (both producer warps
+    // meet at a named barrier before and after, the cache being shared) and
+    // loads the K/V tile once the previous item's S^T / dP^T products are
+    // done.  Query rows: select mode with the cache and G <= 8 in 8-row
+    // windows by TMA (grouped); other select cases gathered with 16-byte
+    // cp.async (from the cache, or by a sequential walk of the map by warp
+    // 8 alone); dense modes one TMA box per operand.  The two warps take
+    // alternate chunks and publish a chunk as soon as its copies have
+    // landed; the lone walking warp publishes two chunks behind.
     const int pw = warp == kDkvProducerWarp ? 0 : 1;
-    if (pw < nprod) {
-      if (MODE == kSelect && lane < 4) {
-        tma_prefetch_desc(&qm.q[lane]);
-        tma_prefetch_desc(&qm.dout[lane]);
+    if (MODE == kSelect && lane < 4) {
+      tma_prefetch_desc(&qm.q[lane]);
+      tma_prefetch_desc(&qm.dout[lane]);
+    }
+    constexpr int CPR = RB / 16;  // 16-byte chunks per row
+    const uint8_t* qbase = static_cast<const uint8_t*>(prm.q);
+    const uint8_t* dobase = static_cast<const uint8_t*>(prm.dout);
+    const int W = G <= 8 ? 8 / G : 1;  // queries per 8-row window
+    int Jbase = 0, it_n = 0, kv_loads = 0, cache_uses = 0;
+    int last_issued_J = -1;             // this warp's last issued chunk (global index), for teardown
+    bool ok = true;
+    for (int rnd = 0, i = item_at(0); i < n_items && ok; i = item_at(++rnd)) {
+      const KvItem w = item_of(i);
+      if (w.skip) continue;
+      const int h = w.h;
+      const QTile& kt = w.kt;
+      const bool cached = MODE == kSelect && w.cached;
+      const bool grouped = cached && G <= 8;
+      const int nprod = (MODE == kSelect && !cached) ? 1 : 2;  // the sequential walk needs one warp
+      if constexpr (MODE == kSelect) {
+        if (cached) {
+          // hand the cache over: both warps release it, warp 8 refills it
+          const uint32_t par = cache_uses & 1;
+          ++cache_uses;
+          if (lane == 0) mbar_arrive(rc_empty);
+          if (pw == 0) {
+            if (!warp_wait(rc_empty, par, abort_flag, prm.err)) { ok = false; break; }
+            rev_cache_fill(rc, prm, h, kt.seg);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rc_full);
+          } else {
+            if (!warp_wait(rc_full, par, abort_flag, prm.err)) { ok = false; break; }
+          }
+        }
       }
-      if (pw == 0 && lane == 0) {
-        mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
-        tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
-        tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+      if (pw == 0) {
+        if (!warp_wait(kv_empty, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+          tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
+          tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+        }
+        kv_loads = it_n + 1;
       }
-      constexpr int CPR = RB / 16;  // 16-byte chunks per row
-      // two warps: publish each chunk as soon as its copies land (the other
-      // warp keeps the pipe busy meanwhile); one warp: publish LAG chunks later
       const int LAG = nprod == 2 ? 0 : STAGES - 2;
-      const uint8_t* qbase = static_cast<const uint8_t*>(prm.q);
-      const uint8_t* dobase = static_cast<const uint8_t*>(prm.dout);
       const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
       const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
       int e = 0, e_end = 0, tq0 = 0;
@@ -871,59 +915,147 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       auto publish = [&](int cc) {
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&q_full[cc % STAGES]);
+        if (lane == 0) mbar_arrive(&q_full[(Jbase + cc) % STAGES]);
       };
-      int issued = 0, published = 0;  // in this warp's own chunk sequence
+      int issued = 0, published = 0;  // in this warp's own chunk sequence of this item
       int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
       int gcur = 0;                   // group cursor (grouped path)
-      const bool grouped = cached && G <= 8;
-      const int W = G <= 8 ? 8 / G : 1;  // queries per 8-row window
-      for (int c = pw; c < n_chunks; c += nprod) {
-        const int s = c % STAGES;
-        if (!warp_wait(&q_empty[s], ((c / STAGES) & 1) ^ 1, abort_flag, prm.err)) break;
-        KvMeta& mt = meta[s];
-        if (grouped) {
-          // 8 groups of 8 rows: lane g < 8 finds its group's window; each
-          // group lands by TMA at an 8-row boundary (boxes of whole windows,
-          // merged when adjacent); rows whose query did not select the block
-          // get lse = +inf, so their P and dS are exactly zero
-          int tok = -1;
-          uint32_t bits = 0u;
-          if (lane < 8) {
-            const int gg = 8 * c + lane;
-            if (gg < rc.groups) {
-              int lo = gcur;
-              while (lo + 1 < rc.n && rc.gstart[lo + 1] <= gg) ++lo;
-              gcur = lo;
-              const int w = nth_set_bit((uint32_t)rc.wmask[lo], gg - rc.gstart[lo]);
-              tok = rc.tq0[lo] + w * W;
-              bits = window_bits(rc.mask[lo], w, W);
+      const int n_chunks = w.n_chunks;
+      if (pw < nprod) {
+        for (int c = pw; c < n_chunks; c += nprod) {
+          const int J = Jbase + c;
+          const int s = J % STAGES;
+          if (!warp_wait(&q_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          last_issued_J = J;
+          KvMeta& mt = meta[s];
+          if (grouped) {
+            // 8 groups of 8 rows: lane g < 8 finds its group's window; each
+            // group lands by TMA at an 8-row boundary (boxes of whole windows,
+            // merged when adjacent); rows whose query did not select the block
+            // get lse = +inf, so their P and dS are exactly zero
+            int tok = -1;
+            uint32_t bits = 0u;
+            if (lane < 8) {
+              const int gg = 8 * c + lane;
+              if (gg < rc.groups) {
+                int lo = gcur;
+                while (lo + 1 < rc.n && rc.gstart[lo + 1] <= gg) ++lo;
+                gcur = lo;
+                const int wdx = nth_set_bit((uint32_t)rc.wmask[lo], gg - rc.gstart[lo]);
+                tok = rc.tq0[lo] + wdx * W;
+                bits = window_bits(rc.mask[lo], wdx, W);
+              }
             }
-          }
 #pragma unroll
-          for (int k = 0; k < kKvQRows / 32; ++k) {
-            const int row = lane + 32 * k, grp = row >> 3, rr = row & 7;
-            const int t = __shfl_sync(0xffffffffu, tok, grp);
-            const uint32_t bb = __shfl_sync(0xffffffffu, bits, grp);
-            const int qq = rr >> lg_g, g = rr & (G - 1);
-            const bool valid = t >= 0 && ((bb >> qq) & 1u);
-            mt.qidx[row] = valid ? t + qq : -1;
-            if (valid) {
-              const size_t si = (size_t)(h * G + g) * prm.total_q + (t + qq);
-              cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
-              cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+            for (int k = 0; k < kKvQRows / 32; ++k) {
+              const int row = lane + 32 * k, grp = row >> 3, rr = row & 7;
+              const int t = __shfl_sync(0xffffffffu, tok, grp);
+              const uint32_t bb = __shfl_sync(0xffffffffu, bits, grp);
+              const int qq = rr >> lg_g, g = rr & (G - 1);
+              const bool valid = t >= 0 && ((bb >> qq) & 1u);
+              mt.qidx[row] = valid ? t + qq : -1;
+              if (valid) {
+                const size_t si = (size_t)(h * G + g) * prm.total_q + (t + qq);
+                cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
+                cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+              } else {
+                mt.lse2[row] = INFINITY;
+                mt.delta[row] = 0.f;
+              }
+            }
+            if (lane == 0) {
+              mt.n_rows = kKvQRows;
+              mbar_expect_tx(&q_full[s], 2 * L::QTILE);
+            }
+            __syncwarp();
+            issue_group_runs<8, RB>(tok, sQ + s * L::QTILE, sDO + s * L::QTILE, qm.q, qm.dout, h * G, prm.total_q,
+                                    &q_full[s], W);
+          } else {
+            int n = 0;
+            if constexpr (MODE == kSelect) {
+              if (cached) {
+                n = rev_cache_chunk(rc, c, qpc, mt.qlist, rcur);
+              } else {
+                while (n < qpc) {
+                  if ((w0 | w1 | w2 | w3) == 0u) {
+                    if (e + 1 >= e_end) break;
+                    ++e;
+                    const int2 x = ent[e];
+                    const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
+                    w0 = m.x;
+                    w1 = m.y;
+                    w2 = m.z;
+                    w3 = m.w;
+                    tq0 = prm.qtiles[x.x].q_start;
+                    continue;
+                  }
+                  const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
+                  const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
+                  const bool bit = (word >> lane) & 1u;
+                  const int rank = __popc(word & ((1u << lane) - 1u));
+                  const bool take = bit && rank < qpc - n;
+                  if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
+                  const uint32_t taken = __ballot_sync(0xffffffffu, take);
+                  n += __popc(taken);
+                  if (wi == 0) w0 &= ~taken;
+                  else if (wi == 1) w1 &= ~taken;
+                  else if (wi == 2) w2 &= ~taken;
+                  else w3 &= ~taken;
+                }
+                for (int i2 = n + lane; i2 < qpc; i2 += 32) mt.qlist[i2] = -1;
+              }
             } else {
-              mt.lse2[row] = INFINITY;
-              mt.delta[row] = 0.f;
+              const int q0 = w.q_lo + c * qpc;
+              n = max(0, min(qpc, w.q_hi - q0));
+              for (int i2 = lane; i2 < qpc; i2 += 32) mt.qlist[i2] = i2 < n ? q0 + i2 : -1;
+            }
+            if (lane == 0) mt.n_rows = n * G;
+            __syncwarp();
+            for (int row = lane; row < kKvQRows; row += 32) {
+              const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
+              mt.qidx[row] = q;
+              if (q >= 0) {
+                const size_t si = (size_t)(h * G + g) * prm.total_q + q;
+                cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
+                cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
+              } else {
+                mt.lse2[row] = 0.f;
+                mt.delta[row] = 0.f;
+              }
+            }
+            __syncwarp();
+            const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
+            if constexpr (MODE != kSelect) {
+              // contiguous queries: one TMA box per operand; rows past the range are
+              // other tokens' data (finite, masked) or zero fill past the tensor
+              if (lane == 0) {
+                const int q0 = w.q_lo + c * qpc;
+                mbar_expect_tx(&q_full[s], 2 * L::QTILE);
+                tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
+                tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
+              }
+            } else {
+              // lane: 16-byte column j of rows r0, r0 + 32/CPR, ...; the head and
+              // column offsets are folded into the lane's base pointers
+              const int j = lane % CPR, r0 = lane / CPR;
+              const uint8_t* qb = qbase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
+              const uint8_t* db = dobase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
+              const size_t tok_bytes = (size_t)prm.q_tok_stride * 2;
+#pragma unroll
+              for (int row = r0; row < kKvQRows; row += 32 / CPR) {
+                const int q = mt.qidx[row];
+                const uint32_t o = swz_offset<RB>(row, j);
+                if (q >= 0) {
+                  const size_t off2 = (size_t)q * tok_bytes + (size_t)(row & (G - 1)) * (D * 2);
+                  cp_async_16(dq_s + o, qb + off2);
+                  cp_async_16(ddo_s + o, db + off2);
+                } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
+                  st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
+                  st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
+                }
+              }
             }
           }
-          if (lane == 0) {
-            mt.n_rows = kKvQRows;
-            mbar_expect_tx(&q_full[s], 2 * L::QTILE);
-          }
-          __syncwarp();
-          issue_group_runs<8, RB>(tok, sQ + s * L::QTILE, sDO + s * L::QTILE, qm.q, qm.dout, h * G, prm.total_q,
-                                  &q_full[s], W);
           cp_async_commit();
           ++issued;
           if (issued > LAG) {
@@ -932,104 +1064,16 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             publish(pw + nprod * published);
             ++published;
           }
-          continue;
         }
-        int n = 0;
-        if constexpr (MODE == kSelect) {
-          if (cached) {
-            n = rev_cache_chunk(rc, c, qpc, mt.qlist, rcur);
-          } else {
-            while (n < qpc) {
-              if ((w0 | w1 | w2 | w3) == 0u) {
-                if (e + 1 >= e_end) break;
-                ++e;
-                const int2 x = ent[e];
-                const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-                w0 = m.x;
-                w1 = m.y;
-                w2 = m.z;
-                w3 = m.w;
-                tq0 = prm.qtiles[x.x].q_start;
-                continue;
-              }
-              const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
-              const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
-              const bool bit = (word >> lane) & 1u;
-              const int rank = __popc(word & ((1u << lane) - 1u));
-              const bool take = bit && rank < qpc - n;
-              if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
-              const uint32_t taken = __ballot_sync(0xffffffffu, take);
-              n += __popc(taken);
-              if (wi == 0) w0 &= ~taken;
-              else if (wi == 1) w1 &= ~taken;
-              else if (wi == 2) w2 &= ~taken;
-              else w3 &= ~taken;
-            }
-            for (int i = n + lane; i < qpc; i += 32) mt.qlist[i] = -1;
-          }
-        } else {
-          const int q0 = q_lo + c * qpc;
-          n = max(0, min(qpc, q_hi - q0));
-          for (int i = lane; i < qpc; i += 32) mt.qlist[i] = i < n ? q0 + i : -1;
-        }
-        if (lane == 0) mt.n_rows = n * G;
-        __syncwarp();
-        for (int row = lane; row < kKvQRows; row += 32) {
-          const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
-          mt.qidx[row] = q;
-          if (q >= 0) {
-            const size_t si = (size_t)(h * G + g) * prm.total_q + q;
-            cp_async_4(smem_u32(&mt.lse2[row]), prm.lse + si);
-            cp_async_4(smem_u32(&mt.delta[row]), prm.delta + si);
-          } else {
-            mt.lse2[row] = 0.f;
-            mt.delta[row] = 0.f;
-          }
-        }
-        __syncwarp();
-        const uint32_t dq_s = smem_u32(sQ + s * L::QTILE), ddo_s = smem_u32(sDO + s * L::QTILE);
-        if constexpr (MODE != kSelect) {
-          // contiguous queries: one TMA box per operand; rows past the range are
-          // other tokens' data (finite, masked) or zero fill past the tensor
-          if (lane == 0) {
-            const int q0 = q_lo + c * qpc;
-            mbar_expect_tx(&q_full[s], 2 * L::QTILE);
-            tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
-            tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
-          }
-        } else {
-          // lane: 16-byte column j of rows r0, r0 + 32/CPR, ...; the head and
-          // column offsets are folded into the lane's base pointers
-          const int j = lane % CPR, r0 = lane / CPR;
-          const uint8_t* qb = qbase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
-          const uint8_t* db = dobase + ((size_t)h * G * D) * 2 + (size_t)j * 16;
-          const size_t tok_bytes = (size_t)prm.q_tok_stride * 2;
-#pragma unroll
-          for (int row = r0; row < kKvQRows; row += 32 / CPR) {
-            const int q = mt.qidx[row];
-            const uint32_t o = swz_offset<RB>(row, j);
-            if (q >= 0) {
-              const size_t off = (size_t)q * tok_bytes + (size_t)(row & (G - 1)) * (D * 2);
-              cp_async_16(dq_s + o, qb + off);
-              cp_async_16(ddo_s + o, db + off);
-            } else {  // padding rows: zeros, so P^T dO and dS^T Q add nothing
-              st_shared_v4(dq_s + o, 0u, 0u, 0u, 0u);
-              st_shared_v4(ddo_s + o, 0u, 0u, 0u, 0u);
-            }
-          }
-        }
-        cp_async_commit();
-        ++issued;
-        if (issued > LAG) {
-          if (LAG == 0) cp_async_wait<0>();
-          else cp_async_wait<STAGES - 2>();
-          publish(pw + nprod * published);
-          ++published;
-        }
+        cp_async_wait<0>();
+        for (; published < issued; ++published) publish(pw + nprod * published);
       }
-      cp_async_wait<0>();
-      for (; published < issued; ++published) publish(pw + nprod * published);
-      if (pw == 0 && lane == 0 && *abort_flag) mbar_wait_drain(kv_full, 0);
+      Jbase += n_chunks;
+      ++it_n;
+    }
+    if (lane == 0 && *abort_flag) {
+      if (pw == 0 && kv_loads > 0) mbar_wait_drain(kv_full, (kv_loads - 1) & 1);
+      if (last_issued_J >= 0) mbar_wait_drain(&q_full[last_issued_J % STAGES], (last_issued_J / STAGES) & 1);
     }
     __syncwarp();
   } else if (warp == kDkvMmaWarp) {
@@ -1037,8 +1081,8 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_st = make_idesc(AB, 0, 0, 128, kKvQRows);
       const uint32_t idesc_acc = make_idesc(AB, 0, 1, 128, D);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, prm.err);
-      auto issue_acc = [&](int i) -> bool {
+      // dV += P^T dO, dK += dS^T Q for chunk i; `first` starts the item's accumulators
+      auto issue_acc = [&](int i, bool first) -> bool {
         const int pb = i & 1, s = i % STAGES;
         if (!mbar_wait(&pds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
         tc_fence_after();
@@ -1047,22 +1091,36 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < kKvQRows / 16; ++ks) {
           umma_f16(tm_dv, make_sdesc(pt + ks * 32, 16, 1024, kSw128),
-                   make_sdesc(dob + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
+                   make_sdesc(dob + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (!first || ks > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int ks = 0; ks < kKvQRows / 16; ++ks) {
           umma_f16(tm_dk, make_sdesc(dst + ks * 32, 16, 1024, kSw128),
-                   make_sdesc(qb + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
+                   make_sdesc(qb + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (!first || ks > 0) ? 1u : 0u);
         }
         umma_commit(&pds_free[pb]);
         umma_commit(&q_empty[s]);
         return true;
       };
-      if (ok) {
-        for (int c = 0; c < n_chunks && ok; ++c) {
-          const int s = c % STAGES, sb = c & 1;
-          if (!mbar_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
-          if (!mbar_wait(&st_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      bool ok = true;
+      int Jbase = 0, it_n = 0;
+      for (int rnd = 0, i = item_at(0); i < n_items && ok; i = item_at(++rnd)) {
+        const KvItem w = item_of(i);
+        if (w.skip) continue;
+        const int n_chunks = w.n_chunks;
+        if (!mbar_wait(kv_full, it_n & 1, abort_flag, prm.err)) { ok = false; break; }
+        // the previous item's accumulators must have been read out first
+        bool waited_free = false;
+        auto wait_free = [&]() -> bool {
+          if (waited_free) return true;
+          waited_free = true;
+          return mbar_wait(acc_free, (it_n & 1) ^ 1, abort_flag, prm.err);
+        };
+        for (int c = 0; c < n_chunks; ++c) {
+          const int J = Jbase + c;
+          const int s = J % STAGES, sb = J & 1;
+          if (!mbar_wait(&q_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&st_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t kb = smem_u32(sK), vb = smem_u32(sV);
           const uint32_t qb = smem_u32(sQ + s * L::QTILE), dob = smem_u32(sDO + s * L::QTILE);
@@ -1075,11 +1133,19 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             umma_f16(tm_dpt0 + sb * kKvQRows, make_sdesc(vb + ks * 32, 16, 8 * RB, SWZ),
                      make_sdesc(dob + ks * 32, 16, 8 * RB, SWZ), idesc_st, ks > 0);
           umma_commit(&st_full[sb]);
-          if (c >= 1 && !issue_acc(c - 1)) { ok = false; break; }
+          if (c >= 1) {
+            if (c == 1 && !wait_free()) { ok = false; break; }
+            if (!issue_acc(J - 1, c == 1)) { ok = false; break; }
+          }
         }
-        if (ok && n_chunks > 0) issue_acc(n_chunks - 1);
+        if (!ok) break;
+        umma_commit(kv_empty);  // K / V are free once the item's S^T and dP^T products are done
+        if (!wait_free()) { ok = false; break; }
+        if (n_chunks > 0 && !issue_acc(Jbase + n_chunks - 1, n_chunks == 1)) { ok = false; break; }
+        umma_commit(acc_done);  // one completion per item
+        Jbase += n_chunks;
+        ++it_n;
       }
-      umma_commit(acc_done);
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
     }
@@ -1089,16 +1155,23 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     // warp w: key rows 32*(w%4).., query columns 32*(w/4).. of each chunk
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;  // key row
-    const bool row_valid = r < kt.n_q;
-    const int kidx = kt.q_start + r;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = prm.scale_log2, scale = prm.scale;
     const float lse_mul = prm.lse_natural ? 1.4426950408889634f : 1.f;
     bool ok = true;
+    int Jbase = 0, it_n = 0;
+    for (int rnd = 0, it = item_at(0); it < n_items && ok; it = item_at(++rnd)) {
+    const KvItem w = item_of(it);
+    if (w.skip) continue;
+    const QTile& kt = w.kt;
+    const int n_chunks = w.n_chunks, h = w.h, split = w.split, kt_idx = w.kt_idx;
+    const bool row_valid = r < kt.n_q;
+    const int kidx = kt.q_start + r;
     for (int c = 0; c < n_chunks; ++c) {
-      const int s = c % STAGES, sb = c & 1;
-      if (!warp_wait(&st_full[sb], (c >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-      if (!warp_wait(&q_full[s], (c / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
+      const int J = Jbase + c;
+      const int s = J % STAGES, sb = J & 1;
+      if (!warp_wait(&st_full[sb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&q_full[s], (J / STAGES) & 1, abort_flag, prm.err)) { ok = false; break; }
       tc_fence_after();
       const KvMeta& mt = meta[s];
       const int n_rows = mt.n_rows;
@@ -1148,7 +1221,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
           dpt[cc] = valid ? p * (dpt[cc] - dl_c[cc]) * scale : 0.f;
         }
       }
-      if (!warp_wait(&pds_free[sb], ((c >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      if (!warp_wait(&pds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
       const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
 #pragma unroll
       for (int q8 = 0; q8 < 4; ++q8) {
@@ -1163,10 +1236,11 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&pds_full[sb]);
     }
-    // epilogue: warps of half 0 write dK, of half 1 write dV (key row r)
-    bool have = ok;
-    if (ok && n_chunks > 0) have = warp_wait(acc_done, 0, abort_flag, prm.err);
-    if (have) {
+    if (!ok) break;
+    // epilogue: warps of half 0 write dK, of half 1 write dV (key row r);
+    // then all eight warps hand the accumulators to the next item
+    if (!warp_wait(acc_done, it_n & 1, abort_flag, prm.err)) { ok = false; break; }
+    {
       tc_fence_after();
       const int which = half;
       const uint32_t tm_acc = which == 0 ? tm_dk : tm_dv;
@@ -1201,6 +1275,12 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         }
       }
     }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(acc_free);
+    Jbase += n_chunks;
+    ++it_n;
+    }  // items
   }
 
   tc_fence_before();

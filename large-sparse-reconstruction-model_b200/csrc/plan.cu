@@ -466,11 +466,14 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
 // The chunk count follows the dK/dV kernel's rule: a block whose reverse
 // list fits the shared-memory cache and G <= 8 runs in 8-row query groups
 // (chunks of 8 groups), otherwise in chunks of 64/G gathered queries.
+// One warp per item: the lanes stride over the block's reverse entries.
 __global__ void sched_key_kernel(SelectPlan p, int G) {
   const int items = p.hkv * p.kvtiles_ub;
   const int n_kv = *p.n_kvtiles;
   const int qpc = 64 / G, W = G <= 8 ? 8 / G : 1;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < items; i += warps) {
     const int h = i / p.kvtiles_ub, kt = i - h * p.kvtiles_ub;
     int bin = kSchedBins - 1;  // empty / unused items last
     int chunks = 0;
@@ -478,20 +481,28 @@ __global__ void sched_key_kernel(SelectPlan p, int G) {
       const int blk = p.kvtiles[kt].seg;
       const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
       const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
-      const bool grouped = off[blk + 1] - off[blk] <= kRevCacheCap && G <= 8;
+      const int e0 = off[blk], e1 = off[blk + 1];
+      const bool grouped = e1 - e0 <= kRevCacheCap && G <= 8;
       int nq = 0, ng = 0;
-      for (int e = off[blk]; e < off[blk + 1]; ++e) {
+      for (int e = e0 + lane; e < e1; e += 32) {
         const int2 x = ent[e];
         const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
         nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
-        if (grouped) ng += __popc(window_mask(m, W));
+        if (grouped) ng += window_count(m, W);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        nq += __shfl_xor_sync(0xffffffffu, nq, o);
+        ng += __shfl_xor_sync(0xffffffffu, ng, o);
       }
       chunks = grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
       bin = kSchedBins - 1 - min(chunks, kSchedBins - 1);
     }
-    p.sched_key[i] = bin;
-    p.item_nch[i] = chunks;
-    atomicAdd(&p.sched_bins[bin], 1);
+    if (lane == 0) {
+      p.sched_key[i] = bin;
+      p.item_nch[i] = chunks;
+      atomicAdd(&p.sched_bins[bin], 1);
+    }
   }
 }
 
@@ -535,7 +546,7 @@ int launch_build_kv_schedule(const SelectPlan& p, int G, cudaStream_t s) {
   LSRM_CUDA_TRY(cudaMemsetAsync(p.sched_bins, 0, sizeof(int) * kSchedBins, s));
   const int items = p.hkv * p.kvtiles_ub;
   const int grid = std::min((items + 255) / 256, 148 * 8);
-  sched_key_kernel<<<grid, 256, 0, s>>>(p, G);
+  sched_key_kernel<<<std::min((items + 7) / 8, 148 * 16), 256, 0, s>>>(p, G);  // 8 items (warps) per block
   LSRM_LAUNCH_CHECK();
   sched_scan_kernel<<<1, kSchedBins, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();

@@ -91,6 +91,18 @@ __device__ __forceinline__ uint32_t window_bits(const uint4& m, int w, int W) {
   return (word >> (o & 31)) & ((1u << W) - 1u);
 }
 
+// Number of non-empty windows (W in {1, 2, 4, 8}) of a 128-bit mask.
+__device__ __forceinline__ int window_count(const uint4& m, int W) {
+  auto f = [&](uint32_t x) {
+    if (W >= 2) x |= x >> 1;
+    if (W >= 4) x |= x >> 2;
+    if (W >= 8) x |= x >> 4;
+    const uint32_t keep = W == 1 ? 0xffffffffu : W == 2 ? 0x55555555u : W == 4 ? 0x11111111u : 0x01010101u;
+    return __popc(x & keep);
+  };
+  return f(m.x) + f(m.y) + f(m.z) + f(m.w);
+}
+
 __device__ __forceinline__ uint32_t window_mask(const uint4& m, int W) {
   uint32_t wm = 0u;
 #pragma unroll
