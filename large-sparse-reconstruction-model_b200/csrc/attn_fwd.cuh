@@ -484,16 +484,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
+      // each warp keeps the row sum of its own columns (same scale m in both);
+      // the halves are added once, after the last chunk
       const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      xch[256 + half * 128 + r] = rs;
-      pair_bar(quarter);
-      const float rowsum = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps
-      l = l * alpha + rowsum;
+      l = l * alpha + rs;
       if (j >= 1 && !fold_pv(J - 1)) { ok = false; break; }
       alpha_prev = alpha;
       m = m_new;
     }
     if (ok && n_chunks > 0) ok = fold_pv(J - 1);
+    if (ok) {  // both warps of a pair agree on ok: they fail on the same barriers
+      xch[256 + half * 128 + r] = l;
+      pair_bar(quarter);
+      l = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps
+      pair_bar(quarter);                      // the slots are reused by the next item
+    }
     if (ok && row_valid) {
       const float inv = (l > 0.f) ? 1.f / l : __int_as_float(0x7fc00000);
       uint8_t* orow =
