@@ -583,18 +583,15 @@ struct DkvSmem {
   static constexpr int RB = 2 * D;
   static constexpr int KTILE = 128 * RB;
   static constexpr int QTILE = kKvQRows * RB;
-  static constexpr int PT_BYTES = 128 * 128;  // 128 keys x 64 query rows x 2 B
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = KTILE;
   static constexpr int OFF_Q = 2 * KTILE;
   static constexpr int OFF_DO = OFF_Q + STAGES * QTILE;
-  static constexpr int OFF_PT = OFF_DO + STAGES * QTILE;
-  static constexpr int OFF_DST = OFF_PT + 2 * PT_BYTES;
-  static constexpr int OFF_META = OFF_DST + 2 * PT_BYTES;
+  static constexpr int OFF_META = OFF_DO + STAGES * QTILE;  // P^T / dS^T live in TMEM
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(KvMeta);
   // kv_full, kv_empty, q_full[S], q_empty[S], st_full[2], st_free[2], pds_full[2], pds_free[2],
-  // acc_done, acc_free, mma_done, rc_empty, rc_full
-  static constexpr int NBAR = 2 + 2 * STAGES + 8 + 5;
+  // acc_done, acc_free, mma_done, rc_empty, rc_full, acc_mma_done
+  static constexpr int NBAR = 2 + 2 * STAGES + 8 + 6;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_RC = (OFF_MISC + 32 + 15) / 16 * 16;  // select mode: the block's reverse map
   static constexpr int BYTES = OFF_RC + (int)sizeof(RevCache);
@@ -604,11 +601,13 @@ struct DkvSmem {
 
 
 // Threads of the dK/dV kernel: 8 compute warps (two per TMEM lane quarter,
-// splitting the 64 query columns of a chunk), a producer warp, an MMA warp.
-constexpr int kDkvThreads = 352;
+// splitting the 64 query columns of a chunk), two producer warps and two
+// MMA-issuing warps.
+constexpr int kDkvThreads = 384;
 constexpr int kDkvProducerWarp = 8;
 constexpr int kDkvMmaWarp = 9;
 constexpr int kDkvProducer2Warp = 10;  // select mode: gathers every other chunk
+constexpr int kDkvAccWarp = 11;        // issues the dV / dK accumulation MMAs
 
 // Warp-wide fill of the reverse cache for block `blk` of kv head `h`.
 __device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& prm, int h, int blk) {
@@ -742,8 +741,6 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   uint8_t* sV = smem + L::OFF_V;
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sDO = smem + L::OFF_DO;
-  uint8_t* sPT = smem + L::OFF_PT;
-  uint8_t* sDST = smem + L::OFF_DST;
   KvMeta* meta = reinterpret_cast<KvMeta*>(smem + L::OFF_META);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
@@ -759,6 +756,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   uint64_t* mma_done = acc_free + 1;
   uint64_t* rc_empty = mma_done + 1;  // both producer warps are done with the cache (count 2)
   uint64_t* rc_full = rc_empty + 1;   // warp 8 has filled it for the next item (count 1)
+  uint64_t* acc_mma_done = rc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -832,6 +830,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     mbar_init(mma_done, 1);
     mbar_init(rc_empty, 2);
     mbar_init(rc_full, 1);
+    mbar_init(acc_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -845,7 +844,9 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int lg_g = __ffs(G) - 1;  // G is a power of two
   // TMEM: St0 [0,64) St1 [64,128) dPt0 [128,192) dPt1 [192,256) dK [256,256+D) dV [256+D, 256+2D)
+  // P^T 0/1 [384,416) [416,448), dS^T 0/1 [448,480) [480,512): 16-bit pairs, the A operand of dV / dK
   const uint32_t tm_st0 = tmem, tm_dpt0 = tmem + 128, tm_dk = tmem + 256, tm_dv = tmem + 256 + D;
+  const uint32_t tm_pt = tmem + 384, tm_dst = tmem + 448;
 
   if (warp == kDkvProducerWarp || warp == kDkvProducer2Warp) {
     // ------------------------------ producers -----------------------------
@@ -1077,31 +1078,13 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     }
     __syncwarp();
   } else if (warp == kDkvMmaWarp) {
-    // ------------------------------ MMA issuer -----------------------------
+    // --------------------------- MMA issuer: S^T, dP^T ----------------------
+    // Two threads issue the tensor-core work: this one S^T = K Q^T and
+    // dP^T = V dO^T of every chunk, warp 11 the dV / dK accumulation.  One
+    // issuing thread spends ~90 cycles per tcgen05.mma in bursts of 8; two
+    // keep the pipe near its operand-read rate (~56 cycles per 128x64x16).
     if (lane == 0) {
       const uint32_t idesc_st = make_idesc(AB, 0, 0, 128, kKvQRows);
-      const uint32_t idesc_acc = make_idesc(AB, 0, 1, 128, D);
-      // dV += P^T dO, dK += dS^T Q for chunk i; `first` starts the item's accumulators
-      auto issue_acc = [&](int i, bool first) -> bool {
-        const int pb = i & 1, s = i % STAGES;
-        if (!mbar_wait(&pds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
-        tc_fence_after();
-        const uint32_t pt = smem_u32(sPT + pb * L::PT_BYTES), dst = smem_u32(sDST + pb * L::PT_BYTES);
-        const uint32_t qb = smem_u32(sQ + s * L::QTILE), dob = smem_u32(sDO + s * L::QTILE);
-#pragma unroll
-        for (int ks = 0; ks < kKvQRows / 16; ++ks) {
-          umma_f16(tm_dv, make_sdesc(pt + ks * 32, 16, 1024, kSw128),
-                   make_sdesc(dob + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (!first || ks > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int ks = 0; ks < kKvQRows / 16; ++ks) {
-          umma_f16(tm_dk, make_sdesc(dst + ks * 32, 16, 1024, kSw128),
-                   make_sdesc(qb + ks * 16 * RB, L::QTILE, 8 * RB, SWZ), idesc_acc, (!first || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(&pds_free[pb]);
-        umma_commit(&q_empty[s]);
-        return true;
-      };
       bool ok = true;
       int Jbase = 0, it_n = 0;
       for (int rnd = 0, i = item_at(0); i < n_items && ok; i = item_at(++rnd)) {
@@ -1109,13 +1092,6 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         if (w.skip) continue;
         const int n_chunks = w.n_chunks;
         if (!mbar_wait(kv_full, it_n & 1, abort_flag, prm.err)) { ok = false; break; }
-        // the previous item's accumulators must have been read out first
-        bool waited_free = false;
-        auto wait_free = [&]() -> bool {
-          if (waited_free) return true;
-          waited_free = true;
-          return mbar_wait(acc_free, (it_n & 1) ^ 1, abort_flag, prm.err);
-        };
         for (int c = 0; c < n_chunks; ++c) {
           const int J = Jbase + c;
           const int s = J % STAGES, sb = J & 1;
@@ -1133,21 +1109,57 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             umma_f16(tm_dpt0 + sb * kKvQRows, make_sdesc(vb + ks * 32, 16, 8 * RB, SWZ),
                      make_sdesc(dob + ks * 32, 16, 8 * RB, SWZ), idesc_st, ks > 0);
           umma_commit(&st_full[sb]);
-          if (c >= 1) {
-            if (c == 1 && !wait_free()) { ok = false; break; }
-            if (!issue_acc(J - 1, c == 1)) { ok = false; break; }
-          }
         }
         if (!ok) break;
         umma_commit(kv_empty);  // K / V are free once the item's S^T and dP^T products are done
-        if (!wait_free()) { ok = false; break; }
-        if (n_chunks > 0 && !issue_acc(Jbase + n_chunks - 1, n_chunks == 1)) { ok = false; break; }
-        umma_commit(acc_done);  // one completion per item
         Jbase += n_chunks;
         ++it_n;
       }
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else if (warp == kDkvAccWarp) {
+    // ------------------------ MMA issuer: dV, dK ----------------------------
+    // dV += P^T dO, dK += dS^T Q of each chunk once the compute warps have
+    // written P^T / dS^T.  The chunk's S^T / dP^T products are complete by
+    // then (the compute warps read them first), so this thread's commit
+    // alone releases the chunk's Q / dO stage.
+    if (lane == 0) {
+      const uint32_t idesc_acc = make_idesc(AB, 0, 1, 128, D);
+      bool ok = true;
+      int Jbase = 0, it_n = 0;
+      for (int rnd = 0, i = item_at(0); i < n_items && ok; i = item_at(++rnd)) {
+        const KvItem w = item_of(i);
+        if (w.skip) continue;
+        const int n_chunks = w.n_chunks;
+        // the previous item's accumulators must have been read out first
+        if (!mbar_wait(acc_free, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+        for (int c = 0; c < n_chunks; ++c) {
+          const int J = Jbase + c;
+          const int pb = J & 1, s = J % STAGES;
+          const uint32_t accum0 = c > 0 ? 1u : 0u;
+          if (!mbar_wait(&pds_full[pb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qb = smem_u32(sQ + s * L::QTILE), dob = smem_u32(sDO + s * L::QTILE);
+#pragma unroll
+          for (int ks = 0; ks < kKvQRows / 16; ++ks)
+            umma_f16_ts(tm_dv, tm_pt + pb * 32 + ks * 8, make_sdesc(dob + ks * 16 * RB, L::QTILE, 8 * RB, SWZ),
+                        idesc_acc, ks > 0 ? 1u : accum0);
+#pragma unroll
+          for (int ks = 0; ks < kKvQRows / 16; ++ks)
+            umma_f16_ts(tm_dk, tm_dst + pb * 32 + ks * 8, make_sdesc(qb + ks * 16 * RB, L::QTILE, 8 * RB, SWZ),
+                        idesc_acc, ks > 0 ? 1u : accum0);
+          umma_commit(&pds_free[pb]);
+          umma_commit(&q_empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(acc_done);  // one completion per item
+        Jbase += n_chunks;
+        ++it_n;
+      }
+      umma_commit(acc_mma_done);
+      mbar_wait_drain(acc_mma_done, 0);
     }
     __syncwarp();
   } else if (warp < 8) {
@@ -1221,18 +1233,20 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
           dpt[cc] = valid ? p * (dpt[cc] - dl_c[cc]) * scale : 0.f;
         }
       }
-      if (!warp_wait(&pds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-      const uint32_t pt = smem_u32(sPT + sb * L::PT_BYTES), dst = smem_u32(sDST + sb * L::PT_BYTES);
+      // key row r's 32 query columns of P^T and dS^T, 16-bit pairs, into
+      // this warp's TMEM lanes (the dV / dK MMAs read them as operand A)
+      uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        const int ch = half * 4 + q8;
-        const uint32_t o = swz_offset<128>(r, ch);
-        st_shared_v4(pt + o, pack2<BF16>(st[q8 * 8], st[q8 * 8 + 1]), pack2<BF16>(st[q8 * 8 + 2], st[q8 * 8 + 3]),
-                     pack2<BF16>(st[q8 * 8 + 4], st[q8 * 8 + 5]), pack2<BF16>(st[q8 * 8 + 6], st[q8 * 8 + 7]));
-        st_shared_v4(dst + o, pack2<BF16>(dpt[q8 * 8], dpt[q8 * 8 + 1]), pack2<BF16>(dpt[q8 * 8 + 2], dpt[q8 * 8 + 3]),
-                     pack2<BF16>(dpt[q8 * 8 + 4], dpt[q8 * 8 + 5]), pack2<BF16>(dpt[q8 * 8 + 6], dpt[q8 * 8 + 7]));
+      for (int j = 0; j < 16; ++j) {
+        pk[j] = pack2<BF16>(st[2 * j], st[2 * j + 1]);
+        dk[j] = pack2<BF16>(dpt[2 * j], dpt[2 * j + 1]);
       }
-      fence_proxy_async_smem();
+      if (!warp_wait(&pds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      tmem_st16(tm_pt + sb * 32 + half * 16 + lane_base, pk);
+      tmem_st16(tm_dst + sb * 32 + half * 16 + lane_base, dk);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pds_full[sb]);
     }
