@@ -40,7 +40,7 @@ __global__ void zero_tail_kernel(uint16_t* dk, uint16_t* dv, const int32_t* star
 template <int D, bool BF16, int MODE>
 static int launch_dq_t(const CUtensorMap& mq, const CUtensorMap& mdo, const KVMaps& kv, const DqParams& p, int grid_x,
                        int hkv, cudaStream_t s) {
-  constexpr int STAGES = 4;
+  constexpr int STAGES = 6;
   using L = DqSmem<D, STAGES>;
   auto kern = attn_dq_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));

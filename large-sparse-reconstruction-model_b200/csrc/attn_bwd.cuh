@@ -66,17 +66,15 @@ struct DqSmem {
   static constexpr int RB = 2 * D;
   static constexpr int QTILE = 128 * RB;
   static constexpr int KTILE = kDqChunk * RB;
-  static constexpr int DS_BYTES = 128 * 128;  // 128 rows x 64 keys x 2 B
   static constexpr int OFF_Q = 0;            // two Q tiles and two dO tiles (the next item's prefetch)
   static constexpr int OFF_DO = 2 * QTILE;
   static constexpr int OFF_K = 4 * QTILE;
   static constexpr int OFF_V = OFF_K + STAGES * KTILE;
-  static constexpr int OFF_DS = OFF_V + STAGES * KTILE;
-  static constexpr int OFF_META = OFF_DS + 2 * DS_BYTES;
+  static constexpr int OFF_META = OFF_V + STAGES * KTILE;  // dS lives in TMEM
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(DqMeta);
   // kv_full[S], kv_empty[S], qdo_full[2], qdo_empty[2], sd_full[2], sd_free[2],
-  // ds_full[2], ds_free[2], dq_done, dq_free, mma_done
-  static constexpr int NBAR = 2 * STAGES + 4 + 8 + 3;
+  // ds_full[2], ds_free[2], dq_done, dq_free, mma_done, dq_mma_done
+  static constexpr int NBAR = 2 * STAGES + 4 + 8 + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
@@ -120,8 +118,9 @@ __device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, 
 }
 
 // Threads of the dQ kernel: 8 compute warps (two per TMEM lane quarter,
-// splitting the 64 key columns of a chunk), a producer warp, an MMA warp.
-constexpr int kDqThreads = 320;
+// splitting the 64 key columns of a chunk), a producer warp and two
+// MMA-issuing warps (S / dP, and the dQ accumulation).
+constexpr int kDqThreads = 352;
 
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kDqThreads, 1)
@@ -142,7 +141,6 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint8_t* sDO = smem + L::OFF_DO;
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
-  uint8_t* sDS = smem + L::OFF_DS;
   DqMeta* meta = reinterpret_cast<DqMeta*>(smem + L::OFF_META);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
@@ -156,6 +154,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint64_t* dq_done = ds_free + 2;
   uint64_t* dq_free = dq_done + 1;
   uint64_t* mma_done = dq_free + 1;
+  uint64_t* dq_mma_done = mma_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -201,6 +200,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     mbar_init(dq_done, 1);
     mbar_init(dq_free, 8);
     mbar_init(mma_done, 1);
+    mbar_init(dq_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM: S0 [0,64) S1 [64,128) dP0 [128,192) dP1 [192,256) dQ [256, 256+D)
-  const uint32_t tm_s0 = tmem, tm_dp0 = tmem + 128, tm_dq = tmem + 256;
+  // dS 0/1 [384,416) [416,448): 16-bit pairs, the A operand of the dQ product
+  const uint32_t tm_s0 = tmem, tm_dp0 = tmem + 128, tm_dq = tmem + 256, tm_ds = tmem + 384;
 
   if (warp == 8) {
     if (lane == 0) {
@@ -293,38 +294,17 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
     __syncwarp();
   } else if (warp == 9) {
+    // --------------------------- MMA issuer: S, dP --------------------------
+    // One thread issues S = Q K^T and dP = dO V^T of every chunk, warp 10 the
+    // dQ accumulation (one issuing thread spends ~90 cycles per tcgen05.mma
+    // in short bursts; two keep the tensor pipe busy).
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc(AB, 0, 0, 128, kDqChunk);
-      const uint32_t idesc_dq = make_idesc(AB, 0, 1, 128, D);
-      // dQ(i) += dS(i) K(i); `first` starts the item's accumulator
-      auto issue_dq = [&](int i, bool first) -> bool {
-        const int pb = i & 1, s = i % STAGES;
-        if (!mbar_wait(&ds_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(sDS + pb * L::DS_BYTES);
-        const uint32_t k_base = smem_u32(sK + s * L::KTILE);
-#pragma unroll
-        for (int ks = 0; ks < kDqChunk / 16; ++ks) {
-          const uint64_t da = make_sdesc(a_base + ks * 32, 16, 1024, kSw128);
-          const uint64_t db = make_sdesc(k_base + ks * 16 * RB, L::KTILE, 8 * RB, SWZ);
-          umma_f16(tm_dq, da, db, idesc_dq, (!first || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(&ds_free[pb]);
-        umma_commit(&kv_empty[s]);
-        return true;
-      };
       bool ok = true;
       int J = 0, it_n = 0;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
         const int n_chunks = item_of(i).n_chunks, qb = it_n & 1;
         if (!mbar_wait(&qdo_full[qb], (it_n >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-        // the previous item's dQ accumulator must have been read out before this item's first dQ product
-        bool waited_free = false;
-        auto wait_free = [&]() -> bool {
-          if (waited_free) return true;
-          waited_free = true;
-          return mbar_wait(dq_free, (it_n & 1) ^ 1, abort_flag, prm.err);
-        };
         const uint32_t q_base = smem_u32(sQ + qb * L::QTILE), do_base = smem_u32(sDO + qb * L::QTILE);
         for (int j = 0; j < n_chunks; ++j, ++J) {
           const int s = J % STAGES, sb = J & 1;
@@ -343,19 +323,45 @@ __global__ void __launch_bounds__(kDqThreads, 1)
                      make_sdesc(v_base + ks * 32, 16, 8 * RB, SWZ), idesc_s, ks > 0);
           }
           umma_commit(&sd_full[sb]);
-          if (j >= 1) {
-            if (j == 1 && !wait_free()) { ok = false; break; }
-            if (!issue_dq(J - 1, j == 1)) { ok = false; break; }
-          }
         }
         if (!ok) break;
         umma_commit(&qdo_empty[qb]);  // Q / dO tiles free once the item's S and dP products are done
-        if (!wait_free()) { ok = false; break; }
-        if (n_chunks > 0 && !issue_dq(J - 1, n_chunks == 1)) { ok = false; break; }
-        umma_commit(dq_done);  // one completion per item
       }
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------- MMA issuer: dQ += dS K -----------------------
+    // The chunk's S / dP products are complete once its dS is written (the
+    // compute warps read them first), so this thread's commit alone releases
+    // the chunk's K / V stage.
+    if (lane == 0) {
+      const uint32_t idesc_dq = make_idesc(AB, 0, 1, 128, D);
+      bool ok = true;
+      int J = 0, it_n = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
+        const int n_chunks = item_of(i).n_chunks;
+        // the previous item's dQ accumulator must have been read out first
+        if (!mbar_wait(dq_free, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+        for (int j = 0; j < n_chunks; ++j, ++J) {
+          const int pb = J & 1, s = J % STAGES;
+          if (!mbar_wait(&ds_full[pb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(sK + s * L::KTILE);
+#pragma unroll
+          for (int ks = 0; ks < kDqChunk / 16; ++ks) {
+            const uint64_t db = make_sdesc(k_base + ks * 16 * RB, L::KTILE, 8 * RB, SWZ);
+            umma_f16_ts(tm_dq, tm_ds + pb * 32 + ks * 8, db, idesc_dq, (j > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(&ds_free[pb]);
+          umma_commit(&kv_empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(dq_done);  // one completion per item
+      }
+      umma_commit(dq_mma_done);
+      mbar_wait_drain(dq_mma_done, 0);
     }
     __syncwarp();
   } else {
@@ -437,16 +443,16 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           sv[c] = valid ? p * (dp[c] - delta) * scale : 0.f;
         }
       }
-      if (!warp_wait(&ds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-      const uint32_t ds_base = smem_u32(sDS + sb * L::DS_BYTES);
+      // row r's 32 key columns of dS, 16-bit pairs, into this warp's TMEM
+      // lanes (the dQ MMA reads them as operand A)
+      uint32_t pk[16];
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        const int ch = half * 4 + q8;
-        st_shared_v4(ds_base + swz_offset<128>(r, ch), pack2<BF16>(sv[q8 * 8 + 0], sv[q8 * 8 + 1]),
-                     pack2<BF16>(sv[q8 * 8 + 2], sv[q8 * 8 + 3]), pack2<BF16>(sv[q8 * 8 + 4], sv[q8 * 8 + 5]),
-                     pack2<BF16>(sv[q8 * 8 + 6], sv[q8 * 8 + 7]));
-      }
-      fence_proxy_async_smem();
+      for (int c = 0; c < 16; ++c) pk[c] = pack2<BF16>(sv[2 * c], sv[2 * c + 1]);
+      if (!warp_wait(&ds_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      tmem_st16(tm_ds + sb * 32 + half * 16 + lane_base, pk);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[sb]);
     }

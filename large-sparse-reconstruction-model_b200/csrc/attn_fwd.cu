@@ -12,7 +12,7 @@ namespace lsrm {
 template <int D, bool BF16, int MODE>
 static int launch_fwd_t(const CUtensorMap& mq, const KVMaps& kv, const FwdParams& p, int grid_x, int hkv,
                         cudaStream_t s) {
-  constexpr int STAGES = 3;
+  constexpr int STAGES = 5;
   using L = FwdSmem<D, STAGES>;
   auto kern = attn_fwd_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));

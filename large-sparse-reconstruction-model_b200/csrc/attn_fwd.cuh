@@ -1,17 +1,18 @@
 // Forward attention kernel for sm_100a: one CTA per (query tile, kv head).
 //
-// Roles (320 threads):
+// Roles (352 threads):
 //   warps 0-7  softmax: warps w and w+4 own MMA rows 32*(w%4).. (row r =
 //              query r/G, head r%G) and split each 128-key chunk into two
 //              64-key halves; they read S = Q K^T from TMEM, apply the row's
-//              key mask, exchange partial row max / row sum through shared
-//              memory (online softmax in log2 units), write their half of P
-//              (bf16/fp16) to shared memory, and each folds half of O's
-//              columns of P V from TMEM into fp32 registers.
+//              key mask, exchange the partial row max through shared memory
+//              (online softmax in log2 units), write their half of P
+//              (bf16/fp16) to TMEM, and each folds half of O's columns of
+//              P V from TMEM into fp32 registers.
 //   warp 8     producer: TMA loads of the Q tile and of K/V chunks (128 keys)
 //              into a STAGES-deep ring.
-//   warp 9     MMA issuer (lane 0): S_j = Q K_j^T (M=128, N=128), then
-//              O_j = P_j V_j (M=128, N=D); S and PV double-buffered in TMEM.
+//   warp 9     MMA issuer (lane 0): S_j = Q K_j^T (M=128, N=128).
+//   warp 10    MMA issuer (lane 0): O_j = P_j V_j (M=128, N=D), P read from
+//              TMEM.  S, P and PV are double-buffered in TMEM.
 //
 // KV chunk sources:
 //   kSelect : the union of the blocks selected by the tile's queries, walked
@@ -68,17 +69,15 @@ template <int D, int STAGES>
 struct FwdSmem {
   static constexpr int RB = 2 * D;
   static constexpr int TILE = 128 * RB;
-  static constexpr int P_BYTES = 2 * 128 * 128;  // two 64-key regions, 128B rows
   static constexpr int OFF_Q = 0;                 // two Q tiles (persistent CTAs prefetch the next)
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
-  static constexpr int OFF_P = OFF_V + STAGES * TILE;
-  static constexpr int OFF_XCH = OFF_P + 2 * P_BYTES;  // row max / row sum exchange [2][2][128]
+  static constexpr int OFF_XCH = OFF_V + STAGES * TILE;  // row max / row sum exchange [2][2][128]; P is in TMEM
   static constexpr int OFF_META = OFF_XCH + 4 * 128 * 4;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(ChunkMeta);
   // barriers: kv_full[S], kv_empty[S], q_full[2], q_empty[2], s_full[2], s_free[2],
-  // p_full[2], p_free[2], pv_full[2], pv_free[2], mma_done
-  static constexpr int NBAR = 2 * STAGES + 4 + 12 + 1;
+  // p_full[2], p_free[2], pv_full[2], pv_free[2], mma_done, pv_mma_done
+  static constexpr int NBAR = 2 * STAGES + 4 + 12 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
@@ -87,7 +86,7 @@ struct FwdSmem {
   static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
-constexpr int kFwdThreads = 320;
+constexpr int kFwdThreads = 352;
 
 __device__ __forceinline__ void pair_bar(int quarter) {
   asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
@@ -116,7 +115,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
-  uint8_t* sP = smem + L::OFF_P;
   ChunkMeta* meta = reinterpret_cast<ChunkMeta*>(smem + L::OFF_META);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
@@ -130,6 +128,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* pv_full = p_free + 2;
   uint64_t* pv_free = pv_full + 2;
   uint64_t* mma_done = pv_free + 2;
+  uint64_t* pv_mma_done = mma_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -176,6 +175,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&pv_free[i], 8);
     }
     mbar_init(mma_done, 1);
+    mbar_init(pv_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -187,8 +187,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,128), S1 [128,256), PV0 [256,256+D), PV1 [256+D, 256+2D)
-  const uint32_t tm_s0 = tmem, tm_pv0 = tmem + 256;
+  // TMEM columns: S0 [0,128), S1 [128,256), PV0 [256,256+D), PV1 [256+D, 256+2D),
+  // P0 [384,448), P1 [448,512) (16-bit pairs: the A operand of P V)
+  const uint32_t tm_s0 = tmem, tm_pv0 = tmem + 256, tm_p0 = tmem + 384;
 
   if (warp == 8) {
     // ------------------------------ producer ------------------------------
@@ -290,28 +291,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     __syncwarp();
   } else if (warp == 9) {
-    // ------------------------------ MMA issuer -----------------------------
+    // --------------------------- MMA issuer: S = Q K^T ----------------------
+    // Two threads issue the tensor-core work (one spends ~90 cycles per
+    // tcgen05.mma in short bursts): this one S, warp 10 the P V products.
     if (lane == 0) {
       const uint32_t idesc_qk = make_idesc(AB, 0, 0, 128, 128);
-      const uint32_t idesc_pv = make_idesc(AB, 0, 1, 128, D);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1, s = i % STAGES;
-        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
-        if (!mbar_wait(&pv_free[pb], ((i >> 1) & 1) ^ 1, abort_flag, prm.err)) return false;
-        tc_fence_after();
-        const uint32_t p_base = smem_u32(sP + pb * L::P_BYTES);
-        const uint32_t v_base = smem_u32(sV + s * L::TILE);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t da = make_sdesc(p_base + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSw128);
-          const uint64_t db = make_sdesc(v_base + ks * 16 * RB, L::TILE, 8 * RB, SWZ);
-          umma_f16(tm_pv0 + pb * D, da, db, idesc_pv, ks > 0);
-        }
-        umma_commit(&pv_full[pb]);
-        umma_commit(&p_free[pb]);
-        umma_commit(&kv_empty[s]);
-        return true;
-      };
       bool ok = true;
       int J = 0, it_n = 0;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
@@ -331,14 +315,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             umma_f16(tm_s0 + sb * 128, da, db, idesc_qk, ks > 0);
           }
           umma_commit(&s_full[sb]);
-          if (j >= 1 && !issue_pv(J - 1)) { ok = false; break; }
         }
         if (!ok) break;
         umma_commit(&q_empty[qb]);  // the item's Q tile is free once its S products are done
-        if (n_chunks > 0 && !issue_pv(J - 1)) { ok = false; break; }
       }
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // --------------------------- MMA issuer: O_j = P_j V_j ------------------
+    // S_j is complete once P_j is written (the softmax warps read it first),
+    // so this thread's commit alone releases the chunk's K / V stage.
+    if (lane == 0) {
+      const uint32_t idesc_pv = make_idesc(AB, 0, 1, 128, D);
+      bool ok = true;
+      int J = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+        const int n_chunks = item_of(i).n_chunks;
+        for (int j = 0; j < n_chunks; ++j, ++J) {
+          const int pb = J & 1, s = J % STAGES;
+          if (!mbar_wait(&p_full[pb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+          if (!mbar_wait(&pv_free[pb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(sV + s * L::TILE);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t db = make_sdesc(v_base + ks * 16 * RB, L::TILE, 8 * RB, SWZ);
+            umma_f16_ts(tm_pv0 + pb * D, tm_p0 + pb * 64 + ks * 8, db, idesc_pv, ks > 0);
+          }
+          umma_commit(&pv_full[pb]);
+          umma_commit(&p_free[pb]);
+          umma_commit(&kv_empty[s]);
+        }
+      }
+      umma_commit(pv_mma_done);
+      mbar_wait_drain(pv_mma_done, 0);
     }
     __syncwarp();
   } else {
@@ -450,10 +462,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float m_new = fmaxf(m, mx * sl2);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      // probabilities -> P (shared, K-major 128B swizzle; this half = region `half`)
-      if (!warp_wait(&p_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      // probabilities -> P: this warp's 64 keys as 16-bit pairs into TMEM
+      // columns [half*32, half*32+32) of the P buffer (operand A of P V)
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t p_base = smem_u32(sP + sb * L::P_BYTES) + half * 16384;
+      uint32_t pk[2][16];
 #pragma unroll
       for (int xx = 0; xx < 2; ++xx) {
         if (full) {
@@ -473,15 +485,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = xx * 4 + q8;  // 16-byte chunk inside this half's 64-key region
-          st_shared_v4(p_base + swz_offset<128>(r, ch), pack2<BF16>(sv[xx][q8 * 8 + 0], sv[xx][q8 * 8 + 1]),
-                       pack2<BF16>(sv[xx][q8 * 8 + 2], sv[xx][q8 * 8 + 3]),
-                       pack2<BF16>(sv[xx][q8 * 8 + 4], sv[xx][q8 * 8 + 5]),
-                       pack2<BF16>(sv[xx][q8 * 8 + 6], sv[xx][q8 * 8 + 7]));
-        }
+        for (int c = 0; c < 16; ++c) pk[xx][c] = pack2<BF16>(sv[xx][2 * c], sv[xx][2 * c + 1]);
       }
-      fence_proxy_async_smem();
+      if (!warp_wait(&p_free[sb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+      tc_fence_after();
+      tmem_st16(tm_p0 + sb * 64 + half * 32 + lane_base, pk[0]);
+      tmem_st16(tm_p0 + sb * 64 + half * 32 + 16 + lane_base, pk[1]);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
       // each warp keeps the row sum of its own columns (same scale m in both);
