@@ -16,6 +16,8 @@
 //   per KV tile, query chunks in ascending order: deterministic.
 #pragma once
 
+#include <climits>
+
 #include "attn_fwd.cuh"
 #include "common.cuh"
 #include "plan.cuh"
@@ -926,7 +928,12 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       };
       int issued = 0, published = 0;  // in this warp's own chunk sequence of this item
       int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
-      int gcur = 0;                   // group cursor (grouped path)
+      // grouped path: this lane's current cache entry (index, first group,
+      // next entry's first group, windows, first query, query mask)
+      int e_lo = -1, e_gs = 0, e_gnext = 0, e_tq0 = 0;
+      uint32_t e_wm = 0u;
+      uint4 e_mask = make_uint4(0u, 0u, 0u, 0u);
+      const int rc_n = grouped ? rc.n : 0, rc_groups = grouped ? rc.groups : 0;
       const int n_chunks = w.n_chunks;
       if (pw < nprod) {
         for (int c = pw; c < n_chunks; c += nprod) {
@@ -944,13 +951,25 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             uint32_t bits = 0u;
             if (lane < 8) {
               const int gg = 8 * c + lane;
-              if (gg < rc.groups) {
-                int lo = gcur;
-                while (lo + 1 < rc.n && rc.gstart[lo + 1] <= gg) ++lo;
-                gcur = lo;
-                const int wdx = nth_set_bit((uint32_t)rc.wmask[lo], gg - rc.gstart[lo]);
-                tok = rc.tq0[lo] + wdx * W;
-                bits = window_bits(rc.mask[lo], wdx, W);
+              if (gg < rc_groups) {
+                // the lane's entry only moves forward: step over gstart alone,
+                // then fetch the entry's fields once (shared-memory loads are
+                // slow while the tensor pipe streams its operands)
+                bool moved = false;
+                while (e_gnext <= gg) {
+                  ++e_lo;
+                  e_gs = e_gnext;
+                  e_gnext = e_lo + 1 < rc_n ? rc.gstart[e_lo + 1] : INT_MAX;
+                  moved = true;
+                }
+                if (moved) {
+                  e_wm = (uint32_t)rc.wmask[e_lo];
+                  e_tq0 = rc.tq0[e_lo];
+                  e_mask = rc.mask[e_lo];
+                }
+                const int wdx = nth_set_bit(e_wm, gg - e_gs);
+                tok = e_tq0 + wdx * W;
+                bits = window_bits(e_mask, wdx, W);
               }
             }
 #pragma unroll

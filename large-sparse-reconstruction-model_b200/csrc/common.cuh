@@ -477,29 +477,38 @@ __device__ __forceinline__ int union_cache_chunk(const UnionCache& uc, int j, in
 // Issues the TMA loads of one chunk's groups, lanes in parallel.  Runs of
 // groups contiguous in memory (or runs of unused groups, read past the end of
 // the tensor: zero fill) are split greedily into power-of-two boxes
-// (8 << i rows, maps[i]); the lane of each box's first group issues it.
-// `r` is the lane's group's first token (-1 unused); consecutive groups of a
-// run are `step` tokens apart (a group is 8 rows: 8 tokens of one head, or
-// 8/G tokens of G heads).  Warp-wide; the caller has armed `bar` with the
+// (8 << i rows, maps[i]); the box's first group's lane g issues its first
+// operand and lane g + NG its second in the same instruction (a TMA issue
+// holds the issuing warp ~150-300 cycles; lanes that issue together share
+// it).  `r` is lane g's group's first token (-1 unused); consecutive groups
+// of a run are `step` tokens apart (a group is 8 rows: 8 tokens of one head,
+// or 8/G tokens of G heads).  Warp-wide; the caller has armed `bar` with the
 // chunk's bytes.
 template <int NG, int RB>
 __device__ __forceinline__ void issue_group_runs(int r, uint8_t* dK, uint8_t* dV, const CUtensorMap* maps_k,
                                                  const CUtensorMap* maps_v, int h, int oob_row, uint64_t* bar,
                                                  int step = 8) {
+  static_assert(2 * NG <= 32, "two lanes per group");
   const int lane = threadIdx.x & 31;
   const int prev = __shfl_up_sync(0xffffffffu, r, 1);
   const bool cont = lane > 0 && lane < NG && ((r >= 0 && prev == r - step) || (r < 0 && prev < 0));
   const uint32_t starts = __ballot_sync(0xffffffffu, lane < NG && !cont) | (1u << NG);
+  int go = 0, hb = 0;
   if (lane < NG) {
     const int s0 = 31 - __clz(starts & ((2u << lane) - 1u));        // this run's first group
     const int s1 = __ffs(starts & ~((2u << lane) - 1u)) - 1;         // next run's first group
     const int n = s1 - s0, d = lane - s0;
-    const int hb = 31 - __clz(n - d);                                // largest box that fits
-    if (d == ((n >> (hb + 1)) << (hb + 1))) {
-      const int row = r >= 0 ? r : oob_row;
-      tma_load_3d(dK + lane * 8 * RB, &maps_k[hb], 0, h, row, bar);
-      tma_load_3d(dV + lane * 8 * RB, &maps_v[hb], 0, h, row, bar);
-    }
+    hb = 31 - __clz(n - d);                                          // largest box that fits
+    go = d == ((n >> (hb + 1)) << (hb + 1));
+  }
+  const int g = lane < NG ? lane : lane - NG;
+  go = __shfl_sync(0xffffffffu, go, g);
+  hb = __shfl_sync(0xffffffffu, hb, g);
+  const int rg = __shfl_sync(0xffffffffu, r, g);
+  if (lane < 2 * NG && go) {
+    const bool second = lane >= NG;
+    tma_load_3d((second ? dV : dK) + g * 8 * RB, second ? &maps_v[hb] : &maps_k[hb], 0, h, rg >= 0 ? rg : oob_row,
+                bar);
   }
 }
 
