@@ -75,8 +75,8 @@ struct DqSmem {
   static constexpr int OFF_META = OFF_V + STAGES * KTILE;  // dS lives in TMEM
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(DqMeta);
   // kv_full[S], kv_empty[S], qdo_full[2], qdo_empty[2], sd_full[2], sd_free[2],
-  // ds_full[2], ds_free[2], dq_done, dq_free, mma_done, dq_mma_done
-  static constexpr int NBAR = 2 * STAGES + 4 + 8 + 4;
+  // ds_full[2], ds_free[2], dq_done, dq_free, mma_done, dq_mma_done, uc_empty, uc_full
+  static constexpr int NBAR = 2 * STAGES + 4 + 8 + 6;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
@@ -120,9 +120,9 @@ __device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, 
 }
 
 // Threads of the dQ kernel: 8 compute warps (two per TMEM lane quarter,
-// splitting the 64 key columns of a chunk), a producer warp and two
-// MMA-issuing warps (S / dP, and the dQ accumulation).
-constexpr int kDqThreads = 352;
+// splitting the 64 key columns of a chunk), two producer warps (8 and 11,
+// alternate chunks) and two MMA-issuing warps (9: S / dP, 10: dQ).
+constexpr int kDqThreads = 384;
 
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kDqThreads, 1)
@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint64_t* dq_free = dq_done + 1;
   uint64_t* mma_done = dq_free + 1;
   uint64_t* dq_mma_done = mma_done + 1;
+  uint64_t* uc_empty = dq_mma_done + 1;  // both producer warps are done with the union cache (count 2)
+  uint64_t* uc_full = uc_empty + 1;      // warp 8 has filled it for the next item (count 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -203,6 +205,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     mbar_init(dq_free, 8);
     mbar_init(mma_done, 1);
     mbar_init(dq_mma_done, 1);
+    mbar_init(uc_empty, 2);
+    mbar_init(uc_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -218,37 +222,65 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   // dS 0/1 [384,416) [416,448): 16-bit pairs, the A operand of the dQ product
   const uint32_t tm_s0 = tmem, tm_dp0 = tmem + 128, tm_dq = tmem + 256, tm_ds = tmem + 384;
 
-  if (warp == 8) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_do);
-    }
-    if (lane < kNumBoxes) {
-      tma_prefetch_desc(&kv.k[lane]);
-      tma_prefetch_desc(&kv.v[lane]);
+  if (warp == 8 || warp == 11) {
+    // ------------------------------ producers -----------------------------
+    // Warp 8 loads each item's Q / dO tiles and fills the union cache (the
+    // two warps hand it over through uc_empty / uc_full); the warps then lay
+    // out and load alternate chunks.  Dense modes: alternate chunks, one box
+    // per operand.  A select-mode union too large for the cache is walked by
+    // lane 0 of warp 8 alone.
+    const int pw = warp == 8 ? 0 : 1;
+    if (pw == 0) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_do);
+      }
+      if (lane < kNumBoxes) {
+        tma_prefetch_desc(&kv.k[lane]);
+        tma_prefetch_desc(&kv.v[lane]);
+      }
     }
     UnionCache& uc = *reinterpret_cast<UnionCache*>(smem + L::OFF_UC);
-    int J = 0, issued = 0, it_n = 0, q_loads = 0;
+    int Jbase = 0, it_n = 0, q_loads = 0, cache_uses = 0;
+    int hist[STAGES];  // this warp's last STAGES issued chunks (teardown drain), newest first
+#pragma unroll
+    for (int k = 0; k < STAGES; ++k) hist[k] = -1;
+    auto note_issued = [&](int J) {
+#pragma unroll
+      for (int k = STAGES - 1; k > 0; --k) hist[k] = hist[k - 1];
+      hist[0] = J;
+    };
     bool ok = true;
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
       const Item w = item_of(i);
       const QTile& tile = w.tile;
       const int h = w.h, qb = it_n & 1;
-      if (!warp_wait(&qdo_empty[qb], ((it_n >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&qdo_full[qb], 2 * L::QTILE);
-        tma_load_3d(sQ + qb * L::QTILE, &tm_q, 0, h * G, tile.q_start, &qdo_full[qb]);
-        tma_load_3d(sDO + qb * L::QTILE, &tm_do, 0, h * G, tile.q_start, &qdo_full[qb]);
+      if (pw == 0) {
+        if (!warp_wait(&qdo_empty[qb], ((it_n >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qdo_full[qb], 2 * L::QTILE);
+          tma_load_3d(sQ + qb * L::QTILE, &tm_q, 0, h * G, tile.q_start, &qdo_full[qb]);
+          tma_load_3d(sDO + qb * L::QTILE, &tm_do, 0, h * G, tile.q_start, &qdo_full[qb]);
+        }
+        q_loads = it_n + 1;
       }
-      q_loads = it_n + 1;
-      bool cached = false;
-      if constexpr (MODE == kSelect)
-        cached = union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens,
-                                  tile.kv_lo, tile.kv_hi);
+      const bool cached = MODE == kSelect && w.U <= kUnionCacheCap;
       if (cached) {
+        const uint32_t par = cache_uses & 1;
+        ++cache_uses;
+        if (lane == 0) mbar_arrive(uc_empty);
+        if (pw == 0) {
+          if (!warp_wait(uc_empty, par, abort_flag, prm.err)) { ok = false; break; }
+          union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens, tile.kv_lo,
+                           tile.kv_hi);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(uc_full);
+        } else {
+          if (!warp_wait(uc_full, par, abort_flag, prm.err)) { ok = false; break; }
+        }
         int ucur = 0;
-        for (int j = 0; j < w.n_chunks; ++j, ++J) {
-          const int s = J % STAGES;
+        for (int j = pw; j < w.n_chunks; j += 2) {
+          const int J = Jbase + j, s = J % STAGES;
           if (!warp_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           DqMeta& mt = meta[s];
           const int r = union_cache_chunk<kDqGroups>(uc, j, mt.row0, mt.qmask, mt.colmask, ucur);
@@ -257,42 +289,52 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           __syncwarp();
           issue_group_runs<kDqGroups, RB>(r, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
                                           &kv_full[s]);
-          issued = J + 1;
+          note_issued(J);
         }
-      } else {
+      } else if (MODE != kSelect) {
+        for (int j = pw; j < w.n_chunks; j += 2) {
+          const int J = Jbase + j, s = J % STAGES;
+          if (!warp_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          if (lane == 0) {
+            DqMeta& mt = meta[s];
+            const int k0 = tile.kv_lo + j * kDqChunk;
+            mt.kv_start = k0;
+            mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
+            mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+            tma_load_3d(sK + s * L::KTILE, &kv.k[3], 0, h, k0, &kv_full[s]);  // 64-row box
+            tma_load_3d(sV + s * L::KTILE, &kv.v[3], 0, h, k0, &kv_full[s]);
+          }
+          note_issued(J);
+        }
+      } else if (pw == 0) {
         if (lane == 0) {
           int u = -1, tcur = 0, tend = 0;
-          for (int j = 0; j < w.n_chunks; ++j, ++J) {
-            const int s = J % STAGES;
+          for (int j = 0; j < w.n_chunks; ++j) {
+            const int J = Jbase + j, s = J % STAGES;
             if (!mbar_wait(&kv_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
             DqMeta& mt = meta[s];
-            uint8_t* dK = sK + s * L::KTILE;
-            uint8_t* dV = sV + s * L::KTILE;
-            if constexpr (MODE == kSelect) {
-              walk_union_groups<kDqGroups>(u, tcur, tend, w.U, prm.union_blk, prm.union_mask, w.ubase,
-                                           prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
-                                           mt.colmask);
-              mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-              load_group_runs<kDqGroups, RB>(mt.row0, dK, dV, kv.k, kv.v, h, prm.total_k, &kv_full[s]);
-            } else {
-              const int k0 = tile.kv_lo + j * kDqChunk;
-              mt.kv_start = k0;
-              mt.n_valid = min(kDqChunk, tile.kv_hi - k0);
-              mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
-              tma_load_3d(dK, &kv.k[3], 0, h, k0, &kv_full[s]);  // 64-row box
-              tma_load_3d(dV, &kv.v[3], 0, h, k0, &kv_full[s]);
-            }
-            issued = J + 1;
+            walk_union_groups<kDqGroups>(u, tcur, tend, w.U, prm.union_blk, prm.union_mask, w.ubase,
+                                         prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
+                                         mt.colmask);
+            mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
+            load_group_runs<kDqGroups, RB>(mt.row0, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
+                                           &kv_full[s]);
+            note_issued(J);
           }
         }
-        J = __shfl_sync(0xffffffffu, J, 0);
-        issued = __shfl_sync(0xffffffffu, issued, 0);
         ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+#pragma unroll
+        for (int k = 0; k < STAGES; ++k) hist[k] = __shfl_sync(0xffffffffu, hist[k], 0);
       }
+      Jbase += w.n_chunks;
     }
+    // Teardown after an abort: let this warp's issued copies land before the CTA exits.
     if (lane == 0 && *abort_flag) {
-      for (int k = max(0, q_loads - 2); k < q_loads; ++k) mbar_wait_drain(&qdo_full[k & 1], (k >> 1) & 1);
-      for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait_drain(&kv_full[j % STAGES], (j / STAGES) & 1);
+      if (pw == 0)
+        for (int k = max(0, q_loads - 2); k < q_loads; ++k) mbar_wait_drain(&qdo_full[k & 1], (k >> 1) & 1);
+#pragma unroll
+      for (int k = 0; k < STAGES; ++k)
+        if (hist[k] >= 0) mbar_wait_drain(&kv_full[hist[k] % STAGES], (hist[k] / STAGES) & 1);
     }
     __syncwarp();
   } else if (warp == 9) {
