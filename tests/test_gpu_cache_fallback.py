@@ -3,7 +3,9 @@ shared-memory caches, so the producers walk them from global memory:
 
 * a query tile whose union of selected blocks has more than 512 entries
   (forward and dQ union cache), and
-* a KV block selected by more than 1024 query tiles (dK/dV reverse-map cache).
+* a KV block selected by more than 1024 query tiles (dK/dV reverse-map cache),
+* a KV block with more than 4096 8-row query windows (dK/dV window list) but
+  few enough reverse entries for the reverse-map cache.
 
 Checked against a gather-based fp32 torch reference of the same op (each query
 attends the tokens of its selected blocks), forward and backward."""
@@ -74,6 +76,7 @@ CASES = [
     # name, N, L, Hq, Hkv, D, picks, popular
     ("union_over_512", 4096, 4, 1, 1, 64, 8, False),        # ~645 blocks per 128-query tile
     ("reverse_over_1024", 20000, 4, 8, 1, 64, 4, True),     # block 0 in all 1250 16-query tiles
+    ("windows_over_4096", 40000, 4, 1, 1, 64, 4, True),     # block 0: 313 tiles, ~5000 8-query windows
 ]
 
 
