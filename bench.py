@@ -7,8 +7,9 @@ one synthetic voxel sequence (BASELINE config 2 by default): block-mean
 compression of K/V, compressed attention, bit-exact per-query-block top-16
 scoring (own block forced), selected-block attention, sliding window 512,
 per-head sigmoid-gated merge, then the backward of everything.
-Rank r of N processes its own sequence (weak scaling, no collective on the
-data path).  Prints one JSON line on rank 0.
+With N > 1 processes the same sequence is split over the ranks by Ulysses
+sequence parallelism (strong scaling: NCCL all-to-all exchanges of q/k/v and
+the outputs).  Prints one JSON line on rank 0.
 """
 
 from __future__ import annotations
@@ -132,9 +133,14 @@ def forward_backward(p: Problem, want_loss=False, capture=None):
         capture["block_topk"] = bt
     o_s, _ = F.select_attention(p.q, p.k, p.v, bt, meta, None, p.cu_blk)
     o_w, _ = F.dense_attention(p.q, p.k, p.v, meta, ops.DENSE_SLIDING, cfg["window"])
+    ready = getattr(p, "ready", None)  # e2e run: the copies of x and g may still be in flight
+    if ready:
+        torch.cuda.current_stream().wait_event(ready["x"])
     z = torch.nn.functional.linear(p.x, p.wg)
     out = F.gate_merge(z, [o_c.view(N, -1), o_s.view(N, -1), o_w.view(N, -1)], per_head=cfg["gate"] == "per_head",
                        head_dim=D)
+    if ready:
+        torch.cuda.current_stream().wait_event(ready["g"])
     loss = (out.float() * p.g.float()).sum() if want_loss else None
     out.backward(p.g)
     return loss
@@ -456,22 +462,41 @@ def run_ours(args, cfg):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         copy_stream = torch.cuda.Stream(device=dev)
 
+        partial = isinstance(p, Problem)  # single GPU: x and g are awaited where the step first uses them
+        names = {2: "qkv", 3: "x", 4: "g"}
+
         def fetch():
-            # this step's inputs, pinned host -> device on the copy stream
+            # this step's inputs, pinned host -> device on the copy stream: block
+            # tables, q, k, v first (the first kernels use them), then x and g
+            hs = p.host_inputs()
+            order = list(range(5, len(hs))) + [0, 1, 2, 3, 4] if partial else list(range(len(hs)))
+            ts = [None] * len(hs)
+            evs = {}
             with torch.cuda.stream(copy_stream):
-                ts = [h.to(dev, non_blocking=True) for h in p.host_inputs()]
-                ev = torch.cuda.Event()
-                ev.record(copy_stream)
-            return ts, ev
+                for j in order:
+                    ts[j] = hs[j].to(dev, non_blocking=True)
+                    if partial and j in names:
+                        evs[names[j]] = torch.cuda.Event()
+                        evs[names[j]].record(copy_stream)
+                evs["all"] = torch.cuda.Event()
+                evs["all"].record(copy_stream)
+            return ts, evs
+
+        def take(nx):
+            ts, evs = nx
+            if partial:
+                stream.wait_event(evs["qkv"])
+                p.ready = {"x": evs["x"], "g": evs["g"]}
+            else:
+                stream.wait_event(evs["all"])
+            for t in ts:
+                t.record_stream(stream)
+            p.adopt(ts)
 
         # one untimed round trip first: the allocator then holds the buffers of
         # two steps' inputs (the prefetch keeps two alive)
         for _ in range(2):
-            ts, ev = fetch()
-            stream.wait_event(ev)
-            for t in ts:
-                t.record_stream(stream)
-            p.adopt(ts)
+            take(fetch())
             nxt_w = fetch()
             loss = step(p, want_loss=True)
             float(loss.item())
@@ -479,22 +504,31 @@ def run_ours(args, cfg):
             del nxt_w
         torch.cuda.synchronize()
         step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(e_steps + 1)]
+        # each step's loss goes device -> pinned host on the compute stream; the
+        # host reads it one step later, so it never stalls the GPU between steps
+        loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+        loss_ev = [torch.cuda.Event() for _ in range(2)]
+        losses = []
         e0.record(stream)
         nxt = fetch()
         for i in range(e_steps):
-            ts, ev = nxt
-            stream.wait_event(ev)
-            for t in ts:
-                t.record_stream(stream)
-            p.adopt(ts)
+            take(nxt)
             if i + 1 < e_steps:
                 nxt = fetch()  # the next step's copy overlaps this step's compute
             loss = step(p, want_loss=True)
-            float(loss.item())  # device -> host read of the step's result
+            loss_host[i & 1].copy_(loss.detach().float(), non_blocking=True)  # device -> host: the step's result
+            loss_ev[i & 1].record(stream)
             zero_grads(p)
             step_ev[i + 1].record(stream)
+            if i >= 1:
+                loss_ev[(i - 1) & 1].synchronize()
+                losses.append(float(loss_host[(i - 1) & 1]))
         e1.record(stream)
+        loss_ev[(e_steps - 1) & 1].synchronize()
+        losses.append(float(loss_host[(e_steps - 1) & 1]))
         torch.cuda.synchronize()
+        p.ready = None
+        assert len(losses) == e_steps and all(math.isfinite(x) for x in losses), "non-finite loss in the e2e run"
         e_ms = e0.elapsed_time(e1) / e_steps
         per_step = [e0.elapsed_time(step_ev[1])] + [step_ev[i].elapsed_time(step_ev[i + 1])
                                                    for i in range(1, e_steps)]
@@ -507,7 +541,8 @@ def run_ours(args, cfg):
         e2e = {"value": flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": p.h2d_bytes(), "d2h_bytes_per_step": 4,
                "note": "every step copies its inputs from pinned host memory (copy stream, overlapped with the "
-                       "previous step's compute) and reads its loss back"}
+                       "previous step's compute) and copies its loss back to pinned host memory (read by the "
+                       "host one step later)"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
