@@ -591,6 +591,132 @@ def traffic_for(kernel):
     return None
 
 
+# ---------------------------------------------------------------------------
+# --path volume_output: VolTransformer.prepare_volume_output (the decoder's
+# output formatting, models_sparse/voldecoder.py:196-268)
+# ---------------------------------------------------------------------------
+
+VOLUME_CFG = dict(n=131072, res=256, upsample=2, channels=32)  # cfg2's voxel shell; the VolUpsampler default of 32
+
+
+def volume_problem(seed):
+    from lsrm_sparse import synth
+
+    c = VOLUME_CFG
+    vox, shell = synth.sdf_shell_voxels(c["res"], c["n"], seed)  # [n, 3] x, y, z, Morton order
+    n = vox.shape[0]
+    vidx = torch.zeros(n, 4, dtype=torch.int32)
+    vidx[:, 1], vidx[:, 2], vidx[:, 3] = (torch.from_numpy(vox[:, j].copy()) for j in (2, 1, 0))
+    g = torch.Generator().manual_seed(seed)
+    vol = torch.randn(n, c["channels"] * c["upsample"] ** 3, generator=g).bfloat16()
+    return vol, vidx, shell
+
+
+def volume_bytes(n):
+    """Algorithmic HBM bytes of one call: the -1 fill of the index volume,
+    the feature transpose (read + write), the index reads (boundary and
+    scatter passes) and one 4-byte index write per sub-voxel."""
+    c = VOLUME_CFG
+    S, R = c["upsample"] ** 3, c["res"] * c["upsample"]
+    return R ** 3 * 4 + 2 * n * c["channels"] * S * 2 + 2 * n * 16 + n * S * 4
+
+
+def volume_cpu_sample(vol, vidx, n_tok):
+    import oracle
+
+    c = VOLUME_CFG
+    t0 = time.perf_counter()
+    oracle.prepare_volume_output(vol[:n_tok].float().numpy(), vidx[:n_tok].numpy(), c["channels"], c["upsample"],
+                                 c["res"], batch_size=1)
+    dt = time.perf_counter() - t0
+    return dict(value=volume_bytes(n_tok) / dt / 1e9, unit="GB/s", cores=1, kind="port",
+                sample=f"{n_tok} of {vidx.shape[0]} tokens (full {c['res'] * c['upsample']}^3 index volume), numpy "
+                       f"oracle on one host thread", seconds=dt)
+
+
+def run_volume_output(args):
+    ws, rank, local = dist_env()
+    if rank != 0:  # single-GPU path: the other ranks have nothing to do
+        return
+    c = VOLUME_CFG
+    vol_h, vidx_h, shell = volume_problem(args.seed)
+    n = vidx_h.shape[0]
+    base = {"metric": "prepare_volume_output HBM throughput (algorithmic bytes / time)", "unit": "GB/s",
+            "higher_is_better": True,
+            "config": {"workload": f"prepare_volume_output, {n} voxel tokens of a {c['res']}^3 SDF shell, upsample "
+                                   f"x{c['upsample']}, {c['channels']} channels bf16, batch 1",
+                       "l2": "the 537 MB index volume written every call is larger than L2"}}
+    if args.impl == "reference":
+        sample = 2048
+        for _ in range(min(args.warmup, 1)):
+            volume_cpu_sample(vol_h, vidx_h, sample)
+        vals = [volume_cpu_sample(vol_h, vidx_h, sample) for _ in range(args.steps)]
+        v = statistics.median(r["value"] for r in vals)
+        cb = dict(vals[0])
+        cb["value"] = v
+        cb.pop("seconds", None)
+        line = dict(base, impl="reference", value=v, n_gpus=ws, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=statistics.median(r["seconds"] for r in vals) * 1e3, scaling="weak",
+                    vs_baseline=None, dtype="u8", data="synthetic", cpu_baseline=cb,
+                    e2e={"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return
+    from lsrm_sparse import _lib
+    from lsrm_sparse import ops
+    from lsrm_sparse import volume as V
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    vol_h, vidx_h = vol_h.pin_memory(), vidx_h.pin_memory()
+    vol, vidx = vol_h.to(dev), vidx_h.to(dev)
+    prior = torch.zeros(1, device=dev)
+    call = lambda v, i: V.prepare_volume_output(v, i, prior, c["channels"], c["upsample"], c["res"], batch_size=1)
+    for _ in range(args.warmup):
+        call(vol, vidx)
+    assert ops.read_errors() == 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            call(vol, vidx)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = volume_bytes(n)
+    value = nbytes / (ms * 1e-3) / 1e9
+    peaks, kind = load_peaks()
+    # end to end: the call's inputs from pinned host memory, its boundaries back
+    cu_h = torch.empty(2, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = call(vol_h.to(dev, non_blocking=True), vidx_h.to(dev, non_blocking=True))
+        cu_h.copy_(out["cu_seqlens"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    assert ops.read_errors() == 0 and int(cu_h[1]) == n * c["upsample"] ** 3
+    e_ms = e0.elapsed_time(e1) / args.steps
+    cpu = None
+    if not args.no_cpu:
+        cpu = volume_cpu_sample(vol_h, vidx_h, 2048)
+        cpu.pop("seconds", None)
+    line = dict(base, value=value, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, scaling="weak",
+                vs_baseline=None, dtype="u8",
+                data=f"synthetic: seeded random-sphere SDF shell ({shell} shell voxels, subsampled), features N(0,1)",
+                roofline={"kernel": "volume_output", "bound": "hbm", "achieved": value, "peak": peaks["hbm_gbs"],
+                          "unit": "GB/s", "frac": value / peaks["hbm_gbs"], "traffic": None,
+                          "peak_source": f"hbm_gbs of {kind}"},
+                cpu_baseline=cpu,
+                e2e={"value": nbytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e_ms,
+                     "h2d_bytes_per_step": int(vol_h.numel() * 2 + vidx_h.numel() * 4), "d2h_bytes_per_step": 8},
+                gpu_launches=int(launches), clocks=clk.summary())
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -602,10 +728,15 @@ def main():
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--path", choices=["attention", "volume_output"], default="attention",
+                    help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
+                         "decoder's output formatting (prepare_volume_output)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
-    if args.impl == "reference":
+    if args.path == "volume_output":
+        run_volume_output(args)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_ours(args, cfg)

@@ -289,6 +289,27 @@ int lsrm_ulysses_unpack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, i
                         const void* src, int64_t dst_token_stride, void* dst, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Volume output preparation (models_sparse/voldecoder.py:196-268)          */
+/* ---------------------------------------------------------------------- */
+/* VolTransformer.prepare_volume_output on the device, no host sync.
+ * volume: [n_tokens, channels * u^3] elements of elem_bytes (2 or 4), each
+ * token's features channel-major (c * u^3 + s); volume_index: [n_tokens, 4]
+ * int32 (batch, z, y, x), grouped by ascending batch id in [0, batch_size),
+ * coordinates in [0, vol_res), unique per batch element (the reference's
+ * assumptions; a batch id without tokens gets an empty range).  Writes
+ *   sparse_feat  [n_tokens * u^3, channels]: row i * u^3 + s is token i's
+ *                sub-voxel s = (dz * u + dy) * u + dx,
+ *   cu_seqlens   [batch_size + 1] and seqlens [batch_size], in sub-voxels,
+ *   index_volume [batch_size, R, R, R] int32 (R = vol_res * u): -1, or the
+ *                sequence-local row of the sub-voxel at (z*u+dz, y*u+dy, x*u+dx).
+ * Out-of-range batch ids or coordinates, or tokens not grouped by batch, set
+ * LSRM_ERR_BAD_INDEX in err_flags (required) and are skipped. */
+int lsrm_prepare_volume_output(const void* volume, int32_t elem_bytes, const int32_t* volume_index, int64_t n_tokens,
+                               int32_t channels, int32_t upsample_scale, int32_t vol_res, int32_t batch_size,
+                               void* sparse_feat, int32_t* cu_seqlens, int32_t* seqlens, int32_t* index_volume,
+                               int* err_flags, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Self-test of the tcgen05 / TMA building blocks (used by the GPU tests)   */
 /* ---------------------------------------------------------------------- */
 /* a, b, v: [128, D] bf16; p: [128, 128] bf16; c1 = a @ b^T [128,128] fp32,

@@ -55,6 +55,7 @@ __all__ = [
     "three_branch_sample_step",
     "volume_sort_keys",
     "block_separation",
+    "prepare_volume_output",
 ]
 
 
@@ -709,3 +710,37 @@ def block_separation(coords, dim: int, block_size, batch: int, resolution):
     allc = np.concatenate(counts) if counts else np.zeros(0, np.int64)
     cu_blk = np.concatenate([[0], np.cumsum(allc)]).astype(np.int32)
     return cu_sb, cu_blk
+
+
+def prepare_volume_output(volume, volume_index, output_dim: int, upsample_scale: int, vol_res: int,
+                          batch_size: Optional[int] = None):
+    """``VolTransformer.prepare_volume_output`` (models_sparse/voldecoder.py:
+    196-268), restated in numpy with explicit loops over tokens and
+    sub-voxels.  ``volume`` [N, C * u^3] (token i's features channel-major,
+    element c * u^3 + s), ``volume_index`` [N, 4] (batch, z, y, x) grouped by
+    batch.  Sub-voxel s = (dz * u + dy) * u + dx (:210-230, meshgrid "ij").
+    Returns ``(sparse_feat [N * u^3, C], cu_seqlens, seqlens,
+    index_volume [B, R*u, R*u, R*u])``; batch boundaries are where the batch
+    id changes (:232-241), scaled by u^3 (:242); the index volume holds the
+    sub-voxel's row inside its sequence, -1 elsewhere (:246-259)."""
+    vol = np.asarray(volume)
+    vi = np.asarray(volume_index).astype(np.int64)
+    n = vi.shape[0]
+    u = int(upsample_scale)
+    S = u ** 3
+    C = int(output_dim)
+    B = int(vi[:, 0].max()) + 1 if batch_size is None else int(batch_size)
+    feat = vol.reshape(n, C, S).transpose(0, 2, 1).reshape(n * S, C).copy()
+    starts = [0] + [i for i in range(1, n) if vi[i, 0] != vi[i - 1, 0]] + [n]
+    cu = np.array(starts, dtype=np.int64) * S
+    cu = cu.astype(np.int32)
+    seqlens = (cu[1:] - cu[:-1]).astype(np.int32)
+    R = int(vol_res) * u
+    index_volume = np.full((B, R, R, R), -1, dtype=np.int32)
+    for b in range(B):
+        t0, t1 = int(cu[b]) // S, int(cu[b + 1]) // S
+        for i in range(t0, t1):
+            for s in range(S):
+                dz, dy, dx = s // (u * u), (s // u) % u, s % u
+                index_volume[b, vi[i, 1] * u + dz, vi[i, 2] * u + dy, vi[i, 3] * u + dx] = (i - t0) * S + s
+    return feat, cu, seqlens, index_volume

@@ -220,16 +220,48 @@ def make_block_metadata(sparse_utils, seed):
                 img_cu_block_include_tokens=img_blk.numpy().astype(np.int32))
 
 
+def make_volume_output(voldecoder, seed):
+    """VolTransformer.prepare_volume_output (models_sparse/voldecoder.py:196-268)
+    run on the CPU through the reference method itself (a stand-in `self`
+    carrying output_dim / upsample_scale / vol_res): three batch elements of
+    unique voxels in shuffled order (grouped by batch), u = 2, 8 channels, a
+    16^3 token grid."""
+    import types
+
+    gen = torch.Generator().manual_seed(seed)
+    res, u, C = 16, 2, 8
+    parts = []
+    for b, n in enumerate((150, 37, 200)):
+        flat = torch.randperm(res ** 3, generator=gen)[:n]
+        z, y, x = flat // (res * res), (flat // res) % res, flat % res
+        parts.append(torch.stack([torch.full_like(z, b), z, y, x], 1))
+    vidx = torch.cat(parts).to(torch.int32)
+    volume = torch.randn(vidx.shape[0], C * u ** 3, generator=gen)
+    prior = torch.zeros(1)
+    me = types.SimpleNamespace(output_dim=C, upsample_scale=u, vol_res=res)
+    out = voldecoder.VolTransformer.prepare_volume_output(me, volume, vidx, prior)
+    return dict(volume=volume.numpy(), volume_index=vidx.numpy(), output_dim=np.int32(C), upsample_scale=np.int32(u),
+                vol_res=np.int32(res), sparse_feat=out["sparse_feat"].numpy(),
+                cu_seqlens=out["cu_seqlens"].numpy().astype(np.int32), seqlens=out["seqlens"].numpy().astype(np.int32),
+                index_volume=out["index_volume"].numpy().astype(np.int32))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks"], default=None, help="regenerate one group of fixtures")
+    ap.add_argument("--only", choices=["blocks", "volume"], default=None, help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.ref)
     from misc import sparse_utils
 
+    if args.only == "volume":
+        from models_sparse import voldecoder
+
+        np.savez_compressed(os.path.join(HERE, "volume_output.npz"), **make_volume_output(voldecoder, 51))
+        print("wrote volume_output")
+        return
     np.savez_compressed(os.path.join(HERE, "block_metadata.npz"), **make_block_metadata(sparse_utils, 41))
     print("wrote block_metadata")
     if args.only == "blocks":

@@ -162,3 +162,15 @@ def test_block_metadata_matches_reference(golden):
     cu_sb, cu_blk = oracle.block_separation(g["img_coords"], 3, [1, 4, 4], 2, [3, 8, 8])
     assert np.array_equal(cu_sb, g["img_cu_seqblocks"])
     assert np.array_equal(cu_blk, g["img_cu_block_include_tokens"])
+
+
+def test_volume_output_matches_reference(golden):
+    """prepare_volume_output restated in the oracle vs the reference method's
+    own outputs (models_sparse/voldecoder.py:196-268), bit for bit."""
+    g = golden("volume_output")
+    feat, cu, seqlens, iv = oracle.prepare_volume_output(g["volume"], g["volume_index"], int(g["output_dim"]),
+                                                         int(g["upsample_scale"]), int(g["vol_res"]))
+    assert np.array_equal(feat, g["sparse_feat"])
+    assert np.array_equal(cu, g["cu_seqlens"])
+    assert np.array_equal(seqlens, g["seqlens"])
+    assert np.array_equal(iv, g["index_volume"])
