@@ -55,6 +55,51 @@ __global__ void __launch_bounds__(kTrWarps * 32) volume_transpose_kernel(const E
   }
 }
 
+// The same transpose for power-of-two C and S (the common C = 32, u = 2 or 4):
+// 16-byte loads and stores, shift / mask indexing, kTpw tokens per warp
+// iteration so that each lane keeps several loads in flight.  Requires
+// C * S * sizeof(E) % 16 == 0, C % (16 / sizeof(E)) == 0 and 16-byte
+// aligned rows.
+constexpr int kTpw = 4;
+template <typename E>
+__global__ void __launch_bounds__(kTrWarps * 32) volume_transpose_vec_kernel(const uint4* __restrict__ in,
+                                                                            uint4* __restrict__ out, long long n_tok,
+                                                                            int lgC, int lgS) {
+  extern __shared__ uint32_t tr_smem[];
+  constexpr int V = 16 / (int)sizeof(E);  // elements per 16-byte chunk
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = 1 << lgC, S = 1 << lgS, stride = S + 1;
+  const int chunks = (C << lgS) / V;  // per token
+  E* wb = reinterpret_cast<E*>(tr_smem) + (size_t)warp * kTpw * C * stride;
+  for (long long i0 = ((long long)blockIdx.x * kTrWarps + warp) * kTpw; i0 < n_tok;
+       i0 += (long long)gridDim.x * kTrWarps * kTpw) {
+    const int nt = n_tok - i0 < kTpw ? (int)(n_tok - i0) : kTpw;
+    for (int q = lane; q < nt * chunks; q += 32) {
+      const int t = q / chunks, r = q - t * chunks;
+      const uint4 x = in[(i0 + t) * chunks + r];
+      const E* e = reinterpret_cast<const E*>(&x);
+      E* tb = wb + t * C * stride;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const int k = r * V + j;
+        tb[(k >> lgS) * stride + (k & (S - 1))] = e[j];
+      }
+    }
+    __syncwarp();
+    for (int q = lane; q < nt * chunks; q += 32) {
+      const int t = q / chunks, r = q - t * chunks;
+      const int k0 = r * V, sv = k0 >> lgC, c0 = k0 & (C - 1);
+      const E* tb = wb + t * C * stride;
+      uint4 x;
+      E* e = reinterpret_cast<E*>(&x);
+#pragma unroll
+      for (int j = 0; j < V; ++j) e[j] = tb[(c0 + j) * stride + sv];
+      out[(i0 + t) * chunks + r] = x;
+    }
+    __syncwarp();
+  }
+}
+
 // cu[b] = first sub-voxel row of batch element b.  Tokens are grouped by
 // batch id in ascending order; a batch id without tokens gets an empty range.
 __global__ void volume_cu_kernel(const int32_t* __restrict__ vidx, long long n_tok, int B, int S, int32_t* cu,
@@ -74,16 +119,13 @@ __global__ void volume_cu_kernel(const int32_t* __restrict__ vidx, long long n_t
   for (int b = prev + 1; b <= cur; ++b) cu[b] = (int32_t)(i * S);
 }
 
-__global__ void volume_seqlens_kernel(const int32_t* __restrict__ cu, int B, int32_t* seqlens) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b < B) seqlens[b] = cu[b + 1] - cu[b];
-}
-
-// index_volume[b, z, y, x] = row of the sub-voxel inside its sequence.
+// index_volume[b, z, y, x] = row of the sub-voxel inside its sequence; the
+// first B threads also write seqlens (cu is complete when this kernel runs).
 __global__ void volume_scatter_kernel(const int32_t* __restrict__ vidx, long long n_sub, int u, int S, int B,
                                       int Ru, const int32_t* __restrict__ cu, int32_t* __restrict__ index_volume,
-                                      int* err) {
+                                      int32_t* __restrict__ seqlens, int* err) {
   const long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j < B) seqlens[j] = cu[j + 1] - cu[j];
   if (j >= n_sub) return;
   const long long i = j / S;
   const int s = (int)(j - i * S);
@@ -126,9 +168,43 @@ extern "C" int lsrm_prepare_volume_output(const void* volume, int32_t elem_bytes
   volume_cu_kernel<<<vo_grid(n_tokens + 1, 256), 256, 0, s>>>(volume_index, n_tokens, batch_size, (int)S, cu_seqlens,
                                                               err_flags);
   LSRM_LAUNCH_CHECK();
-  volume_seqlens_kernel<<<vo_grid(batch_size, 256), 256, 0, s>>>(cu_seqlens, batch_size, seqlens);
-  LSRM_LAUNCH_CHECK();
-  if (n_tokens == 0) return LSRM_OK;
+  if (n_tokens == 0) {  // no sub-voxel: only the (empty) lengths
+    volume_scatter_kernel<<<vo_grid(batch_size, 256), 256, 0, s>>>(volume_index, 0, upsample_scale, (int)S,
+                                                                   batch_size, (int)Ru, cu_seqlens, index_volume,
+                                                                   seqlens, err_flags);
+    LSRM_LAUNCH_CHECK();
+    return LSRM_OK;
+  }
+  const auto pow2 = [](long long x) { return x > 0 && (x & (x - 1)) == 0; };
+  const int V = 16 / elem_bytes;
+  if (pow2(channels) && pow2(S) && channels % V == 0 && ((uintptr_t)volume & 15) == 0 &&
+      ((uintptr_t)sparse_feat & 15) == 0) {
+    const int lgC = __builtin_ctz((unsigned)channels), lgS = __builtin_ctzll((unsigned long long)S);
+    const size_t vstage = (size_t)kTrWarps * kTpw * channels * (S + 1) * elem_bytes;
+    const int grid_v =
+        (int)std::min<long long>((n_tokens + kTrWarps * kTpw - 1) / (kTrWarps * kTpw), (long long)num_sms() * 8);
+    if (vstage <= 200 * 1024) {
+      if (elem_bytes == 2) {
+        if (vstage > 48 * 1024)
+          LSRM_CUDA_TRY(cudaFuncSetAttribute(volume_transpose_vec_kernel<uint16_t>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vstage));
+        volume_transpose_vec_kernel<uint16_t><<<grid_v, kTrWarps * 32, vstage, s>>>(
+            static_cast<const uint4*>(volume), static_cast<uint4*>(sparse_feat), n_tokens, lgC, lgS);
+      } else {
+        if (vstage > 48 * 1024)
+          LSRM_CUDA_TRY(cudaFuncSetAttribute(volume_transpose_vec_kernel<uint32_t>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vstage));
+        volume_transpose_vec_kernel<uint32_t><<<grid_v, kTrWarps * 32, vstage, s>>>(
+            static_cast<const uint4*>(volume), static_cast<uint4*>(sparse_feat), n_tokens, lgC, lgS);
+      }
+      LSRM_LAUNCH_CHECK();
+      volume_scatter_kernel<<<vo_grid(std::max<long long>(n_tokens * S, batch_size), 256), 256, 0, s>>>(
+          volume_index, n_tokens * S, upsample_scale, (int)S, batch_size, (int)Ru, cu_seqlens, index_volume, seqlens,
+          err_flags);
+      LSRM_LAUNCH_CHECK();
+      return LSRM_OK;
+    }
+  }
   const int grid_tr = (int)std::min<long long>((n_tokens + kTrWarps - 1) / kTrWarps, (long long)num_sms() * 8);
   if (elem_bytes == 2) {
     if (stage > 48 * 1024)
@@ -144,9 +220,9 @@ extern "C" int lsrm_prepare_volume_output(const void* volume, int32_t elem_bytes
         static_cast<const uint32_t*>(volume), static_cast<uint32_t*>(sparse_feat), n_tokens, channels, (int)S);
   }
   LSRM_LAUNCH_CHECK();
-  volume_scatter_kernel<<<vo_grid(n_tokens * S, 256), 256, 0, s>>>(volume_index, n_tokens * S, upsample_scale, (int)S,
-                                                                   batch_size, (int)Ru, cu_seqlens, index_volume,
-                                                                   err_flags);
+  volume_scatter_kernel<<<vo_grid(std::max<long long>(n_tokens * S, batch_size), 256), 256, 0, s>>>(
+      volume_index, n_tokens * S, upsample_scale, (int)S, batch_size, (int)Ru, cu_seqlens, index_volume, seqlens,
+      err_flags);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }
