@@ -722,6 +722,154 @@ def run_volume_output(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# --path volume_geo_topk: the geometric volume-to-volume block selection of
+# build_volume_to_volume_attn (misc/sparse_utils.py:1203-1279)
+# ---------------------------------------------------------------------------
+
+GEO_CFG = dict(res=64, block_size=8, topk=8, bbox_radius=0.5, batch=2)  # the reference's defaults
+
+
+def geo_problem(seed):
+    from lsrm_sparse import synth
+
+    c = GEO_CFG
+    parts = []
+    for b in range(c["batch"]):
+        vox, _ = synth.sdf_shell_voxels(c["res"], 1 << 30, seed + b)  # every shell voxel
+        t = torch.zeros(vox.shape[0], 4, dtype=torch.int32)
+        t[:, 0] = b
+        t[:, 1], t[:, 2], t[:, 3] = (torch.from_numpy(vox[:, j].copy()) for j in (2, 1, 0))
+        parts.append(t)
+    return torch.cat(parts)
+
+
+def run_volume_geo(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    import types
+
+    c = GEO_CFG
+    coords_h = geo_problem(args.seed)
+    n = coords_h.shape[0]
+    base = {"metric": "geometric volume-to-volume block selection (tokens/s)", "unit": "tokens/s",
+            "higher_is_better": True,
+            "config": {"workload": f"build_volume_to_volume_attn top-{c['topk']}: {n} voxel tokens of {c['batch']} SDF "
+                                   f"shells, {c['res']}^3 volume, {c['block_size']}^3 blocks",
+                       "l2": "inputs fit in L2; the selection is bound by distance evaluations, not memory"}}
+    from lsrm_sparse import blocks
+
+    if args.impl == "reference":
+        import oracle
+
+        cs, cb, srt = blocks_cpu_separation(coords_h)
+        sample = 2000
+        rows = np.linspace(0, n - 1, sample).astype(np.int64)
+        secs = []
+        for _ in range(max(1, args.steps)):
+            t0 = time.perf_counter()
+            oracle.volume_block_topk(srt, cs, cb, c["batch"], c["res"], c["bbox_radius"], c["topk"], rows=rows)
+            secs.append(time.perf_counter() - t0)
+        v = sample / statistics.median(secs)
+        cb_line = dict(value=v, unit="tokens/s", cores=1, kind="port",
+                       sample=f"{sample} of {n} tokens (evenly spaced), numpy oracle on one host thread (block centres "
+                              f"of the whole set included)")
+        print(json.dumps(dict(base, impl="reference", value=v, n_gpus=ws, steps=args.steps, warmup=args.warmup,
+                              ms_per_step=statistics.median(secs) * 1e3, scaling="weak", vs_baseline=None,
+                              dtype="f32", data="synthetic", cpu_baseline=cb_line,
+                              e2e={"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                   "d2h_bytes_per_step": 0})), flush=True)
+        return
+    from lsrm_sparse import _lib, ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    coords = coords_h.to(dev)
+    keys = blocks.volume_sort_keys(coords, c["res"], c["block_size"])
+    coords = coords[torch.argsort(keys, stable=True)].contiguous()
+    bs = c["block_size"]
+    cu_sb, cu_blk, _ = blocks.block_separation(coords, 3, [bs] * 3, c["batch"], [c["res"]] * 3)
+    nb = int(cu_sb[-1])
+    call = lambda: blocks.volume_block_topk(coords, cu_sb, cu_blk, c["batch"], c["res"], c["bbox_radius"], c["topk"])
+    for _ in range(args.warmup):
+        call()
+    assert ops.read_errors() == 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    value = n / (ms * 1e-3)
+    # distance evaluations: each token against every block of its batch element
+    blocks_per_elem = (cu_sb[1:] - cu_sb[:-1]).cpu().tolist()
+    counts = torch.bincount(coords_h[:, 0].long(), minlength=c["batch"]).tolist()
+    evals = sum(a * b for a, b in zip(counts, blocks_per_elem))
+    hbm_bytes = n * 16 * 2 + n * c["topk"] * 4 + nb * 12  # coordinates (two passes), selections, centres
+    peaks, kind = load_peaks()
+    # end to end through the public call: block-sorted coordinates from pinned host
+    # memory, separation + selection, the first selection row read back
+    args_ns = types.SimpleNamespace(block_size=bs, volume_res=c["res"], use_3d_aware_attn=True,
+                                    topk_volume=c["topk"], bbox_radius=c["bbox_radius"])
+    sorted_h = coords.cpu().pin_memory()
+    row_h = torch.empty(c["topk"], dtype=torch.int32).pin_memory()
+    blocks.build_volume_to_volume_attn(sorted_h.to(dev), args_ns)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        res = blocks.build_volume_to_volume_attn(sorted_h.to(dev, non_blocking=True), args_ns)
+        row_h.copy_(res["block_topk"][0, 0], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1) / args.steps
+    cpu = None
+    if not args.no_cpu:
+        import oracle
+
+        rows = np.linspace(0, n - 1, 2000).astype(np.int64)
+        t0 = time.perf_counter()
+        oracle.volume_block_topk(coords.cpu().numpy(), cu_sb.cpu().numpy(), cu_blk.cpu().numpy(), c["batch"], c["res"],
+                                 c["bbox_radius"], c["topk"], rows=rows)
+        dt = time.perf_counter() - t0
+        cpu = dict(value=2000 / dt, unit="tokens/s", cores=1, kind="port",
+                   sample=f"2000 of {n} tokens (evenly spaced), numpy oracle on one host thread (block centres of "
+                          f"the whole set included)")
+    print(json.dumps(dict(
+        base, value=value, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, scaling="weak",
+        vs_baseline=None, dtype="f32", data=f"synthetic: {c['batch']} seeded random-sphere SDF shells, {nb} blocks",
+        distance_evals_per_s=evals / (ms * 1e-3),
+        roofline={"kernel": "volume_block_topk", "bound": "hbm", "achieved": hbm_bytes / (ms * 1e-3) / 1e9,
+                  "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": hbm_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                  "traffic": None, "peak_source": f"hbm_gbs of {kind}",
+                  "note": "memory is not the bound: the kernel evaluates every (token, block) distance of a batch "
+                          "element on the fp32 pipe (distance_evals_per_s)"},
+        cpu_baseline=cpu,
+        e2e={"value": n / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+             "h2d_bytes_per_step": int(sorted_h.numel() * 4), "d2h_bytes_per_step": c["topk"] * 4},
+        gpu_launches=int(launches), clocks=clk.summary())), flush=True)
+
+
+def blocks_cpu_separation(coords_h):
+    """Block order and separation of the geometric workload with the oracle
+    (for the CPU baseline, which needs the whole set's block centres)."""
+    import oracle
+
+    c = GEO_CFG
+    keys = oracle.volume_sort_keys(coords_h.numpy(), c["res"], c["block_size"])
+    order = np.argsort(keys, kind="stable")
+    srt = coords_h.numpy()[order]
+    bs = c["block_size"]
+    cs, cb = oracle.block_separation(srt, 3, [bs] * 3, c["batch"], [c["res"]] * 3)
+    return cs, cb, srt
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -733,14 +881,17 @@ def main():
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--path", choices=["attention", "volume_output"], default="attention",
+    ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk"], default="attention",
                     help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
-                         "decoder's output formatting (prepare_volume_output)")
+                         "decoder's output formatting (prepare_volume_output); volume_geo_topk: the geometric "
+                         "volume-to-volume block selection (build_volume_to_volume_attn)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
     if args.path == "volume_output":
         run_volume_output(args)
+    elif args.path == "volume_geo_topk":
+        run_volume_geo(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -288,6 +288,21 @@ int lsrm_ulysses_pack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int
 int lsrm_ulysses_unpack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int32_t world, int32_t dtype,
                         const void* src, int64_t dst_token_stride, void* dst, void* stream);
 
+/* Geometric volume-to-volume block selection (build_volume_to_volume_attn
+ * with use_3d_aware_attn, misc/sparse_utils.py:1203-1279): coords [n, 4]
+ * int32 (batch, z, y, x) in block order, with cu_seqblocks [batch+1] and
+ * cu_block_include_tokens from lsrm_block_separation.  Each token's point is
+ * 2 * (c / (volume_res - 1) - 0.5) * radius (radius = bbox_radius * 1.05, as
+ * the reference; x, y, z from columns 3, 2, 1); block centres are the fp32
+ * sequential means of their tokens' points (written to centroids, scratch of
+ * 3 * n floats).  block_topk [n, topk] (topk <= 64): per token the topk blocks
+ * of its batch element with the smallest squared distance (ties to the lower
+ * id), as sorted sequence-local ids, -1 padding.  Batch ids out of range set
+ * LSRM_ERR_BAD_INDEX in err_flags (required). */
+int lsrm_volume_block_topk(const int32_t* coords, int64_t n_tokens, const int32_t* cu_seqblocks,
+                           const int32_t* cu_block_include_tokens, int32_t batch, int32_t volume_res, float radius,
+                           int32_t topk, float* centroids, int32_t* block_topk, int* err_flags, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Volume output preparation (models_sparse/voldecoder.py:196-268)          */
 /* ---------------------------------------------------------------------- */

@@ -126,6 +126,10 @@ _SIGS = {
     "lsrm_ulysses_unpack": (
         c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
     ),
+    "lsrm_volume_block_topk": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float, c_int32, c_void_p, c_void_p,
+                c_void_p, c_void_p]
+    ),
     "lsrm_prepare_volume_output": (
         c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
                 c_void_p, c_void_p, c_void_p, c_void_p]

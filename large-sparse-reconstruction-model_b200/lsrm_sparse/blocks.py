@@ -74,3 +74,44 @@ def block_separation(k_coords: torch.Tensor, DIM: int, block_size: Sequence[int]
     check(rc, "lsrm_block_separation")
     nb = int(nblk.item())
     return cu_seqblocks, cu_blk[: nb + 1], cu_seqlens
+
+
+def volume_block_topk(coords: torch.Tensor, cu_seqblocks: torch.Tensor, cu_block_include_tokens: torch.Tensor,
+                      batch_size: int, volume_res: int, bbox_radius: float, topk: int) -> torch.Tensor:
+    """[n, topk] int32: per voxel token the topk blocks of its batch element
+    nearest to it (block centre = mean of its voxels' points), sorted ids,
+    -1 padding.  No host synchronisation."""
+    L = _lib.lib()
+    coords = coords.to(torch.int32).contiguous()
+    if coords.dim() != 2 or coords.shape[1] != 4:
+        raise ValueError("coords must be [n, 4] (batch, z, y, x)")
+    n = coords.shape[0]
+    out = torch.empty(n, int(topk), dtype=torch.int32, device=coords.device)
+    cent = torch.empty(max(n, 1), 3, dtype=torch.float32, device=coords.device)
+    radius = float(bbox_radius) * 1.05  # as from_volcoords_to_points (misc/sparse_utils.py:645)
+    rc = L.lsrm_volume_block_topk(ops._ptr(coords), n, ops._ptr(ops._i32(cu_seqblocks)),
+                                  ops._ptr(ops._i32(cu_block_include_tokens)), int(batch_size), int(volume_res),
+                                  radius, int(topk), ops._ptr(cent), ops._ptr(out),
+                                  ops._ptr(ops._err_word(coords.device)), ops._stream())
+    check(rc, "lsrm_volume_block_topk")
+    return out
+
+
+def build_volume_to_volume_attn(volfeat_coords: torch.Tensor, args):
+    """``build_volume_to_volume_attn`` (misc/sparse_utils.py:1203-1279): the
+    block separation of the (block-sorted) voxel tokens and, with
+    ``args.use_3d_aware_attn``, the geometric top-``args.topk_volume`` block
+    selection, stacked twice as the reference does.  Same arguments and dict
+    keys; ``volfeat_coords`` is not modified.  One host synchronisation for the
+    batch size (as the reference) and one inside the separation."""
+    bs = int(args.block_size)
+    res = int(args.volume_res)
+    batch_size = int(volfeat_coords[:, 0].max().item()) + 1
+    cu_seqblocks, cu_blk, _ = block_separation(volfeat_coords, 3, [bs, bs, bs], batch_size, [res, res, res])
+    block_topk = None
+    if getattr(args, "use_3d_aware_attn", False):
+        bt = volume_block_topk(volfeat_coords, cu_seqblocks, cu_blk, batch_size, res, args.bbox_radius,
+                               args.topk_volume)
+        block_topk = torch.stack([bt, bt], dim=0)
+    return {"block_topk": block_topk, "cu_seqblocks": cu_seqblocks.to(torch.int32),
+            "cu_block_include_tokens": cu_blk.to(torch.int32)}

@@ -56,6 +56,7 @@ __all__ = [
     "volume_sort_keys",
     "block_separation",
     "prepare_volume_output",
+    "volume_block_topk",
 ]
 
 
@@ -744,3 +745,49 @@ def prepare_volume_output(volume, volume_index, output_dim: int, upsample_scale:
                 dz, dy, dx = s // (u * u), (s // u) % u, s % u
                 index_volume[b, vi[i, 1] * u + dz, vi[i, 2] * u + dy, vi[i, 3] * u + dx] = (i - t0) * S + s
     return feat, cu, seqlens, index_volume
+
+
+def volume_block_topk(coords, cu_seqblocks, cu_block_include_tokens, batch: int, volume_res: int,
+                      bbox_radius: float, topk: int, return_geometry: bool = False, rows=None):
+    """The geometric block selection of ``build_volume_to_volume_attn`` with
+    ``use_3d_aware_attn`` (misc/sparse_utils.py:1203-1279), one row per token
+    (the reference stacks the result twice, :1270).  ``coords`` [n, 4]
+    (batch, z, y, x) sorted by block (the separation's order).  In fp32, in the
+    reference's order: point = 2 * (c / (res - 1) - 0.5) * r with
+    r = bbox_radius * 1.05 and (x, y, z) from columns 3, 2, 1 (:644-650);
+    block centre = sequential sum of its points / count (segment_reduce mean,
+    :1238-1243); d^2 = (dx^2 + dy^2) + dz^2 (:1245-1249).  Blocks are ranked
+    by d^2, ties to the lower id (the reference ranks sqrt(d^2) with
+    torch.topk), the first ``topk`` ids sorted ascending, -1 padding (:1250-1266).
+    ``return_geometry`` also returns the points and block centres; ``rows``
+    (token indices) evaluates only those tokens (centres still from all)."""
+    c = np.asarray(coords).astype(np.int64)
+    cu_sb = np.asarray(cu_seqblocks).astype(np.int64)
+    cu_blk = np.asarray(cu_block_include_tokens).astype(np.int64)
+    f32 = np.float32
+    r = f32(bbox_radius * 1.05)
+    den = f32(volume_res - 1)
+
+    def pt(v):
+        return (f32(2.0) * ((v.astype(f32) / den).astype(f32) - f32(0.5))).astype(f32) * r
+
+    pts = np.stack([pt(c[:, 3]), pt(c[:, 2]), pt(c[:, 1])], 1).astype(f32)
+    nb_all = int(cu_sb[batch])
+    cent = np.zeros((nb_all, 3), f32)
+    for j in range(nb_all):
+        acc = np.zeros(3, f32)
+        for t in range(int(cu_blk[j]), int(cu_blk[j + 1])):
+            acc = (acc + pts[t]).astype(f32)
+        cent[j] = (acc / f32(cu_blk[j + 1] - cu_blk[j])).astype(f32)
+    rows = range(c.shape[0]) if rows is None else [int(x) for x in rows]
+    out = np.full((len(rows), topk), -1, dtype=np.int32)
+    for o, t in enumerate(rows):
+        b = int(c[t, 0])
+        b0, b1 = int(cu_sb[b]), int(cu_sb[b + 1])
+        d = (pts[t][None, :] - cent[b0:b1]).astype(f32)
+        sq = (d * d).astype(f32)
+        d2 = ((sq[:, 0] + sq[:, 1]).astype(f32) + sq[:, 2]).astype(f32)
+        order = np.lexsort((np.arange(b1 - b0), d2))[:topk]
+        sel = np.sort(order)
+        out[o, : sel.size] = sel
+    return (out, pts, cent) if return_geometry else out

@@ -246,16 +246,53 @@ def make_volume_output(voldecoder, seed):
                 index_volume=out["index_volume"].numpy().astype(np.int32))
 
 
+def make_volume_geo_topk(sparse_utils, seed):
+    """build_volume_to_volume_attn with use_3d_aware_attn (misc/sparse_utils.py:
+    1203-1279) on two batch elements of an SDF-shell-like voxel set, sorted
+    into blocks by sort_volume_blocks first (the reference's order).  The
+    separation's torch.histc has no CPU kernel for integer tensors: it is
+    called here on a float copy of the (integral) input, same counts."""
+    import types
+
+    gen = torch.Generator().manual_seed(seed)
+    res, bs, k = 32, 8, 8
+    parts = []
+    for b, n in enumerate((900, 400)):
+        flat = torch.randperm(res ** 3, generator=gen)[:n]
+        z, y, x = flat // (res * res), (flat // res) % res, flat % res
+        parts.append(torch.stack([torch.full_like(z, b), z, y, x], 1))
+    coords = torch.cat(parts).to(torch.int32)
+    args = types.SimpleNamespace(block_size=bs, volume_res=res, use_3d_aware_attn=True, topk_volume=k,
+                                 bbox_radius=0.5)
+    feats = torch.zeros(coords.shape[0], 1)
+    _, coords_sorted, _ = sparse_utils.sort_volume_blocks(feats, coords.clone(), args)
+    histc = torch.histc
+    torch.histc = lambda x, *a, **kw: histc(x.float(), *a, **kw)
+    try:
+        out = sparse_utils.build_volume_to_volume_attn(coords_sorted.clone(), args)
+    finally:
+        torch.histc = histc
+    return dict(coords=coords_sorted.numpy().astype(np.int32), volume_res=np.int32(res), block_size=np.int32(bs),
+                topk=np.int32(k), bbox_radius=np.float64(0.5), batch=np.int32(2),
+                block_topk=out["block_topk"].numpy(), cu_seqblocks=out["cu_seqblocks"].numpy(),
+                cu_block_include_tokens=out["cu_block_include_tokens"].numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks", "volume"], default=None, help="regenerate one group of fixtures")
+    ap.add_argument("--only", choices=["blocks", "volume", "geo"], default=None,
+                    help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.ref)
     from misc import sparse_utils
 
+    if args.only == "geo":
+        np.savez_compressed(os.path.join(HERE, "volume_geo_topk.npz"), **make_volume_geo_topk(sparse_utils, 61))
+        print("wrote volume_geo_topk")
+        return
     if args.only == "volume":
         from models_sparse import voldecoder
 

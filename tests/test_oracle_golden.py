@@ -174,3 +174,13 @@ def test_volume_output_matches_reference(golden):
     assert np.array_equal(cu, g["cu_seqlens"])
     assert np.array_equal(seqlens, g["seqlens"])
     assert np.array_equal(iv, g["index_volume"])
+
+
+def test_volume_geo_topk_matches_reference(golden):
+    """The geometric block selection restated in the oracle vs
+    build_volume_to_volume_attn's own output (misc/sparse_utils.py:1203-1279)."""
+    g = golden("volume_geo_topk")
+    out = oracle.volume_block_topk(g["coords"], g["cu_seqblocks"], g["cu_block_include_tokens"], int(g["batch"]),
+                                   int(g["volume_res"]), float(g["bbox_radius"]), int(g["topk"]))
+    assert np.array_equal(out, g["block_topk"][0])
+    assert np.array_equal(g["block_topk"][0], g["block_topk"][1])
