@@ -71,7 +71,7 @@ static int launch_dq(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap&
 template <int D, bool BF16, int MODE>
 static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const CUtensorMap& mdo,
                          const QMaps& qm, const DkvParams& p, int grid_x, int hkv, cudaStream_t s) {
-  constexpr int STAGES = 8;
+  constexpr int STAGES = 6;
   using L = DkvSmem<D, STAGES>;
   auto kern = attn_dkdv_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
