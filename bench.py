@@ -870,6 +870,122 @@ def blocks_cpu_separation(coords_h):
     return cs, cb, srt
 
 
+# ---------------------------------------------------------------------------
+# --path head_layernorm_pack: per-head LayerNorm32 fused with the Ulysses pack
+# (models_sparse/utils.py:239-270 normalisation before the exchange)
+# ---------------------------------------------------------------------------
+
+HLN_CFG = dict(n=131072, heads=16, head_dim=64, world=8)  # cfg2's q, packed for 8 ranks
+
+
+def run_head_layernorm(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    c = HLN_CFG
+    n, H, D, W = c["n"], c["heads"], c["head_dim"], c["world"]
+    g = torch.Generator().manual_seed(args.seed)
+    x_h = torch.randn(n, H, D, generator=g).bfloat16()
+    gy_h = torch.randn(W, n, H // W, D, generator=g).bfloat16()
+    elem = n * H * D * 2
+    base = {"metric": "per-head LayerNorm + Ulysses pack, forward + backward HBM throughput", "unit": "GB/s",
+            "higher_is_better": True,
+            "config": {"workload": f"head_layernorm_pack fwd + bwd of [{n}, {H}, {D}] bf16 for {W} ranks",
+                       "l2": "every tensor (268 MB) is larger than L2"}}
+    nbytes = 2 * elem + 3 * elem  # forward: read x, write packed; backward: read x and grad, write dx
+
+    def cpu_sample(reps):
+        torch.set_num_threads(os.cpu_count() or 1)
+        xs, gs = x_h[:8192], gy_h[:, :8192]
+        secs = []
+        for _ in range(max(1, reps)):
+            t0 = time.perf_counter()
+            xr = xs.float().requires_grad_()
+            y = F_layer_norm(xr, D)
+            y.to(torch.bfloat16).view(8192, W, H // W, D).permute(1, 0, 2, 3).contiguous()
+            y.backward(gs.permute(1, 0, 2, 3).reshape(8192, H, D).float())
+            secs.append(time.perf_counter() - t0)
+        v = nbytes * 8192 / n / statistics.median(secs) / 1e9
+        return dict(value=v, unit="GB/s", cores=torch.get_num_threads(), kind="port",
+                    sample=f"8192 of {n} tokens: torch fp32 layer_norm + pack + autograd backward on the host"), secs
+
+    if args.impl == "reference":
+        cb, secs = cpu_sample(args.steps)
+        v = cb["value"]
+        print(json.dumps(dict(base, impl="reference", value=v, n_gpus=ws, steps=args.steps, warmup=args.warmup,
+                              ms_per_step=statistics.median(secs) * 1e3, scaling="weak", vs_baseline=None,
+                              dtype="bf16", data="synthetic", cpu_baseline=cb,
+                              e2e={"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                   "d2h_bytes_per_step": 0})), flush=True)
+        return
+    from lsrm_sparse import _lib, ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    x, gy = x_h.to(dev), gy_h.to(dev)
+
+    def step():
+        ops.head_layernorm_pack(x, W)
+        ops.head_layernorm_pack_bwd(x, gy)
+
+    def unfused():  # the reference's order: LayerNorm32 as its own pass, then the pack
+        y = F_layer_norm(x.float(), D).to(torch.bfloat16)
+        ops.ulysses_pack(y, W)
+
+    for _ in range(args.warmup):
+        step()
+        unfused()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    e0.record(stream)
+    for _ in range(args.steps):
+        unfused()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_unfused_fwd = e0.elapsed_time(e1) / args.steps
+    value = nbytes / (ms * 1e-3) / 1e9
+    peaks, kind = load_peaks()
+    x_p, gy_p = x_h.pin_memory(), gy_h.pin_memory()
+    x_d, gy_d = torch.empty_like(x), torch.empty_like(gy)
+    out_h = torch.empty(8, dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        x_d.copy_(x_p, non_blocking=True)
+        gy_d.copy_(gy_p, non_blocking=True)
+        dx = ops.head_layernorm_pack_bwd(x_d, gy_d)
+        ops.head_layernorm_pack(x_d, W)
+        out_h.copy_(dx[0, 0, :8], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps(dict(
+        base, value=value, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, scaling="weak",
+        vs_baseline=None, dtype="bf16", data="synthetic: x N(0,1), packed gradient N(0,1)",
+        unfused_forward_ms=ms_unfused_fwd,
+        roofline={"kernel": "head_layernorm_pack(+bwd)", "bound": "hbm", "achieved": value, "peak": peaks["hbm_gbs"],
+                  "unit": "GB/s", "frac": value / peaks["hbm_gbs"], "traffic": None,
+                  "peak_source": f"hbm_gbs of {kind}"},
+        cpu_baseline=None if args.no_cpu else cpu_sample(3)[0],
+        e2e={"value": nbytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e_ms,
+             "h2d_bytes_per_step": 2 * elem, "d2h_bytes_per_step": 16},
+        gpu_launches=int(launches), clocks=clk.summary())), flush=True)
+
+
+def F_layer_norm(x, D):
+    return torch.nn.functional.layer_norm(x, (D,), eps=1e-5)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -881,10 +997,12 @@ def main():
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk"], default="attention",
+    ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack"],
+                    default="attention",
                     help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
                          "decoder's output formatting (prepare_volume_output); volume_geo_topk: the geometric "
-                         "volume-to-volume block selection (build_volume_to_volume_attn)")
+                         "volume-to-volume block selection (build_volume_to_volume_attn); head_layernorm_pack: the "
+                         "per-head LayerNorm fused with the Ulysses pack")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
@@ -892,6 +1010,8 @@ def main():
         run_volume_output(args)
     elif args.path == "volume_geo_topk":
         run_volume_geo(args)
+    elif args.path == "head_layernorm_pack":
+        run_head_layernorm(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

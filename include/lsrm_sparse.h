@@ -324,6 +324,22 @@ int lsrm_prepare_volume_output(const void* volume, int32_t elem_bytes, const int
                                void* sparse_feat, int32_t* cu_seqlens, int32_t* seqlens, int32_t* index_volume,
                                int* err_flags, void* stream);
 
+/* Per-head LayerNorm fused with the Ulysses pack (models_sparse/utils.py:
+ * 21-23 LayerNorm32, :133-134 non-affine over head_dim, :239-270 q / k /
+ * compressed-k normalisation before the sequence-parallel exchange).
+ * pack: src [n, H, D] (token stride src_token_stride elements) ->
+ *   dst [W, n, H/W, D] (rank-major head slices; W = 1: [n, H, D]), each
+ *   (token, head) row normalised in fp32: (x - mean) / sqrt(var + eps),
+ *   biased variance, cast back to dtype.  H % W == 0, D in 16..256 (powers
+ *   of two), 16-byte aligned rows.
+ * bwd: the gradient of pack: src (the same x), grad_packed [W, n, H/W, D] ->
+ *   grad_src [n, H, D] contiguous (statistics recomputed from x). */
+int lsrm_head_layernorm_pack(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int32_t world, int32_t dtype,
+                             int64_t src_token_stride, float eps, const void* src, void* dst, void* stream);
+int lsrm_head_layernorm_pack_bwd(int32_t n_tokens, int32_t num_heads, int32_t head_dim, int32_t world, int32_t dtype,
+                                 int64_t src_token_stride, float eps, const void* src, const void* grad_packed,
+                                 void* grad_src, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Self-test of the tcgen05 / TMA building blocks (used by the GPU tests)   */
 /* ---------------------------------------------------------------------- */

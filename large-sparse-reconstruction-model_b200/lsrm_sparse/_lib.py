@@ -126,6 +126,13 @@ _SIGS = {
     "lsrm_ulysses_unpack": (
         c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
     ),
+    "lsrm_head_layernorm_pack": (
+        c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, ctypes.c_float, c_void_p, c_void_p, c_void_p]
+    ),
+    "lsrm_head_layernorm_pack_bwd": (
+        c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, ctypes.c_float, c_void_p, c_void_p, c_void_p,
+                c_void_p]
+    ),
     "lsrm_volume_block_topk": (
         c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float, c_int32, c_void_p, c_void_p,
                 c_void_p, c_void_p]

@@ -342,3 +342,32 @@ def ulysses_unpack(y: torch.Tensor, num_heads: int) -> torch.Tensor:
     rc = L.lsrm_ulysses_unpack(n, num_heads, D, world, _dtype_code(y), _ptr(y), out.stride(0), _ptr(out), _stream())
     check(rc, "lsrm_ulysses_unpack")
     return out
+
+
+def head_layernorm_pack(x: torch.Tensor, world: int = 1, eps: float = 1e-5) -> torch.Tensor:
+    """Per-head non-affine LayerNorm (fp32, cast back) of x [n, H, D] written
+    straight into the Ulysses send layout [W, n, H/W, D] (W = 1: [1, n, H, D])."""
+    L = _lib.lib()
+    n, H, D = x.shape
+    if x.stride(2) != 1 or x.stride(1) != D:
+        x = x.contiguous()
+    out = torch.empty(world, n, H // world, D, dtype=x.dtype, device=x.device)
+    rc = L.lsrm_head_layernorm_pack(n, H, D, world, _dtype_code(x), x.stride(0), float(eps), _ptr(x), _ptr(out),
+                                    _stream())
+    check(rc, "lsrm_head_layernorm_pack")
+    return out
+
+
+def head_layernorm_pack_bwd(x: torch.Tensor, grad_packed: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Gradient of ``head_layernorm_pack`` with respect to x [n, H, D]."""
+    L = _lib.lib()
+    n, H, D = x.shape
+    if x.stride(2) != 1 or x.stride(1) != D:
+        x = x.contiguous()
+    world = grad_packed.shape[0]
+    g = grad_packed.contiguous()
+    out = torch.empty(n, H, D, dtype=x.dtype, device=x.device)
+    rc = L.lsrm_head_layernorm_pack_bwd(n, H, D, world, _dtype_code(x), x.stride(0), float(eps), _ptr(x), _ptr(g),
+                                        _ptr(out), _stream())
+    check(rc, "lsrm_head_layernorm_pack_bwd")
+    return out

@@ -146,10 +146,34 @@ class _HeadToSeq(torch.autograd.Function):
 
 
 def seq_to_head(x: torch.Tensor, plan: ShardPlan, group=None, pack: Callable = ops.ulysses_pack,
-                unpack: Callable = ops.ulysses_unpack) -> torch.Tensor:
+                unpack: Callable = ops.ulysses_unpack, normalize: bool = False, eps: float = 1e-5) -> torch.Tensor:
     """[n_local, H, D] (this rank's tokens, all heads) -> [N, hp, D] (all
-    tokens, this rank's heads).  Differentiable."""
+    tokens, this rank's heads).  Differentiable.  ``normalize`` applies the
+    reference's per-head LayerNorm32 (non-affine, over D; models_sparse/utils.py:
+    239-270) in the same pass that packs the send buffer (H % W == 0)."""
+    if normalize:
+        pack = lambda t, W: ops.head_layernorm_pack(t, W, eps)  # noqa: E731
+        unpack = lambda back, H: ops.head_layernorm_pack_bwd(x, back, eps)  # noqa: E731
     return _SeqToHead.apply(x, plan, group, pack, unpack)
+
+
+class _HeadLayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eps):
+        ctx.save_for_backward(x)
+        ctx.eps = eps
+        return ops.head_layernorm_pack(x, 1, eps)[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        return ops.head_layernorm_pack_bwd(x, g.unsqueeze(0), ctx.eps), None
+
+
+def head_layernorm(x: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Per-head LayerNorm32 of x [n, H, D] (non-affine, fp32, cast back) on
+    one GPU, differentiable: the W = 1 case of the fused pack."""
+    return _HeadLayerNorm.apply(x, eps)
 
 
 def head_to_seq(y: torch.Tensor, plan: ShardPlan, num_heads: int, group=None, pack: Callable = ops.ulysses_pack,
