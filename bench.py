@@ -982,6 +982,173 @@ def run_head_layernorm(args):
         gpu_launches=int(launches), clocks=clk.summary())), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# --path view_block_topk: the volume-to-image block selection of
+# build_volume_to_image_attn (misc/sparse_utils.py:991-1200)
+# ---------------------------------------------------------------------------
+
+# test_rgb.sh's image settings (16 views of 768^2, patch 8, block 8, window 3x3,
+# 4 blocks per view) with the surface points at half resolution (the reference
+# renders them at input_image_res[1] // 2), and cfg2's 131072 voxels as queries
+VIEW_CFG = dict(views=16, image_res=768, patch_size=8, block_size=8, surface_res=384, attn_winsize=3,
+                topk_multiimage=4, n=131072, res=256, bbox_radius=0.5)
+
+
+def view_problem(seed):
+    from lsrm_sparse import synth
+
+    c = VIEW_CFG
+    vox, _ = synth.sdf_shell_voxels(c["res"], c["n"], seed)
+    coords = np.zeros((len(vox), 4), np.int32)
+    coords[:, 1], coords[:, 2], coords[:, 3] = vox[:, 2], vox[:, 1], vox[:, 0]
+    centres, radii = synth.scene_spheres(seed)
+    sc = synth.view_scene(centres, radii, 1, c["views"], c["image_res"], c["surface_res"], seed + 1)
+    im = synth.image_tokens(sc["mask_input"], c["patch_size"], c["block_size"])
+    return coords, im, sc
+
+
+def run_view_maps(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    import types
+
+    c = VIEW_CFG
+    coords_h, im_h, sc = view_problem(args.seed)
+    n, M = coords_h.shape[0], c["views"]
+    win, topk = c["attn_winsize"] ** 2, c["topk_multiimage"] * M
+    ps, bs, S, H = c["patch_size"], c["block_size"], c["surface_res"], c["image_res"]
+    nbi = (H // (ps * bs)) ** 2
+    P = (S // (H // (ps * bs))) ** 2
+    base = {"metric": "volume-to-image block selection (voxel queries/s)", "unit": "tokens/s",
+            "higher_is_better": True,
+            "config": {"workload": f"build_volume_to_image_attn: {n} voxel queries (cfg2 shell) x {M} views of "
+                                   f"{H}^2 px (patch {ps}, block {bs}: {nbi} blocks of {P} surface points per view), "
+                                   f"window {win}, top-{topk}",
+                       "l2": "the packed surface points (<= 38 MB) stay in L2; the selection is bound by distance "
+                             "evaluations, not memory"}}
+    sample = 512
+    rows = np.linspace(0, n - 1, sample).astype(np.int64)
+
+    def cpu_sample(reps):
+        import oracle
+
+        w2c_o, th_o, _ = oracle.camera_terms(sc["cameras"])
+        pts_o = oracle.voxel_points(coords_h[rows], c["res"], c["bbox_radius"])
+        secs = []
+        for _ in range(max(1, reps)):
+            t0 = time.perf_counter()
+            oracle.view_block_topk(pts_o, coords_h[rows, 0], sc["mask_input"][:, :, 0], sc["surface_points"],
+                                   sc["surface_masks"], w2c_o, th_o, ps, bs, win, topk, 2 * c["bbox_radius"])
+            secs.append(time.perf_counter() - t0)
+        v = sample / statistics.median(secs)
+        return dict(value=v, unit="tokens/s", cores=1, kind="port",
+                    sample=f"{sample} of {n} voxel queries (evenly spaced), numpy oracle on one host thread "
+                           f"(every view's block preparation included)"), secs
+
+    if args.impl == "reference":
+        cb, secs = cpu_sample(args.steps)
+        v = cb["value"]
+        print(json.dumps(dict(base, impl="reference", value=v, n_gpus=ws, steps=args.steps, warmup=args.warmup,
+                              ms_per_step=statistics.median(secs) * 1e3, scaling="weak", vs_baseline=None,
+                              dtype="f32", data="synthetic", cpu_baseline=cb,
+                              e2e={"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                   "d2h_bytes_per_step": 0})), flush=True)
+        return
+    from lsrm_sparse import _lib, blocks, ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    host = {"cameras_input": torch.from_numpy(sc["cameras"]), "mask_input": torch.from_numpy(sc["mask_input"])}
+    dense_h = {"surface_points_input": torch.from_numpy(sc["surface_points"]),
+               "masks_input": torch.from_numpy(sc["surface_masks"])}
+    coords = torch.from_numpy(coords_h).to(dev)
+    batch = {k: v.to(dev) for k, v in host.items()}
+    dense = {k: v.to(dev) for k, v in dense_h.items()}
+    w2c, th, _ = blocks.camera_terms(batch, dev)
+    mi = batch["mask_input"][:, :, 0]
+
+    def call():
+        pts = blocks.voxel_points(coords, c["res"], c["bbox_radius"])
+        return blocks.view_block_topk_raw(pts, coords, mi, dense["surface_points_input"], dense["masks_input"], w2c,
+                                          th, None, ps, bs, win, topk, 2 * c["bbox_radius"])
+
+    for _ in range(args.warmup):
+        out = call()
+    assert ops.read_errors() == 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    value = n / (ms * 1e-3)
+    valid = (out >= 0).sum(1).float().mean().item()
+    # the reference's distance evaluations: every query against all points of its window blocks
+    sel = sc["mask_input"][0, :, 0].reshape(M, H // (ps * bs), ps * bs, H // (ps * bs), ps * bs).any((2, 4))
+    C = int(np.minimum(sel.reshape(M, -1).sum(1), win).sum())
+    ref_evals = n * C * P
+    hbm_bytes = (M * S * S * 16 + M * H * H * 4 + n * (16 + 12) + n * topk * 4)
+    peaks, kind = load_peaks()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    clock_hz = 1965e6
+    issue_evals = sms * 4 * 32 * clock_hz / 10  # 10 warp instructions per 32 point evaluations
+
+    e2e = None
+    if not args.no_e2e:
+        args_ns = types.SimpleNamespace(block_size=bs, patch_size=ps, input_image_res=[H // 2, H],
+                                        attn_winsize=c["attn_winsize"], topk_multiimage=c["topk_multiimage"],
+                                        image_num_per_batch=M, bbox_radius=c["bbox_radius"], volume_res=c["res"],
+                                        use_3d_aware_attn=True)
+        pin = {"vol": torch.from_numpy(coords_h).pin_memory(), "im": torch.from_numpy(im_h).pin_memory()}
+        pin.update({k: v.pin_memory() for k, v in host.items()})
+        pin.update({k: v.pin_memory() for k, v in dense_h.items()})
+        row_h = torch.empty(topk, dtype=torch.int32).pin_memory()
+
+        def e2e_call():
+            g = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
+            b_ = {"cameras_input": g["cameras_input"], "mask_input": g["mask_input"]}
+            d_ = {"surface_points_input": g["surface_points_input"], "masks_input": g["masks_input"]}
+            res = blocks.build_volume_to_image_attn(g["im"], g["vol"], b_, d_, args_ns)
+            row_h.copy_(res["block_topk"][0, 0], non_blocking=True)
+
+        for _ in range(2):
+            e2e_call()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": n / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": int(sum(v.numel() * v.element_size() for v in pin.values())),
+               "d2h_bytes_per_step": topk * 4}
+    print(json.dumps(dict(
+        base, value=value, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, scaling="weak",
+        vs_baseline=None, dtype="f32",
+        data=f"synthetic: seeded random-sphere scene, {M} posed views ray-cast at {H}^2 and {S}^2, "
+             f"{C} window candidates per query, {valid:.1f} blocks kept per query on average",
+        ref_distance_evals_per_s=ref_evals / (ms * 1e-3),
+        roofline={"kernel": "view_block_topk", "bound": "hbm", "achieved": hbm_bytes / (ms * 1e-3) / 1e9,
+                  "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": hbm_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                  "traffic": None, "peak_source": f"hbm_gbs of {kind}",
+                  "note": "memory is not the bound: distance evaluations on the fp32 pipe are (compute)"},
+        compute={"ref_distance_evals_per_s": ref_evals / (ms * 1e-3), "issue_ceiling_evals_per_s": issue_evals,
+                 "frac": ref_evals / (ms * 1e-3) / issue_evals,
+                 "note": "the reference's evaluations (every window block's points) against the nominal issue "
+                         "rate at 10 warp instructions per 32 evaluations; the kernel skips invalid points and "
+                         "walks the union of a warp's windows"},
+        cpu_baseline=None if args.no_cpu else cpu_sample(1)[0], e2e=e2e,
+        gpu_launches=int(launches), clocks=clk.summary())), flush=True)
+
+
 def F_layer_norm(x, D):
     return torch.nn.functional.layer_norm(x, (D,), eps=1e-5)
 
@@ -997,12 +1164,14 @@ def main():
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack"],
+    ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack",
+                                       "view_block_topk"],
                     default="attention",
                     help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
                          "decoder's output formatting (prepare_volume_output); volume_geo_topk: the geometric "
                          "volume-to-volume block selection (build_volume_to_volume_attn); head_layernorm_pack: the "
-                         "per-head LayerNorm fused with the Ulysses pack")
+                         "per-head LayerNorm fused with the Ulysses pack; view_block_topk: the volume-to-image "
+                         "block selection (build_volume_to_image_attn)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
@@ -1012,6 +1181,8 @@ def main():
         run_volume_geo(args)
     elif args.path == "head_layernorm_pack":
         run_head_layernorm(args)
+    elif args.path == "view_block_topk":
+        run_view_maps(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -303,6 +303,71 @@ int lsrm_volume_block_topk(const int32_t* coords, int64_t n_tokens, const int32_
                            const int32_t* cu_block_include_tokens, int32_t batch, int32_t volume_res, float radius,
                            int32_t topk, float* centroids, int32_t* block_topk, int* err_flags, void* stream);
 
+/* Image-to-volume block selection (build_image_to_volume_attn with
+ * use_3d_aware_attn, misc/sparse_utils.py:901-988): as lsrm_volume_block_topk,
+ * but the query points are given (points [n_points, 3] float32, e.g. from
+ * lsrm_image_token_points; point_coords [n_points, 4] int32 only for the batch
+ * id in column 0) and the block centres come from the voxels volume_coords
+ * [n_voxels, 4] in block order (centroids: scratch of 3 * n_voxels floats). */
+int lsrm_points_volume_block_topk(const float* points, const int32_t* point_coords, int64_t n_points,
+                                  const int32_t* volume_coords, int64_t n_voxels, const int32_t* cu_seqblocks,
+                                  const int32_t* cu_block_include_tokens, int32_t batch, int32_t volume_res,
+                                  float radius, int32_t topk, float* centroids, int32_t* block_topk, int* err_flags,
+                                  void* stream);
+
+/* from_volcoords_to_points (misc/sparse_utils.py:644-650): points [n, 3]
+ * float32 = 2 * (c / (volume_res - 1) - 0.5) * radius for (x, y, z) = coords
+ * columns (3, 2, 1), radius = bbox_radius * 1.05 as the reference passes. */
+int lsrm_voxel_points(const int32_t* coords, int64_t n_tokens, int32_t volume_res, float radius, float* points,
+                      void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Image-side 3D-aware attention maps (misc/sparse_utils.py:653-1200)       */
+/* ---------------------------------------------------------------------- */
+/* from_imcoords_to_points (:653-687): image_coords [n, 4] int32 (batch, view,
+ * patch row, patch column); surface_points [B, M, S, S, 3] and surface_masks
+ * [B, M, S, S] float32 (S a multiple of patch_res, the patch grid per side).
+ * points [n, 3]: the surface point of the token's patch whose mask value is
+ * largest (the first in row-major order on ties).  Coordinates out of range
+ * set LSRM_ERR_BAD_INDEX in err_flags (required) and give (0, 0, 0). */
+int lsrm_image_token_points(const int32_t* image_coords, int64_t n_tokens, const float* surface_points,
+                            const float* surface_masks, int32_t batch, int32_t views, int32_t surface_res,
+                            int32_t patch_res, float* points, int* err_flags, void* stream);
+
+/* The view-block selection of build_volume_to_image_attn (:991-1200) and
+ * build_image_to_image_attn (:690-898) with use_3d_aware_attn, for query
+ * points [n, 3] float32 (voxel points or image-token points) whose batch id
+ * is column 0 of point_coords [n, 4] int32.
+ *   mask_input     view v = b * views + m at mask_input + v * mask_image_stride,
+ *                  [image_h, image_w] float32, non-negative; a block of
+ *                  (patch_size * block_size)^2 pixels is selected when some
+ *                  value is non-zero (blocks numbered row-major per view).
+ *   surface_points [B, M, S, S, 3], surface_masks [B, M, S, S] float32; a
+ *                  block owns an (S / blocks per side)^2 tile of them; a point
+ *                  is valid when its mask > 0.2.
+ *   world_to_cam   [B, M, 4, 4] (the inverse of the camera-to-world matrix),
+ *   tan_half_fov   [B, M] = tan(fov / 2), both computed by the caller with the
+ *                  reference's calls; crop [B, M, 4] = (origin - 1, rows
+ *                  start, columns start, crop size - 1), or NULL without crop.
+ * Per view with selected blocks, the win (<= 25) blocks nearest to the
+ * point's projection in block units; each candidate's value is the smallest
+ * distance to its valid points, capped at max_dist when it has an invalid
+ * one (max_dist when it has none).  block_topk [n, topk]: the min(C, topk)
+ * smallest of the C candidates (views * win <= 512), in candidate order
+ * (view, then nearness), as block ids offset by the selected-block count of
+ * the earlier views; -1 padding.  Ties go to the lower position.  The
+ * workspace size comes from lsrm_view_block_topk_workspace_bytes (0 for
+ * unsupported geometry).  Blocks per side must be equal and divide S. */
+int64_t lsrm_view_block_topk_workspace_bytes(int32_t batch, int32_t views, int32_t image_h, int32_t image_w,
+                                             int32_t surface_res, int32_t patch_size, int32_t block_size, int32_t win,
+                                             int64_t n_queries);
+int lsrm_view_block_topk(const float* points, const int32_t* point_coords, int64_t n_queries, int32_t batch,
+                         int32_t views, const float* mask_input, int64_t mask_image_stride, int32_t image_h,
+                         int32_t image_w, const float* surface_points, const float* surface_masks,
+                         int32_t surface_res, int32_t patch_size, int32_t block_size, const float* world_to_cam,
+                         const float* tan_half_fov, const float* crop, int32_t win, int32_t topk, float max_dist,
+                         int32_t* block_topk, void* workspace, int64_t workspace_bytes, int* err_flags, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Volume output preparation (models_sparse/voldecoder.py:196-268)          */
 /* ---------------------------------------------------------------------- */

@@ -67,10 +67,12 @@ __global__ void geo_centroid_kernel(const int32_t* __restrict__ coords, const in
 }
 
 // Per token: the k nearest blocks of its element (k <= K), sorted by id.
+// The token's point is its voxel's (coords [n, 4]) or, with ``qpts``, given
+// ([n, 3] floats; coords column 0 still names the batch element).
 template <int K>
-__global__ void geo_topk_kernel(const int32_t* __restrict__ coords, long long n, const int32_t* __restrict__ cu_sb,
-                                int batch, const float* __restrict__ cent, float den, float r, int k,
-                                int32_t* __restrict__ out, int* err) {
+__global__ void geo_topk_kernel(const int32_t* __restrict__ coords, const float* __restrict__ qpts, long long n,
+                                const int32_t* __restrict__ cu_sb, int batch, const float* __restrict__ cent,
+                                float den, float r, int k, int32_t* __restrict__ out, int* err) {
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= n) return;
   const int4 c = reinterpret_cast<const int4*>(coords)[t];
@@ -80,7 +82,7 @@ __global__ void geo_topk_kernel(const int32_t* __restrict__ coords, long long n,
     for (int i = 0; i < k; ++i) o[i] = -1;
     return;
   }
-  const float3 p = voxel_point(c, den, r);
+  const float3 p = qpts ? make_float3(qpts[3 * t], qpts[3 * t + 1], qpts[3 * t + 2]) : voxel_point(c, den, r);
   const int b0 = cu_sb[c.x], nb = cu_sb[c.x + 1] - b0;
   float bd[K];
   int bi[K];
@@ -145,11 +147,29 @@ __global__ void geo_topk_kernel(const int32_t* __restrict__ coords, long long n,
 }
 
 template <int K>
-int launch_geo_topk(const int32_t* coords, long long n, const int32_t* cu_sb, int batch, const float* cent, float den,
-                    float r, int k, int32_t* out, int* err, cudaStream_t s) {
-  geo_topk_kernel<K><<<geo_grid(n, 128), 128, 0, s>>>(coords, n, cu_sb, batch, cent, den, r, k, out, err);
+int launch_geo_topk(const int32_t* coords, const float* qpts, long long n, const int32_t* cu_sb, int batch,
+                    const float* cent, float den, float r, int k, int32_t* out, int* err, cudaStream_t s) {
+  geo_topk_kernel<K><<<geo_grid(n, 128), 128, 0, s>>>(coords, qpts, n, cu_sb, batch, cent, den, r, k, out, err);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
+}
+
+int dispatch_geo_topk(const int32_t* coords, const float* qpts, long long n, const int32_t* cu_sb, int batch,
+                      const float* cent, float den, float r, int k, int32_t* out, int* err, cudaStream_t s) {
+  if (k <= 8) return launch_geo_topk<8>(coords, qpts, n, cu_sb, batch, cent, den, r, k, out, err, s);
+  if (k <= 16) return launch_geo_topk<16>(coords, qpts, n, cu_sb, batch, cent, den, r, k, out, err, s);
+  if (k <= 32) return launch_geo_topk<32>(coords, qpts, n, cu_sb, batch, cent, den, r, k, out, err, s);
+  return launch_geo_topk<64>(coords, qpts, n, cu_sb, batch, cent, den, r, k, out, err, s);
+}
+
+__global__ void voxel_points_kernel(const int32_t* __restrict__ coords, long long n, float den, float r,
+                                    float* __restrict__ pts) {
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const float3 p = voxel_point(reinterpret_cast<const int4*>(coords)[t], den, r);
+  pts[3 * t] = p.x;
+  pts[3 * t + 1] = p.y;
+  pts[3 * t + 2] = p.z;
 }
 
 }  // namespace
@@ -174,15 +194,44 @@ extern "C" int lsrm_volume_block_topk(const int32_t* coords, int64_t n_tokens, c
                                                                    cu_block_include_tokens, den, radius, n_tokens,
                                                                    centroids);
   LSRM_LAUNCH_CHECK();
-  if (topk <= 8)
-    return launch_geo_topk<8>(coords, n_tokens, cu_seqblocks, batch, centroids, den, radius, topk, block_topk,
-                              err_flags, s);
-  if (topk <= 16)
-    return launch_geo_topk<16>(coords, n_tokens, cu_seqblocks, batch, centroids, den, radius, topk, block_topk,
-                               err_flags, s);
-  if (topk <= 32)
-    return launch_geo_topk<32>(coords, n_tokens, cu_seqblocks, batch, centroids, den, radius, topk, block_topk,
-                               err_flags, s);
-  return launch_geo_topk<64>(coords, n_tokens, cu_seqblocks, batch, centroids, den, radius, topk, block_topk,
-                             err_flags, s);
+  return dispatch_geo_topk(coords, nullptr, n_tokens, cu_seqblocks, batch, centroids, den, radius, topk, block_topk,
+                           err_flags, s);
+}
+
+extern "C" int lsrm_points_volume_block_topk(const float* points, const int32_t* point_coords, int64_t n_points,
+                                             const int32_t* volume_coords, int64_t n_voxels,
+                                             const int32_t* cu_seqblocks, const int32_t* cu_block_include_tokens,
+                                             int32_t batch, int32_t volume_res, float radius, int32_t topk,
+                                             float* centroids, int32_t* block_topk, int* err_flags, void* stream) {
+  LSRM_CHECK_ARG(n_points >= 0 && n_points < (1ll << 31) && n_voxels >= 0 && n_voxels < (1ll << 31) && batch >= 1 &&
+                     volume_res >= 2,
+                 "bad sizes");
+  LSRM_CHECK_ARG(topk >= 1 && topk <= 64, "topk must be in [1, 64] (got %d)", topk);
+  LSRM_CHECK_ARG(((uintptr_t)point_coords & 15) == 0 && ((uintptr_t)volume_coords & 15) == 0,
+                 "coords must be 16-byte aligned ([n, 4] int32)");
+  LSRM_CHECK_ARG(err_flags != nullptr && points != nullptr, "points and err_flags are required");
+  if (n_points == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProfScope ps("points_volume_block_topk", s);
+  const float den = (float)(volume_res - 1);
+  if (n_voxels > 0) {
+    geo_centroid_kernel<<<geo_grid(n_voxels * 32, 256), 256, 0, s>>>(volume_coords, cu_seqblocks, batch,
+                                                                     cu_block_include_tokens, den, radius, n_voxels,
+                                                                     centroids);
+    LSRM_LAUNCH_CHECK();
+  }
+  return dispatch_geo_topk(point_coords, points, n_points, cu_seqblocks, batch, centroids, den, radius, topk,
+                           block_topk, err_flags, s);
+}
+
+extern "C" int lsrm_voxel_points(const int32_t* coords, int64_t n_tokens, int32_t volume_res, float radius,
+                                 float* points, void* stream) {
+  LSRM_CHECK_ARG(n_tokens >= 0 && volume_res >= 2, "bad sizes");
+  LSRM_CHECK_ARG(((uintptr_t)coords & 15) == 0, "coords must be 16-byte aligned ([n, 4] int32)");
+  if (n_tokens == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  voxel_points_kernel<<<geo_grid(n_tokens, 256), 256, 0, s>>>(coords, n_tokens, (float)(volume_res - 1), radius,
+                                                              points);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
 }

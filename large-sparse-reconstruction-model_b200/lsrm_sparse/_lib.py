@@ -137,6 +137,23 @@ _SIGS = {
         c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float, c_int32, c_void_p, c_void_p,
                 c_void_p, c_void_p]
     ),
+    "lsrm_points_volume_block_topk": (
+        c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float,
+                c_int32, c_void_p, c_void_p, c_void_p, c_void_p]
+    ),
+    "lsrm_voxel_points": (c_int, [c_void_p, c_int64, c_int32, ctypes.c_float, c_void_p, c_void_p]),
+    "lsrm_image_token_points": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                c_void_p]
+    ),
+    "lsrm_view_block_topk_workspace_bytes": (
+        c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int64]
+    ),
+    "lsrm_view_block_topk": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32, c_void_p,
+                c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float,
+                c_void_p, c_void_p, c_int64, c_void_p, c_void_p]
+    ),
     "lsrm_prepare_volume_output": (
         c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
                 c_void_p, c_void_p, c_void_p, c_void_p]

@@ -115,3 +115,189 @@ def build_volume_to_volume_attn(volfeat_coords: torch.Tensor, args):
         block_topk = torch.stack([bt, bt], dim=0)
     return {"block_topk": block_topk, "cu_seqblocks": cu_seqblocks.to(torch.int32),
             "cu_block_include_tokens": cu_blk.to(torch.int32)}
+
+
+# ---------------------------------------------------------------------------
+# Image-side 3D-aware attention maps (misc/sparse_utils.py:644-1300)
+# ---------------------------------------------------------------------------
+
+def _f32(t: torch.Tensor, device) -> torch.Tensor:
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+def voxel_points(coords: torch.Tensor, volume_res: int, bbox_radius: float) -> torch.Tensor:
+    """``from_volcoords_to_points`` (misc/sparse_utils.py:644-650): [n, 3]
+    float32 points of voxel coords (batch, z, y, x)."""
+    L = _lib.lib()
+    coords = coords.to(torch.int32).contiguous()
+    out = torch.empty(coords.shape[0], 3, dtype=torch.float32, device=coords.device)
+    rc = L.lsrm_voxel_points(ops._ptr(coords), coords.shape[0], int(volume_res), float(bbox_radius) * 1.05,
+                             ops._ptr(out), ops._stream())
+    check(rc, "lsrm_voxel_points")
+    return out
+
+
+def from_volcoords_to_points(volcoords: torch.Tensor, args) -> torch.Tensor:
+    """Same arguments as the reference function (misc/sparse_utils.py:644)."""
+    return voxel_points(volcoords, args.volume_res, args.bbox_radius)
+
+
+def from_imcoords_to_points(imcoords: torch.Tensor, dense_points, args) -> torch.Tensor:
+    """``from_imcoords_to_points`` (misc/sparse_utils.py:653-687): per image
+    token (batch, view, patch row, patch column) the surface point of its
+    patch whose mask value is largest (the first on ties).  [n, 3] float32."""
+    L = _lib.lib()
+    dev = imcoords.device
+    coords = imcoords.to(torch.int32).contiguous()
+    sp = _f32(dense_points["surface_points_input"], dev)
+    B, M, S = sp.shape[0], sp.shape[1], sp.shape[2]
+    sm = _f32(dense_points["masks_input"], dev).reshape(B, M, S, S)
+    pr = int(args.input_image_res[1]) // int(args.patch_size)
+    out = torch.empty(coords.shape[0], 3, dtype=torch.float32, device=dev)
+    rc = L.lsrm_image_token_points(ops._ptr(coords), coords.shape[0], ops._ptr(sp), ops._ptr(sm), B, M, S, pr,
+                                   ops._ptr(out), ops._ptr(ops._err_word(dev)), ops._stream())
+    check(rc, "lsrm_image_token_points")
+    return out
+
+
+def camera_terms(batch, device):
+    """The per-view values of misc/sparse_utils.py:1097-1135 with the
+    reference's own torch calls (batched over views, on ``device``):
+    world_to_cam = inverse(camera[:16] as 4x4) [B, M, 4, 4], tan(fov / 2)
+    [B, M], and with ``crop_input`` / ``origin_size`` in ``batch``
+    (origin - 1, rows start, columns start, crop size - 1) [B, M, 4]."""
+    cams = batch["cameras_input"].to(device)
+    B, M = cams.shape[:2]
+    w2c = torch.inverse(cams[..., :16].reshape(B, M, 4, 4))
+    th = torch.tan(cams[..., 16] / 2.0)
+    crop = None
+    if "crop_input" in batch:
+        ci = batch["crop_input"].to(device)
+        osz = batch["origin_size"].to(device)[:, 0]
+        o1 = (osz - 1)[:, None].expand(B, M)
+        crop = torch.stack([o1.to(torch.float32), ci[..., 0].to(torch.float32), ci[..., 2].to(torch.float32),
+                            (ci[..., 1] - ci[..., 0] - 1).to(torch.float32)], -1)
+    return _f32(w2c, device), _f32(th, device), (None if crop is None else _f32(crop, device))
+
+
+def view_block_topk(points: torch.Tensor, point_coords: torch.Tensor, batch, dense_points, args) -> torch.Tensor:
+    """The view-block selection shared by build_volume_to_image_attn and
+    build_image_to_image_attn (misc/sparse_utils.py:1019-1187, :717-885):
+    [n, topk_multiimage * image_num_per_batch] int32 per query point.  No host
+    synchronisation."""
+    dev = points.device
+    mi = batch["mask_input"].to(device=dev)[:, :, 0]
+    w2c, th, crop = camera_terms(batch, dev)
+    return view_block_topk_raw(points, point_coords, mi, dense_points["surface_points_input"],
+                               dense_points["masks_input"], w2c, th, crop, int(args.patch_size), int(args.block_size),
+                               int(args.attn_winsize) ** 2, int(args.topk_multiimage) * int(args.image_num_per_batch),
+                               float(args.bbox_radius) * 2)
+
+
+def view_block_topk_raw(points, point_coords, mask_input, surface_points, surface_masks, world_to_cam, tan_half,
+                        crop, patch_size: int, block_size: int, win: int, topk: int, max_dist: float):
+    """``lsrm_view_block_topk`` on tensors: ``mask_input`` [B, M, H, W],
+    ``surface_points`` [B, M, S, S, 3], ``surface_masks`` [B, M, S, S(, 1)],
+    ``world_to_cam`` [B, M, 4, 4], ``tan_half`` [B, M], ``crop`` [B, M, 4] or
+    None (see ``camera_terms``)."""
+    L = _lib.lib()
+    dev = points.device
+    pts = _f32(points, dev)
+    qc = point_coords.to(torch.int32).contiguous()
+    sp = _f32(surface_points, dev)
+    B, M, S = sp.shape[0], sp.shape[1], sp.shape[2]
+    sm = _f32(surface_masks, dev).reshape(B, M, S, S)
+    mi = mask_input.to(device=dev)
+    if mi.dtype != torch.float32:
+        mi = mi.to(torch.float32)
+    H, W = mi.shape[-2:]
+    if mi.stride(-1) != 1 or mi.stride(-2) != W or mi.stride(0) != M * mi.stride(1):
+        mi = mi.contiguous()
+    w2c, th = _f32(world_to_cam, dev), _f32(tan_half, dev)
+    crop = None if crop is None else _f32(crop, dev)
+    n = pts.shape[0]
+    ps, bs = int(patch_size), int(block_size)
+    nbytes = L.lsrm_view_block_topk_workspace_bytes(B, M, H, W, S, ps, bs, win, n)
+    if nbytes == 0:
+        raise ValueError("unsupported view geometry (blocks per side must agree and divide the surface grid; "
+                         "views * attn_winsize^2 <= 512, attn_winsize <= 5)")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty(n, topk, dtype=torch.int32, device=dev)
+    rc = L.lsrm_view_block_topk(ops._ptr(pts), ops._ptr(qc), n, B, M, ops._ptr(mi), mi.stride(1), H, W,
+                                ops._ptr(sp), ops._ptr(sm), S, ps, bs, ops._ptr(w2c), ops._ptr(th), ops._ptr(crop),
+                                int(win), int(topk), float(max_dist), ops._ptr(out), ops._ptr(ws), nbytes,
+                                ops._ptr(ops._err_word(dev)), ops._stream())
+    check(rc, "lsrm_view_block_topk")
+    return out
+
+
+def _image_separation(imfeat_coords, dense_points, args):
+    bs = int(args.block_size)
+    batch_size = int(imfeat_coords[:, 0].max().item()) + 1
+    r = int(args.input_image_res[-1]) // bs
+    M = dense_points["surface_points_input"].shape[1]
+    cu_sb, cu_blk, _ = block_separation(imfeat_coords, 3, [1, bs, bs], batch_size, [M, r, r])
+    return cu_sb, cu_blk
+
+
+def build_image_to_image_attn(imfeat_coords: torch.Tensor, batch, dense_points, args):
+    """``build_image_to_image_attn`` (misc/sparse_utils.py:690-898): same
+    arguments and dict keys; ``imfeat_coords`` is not modified."""
+    cu_sb, cu_blk = _image_separation(imfeat_coords, dense_points, args)
+    block_topk = None
+    if getattr(args, "use_3d_aware_attn", False):
+        pts = from_imcoords_to_points(imfeat_coords, dense_points, args)
+        bt = view_block_topk(pts, imfeat_coords, batch, dense_points, args)
+        block_topk = torch.stack([bt, bt], dim=0)
+    return {"block_topk": block_topk, "cu_seqblocks": cu_sb.to(torch.int32),
+            "cu_block_include_tokens": cu_blk.to(torch.int32)}
+
+
+def build_volume_to_image_attn(imfeat_coords: torch.Tensor, volfeat_coords: torch.Tensor, batch, dense_points, args):
+    """``build_volume_to_image_attn`` (misc/sparse_utils.py:991-1200): same
+    arguments and dict keys (image blocks as keys, voxels as queries)."""
+    cu_sb, cu_blk = _image_separation(imfeat_coords, dense_points, args)
+    block_topk = None
+    if getattr(args, "use_3d_aware_attn", False):
+        pts = from_volcoords_to_points(volfeat_coords, args)
+        bt = view_block_topk(pts, volfeat_coords, batch, dense_points, args)
+        block_topk = torch.stack([bt, bt], dim=0)
+    return {"block_topk": block_topk, "cu_seqblocks": cu_sb.to(torch.int32),
+            "cu_block_include_tokens": cu_blk.to(torch.int32)}
+
+
+def build_image_to_volume_attn(imfeat_coords: torch.Tensor, volfeat_coords: torch.Tensor, dense_points, args):
+    """``build_image_to_volume_attn`` (misc/sparse_utils.py:901-988): same
+    arguments and dict keys (volume blocks as keys, image tokens as
+    queries)."""
+    bs = int(args.block_size)
+    res = int(args.volume_res)
+    batch_size = int(volfeat_coords[:, 0].max().item()) + 1
+    cu_sb, cu_blk, _ = block_separation(volfeat_coords, 3, [bs, bs, bs], batch_size, [res, res, res])
+    block_topk = None
+    if getattr(args, "use_3d_aware_attn", False):
+        L = _lib.lib()
+        dev = volfeat_coords.device
+        pts = from_imcoords_to_points(imfeat_coords, dense_points, args)
+        qc = imfeat_coords.to(torch.int32).contiguous()
+        vc = volfeat_coords.to(torch.int32).contiguous()
+        topk = int(args.topk_volume)
+        bt = torch.empty(qc.shape[0], topk, dtype=torch.int32, device=dev)
+        cent = torch.empty(max(vc.shape[0], 1), 3, dtype=torch.float32, device=dev)
+        rc = L.lsrm_points_volume_block_topk(ops._ptr(pts), ops._ptr(qc), qc.shape[0], ops._ptr(vc), vc.shape[0],
+                                             ops._ptr(cu_sb), ops._ptr(cu_blk), batch_size, res,
+                                             float(args.bbox_radius) * 1.05, topk, ops._ptr(cent), ops._ptr(bt),
+                                             ops._ptr(ops._err_word(dev)), ops._stream())
+        check(rc, "lsrm_points_volume_block_topk")
+        block_topk = torch.stack([bt, bt], dim=0)
+    return {"block_topk": block_topk, "cu_seqblocks": cu_sb.to(torch.int32),
+            "cu_block_include_tokens": cu_blk.to(torch.int32)}
+
+
+def build_3D_aware_attn(imfeat_coords: torch.Tensor, volfeat_coords: torch.Tensor, batch, dense_points, args):
+    """``build_3D_aware_attn`` (misc/sparse_utils.py:1283-1298): the four maps
+    under the reference's keys."""
+    return {"img_to_img_attn": build_image_to_image_attn(imfeat_coords, batch, dense_points, args),
+            "img_to_vol_attn": build_image_to_volume_attn(imfeat_coords, volfeat_coords, dense_points, args),
+            "vol_to_img_attn": build_volume_to_image_attn(imfeat_coords, volfeat_coords, batch, dense_points, args),
+            "vol_to_vol_attn": build_volume_to_volume_attn(volfeat_coords, args)}

@@ -15,6 +15,10 @@ What runs, all unmodified reference code:
 * ``sort_volume_blocks`` / ``compute_block_separation``
   (misc/sparse_utils.py:126-152, 592-641): block metadata of voxel and
   image-patch coordinates.
+* ``build_image_to_image_attn``, ``build_image_to_volume_attn``,
+  ``build_volume_to_image_attn`` and ``from_imcoords_to_points``
+  (misc/sparse_utils.py:653-1200) on posed views of a sphere scene from
+  ``lsrm_sparse.synth.view_scene`` (``--only image``).
 * ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
   without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
   for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
@@ -278,10 +282,65 @@ def make_volume_geo_topk(sparse_utils, seed):
                 cu_block_include_tokens=out["cu_block_include_tokens"].numpy())
 
 
+def make_image_maps(sparse_utils, seed, crop):
+    """The image-side attention maps with use_3d_aware_attn on two batch
+    elements of three 64x64 views (patch 4, block 4: 4x4 blocks per view,
+    32x32 surface points) of a two-to-three-sphere scene, and the voxels of
+    the same scene's shell (32^3 grid).  Cameras, masks and surface points come
+    from ``lsrm_sparse.synth.view_scene``; image tokens are the patches with
+    mask, in sort_image_blocks order; voxels are sorted by sort_volume_blocks.
+    The separation's torch.histc gets a float copy (see
+    ``make_volume_geo_topk``)."""
+    import types
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "large-sparse-reconstruction-model_b200"))
+    from lsrm_sparse import synth
+
+    res, bs, ps, H, S, B, M = 32, 4, 4, 64, 32, 2, 3
+    centres, radii = synth.scene_spheres(seed, (2, 3), (0.2, 0.3))
+    scene = synth.view_scene(centres, radii, B, M, H, S, seed + 1, crop=crop)
+    imcoords = torch.from_numpy(synth.image_tokens(scene["mask_input"], ps, bs))
+    parts = []
+    for b, n in enumerate((1500, 1100)):
+        vox, _ = synth.sdf_shell_voxels(res, n, seed, (2, 3), (0.2, 0.3))
+        parts.append(np.stack([np.full(len(vox), b), vox[:, 2], vox[:, 1], vox[:, 0]], 1))
+    volcoords = torch.from_numpy(np.concatenate(parts).astype(np.int32))
+    args = types.SimpleNamespace(block_size=bs, volume_res=res, use_3d_aware_attn=True, topk_volume=8,
+                                 bbox_radius=0.5, attn_winsize=2, topk_multiimage=2, image_num_per_batch=M,
+                                 input_image_res=[H // 2, H], patch_size=ps)
+    _, volcoords, _ = sparse_utils.sort_volume_blocks(torch.zeros(volcoords.shape[0], 1), volcoords.clone(), args)
+    batch = {"mask_input": torch.from_numpy(scene["mask_input"]),
+             "cameras_input": torch.from_numpy(scene["cameras"])}
+    if crop:
+        batch["crop_input"] = torch.from_numpy(scene["crop_input"])
+        batch["origin_size"] = torch.from_numpy(scene["origin_size"])
+    dense = {"surface_points_input": torch.from_numpy(scene["surface_points"]),
+             "masks_input": torch.from_numpy(scene["surface_masks"])}
+    histc = torch.histc
+    torch.histc = lambda x, *a, **kw: histc(x.float(), *a, **kw)
+    try:
+        i2i = sparse_utils.build_image_to_image_attn(imcoords.clone(), batch, dense, args)
+        i2v = sparse_utils.build_image_to_volume_attn(imcoords.clone(), volcoords.clone(), dense, args)
+        v2i = sparse_utils.build_volume_to_image_attn(imcoords.clone(), volcoords.clone(), batch, dense, args)
+    finally:
+        torch.histc = histc
+    impoints = sparse_utils.from_imcoords_to_points(imcoords.clone(), dense, args)
+    out = dict(imcoords=imcoords.numpy(), volcoords=volcoords.numpy().astype(np.int32),
+               impoints=impoints.numpy(), volume_res=np.int32(res), block_size=np.int32(bs),
+               patch_size=np.int32(ps), image_res=np.int32(H), topk_volume=np.int32(8), attn_winsize=np.int32(2),
+               topk_multiimage=np.int32(2), bbox_radius=np.float64(0.5), batch=np.int32(B))
+    for k, v in scene.items():
+        out["scene_" + k] = v
+    for name, r in (("i2i", i2i), ("i2v", i2v), ("v2i", v2i)):
+        for k, v in r.items():
+            out[f"{name}_{k}"] = v.numpy()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks", "volume", "geo"], default=None,
+    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image"], default=None,
                     help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
@@ -289,6 +348,12 @@ def main():
     sys.path.insert(0, args.ref)
     from misc import sparse_utils
 
+    if args.only == "image":
+        for crop in (False, True):
+            name = "image_maps_crop" if crop else "image_maps"
+            np.savez_compressed(os.path.join(HERE, name + ".npz"), **make_image_maps(sparse_utils, 71, crop))
+            print("wrote", name)
+        return
     if args.only == "geo":
         np.savez_compressed(os.path.join(HERE, "volume_geo_topk.npz"), **make_volume_geo_topk(sparse_utils, 61))
         print("wrote volume_geo_topk")

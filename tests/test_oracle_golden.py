@@ -184,3 +184,51 @@ def test_volume_geo_topk_matches_reference(golden):
                                    int(g["volume_res"]), float(g["bbox_radius"]), int(g["topk"]))
     assert np.array_equal(out, g["block_topk"][0])
     assert np.array_equal(g["block_topk"][0], g["block_topk"][1])
+
+
+def _image_case(g):
+    B, M = g["scene_cameras"].shape[:2]
+    w2c, th, crop = oracle.camera_terms(g["scene_cameras"], g.get("scene_crop_input"), g.get("scene_origin_size"))
+    ps, bs, H = int(g["patch_size"]), int(g["block_size"]), int(g["image_res"])
+    return dict(B=B, M=M, w2c=w2c, th=th, crop=crop, ps=ps, bs=bs, H=H, win=int(g["attn_winsize"]) ** 2,
+                topk=int(g["topk_multiimage"]) * M, max_dist=2 * float(g["bbox_radius"]))
+
+
+@pytest.mark.parametrize("name", ["image_maps", "image_maps_crop"])
+def test_image_maps_match_reference(golden, name):
+    """The image-side maps restated in the oracle vs the reference's own
+    build_image_to_image_attn / build_image_to_volume_attn /
+    build_volume_to_image_attn and from_imcoords_to_points
+    (misc/sparse_utils.py:653-1200), with and without cropped views.  Token
+    points and the image-to-volume map are equal; the view maps are equal
+    except where torch.topk resolved a tie, and those rows must be valid for
+    some resolution of the ties (``view_rows_equivalent``).  A planted
+    mistake (a block outside every window) must be caught."""
+    g = golden(name)
+    c = _image_case(g)
+    impts = oracle.image_token_points(g["imcoords"], g["scene_surface_points"], g["scene_surface_masks"],
+                                      c["H"] // c["ps"])
+    assert np.array_equal(impts, g["impoints"])
+    i2v = oracle.image_volume_block_topk(impts, g["imcoords"][:, 0], g["volcoords"], g["i2v_cu_seqblocks"],
+                                         g["i2v_cu_block_include_tokens"], c["B"], int(g["volume_res"]),
+                                         float(g["bbox_radius"]), int(g["topk_volume"]))
+    assert np.array_equal(i2v, g["i2v_block_topk"][0])
+    volpts = oracle.voxel_points(g["volcoords"], int(g["volume_res"]), float(g["bbox_radius"]))
+    mi = g["scene_mask_input"][:, :, 0]
+    equal_rows = 0
+    for key, pts, bid in (("i2i", impts, g["imcoords"][:, 0]), ("v2i", volpts, g["volcoords"][:, 0])):
+        out, det = oracle.view_block_topk(pts, bid, mi, g["scene_surface_points"], g["scene_surface_masks"],
+                                          c["w2c"], c["th"], c["ps"], c["bs"], c["win"], c["topk"], c["max_dist"],
+                                          crop=c["crop"], return_values=True)
+        ref = g[f"{key}_block_topk"]
+        assert np.array_equal(ref[0], ref[1])
+        assert oracle.view_rows_equivalent(out, ref[0], det, c["win"]) == []
+        equal_rows += int((out == ref[0]).all(1).sum())
+        if key == "v2i":
+            assert np.array_equal(out, ref[0])  # no ties on these points
+            planted = ref[0].copy()
+            row = int(np.nonzero((planted >= 0).sum(1) == planted.shape[1])[0][0])
+            far = [x for x in range(int(g["v2i_cu_seqblocks"][1])) if x not in planted[row]]
+            planted[row, 0] = far[-1]
+            assert row in oracle.view_rows_equivalent(out, planted, det, c["win"])
+    assert equal_rows > 0.8 * (g["imcoords"].shape[0] + g["volcoords"].shape[0])
