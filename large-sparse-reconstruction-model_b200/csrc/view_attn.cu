@@ -44,9 +44,20 @@ struct ViewGeom {
   int nbi;  // blocks per image
   int ib;   // surface points per block side
   int P;    // surface points per block
-  int P4;   // P rounded up to a multiple of 4 (the packed arrays' stride)
+  int T;    // tile side (surface points): ceil(ib / 4), so at most 4 x 4 tiles per block
+  int nt;   // tiles per block side
+  int NT;   // tiles per block (<= kMaxTiles)
+  int TC;   // points per tile, rounded up to a multiple of 4
+  int R;    // floats per packed block record
   int win, Cmax;
 };
+
+// A packed block record (floats): per tile its valid-point count (as int) and
+// bounding box (lo xyz, hi xyz), then the points as x[NT * TC], y[...], z[...],
+// tile t's valid points at [t * TC, t * TC + count), +inf up to the next
+// multiple of 4.
+constexpr int kMaxTiles = 16;
+constexpr int kHdr = kMaxTiles * 7;  // counts, then boxes
 
 int va_grid(long long work, int threads) {
   return (int)std::max<long long>(1, std::min<long long>((work + threads - 1) / threads, 1ll << 30));
@@ -83,10 +94,9 @@ __global__ void image_token_points_kernel(const int4* __restrict__ coords, long 
 }
 
 // One CTA per (image, block): whether the block's pixel mask has a non-zero
-// value, and its valid surface points (mask > 0.2) packed as three arrays
-// x[P4], y[P4], z[P4] (their order is free: only their minimum distance is
-// used); the slots up to the next multiple of 4 hold +inf, which no minimum
-// takes.
+// value, and its valid surface points (mask > 0.2) packed tile by tile with
+// each tile's bounding box (the order inside a tile is free: only the minimum
+// distance is used; the +inf pads are never a minimum).
 __global__ void view_block_prep_kernel(const float* __restrict__ mask, long long img_stride,
                                        const float* __restrict__ sp, const float* __restrict__ sm, ViewGeom g,
                                        int* __restrict__ cnt, int* __restrict__ selflag, float* __restrict__ packed) {
@@ -99,28 +109,62 @@ __global__ void view_block_prep_kernel(const float* __restrict__ mask, long long
     any = mi[(long long)(by * g.bp + y) * g.W + bx * g.bp + x] != 0.f;
   }
   any = __syncthreads_or(any);
-  __shared__ int n_valid;
-  if (threadIdx.x == 0) n_valid = 0;
+  __shared__ int tcount[kMaxTiles];
+  if (threadIdx.x < kMaxTiles) tcount[threadIdx.x] = 0;
   __syncthreads();
   const long long gb = (long long)bm * g.nbi + blk;
-  float* dst = packed + gb * 3 * g.P4;
+  float* rec = packed + gb * g.R;
+  float* X = rec + kHdr;
+  const int span = g.NT * g.TC;
   for (int i = threadIdx.x; i < g.P; i += blockDim.x) {
     const int iy = i / g.ib, ix = i % g.ib;
     const long long pix = ((long long)bm * g.S + by * g.ib + iy) * g.S + bx * g.ib + ix;
     if (sm[pix] > 0.2f) {
-      const int slot = atomicAdd(&n_valid, 1);
-      dst[slot] = sp[3 * pix];
-      dst[g.P4 + slot] = sp[3 * pix + 1];
-      dst[2 * g.P4 + slot] = sp[3 * pix + 2];
+      const int t = (iy / g.T) * g.nt + ix / g.T;
+      const int slot = t * g.TC + atomicAdd(&tcount[t], 1);
+      X[slot] = sp[3 * pix];
+      X[span + slot] = sp[3 * pix + 1];
+      X[2 * span + slot] = sp[3 * pix + 2];
     }
   }
   __syncthreads();
-  const int c = n_valid;
-  if (threadIdx.x < 3 * 4) {
-    const int slot = c + (threadIdx.x & 3);
-    if (slot < ((c + 3) & ~3)) dst[(threadIdx.x >> 2) * g.P4 + slot] = INFINITY;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int t = warp; t < kMaxTiles; t += nwarps) {  // per tile: pads and bounding box
+    const int c = t < g.NT ? tcount[t] : 0;
+    float lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
+    for (int i = lane; i < c; i += 32) {
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const float v = X[a * span + t * g.TC + i];
+        lo[a] = fminf(lo[a], v);
+        hi[a] = fmaxf(hi[a], v);
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        lo[a] = fminf(lo[a], __shfl_xor_sync(0xffffffffu, lo[a], o));
+        hi[a] = fmaxf(hi[a], __shfl_xor_sync(0xffffffffu, hi[a], o));
+      }
+    }
+    if (t < g.NT && lane < 3 && c + lane < ((c + 3) & ~3)) {
+#pragma unroll
+      for (int a = 0; a < 3; ++a) X[a * span + t * g.TC + c + lane] = INFINITY;
+    }
+    if (lane == 0) {
+      reinterpret_cast<int*>(rec)[t] = c;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        rec[kMaxTiles + 6 * t + a] = lo[a];
+        rec[kMaxTiles + 6 * t + 3 + a] = hi[a];
+      }
+    }
   }
+  __syncthreads();
   if (threadIdx.x == 0) {
+    int c = 0;
+    for (int t = 0; t < g.NT; ++t) c += tcount[t];
     cnt[gb] = c;
     selflag[gb] = any;
   }
@@ -193,20 +237,40 @@ __global__ void view_image_list_kernel(const int* __restrict__ selflag, ViewGeom
 // points into its own minimum with packed fp32 pairs, 4 points per step.
 constexpr int kCandThreads = 128;
 
-// Copies block blk's packed points (count rounded up to 4) into stage buffer buf.
-__device__ __forceinline__ void stage_points(int blk, int buf, long long gbase, int P4, const int* __restrict__ cnt,
+// Copies block blk's packed record into stage buffer buf.
+__device__ __forceinline__ void stage_points(int blk, int buf, long long gbase, int R,
                                              const float* __restrict__ packed, float* stage, int tid) {
-  const int c4 = (cnt[gbase + blk] + 3) >> 2;
-  const float* src = packed + (gbase + blk) * 3 * P4;
-  float* dst = stage + buf * 3 * P4;
-  for (int t = tid; t < 3 * c4; t += kCandThreads) {
-    const int arr = t / c4, i = t - arr * c4;
-    cp_async16(dst + arr * P4 + 4 * i, src + arr * P4 + 4 * i);
+  const float* src = packed + (gbase + blk) * R;
+  float* dst = stage + buf * R;
+  for (int i = tid; i < (R >> 2); i += kCandThreads) cp_async16(dst + 4 * i, src + 4 * i);
+}
+
+// Folds tile t of a staged record into the lane's minimum (4 points per step).
+__device__ __forceinline__ float tile_min(const float* rec, int t, int TC, int span, unsigned long long P2x,
+                                          unsigned long long P2y, unsigned long long P2z, float mn) {
+  const int c4 = (reinterpret_cast<const int*>(rec)[t] + 3) >> 2;
+  const float* base = rec + kHdr + t * TC;
+  const ulonglong2* X = reinterpret_cast<const ulonglong2*>(base);
+  const ulonglong2* Y = reinterpret_cast<const ulonglong2*>(base + span);
+  const ulonglong2* Z = reinterpret_cast<const ulonglong2*>(base + 2 * span);
+  float mn1 = INFINITY;
+#pragma unroll 2
+  for (int i = 0; i < c4; ++i) {
+    const ulonglong2 x = X[i], y = Y[i], z = Z[i];
+    {
+      const unsigned long long dx = f2_sub(P2x, x.x), dy = f2_sub(P2y, y.x), dz = f2_sub(P2z, z.x);
+      mn = f2_min(f2_add(f2_add(f2_mul(dx, dx), f2_mul(dy, dy)), f2_mul(dz, dz)), mn);
+    }
+    {
+      const unsigned long long dx = f2_sub(P2x, x.y), dy = f2_sub(P2y, y.y), dz = f2_sub(P2z, z.y);
+      mn1 = f2_min(f2_add(f2_add(f2_mul(dx, dx), f2_mul(dy, dy)), f2_mul(dz, dz)), mn1);
+    }
   }
+  return fminf(mn, mn1);
 }
 
 template <int WM>
-__global__ void __launch_bounds__(kCandThreads) view_candidates_kernel(
+__global__ void __launch_bounds__(kCandThreads, (WM <= 9 ? 8 : 6)) view_candidates_kernel(
     const float* __restrict__ pts, const int32_t* __restrict__ qc, long long n, ViewGeom g,
     const float* __restrict__ w2c, const float* __restrict__ tan_half, const float* __restrict__ crop,
     float max_dist, const int* __restrict__ sel_list, const int4* __restrict__ img_info,
@@ -214,8 +278,8 @@ __global__ void __launch_bounds__(kCandThreads) view_candidates_kernel(
     int* __restrict__ cand_id, int* err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int nwords = (g.nbi + 31) >> 5;
-  float* stage = reinterpret_cast<float*>(smem_raw);                  // [2][3 * P4]
-  unsigned* bitmap = reinterpret_cast<unsigned*>(stage + 6 * g.P4);   // [nwords]
+  float* stage = reinterpret_cast<float*>(smem_raw);                  // [2][R]
+  unsigned* bitmap = reinterpret_cast<unsigned*>(stage + 2 * g.R);    // [nwords]
   int* ulist = reinterpret_cast<int*>(bitmap + nwords);               // [nbi]
   __shared__ int s_ucount, s_blo, s_bhi;
 
@@ -347,10 +411,10 @@ __global__ void __launch_bounds__(kCandThreads) view_candidates_kernel(
       __syncthreads();
       const int ucount = s_ucount;
       const long long gbase = (long long)bm * g.nbi;
-      if (ucount > 0) stage_points(ulist[0], 0, gbase, g.P4, cnt, packed, stage, tid);
+      if (ucount > 0) stage_points(ulist[0], 0, gbase, g.R, packed, stage, tid);
       cp_async_commit();
       for (int u = 0; u < ucount; ++u) {
-        if (u + 1 < ucount) stage_points(ulist[u + 1], (u + 1) & 1, gbase, g.P4, cnt, packed, stage, tid);
+        if (u + 1 < ucount) stage_points(ulist[u + 1], (u + 1) & 1, gbase, g.R, packed, stage, tid);
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
@@ -360,25 +424,39 @@ __global__ void __launch_bounds__(kCandThreads) view_candidates_kernel(
         for (int i = 0; i < WM; ++i) want |= key[i] == blk;
         if (__any_sync(0xffffffffu, want)) {
           const int c = cnt[gbase + blk];
-          const int c4 = (c + 3) >> 2;
-          const float* sx = stage + (u & 1) * 3 * g.P4;
-          const ulonglong2* X = reinterpret_cast<const ulonglong2*>(sx);
-          const ulonglong2* Y = reinterpret_cast<const ulonglong2*>(sx + g.P4);
-          const ulonglong2* Z = reinterpret_cast<const ulonglong2*>(sx + 2 * g.P4);
-          float mn0 = INFINITY, mn1 = INFINITY;
-#pragma unroll 2
-          for (int i = 0; i < c4; ++i) {
-            const ulonglong2 x = X[i], y = Y[i], z = Z[i];
-            {
-              const unsigned long long dx = f2_sub(P2x, x.x), dy = f2_sub(P2y, y.x), dz = f2_sub(P2z, z.x);
-              mn0 = f2_min(f2_add(f2_add(f2_mul(dx, dx), f2_mul(dy, dy)), f2_mul(dz, dz)), mn0);
-            }
-            {
-              const unsigned long long dx = f2_sub(P2x, x.y), dy = f2_sub(P2y, y.y), dz = f2_sub(P2z, z.y);
-              mn1 = f2_min(f2_add(f2_add(f2_mul(dx, dx), f2_mul(dy, dy)), f2_mul(dz, dz)), mn1);
+          const float* rec = stage + (u & 1) * g.R;
+          const int span = g.NT * g.TC;
+          // per tile a lower bound of every point's d^2: the box gap per axis, squared and summed in the
+          // same order (each rounded step is monotone, so no point of the tile can come out below it)
+          float lb[kMaxTiles];
+          int first = 0;
+          float best = INFINITY;
+#pragma unroll
+          for (int t = 0; t < kMaxTiles; ++t) {
+            lb[t] = INFINITY;
+            if (t < g.NT) {
+              const float* bx = rec + kMaxTiles + 6 * t;
+              const float gx = fmaxf(fmaxf(__fsub_rn(bx[0], px), __fsub_rn(px, bx[3])), 0.f);
+              const float gy = fmaxf(fmaxf(__fsub_rn(bx[1], py), __fsub_rn(py, bx[4])), 0.f);
+              const float gz = fmaxf(fmaxf(__fsub_rn(bx[2], pz), __fsub_rn(pz, bx[5])), 0.f);
+              lb[t] = __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
+              if (lb[t] < best) {
+                best = lb[t];
+                first = t;
+              }
             }
           }
-          float dist = __fsqrt_rn(fminf(mn0, mn1));
+          // the tiles some lane bounds lowest first, then the others unless no lane can improve
+          const unsigned firsts = __reduce_or_sync(0xffffffffu, best < INFINITY ? 1u << first : 0u);
+          float mn = INFINITY;
+          for (unsigned f = firsts; f; f &= f - 1)
+            mn = tile_min(rec, __ffs(f) - 1, g.TC, span, P2x, P2y, P2z, mn);
+#pragma unroll
+          for (int t = 0; t < kMaxTiles; ++t) {
+            if (t < g.NT && !((firsts >> t) & 1u) && __any_sync(0xffffffffu, lb[t] < mn))
+              mn = tile_min(rec, t, g.TC, span, P2x, P2y, P2z, mn);
+          }
+          float dist = __fsqrt_rn(mn);
           if (c < g.P) dist = fminf(dist, max_dist);
 #pragma unroll
           for (int i = 0; i < WM; ++i)
@@ -400,8 +478,12 @@ __global__ void __launch_bounds__(kCandThreads) view_candidates_kernel(
   }
 }
 
-// Warp = query: rank its candidates by (value, position), keep the first
-// min(C, topk) in position order, pad with -1.
+// Warp = query: keep the K = min(C, topk) candidates smallest by (value,
+// position), in position order, pad with -1.  Values are non-negative
+// floats (distances or +inf), whose bit patterns order like the values: the
+// K-th smallest pattern is found bit by bit from the top (31 rounds of a
+// warp-wide count), then the candidates below it and, in position order, as
+// many equal to it as are missing are kept.
 template <int R>
 __global__ void __launch_bounds__(256) view_final_kernel(const int32_t* __restrict__ qc, long long n, int B,
                                                          const int* __restrict__ cand_total, int Cmax, int topk,
@@ -413,36 +495,40 @@ __global__ void __launch_bounds__(256) view_final_kernel(const int32_t* __restri
   const int b = qc[4 * q];
   const int C = (b >= 0 && b < B) ? cand_total[b] : 0;
   const int K = min(C, topk);
-  float v[R];
-  int id[R], rank[R];
+  unsigned key[R];
+  int id[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int pos = r * 32 + lane;
-    v[r] = pos < C ? cand_val[q * Cmax + pos] : INFINITY;
+    key[r] = pos < C ? __float_as_uint(cand_val[q * Cmax + pos]) : 0xffffffffu;  // padding sorts last
     id[r] = pos < C ? cand_id[q * Cmax + pos] : -1;
-    rank[r] = 0;
   }
-  const int RC = (C + 31) >> 5;
-  for (int ro = 0; ro < RC; ++ro) {
-    float vo = 0.f;
+  unsigned T = 0;  // the largest pattern with fewer than K keys below it = the K-th smallest key
+  if (K > 0) {
+    for (int bit = 30; bit >= 0; --bit) {  // bit 31 (sign) is clear in every key
+      const unsigned cand = T | (1u << bit);
+      int below = 0;
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-      if (r == ro) vo = v[r];
-    const int lim = min(32, C - ro * 32);
-    for (int l = 0; l < lim; ++l) {
-      const float vj = __shfl_sync(0xffffffffu, vo, l);
-      const int j = ro * 32 + l;
-#pragma unroll
-      for (int r = 0; r < R; ++r) rank[r] += (vj < v[r] || (vj == v[r] && j < r * 32 + lane)) ? 1 : 0;
+      for (int r = 0; r < R; ++r) below += __popc(__ballot_sync(0xffffffffu, key[r] < cand));
+      if (below < K) T = cand;
     }
   }
-  int base = 0;
+  int below = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) below += __popc(__ballot_sync(0xffffffffu, key[r] < T));
+  const int need = K - below;  // keys equal to T to keep, the first ones by position
+  const unsigned lt_mask = (1u << lane) - 1;
+  int base = 0, eq_seen = 0;
   int32_t* o = out + q * topk;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const bool sel = r * 32 + lane < C && rank[r] < K;
+    const bool valid = r * 32 + lane < C;
+    const bool eq = valid && key[r] == T;
+    const unsigned be = __ballot_sync(0xffffffffu, eq);
+    const bool sel = K > 0 && valid && (key[r] < T || (eq && eq_seen + __popc(be & lt_mask) < need));
+    eq_seen += __popc(be);
     const unsigned bal = __ballot_sync(0xffffffffu, sel);
-    if (sel) o[base + __popc(bal & ((1u << lane) - 1))] = id[r];
+    if (sel) o[base + __popc(bal & lt_mask)] = id[r];
     base += __popc(bal);
   }
   for (int s = K + lane; s < topk; s += 32) o[s] = -1;
@@ -473,7 +559,7 @@ ViewWs view_ws_layout(const ViewGeom& g, long long n, char* base) {
   w.sel_list = (int*)take(nb * 4);
   w.img_info = (int4*)take((size_t)g.B * g.M * 16);
   w.cand_total = (int*)take((size_t)g.B * 4);
-  w.packed = (float*)take(nb * 3 * g.P4 * 4);
+  w.packed = (float*)take(nb * g.R * 4);
   w.cand_val = (float*)take((size_t)n * g.Cmax * 4);
   w.cand_id = (int*)take((size_t)n * g.Cmax * 4);
   w.bytes = off;
@@ -481,7 +567,7 @@ ViewWs view_ws_layout(const ViewGeom& g, long long n, char* base) {
 }
 
 size_t cand_smem_bytes(const ViewGeom& g) {
-  return (size_t)6 * g.P4 * 4 + (size_t)((g.nbi + 31) / 32) * 4 + (size_t)g.nbi * 4;
+  return (size_t)2 * g.R * 4 + (size_t)((g.nbi + 31) / 32) * 4 + (size_t)g.nbi * 4;
 }
 
 int view_geom(int32_t batch, int32_t views, int32_t H, int32_t W, int32_t S, int32_t patch, int32_t block, int32_t win,
@@ -505,7 +591,11 @@ int view_geom(int32_t batch, int32_t views, int32_t H, int32_t W, int32_t S, int
   g->nbi = bh * bw;
   g->ib = S / bh;
   g->P = g->ib * g->ib;
-  g->P4 = (g->P + 3) & ~3;
+  g->T = (g->ib + 3) / 4;
+  g->nt = (g->ib + g->T - 1) / g->T;
+  g->NT = g->nt * g->nt;
+  g->TC = (g->T * g->T + 3) & ~3;
+  g->R = (kHdr + 3 * g->NT * g->TC + 3) & ~3;
   LSRM_CHECK_ARG(cand_smem_bytes(*g) <= 200 * 1024, "surface points per block (%d) exceed the shared-memory stage",
                  g->P);
   g->win = win;
