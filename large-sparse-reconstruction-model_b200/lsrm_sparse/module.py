@@ -157,3 +157,24 @@ class SpatialSparseAttentionOut(torch.nn.Module):
         # gate logits by a cuBLAS GEMM; sigmoid and the weighted sum fused in CUDA
         z = torch.nn.functional.linear(x, self.gate[0].weight)
         return F.gate_merge(z, branches, per_head=self.gate_mode == "per_head", head_dim=self.head_dim)
+
+
+class CrossSelfGate(torch.nn.Module):
+    """The closing step of CrossAttention for one token set
+    (models_sparse/utils.py:131-132, 559-570):
+    ``proj_x(x_cross * g[:, :dim] + x_self * g[:, dim:])`` with
+    ``g = sigmoid(gate_x(x))``.  The sigmoid and the two-way merge run as one
+    fused pass (``lsrm_gate_merge_fwd/bwd`` with two per-channel branches, fp32
+    inside); the two Linears are library GEMMs.  Parameter names follow the
+    reference (``gate_x.0``, ``proj_x``) so its state dict loads unchanged;
+    ``gate_x`` holds only the Linear because its Sigmoid is fused."""
+
+    def __init__(self, dim: int):
+        super().__init__()
+        self.dim = dim
+        self.gate_x = nn.Sequential(nn.Linear(dim, 2 * dim))
+        self.proj_x = nn.Linear(dim, dim)
+
+    def forward(self, x: torch.Tensor, x_cross: torch.Tensor, x_self: torch.Tensor) -> torch.Tensor:
+        logits = self.gate_x(x)
+        return self.proj_x(F.gate_merge(logits, [x_cross, x_self]))
