@@ -1150,6 +1150,141 @@ def run_view_maps(args):
         gpu_launches=int(launches), clocks=clk.summary())), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# --path decoder: a stack of BlockMix layers (models_sparse/utils.py:575-640)
+# over voxel and image tokens with the 3D-aware maps, forward + backward +
+# optimizer step (the sparse decoder's training step without its embedding
+# and upsampler)
+# ---------------------------------------------------------------------------
+
+# cfg4's decoder (24 layers, hidden 1024, 16 heads, MLP 4x, multi-head: 16 key/value heads; the
+# head-independent 3D-aware maps are repeated once per key/value head) and image side (8 views x 1024
+# tokens); the remaining settings are the reference's argument defaults
+DEC_CFG = dict(layers=24, dim=1024, q_heads=16, kv_heads=16, mlp_ratio=4.0, n_vol=524288, volume_res=512, views=8,
+               image_res=256, patch_size=8, block_size=8, surface_res=128, topk_volume=8, topk_multiimage=2,
+               attn_winsize=2, bbox_radius=0.5)
+
+
+def decoder_problem(seed, n_vol, dev):
+    import types
+
+    from lsrm_sparse import blocks, synth
+
+    c = DEC_CFG
+    vox, shell = synth.sdf_shell_voxels(c["volume_res"], n_vol, seed)
+    vol = np.zeros((len(vox), 4), np.int32)
+    vol[:, 1], vol[:, 2], vol[:, 3] = vox[:, 2], vox[:, 1], vox[:, 0]
+    volc = torch.from_numpy(vol).to(dev)
+    volc = volc[torch.argsort(blocks.volume_sort_keys(volc, c["volume_res"], c["block_size"]), stable=True)]
+    centres, radii = synth.scene_spheres(seed)
+    sc = synth.view_scene(centres, radii, 1, c["views"], c["image_res"], c["surface_res"], seed + 1)
+    sc["mask_input"][:] = 1.0  # every patch is a token: 8 x 1024 image tokens
+    imc = torch.from_numpy(synth.image_tokens(sc["mask_input"], c["patch_size"], c["block_size"])).to(dev)
+    args = types.SimpleNamespace(block_size=c["block_size"], volume_res=c["volume_res"], use_3d_aware_attn=True,
+                                 topk_volume=c["topk_volume"], bbox_radius=c["bbox_radius"],
+                                 attn_winsize=c["attn_winsize"], topk_multiimage=c["topk_multiimage"],
+                                 image_num_per_batch=c["views"], input_image_res=[c["image_res"] // 2, c["image_res"]],
+                                 patch_size=c["patch_size"])
+    batch = {"mask_input": torch.from_numpy(sc["mask_input"]).to(dev),
+             "cameras_input": torch.from_numpy(sc["cameras"]).to(dev)}
+    dense = {"surface_points_input": torch.from_numpy(sc["surface_points"]).to(dev),
+             "masks_input": torch.from_numpy(sc["surface_masks"]).to(dev)}
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    maps = blocks.build_3D_aware_attn(imc.contiguous(), volc.contiguous(), batch, dense, args)
+    for m in maps.values():  # one copy of the head-independent selection per key/value head
+        m["block_topk"] = m["block_topk"][:1].expand(c["kv_heads"], -1, -1).contiguous()
+    torch.cuda.synchronize()
+    map_ms = (time.perf_counter() - t0) * 1e3
+    return maps, volc.shape[0], imc.shape[0], shell, map_ms
+
+
+def run_decoder(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    c = DEC_CFG
+    n_req = args.decoder_tokens or c["n_vol"]
+    base = {"metric": "sparse decoder training step (voxel tokens/s)", "unit": "tokens/s", "higher_is_better": True}
+    if args.impl == "reference":
+        print(json.dumps(dict(base, impl="reference", unavailable="the reference decoder needs its Triton kernels "
+                              "and flash-attn on the GPU; its CPU path (Triton interpreter, fp16 only) takes ~24 s "
+                              "for one 256-token attention call, so a decoder step is out of reach")), flush=True)
+        return
+    from lsrm_sparse import _lib, ops
+    from lsrm_sparse.decoder import BlockMix
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    maps, nx, ny, shell, map_ms = decoder_problem(args.seed, n_req, dev)
+    torch.manual_seed(args.seed)
+    layers = torch.nn.ModuleList(
+        BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
+                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"]) for _ in range(c["layers"])
+    ).to(dev).to(torch.bfloat16)
+    opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
+    cu_x = torch.tensor([0, nx], dtype=torch.int32, device=dev)
+    cu_y = torch.tensor([0, ny], dtype=torch.int32, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    x_in = torch.randn(nx, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
+    y_in = torch.randn(ny, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
+    import torch.utils.checkpoint as cp
+
+    def step(x, y):
+        opt.zero_grad(set_to_none=True)
+        for blk in layers:  # one checkpoint per block (the reference's cp_freq = 1)
+            x, y, _ = cp.checkpoint(blk, x, cu_x, y, cu_y, maps, c["views"], use_reentrant=False)
+        loss = x.float().square().mean() + y.float().square().mean()
+        loss.backward()
+        opt.step()
+        return loss.detach()
+
+    for _ in range(args.warmup):
+        step(x_in, y_in)
+    torch.cuda.synchronize()
+    assert ops.read_errors() == 0
+    mem_gb = torch.cuda.max_memory_allocated(dev) / 2 ** 30
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(x_in, y_in)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    e2e = None
+    if not args.no_e2e:
+        xh, yh = x_in.cpu().pin_memory(), y_in.cpu().pin_memory()
+        loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss_h.copy_(step(xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": nx / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": (nx + ny) * c["dim"] * 2, "d2h_bytes_per_step": 4}
+    print(json.dumps(dict(
+        base, value=nx / (ms * 1e-3), n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
+        scaling="weak", vs_baseline=None, dtype="bf16",
+        config={"workload": f"{c['layers']} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
+                            f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
+                            f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
+                            f"({c['views']} views x 1024); 3D-aware maps (top-{c['topk_volume']} volume blocks, "
+                            f"{c['attn_winsize']}^2 window, top-{c['topk_multiimage'] * c['views']} image blocks); "
+                            f"one checkpoint per block; AdamW step",
+                "l2": "activations are far larger than L2"},
+        data=f"synthetic: seeded random-sphere shell ({shell} voxels before subsampling), N(0,1) token features, "
+             f"random-init weights",
+        attn_map_ms=map_ms, peak_mem_gib=mem_gb, cpu_baseline=None, e2e=e2e, gpu_launches=int(launches),
+        clocks=clk.summary())), flush=True)
+
+
 def F_layer_norm(x, D):
     return torch.nn.functional.layer_norm(x, (D,), eps=1e-5)
 
@@ -1166,13 +1301,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack",
-                                       "view_block_topk"],
+                                       "view_block_topk", "decoder"],
                     default="attention",
                     help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
                          "decoder's output formatting (prepare_volume_output); volume_geo_topk: the geometric "
                          "volume-to-volume block selection (build_volume_to_volume_attn); head_layernorm_pack: the "
                          "per-head LayerNorm fused with the Ulysses pack; view_block_topk: the volume-to-image "
-                         "block selection (build_volume_to_image_attn)")
+                         "block selection (build_volume_to_image_attn); decoder: a 24-layer BlockMix "
+                         "training step (decoder tokens/s)")
+    ap.add_argument("--decoder-tokens", type=int, default=0, help="voxel tokens of --path decoder (default cfg4's)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
@@ -1184,6 +1321,8 @@ def main():
         run_head_layernorm(args)
     elif args.path == "view_block_topk":
         run_view_maps(args)
+    elif args.path == "decoder":
+        run_decoder(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -81,8 +81,9 @@ def set_variant(variant: str):
 def sparse_window_attention(q, k, v, cu_block_include_tokens, softmax_scale=None):
     """Self-attention independently within each block."""
     n = q.shape[0]
-    cu_seq = torch.tensor([0, n], dtype=torch.int32, device=q.device)
-    cu_sb = torch.tensor([0, cu_block_include_tokens.numel() - 1], dtype=torch.int32, device=q.device)
+    two = torch.arange(2, dtype=torch.int32, device=q.device)  # built on the device: no host synchronisation
+    cu_seq = two * n
+    cu_sb = two * (cu_block_include_tokens.numel() - 1)
     meta = ops.Meta(cu_seq, cu_seq, cu_sb, cu_block_include_tokens)
     out, _ = F.dense_attention(q.contiguous(), k.contiguous(), v.contiguous(), meta, ops.DENSE_INTRA_BLOCK, 0,
                                softmax_scale)

@@ -101,6 +101,14 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 
 
+def _check_block_topk(block_topk, num_kv_heads: int, rows: int):
+    """The kernels read block_topk as [num_kv_heads, rows, topk]: reject any
+    other shape before it reaches them."""
+    if block_topk.dim() != 3 or tuple(block_topk.shape[:2]) != (num_kv_heads, rows):
+        raise ValueError(f"block_topk must be [num_kv_heads={num_kv_heads}, {rows}, topk], got "
+                         f"{tuple(block_topk.shape)}")
+
+
 def select_attn_fwd(q, k, v, block_topk, meta: Meta, softmax_scale=None, cu_query_blocks=None,
                     workspace: Optional[torch.Tensor] = None):
     """Returns (out [Nq,Hq,D], lse_log2 [Hq,Nq] fp32, workspace)."""
@@ -110,6 +118,7 @@ def select_attn_fwd(q, k, v, block_topk, meta: Meta, softmax_scale=None, cu_quer
     block_topk = _i32(block_topk)
     topk = block_topk.shape[-1]
     nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
+    _check_block_topk(block_topk, k.shape[1], nqb if nqb > 0 else q.shape[0])
     cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
     vl = meta.struct(q.shape[0], k.shape[0])
     sh = _shape(q, k, softmax_scale)
@@ -136,6 +145,7 @@ def select_attn_bwd(q, k, v, out, lse, dout, block_topk, meta: Meta, softmax_sca
     block_topk = _i32(block_topk)
     topk = block_topk.shape[-1]
     nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
+    _check_block_topk(block_topk, k.shape[1], nqb if nqb > 0 else q.shape[0])
     cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
     vl = meta.struct(q.shape[0], k.shape[0])
     sh = _shape(q, k, softmax_scale)

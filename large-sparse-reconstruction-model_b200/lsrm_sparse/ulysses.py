@@ -269,8 +269,9 @@ def whole_sequence_branches(q, k, v, z, cu_blk, topk: int, window: int, softmax_
     Hkv = k.shape[1]
     nb = cu_blk.numel() - 1
     dev = q.device
-    cu_seq = torch.tensor([0, N], dtype=torch.int32, device=dev)
-    cu_sb = torch.tensor([0, nb], dtype=torch.int32, device=dev)
+    two = torch.arange(2, dtype=torch.int32, device=dev)  # built on the device: no host synchronisation
+    cu_seq = two * N
+    cu_sb = two * nb
     meta = ops.Meta(cu_seq, cu_seq, cu_sb, cu_blk)
     meta_c = ops.Meta(cu_seq, cu_seq, cu_sb, torch.arange(nb + 1, dtype=torch.int32, device=dev))
     ck = F.block_mean(k.reshape(N, Hkv * D), cu_blk).view(nb, Hkv, D)
