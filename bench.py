@@ -1218,9 +1218,10 @@ def run_decoder(args):
     torch.cuda.set_device(dev)
     maps, nx, ny, shell, map_ms = decoder_problem(args.seed, n_req, dev)
     torch.manual_seed(args.seed)
+    n_layers = args.decoder_layers or c["layers"]
     layers = torch.nn.ModuleList(
         BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
-                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"]) for _ in range(c["layers"])
+                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"]) for _ in range(n_layers)
     ).to(dev).to(torch.bfloat16)
     opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
     cu_x = torch.tensor([0, nx], dtype=torch.int32, device=dev)
@@ -1256,6 +1257,14 @@ def run_decoder(args):
         torch.cuda.synchronize()
     launches = _lib.launch_count() - n0
     ms = e0.elapsed_time(e1) / args.steps
+    if args.torch_profile:  # per-kernel device time of one more step, as a table on stderr
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            step(x_in, y_in)
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=70),
+              file=sys.stderr, flush=True)
     e2e = None
     if not args.no_e2e:
         xh, yh = x_in.cpu().pin_memory(), y_in.cpu().pin_memory()
@@ -1272,7 +1281,7 @@ def run_decoder(args):
     print(json.dumps(dict(
         base, value=nx / (ms * 1e-3), n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
         scaling="weak", vs_baseline=None, dtype="bf16",
-        config={"workload": f"{c['layers']} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
+        config={"workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
                             f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
                             f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
                             f"({c['views']} views x 1024); 3D-aware maps (top-{c['topk_volume']} volume blocks, "
@@ -1310,6 +1319,9 @@ def main():
                          "block selection (build_volume_to_image_attn); decoder: a 24-layer BlockMix "
                          "training step (decoder tokens/s)")
     ap.add_argument("--decoder-tokens", type=int, default=0, help="voxel tokens of --path decoder (default cfg4's)")
+    ap.add_argument("--decoder-layers", type=int, default=0, help="layers of --path decoder (default 24)")
+    ap.add_argument("--torch-profile", action="store_true",
+                    help="--path decoder: print torch.profiler's per-kernel table of one extra step on stderr")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
