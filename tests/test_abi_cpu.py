@@ -90,6 +90,7 @@ def _fwd(lib, meta, shape, topk=4, ws=None, ws_bytes=0):
     (dict(dtype=7), "LSRM_ERR_INVALID_ARG", "dtype"),
     (dict(Hq=6, Hkv=2), "LSRM_ERR_INVALID_ARG", "power of two"),
     (dict(Hq=5, Hkv=2), "LSRM_ERR_INVALID_ARG", "multiple"),
+    (dict(Hq=16, Hkv=2), "LSRM_ERR_INVALID_ARG", "open fault"),  # 8 query heads per kv head, 2 kv heads
 ])
 def test_select_fwd_rejects_bad_shapes_on_host(lib, bad, code, msg):
     rc = _fwd(lib, _meta(), _shape(**bad))
