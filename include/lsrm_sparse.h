@@ -253,6 +253,14 @@ int lsrm_gate_merge_bwd(int32_t total_tokens, int32_t channels, int32_t n_branch
 int lsrm_volume_sort_keys(int64_t n_tokens, const int32_t* coords, int32_t volume_res, int32_t block_size,
                           int64_t* keys, void* stream);
 
+/* sort_image_blocks (misc/sparse_utils.py:95-124): keys [n] int64 of image
+ * tokens coords [n, 4] int32 (batch, view, patch row, patch column) with the
+ * reference's offsets (views = the view count it reads as coords[:, 1].max() + 1,
+ * patch_res = input_image_res[1] / patch_size); argsort of the keys is the
+ * block-major order. */
+int lsrm_image_sort_keys(int64_t n_tokens, const int32_t* coords, int32_t views, int32_t patch_res,
+                         int32_t block_size, int64_t* keys, void* stream);
+
 /* compute_block_separation (misc/sparse_utils.py:592-641): coords
  * [n, dim+1] int32 (batch, then dim coordinates), grouped by batch; host
  * arrays block_size[dim], resolution[dim] (cells per dimension =

@@ -46,6 +46,19 @@ __global__ void volume_keys_kernel(const int32_t* __restrict__ coords, long long
   }
 }
 
+// sort_image_blocks (misc/sparse_utils.py:95-124): image tokens (batch, view,
+// patch row, patch column) by batch, view, block row, block column, then row
+// and column inside the block, with the reference's offsets.
+__global__ void image_keys_kernel(const int32_t* __restrict__ coords, long long n, int views, int pr, int bs,
+                                  int64_t* __restrict__ keys) {
+  const long long o1 = (long long)views * pr * pr, o2 = (long long)pr * pr, o3 = (long long)pr * bs,
+                  o4 = (long long)bs * bs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int4 c = reinterpret_cast<const int4*>(coords)[i];
+    keys[i] = o1 * c.x + o2 * c.y + o3 * (c.z / bs) + o4 * (c.w / bs) + (long long)bs * (c.z % bs) + (c.w % bs);
+  }
+}
+
 __global__ void block_hist_kernel(SepParams p) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x) {
     const int32_t* c = p.coords + i * (p.dim + 1);
@@ -246,6 +259,17 @@ extern "C" int lsrm_volume_sort_keys(int64_t n_tokens, const int32_t* coords, in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ProfScope ps("volume_keys", s);
   volume_keys_kernel<<<grid_of(n_tokens, 256), 256, 0, s>>>(coords, n_tokens, volume_res, block_size, keys);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+extern "C" int lsrm_image_sort_keys(int64_t n_tokens, const int32_t* coords, int32_t views, int32_t patch_res,
+                                    int32_t block_size, int64_t* keys, void* stream) {
+  LSRM_CHECK_ARG(n_tokens >= 0 && views > 0 && patch_res > 0 && block_size > 0, "bad sizes");
+  LSRM_CHECK_ARG(((uintptr_t)coords & 15) == 0, "coords must be 16-byte aligned ([n, 4] int32)");
+  if (n_tokens == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  image_keys_kernel<<<grid_of(n_tokens, 256), 256, 0, s>>>(coords, n_tokens, views, patch_res, block_size, keys);
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }

@@ -141,6 +141,7 @@ _SIGS = {
         c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, ctypes.c_float,
                 c_int32, c_void_p, c_void_p, c_void_p, c_void_p]
     ),
+    "lsrm_image_sort_keys": (c_int, [c_int64, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "lsrm_voxel_points": (c_int, [c_void_p, c_int64, c_int32, ctypes.c_float, c_void_p, c_void_p]),
     "lsrm_image_token_points": (
         c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,

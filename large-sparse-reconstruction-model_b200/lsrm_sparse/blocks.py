@@ -40,6 +40,33 @@ def sort_volume_blocks(feats, coords, args, coords_idx=None):
     return feats[coords_idx, :], coords[coords_idx, :], coords_idx
 
 
+def image_sort_keys(coords: torch.Tensor, views: int, patch_res: int, block_size: int) -> torch.Tensor:
+    """int64 key per image token: batch, view, block row, block column,
+    position in the block (misc/sparse_utils.py:97-116)."""
+    L = _lib.lib()
+    coords = coords.to(torch.int32).contiguous()
+    if coords.dim() != 2 or coords.shape[1] != 4:
+        raise ValueError("coords must be [n, 4] (batch, view, patch row, patch column)")
+    keys = torch.empty(coords.shape[0], dtype=torch.int64, device=coords.device)
+    rc = L.lsrm_image_sort_keys(coords.shape[0], ops._ptr(coords), int(views), int(patch_res), int(block_size),
+                                ops._ptr(keys), ops._stream())
+    check(rc, "lsrm_image_sort_keys")
+    return keys
+
+
+def sort_image_blocks(feats, coords, args, coords_idx=None):
+    """``sort_image_blocks`` (misc/sparse_utils.py:95-124): reorders image
+    tokens block-major; returns ``(feats, coords, coords_idx)``.  ``args``
+    needs ``block_size``, ``patch_size`` and ``input_image_res``.  One host
+    synchronisation for the view count, as the reference."""
+    if coords_idx is None:
+        views = int(coords[:, 1].max().item()) + 1
+        keys = image_sort_keys(coords, views, int(args.input_image_res[1]) // int(args.patch_size),
+                               int(args.block_size))
+        coords_idx = torch.argsort(keys)
+    return feats[coords_idx, :], coords[coords_idx, :], coords_idx
+
+
 def compute_block_separation(k_coords: torch.Tensor, DIM: int, block_size: Sequence[int], batch_size: int,
                              resolution: Sequence[int]):
     """``(cu_seqblocks, cu_block_include_tokens)`` int32 on the coordinates'

@@ -14,6 +14,7 @@ against them.
 """
 
 from .nsa_oracle import *  # noqa: F401,F403
-from .attn_maps import (camera_terms, fma32, image_token_points, image_volume_block_topk,  # noqa: F401
+from .attn_maps import (camera_terms, fma32, image_sort_keys, image_token_points,  # noqa: F401
+                        image_volume_block_topk,
                         project_to_blocks, view_block_geometry, view_block_topk, view_rows_equivalent,
                         voxel_points)

@@ -317,3 +317,13 @@ def view_rows_equivalent(ours, ref, detail, win: int):
         if not ok:
             bad.append(t)
     return bad
+
+
+def image_sort_keys(coords, views: int, patch_res: int, block_size: int):
+    """sort_image_blocks' key (misc/sparse_utils.py:97-116) in int64:
+    batch, view, block row, block column, row and column in the block."""
+    c = np.asarray(coords).astype(np.int64)
+    bs = int(block_size)
+    o1, o2, o3, o4 = views * patch_res * patch_res, patch_res * patch_res, patch_res * bs, bs * bs
+    return (o1 * c[:, 0] + o2 * c[:, 1] + o3 * (c[:, 2] // bs) + o4 * (c[:, 3] // bs) + bs * (c[:, 2] % bs)
+            + c[:, 3] % bs)

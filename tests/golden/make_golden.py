@@ -15,6 +15,7 @@ What runs, all unmodified reference code:
 * ``sort_volume_blocks`` / ``compute_block_separation``
   (misc/sparse_utils.py:126-152, 592-641): block metadata of voxel and
   image-patch coordinates.
+* ``sort_image_blocks`` (misc/sparse_utils.py:95-124, ``--only imsort``).
 * ``build_image_to_image_attn``, ``build_image_to_volume_attn``,
   ``build_volume_to_image_attn`` and ``from_imcoords_to_points``
   (misc/sparse_utils.py:653-1200) on posed views of a sphere scene from
@@ -337,10 +338,32 @@ def make_image_maps(sparse_utils, seed, crop):
     return out
 
 
+def make_image_sort(sparse_utils, seed):
+    """sort_image_blocks (misc/sparse_utils.py:95-124) on shuffled image
+    tokens of two batch elements, three views of 16 x 16 patches, blocks of
+    4 x 4 patches."""
+    import types
+
+    gen = torch.Generator().manual_seed(seed)
+    parts = []
+    for b in range(2):
+        v, r, c = torch.meshgrid(torch.arange(3), torch.arange(16), torch.arange(16), indexing="ij")
+        keep = torch.rand(v.numel(), generator=gen) < 0.5
+        parts.append(torch.stack([torch.full((int(keep.sum()),), b), v.flatten()[keep], r.flatten()[keep],
+                                  c.flatten()[keep]], 1))
+    coords = torch.cat(parts).to(torch.int32)
+    coords = coords[torch.randperm(coords.shape[0], generator=gen)]
+    args = types.SimpleNamespace(block_size=4, patch_size=8, input_image_res=[64, 128])
+    feats = torch.arange(coords.shape[0], dtype=torch.float32)[:, None]
+    _, sorted_coords, idx = sparse_utils.sort_image_blocks(feats, coords.clone(), args)
+    return dict(coords=coords.numpy(), sorted_coords=sorted_coords.numpy(), sort_idx=idx.numpy().astype(np.int64),
+                block_size=np.int32(4), patch_size=np.int32(8), image_res=np.int32(128))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image"], default=None,
+    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image", "imsort"], default=None,
                     help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
@@ -348,6 +371,10 @@ def main():
     sys.path.insert(0, args.ref)
     from misc import sparse_utils
 
+    if args.only == "imsort":
+        np.savez_compressed(os.path.join(HERE, "image_sort.npz"), **make_image_sort(sparse_utils, 81))
+        print("wrote image_sort")
+        return
     if args.only == "image":
         for crop in (False, True):
             name = "image_maps_crop" if crop else "image_maps"

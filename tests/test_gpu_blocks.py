@@ -72,3 +72,21 @@ def test_block_separation_bad_batch_id_sets_error_bit():
     coords = np.array([[0, 0, 0, 0], [3, 1, 1, 1]], dtype=np.int32)
     blocks.block_separation(torch.from_numpy(coords).cuda(), 3, [2, 2, 2], 2, [4, 4, 4])
     assert ops.read_errors() & _lib.LSRM_ERR_BAD_INDEX
+
+
+def test_sort_image_blocks_matches_reference_fixture(golden):
+    """lsrm_image_sort_keys + argsort (sort_image_blocks) vs the reference's
+    own output on shuffled image tokens."""
+    import types
+
+    from lsrm_sparse import blocks
+
+    g = golden("image_sort")
+    coords = torch.from_numpy(g["coords"]).cuda()
+    args = types.SimpleNamespace(block_size=int(g["block_size"]), patch_size=int(g["patch_size"]),
+                                 input_image_res=[int(g["image_res"]) // 2, int(g["image_res"])])
+    feats = torch.arange(coords.shape[0], dtype=torch.float32, device="cuda")[:, None]
+    f, c, idx = blocks.sort_image_blocks(feats, coords, args)
+    assert np.array_equal(idx.cpu().numpy(), g["sort_idx"])
+    assert np.array_equal(c.cpu().numpy(), g["sorted_coords"])
+    assert np.array_equal(f[:, 0].long().cpu().numpy(), g["sort_idx"])

@@ -232,3 +232,15 @@ def test_image_maps_match_reference(golden, name):
             planted[row, 0] = far[-1]
             assert row in oracle.view_rows_equivalent(out, planted, det, c["win"])
     assert equal_rows > 0.8 * (g["imcoords"].shape[0] + g["volcoords"].shape[0])
+
+
+def test_image_sort_matches_reference(golden):
+    """sort_image_blocks' key restated in the oracle gives the reference's
+    order (misc/sparse_utils.py:95-124)."""
+    g = golden("image_sort")
+    c = g["coords"]
+    keys = oracle.image_sort_keys(c, int(c[:, 1].max()) + 1, int(g["image_res"]) // int(g["patch_size"]),
+                                  int(g["block_size"]))
+    idx = np.argsort(keys, kind="stable")
+    assert np.array_equal(idx, g["sort_idx"])
+    assert np.array_equal(c[idx], g["sorted_coords"])
