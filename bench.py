@@ -1189,8 +1189,9 @@ def decoder_problem(seed, n_vol, dev):
              "cameras_input": torch.from_numpy(sc["cameras"]).to(dev)}
     dense = {"surface_points_input": torch.from_numpy(sc["surface_points"]).to(dev),
              "masks_input": torch.from_numpy(sc["surface_masks"]).to(dev)}
+    maps = blocks.build_3D_aware_attn(imc.contiguous(), volc.contiguous(), batch, dense, args)  # first call: loads
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    t0 = time.perf_counter()  # the steady-state construction time, as every training step pays it
     maps = blocks.build_3D_aware_attn(imc.contiguous(), volc.contiguous(), batch, dense, args)
     for m in maps.values():  # one copy of the head-independent selection per key/value head
         m["block_topk"] = m["block_topk"][:1].expand(c["kv_heads"], -1, -1).contiguous()
