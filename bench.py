@@ -315,11 +315,14 @@ def run_reference(args, cfg):
     if rank != 0:
         return
     p = Problem(cfg, args.seed, "cpu", pin=False)  # host tensors only
+    # a third of the baseline's sample per step and two query blocks per warm-up, so that the default
+    # 3 + 10 steps end within a few minutes on the host
+    per_step = max(4, args.cpu_qblocks // 3)
     for _ in range(args.warmup):
-        cpu_sample(p, args.cpu_qblocks, args.seed)
+        cpu_sample(p, 2, args.seed)
     vals, secs = [], []
     for i in range(args.steps):
-        r = cpu_sample(p, args.cpu_qblocks, args.seed + 1 + i)
+        r = cpu_sample(p, per_step, args.seed + 1 + i)
         vals.append(r["value"])
         secs.append(r["seconds"])
     v = statistics.median(vals)
