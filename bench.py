@@ -367,6 +367,9 @@ def run_ours(args, cfg):
     if ws > 1:
         import datetime
 
+        # NCCL's version banner goes to stdout, where the one JSON result line belongs
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
     from lsrm_sparse import _lib, ops
