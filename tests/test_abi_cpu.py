@@ -134,3 +134,18 @@ def test_ops_fail_loudly_without_a_device():
     meta = ops.Meta(cu, cu, torch.tensor([0, 1], dtype=torch.int32), cu)
     with pytest.raises(Exception):
         ops.select_attn_fwd(q, q, q, torch.zeros(2, 8, 1, dtype=torch.int32), meta)
+
+
+def test_view_block_topk_workspace_query_validates_geometry(lib):
+    """lsrm_view_block_topk_workspace_bytes runs on the host: a positive size
+    for a supported view geometry, 0 with a message for the unsupported ones
+    (window > 25, views x window > 512, unequal blocks per side)."""
+    h = lib.lib()
+    ok = h.lsrm_view_block_topk_workspace_bytes(1, 16, 768, 768, 384, 8, 8, 9, 131072)
+    assert ok > 131072 * 16 * 9 * 8  # at least the candidate lists
+    assert h.lsrm_view_block_topk_workspace_bytes(1, 16, 768, 768, 384, 8, 8, 26, 1024) == 0
+    assert "window" in h.lsrm_last_error().decode()
+    assert h.lsrm_view_block_topk_workspace_bytes(1, 64, 768, 768, 384, 8, 8, 9, 1024) == 0
+    assert "512" in h.lsrm_last_error().decode()
+    assert h.lsrm_view_block_topk_workspace_bytes(1, 4, 768, 512, 384, 8, 8, 4, 1024) == 0
+    assert "blocks per side" in h.lsrm_last_error().decode()
