@@ -149,3 +149,25 @@ def test_view_block_topk_workspace_query_validates_geometry(lib):
     assert "512" in h.lsrm_last_error().decode()
     assert h.lsrm_view_block_topk_workspace_bytes(1, 4, 768, 512, 384, 8, 8, 4, 1024) == 0
     assert "blocks per side" in h.lsrm_last_error().decode()
+
+
+def test_new_entry_points_reject_bad_arguments_on_host(lib):
+    """Argument checks of the map, token and norm entry points run before any
+    launch (the dummy pointers below are never dereferenced)."""
+    h = lib.lib()
+    p = ctypes.c_void_p(16)
+    bad = _header_define("LSRM_ERR_INVALID_ARG")
+    # top-k beyond 64
+    assert h.lsrm_volume_block_topk(p, 100, p, p, 1, 32, 0.5, 65, p, p, p, None) == bad
+    assert "topk" in h.lsrm_last_error().decode()
+    assert h.lsrm_points_volume_block_topk(p, p, 100, p, 100, p, p, 1, 32, 0.5, 0, p, p, p, None) == bad
+    # surface grid not a multiple of the patch grid
+    assert h.lsrm_image_token_points(p, 10, p, p, 1, 1, 30, 16, p, p, None) == bad
+    assert "multiple" in h.lsrm_last_error().decode()
+    # head_dim outside 16..256 powers of two; heads not divisible by the world size
+    assert h.lsrm_head_layernorm_pack(10, 16, 48, 1, 1, 16 * 48, 1e-5, p, p, None) == bad
+    assert "head_dim" in h.lsrm_last_error().decode()
+    assert h.lsrm_head_layernorm_pack(10, 6, 64, 4, 1, 6 * 64, 1e-5, p, p, None) == bad
+    # misaligned coordinates
+    assert h.lsrm_image_sort_keys(10, ctypes.c_void_p(20), 2, 16, 4, p, None) == bad
+    assert "aligned" in h.lsrm_last_error().decode()
