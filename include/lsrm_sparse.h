@@ -143,9 +143,10 @@ int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, 
  * results as lsrm_select_attn_fwd; the selection plan lives in a fixed
  * LSRM_NOALLOC_SCRATCH_BYTES device array inside the library.  Problems whose
  * plan exceeds it are rejected with LSRM_ERR_WORKSPACE and a message.  The
- * first call on each device resolves the array's device address (make that
- * first call before any stream capture); all calls share the array, so calls
- * that overlap on the GPU race on it. */
+ * array's device address differs per CUDA context, so the first call in each
+ * context (each device's primary context, or a context the host made current)
+ * resolves it (make that first call before any stream capture); all calls in
+ * a context share the array, so calls that overlap on the GPU race on it. */
 int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q,
                                  const void* k, const void* v, const int32_t* block_topk, int32_t topk,
                                  const int32_t* cu_query_blocks, int32_t num_query_blocks, void* out,

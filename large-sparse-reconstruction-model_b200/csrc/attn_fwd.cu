@@ -219,25 +219,68 @@ namespace lsrm {
 
 static __device__ __align__(256) uint8_t g_select_fwd_scratch[LSRM_NOALLOC_SCRATCH_BYTES];
 
-// Device address of the scratch array, resolved once per device on the first
-// call made with that device current (host code cannot use the symbol itself:
-// on the host it names a stand-in, not device memory).
+// Device address of the scratch array.  A __device__ array has its own address
+// in every CUDA context (the runtime's primary context of each device, a
+// driver-API context a plugin host made current, a context re-created after
+// cudaDeviceReset), so the address is resolved on the first call in each
+// context and cached under the context's process-unique id (cuCtxGetId), which
+// a destroyed context never passes on to a new one.  Host code cannot use the
+// symbol itself: on the host it names a stand-in, not device memory.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
 static int noalloc_scratch_ptr(void** out) {
   static std::mutex mu;
-  static void* cache[128] = {};
-  int dev = 0;
-  LSRM_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 128) {
-    set_error("device ordinal %d out of range", dev);
-    return LSRM_ERR_UNSUPPORTED;
-  }
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  constexpr int kSlots = 64;
+  static unsigned long long ids[kSlots] = {};
+  static void* ptrs[kSlots] = {};
+  static int next_slot = 0;
   std::lock_guard<std::mutex> g(mu);
-  if (!cache[dev]) {
-    void* p = nullptr;
-    LSRM_CUDA_TRY(cudaGetSymbolAddress(&p, g_select_fwd_scratch));
-    cache[dev] = p;
+  if (!get_current || !get_id) {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) != cudaSuccess ||
+        qa != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) != cudaSuccess ||
+        qb != cudaDriverEntryPointSuccess) {
+      set_error("cuCtxGetCurrent / cuCtxGetId are unavailable from the driver");
+      return LSRM_ERR_CUDA;
+    }
+    get_current = reinterpret_cast<CtxGetCurrentFn>(a);
+    get_id = reinterpret_cast<CtxGetIdFn>(b);
   }
-  *out = cache[dev];
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) {
+    set_error("cuCtxGetCurrent failed");
+    return LSRM_ERR_CUDA;
+  }
+  void* p = nullptr;
+  if (!ctx) {  // no context current yet: the runtime makes its primary context current here
+    LSRM_CUDA_TRY(cudaGetSymbolAddress(&p, g_select_fwd_scratch));
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) {
+      set_error("no CUDA context is current");
+      return LSRM_ERR_CUDA;
+    }
+  }
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS || id == 0) {
+    set_error("cuCtxGetId failed");
+    return LSRM_ERR_CUDA;
+  }
+  for (int i = 0; i < kSlots; ++i) {
+    if (ids[i] == id) {
+      *out = ptrs[i];
+      return LSRM_OK;
+    }
+  }
+  if (!p) LSRM_CUDA_TRY(cudaGetSymbolAddress(&p, g_select_fwd_scratch));
+  ids[next_slot] = id;  // oldest entry makes room once every slot is taken
+  ptrs[next_slot] = p;
+  next_slot = (next_slot + 1) % kSlots;
+  *out = p;
   return LSRM_OK;
 }
 

@@ -122,6 +122,24 @@ def test_noalloc_scratch_bound_is_the_header_constant(lib):
     assert m and int(m.group(1)) << int(m.group(2)) == 16 << 20
 
 
+def test_noalloc_rejects_an_oversized_plan_on_host(lib):
+    """The size check of the allocation-free forward runs before any CUDA
+    call: a per-token selection over 32768 queries, 4096 blocks and top-64
+    needs far more than the fixed scratch (the pointers are never used)."""
+    h = lib.lib()
+    p = ctypes.c_void_p(256)
+    meta = _meta(32768, 4096)
+    shape = _shape(Hq=4, Hkv=4)
+    rc = h.lsrm_select_attn_fwd_noalloc(ctypes.byref(meta), ctypes.byref(shape), p, p, p, p, 64, None, 0, p, p,
+                                        None, None)
+    assert rc == _header_define("LSRM_ERR_WORKSPACE")
+    assert "plan scratch" in h.lsrm_last_error().decode()
+    # a bad shape is still reported as such, before the size check
+    rc = h.lsrm_select_attn_fwd_noalloc(ctypes.byref(meta), ctypes.byref(_shape(D=48)), p, p, p, p, 64, None, 0, p,
+                                        p, None, None)
+    assert rc == _header_define("LSRM_ERR_INVALID_ARG")
+
+
 def test_ops_fail_loudly_without_a_device():
     import torch
 
