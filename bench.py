@@ -38,13 +38,14 @@ CONFIGS = {
                  gate="per_head", voxel=True),
     # configs[0] at its sizes (contiguous uniform blocks), on the GPU
     "cfg1": dict(n=4096, heads=8, head_dim=64, n_blocks=64, blk_min=32, blk_max=96, topk=8, window=128,
-                 gate="per_head", voxel=False),
+                 gate="per_head", voxel=False, qkv_scale=0.5),
     # half-size cfg2 (same grid, block sizes, top-k, window) for full ncu captures
     "cfg2s": dict(n=65536, heads=16, head_dim=64, res=256, blk_min=64, blk_max=256, topk=16, window=512,
                   gate="per_head", voxel=True),
-    # 512^3 shell, blocks 32-512, window 1024
+    # 512^3 shell, blocks 32-512, window 1024, K/V compressed by the token-wise ResBlock
+    # (2 x Linear(C -> C), C = H * head_dim) before the block mean
     "cfg3": dict(n=262144, heads=16, head_dim=64, res=512, blk_min=32, blk_max=512, topk=16, window=1024,
-                 gate="per_head", voxel=True),
+                 gate="per_head", voxel=True, compression="resblock"),
 }
 
 
@@ -82,13 +83,21 @@ class Problem:
         g = torch.Generator(device="cpu").manual_seed(seed)
         pinned = (lambda t: t.pin_memory()) if pin else (lambda t: t)
         # host copies (pinned) for the end-to-end path
-        self.h_q = pinned(torch.randn(N, H, D, generator=g).bfloat16())
-        self.h_k = pinned(torch.randn(N, H, D, generator=g).bfloat16())
-        self.h_v = pinned(torch.randn(N, H, D, generator=g).bfloat16())
+        sc = cfg.get("qkv_scale", 1.0)
+        self.h_q = pinned((torch.randn(N, H, D, generator=g) * sc).bfloat16())
+        self.h_k = pinned((torch.randn(N, H, D, generator=g) * sc).bfloat16())
+        self.h_v = pinned((torch.randn(N, H, D, generator=g) * sc).bfloat16())
         self.h_x = pinned(torch.randn(N, self.hidden, generator=g).bfloat16())
         self.h_g = pinned((torch.randn(N, self.hidden, generator=g) * 0.1).bfloat16())
         n_gate = 3 * H if cfg["gate"] == "per_head" else 3 * self.hidden
         self.gate_w = (torch.randn(n_gate, self.hidden, generator=g) / math.sqrt(self.hidden)).bfloat16()
+        # ResBlock compression weights (nn.Linear's default init range), bf16 like the step
+        self.compression = cfg.get("compression", "mean")
+        self.res_w = None
+        if self.compression == "resblock":
+            C, bound = self.hidden, 1.0 / math.sqrt(self.hidden)
+            u = lambda *shape: ((torch.rand(*shape, generator=g) * 2 - 1) * bound).bfloat16()  # noqa: E731
+            self.res_w = {s: (u(C, C), u(C), u(C, C), u(C)) for s in ("k", "v")}
         cu_blk = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
         self.h_cu_blk = pinned(cu_blk)
         self.h_cu_seq = pinned(torch.tensor([0, N], dtype=torch.int32))
@@ -105,6 +114,13 @@ class Problem:
         self.q, self.k, self.v, self.x = (t.requires_grad_() for t in (q, k, v, x))
         if not hasattr(self, "wg"):
             self.wg = self.gate_w.to(self.device).requires_grad_()
+            self.compress = make_compress(self.res_w, self.device)
+
+    def params(self):
+        ps = [self.wg]
+        if self.compress is not None:
+            ps += list(self.compress.params)
+        return ps
 
     def to_device(self, non_blocking=False):
         self.adopt([t.to(self.device, non_blocking=non_blocking) for t in self.host_inputs()])
@@ -113,32 +129,49 @@ class Problem:
         return int(sum(t.numel() * t.element_size() for t in self.host_inputs()))
 
 
+def make_compress(res_w, device):
+    """The ResBlock compression of SpatialSparseAttentionIn (a SparseResBlock
+    per K and V, then the block mean; spatial_sparse_attention.py:46-66) with
+    the given weights, or None for the plain block mean."""
+    if res_w is None:
+        return None
+    from lsrm_sparse.module import SparseResBlock
+
+    mods = {}
+    for s in ("k", "v"):
+        m = SparseResBlock(res_w[s][0].shape[0]).to(device).bfloat16()
+        with torch.no_grad():
+            m.act_layers[0].weight.copy_(res_w[s][0])
+            m.act_layers[0].bias.copy_(res_w[s][1])
+            m.act_layers[2].weight.copy_(res_w[s][2])
+            m.act_layers[2].bias.copy_(res_w[s][3])
+        mods[s] = m
+
+    def compress(k2, v2, cu_blk):
+        return mods["k"].forward_block_mean(k2, cu_blk), mods["v"].forward_block_mean(v2, cu_blk)
+
+    compress.params = [t for m in mods.values() for t in m.parameters()]
+    compress.modules = mods
+    return compress
+
+
 def forward_backward(p: Problem, want_loss=False, capture=None):
-    """One step through the public API (lsrm_sparse.functional / ops)."""
+    """One step through the public API: lsrm_sparse.functional.three_branch_attention
+    (the same function every rank runs under sequence parallelism), the gate
+    Linear, and the backward of all of it."""
     from lsrm_sparse import functional as F
-    from lsrm_sparse import ops
 
     cfg = p.cfg
-    N, H, D, nb = p.N, p.H, p.D, p.nb
-    meta = ops.Meta(p.cu_seq, p.cu_seq, p.cu_sb, p.cu_blk)
-    dummy = torch.arange(nb + 1, dtype=torch.int32, device=p.device) if not hasattr(p, "_cblk") else p._cblk
-    p._cblk = dummy
-    meta_c = ops.Meta(p.cu_seq, p.cu_seq, p.cu_sb, dummy)
-    ck = F.block_mean(p.k.view(N, H * D), p.cu_blk).view(nb, H, D)
-    cv = F.block_mean(p.v.view(N, H * D), p.cu_blk).view(nb, H, D)
-    o_c, lse = F.dense_attention(p.q, ck, cv, meta_c, ops.DENSE_COMPRESSED)
-    with torch.no_grad():
-        bt = ops.block_topk(p.q, ck, lse, cfg["topk"], meta_c, cu_query_blocks=p.cu_blk, force_self=True)
-    if capture is not None:
-        capture["block_topk"] = bt
-    o_s, _ = F.select_attention(p.q, p.k, p.v, bt, meta, None, p.cu_blk)
-    o_w, _ = F.dense_attention(p.q, p.k, p.v, meta, ops.DENSE_SLIDING, cfg["window"])
-    ready = getattr(p, "ready", None)  # e2e run: the copies of x and g may still be in flight
-    if ready:
-        torch.cuda.current_stream().wait_event(ready["x"])
-    z = torch.nn.functional.linear(p.x, p.wg)
-    out = F.gate_merge(z, [o_c.view(N, -1), o_s.view(N, -1), o_w.view(N, -1)], per_head=cfg["gate"] == "per_head",
-                       head_dim=D)
+
+    def gate_logits():
+        ready = getattr(p, "ready", None)  # e2e run: the copy of x may still be in flight
+        if ready:
+            torch.cuda.current_stream().wait_event(ready["x"])
+        return torch.nn.functional.linear(p.x, p.wg)
+
+    out = F.three_branch_attention(p.q, p.k, p.v, p.cu_blk, cfg["topk"], cfg["window"], gate_logits,
+                                   compress=p.compress, per_head=cfg["gate"] == "per_head", capture=capture)
+    ready = getattr(p, "ready", None)
     if ready:
         torch.cuda.current_stream().wait_event(ready["g"])
     loss = (out.float() * p.g.float()).sum() if want_loss else None
@@ -197,7 +230,7 @@ def forward_backward_sp(p: ShardedProblem, want_loss=False, capture=None):
 
 
 def zero_grads(p: Problem):
-    for t in (p.q, p.k, p.v, p.x, p.wg):
+    for t in [p.q, p.k, p.v, p.x] + (p.params() if hasattr(p, "params") else [p.wg]):
         t.grad = None
 
 
@@ -372,13 +405,16 @@ def run_ours(args, cfg):
             os.environ["NCCL_DEBUG"] = "WARN"
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
-    from lsrm_sparse import _lib, ops
+    from lsrm_sparse import _lib, ops, ulysses
 
     lib_launches = _lib.launch_count
     if ws > 1:
         # Ulysses sequence parallelism: every rank builds the same whole
         # problem on the host and keeps its token shard on the device
         from lsrm_sparse import ulysses
+
+        if cfg.get("compression", "mean") != "mean":
+            raise SystemExit("the sequence-parallel bench runs the block-mean compression only")
 
         full = Problem(cfg, args.seed, "cpu", pin=True)
         plan = ulysses.ShardPlan(full.h_cu_blk.tolist(), ws, rank)
@@ -394,12 +430,19 @@ def run_ours(args, cfg):
     if err:
         raise RuntimeError(f"device error bits 0x{err:x} in the first step")
     pairs = count_pairs(p, cap["block_topk"])
+    # this rank's own work (all heads on one GPU; H / N heads of the whole sequence under Ulysses)
+    rank_pairs = dict(pairs)
     if ws > 1:
+        rank_pairs["compressed"] = pairs["compressed"] // ws
+        rank_pairs["sliding"] = pairs["sliding"] // ws
         # each rank selected for its own heads: the whole job's pairs are the sum
         t = torch.tensor([float(pairs["select"])], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t)
         pairs["select"] = int(t.item())
-    flops_step = 14.0 * p.D * (pairs["select"] + pairs["compressed"] + pairs["sliding"])
+    flops_attn = 14.0 * p.D * (pairs["select"] + pairs["compressed"] + pairs["sliding"])
+    # ResBlock compression (cfg3): two C x C Linears per K and V, forward 2 FLOPs per MAC, backward twice that
+    flops_comp = 24.0 * p.N * p.hidden ** 2 if getattr(p, "res_w", None) is not None else 0.0
+    flops_step = flops_attn + flops_comp
     for _ in range(max(args.warmup - 1, 0)):
         step(p)
         zero_grads(p)
@@ -436,27 +479,47 @@ def run_ours(args, cfg):
 
     # ---- profiled pass: per-kernel device time (events on the launching stream) ----
     _lib.profile_enable(True)
+    xtimer = ulysses.time_exchanges(True) if ws > 1 else None
     for _ in range(args.steps):
         step(p)
         zero_grads(p)
     torch.cuda.synchronize()
     prof = _lib.profile_collect()
     _lib.profile_enable(False)
+    exchange = None
+    if xtimer is not None:
+        xs = xtimer.stats()
+        ulysses.time_exchanges(False)
+        # the busiest rank's exchange time; bytes are this rank's per direction
+        t = torch.tensor([xs["ms"]], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        a2a_ms = float(t.item()) / args.steps
+        out_b = xs["bytes_out"] / args.steps
+        exchange = {"a2a_ms_per_step": a2a_ms, "calls_per_step": xs["calls"] / args.steps,
+                    "bytes_out_per_step": out_b, "bytes_in_per_step": xs["bytes_in"] / args.steps,
+                    "a2a_gbs": out_b / (a2a_ms * 1e-3) / 1e9 if a2a_ms > 0 else None,
+                    "link_gbs": 900.0, "link_note": "NVLink 5 nominal per direction per GPU (measured peer copy "
+                                                    "on this pool: 770)",
+                    "share_of_step": a2a_ms / ms_max,
+                    "how": "CUDA events on the compute stream around every all_to_all_single of the step (forward "
+                           "and backward: q, k, v, gate logits, output); bytes = what leaves this rank"}
     peaks, peak_kind = load_peaks()
     total_prof = sum(v[0] for v in prof.values())
     kernels = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
                    "share": v[0] / total_prof if total_prof else None} for k, v in sorted(prof.items())}
-    attn = {k: v for k, v in prof.items() if kernel_flops(k, pairs, p.H, p.D, p.N, p.nb)[0] is not None}
+    attn = {k: v for k, v in prof.items() if kernel_flops(k, rank_pairs, p.H, p.D, p.N, p.nb)[0] is not None}
     dom = max(attn.items(), key=lambda kv: kv[1][0])[0] if attn else None
     roofline = None
     if dom is not None:
-        fl, bound = kernel_flops(dom, pairs, p.H, p.D, p.N, p.nb)
+        # one GPU's kernel: this rank's own pairs over this rank's launch time, against one GPU's peak
+        fl, bound = kernel_flops(dom, rank_pairs, p.H, p.D, p.N, p.nb)
         avg_ms = prof[dom][0] / prof[dom][1]
         achieved = fl / (avg_ms * 1e-3) / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak, "traffic": traffic_for(dom),
-                    "peak_source": f"bf16_tflops_sustained of {peak_kind} (kernel timed inside a long step)"}
+                    "peak_source": f"bf16_tflops_sustained of {peak_kind} (kernel timed inside a long step)",
+                    "scope": "one GPU (rank 0): its own pairs and launch time" if ws > 1 else "one GPU"}
     slowest = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
 
     # ---- end to end through the public API: H2D inputs, D2H loss ----
@@ -569,12 +632,15 @@ def run_ours(args, cfg):
         "config": workload_config(cfg, p, ws),
         "tokens_per_s": p.N / (ms_max * 1e-3),
         "flops_per_step": flops_step,
+        "attention_tflops": flops_attn / (ms_max * 1e-3) / 1e12,
+        "compression_flops_per_step": flops_comp,
         "pairs_per_step": pairs,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
+        "exchange": exchange,
         "kernels": kernels,
         "slowest_kernel": slowest,
     }

@@ -119,3 +119,54 @@ def resnorm_mean(x, h, cu_block_include_tokens, eps=1e-5):
 
 def gate_merge(z, branches: Sequence[torch.Tensor], per_head=False, head_dim=0):
     return GateMergeFn.apply(z, per_head, head_dim, *branches)
+
+
+def three_branch_attention(q, k, v, cu_blk, topk: int, window: int, gate_logits, *, compress=None,
+                           per_head: bool = True, softmax_scale=None, capture=None):
+    """The full native-sparse-attention op on one whole sequence, as
+    SpatialSparseAttentionIn / Mid / Out run it (spatial_sparse_attention.py:
+    16-270) with the BASELINE extensions on: compression of K/V per block,
+    compressed attention (natural-log LSE), per-query-block top-k selection
+    with the query block's own block forced (block_score.py:16-98 summed over
+    the query block's tokens), selected-block attention, sliding-window
+    attention (|i - j| <= window // 2) and the sigmoid-gated merge.
+
+    q [N, H, D], k/v [N, Hkv, D] (one sequence, blocks given by ``cu_blk``,
+    which are also the query blocks); ``gate_logits`` is a tensor [N, 3*H]
+    (per head) or [N, 3*H*D] (per channel), or a callable returning it (it is
+    called after the attention branches are enqueued, so a caller can wait for
+    the gate input there).  ``compress(k2d, v2d, cu_blk) -> (ck, cv)`` replaces
+    the block mean (e.g. the ResBlock compression); it returns [nb, Hkv*D].
+    Returns the merged output [N, H*D].  Metadata is built on the device, so
+    the call never synchronises the host.  ``capture`` (a dict) receives the
+    selection, the compressed keys / values, the compressed LSE, the merged
+    output and, after the backward, the gradients of the compressed keys /
+    values (``dck``, ``dcv``)."""
+    N, H, D = q.shape
+    Hkv = k.shape[1]
+    nb = cu_blk.numel() - 1
+    dev = q.device
+    two = torch.arange(2, dtype=torch.int32, device=dev)
+    cu_seq = two * N
+    meta = ops.Meta(cu_seq, cu_seq, two * nb, cu_blk)
+    meta_c = ops.Meta(cu_seq, cu_seq, two * nb, torch.arange(nb + 1, dtype=torch.int32, device=dev))
+    k2, v2 = k.reshape(N, Hkv * D), v.reshape(N, Hkv * D)
+    if compress is None:
+        ck, cv = block_mean(k2, cu_blk), block_mean(v2, cu_blk)
+    else:
+        ck, cv = compress(k2, v2, cu_blk)
+    ck, cv = ck.view(nb, Hkv, D), cv.view(nb, Hkv, D)
+    if capture is not None and ck.requires_grad:  # the gradients reaching the compression
+        ck.register_hook(lambda g: capture.__setitem__("dck", g))
+        cv.register_hook(lambda g: capture.__setitem__("dcv", g))
+    o_c, lse = dense_attention(q, ck, cv, meta_c, ops.DENSE_COMPRESSED, 0, softmax_scale)
+    with torch.no_grad():
+        bt = ops.block_topk(q, ck, lse, topk, meta_c, cu_query_blocks=cu_blk, force_self=True,
+                            sm_scale=softmax_scale)
+    o_s, _ = select_attention(q, k, v, bt, meta, softmax_scale, cu_blk)
+    o_w, _ = dense_attention(q, k, v, meta, ops.DENSE_SLIDING, window, softmax_scale)
+    z = gate_logits() if callable(gate_logits) else gate_logits
+    out = gate_merge(z, [o_c.view(N, -1), o_s.view(N, -1), o_w.view(N, -1)], per_head=per_head, head_dim=D)
+    if capture is not None:
+        capture.update(block_topk=bt, ck=ck.detach(), cv=cv.detach(), lse=lse, out=out.detach())
+    return out

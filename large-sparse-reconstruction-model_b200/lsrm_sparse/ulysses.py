@@ -27,7 +27,7 @@ import torch.distributed as dist
 from . import ops
 
 __all__ = ["shard_blocks", "ShardPlan", "seq_to_head", "head_to_seq", "exchange_gate_logits",
-           "three_branch_attention"]
+           "three_branch_attention", "time_exchanges", "ExchangeTimer"]
 
 
 def shard_blocks(cu_block_include_tokens: Sequence[int], world: int) -> List[Tuple[int, int]]:
@@ -86,6 +86,49 @@ class ShardPlan:
         return h, h + 1
 
 
+class ExchangeTimer:
+    """Device timing of the exchanges, off unless enabled: CUDA events on the
+    current stream around every ``all_to_all_single`` of this module (the
+    collective waits for the stream's earlier work and the stream waits for
+    it), and the bytes each one sends to and receives from other ranks (a
+    rank's own slice is a local copy and is not counted)."""
+
+    def __init__(self):
+        self.records = []
+
+    def stats(self) -> dict:
+        """Totals since the timer was enabled: ``ms``, ``calls``,
+        ``bytes_out`` / ``bytes_in`` (crossing the links).  Synchronises."""
+        if not self.records:
+            return {"ms": 0.0, "calls": 0, "bytes_out": 0, "bytes_in": 0}
+        torch.cuda.synchronize()
+        return {"ms": sum(a.elapsed_time(b) for a, b, _, _ in self.records), "calls": len(self.records),
+                "bytes_out": sum(r[2] for r in self.records), "bytes_in": sum(r[3] for r in self.records)}
+
+
+_timer: Optional[ExchangeTimer] = None
+
+
+def time_exchanges(on: bool = True) -> Optional[ExchangeTimer]:
+    """Start (a fresh timer) or stop timing the exchanges; returns the timer."""
+    global _timer
+    _timer = ExchangeTimer() if on else None
+    return _timer
+
+
+def _a2a(recv: torch.Tensor, send: torch.Tensor, out_splits, in_splits, group, rank: int):
+    t = _timer
+    if t is None or not recv.is_cuda:
+        dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+        return
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+    e1.record()
+    el = recv.element_size()
+    t.records.append((e0, e1, (sum(in_splits) - in_splits[rank]) * el, (sum(out_splits) - out_splits[rank]) * el))
+
+
 def _check_heads(H: int, W: int):
     if H % W and W % H:
         raise ValueError(f"heads ({H}) and world size ({W}) must divide one another")
@@ -101,8 +144,7 @@ class _SeqToHead(torch.autograd.Function):
         send = pack(x, W)  # [W, n, hp, D]
         recv = torch.empty(plan.total, hp, D, dtype=x.dtype, device=x.device)
         row = hp * D
-        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W,
-                               group=group)
+        _a2a(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W, group, plan.rank)
         ctx.plan, ctx.group, ctx.unpack, ctx.H = plan, group, unpack, H
         return recv
 
@@ -113,8 +155,8 @@ class _SeqToHead(torch.autograd.Function):
         n = plan.counts[plan.rank]
         back = torch.empty(plan.world, n, hp, D, dtype=g.dtype, device=g.device)
         row = hp * D
-        dist.all_to_all_single(back.view(-1), g.contiguous().view(-1), [n * row] * plan.world,
-                               [c * row for c in plan.counts], group=ctx.group)
+        _a2a(back.view(-1), g.contiguous().view(-1), [n * row] * plan.world, [c * row for c in plan.counts],
+             ctx.group, plan.rank)
         return ctx.unpack(back, ctx.H), None, None, None, None
 
 
@@ -127,8 +169,8 @@ class _HeadToSeq(torch.autograd.Function):
         n = plan.counts[plan.rank]
         back = torch.empty(plan.world, n, hp, D, dtype=y.dtype, device=y.device)
         row = hp * D
-        dist.all_to_all_single(back.view(-1), y.contiguous().view(-1), [n * row] * plan.world,
-                               [c * row for c in plan.counts], group=group)
+        _a2a(back.view(-1), y.contiguous().view(-1), [n * row] * plan.world, [c * row for c in plan.counts], group,
+             plan.rank)
         ctx.plan, ctx.group, ctx.pack = plan, group, pack
         return unpack(back, num_heads)
 
@@ -140,8 +182,8 @@ class _HeadToSeq(torch.autograd.Function):
         send = ctx.pack(g, plan.world)
         recv = torch.empty(plan.total, hp, D, dtype=g.dtype, device=g.device)
         row = hp * D
-        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * plan.world,
-                               group=ctx.group)
+        _a2a(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * plan.world, ctx.group,
+             plan.rank)
         return recv, None, None, None, None, None
 
 
@@ -206,8 +248,7 @@ class _GateExchange(torch.autograd.Function):
         hp = H // W
         recv = torch.empty(plan.total, n_branch, hp, dtype=z.dtype, device=z.device)
         row = n_branch * hp
-        dist.all_to_all_single(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W,
-                               group=group)
+        _a2a(recv.view(-1), send.view(-1), [c * row for c in plan.counts], [n * row] * W, group, plan.rank)
         ctx.plan, ctx.group, ctx.B, ctx.H = plan, group, n_branch, H
         return recv.view(plan.total, n_branch * hp)
 
@@ -219,8 +260,8 @@ class _GateExchange(torch.autograd.Function):
         n = plan.counts[plan.rank]
         back = torch.empty(W, n, B, hp, dtype=g.dtype, device=g.device)
         row = B * hp
-        dist.all_to_all_single(back.view(-1), g.contiguous().view(-1), [n * row] * W, [c * row for c in plan.counts],
-                               group=ctx.group)
+        _a2a(back.view(-1), g.contiguous().view(-1), [n * row] * W, [c * row for c in plan.counts], ctx.group,
+             plan.rank)
         return _unpack_small(back, B, H).reshape(n, B * H), None, None, None
 
 
@@ -266,23 +307,6 @@ def whole_sequence_branches(q, k, v, z, cu_blk, topk: int, window: int, softmax_
     from . import functional as F
 
     N, H, D = q.shape
-    Hkv = k.shape[1]
-    nb = cu_blk.numel() - 1
-    dev = q.device
-    two = torch.arange(2, dtype=torch.int32, device=dev)  # built on the device: no host synchronisation
-    cu_seq = two * N
-    cu_sb = two * nb
-    meta = ops.Meta(cu_seq, cu_seq, cu_sb, cu_blk)
-    meta_c = ops.Meta(cu_seq, cu_seq, cu_sb, torch.arange(nb + 1, dtype=torch.int32, device=dev))
-    ck = F.block_mean(k.reshape(N, Hkv * D), cu_blk).view(nb, Hkv, D)
-    cv = F.block_mean(v.reshape(N, Hkv * D), cu_blk).view(nb, Hkv, D)
-    o_c, lse = F.dense_attention(q, ck, cv, meta_c, ops.DENSE_COMPRESSED, 0, softmax_scale)
-    with torch.no_grad():
-        bt = ops.block_topk(q, ck, lse, topk, meta_c, cu_query_blocks=cu_blk, force_self=True,
-                            sm_scale=softmax_scale)
-    if capture is not None:
-        capture["block_topk"] = bt
-    o_s, _ = F.select_attention(q, k, v, bt, meta, softmax_scale, cu_blk)
-    o_w, _ = F.dense_attention(q, k, v, meta, ops.DENSE_SLIDING, window, softmax_scale)
-    out = F.gate_merge(z, [o_c.reshape(N, -1), o_s.reshape(N, -1), o_w.reshape(N, -1)], per_head=True, head_dim=D)
+    out = F.three_branch_attention(q, k, v, cu_blk, topk, window, z, per_head=True, softmax_scale=softmax_scale,
+                                   capture=capture)
     return out.view(N, H, D)

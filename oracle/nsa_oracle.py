@@ -53,6 +53,11 @@ __all__ = [
     "selection_flops",
     "dense_attention_flops",
     "three_branch_sample_step",
+    "qblock_selection_exact",
+    "three_branch_masked_dense",
+    "three_branch_sampled",
+    "compress_vjp",
+    "compress_forward",
     "volume_sort_keys",
     "block_separation",
     "prepare_volume_output",
@@ -668,6 +673,238 @@ def three_branch_sample_step(q, k, v, x, gate_w, g, cu_blk, qblock_ids, topk, wi
         loss = loss + (out.reshape(L, -1) * g[r0:r1].float()).sum()
     loss.backward()
     return float(loss.detach()), 14.0 * D * H * pairs
+
+
+# ---------------------------------------------------------------------------
+# The whole three-branch step with its gradients (parity of the timed path)
+# ---------------------------------------------------------------------------
+
+
+def qblock_selection_exact(q_rows, ck, lse_rows, topk: int, force_block: Optional[int] = None, sm_scale=None):
+    """Selection of ONE query block in the fixed float32 order of
+    ``get_block_score_qblock_exact``: the per-token scores of
+    ``token_block_scores_exact`` (block_score.py:57-92) summed over the block's
+    tokens in ascending order, top-k with ties to the lower id, ``force_block``
+    always chosen, ids ascending (block_score.py:85-96).  q_rows [L, Hq, D],
+    ck [nb, Hkv, D], lse_rows [Hq, L] (natural log).  Returns [Hkv, topk]."""
+    L = q_rows.shape[0]
+    nb = ck.shape[0]
+    cq = torch.tensor([0, L], dtype=torch.int32)
+    cc = torch.tensor([0, nb], dtype=torch.int32)
+    sc = token_block_scores_exact(q_rows, ck, lse_rows, cq, cc, sm_scale)[0]  # [Hkv, L, nb]
+    out = np.full((sc.shape[0], topk), -1, dtype=np.int32)
+    force = None if force_block is None else np.array([force_block])
+    for h in range(sc.shape[0]):
+        acc = np.zeros(nb, dtype=_F32)
+        for t in range(L):
+            acc = (acc + sc[h, t]).astype(_F32)
+        out[h] = _topk_lowest_id(acc[None], topk, force)[0]
+    return torch.from_numpy(out)
+
+
+def _gate_slices(z, i, h, H, D, per_head):
+    """Gate of branch ``i`` for head ``h``: per head one column ``i*H + h``
+    broadcast over D; per channel the D columns of the head
+    (spatial_sparse_attention.py:257-269)."""
+    if per_head:
+        return z[:, i * H + h : i * H + h + 1]
+    C = H * D
+    return z[:, i * C + h * D : i * C + (h + 1) * D]
+
+
+def _res_block_tokens(x, w):
+    """SparseResBlock on tokens (residual_block.py:16-34) in x's dtype."""
+    w1, b1, w2, b2 = (t.to(x.dtype) for t in w)
+    h = torch.nn.functional.linear(torch.nn.functional.silu(torch.nn.functional.linear(x, w1, b1)), w2, b2)
+    y = x + h
+    return torch.nn.functional.layer_norm(y, (y.shape[-1],), eps=1e-5)
+
+
+def three_branch_masked_dense(q, k, v, x, gate_w, g, cu_blk, block_topk, window: int, per_head: bool = True,
+                              compress=None, softmax_scale=None, dtype=torch.float64):
+    """The three-branch op on one sequence as masked DENSE attention, forward
+    and backward, with autograd in ``dtype`` (the BASELINE config-1 check).
+
+    * compression: ``compress=None`` block mean of K/V
+      (spatial_sparse_attention.py:27-37); else ``{"k": (w1, b1, w2, b2),
+      "v": (...)}`` runs the token-wise ResBlock first (:46-66,
+      residual_block.py:16-34);
+    * compressed branch: softmax over every block of the sequence
+      (spatial_sparse_attention.py:121-143), natural-log LSE kept;
+    * selected branch: query i attends key j when block(j) is in
+      ``block_topk[h_kv, block(i)]`` (per-query-block selection [Hkv, nb, k],
+      ids of the one sequence; kvcentric.py:127-247);
+    * sliding window: ``|i - j| <= window // 2``;
+    * gates: ``sigmoid(x · gate_wᵀ)``, branches in the order compressed,
+      selected, window (:257-269), per head or per channel.
+
+    Loss = Σ out ⊙ g.  Returns a dict with ``out`` [N, H*D], ``lse_c`` [H, N],
+    ``ck``/``cv`` [nb, Hkv, D] and the gradients ``q, k, v, x, gate_w``,
+    ``dck``/``dcv`` (and ``compress_k`` / ``compress_v`` weight-gradient
+    tuples).  Each head's dense
+    [N, N] work is checkpointed, so memory stays at one head's matrices."""
+    from torch.utils.checkpoint import checkpoint
+
+    N, H, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    cb = _i(cu_blk)
+    nb = len(cb) - 1
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    lens = torch.tensor(np.diff(np.array(cb)), dtype=dtype)
+    blk_of = torch.repeat_interleave(torch.arange(nb), lens.long())
+    leaf = lambda t: t.detach().to(dtype).requires_grad_()  # noqa: E731
+    qd, kd, vd, xd, wd = leaf(q), leaf(k), leaf(v), leaf(x), leaf(gate_w)
+    cw = None
+    if compress is not None:
+        cw = {s: tuple(leaf(t) for t in compress[s]) for s in ("k", "v")}
+        kc = _res_block_tokens(kd.reshape(N, -1), cw["k"]).view(N, Hkv, D)
+        vc = _res_block_tokens(vd.reshape(N, -1), cw["v"]).view(N, Hkv, D)
+    else:
+        kc, vc = kd, vd
+    ck = torch.zeros(nb, Hkv, D, dtype=dtype).index_add(0, blk_of, kc) / lens[:, None, None]
+    cv = torch.zeros(nb, Hkv, D, dtype=dtype).index_add(0, blk_of, vc) / lens[:, None, None]
+    ck.retain_grad()
+    cv.retain_grad()
+    z = torch.sigmoid(xd @ wd.t())
+    bt = torch.as_tensor(block_topk).long()
+    idx = torch.arange(N)
+    band = (idx[:, None] - idx[None, :]).abs() <= window // 2
+    allowed = []
+    for hk in range(Hkv):
+        a = torch.zeros(nb, nb, dtype=torch.bool)
+        sel = bt[hk]
+        valid = (sel >= 0) & (sel < nb)
+        rows = torch.arange(nb)[:, None].expand_as(sel)
+        a[rows[valid], sel[valid]] = True
+        allowed.append(a)
+
+    def head(h, qh, kh, vh, ckh, cvh, zz):
+        sc = (qh @ ckh.t()) * scale
+        lse = torch.logsumexp(sc, -1)
+        o_c = torch.softmax(sc, -1) @ cvh
+        s = (qh @ kh.t()) * scale
+        m_sel = allowed[h // G][blk_of][:, blk_of]
+        o_s = torch.softmax(s.masked_fill(~m_sel, -math.inf), -1) @ vh
+        o_w = torch.softmax(s.masked_fill(~band, -math.inf), -1) @ vh
+        out = sum(_gate_slices(zz, i, h, H, D, per_head) * o for i, o in enumerate((o_c, o_s, o_w)))
+        return out, lse
+
+    outs, lses = [], []
+    for h in range(H):
+        hk = h // G
+        o, l = checkpoint(head, h, qd[:, h], kd[:, hk], vd[:, hk], ck[:, hk], cv[:, hk], z, use_reentrant=False)
+        outs.append(o)
+        lses.append(l)
+    out = torch.stack(outs, 1).reshape(N, H * D)
+    loss = (out * torch.as_tensor(g).to(dtype)).sum()
+    loss.backward()
+    res = dict(out=out.detach(), lse_c=torch.stack(lses).detach(), ck=ck.detach(), cv=cv.detach(), q=qd.grad,
+               k=kd.grad, v=vd.grad, x=xd.grad, gate_w=wd.grad, dck=ck.grad, dcv=cv.grad)
+    if cw is not None:
+        res["compress_k"] = tuple(t.grad for t in cw["k"])
+        res["compress_v"] = tuple(t.grad for t in cw["v"])
+    return res
+
+
+def three_branch_sampled(q, k, v, x, gate_w, g, cu_blk, block_topk, qblock_ids, window: int, ck, cv,
+                         per_head: bool = True, softmax_scale=None, dtype=torch.float32):
+    """Forward and backward of the three-branch op for the query blocks
+    ``qblock_ids`` only (loss = Σ over their rows of out ⊙ g), keys gathered
+    per query block and head, autograd in ``dtype``.  Same branches and gate
+    rule as :func:`three_branch_masked_dense`; the compressed keys/values
+    ``ck``/``cv`` [nb, Hkv, D] are inputs (their gradients are returned, so a
+    caller maps them back through its compression), ``block_topk`` [Hkv, nb,
+    k] the per-query-block selection.
+
+    Returns a dict: ``rows`` (token ids of the sampled blocks, block order),
+    ``out`` [R, H*D], ``q`` [R, H, D] and ``x`` [R, hidden] (gradients of those
+    rows; every other row's gradient is zero), ``gate_w``, ``ck``/``cv``
+    (gradients [nb, Hkv, D]), ``k_direct``/``v_direct`` [N, Hkv, D] (the
+    gradients through the selected and window branches, without the
+    compression path), ``lse_c`` [H, R]."""
+    N, H, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    cb = _i(cu_blk)
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    half = window // 2
+    bt = torch.as_tensor(block_topk).long()
+    ckl = ck.detach().to(dtype).requires_grad_()
+    cvl = cv.detach().to(dtype).requires_grad_()
+    wl = gate_w.detach().to(dtype).requires_grad_()
+    gt = torch.as_tensor(g)
+    kd_direct = torch.zeros(N, Hkv, D, dtype=dtype)
+    vd_direct = torch.zeros(N, Hkv, D, dtype=dtype)
+    rows, outs, dqs, dxs, lses = [], [], [], [], []
+    for qb in qblock_ids:
+        r0, r1 = cb[qb], cb[qb + 1]
+        L = r1 - r0
+        qq = q[r0:r1].detach().to(dtype).requires_grad_()
+        xx = x[r0:r1].detach().to(dtype).requires_grad_()
+        z = torch.sigmoid(xx @ wl.t())
+        k0, k1 = max(0, r0 - half), min(N, r1 + half)
+        ii = torch.arange(r0, r1)[:, None]
+        jj = torch.arange(k0, k1)[None, :]
+        band = (ii - jj).abs() <= half
+        leaves = []
+        out = torch.zeros(L, H * D, dtype=dtype)
+        lse_b = []
+        for hk in range(Hkv):
+            sel = [int(b) for b in bt[hk, qb] if 0 <= int(b) < len(cb) - 1]
+            keys = torch.cat([torch.arange(cb[b], cb[b + 1]) for b in sel]) if sel else torch.zeros(0, dtype=torch.long)
+            ks = k[keys, hk].detach().to(dtype).requires_grad_()
+            vs = v[keys, hk].detach().to(dtype).requires_grad_()
+            kw = k[k0:k1, hk].detach().to(dtype).requires_grad_()
+            vw = v[k0:k1, hk].detach().to(dtype).requires_grad_()
+            leaves.append((keys, ks, vs, kw, vw, hk))
+            for h in range(hk * G, (hk + 1) * G):
+                qh = qq[:, h]
+                sc = (qh @ ckl[:, hk].t()) * scale
+                lse_b.append(torch.logsumexp(sc, -1))
+                o_c = torch.softmax(sc, -1) @ cvl[:, hk]
+                o_s = torch.softmax((qh @ ks.t()) * scale, -1) @ vs
+                sw = ((qh @ kw.t()) * scale).masked_fill(~band, -math.inf)
+                o_w = torch.softmax(sw, -1) @ vw
+                o_h = sum(_gate_slices(z, i, h, H, D, per_head) * o for i, o in enumerate((o_c, o_s, o_w)))
+                out = out.index_copy(1, torch.arange(h * D, (h + 1) * D), o_h)
+        loss = (out * gt[r0:r1].to(dtype)).sum()
+        loss.backward()
+        for keys, ks, vs, kw, vw, hk in leaves:
+            kd_direct[:, hk].index_add_(0, keys, ks.grad)
+            vd_direct[:, hk].index_add_(0, keys, vs.grad)
+            kd_direct[k0:k1, hk] += kw.grad
+            vd_direct[k0:k1, hk] += vw.grad
+        rows.append(torch.arange(r0, r1))
+        outs.append(out.detach())
+        dqs.append(qq.grad)
+        dxs.append(xx.grad)
+        lses.append(torch.stack(lse_b).detach())
+    return dict(rows=torch.cat(rows), out=torch.cat(outs), q=torch.cat(dqs), x=torch.cat(dxs), gate_w=wl.grad,
+                ck=ckl.grad, cv=cvl.grad, k_direct=kd_direct, v_direct=vd_direct, lse_c=torch.cat(lses, 1))
+
+
+def compress_vjp(x_rows, dy_rows, weights=None, dtype=torch.float32):
+    """Gradient of the token-wise compression input for some token rows:
+    identity for the block mean (``weights=None``); the ResBlock's vector-
+    Jacobian product (residual_block.py:16-34) otherwise.  ``dy_rows`` is the
+    gradient of the compressed per-token values (for the block mean of block b
+    that is dck[b] / L_b on each of b's tokens).  Returns (dx_rows, weight
+    gradients or None)."""
+    if weights is None:
+        return dy_rows.to(dtype), None
+    xl = x_rows.detach().to(dtype).requires_grad_()
+    wl = tuple(t.detach().to(dtype).requires_grad_() for t in weights)
+    y = _res_block_tokens(xl, wl)
+    y.backward(dy_rows.to(dtype))
+    return xl.grad, tuple(t.grad for t in wl)
+
+
+def compress_forward(x_rows, weights=None, dtype=torch.float32):
+    """Token-wise compression values (before the block mean): x itself, or
+    the ResBlock output."""
+    xr = x_rows.detach().to(dtype)
+    return xr if weights is None else _res_block_tokens(xr, tuple(t.to(dtype) for t in weights))
 
 
 # ---------------------------------------------------------------------------
