@@ -323,11 +323,21 @@ def cpu_sample(p: Problem, n_qblocks: int, seed: int):
     t0 = time.perf_counter()
     _, flops = oracle.three_branch_sample_step(p.h_q, p.h_k, p.h_v, p.h_x, p.gate_w, p.h_g, p.h_cu_blk, qbs,
                                                p.cfg["topk"], p.cfg["window"], per_head=p.cfg["gate"] == "per_head")
-    dt = time.perf_counter() - t0
     tokens = int(sum(p.lens[i] for i in qbs))
+    what = "three-branch fwd+bwd incl. exact scoring"
+    if getattr(p, "res_w", None) is not None:
+        # the ResBlock compression (token-wise) on as many tokens as the sample has queries, fwd + bwd
+        cb = p.h_cu_blk.long()
+        rows = torch.cat([torch.arange(int(cb[i]), int(cb[i + 1])) for i in qbs])
+        for s in ("k", "v"):
+            x = getattr(p, "h_" + s)[rows].reshape(rows.numel(), -1)
+            oracle.compress_vjp(x, torch.ones(x.shape), p.res_w[s])
+        flops += 24.0 * rows.numel() * p.hidden ** 2
+        what += " and the ResBlock K/V compression of as many tokens"
+    dt = time.perf_counter() - t0
     return dict(value=flops / dt / 1e12, unit="TFLOP/s", cores=torch.get_num_threads(), kind="port",
-                sample=f"{len(qbs)} of {p.nb} query blocks ({tokens} of {p.N} queries), three-branch fwd+bwd "
-                       f"incl. exact scoring, fp32 torch on {torch.get_num_threads()} host threads",
+                sample=f"{len(qbs)} of {p.nb} query blocks ({tokens} of {p.N} queries), {what}, fp32 torch on "
+                       f"{torch.get_num_threads()} host threads",
                 seconds=dt)
 
 

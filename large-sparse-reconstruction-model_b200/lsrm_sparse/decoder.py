@@ -90,10 +90,11 @@ class CrossAttention(nn.Module):
                 dim, num_q_heads, num_kv_heads, True)
             self.y_2_x_attn_in, self.y_2_x_attn_mid, self.y_2_x_attn_out = _attn_triple(
                 dim, num_q_heads, num_kv_heads, False)
-        if use_weight_norm:
+        if use_weight_norm:  # the same projections as models_sparse/utils.py:228-236
             wn = nn.utils.parametrizations.weight_norm
             self.q_proj_x, self.k_proj_x, self.v_proj_x = wn(self.q_proj_x), wn(self.k_proj_x), wn(self.v_proj_x)
             self.proj_x = wn(self.proj_x)
+            self.k_proj_y, self.v_proj_y = wn(self.k_proj_y), wn(self.v_proj_y)
             if not oneside:
                 self.q_proj_y, self.proj_y = wn(self.q_proj_y), wn(self.proj_y)
 

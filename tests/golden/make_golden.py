@@ -20,6 +20,9 @@ What runs, all unmodified reference code:
   ``build_volume_to_image_attn`` and ``from_imcoords_to_points``
   (misc/sparse_utils.py:653-1200) on posed views of a sphere scene from
   ``lsrm_sparse.synth.view_scene`` (``--only image``).
+* the state-dict layout of ``BlockMix`` / ``BlockMixOneside``
+  (models_sparse/utils.py:575-705) with and without weight norm
+  (``--only modules``, ``module_keys.json``).
 * ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
   without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
   for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
@@ -360,10 +363,31 @@ def make_image_sort(sparse_utils, seed):
                 block_size=np.int32(4), patch_size=np.int32(8), image_res=np.int32(128))
 
 
+MODULE_CASES = [  # (name, BlockMix kwargs): small dims, the reference's layer layout
+    ("blockmix", dict(dim=64, num_q_heads=4, num_kv_heads=2)),
+    ("blockmix_weight_norm", dict(dim=64, num_q_heads=4, num_kv_heads=2, use_weight_norm=True, qkv_bias=True)),
+    ("blockmix_oneside_weight_norm", dict(dim=64, num_q_heads=4, num_kv_heads=4, use_weight_norm=True,
+                                          oneside=True)),
+]
+
+
+def make_module_keys(utils):
+    """State-dict layout (parameter name -> shape) of the reference's
+    ``BlockMix`` / ``BlockMixOneside`` (models_sparse/utils.py:575-705), which
+    holds ``CrossAttention`` (:80-240, weight norm at :228-236) and ``Mlp``."""
+    out = {}
+    for name, kw in MODULE_CASES:
+        kw = dict(kw)
+        cls = utils.BlockMixOneside if kw.pop("oneside", False) else utils.BlockMix
+        m = cls(**kw)
+        out[name] = {k: list(v.shape) for k, v in m.state_dict().items()}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image", "imsort"], default=None,
+    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image", "imsort", "modules"], default=None,
                     help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
@@ -371,6 +395,15 @@ def main():
     sys.path.insert(0, args.ref)
     from misc import sparse_utils
 
+    if args.only == "modules":
+        import json
+
+        from models_sparse import utils
+
+        with open(os.path.join(HERE, "module_keys.json"), "w") as f:
+            json.dump(make_module_keys(utils), f, indent=1, sort_keys=True)
+        print("wrote module_keys.json")
+        return
     if args.only == "imsort":
         np.savez_compressed(os.path.join(HERE, "image_sort.npz"), **make_image_sort(sparse_utils, 81))
         print("wrote image_sort")
