@@ -1284,7 +1284,7 @@ def decoder_problem(seed, n_vol, dev):
 
 def run_decoder(args):
     ws, rank, local = dist_env()
-    if rank != 0:
+    if args.impl == "reference" and rank != 0:
         return
     c = DEC_CFG
     n_req = args.decoder_tokens or c["n_vol"]
@@ -1294,32 +1294,53 @@ def run_decoder(args):
                               "and flash-attn on the GPU; its CPU path (Triton interpreter, fp16 only) takes ~24 s "
                               "for one 256-token attention call, so a decoder step is out of reach")), flush=True)
         return
-    from lsrm_sparse import _lib, ops
+    from lsrm_sparse import _lib, ops, ulysses
     from lsrm_sparse.decoder import BlockMix
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if ws > 1:
+        import datetime
+
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    # every rank builds the whole problem (maps over all tokens, as each rank needs them for its heads)
     maps, nx, ny, shell, map_ms = decoder_problem(args.seed, n_req, dev)
-    torch.manual_seed(args.seed)
+    torch.manual_seed(args.seed)  # the same weights on every rank
     n_layers = args.decoder_layers or c["layers"]
     layers = torch.nn.ModuleList(
         BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
-                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"]) for _ in range(n_layers)
+                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1)
+        for _ in range(n_layers)
     ).to(dev).to(torch.bfloat16)
     opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
-    cu_x = torch.tensor([0, nx], dtype=torch.int32, device=dev)
-    cu_y = torch.tensor([0, ny], dtype=torch.int32, device=dev)
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     x_in = torch.randn(nx, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
     y_in = torch.randn(ny, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
+    if ws > 1:
+        # sequence parallel: this rank's whole blocks of both token sets (the reference's distribute step)
+        (x_in,), (y_in,), cu_x, cu_y, maps = ulysses.seq_parallel_token_blocks([x_in], [y_in], maps, "distribute")
+        x_in, y_in = x_in.contiguous(), y_in.contiguous()
+        params = list(layers.parameters())
+    else:
+        cu_x = torch.tensor([0, nx], dtype=torch.int32, device=dev)
+        cu_y = torch.tensor([0, ny], dtype=torch.int32, device=dev)
     import torch.utils.checkpoint as cp
 
     def step(x, y):
         opt.zero_grad(set_to_none=True)
         for blk in layers:  # one checkpoint per block (the reference's cp_freq = 1)
             x, y, _ = cp.checkpoint(blk, x, cu_x, y, cu_y, maps, c["views"], use_reentrant=False)
-        loss = x.float().square().mean() + y.float().square().mean()
+        # the loss of the whole token set: every rank's share over the global counts
+        loss = x.float().square().sum() / nx + y.float().square().sum() / ny
         loss.backward()
+        if ws > 1:  # weights are replicated: sum the ranks' gradients in one flat exchange
+            grads = [p.grad for p in params]
+            flat = torch._utils._flatten_dense_tensors(grads)
+            torch.distributed.all_reduce(flat)
+            for g_, f_ in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+                g_.copy_(f_)
         opt.step()
         return loss.detach()
 
@@ -1331,6 +1352,8 @@ def run_decoder(args):
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = _lib.launch_count()
+    if ws > 1:
+        torch.distributed.barrier()
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         e0.record(stream)
@@ -1340,6 +1363,21 @@ def run_decoder(args):
         torch.cuda.synchronize()
     launches = _lib.launch_count() - n0
     ms = e0.elapsed_time(e1) / args.steps
+    exchange = None
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        xt = ulysses.time_exchanges(True)  # one more step with the exchanges timed
+        step(x_in, y_in)
+        xs = xt.stats()
+        ulysses.time_exchanges(False)
+        t = torch.tensor([xs["ms"]], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        exchange = {"a2a_ms_per_step": float(t.item()), "calls_per_step": xs["calls"],
+                    "bytes_out_per_step": xs["bytes_out"], "share_of_step": float(t.item()) / ms,
+                    "a2a_gbs": xs["bytes_out"] / (float(t.item()) * 1e-3) / 1e9 if t.item() > 0 else None,
+                    "link_gbs": 900.0}
     if args.torch_profile:  # per-kernel device time of one more step, as a table on stderr
         from torch.profiler import ProfilerActivity, profile
 
@@ -1350,7 +1388,7 @@ def run_decoder(args):
               file=sys.stderr, flush=True)
     e2e = None
     if not args.no_e2e:
-        xh, yh = x_in.cpu().pin_memory(), y_in.cpu().pin_memory()
+        xh, yh = x_in.cpu().pin_memory(), y_in.cpu().pin_memory()  # this rank's tokens
         loss_h = torch.empty((), dtype=torch.float32).pin_memory()
         torch.cuda.synchronize()
         e0.record(stream)
@@ -1359,12 +1397,23 @@ def run_decoder(args):
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1) / args.steps
+        if ws > 1:
+            t = torch.tensor([e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e_ms = float(t.item())
         e2e = {"value": nx / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
-               "h2d_bytes_per_step": (nx + ny) * c["dim"] * 2, "d2h_bytes_per_step": 4}
+               "h2d_bytes_per_step": (x_in.shape[0] + y_in.shape[0]) * c["dim"] * 2, "d2h_bytes_per_step": 4}
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+        if rank != 0:
+            return
     print(json.dumps(dict(
-        base, value=nx / (ms * 1e-3), n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
-        scaling="weak", vs_baseline=None, dtype="bf16",
-        config={"workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
+        base, value=nx / (ms * 1e-3), n_gpus=ws, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
+        scaling="strong", vs_baseline=None, dtype="bf16", exchange=exchange,
+        config={"parallelism": f"Ulysses sequence parallel over {ws} GPUs (whole blocks per rank, all-to-all "
+                               "around the attention cores, gradients all-reduced)" if ws > 1 else "single GPU",
+                "workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
                             f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
                             f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
                             f"({c['views']} views x 1024); 3D-aware maps (top-{c['topk_volume']} volume blocks, "

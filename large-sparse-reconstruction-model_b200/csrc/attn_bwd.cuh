@@ -603,7 +603,7 @@ struct RevCache {
   int gstart[kRevCacheCap];  // query groups before the entry (G <= 8)
   int wmask[kRevCacheCap];   // the entry's non-empty query windows (16 bits)
   uint4 mask[kRevCacheCap];
-  int n;       // entries (-1: the block's list did not fit)
+  int n;       // entries of the segment held
   int total;   // queries
   int groups;  // query groups (G <= 8): 8 rows = 8/G queries of one window
   int pad;
@@ -659,16 +659,11 @@ constexpr int kDkvMmaWarp = 9;
 constexpr int kDkvProducer2Warp = 10;  // select mode: gathers every other chunk
 constexpr int kDkvAccWarp = 11;        // issues the dV / dK accumulation MMAs
 
-// Warp-wide fill of the reverse cache for block `blk` of kv head `h`.
-__device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& prm, int h, int blk) {
+// Warp-wide fill of the reverse cache with entries [e0, e0 + n) of kv head
+// `h`'s reverse map (one segment of a block's list, n <= kRevCacheCap).
+__device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& prm, int h, int e0, int n) {
   const int lane = threadIdx.x & 31;
-  const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
-  const int e0 = off[blk], n = off[blk + 1] - e0;
-  if (n > kRevCacheCap) {
-    if (lane == 0) rc.n = -1;
-    __syncwarp();
-    return;
-  }
+  n = max(0, min(n, kRevCacheCap));
   const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
   int carry = 0, gcarry = 0;
   for (int b0 = 0; b0 < n; b0 += 32) {
@@ -815,7 +810,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   struct KvItem {
     QTile kt;
     int kt_idx, h, split, n_chunks, q_lo, q_hi;
-    bool skip, cached;  // cached: the block's reverse list fits the shared-memory cache
+    bool skip;
   };
   auto item_of = [&](int i) {
     KvItem it;
@@ -833,15 +828,12 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     }
     it.skip = it.kt_idx >= n_kv;
     it.n_chunks = 0;
-    it.cached = false;
     it.q_lo = it.q_hi = 0;
     if (it.skip) return it;
     it.kt = prm.kvtiles[it.kt_idx];  // rows = keys [q_start, q_start + n_q)
     it.q_lo = it.kt.kv_lo;
     it.q_hi = it.kt.kv_hi;
     if constexpr (MODE == kSelect) {
-      const int* off = prm.rev_off + (size_t)it.h * (prm.num_blocks + 1);
-      it.cached = off[it.kt.seg + 1] - off[it.kt.seg] <= kRevCacheCap;
       it.n_chunks = prm.item_nch[(size_t)it.h * prm.kvtiles_ub + it.kt_idx];
     } else {
       const int nq = max(it.q_hi - it.q_lo, 0);
@@ -900,15 +892,14 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
 
   if (warp == kDkvProducerWarp || warp == kDkvProducer2Warp) {
     // ------------------------------ producers -----------------------------
-    // Per item: warp 8 fills the reverse-map cache (both producer warps
-    // meet at a named barrier before and after, the cache being shared) and
-    // loads the K/V tile once the previous item's S^T / dP^T products are
-    // done.  Query rows: select mode with the cache and G <= 8 in 8-row
-    // windows by TMA (grouped); other select cases gathered with 16-byte
-    // cp.async (from the cache, or by a sequential walk of the map by warp
-    // 8 alone); dense modes one TMA box per operand.  The two warps take
-    // alternate chunks and publish a chunk as soon as its copies have
-    // landed; the lone walking warp publishes two chunks behind.
+    // Per item: warp 8 loads the K/V tile once the previous item's S^T /
+    // dP^T products are done and, in select mode, fills the reverse-map cache
+    // with each segment of the block's list in turn (both producer warps meet
+    // at barriers before and after every fill, the cache being shared).
+    // Query rows: select mode with G <= 8 in 8-row windows by TMA (grouped),
+    // G > 8 gathered with 16-byte cp.async from the cache; dense modes one
+    // TMA box per operand.  The two warps take alternate chunks and publish a
+    // chunk as soon as its copies have landed.
     const int pw = warp == kDkvProducerWarp ? 0 : 1;
     if (MODE == kSelect && lane < 4) {
       tma_prefetch_desc(&qm.q[lane]);
@@ -926,60 +917,65 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       if (w.skip) continue;
       const int h = w.h;
       const QTile& kt = w.kt;
-      const bool cached = MODE == kSelect && w.cached;
-      const bool grouped = cached && G <= 8;
-      const int nprod = (MODE == kSelect && !cached) ? 1 : 2;  // the sequential walk needs one warp
+      const int n_chunks = w.n_chunks;
+      // Select mode: the block's reverse list streams through the shared-memory
+      // cache in segments of at most kRevCacheCap entries.  Per segment both
+      // warps release the cache, warp 8 refills it, and the segment's chunks
+      // are produced (the warps alternate); the last segment pads up to the
+      // item's scheduled chunk count.  Dense modes: one segment, no cache.
+      int e_first = 0, e_count = 0;
       if constexpr (MODE == kSelect) {
-        if (cached) {
-          // hand the cache over: both warps release it, warp 8 refills it
+        const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
+        e_first = off[kt.seg];
+        e_count = off[kt.seg + 1] - e_first;
+      }
+      const int n_seg = MODE == kSelect ? (e_count + kRevCacheCap - 1) / kRevCacheCap : 1;
+      const bool have_rc = MODE == kSelect && n_seg > 0;
+      const bool grouped = MODE == kSelect && G <= 8;
+      auto publish = [&](int ci) {  // ci: chunk index within the item
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[(Jbase + ci) % STAGES]);
+      };
+      int cbase = 0;  // the current segment's first chunk within the item
+      for (int sg = 0; sg < (n_seg > 0 ? n_seg : 1) && ok; ++sg) {
+        if (have_rc) {
           const uint32_t par = cache_uses & 1;
           ++cache_uses;
           if (lane == 0) mbar_arrive(rc_empty);
           if (pw == 0) {
             if (!warp_wait(rc_empty, par, abort_flag, prm.err)) { ok = false; break; }
-            rev_cache_fill(rc, prm, h, kt.seg);
+            rev_cache_fill(rc, prm, h, e_first + sg * kRevCacheCap, min(kRevCacheCap, e_count - sg * kRevCacheCap));
             __syncwarp();
             if (lane == 0) mbar_arrive(rc_full);
           } else {
             if (!warp_wait(rc_full, par, abort_flag, prm.err)) { ok = false; break; }
           }
         }
-      }
-      if (pw == 0) {
-        if (!warp_wait(kv_empty, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
-          tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
-          tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+        if (sg == 0 && pw == 0) {
+          if (!warp_wait(kv_empty, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+            tma_load_3d(sK, &tm_k, 0, h, kt.q_start, kv_full);
+            tma_load_3d(sV, &tm_v, 0, h, kt.q_start, kv_full);
+          }
+          kv_loads = it_n + 1;
         }
-        kv_loads = it_n + 1;
-      }
-      const int LAG = nprod == 2 ? 0 : STAGES - 2;
-      const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
-      const int2* ent = prm.rev_entries + (size_t)h * prm.tiles_ub * prm.union_cap;
-      int e = 0, e_end = 0, tq0 = 0;
-      uint32_t w0 = 0u, w1 = 0u, w2 = 0u, w3 = 0u;  // uniform across the warp
-      if constexpr (MODE == kSelect) {
-        e = off[kt.seg] - 1;
-        e_end = off[kt.seg + 1];
-      }
-      auto publish = [&](int cc) {
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&q_full[(Jbase + cc) % STAGES]);
-      };
-      int issued = 0, published = 0;  // in this warp's own chunk sequence of this item
-      int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
-      // grouped path: this lane's current cache entry (index, first group,
-      // next entry's first group, windows, first query, query mask)
-      int e_lo = -1, e_gs = 0, e_gnext = 0, e_tq0 = 0;
-      uint32_t e_wm = 0u;
-      uint4 e_mask = make_uint4(0u, 0u, 0u, 0u);
-      const int rc_n = grouped ? rc.n : 0, rc_groups = grouped ? rc.groups : 0;
-      const int n_chunks = w.n_chunks;
-      if (pw < nprod) {
-        for (int c = pw; c < n_chunks; c += nprod) {
-          const int J = Jbase + c;
+        const int rc_n = have_rc ? rc.n : 0, rc_groups = have_rc ? rc.groups : 0;
+        const int own = !have_rc ? 0 : grouped ? (rc_groups + 7) / 8 : (rc.total + qpc - 1) / qpc;
+        int nch = max(n_chunks - cbase, 0);  // the last segment pads up to the scheduled count
+        if (sg + 1 < n_seg) nch = min(own, nch);
+        else if (own > nch && lane == 0 && pw == 0) atomicOr(prm.err, LSRM_ERR_CAPACITY);  // plan disagrees
+        int issued = 0, published = 0;  // in this warp's own chunk sequence of this segment
+        int rcur[kKvQRows / 32] = {};   // reverse-cache cursors of this lane
+        // grouped path: this lane's current cache entry (index, first group,
+        // next entry's first group, windows, first query, query mask)
+        int e_lo = -1, e_gs = 0, e_gnext = 0, e_tq0 = 0;
+        uint32_t e_wm = 0u;
+        uint4 e_mask = make_uint4(0u, 0u, 0u, 0u);
+        for (int cl = pw; cl < nch; cl += 2) {
+          const int ci = cbase + cl;  // chunk within the item
+          const int J = Jbase + ci;
           const int s = J % STAGES;
           if (!warp_wait(&q_empty[s], ((J / STAGES) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           last_issued_J = J;
@@ -992,7 +988,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             int tok = -1;
             uint32_t bits = 0u;
             if (lane < 8) {
-              const int gg = 8 * c + lane;
+              const int gg = 8 * cl + lane;
               if (gg < rc_groups) {
                 // the lane's entry only moves forward: step over gstart alone,
                 // then fetch the entry's fields once (shared-memory loads are
@@ -1041,39 +1037,13 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
           } else {
             int n = 0;
             if constexpr (MODE == kSelect) {
-              if (cached) {
-                n = rev_cache_chunk(rc, c, qpc, mt.qlist, rcur);
-              } else {
-                while (n < qpc) {
-                  if ((w0 | w1 | w2 | w3) == 0u) {
-                    if (e + 1 >= e_end) break;
-                    ++e;
-                    const int2 x = ent[e];
-                    const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-                    w0 = m.x;
-                    w1 = m.y;
-                    w2 = m.z;
-                    w3 = m.w;
-                    tq0 = prm.qtiles[x.x].q_start;
-                    continue;
-                  }
-                  const int wi = w0 ? 0 : (w1 ? 1 : (w2 ? 2 : 3));
-                  const uint32_t word = wi == 0 ? w0 : (wi == 1 ? w1 : (wi == 2 ? w2 : w3));
-                  const bool bit = (word >> lane) & 1u;
-                  const int rank = __popc(word & ((1u << lane) - 1u));
-                  const bool take = bit && rank < qpc - n;
-                  if (take) mt.qlist[n + rank] = tq0 + wi * 32 + lane;
-                  const uint32_t taken = __ballot_sync(0xffffffffu, take);
-                  n += __popc(taken);
-                  if (wi == 0) w0 &= ~taken;
-                  else if (wi == 1) w1 &= ~taken;
-                  else if (wi == 2) w2 &= ~taken;
-                  else w3 &= ~taken;
-                }
-                for (int i2 = n + lane; i2 < qpc; i2 += 32) mt.qlist[i2] = -1;
+              if (have_rc) {
+                n = rev_cache_chunk(rc, cl, qpc, mt.qlist, rcur);
+              } else {  // an empty list: padding chunks only
+                for (int i2 = lane; i2 < qpc; i2 += 32) mt.qlist[i2] = -1;
               }
             } else {
-              const int q0 = w.q_lo + c * qpc;
+              const int q0 = w.q_lo + ci * qpc;
               n = max(0, min(qpc, w.q_hi - q0));
               for (int i2 = lane; i2 < qpc; i2 += 32) mt.qlist[i2] = i2 < n ? q0 + i2 : -1;
             }
@@ -1097,7 +1067,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
               // contiguous queries: one TMA box per operand; rows past the range are
               // other tokens' data (finite, masked) or zero fill past the tensor
               if (lane == 0) {
-                const int q0 = w.q_lo + c * qpc;
+                const int q0 = w.q_lo + ci * qpc;
                 mbar_expect_tx(&q_full[s], 2 * L::QTILE);
                 tma_load_3d(sQ + s * L::QTILE, &tm_q, 0, h * G, q0, &q_full[s]);
                 tma_load_3d(sDO + s * L::QTILE, &tm_do, 0, h * G, q0, &q_full[s]);
@@ -1126,15 +1096,13 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
           }
           cp_async_commit();
           ++issued;
-          if (issued > LAG) {
-            if (LAG == 0) cp_async_wait<0>();
-            else cp_async_wait<STAGES - 2>();
-            publish(pw + nprod * published);
-            ++published;
-          }
+          cp_async_wait<0>();
+          publish(cbase + pw + 2 * published);
+          ++published;
         }
         cp_async_wait<0>();
-        for (; published < issued; ++published) publish(pw + nprod * published);
+        for (; published < issued; ++published) publish(cbase + pw + 2 * published);
+        cbase += nch;
       }
       Jbase += n_chunks;
       ++it_n;

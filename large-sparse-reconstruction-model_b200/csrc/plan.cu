@@ -463,10 +463,11 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
 // items are listed heaviest bucket first, so the longest CTAs start early
 // instead of trailing the launch.  Order inside a bucket is arbitrary; it
 // does not change any result.
-// The chunk count follows the dK/dV kernel's rule: a block whose reverse
-// list fits the shared-memory cache and G <= 8 runs in 8-row query groups
-// (chunks of 8 groups), otherwise in chunks of 64/G gathered queries.
-// One warp per item: the lanes stride over the block's reverse entries.
+// The chunk count follows the dK/dV kernel's rule: the block's reverse list
+// runs in segments of kRevCacheCap entries (one shared-memory cache fill
+// each); within a segment, G <= 8 runs in 8-row query groups (chunks of 8
+// groups), G > 8 in chunks of 64/G gathered queries.  One warp per item: the
+// lanes stride over each segment's entries.
 __global__ void sched_key_kernel(SelectPlan p, int G) {
   const int items = p.hkv * p.kvtiles_ub;
   const int n_kv = *p.n_kvtiles;
@@ -482,20 +483,23 @@ __global__ void sched_key_kernel(SelectPlan p, int G) {
       const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
       const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
       const int e0 = off[blk], e1 = off[blk + 1];
-      const bool grouped = e1 - e0 <= kRevCacheCap && G <= 8;
-      int nq = 0, ng = 0;
-      for (int e = e0 + lane; e < e1; e += 32) {
-        const int2 x = ent[e];
-        const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
-        nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
-        if (grouped) ng += window_count(m, W);
-      }
+      const bool grouped = G <= 8;
+      for (int s0 = e0; s0 < e1; s0 += kRevCacheCap) {
+        const int s1 = min(e1, s0 + kRevCacheCap);
+        int nq = 0, ng = 0;
+        for (int e = s0 + lane; e < s1; e += 32) {
+          const int2 x = ent[e];
+          const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
+          nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+          if (grouped) ng += window_count(m, W);
+        }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        nq += __shfl_xor_sync(0xffffffffu, nq, o);
-        ng += __shfl_xor_sync(0xffffffffu, ng, o);
+        for (int o = 16; o > 0; o >>= 1) {
+          nq += __shfl_xor_sync(0xffffffffu, nq, o);
+          ng += __shfl_xor_sync(0xffffffffu, ng, o);
+        }
+        chunks += grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
       }
-      chunks = grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
       bin = kSchedBins - 1 - min(chunks, kSchedBins - 1);
     }
     if (lane == 0) {

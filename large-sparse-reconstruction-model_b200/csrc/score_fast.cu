@@ -8,15 +8,19 @@
 //    256 columns so that two CTAs share an SM and one's selection phase
 //    overlaps the other's tensor-core phase).  Reduce warp
 //    w owns block row 32*(w%4)+lane and half of the columns; each element
-//    adds e = exp2(s*qk_scale - lse2) to the block's fast score, plus the
-//    terms of a rigorous error bound (below).
+//    adds e = exp2(t), t = s*qk_scale - lse2, to the block's fast score and
+//    e*t to a second sum, and keeps the largest t; with the pass's largest
+//    |q| and |lse2| these give a rigorous error bound (below).
 // 2. Certified selection.  With U = fast + bound and L = fast - bound, let T
-//    be the k'-th largest L (k' = k minus the forced own block).  Blocks with
-//    U < T are certainly outside the top-k; the rest (the candidates) get
-//    their score recomputed with the exact fixed-order arithmetic of
-//    score_exact.cuh, and the top k' of the candidates by (exact score desc,
-//    block id asc) are the answer.  T comes from an exact radix select.  This is the same set the exact scorer
-//    selects, so the indices stay bit-exact.
+//    be the k'-th largest L and T' the (k'+1)-th largest U (k' = k minus the
+//    forced own block).  Blocks with U < T are certainly outside the top-k;
+//    blocks with L > T' are certainly inside (at most k' blocks have U > T',
+//    the block among them, so at most k'-1 others can score above it).  Only
+//    the blocks in between (the ambiguous candidates) get their score
+//    recomputed with the exact fixed-order arithmetic of score_exact.cuh, and
+//    the best of them by (exact score desc, block id asc) fill the remaining
+//    places.  T and T' come from exact radix selects.  This is the same set
+//    the exact scorer selects, so the indices stay bit-exact.
 //
 // Error bound per block (generous by construction):
 //   |fast dot - exact dot| <= 2^-16 |q| |ck|       (fp32 accumulation of 64
@@ -25,7 +29,12 @@
 //   |t error| <= qk_scale 2^-16 |q||ck| + 2^-20 (2|t| + 2|lse2| + 1)
 //   |e error| <= e (0.7 |t error| + 2^-19)          (ex2 vs exp2_fixed)
 //   sum error <= 2 (n + 1) 2^-23 sum e + n 2^-120   (both accumulations; flush)
-// and the whole bound is doubled.
+// and the whole bound is doubled.  The sums over a block's elements use
+//   sum e |q|        <= max|q| sum e                (the pass's largest |q|)
+//   sum e (2|t| + 2|lse2| + 1) <= 2 (-sum e t + 2 max(t, 0) sum e)
+//                                 + (2 max|lse2| + 1) sum e
+// (|t| = -t + 2 max(t, 0)), so each element costs one exp2 and three
+// accumulations.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -72,8 +81,8 @@ struct SfLayout {
   static constexpr int CKT = 128 * RB;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_CK = QT;
-  static constexpr int OFF_COLS = OFF_CK + kSfStages * CKT;  // lse2[256], qn[256]
-  static constexpr int OFF_PART = OFF_COLS + 2 * kSfCols * 4;  // [2][128][3]
+  static constexpr int OFF_COLS = OFF_CK + kSfStages * CKT;  // lse2[128], qn[128], the pass's max |q|, max |lse2|
+  static constexpr int OFF_PART = OFF_COLS + 2 * kSfCols * 4 + 16;  // [2][128][3]
   static constexpr int OFF_BAR = OFF_PART + 2 * 128 * 3 * 4;
   static constexpr int NBAR = 2 * kSfStages + 2 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
@@ -280,7 +289,8 @@ __global__ void __launch_bounds__(kSfThreads, 2)
       bool ok = true;
       for (int ps = 0; ps < n_pass && ok; ++ps) {
         const int ncols = min(kSfCols, ncols_total - ps * kSfCols);
-        const uint32_t n_mma = (uint32_t)((ncols + 15) / 16 * 16);
+        // whole 32-column slices: every column the reduce warps read is a computed (finite) product
+        const uint32_t n_mma = (uint32_t)((ncols + 31) / 32 * 32);
         const uint32_t idesc = make_idesc(AB, 0, 0, 128, n_mma);
         if (!mbar_wait(q_full, ps & 1, abort_flag, p.err)) break;
         tc_fence_after();
@@ -310,12 +320,16 @@ __global__ void __launch_bounds__(kSfThreads, 2)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float l2e = __uint_as_float(0x3FB8AA3Bu);
     bool ok = true;
+    float* col_max = col_qn + kSfCols;  // [0] max |q|, [1] max |lse2| of the pass (non-negative: int order)
     for (int ps = 0; ps < n_pass && ok; ++ps) {
       const int ncols = min(kSfCols, ncols_total - ps * kSfCols);
       reduce_bar();
+      if (threadIdx.x < 2) col_max[threadIdx.x] = 0.f;
+      reduce_bar();
       {
         const int t = threadIdx.x;  // column of this pass
-        float l2 = 0.f, qn = 0.f;
+        // padding columns: a huge finite lse2 makes e exactly 0, so e * t is exactly 0 too
+        float l2 = 1e30f, qn = 0.f;
         if (t < ncols) {
           const int tok = r0 + ps * tpp + t / G, g = t % G;
           l2 = p.lse[(size_t)(h * G + g) * p.total_q + tok] * l2e;
@@ -324,6 +338,8 @@ __global__ void __launch_bounds__(kSfThreads, 2)
 #pragma unroll
           for (int j = 0; j < D; ++j) qn = fmaf(qv[j], qv[j], qn);
           qn = sqrtf(qn);
+          atomicMax(reinterpret_cast<int*>(&col_max[0]), __float_as_int(qn));
+          atomicMax(reinterpret_cast<int*>(&col_max[1]), __float_as_int(fabsf(l2)));
         }
         if (t < kSfCols) {
           col_lse2[t] = l2;
@@ -331,11 +347,12 @@ __global__ void __launch_bounds__(kSfThreads, 2)
         }
       }
       reduce_bar();
+      const float qmax = col_max[0], l2max = col_max[1];
       for (int c = 0; c < n_ck; ++c) {
         const int j = ps * n_ck + c, sb = j & 1;
         if (!warp_wait(&s_full[sb], (j >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
-        float acc_e = 0.f, acc_w = 0.f, acc_t = 0.f;
+        float acc_e = 0.f, acc_te = 0.f, tmax = -INFINITY;
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
           const int col0 = (2 * x + half) * 32;  // halves interleave 32-column slices
@@ -344,14 +361,17 @@ __global__ void __launch_bounds__(kSfThreads, 2)
             tmem_ld32(tmem + sb * kSfCols + lane_base + col0, sv);
             tmem_wait_ld();
 #pragma unroll
-            for (int cc = 0; cc < 32; ++cc) {
-              const int col = col0 + cc;
-              const float l2 = col_lse2[col];
-              const float t = fmaf(sv[cc], sl2, -l2);
-              const float e = col < ncols ? ex2(t) : 0.f;
-              acc_e += e;
-              acc_w = fmaf(e, col_qn[col], acc_w);
-              acc_t = fmaf(e, 2.f * fabsf(t) + 2.f * fabsf(l2) + 1.f, acc_t);
+            for (int c4 = 0; c4 < 32; c4 += 4) {
+              const float4 l4 = *reinterpret_cast<const float4*>(&col_lse2[col0 + c4]);
+              const float l2v[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float t = fmaf(sv[c4 + i], sl2, -l2v[i]);
+                const float e = ex2(t);
+                acc_e += e;
+                acc_te = fmaf(e, t, acc_te);
+                tmax = fmaxf(tmax, t);
+              }
             }
           }
         }
@@ -361,15 +381,19 @@ __global__ void __launch_bounds__(kSfThreads, 2)
         float* pt = part + (size_t)sb * 128 * 3;
         if (half == 1) {
           pt[row * 3 + 0] = acc_e;
-          pt[row * 3 + 1] = acc_w;
-          pt[row * 3 + 2] = acc_t;
+          pt[row * 3 + 1] = acc_te;
+          pt[row * 3 + 2] = tmax;
         }
         reduce_bar();
         const int b = c * 128 + row;
         if (half == 0 && b < nb) {
-          SF[b] += acc_e + pt[row * 3 + 0];
-          WS[b] += acc_w + pt[row * 3 + 1];
-          TS[b] += acc_t + pt[row * 3 + 2];
+          const float se = acc_e + pt[row * 3 + 0];
+          const float ste = acc_te + pt[row * 3 + 1];
+          const float tm = fmaxf(fmaxf(tmax, pt[row * 3 + 2]), 0.f);
+          SF[b] += se;
+          WS[b] += qmax * se;  // >= sum e |q|
+          // >= sum e (2|t| + 2|lse2| + 1)
+          TS[b] += 2.f * (fmaxf(-ste, 0.f) + 2.f * tm * se) + (2.f * l2max + 1.f) * se;
         }
       }
     }
@@ -412,32 +436,47 @@ __global__ void __launch_bounds__(kSfThreads, 2)
     TS[b] = (b == self) ? -INFINITY : sf + e;
   }
   __syncthreads();
-  // threshold: the kp-th largest lower bound (ties counted), radix select
-  float thr = -INFINITY;
-  if (kp > 0) thr = kth_largest(WS, nb, kp, reinterpret_cast<uint32_t*>(smem + L::OFF_HIST), s_misc + 4);
-  // candidates: upper bound reaches the threshold
+  // thresholds (ties counted, exact radix selects): the kp-th largest lower
+  // bound, and the (kp+1)-th largest upper bound above which a block's lower
+  // bound makes it certainly chosen
+  float thr = -INFINITY, thr_hi = -INFINITY;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L::OFF_HIST);
+  if (kp > 0) thr = kth_largest(WS, nb, kp, hist, s_misc + 4);
+  if (kp > 0 && kp < nb) thr_hi = kth_largest(TS, nb, kp + 1, hist, s_misc + 4);
+  // candidates (upper bound reaches thr): certainly chosen ones go straight to
+  // `chosen`, the ambiguous rest to `cand`
   if (threadIdx.x == 0) {
     s_misc[0] = 0;
     s_misc[1] = 0;
+    s_misc[2] = 0;
+    if (self >= 0) chosen[s_misc[2]++] = self;
   }
   __syncthreads();
   if (kp > 0) {
     for (int b = threadIdx.x; b < nb; b += kSfThreads) {
       if (b != self && TS[b] >= thr) {
-        const int slot = atomicAdd(&s_misc[0], 1);
-        if (slot < kSfCandCap) cand[slot] = b;
-        else s_misc[1] = 1;
+        if (WS[b] > thr_hi) {
+          const int slot = atomicAdd(&s_misc[2], 1);
+          if (slot < 64) chosen[slot] = b;
+        } else {
+          const int slot = atomicAdd(&s_misc[0], 1);
+          if (slot < kSfCandCap) cand[slot] = b;
+          else s_misc[1] = 1;
+        }
       }
     }
   }
   __syncthreads();
   const int n_cand_raw = s_misc[0];
   const bool fallback = s_misc[1] != 0;
+  // places left for the ambiguous candidates
+  const int slots = kp - (s_misc[2] - (self >= 0 ? 1 : 0));
+  __syncthreads();
   // Exact scores of the candidates (every block on the fallback path):
   // stage A, all threads: per (candidate, column) the fixed-order score term;
   // stage B, one thread per candidate: ordered sums (heads, then tokens).
   // Scratch for stage A: the per-block arrays (3 * nb_cap floats).
-  const int n_exact = fallback ? nb : (n_cand_raw > kp ? n_cand_raw : 0);
+  const int n_exact = fallback ? nb : (n_cand_raw > slots && slots > 0 ? n_cand_raw : 0);
   if (n_exact > 0) {
     // Stage A, all threads: per (candidate, column) the fixed-order score
     // term, from the candidates' key rows staged in shared memory (the CK
@@ -530,9 +569,8 @@ __global__ void __launch_bounds__(kSfThreads, 2)
     __syncthreads();
   }
   const int n_cand = n_cand_raw;
-  // choose kp blocks: (exact desc, id asc) among candidates (or all blocks)
-  if (threadIdx.x == 0) s_misc[2] = 0;
-  __syncthreads();
+  // choose: (exact desc, id asc) among the ambiguous candidates for the places
+  // left (or, on the fallback path, kp blocks among all blocks)
   if (fallback) {
     if (threadIdx.x == 0) {
       int n_ch = 0;
@@ -552,12 +590,11 @@ __global__ void __launch_bounds__(kSfThreads, 2)
       s_misc[2] = n_ch;
     }
   } else {
-    // a candidate is chosen when fewer than kp candidates beat it; the
-    // order of `chosen` does not matter (the output is sorted by id)
-    if (threadIdx.x == 0 && self >= 0) chosen[atomicAdd(&s_misc[2], 1)] = self;
+    // an ambiguous candidate is chosen when fewer than `slots` of them beat
+    // it; the order of `chosen` does not matter (the output is sorted by id)
     for (int i = threadIdx.x; i < n_cand; i += kSfThreads) {
-      bool take = n_cand <= kp;
-      if (!take) {
+      bool take = slots > 0 && n_cand <= slots;
+      if (!take && slots > 0) {
         const float v = cand_exact[i];
         const int id = cand[i];
         int beat = 0;
@@ -565,7 +602,7 @@ __global__ void __launch_bounds__(kSfThreads, 2)
           const float w = cand_exact[j];
           beat += (w > v) || (w == v && cand[j] < id);
         }
-        take = beat < kp;
+        take = beat < slots;
       }
       if (take) {
         const int slot = atomicAdd(&s_misc[2], 1);

@@ -12,9 +12,11 @@ are the reference's, so its state dicts load (weight-normed Linears keep the
 reference's parametrization).  Differences inside: the per-head LayerNorm32
 of q / k / compressed k is the fused ``lsrm_head_layernorm_pack`` (one pass
 each way), and the cross/self gate's sigmoid and merge are the fused
-two-branch ``lsrm_gate_merge``; the Linears are library GEMMs.  Sequence
-parallelism goes through ``lsrm_sparse.ulysses`` instead of the reference's
-all-gather path, so ``use_sequence_parallel=True`` is rejected here.
+two-branch ``lsrm_gate_merge``; the Linears are library GEMMs.  With
+``use_sequence_parallel=True`` the inputs are one rank's whole blocks as
+``ulysses.seq_parallel_token_blocks`` distributed them, and the attention
+cores exchange heads and sequence through ``lsrm_sparse.ulysses`` (Ulysses)
+instead of the reference's K/V all-gathers.
 """
 
 from __future__ import annotations
@@ -56,9 +58,6 @@ class CrossAttention(nn.Module):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, qkv_bias=False, use_weight_norm=False, oneside=False,
                  topk_volume=8, topk_multiimage=2, use_sequence_parallel=False, no_checkpoint_all_gather=False):
         super().__init__()
-        if use_sequence_parallel:
-            raise NotImplementedError("sequence parallelism runs through lsrm_sparse.ulysses (head/sequence "
-                                      "all-to-all), not through this module")
         self.num_q_heads = num_q_heads
         self.num_kv_heads = num_kv_heads
         self.dim = dim
@@ -71,7 +70,7 @@ class CrossAttention(nn.Module):
         self.proj_x = nn.Linear(dim, dim)
         self.norm_layer_q = LayerNorm32(self.head_dim, elementwise_affine=False)
         self.norm_layer_kv = LayerNorm32(self.head_dim, elementwise_affine=False)
-        self.use_sequence_parallel = False
+        self.use_sequence_parallel = use_sequence_parallel
         self.no_checkpoint_all_gather = no_checkpoint_all_gather
         self.topk_volume = topk_volume
         self.topk_multiimage = topk_multiimage
@@ -110,6 +109,8 @@ class CrossAttention(nn.Module):
         return F.gate_merge(nn.functional.linear(x, lin.weight, lin.bias), [x_cross, x_self])
 
     def forward(self, x, cu_seqlens_x, y, cu_seqlens_y, im_num, attn_map):
+        if self.use_sequence_parallel:
+            return self._forward_sequence_parallel(x, y, im_num, attn_map)
         q_x, k_x, v_x = self.q_proj_x(x), self.k_proj_x(x), self.v_proj_x(x)
         k_y, v_y = self.k_proj_y(y), self.v_proj_y(y)
         if not self.oneside:
@@ -144,6 +145,87 @@ class CrossAttention(nn.Module):
             return x_new, sparse_info
         y_cross = self.y_2_x_attn_out(y, q_y, k_x, v_x, attn_map["img_to_vol_attn"], y_cross_out)
         y_self = self.y_2_y_attn_out(y, q_y, k_y, v_y, attn_map["img_to_img_attn"], y_self_out)
+        y_new = self.proj_y(self._gate(y, self.gate_y, y_cross, y_self))
+        return x_new, y_new, sparse_info
+
+
+    def _forward_sequence_parallel(self, x, y, im_num, attn_map):
+        """This rank's volume tokens ``x`` and image tokens ``y`` (whole blocks,
+        as ``ulysses.seq_parallel_token_blocks`` distributed them, with
+        ``attn_map["sp"]`` set).  Everything token-local runs on the local
+        tokens with all heads: projections, the ResBlock compression of each
+        local block (``local_cu_block_include_tokens``), the per-head norms,
+        the intra-block window branch and the gates.  The compressed and
+        selected branches, which attend across blocks, run on the whole
+        sequences for this rank's heads: q / k / v and the compressed keys go
+        sequence -> head by one all-to-all each, the branch outputs come back
+        head -> sequence (the Ulysses scheme; the reference all-gathers K/V
+        instead, models_sparse/utils.py:326-474)."""
+        from . import ulysses
+
+        sp = attn_map["sp"]
+        W, rank, group = sp.world, sp.rank, sp.group
+        Hq, Hkv, D = self.num_q_heads, self.num_kv_heads, self.head_dim
+        if Hkv % W:
+            raise ValueError(f"sequence parallelism needs the kv heads ({Hkv}) to split evenly over {W} ranks")
+        hp, hkp = Hq // W, Hkv // W
+        k0, k1 = rank * hkp, (rank + 1) * hkp
+        m_vv, m_vi = attn_map["vol_to_vol_attn"], attn_map["vol_to_img_attn"]
+        q_x, k_x, v_x = self.q_proj_x(x), self.k_proj_x(x), self.v_proj_x(x)
+        k_y, v_y = self.k_proj_y(y), self.v_proj_y(y)
+        # compression of the raw keys / values on local whole blocks, then the per-head norms (the
+        # reference's order: In modules first, _normalize_qkv after)
+        ck_x2x, cv_x2x = self.x_2_x_attn_in(k_x, v_x, m_vv)
+        ck_x2y, cv_x2y = self.x_2_y_attn_in(k_y, v_y, m_vi)
+        if not self.oneside:
+            m_ii, m_iv = attn_map["img_to_img_attn"], attn_map["img_to_vol_attn"]
+            ck_y2y, cv_y2y = self.y_2_y_attn_in(k_y, v_y, m_ii)
+            ck_y2x, cv_y2x = self.y_2_x_attn_in(k_x, v_x, m_iv)
+            q_y = self._norm(self.q_proj_y(y), Hq)
+            ck_y2y, ck_y2x = self._norm(ck_y2y, Hkv), self._norm(ck_y2x, Hkv)
+        q_x, k_x, ck_x2x = self._norm(q_x, Hq), self._norm(k_x, Hkv), self._norm(ck_x2x, Hkv)
+        k_y, ck_x2y = self._norm(k_y, Hkv), self._norm(ck_x2y, Hkv)
+
+        def to_heads(t, plan, heads):  # [n_local, heads*D] -> [N, heads/W * D]
+            h = ulysses.seq_to_head(t.reshape(t.shape[0], heads, D), plan, group)
+            return h.reshape(h.shape[0], -1)
+
+        def to_tokens(t, plan):  # [N, hp*D] -> [n_local, Hq*D]
+            return ulysses.head_to_seq(t.reshape(t.shape[0], hp, D), plan, Hq, group).reshape(-1, Hq * D)
+
+        def heads_of(m):  # this rank's kv heads of a map, the whole sequence's block tables
+            return {"block_topk": m["block_topk"][k0:k1], "cu_seqblocks": m["cu_seqblocks"],
+                    "cu_block_include_tokens": m["cu_block_include_tokens"]}
+
+        mid = SpatialSparseAttentionMid(hidden_dim=hp * D, num_q_heads=hp, num_kv_heads=hkp)
+        Nx, Ny = sp.vol.total, sp.img.total
+        cu_nx = torch.tensor([0, Nx], dtype=torch.int32, device=x.device)
+        cu_ny = torch.tensor([0, Ny], dtype=torch.int32, device=x.device)
+        qh_x, kh_x, vh_x = to_heads(q_x, sp.vol, Hq), to_heads(k_x, sp.vol, Hkv), to_heads(v_x, sp.vol, Hkv)
+        kh_y, vh_y = to_heads(k_y, sp.img, Hkv), to_heads(v_y, sp.img, Hkv)
+        sparse_info = {}
+        o, sparse_info["v_2_i"] = mid(qh_x, cu_nx, kh_y, to_heads(ck_x2y, sp.img_blocks, Hkv), vh_y,
+                                      to_heads(cv_x2y, sp.img_blocks, Hkv), self.topk_multiimage * im_num,
+                                      heads_of(m_vi))
+        x_cross_out = {k: to_tokens(t, sp.vol) for k, t in o.items()}
+        o, sparse_info["v_2_v"] = mid(qh_x, cu_nx, kh_x, to_heads(ck_x2x, sp.vol_blocks, Hkv), vh_x,
+                                      to_heads(cv_x2x, sp.vol_blocks, Hkv), self.topk_volume, heads_of(m_vv))
+        x_self_out = {k: to_tokens(t, sp.vol) for k, t in o.items()}
+        x_cross = self.x_2_y_attn_out(x, q_x, k_y, v_y, m_vi, x_cross_out)
+        x_self = self.x_2_x_attn_out(x, q_x, k_x, v_x, m_vv, x_self_out)  # window: local blocks
+        x_new = self.proj_x(self._gate(x, self.gate_x, x_cross, x_self))
+        if self.oneside:
+            return x_new, sparse_info
+        qh_y = to_heads(q_y, sp.img, Hq)
+        o, sparse_info["i_2_v"] = mid(qh_y, cu_ny, kh_x, to_heads(ck_y2x, sp.vol_blocks, Hkv), vh_x,
+                                      to_heads(cv_y2x, sp.vol_blocks, Hkv), self.topk_volume, heads_of(m_iv))
+        y_cross_out = {k: to_tokens(t, sp.img) for k, t in o.items()}
+        o, sparse_info["i_2_i"] = mid(qh_y, cu_ny, kh_y, to_heads(ck_y2y, sp.img_blocks, Hkv), vh_y,
+                                      to_heads(cv_y2y, sp.img_blocks, Hkv), self.topk_multiimage * im_num,
+                                      heads_of(m_ii))
+        y_self_out = {k: to_tokens(t, sp.img) for k, t in o.items()}
+        y_cross = self.y_2_x_attn_out(y, q_y, k_x, v_x, m_iv, y_cross_out)
+        y_self = self.y_2_y_attn_out(y, q_y, k_y, v_y, m_ii, y_self_out)
         y_new = self.proj_y(self._gate(y, self.gate_y, y_cross, y_self))
         return x_new, y_new, sparse_info
 

@@ -27,7 +27,8 @@ import torch.distributed as dist
 from . import ops
 
 __all__ = ["shard_blocks", "ShardPlan", "seq_to_head", "head_to_seq", "exchange_gate_logits",
-           "three_branch_attention", "time_exchanges", "ExchangeTimer"]
+           "three_branch_attention", "time_exchanges", "ExchangeTimer", "RowPlan", "DecoderShards",
+           "seq_parallel_token_blocks"]
 
 
 def shard_blocks(cu_block_include_tokens: Sequence[int], world: int) -> List[Tuple[int, int]]:
@@ -310,3 +311,111 @@ def whole_sequence_branches(q, k, v, z, cu_blk, topk: int, window: int, softmax_
     out = F.three_branch_attention(q, k, v, cu_blk, topk, window, z, per_head=True, softmax_scale=softmax_scale,
                                    capture=capture)
     return out.view(N, H, D)
+
+
+# ---------------------------------------------------------------------------
+# Token distribution of the sequence-parallel decoder
+# ---------------------------------------------------------------------------
+
+
+class RowPlan:
+    """Split sizes of an exchange over rows of any kind (tokens or blocks):
+    rank r holds ``counts[r]`` consecutive rows of ``total``.  Has the fields
+    the exchanges read (``world``, ``rank``, ``counts``, ``total``)."""
+
+    def __init__(self, counts: Sequence[int], rank: int):
+        self.counts = [int(c) for c in counts]
+        self.world, self.rank = len(self.counts), rank
+        self.total = sum(self.counts)
+        self.start = sum(self.counts[:rank])
+
+    @property
+    def local(self) -> Tuple[int, int]:
+        return self.start, self.start + self.counts[self.rank]
+
+
+class DecoderShards:
+    """Where this rank's volume and image tokens and blocks lie, for the
+    exchanges of ``CrossAttention(use_sequence_parallel=True)``: token plans
+    (``vol``, ``img``: whole blocks, token-balanced) and the matching block
+    plans (``vol_blocks``, ``img_blocks``) for the compressed keys."""
+
+    def __init__(self, cu_vol: Sequence[int], cu_img: Sequence[int], world: int, rank: int, group=None):
+        self.group, self.world, self.rank = group, world, rank
+        self.vol = ShardPlan(cu_vol, world, rank)
+        self.img = ShardPlan(cu_img, world, rank)
+        self.vol_blocks = RowPlan([b - a for a, b in self.vol.blocks], rank)
+        self.img_blocks = RowPlan([b - a for a, b in self.img.blocks], rank)
+
+
+_VOL_KEYED = ("vol_to_vol_attn", "img_to_vol_attn")  # maps whose keys are volume tokens
+_IMG_KEYED = ("img_to_img_attn", "vol_to_img_attn")
+
+
+def _local_blocks(cu: torch.Tensor, plan: ShardPlan) -> torch.Tensor:
+    b0, b1 = plan.blocks[plan.rank]
+    return (cu[b0:b1 + 1] - cu[b0]).to(torch.int32)
+
+
+class _Collect(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, plan: ShardPlan, group):
+        n_max = max(plan.counts)
+        pad = x.new_zeros((n_max,) + tuple(x.shape[1:]))
+        pad[: x.shape[0]] = x
+        full = x.new_empty((plan.world * n_max,) + tuple(x.shape[1:]))
+        dist.all_gather_into_tensor(full, pad.contiguous(), group=group)
+        ctx.plan = plan
+        return torch.cat([full[r * n_max: r * n_max + c] for r, c in enumerate(plan.counts)])
+
+    @staticmethod
+    def backward(ctx, g):
+        s, e = ctx.plan.local
+        return g[s:e], None, None
+
+
+def seq_parallel_token_blocks(vol_token_arr, img_token_arr, attn_map, mode: str = "distribute", group=None):
+    """The token distribution of the sequence-parallel decoder, with the
+    reference's call shape (models_sparse/seqparallel_utils.py:948-1169) for
+    one sequence.
+
+    ``mode="distribute"``: every rank holds all tokens; each tensor of
+    ``vol_token_arr`` / ``img_token_arr`` ([N, C]) is cut to this rank's run of
+    whole blocks (token-balanced, :func:`shard_blocks`; volume blocks from
+    ``attn_map["vol_to_vol_attn"]``, image blocks from ``"img_to_img_attn"``).
+    Every map gets ``local_cu_block_include_tokens`` (this rank's blocks of its
+    key tokens, local offsets) and ``attn_map["sp"]`` the :class:`DecoderShards`;
+    the maps' global tables stay as they are (the attention cores run on the
+    whole sequence for this rank's heads).  Returns ``(vol_tokens, img_tokens,
+    cu_seqlens_volume, cu_seqlens_image, attn_map)`` with local cu_seqlens.
+
+    ``mode="collect"``: all-gathers the volume tensors back to all tokens
+    (differentiable: the backward keeps this rank's rows, i.e. every rank is
+    expected to compute the same loss on the collected tensor).
+    """
+    if mode not in ("distribute", "collect"):
+        raise ValueError("mode must be 'distribute' or 'collect'")
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if mode == "collect":
+        sp = attn_map["sp"]
+        return [_Collect.apply(t, sp.vol, group) for t in vol_token_arr], [], None, None, attn_map
+    cu_vol_t = attn_map["vol_to_vol_attn"]["cu_block_include_tokens"]
+    cu_img_t = attn_map["img_to_img_attn"]["cu_block_include_tokens"]
+    for keyed, ref in ((_VOL_KEYED, cu_vol_t), (_IMG_KEYED, cu_img_t)):
+        for name in keyed:
+            if name in attn_map and not torch.equal(attn_map[name]["cu_block_include_tokens"], ref):
+                raise ValueError(f"{name} must use the same key blocks as {keyed[0]} under sequence parallelism")
+    sp = DecoderShards(cu_vol_t.tolist(), cu_img_t.tolist(), world, rank, group)
+    out = dict(attn_map)
+    for keyed, plan, cu in ((_VOL_KEYED, sp.vol, cu_vol_t), (_IMG_KEYED, sp.img, cu_img_t)):
+        loc = _local_blocks(cu, plan)
+        for name in keyed:
+            if name in out:
+                out[name] = dict(out[name], local_cu_block_include_tokens=loc)
+    out["sp"] = sp
+    (vs, ve), (is_, ie) = sp.vol.local, sp.img.local
+    dev = cu_vol_t.device
+    cu_v = torch.tensor([0, ve - vs], dtype=torch.int32, device=dev)
+    cu_i = torch.tensor([0, ie - is_], dtype=torch.int32, device=dev)
+    return [t[vs:ve] for t in vol_token_arr], [t[is_:ie] for t in img_token_arr], cu_v, cu_i, out

@@ -1,11 +1,14 @@
 """Selected-block attention on problems whose lists overflow the kernels'
-shared-memory caches, so the producers walk them from global memory:
+shared-memory caches:
 
 * a query tile whose union of selected blocks has more than 512 entries
-  (forward and dQ union cache), and
-* a KV block selected by more than 1024 query tiles (dK/dV reverse-map cache),
+  (the forward and dQ producers walk it from global memory),
+* KV blocks selected by more than 1024 query tiles (the dK/dV reverse map
+  streams through its cache in segments of 1024 entries): 1250 tiles, 5000
+  tiles (five segments, 8 query heads per kv head) and 1094 tiles of 128
+  queries on two kv heads,
 * a KV block with more than 4096 8-row query windows (dK/dV window list) but
-  few enough reverse entries for the reverse-map cache.
+  few enough reverse entries for one cache segment.
 
 Checked against a gather-based fp32 torch reference of the same op (each query
 attends the tokens of its selected blocks), forward and backward."""
@@ -77,6 +80,8 @@ CASES = [
     ("union_over_512", 4096, 4, 1, 1, 64, 8, False),        # ~645 blocks per 128-query tile
     ("reverse_over_1024", 20000, 4, 8, 1, 64, 4, True),     # block 0 in all 1250 16-query tiles
     ("windows_over_4096", 40000, 4, 1, 1, 64, 4, True),     # block 0: 313 tiles, ~5000 8-query windows
+    ("reverse_five_segments", 80000, 4, 8, 1, 64, 4, True),  # block 0 in all 5000 16-query tiles
+    ("reverse_two_heads_g1", 140000, 4, 2, 2, 64, 4, True),  # block 0 in all 1094 128-query tiles, per head
 ]
 
 
