@@ -255,6 +255,11 @@ def count_pairs(p: Problem, bt: torch.Tensor):
 
 
 class ClockSampler:
+    """nvidia-smi clock / throttle samples every 200 ms.  Entering starts the
+    sampler and returns once its first sample arrived (up to 5 s), so the
+    timed region that follows is covered; only samples taken between enter
+    and exit count."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -262,27 +267,47 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self._all.append((time.perf_counter(), line))
 
     def __enter__(self):
+        import threading
+
+        self._all = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+        t0 = time.perf_counter()
+        while not self._all and time.perf_counter() - t0 < 5.0:
+            time.sleep(0.02)
+        self.t_enter = time.perf_counter()
         return self
 
     def __exit__(self, *a):
         self.lines = []
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self.proc is None:
+            return
+        t_exit = time.perf_counter()
+        time.sleep(0.25)  # one more sample of the tail of the region
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+        self._thread.join(timeout=5)
+        inside = [l for t, l in self._all if self.t_enter - 0.2 <= t <= t_exit + 0.25]
+        self.lines = inside or [l for _, l in self._all[-1:]]
 
     def summary(self):
         rows = []

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define LSRM_ABI_VERSION 1
+#define LSRM_ABI_VERSION 2
 
 /* return codes (negative) and device error bits (positive) */
 #define LSRM_OK 0
@@ -198,10 +198,18 @@ int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, i
  * scores in ascending token order; force_self always selects block j for
  * query block j of a sequence.  `q` may be fp16/bf16 (shape->dtype); ck has
  * the same dtype; lse_ln fp32.  sm_scale <= 0 selects 1/sqrt(D); the scale
- * used is float(sm_scale * 1.44269504) evaluated in double. */
+ * used is float(sm_scale * 1.44269504) evaluated in double.  Per query block
+ * the scores come from tensor cores with certified error bounds and only the
+ * blocks the bounds leave undecided are scored exactly (same indices); that
+ * path needs `workspace` of lsrm_block_topk_workspace_bytes (the compressed
+ * keys' norms and every (query block, kv head)'s score bounds, fp32); the
+ * per-token path needs none (0 bytes). */
+size_t lsrm_block_topk_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t topk,
+                                       int32_t num_query_blocks);
 int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
                     const float* lse_ln, int32_t topk, const int32_t* cu_query_blocks, int32_t num_query_blocks,
-                    int32_t force_self, double sm_scale, int32_t* block_topk, int* err_flags, void* stream);
+                    int32_t force_self, double sm_scale, int32_t* block_topk, void* workspace,
+                    size_t workspace_bytes, int* err_flags, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Compression (SpatialSparseAttentionIn, spatial_sparse_attention.py:27-67) */

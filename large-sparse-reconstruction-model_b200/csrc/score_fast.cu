@@ -69,7 +69,11 @@ struct FastScoreParams {
   int G;
   int topk;
   int force_self;
-  int nb_cap;
+  int nb_cap;      // blocks per sequence the bound slices and shared arrays hold
+  int nb_total;    // compressed blocks of all sequences (the norm table's row length)
+  int nqb;         // query blocks
+  const float* ckn;  // [Hkv, nb_total] norms of the compressed keys
+  float* bounds;     // [Hkv, nqb, 2, nb_cap] lower / upper score bounds
   float qk_scale;
   int* err;
 };
@@ -86,16 +90,48 @@ struct SfLayout {
   static constexpr int OFF_BAR = OFF_PART + 2 * 128 * 3 * 4;
   static constexpr int NBAR = 2 * kSfStages + 2 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_CAND = OFF_MISC + 64;  // cand ids [cap], exact [cap], chosen[64]
+  static constexpr int OFF_ARR = OFF_MISC + 64;
+  // per-block arrays: fast score SF, |q|-weighted sum WS and t-term sum TS [nb_cap each]
+  static size_t bytes(int nb_cap) { return (size_t)OFF_ARR + 12ull * nb_cap + 1024; }
+};
+
+constexpr int kSelThreads = 256;
+constexpr int kSelStage = 128;  // candidate key rows staged per batch of the exact stage
+
+template <int D>
+struct SelLayout {
+  static constexpr int RB = 2 * D;
+  static constexpr int OFF_CK = 0;                          // staged candidate key rows [kSelStage][D]
+  static constexpr int OFF_MISC = OFF_CK + kSelStage * RB;  // counters, radix-select scratch
+  static constexpr int OFF_CAND = OFF_MISC + 64;            // cand ids [cap], exact [cap], chosen[64]
   static constexpr int OFF_HIST = OFF_CAND + kSfCandCap * 8 + 64 * 4;  // radix-select histogram [256]
   static constexpr int OFF_ARR = OFF_HIST + 256 * 4;
-  // per-block arrays: fast score SF [nb_cap], then weighted sum WS and t-term
-  // sum TS [nb_cap each] inside a scratch of 2 * max(nb_cap, kSfMinScratch)
+  // SF [nb_cap] (the fallback's exact scores), then the lower / upper bounds
+  // WS / TS [nb_cap each] inside a scratch of 2 * max(nb_cap, kSfMinScratch)
   // floats that the exact stage reuses for its terms
   static size_t bytes(int nb_cap) {
-    return (size_t)OFF_ARR + 4ull * nb_cap + 8ull * (size_t)(nb_cap > kSfMinScratch ? nb_cap : kSfMinScratch) + 1024;
+    return (size_t)OFF_ARR + 4ull * nb_cap + 8ull * (size_t)(nb_cap > kSfMinScratch ? nb_cap : kSfMinScratch) + 128;
   }
 };
+
+// |ck| of every (compressed block, kv head), fp32 (exact conversion of the
+// 16-bit values, fused multiply-add accumulation).
+template <typename T, int D>
+__global__ void ck_norms_kernel(const T* __restrict__ ck, long long stride, int hkv, int nb, float* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)nb * hkv) return;
+  const int b = (int)(i / hkv), h = (int)(i - (long long)b * hkv);
+  const uint4* r4 = reinterpret_cast<const uint4*>(ck + (size_t)b * stride + (size_t)h * D);
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    const uint4 u = r4[c];
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf((float)e[j], (float)e[j], acc);
+  }
+  out[(size_t)h * nb + b] = sqrtf(acc);
+}
 
 // Row of D 16-bit values -> fp32 (exact conversion), 16-byte loads.
 template <typename T, int D>
@@ -182,7 +218,7 @@ __device__ float kth_largest(const float* vals, int n, int k, uint32_t* hist, in
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kSfThreads, 2)
-    qblock_topk_fast_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck,
+    qblock_scores_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ck,
                             const FastScoreParams p) {
   using L = SfLayout<D>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -225,10 +261,6 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   uint64_t* mma_done = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  int* s_misc = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);  // [0]=n_cand [1]=fallback
-  int* cand = reinterpret_cast<int*>(smem + L::OFF_CAND);
-  float* cand_exact = reinterpret_cast<float*>(cand + kSfCandCap);
-  int* chosen = reinterpret_cast<int*>(cand_exact + kSfCandCap);
   float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);
   float* WS = SF + p.nb_cap;
   float* TS = WS + p.nb_cap;
@@ -406,7 +438,77 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   }
   if (*abort_flag) return;
 
-  // ------------------------------ selection --------------------------------
+  // ------------------------- certified bounds ------------------------------
+  // lower (L) and upper (U) bound of every block's score, written to this
+  // (query block, kv head)'s slice of the bounds workspace; the forced own
+  // block gets -inf in both (it is chosen apart from the ranking)
+  int self = -1;
+  if (p.force_self && min(p.topk, nb) > 0) {
+    int qb_lo = 0, qb_hi = qb + 1;
+    while (qb_lo < qb_hi) {
+      const int mid = (qb_lo + qb_hi) >> 1;
+      if (p.cu_qblocks[mid] >= p.cu_seqlens_q[seq]) qb_hi = mid;
+      else qb_lo = mid + 1;
+    }
+    const int sidx = qb - qb_lo;
+    if (sidx >= 0 && sidx < nb) self = sidx;
+  }
+  const float n_f = (float)ncols_total;
+  float* Lg = p.bounds + ((size_t)h * p.nqb + qb) * 2 * p.nb_cap;
+  float* Ug = Lg + p.nb_cap;
+  for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+    const float ckn = p.ckn[(size_t)h * p.nb_total + blk0 + b];
+    const float sf = SF[b];
+    const float e = 2.f * (0.7f * (sl2 * 0x1p-16f * ckn * WS[b] + 0x1p-20f * TS[b]) +
+                           (0x1p-19f + (n_f + 1.f) * 0x1p-22f) * sf + n_f * 0x1p-120f);
+    Lg[b] = (b == self) ? -INFINITY : sf - e;
+    Ug[b] = (b == self) ? -INFINITY : sf + e;
+  }
+}
+
+// Selection of one (query block, kv head) from its certified bounds (see the
+// top of this file): thresholds by exact radix selects, certainly chosen
+// blocks directly, the ambiguous ones by the exact fixed-order score.  No
+// tensor cores and small shared memory, so several CTAs share an SM and hide
+// the latency of the bound and query-row loads.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kSelThreads, 4) qblock_select_kernel(const FastScoreParams p) {
+  using L = SelLayout<D>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int qb = blockIdx.x, h = blockIdx.y;
+  const int G = p.G;
+  const int r0 = p.cu_qblocks[qb], r1 = p.cu_qblocks[qb + 1];
+  int lo = 0, hi = p.num_seqs + 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (p.cu_seqlens_q[mid] > r0) hi = mid;
+    else lo = mid + 1;
+  }
+  const int seq = max(lo - 1, 0);
+  const int blk0 = p.cu_cblocks[seq];
+  const int nb = p.cu_cblocks[seq + 1] - blk0;
+  const int ncols_total = max(r1 - r0, 0) * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* sCK = smem + L::OFF_CK;
+  int* s_misc = reinterpret_cast<int*>(smem + L::OFF_MISC);  // [0] n_cand [1] fallback [2] chosen [4..] select
+  int* cand = reinterpret_cast<int*>(smem + L::OFF_CAND);
+  float* cand_exact = reinterpret_cast<float*>(cand + kSfCandCap);
+  int* chosen = reinterpret_cast<int*>(cand_exact + kSfCandCap);
+  float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);  // the fallback's exact scores
+  float* WS = SF + p.nb_cap;                                  // lower bounds, then exact-stage scratch
+  float* TS = WS + p.nb_cap;                                  // upper bounds
+  if (nb > p.nb_cap) {
+    if (threadIdx.x == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
+    return;
+  }
+  const float* Lg = p.bounds + ((size_t)h * p.nqb + qb) * 2 * p.nb_cap;
+  const float* Ug = Lg + p.nb_cap;
+  for (int b = threadIdx.x; b < nb; b += kSelThreads) {
+    WS[b] = Lg[b];
+    TS[b] = Ug[b];
+  }
   const int kk = min(p.topk, nb);
   int self = -1;
   if (p.force_self && kk > 0) {
@@ -420,21 +522,6 @@ __global__ void __launch_bounds__(kSfThreads, 2)
     if (sidx >= 0 && sidx < nb) self = sidx;
   }
   const int kp = kk - (self >= 0 ? 1 : 0);
-  // bounds: WS <- lower, TS <- upper
-  const float n_f = (float)ncols_total;
-  for (int b = threadIdx.x; b < nb; b += kSfThreads) {
-    float kv[D];
-    load_row_f32<T, D>(static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D, kv);
-    float ckn = 0.f;
-#pragma unroll
-    for (int j = 0; j < D; ++j) ckn = fmaf(kv[j], kv[j], ckn);
-    ckn = sqrtf(ckn);
-    const float sf = SF[b];
-    const float e = 2.f * (0.7f * (sl2 * 0x1p-16f * ckn * WS[b] + 0x1p-20f * TS[b]) +
-                           (0x1p-19f + (n_f + 1.f) * 0x1p-22f) * sf + n_f * 0x1p-120f);
-    WS[b] = (b == self) ? -INFINITY : sf - e;
-    TS[b] = (b == self) ? -INFINITY : sf + e;
-  }
   __syncthreads();
   // thresholds (ties counted, exact radix selects): the kp-th largest lower
   // bound, and the (kp+1)-th largest upper bound above which a block's lower
@@ -453,7 +540,7 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   }
   __syncthreads();
   if (kp > 0) {
-    for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+    for (int b = threadIdx.x; b < nb; b += kSelThreads) {
       if (b != self && TS[b] >= thr) {
         if (WS[b] > thr_hi) {
           const int slot = atomicAdd(&s_misc[2], 1);
@@ -479,17 +566,15 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   const int n_exact = fallback ? nb : (n_cand_raw > slots && slots > 0 ? n_cand_raw : 0);
   if (n_exact > 0) {
     // Stage A, all threads: per (candidate, column) the fixed-order score
-    // term, from the candidates' key rows staged in shared memory (the CK
-    // ring is free now) and the query rows of the tile (still in sQ when the
-    // query block took one pass; else read from global memory).
+    // term, from the candidates' key rows staged in shared memory and the
+    // query block's rows read from global memory (L2-resident).
     // Stage B, one thread per candidate: ordered sums (heads, then tokens).
     // Scratch for stage A: the per-block arrays WS and TS (2 * nb_cap floats).
     float* escore = cand_exact;  // [kSfCandCap] (fallback: SF, sized nb)
     float* eterm = WS;           // scratch of cap_terms floats (spans WS and TS)
     const int cap_terms = 2 * max(p.nb_cap, kSfMinScratch);
-    constexpr int kRowsStaged = kSfStages * 128;
+    constexpr int kRowsStaged = kSelStage;
     const float l2e = __uint_as_float(0x3FB8AA3Bu);
-    const bool q_in_smem = n_pass == 1;
     const T* ckrows = reinterpret_cast<const T*>(sCK);
     // candidates per batch: staged key rows fit the CK ring, and one token's
     // G terms per candidate fit the scratch (cap_terms >= 2048 >= G * 16)
@@ -499,32 +584,22 @@ __global__ void __launch_bounds__(kSfThreads, 2)
       // token-aligned column chunks whose terms fit the scratch: nbat * cchunk <= cap_terms
       const int cchunk = min(ncols_total, cap_terms / nbat / G * G);
       __syncthreads();
-      for (int idx = threadIdx.x; idx < nbat * (D / 8); idx += kSfThreads) {
+      for (int idx = threadIdx.x; idx < nbat * (D / 8); idx += kSelThreads) {
         const int ci = idx / (D / 8), v = idx % (D / 8);
         const int b = fallback ? (c0 + ci) : cand[c0 + ci];
         reinterpret_cast<uint4*>(sCK)[ci * (D / 8) + v] = reinterpret_cast<const uint4*>(
             static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D)[v];
       }
-      for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) (fallback ? SF[c0 + ci] : escore[c0 + ci]) = 0.f;
+      for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads) (fallback ? SF[c0 + ci] : escore[c0 + ci]) = 0.f;
       for (int cc0 = 0; cc0 < ncols_total; cc0 += cchunk) {
         const int nc = min(cchunk, ncols_total - cc0);
         __syncthreads();
-        for (int idx = threadIdx.x; idx < nbat * nc; idx += kSfThreads) {
+        for (int idx = threadIdx.x; idx < nbat * nc; idx += kSelThreads) {
           const int ci = idx / nc, col = cc0 + idx % nc;
           const int tok = r0 + col / G, g = col % G;
           const T* kr = ckrows + (size_t)ci * D;
           float dot = 0.f;
-          if (q_in_smem) {
-#pragma unroll
-            for (int c8 = 0; c8 < D / 8; ++c8) {
-              const uint4 qu = *reinterpret_cast<const uint4*>(sQ + swz_offset<RB>(col, c8));
-              const uint4 ku = *reinterpret_cast<const uint4*>(kr + c8 * 8);
-              const T* qe = reinterpret_cast<const T*>(&qu);
-              const T* ke = reinterpret_cast<const T*>(&ku);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) dot = __fadd_rn(dot, __fmul_rn((float)qe[i], (float)ke[i]));
-            }
-          } else {
+          {
             const uint4* qr = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
                                                              (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D);
 #pragma unroll
@@ -537,13 +612,12 @@ __global__ void __launch_bounds__(kSfThreads, 2)
               for (int i = 0; i < 8; ++i) dot = __fadd_rn(dot, __fmul_rn((float)qe[i], (float)ke[i]));
             }
           }
-          const float lse2 =
-              q_in_smem ? col_lse2[col] : __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
+          const float lse2 = __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
           eterm[idx] = exp2_fixed(__fsub_rn(__fmul_rn(dot, p.qk_scale), lse2));
         }
         __syncthreads();
         // ordered sums continue across chunks: heads of a token, then tokens
-        for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads) {
+        for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads) {
           const float* e = eterm + (size_t)ci * nc;
           float& run = fallback ? SF[c0 + ci] : escore[c0 + ci];
           float agg = run;
@@ -562,7 +636,7 @@ __global__ void __launch_bounds__(kSfThreads, 2)
       }
       if (fallback) {
         __syncthreads();
-        for (int ci = threadIdx.x; ci < nbat; ci += kSfThreads)
+        for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads)
           if (c0 + ci == self) SF[c0 + ci] = -INFINITY;
       }
     }
@@ -592,7 +666,7 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   } else {
     // an ambiguous candidate is chosen when fewer than `slots` of them beat
     // it; the order of `chosen` does not matter (the output is sorted by id)
-    for (int i = threadIdx.x; i < n_cand; i += kSfThreads) {
+    for (int i = threadIdx.x; i < n_cand; i += kSelThreads) {
       bool take = slots > 0 && n_cand <= slots;
       if (!take && slots > 0) {
         const float v = cand_exact[i];
@@ -618,7 +692,7 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   __syncthreads();
   const int n_ch = s_misc[2];
   int32_t* dst = p.out + ((size_t)h * gridDim.x + qb) * p.topk;
-  for (int i = threadIdx.x; i < p.topk; i += kSfThreads) {
+  for (int i = threadIdx.x; i < p.topk; i += kSelThreads) {
     if (i < n_ch) {
       const int id = chosen[i];
       int rank = 0;
@@ -631,33 +705,80 @@ __global__ void __launch_bounds__(kSfThreads, 2)
 }
 
 template <int D, bool BF16>
-static int launch_fast_t(const CUtensorMap& mq, const CUtensorMap& mck, const FastScoreParams& p, int nqb, int hkv,
-                         size_t smem, cudaStream_t s) {
-  LSRM_CUDA_TRY(cudaFuncSetAttribute(qblock_topk_fast_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem));
-  ProfScope ps("block_topk_fast", s);
-  qblock_topk_fast_kernel<D, BF16><<<dim3(nqb, hkv), kSfThreads, smem, s>>>(mq, mck, p);
-  LSRM_LAUNCH_CHECK();
+static int launch_fast_t(const CUtensorMap& mq, const CUtensorMap& mck, const FastScoreParams& p, int hkv,
+                         size_t smem_scores, size_t smem_select, long long ck_stride, cudaStream_t s) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  {
+    ProfScope ps("block_topk_norms", s);
+    const long long n = (long long)p.nb_total * hkv;
+    ck_norms_kernel<T, D><<<(int)((n + 255) / 256), 256, 0, s>>>(static_cast<const T*>(p.ck), ck_stride, hkv,
+                                                                 p.nb_total, const_cast<float*>(p.ckn));
+    LSRM_LAUNCH_CHECK();
+  }
+  LSRM_CUDA_TRY(cudaFuncSetAttribute(qblock_scores_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_scores));
+  {
+    ProfScope ps("block_topk_fast", s);
+    qblock_scores_kernel<D, BF16><<<dim3(p.nqb, hkv), kSfThreads, smem_scores, s>>>(mq, mck, p);
+    LSRM_LAUNCH_CHECK();
+  }
+  if (smem_select > 48 * 1024)
+    LSRM_CUDA_TRY(cudaFuncSetAttribute(qblock_select_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem_select));
+  {
+    ProfScope ps("block_topk_select", s);
+    qblock_select_kernel<D, BF16><<<dim3(p.nqb, hkv), kSelThreads, smem_select, s>>>(p);
+    LSRM_LAUNCH_CHECK();
+  }
   return LSRM_OK;
+}
+
+// Shared-memory sizes of the fast path's two kernels, 0 when it does not fit
+// (the exact scorer then serves the call).
+static void fast_smem(int D, int G, int nb_cap, size_t* scores, size_t* select) {
+  *scores = D == 64 ? SfLayout<64>::bytes(nb_cap) : D == 32 ? SfLayout<32>::bytes(nb_cap) : SfLayout<16>::bytes(nb_cap);
+  *select = D == 64 ? SelLayout<64>::bytes(nb_cap) : D == 32 ? SelLayout<32>::bytes(nb_cap)
+                                                             : SelLayout<16>::bytes(nb_cap);
+  if (G > kSfCols || *scores > 220 * 1024 || *select > 220 * 1024) *scores = *select = 0;
+}
+
+// Workspace of the fast path: the key norms and the per-(query block, kv
+// head) score bounds; 0 when the fast path does not serve the problem.
+size_t fast_scorer_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int num_query_blocks) {
+  if (num_query_blocks <= 0 || !meta || !shape || shape->num_kv_heads <= 0) return 0;
+  const int G = shape->num_q_heads / shape->num_kv_heads;
+  const int nb_cap = std::max(meta->num_blocks, 1);
+  size_t a, b;
+  fast_smem(shape->head_dim, G, nb_cap, &a, &b);
+  if (!a) return 0;
+  const size_t hkv = (size_t)shape->num_kv_heads;
+  return align_up(4 * hkv * nb_cap, 256) + align_up(8 * hkv * (size_t)num_query_blocks * nb_cap, 256);
 }
 
 // Returns LSRM_ERR_UNSUPPORTED (without launching) when the problem does not
 // fit the fast path; the caller then uses the exact scorer.
 int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
                             const float* lse_ln, int topk, const int32_t* cu_query_blocks, int num_query_blocks,
-                            int force_self, double qk_scale, int32_t* out, int* err, cudaStream_t s) {
+                            int force_self, double qk_scale, int32_t* out, void* workspace, size_t workspace_bytes,
+                            int* err, cudaStream_t s) {
   const int D = shape->head_dim;
   const int G = shape->num_q_heads / shape->num_kv_heads;
-  if (G > kSfCols) return LSRM_ERR_UNSUPPORTED;
   const int nb_cap = std::max(meta->num_blocks, 1);
-  size_t smem = D == 64 ? SfLayout<64>::bytes(nb_cap) : D == 32 ? SfLayout<32>::bytes(nb_cap) : SfLayout<16>::bytes(nb_cap);
-  if (smem > 220 * 1024) return LSRM_ERR_UNSUPPORTED;
-  // 256 TMEM columns per CTA: two CTAs may share an SM (their 512 columns fit)
+  size_t smem_scores, smem_select;
+  fast_smem(D, G, nb_cap, &smem_scores, &smem_select);
+  if (!smem_scores) return LSRM_ERR_UNSUPPORTED;
+  const size_t need = fast_scorer_workspace_bytes(meta, shape, num_query_blocks);
+  if (!workspace || workspace_bytes < need) {
+    set_error("block_topk: workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    return LSRM_ERR_WORKSPACE;
+  }
+  // 256 TMEM columns per scores CTA: two CTAs may share an SM (their 512 columns fit)
   CUtensorMap mq, mck;
   int rc;
   if ((rc = make_tmap_3d(&mq, q, D, shape->num_q_heads, meta->total_q, shape->q_token_stride, G, kSfCols / G)))
     return rc;
   if ((rc = make_tmap_3d(&mck, ck, D, shape->num_kv_heads, meta->num_blocks, shape->kv_token_stride, 1, 128))) return rc;
+  const size_t hkv = (size_t)shape->num_kv_heads;
   FastScoreParams p{};
   p.q = q;
   p.ck = ck;
@@ -674,15 +795,22 @@ int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shap
   p.topk = topk;
   p.force_self = force_self;
   p.nb_cap = nb_cap;
+  p.nb_total = meta->num_blocks;
+  p.nqb = num_query_blocks;
+  p.ckn = static_cast<const float*>(workspace);
+  p.bounds = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align_up(4 * hkv * nb_cap, 256));
   p.qk_scale = (float)qk_scale;
   p.err = err;
   const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
-  if (D == 64) return bf16 ? launch_fast_t<64, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
-                           : launch_fast_t<64, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
-  if (D == 32) return bf16 ? launch_fast_t<32, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
-                           : launch_fast_t<32, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
-  return bf16 ? launch_fast_t<16, true>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s)
-              : launch_fast_t<16, false>(mq, mck, p, num_query_blocks, shape->num_kv_heads, smem, s);
+  const long long cks = shape->kv_token_stride;
+  if (D == 64)
+    return bf16 ? launch_fast_t<64, true>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s)
+                : launch_fast_t<64, false>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s);
+  if (D == 32)
+    return bf16 ? launch_fast_t<32, true>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s)
+                : launch_fast_t<32, false>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s);
+  return bf16 ? launch_fast_t<16, true>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s)
+              : launch_fast_t<16, false>(mq, mck, p, (int)hkv, smem_scores, smem_select, cks, s);
 }
 
 }  // namespace lsrm

@@ -27,7 +27,9 @@ namespace lsrm {
 
 int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
                             const float* lse_ln, int topk, const int32_t* cu_query_blocks, int num_query_blocks,
-                            int force_self, double qk_scale, int32_t* out, int* err, cudaStream_t s);
+                            int force_self, double qk_scale, int32_t* out, void* workspace, size_t workspace_bytes,
+                            int* err, cudaStream_t s);
+size_t fast_scorer_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int num_query_blocks);
 
 struct ScoreParams {
   const void* q;
@@ -209,10 +211,17 @@ static int launch_topk_t(const ScoreParams& p, int rows, int hkv, size_t smem, c
 
 using namespace lsrm;
 
+extern "C" size_t lsrm_block_topk_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape,
+                                                  int32_t topk, int32_t num_query_blocks) {
+  int G = 1;
+  if (check_shape(meta, shape, G) || topk < 1 || topk > 64) return 0;
+  return fast_scorer_workspace_bytes(meta, shape, num_query_blocks);
+}
+
 extern "C" int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q, const void* ck,
                                const float* lse_ln, int32_t topk, const int32_t* cu_query_blocks,
                                int32_t num_query_blocks, int32_t force_self, double sm_scale, int32_t* block_topk,
-                               int* err_flags, void* stream) {
+                               void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
   int G = 1, rc;
   if ((rc = check_shape(meta, shape, G))) return rc;
   LSRM_CHECK_ARG(topk >= 1 && topk <= 64, "topk must be in [1, 64] (got %d)", topk);
@@ -247,7 +256,7 @@ extern "C" int lsrm_block_topk(const lsrm_varlen* meta, const lsrm_attn_shape* s
   if (num_query_blocks > 0 && !(mode && strcmp(mode, "exact") == 0)) {
     int* err = err_flags;
     rc = launch_qblock_topk_fast(meta, shape, q, ck, lse_ln, topk, cu_query_blocks, num_query_blocks, force_self,
-                                 scale * 1.44269504, block_topk, err, s);
+                                 scale * 1.44269504, block_topk, workspace, workspace_bytes, err, s);
     if (rc != LSRM_ERR_UNSUPPORTED) return rc;
   }
   const size_t nb_cap = ((size_t)std::max(meta->num_blocks, 1) + 3) & ~size_t(3);

@@ -90,10 +90,11 @@ _SIGS = {
         [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "lsrm_block_topk_workspace_bytes": (c_size_t, [c_void_p, c_void_p, c_int32, c_int32]),
     "lsrm_block_topk": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, ctypes.c_double,
-         c_void_p, c_void_p, c_void_p],
+         c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
     "lsrm_block_mean_fwd": (c_int, [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "lsrm_block_mean_bwd": (c_int, [c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),

@@ -238,9 +238,11 @@ def block_topk(q, ck, lse_ln, topk: int, meta: Meta, cu_query_blocks=None, force
     out = torch.empty(ck.shape[1], rows, topk, dtype=torch.int32, device=q.device)
     cqb = _i32(cu_query_blocks) if cu_query_blocks is not None else None
     lse_ln = lse_ln.float().contiguous()
+    nbytes = L.lsrm_block_topk_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), int(topk), nqb)
+    ws = _workspace(nbytes, q.device) if nbytes else None
     rc = L.lsrm_block_topk(ctypes.byref(vl), ctypes.byref(sh), _ptr(q), _ptr(ck), _ptr(lse_ln), int(topk), _ptr(cqb),
-                           nqb, int(bool(force_self)), float(sm_scale) if sm_scale else 0.0, _ptr(out),
-                           _ptr(_err_word(q.device)), _stream())
+                           nqb, int(bool(force_self)), float(sm_scale) if sm_scale else 0.0, _ptr(out), _ptr(ws),
+                           int(nbytes), _ptr(_err_word(q.device)), _stream())
     check(rc, "lsrm_block_topk")
     return out
 

@@ -189,3 +189,19 @@ def test_new_entry_points_reject_bad_arguments_on_host(lib):
     # misaligned coordinates
     assert h.lsrm_image_sort_keys(10, ctypes.c_void_p(20), 2, 16, 4, p, None) == bad
     assert "aligned" in h.lsrm_last_error().decode()
+
+
+def test_block_topk_workspace_query_and_host_rejection(lib):
+    """The per-query-block scorer needs a workspace (key norms and score
+    bounds), the per-token scorer none; a call with a short workspace is
+    rejected on the host before anything runs."""
+    h = lib.lib()
+    meta, shape = _meta(4096, 64), _shape(Hq=8, Hkv=8)
+    per_qb = h.lsrm_block_topk_workspace_bytes(ctypes.byref(meta), ctypes.byref(shape), 8, 64)
+    assert per_qb >= 8 * 64 * 64 * 2 * 4  # [Hkv, nqb, 2, blocks] fp32 bounds at least
+    assert h.lsrm_block_topk_workspace_bytes(ctypes.byref(meta), ctypes.byref(shape), 8, 0) == 0
+    assert h.lsrm_block_topk_workspace_bytes(ctypes.byref(meta), ctypes.byref(_shape(D=48)), 8, 64) == 0
+    p = ctypes.c_void_p(256)
+    rc = h.lsrm_block_topk(ctypes.byref(meta), ctypes.byref(shape), p, p, p, 8, p, 64, 1, 0.0, p, p, 1024, p, None)
+    assert rc == _header_define("LSRM_ERR_WORKSPACE")
+    assert "workspace" in h.lsrm_last_error().decode()
