@@ -100,29 +100,49 @@ constexpr int kTilesSeqCompressedKV = 5;
 __global__ void build_tiles_kernel(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int rows_per_tile,
                                    lsrm_varlen m, const int32_t* cu_seg, int n_seg, int window, int* err) {
   __shared__ int scratch[40];
+  __shared__ int s_off[1024], s_cnt[1024];  // the chunk's segments: first tile (chunk-relative), tile count
   int base = 0;
   const int half = window / 2;
+  const int k = (kind == kTilesSeqCompressedKV) ? kTilesSeq : kind;
+  auto seg = [&](int i, int& row_lo, int& row_hi, int& oth_lo, int& oth_hi, int& sq, int& sel_row) {
+    segment_info(k, i, m, cu_seg, window, row_lo, row_hi, oth_lo, oth_hi, sq, sel_row);
+    if (kind == kTilesSeqCompressedKV) {
+      oth_lo = m.cu_seqblocks[i];
+      oth_hi = m.cu_seqblocks[i + 1];
+    }
+  };
   for (int c0 = 0; c0 < n_seg; c0 += blockDim.x) {
     const int i = c0 + threadIdx.x;
-    int row_lo = 0, row_hi = 0, oth_lo = 0, oth_hi = 0, seq = 0, sel_row = -1;
     int cnt = 0;
     if (i < n_seg) {
-      const int k = (kind == kTilesSeqCompressedKV) ? kTilesSeq : kind;
-      segment_info(k, i, m, cu_seg, window, row_lo, row_hi, oth_lo, oth_hi, seq, sel_row);
-      if (kind == kTilesSeqCompressedKV) {
-        oth_lo = m.cu_seqblocks[i];
-        oth_hi = m.cu_seqblocks[i + 1];
-      }
+      int row_lo, row_hi, oth_lo, oth_hi, sq, sel_row;
+      seg(i, row_lo, row_hi, oth_lo, oth_hi, sq, sel_row);
       if (row_hi > row_lo) cnt = (row_hi - row_lo + rows_per_tile - 1) / rows_per_tile;
     }
     int total;
-    const int off = base + block_exclusive_scan(cnt, &total, scratch);
-    for (int t = 0; t < cnt; ++t) {
-      const int idx = off + t;
+    const int off = block_exclusive_scan(cnt, &total, scratch);
+    s_off[threadIdx.x] = off;
+    s_cnt[threadIdx.x] = cnt;
+    __syncthreads();
+    // the chunk's tiles, one thread each: segment by binary search of the offsets
+    const int nseg_chunk = min((int)blockDim.x, n_seg - c0);
+    for (int t_all = threadIdx.x; t_all < total; t_all += blockDim.x) {
+      // the last segment whose first tile is <= t_all; an empty segment shares
+      // its offset with the next one, so the last such segment holds t_all
+      int lo = 0, hi = nseg_chunk - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_off[mid] <= t_all) lo = mid;
+        else hi = mid - 1;
+      }
+      const int idx = base + t_all;
       if (idx >= tiles_ub) {
         atomicOr(err, LSRM_ERR_CAPACITY);
-        break;
+        continue;
       }
+      const int si = c0 + lo, t = t_all - s_off[lo];
+      int row_lo, row_hi, oth_lo, oth_hi, sq, sel_row;
+      seg(si, row_lo, row_hi, oth_lo, oth_hi, sq, sel_row);
       QTile q;
       q.q_start = row_lo + t * rows_per_tile;
       q.n_q = min(rows_per_tile, row_hi - q.q_start);
@@ -133,13 +153,14 @@ __global__ void build_tiles_kernel(QTile* tiles, int* n_tiles, int tiles_ub, int
         q.kv_lo = max(oth_lo, q.q_start - half);
         q.kv_hi = min(oth_hi, q.q_start + q.n_q + half);
       }
-      q.seq = seq;
+      q.seq = sq;
       q.sel_row = sel_row;
-      q.seg = i;
+      q.seg = si;
       q.pad = 0;
       tiles[idx] = q;
     }
     base += total;
+    __syncthreads();  // s_off / s_cnt are rewritten by the next chunk
   }
   if (threadIdx.x == 0) *n_tiles = min(base, tiles_ub);
 }

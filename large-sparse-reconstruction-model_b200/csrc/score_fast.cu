@@ -38,6 +38,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <climits>
 #include <cmath>
 
 #include "attn_host.h"
@@ -51,8 +52,6 @@ constexpr int kSfThreads = 320;
 constexpr int kSfReduceThreads = 256;
 constexpr int kSfCols = 128;  // query rows per pass: 2 x 128 TMEM columns, so two CTAs share an SM
 constexpr int kSfStages = 3;
-constexpr int kSfCandCap = 1024;
-constexpr int kSfMinScratch = 1024;  // exact-stage terms: >= 2048 floats, more than one token's G <= 256 heads
 
 struct FastScoreParams {
   const void* q;
@@ -72,6 +71,7 @@ struct FastScoreParams {
   int nb_cap;      // blocks per sequence the bound slices and shared arrays hold
   int nb_total;    // compressed blocks of all sequences (the norm table's row length)
   int nqb;         // query blocks
+  int hkv;         // kv heads
   const float* ckn;  // [Hkv, nb_total] norms of the compressed keys
   float* bounds;     // [Hkv, nqb, 2, nb_cap] lower / upper score bounds
   float qk_scale;
@@ -86,33 +86,20 @@ struct SfLayout {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_CK = QT;
   static constexpr int OFF_COLS = OFF_CK + kSfStages * CKT;  // lse2[128], qn[128], the pass's max |q|, max |lse2|
-  static constexpr int OFF_PART = OFF_COLS + 2 * kSfCols * 4 + 16;  // [2][128][3]
-  static constexpr int OFF_BAR = OFF_PART + 2 * 128 * 3 * 4;
+  static constexpr int OFF_BAR = OFF_COLS + 2 * kSfCols * 4 + 16;
   static constexpr int NBAR = 2 * kSfStages + 2 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_ARR = OFF_MISC + 64;
-  // per-block arrays: fast score SF, |q|-weighted sum WS and t-term sum TS [nb_cap each]
-  static size_t bytes(int nb_cap) { return (size_t)OFF_ARR + 12ull * nb_cap + 1024; }
+  // per-block arrays, one per column half: fast score SF, |q|-weighted sum WS
+  // and t-term sum TS [2][nb_cap each]
+  static size_t bytes(int nb_cap) { return (size_t)OFF_ARR + 24ull * nb_cap + 1024; }
 };
 
-constexpr int kSelThreads = 256;
-constexpr int kSelStage = 128;  // candidate key rows staged per batch of the exact stage
-
-template <int D>
-struct SelLayout {
-  static constexpr int RB = 2 * D;
-  static constexpr int OFF_CK = 0;                          // staged candidate key rows [kSelStage][D]
-  static constexpr int OFF_MISC = OFF_CK + kSelStage * RB;  // counters, radix-select scratch
-  static constexpr int OFF_CAND = OFF_MISC + 64;            // cand ids [cap], exact [cap], chosen[64]
-  static constexpr int OFF_HIST = OFF_CAND + kSfCandCap * 8 + 64 * 4;  // radix-select histogram [256]
-  static constexpr int OFF_ARR = OFF_HIST + 256 * 4;
-  // SF [nb_cap] (the fallback's exact scores), then the lower / upper bounds
-  // WS / TS [nb_cap each] inside a scratch of 2 * max(nb_cap, kSfMinScratch)
-  // floats that the exact stage reuses for its terms
-  static size_t bytes(int nb_cap) {
-    return (size_t)OFF_ARR + 4ull * nb_cap + 8ull * (size_t)(nb_cap > kSfMinScratch ? nb_cap : kSfMinScratch) + 128;
-  }
-};
+constexpr int kSelThreads = 256;  // 8 warps, one (query block, kv head) item each
+constexpr int kSelCandCap = 256;  // ambiguous candidates held per item (more: exact scores of every block)
+constexpr int kSelBatch = 8;      // candidates whose exact terms are computed together
+constexpr int kSelTerms = 512;    // exact-stage terms held per warp
+constexpr int kSelUnroll = 8;     // bound loads per lane in flight in the selects and the candidate sweep
 
 // |ck| of every (compressed block, kv head), fp32 (exact conversion of the
 // 16-bit values, fused multiply-add accumulation).
@@ -250,7 +237,6 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   uint8_t* sCK = smem + L::OFF_CK;
   float* col_lse2 = reinterpret_cast<float*>(smem + L::OFF_COLS);
   float* col_qn = col_lse2 + kSfCols;
-  float* part = reinterpret_cast<float*>(smem + L::OFF_PART);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* ck_full = bars;
   uint64_t* ck_empty = bars + kSfStages;
@@ -261,15 +247,15 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   uint64_t* mma_done = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
-  float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);
-  float* WS = SF + p.nb_cap;
-  float* TS = WS + p.nb_cap;
+  float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);  // [2][nb_cap]: the two column halves' sums
+  float* WS = SF + 2 * p.nb_cap;
+  float* TS = WS + 2 * p.nb_cap;
 
   if (nb > p.nb_cap) {  // the host sizes nb_cap from the total block count
     if (threadIdx.x == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
     return;
   }
-  for (int b = threadIdx.x; b < nb; b += kSfThreads) {
+  for (int b = threadIdx.x; b < 2 * p.nb_cap; b += kSfThreads) {
     SF[b] = 0.f;
     WS[b] = 0.f;
     TS[b] = 0.f;
@@ -410,22 +396,16 @@ __global__ void __launch_bounds__(kSfThreads, 2)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
-        float* pt = part + (size_t)sb * 128 * 3;
-        if (half == 1) {
-          pt[row * 3 + 0] = acc_e;
-          pt[row * 3 + 1] = acc_te;
-          pt[row * 3 + 2] = tmax;
-        }
-        reduce_bar();
+        // each half keeps its own sums (no exchange per chunk): the bound of a
+        // block is the sum of the halves' bounds
         const int b = c * 128 + row;
-        if (half == 0 && b < nb) {
-          const float se = acc_e + pt[row * 3 + 0];
-          const float ste = acc_te + pt[row * 3 + 1];
-          const float tm = fmaxf(fmaxf(tmax, pt[row * 3 + 2]), 0.f);
-          SF[b] += se;
-          WS[b] += qmax * se;  // >= sum e |q|
+        if (b < nb) {
+          const size_t hb = (size_t)half * p.nb_cap + b;
+          const float tm = fmaxf(tmax, 0.f);
+          SF[hb] += acc_e;
+          WS[hb] += qmax * acc_e;  // >= sum e |q|
           // >= sum e (2|t| + 2|lse2| + 1)
-          TS[b] += 2.f * (fmaxf(-ste, 0.f) + 2.f * tm * se) + (2.f * l2max + 1.f) * se;
+          TS[hb] += 2.f * (fmaxf(-acc_te, 0.f) + 2.f * tm * acc_e) + (2.f * l2max + 1.f) * acc_e;
         }
       }
     }
@@ -458,8 +438,9 @@ __global__ void __launch_bounds__(kSfThreads, 2)
   float* Ug = Lg + p.nb_cap;
   for (int b = threadIdx.x; b < nb; b += kSfThreads) {
     const float ckn = p.ckn[(size_t)h * p.nb_total + blk0 + b];
-    const float sf = SF[b];
-    const float e = 2.f * (0.7f * (sl2 * 0x1p-16f * ckn * WS[b] + 0x1p-20f * TS[b]) +
+    const float sf = SF[b] + SF[p.nb_cap + b];
+    const float ws = WS[b] + WS[p.nb_cap + b], ts = TS[b] + TS[p.nb_cap + b];
+    const float e = 2.f * (0.7f * (sl2 * 0x1p-16f * ckn * ws + 0x1p-20f * ts) +
                            (0x1p-19f + (n_f + 1.f) * 0x1p-22f) * sf + n_f * 0x1p-120f);
     Lg[b] = (b == self) ? -INFINITY : sf - e;
     Ug[b] = (b == self) ? -INFINITY : sf + e;
@@ -467,15 +448,172 @@ __global__ void __launch_bounds__(kSfThreads, 2)
 }
 
 // Selection of one (query block, kv head) from its certified bounds (see the
-// top of this file): thresholds by exact radix selects, certainly chosen
-// blocks directly, the ambiguous ones by the exact fixed-order score.  No
-// tensor cores and small shared memory, so several CTAs share an SM and hide
-// the latency of the bound and query-row loads.
+// top of this file), one warp per item and eight items per CTA: thresholds by
+// warp-level exact radix selects over the bounds (read from L2, no block-wide
+// barriers), certainly chosen blocks directly, the ambiguous ones by the exact
+// fixed-order score.  Small per-warp shared memory, so many items share an SM
+// and hide the latency of the bound and query-row loads.
+template <int D>
+struct SelWarpMem {
+  uint32_t hist[256];               // radix-select histogram
+  int cand[kSelCandCap];            // ambiguous candidates
+  float cand_exact[kSelCandCap];    // their exact scores
+  int chosen[64];
+  float terms[kSelTerms];           // exact-stage terms of a candidate batch
+  uint16_t ckrow[kSelBatch][D];     // the batch's compressed key rows
+  int misc[8];
+};
+
+// The k-th largest (1 <= k <= n) of vals[0..n), exactly, by an MSB-first
+// 8-bit radix select; warp-wide (no block barriers).
+__device__ float warp_kth_largest(const float* __restrict__ vals, int n, int k, uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0u, mask = 0u;
+  int kk = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) hist[i] = 0u;
+    __syncwarp();
+    for (int b0 = 0; b0 < n; b0 += 32 * kSelUnroll) {
+      float v[kSelUnroll];  // the loads of several rounds in flight at once
+#pragma unroll
+      for (int j = 0; j < kSelUnroll; ++j) {
+        const int b = b0 + 32 * j + lane;
+        v[j] = b < n ? vals[b] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kSelUnroll; ++j) {
+        const int b = b0 + 32 * j + lane;
+        const uint32_t key = b < n ? desc_key(v[j]) : 0u;
+        const bool m = b < n && (key & mask) == prefix;
+        const uint32_t bin = m ? ((key >> shift) & 255u) : 256u + lane;
+        const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+        if (m && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+      }
+    }
+    __syncwarp();
+    uint32_t c[8], tot = 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      c[i] = hist[lane * 8 + i];
+      tot += c[i];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - tot;
+    int d = -1, rem = 0;
+    if (excl < (uint32_t)kk && (uint32_t)kk <= incl) {
+      uint32_t run = excl;
+      d = lane * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (run + c[i] >= (uint32_t)kk) {
+          d = lane * 8 + i;
+          break;
+        }
+        run += c[i];
+      }
+      rem = kk - (int)run;
+    }
+    const uint32_t who = __ballot_sync(0xffffffffu, d >= 0);
+    const int src = __ffs(who) - 1;
+    d = __shfl_sync(0xffffffffu, d, src);
+    kk = __shfl_sync(0xffffffffu, rem, src);
+    prefix |= (uint32_t)d << shift;
+    mask |= 255u << shift;
+    __syncwarp();
+  }
+  const uint32_t asc = ~prefix;
+  return __uint_as_float((asc & 0x80000000u) ? (asc & 0x7fffffffu) : ~asc);
+}
+
+// Exact fixed-order scores of blocks ids[0..n) of one (query block, kv
+// head): sum over the block's tokens in ascending order of (sum over the G
+// heads in order of exp2_fixed(dot * qk_scale - lse2)), the dot product over
+// channels 0..D-1 with separately rounded multiply and add.  Warp-wide;
+// results in out[0..n).
+template <int D, typename T>
+__device__ void warp_exact_scores(const FastScoreParams& p, SelWarpMem<D>& wm, const int* ids, int n, int blk0,
+                                  int h, int r0, int ncols_total, float* out) {
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+  const float l2e = __uint_as_float(0x3FB8AA3Bu);
+  const int bat = max(1, min(kSelBatch, kSelTerms / G));  // nbat * G <= kSelTerms (G <= 128)
+  for (int c0 = 0; c0 < n; c0 += bat) {
+    const int nbat = min(bat, n - c0);
+    __syncwarp();
+    for (int idx = lane; idx < nbat * (D / 8); idx += 32) {
+      const int ci = idx / (D / 8), v = idx % (D / 8);
+      reinterpret_cast<uint4*>(wm.ckrow[ci])[v] = reinterpret_cast<const uint4*>(
+          static_cast<const T*>(p.ck) + (size_t)(blk0 + ids[c0 + ci]) * p.ck_tok_stride + (size_t)h * D)[v];
+    }
+    float run = 0.f;  // lane ci < nbat: candidate c0 + ci's ordered sum
+    // token-aligned column chunks whose terms fit the scratch
+    const int cchunk = max(G, kSelTerms / nbat / G * G);
+    for (int cc0 = 0; cc0 < ncols_total; cc0 += cchunk) {
+      const int nc = min(cchunk, ncols_total - cc0);
+      __syncwarp();
+      // lane = column: its query row is read once and serves every candidate
+      // of the batch (each dot still accumulates channels 0..D-1 in order)
+      for (int cl = lane; cl < nc; cl += 32) {
+        const int col = cc0 + cl;
+        const int tok = r0 + col / G, g = col % G;
+        const uint4* qr = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)tok * p.q_tok_stride +
+                                                         (size_t)(h * G + g) * D);
+        float dot[kSelBatch];
+#pragma unroll
+        for (int ci = 0; ci < kSelBatch; ++ci) dot[ci] = 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < D / 8; ++c8) {
+          const uint4 qu = qr[c8];
+          const T* qe = reinterpret_cast<const T*>(&qu);
+#pragma unroll
+          for (int ci = 0; ci < kSelBatch; ++ci) {
+            if (ci < nbat) {
+              const uint4 ku = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(wm.ckrow[ci]) + c8 * 8);
+              const T* ke = reinterpret_cast<const T*>(&ku);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dot[ci] = __fadd_rn(dot[ci], __fmul_rn((float)qe[i], (float)ke[i]));
+            }
+          }
+        }
+        const float lse2 = __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
+#pragma unroll
+        for (int ci = 0; ci < kSelBatch; ++ci)
+          if (ci < nbat) wm.terms[ci * nc + cl] = exp2_fixed(__fsub_rn(__fmul_rn(dot[ci], p.qk_scale), lse2));
+      }
+      __syncwarp();
+      if (lane < nbat) {
+        const float* e = wm.terms + (size_t)lane * nc;
+        if (G == 1) {
+          for (int t = 0; t < nc; ++t) run = __fadd_rn(run, __fadd_rn(0.f, e[t]));
+        } else {
+          for (int t = 0; t < nc / G; ++t) {
+            float st = 0.f;
+            for (int g = 0; g < G; ++g) st = __fadd_rn(st, e[t * G + g]);
+            run = __fadd_rn(run, st);
+          }
+        }
+      }
+    }
+    if (lane < nbat) out[c0 + lane] = run;
+  }
+  __syncwarp();
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kSelThreads, 4) qblock_select_kernel(const FastScoreParams p) {
-  using L = SelLayout<D>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  const int qb = blockIdx.x, h = blockIdx.y;
+  extern __shared__ uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  SelWarpMem<D>& wm = reinterpret_cast<SelWarpMem<D>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127))[warp];
+  const int item = blockIdx.x * (kSelThreads / 32) + warp;  // h * nqb + qb
+  if (item >= p.nqb * p.hkv) return;
+  const int h = item / p.nqb, qb = item - h * p.nqb;
   const int G = p.G;
   const int r0 = p.cu_qblocks[qb], r1 = p.cu_qblocks[qb + 1];
   int lo = 0, hi = p.num_seqs + 1;
@@ -488,27 +626,14 @@ __global__ void __launch_bounds__(kSelThreads, 4) qblock_select_kernel(const Fas
   const int blk0 = p.cu_cblocks[seq];
   const int nb = p.cu_cblocks[seq + 1] - blk0;
   const int ncols_total = max(r1 - r0, 0) * G;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  uint8_t* sCK = smem + L::OFF_CK;
-  int* s_misc = reinterpret_cast<int*>(smem + L::OFF_MISC);  // [0] n_cand [1] fallback [2] chosen [4..] select
-  int* cand = reinterpret_cast<int*>(smem + L::OFF_CAND);
-  float* cand_exact = reinterpret_cast<float*>(cand + kSfCandCap);
-  int* chosen = reinterpret_cast<int*>(cand_exact + kSfCandCap);
-  float* SF = reinterpret_cast<float*>(smem + L::OFF_ARR);  // the fallback's exact scores
-  float* WS = SF + p.nb_cap;                                  // lower bounds, then exact-stage scratch
-  float* TS = WS + p.nb_cap;                                  // upper bounds
+  int32_t* dst = p.out + ((size_t)h * p.nqb + qb) * p.topk;
   if (nb > p.nb_cap) {
-    if (threadIdx.x == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
+    if (lane == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
+    for (int i = lane; i < p.topk; i += 32) dst[i] = -1;
     return;
   }
-  const float* Lg = p.bounds + ((size_t)h * p.nqb + qb) * 2 * p.nb_cap;
+  float* Lg = p.bounds + ((size_t)h * p.nqb + qb) * 2 * p.nb_cap;  // the fallback overwrites it with exact scores
   const float* Ug = Lg + p.nb_cap;
-  for (int b = threadIdx.x; b < nb; b += kSelThreads) {
-    WS[b] = Lg[b];
-    TS[b] = Ug[b];
-  }
   const int kk = min(p.topk, nb);
   int self = -1;
   if (p.force_self && kk > 0) {
@@ -522,181 +647,134 @@ __global__ void __launch_bounds__(kSelThreads, 4) qblock_select_kernel(const Fas
     if (sidx >= 0 && sidx < nb) self = sidx;
   }
   const int kp = kk - (self >= 0 ? 1 : 0);
-  __syncthreads();
-  // thresholds (ties counted, exact radix selects): the kp-th largest lower
-  // bound, and the (kp+1)-th largest upper bound above which a block's lower
-  // bound makes it certainly chosen
   float thr = -INFINITY, thr_hi = -INFINITY;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L::OFF_HIST);
-  if (kp > 0) thr = kth_largest(WS, nb, kp, hist, s_misc + 4);
-  if (kp > 0 && kp < nb) thr_hi = kth_largest(TS, nb, kp + 1, hist, s_misc + 4);
-  // candidates (upper bound reaches thr): certainly chosen ones go straight to
-  // `chosen`, the ambiguous rest to `cand`
-  if (threadIdx.x == 0) {
-    s_misc[0] = 0;
-    s_misc[1] = 0;
-    s_misc[2] = 0;
-    if (self >= 0) chosen[s_misc[2]++] = self;
-  }
-  __syncthreads();
+  if (kp > 0) thr = warp_kth_largest(Lg, nb, kp, wm.hist);
+  if (kp > 0 && kp < nb) thr_hi = warp_kth_largest(Ug, nb, kp + 1, wm.hist);
+  // candidates whose upper bound reaches thr: certainly chosen ones straight
+  // to `chosen`, the ambiguous rest to `cand` (warp-aggregated appends)
+  int n_ch = 0, n_cand = 0;
+  bool overflow = false;
+  if (self >= 0 && lane == 0) wm.chosen[0] = self;
+  n_ch = self >= 0 ? 1 : 0;
   if (kp > 0) {
-    for (int b = threadIdx.x; b < nb; b += kSelThreads) {
-      if (b != self && TS[b] >= thr) {
-        if (WS[b] > thr_hi) {
-          const int slot = atomicAdd(&s_misc[2], 1);
-          if (slot < 64) chosen[slot] = b;
-        } else {
-          const int slot = atomicAdd(&s_misc[0], 1);
-          if (slot < kSfCandCap) cand[slot] = b;
-          else s_misc[1] = 1;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  const int n_cand_raw = s_misc[0];
-  const bool fallback = s_misc[1] != 0;
-  // places left for the ambiguous candidates
-  const int slots = kp - (s_misc[2] - (self >= 0 ? 1 : 0));
-  __syncthreads();
-  // Exact scores of the candidates (every block on the fallback path):
-  // stage A, all threads: per (candidate, column) the fixed-order score term;
-  // stage B, one thread per candidate: ordered sums (heads, then tokens).
-  // Scratch for stage A: the per-block arrays (3 * nb_cap floats).
-  const int n_exact = fallback ? nb : (n_cand_raw > slots && slots > 0 ? n_cand_raw : 0);
-  if (n_exact > 0) {
-    // Stage A, all threads: per (candidate, column) the fixed-order score
-    // term, from the candidates' key rows staged in shared memory and the
-    // query block's rows read from global memory (L2-resident).
-    // Stage B, one thread per candidate: ordered sums (heads, then tokens).
-    // Scratch for stage A: the per-block arrays WS and TS (2 * nb_cap floats).
-    float* escore = cand_exact;  // [kSfCandCap] (fallback: SF, sized nb)
-    float* eterm = WS;           // scratch of cap_terms floats (spans WS and TS)
-    const int cap_terms = 2 * max(p.nb_cap, kSfMinScratch);
-    constexpr int kRowsStaged = kSelStage;
-    const float l2e = __uint_as_float(0x3FB8AA3Bu);
-    const T* ckrows = reinterpret_cast<const T*>(sCK);
-    // candidates per batch: staged key rows fit the CK ring, and one token's
-    // G terms per candidate fit the scratch (cap_terms >= 2048 >= G * 16)
-    const int nbat_max = min(kRowsStaged, cap_terms / G);
-    for (int c0 = 0; c0 < n_exact; c0 += nbat_max) {
-      const int nbat = min(nbat_max, n_exact - c0);
-      // token-aligned column chunks whose terms fit the scratch: nbat * cchunk <= cap_terms
-      const int cchunk = min(ncols_total, cap_terms / nbat / G * G);
-      __syncthreads();
-      for (int idx = threadIdx.x; idx < nbat * (D / 8); idx += kSelThreads) {
-        const int ci = idx / (D / 8), v = idx % (D / 8);
-        const int b = fallback ? (c0 + ci) : cand[c0 + ci];
-        reinterpret_cast<uint4*>(sCK)[ci * (D / 8) + v] = reinterpret_cast<const uint4*>(
-            static_cast<const T*>(p.ck) + (size_t)(blk0 + b) * p.ck_tok_stride + (size_t)h * D)[v];
-      }
-      for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads) (fallback ? SF[c0 + ci] : escore[c0 + ci]) = 0.f;
-      for (int cc0 = 0; cc0 < ncols_total; cc0 += cchunk) {
-        const int nc = min(cchunk, ncols_total - cc0);
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < nbat * nc; idx += kSelThreads) {
-          const int ci = idx / nc, col = cc0 + idx % nc;
-          const int tok = r0 + col / G, g = col % G;
-          const T* kr = ckrows + (size_t)ci * D;
-          float dot = 0.f;
-          {
-            const uint4* qr = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
-                                                             (size_t)tok * p.q_tok_stride + (size_t)(h * G + g) * D);
+    for (int b0 = 0; b0 < nb; b0 += 32 * kSelUnroll) {
+      float uv[kSelUnroll], lv[kSelUnroll];
 #pragma unroll
-            for (int c8 = 0; c8 < D / 8; ++c8) {
-              const uint4 qu = qr[c8];
-              const uint4 ku = *reinterpret_cast<const uint4*>(kr + c8 * 8);
-              const T* qe = reinterpret_cast<const T*>(&qu);
-              const T* ke = reinterpret_cast<const T*>(&ku);
+      for (int j = 0; j < kSelUnroll; ++j) {
+        const int b = b0 + 32 * j + lane;
+        uv[j] = b < nb ? Ug[b] : -INFINITY;
+        lv[j] = b < nb ? Lg[b] : -INFINITY;
+      }
 #pragma unroll
-              for (int i = 0; i < 8; ++i) dot = __fadd_rn(dot, __fmul_rn((float)qe[i], (float)ke[i]));
-            }
-          }
-          const float lse2 = __fmul_rn(p.lse[(size_t)(h * G + g) * p.total_q + tok], l2e);
-          eterm[idx] = exp2_fixed(__fsub_rn(__fmul_rn(dot, p.qk_scale), lse2));
-        }
-        __syncthreads();
-        // ordered sums continue across chunks: heads of a token, then tokens
-        for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads) {
-          const float* e = eterm + (size_t)ci * nc;
-          float& run = fallback ? SF[c0 + ci] : escore[c0 + ci];
-          float agg = run;
-          if (G == 1) {
-#pragma unroll 8
-            for (int t = 0; t < nc; ++t) agg = __fadd_rn(agg, __fadd_rn(0.f, e[t]));
-          } else {
-            for (int t = 0; t < nc / G; ++t) {
-              float st = 0.f;
-              for (int g = 0; g < G; ++g) st = __fadd_rn(st, e[t * G + g]);
-              agg = __fadd_rn(agg, st);
-            }
-          }
-          run = agg;
+      for (int j = 0; j < kSelUnroll; ++j) {
+      const int b = b0 + 32 * j + lane;
+      bool sure = false, amb = false;
+      if (b < nb && b != self) {
+        if (uv[j] >= thr) {
+          if (lv[j] > thr_hi) sure = true;
+          else amb = true;
         }
       }
-      if (fallback) {
-        __syncthreads();
-        for (int ci = threadIdx.x; ci < nbat; ci += kSelThreads)
-          if (c0 + ci == self) SF[c0 + ci] = -INFINITY;
+      const uint32_t ms = __ballot_sync(0xffffffffu, sure), ma = __ballot_sync(0xffffffffu, amb);
+      const uint32_t below = (1u << lane) - 1u;
+      if (sure) {
+        const int slot = n_ch + __popc(ms & below);
+        if (slot < 64) wm.chosen[slot] = b;
+      }
+      if (amb) {
+        const int slot = n_cand + __popc(ma & below);
+        if (slot < kSelCandCap) wm.cand[slot] = b;
+      }
+      n_ch += __popc(ms);
+      n_cand += __popc(ma);
       }
     }
-    __syncthreads();
+    overflow = n_cand > kSelCandCap;
   }
-  const int n_cand = n_cand_raw;
-  // choose: (exact desc, id asc) among the ambiguous candidates for the places
-  // left (or, on the fallback path, kp blocks among all blocks)
-  if (fallback) {
-    if (threadIdx.x == 0) {
-      int n_ch = 0;
-      if (self >= 0) chosen[n_ch++] = self;
-      for (int r = 0; r < kp; ++r) {
-        float bv = -INFINITY;
-        int bi = -1;
-        for (int b = 0; b < nb; ++b)  // ascending ids: ties keep the lowest id
-          if (SF[b] > bv) {
-            bv = SF[b];
-            bi = b;
-          }
-        if (bi < 0) break;
-        chosen[n_ch++] = bi;
-        SF[bi] = -INFINITY;
-      }
-      s_misc[2] = n_ch;
+  __syncwarp();
+  const int slots = kp - (n_ch - (self >= 0 ? 1 : 0));
+  if (overflow) {
+    // more ambiguous blocks than the list holds: exact scores of every block
+    // (in place of the lower bounds), then the kp best by (exact desc, id asc)
+    n_ch = self >= 0 ? 1 : 0;
+    for (int b0 = 0; b0 < nb; b0 += kSelCandCap) {
+      const int m = min(kSelCandCap, nb - b0);
+      for (int i = lane; i < m; i += 32) wm.cand[i] = b0 + i;
+      __syncwarp();
+      warp_exact_scores<D, T>(p, wm, wm.cand, m, blk0, h, r0, ncols_total, Lg + b0);
     }
-  } else {
-    // an ambiguous candidate is chosen when fewer than `slots` of them beat
-    // it; the order of `chosen` does not matter (the output is sorted by id)
-    for (int i = threadIdx.x; i < n_cand; i += kSelThreads) {
-      bool take = slots > 0 && n_cand <= slots;
-      if (!take && slots > 0) {
-        const float v = cand_exact[i];
-        const int id = cand[i];
-        int beat = 0;
-        for (int j = 0; j < n_cand; ++j) {
-          const float w = cand_exact[j];
-          beat += (w > v) || (w == v && cand[j] < id);
+    __syncwarp();
+    if (self >= 0 && lane == 0) Lg[self] = -INFINITY;
+    __syncwarp();
+    for (int r = 0; r < kp; ++r) {
+      float bv = -INFINITY;
+      int bi = INT_MAX;
+      for (int b = lane; b < nb; b += 32) {
+        const float v = Lg[b];
+        if (v > bv || (v == bv && b < bi)) {
+          bv = v;
+          bi = b;
         }
-        take = beat < slots;
       }
-      if (take) {
-        const int slot = atomicAdd(&s_misc[2], 1);
-        if (slot < 64) chosen[slot] = cand[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
       }
+      if (bi == INT_MAX || bv == -INFINITY) break;
+      if (lane == 0) {
+        wm.chosen[n_ch] = bi;
+        Lg[bi] = -INFINITY;
+      }
+      ++n_ch;
+      __syncwarp();
+    }
+  } else if (slots > 0 && n_cand > 0) {
+    if (n_cand <= slots) {
+      for (int i = lane; i < n_cand; i += 32)
+        if (n_ch + i < 64) wm.chosen[n_ch + i] = wm.cand[i];
+      n_ch += n_cand;
+    } else {
+      warp_exact_scores<D, T>(p, wm, wm.cand, n_cand, blk0, h, r0, ncols_total, wm.cand_exact);
+      // a candidate is chosen when fewer than `slots` of them beat it
+      int taken = 0;
+      for (int i0 = 0; i0 < n_cand; i0 += 32) {
+        const int i = i0 + lane;
+        bool take = false;
+        if (i < n_cand) {
+          const float v = wm.cand_exact[i];
+          const int id = wm.cand[i];
+          int beat = 0;
+          for (int j = 0; j < n_cand; ++j) {
+            const float w = wm.cand_exact[j];
+            beat += (w > v) || (w == v && wm.cand[j] < id);
+          }
+          take = beat < slots;
+        }
+        const uint32_t mt = __ballot_sync(0xffffffffu, take);
+        if (take) {
+          const int slot = n_ch + taken + __popc(mt & ((1u << lane) - 1u));
+          if (slot < 64) wm.chosen[slot] = wm.cand[i];
+        }
+        taken += __popc(mt);
+      }
+      n_ch += taken;
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0 && s_misc[2] > kk) {  // only reachable with non-finite scores
-    s_misc[2] = kk;
-    atomicOr(p.err, LSRM_ERR_CAPACITY);
+  __syncwarp();
+  if (n_ch > kk) {  // only reachable with non-finite scores
+    if (lane == 0) atomicOr(p.err, LSRM_ERR_CAPACITY);
+    n_ch = kk;
   }
-  __syncthreads();
-  const int n_ch = s_misc[2];
-  int32_t* dst = p.out + ((size_t)h * gridDim.x + qb) * p.topk;
-  for (int i = threadIdx.x; i < p.topk; i += kSelThreads) {
+  for (int i = lane; i < p.topk; i += 32) {
     if (i < n_ch) {
-      const int id = chosen[i];
+      const int id = wm.chosen[i];
       int rank = 0;
-      for (int j = 0; j < n_ch; ++j) rank += chosen[j] < id;
+      for (int j = 0; j < n_ch; ++j) rank += wm.chosen[j] < id;
       if (rank < p.topk) dst[rank] = id;
     } else {
       dst[i] = -1;
@@ -727,7 +805,8 @@ static int launch_fast_t(const CUtensorMap& mq, const CUtensorMap& mck, const Fa
                                        (int)smem_select));
   {
     ProfScope ps("block_topk_select", s);
-    qblock_select_kernel<D, BF16><<<dim3(p.nqb, hkv), kSelThreads, smem_select, s>>>(p);
+    const long long items = (long long)p.nqb * hkv, per = kSelThreads / 32;
+    qblock_select_kernel<D, BF16><<<(int)((items + per - 1) / per), kSelThreads, smem_select, s>>>(p);
     LSRM_LAUNCH_CHECK();
   }
   return LSRM_OK;
@@ -737,8 +816,8 @@ static int launch_fast_t(const CUtensorMap& mq, const CUtensorMap& mck, const Fa
 // (the exact scorer then serves the call).
 static void fast_smem(int D, int G, int nb_cap, size_t* scores, size_t* select) {
   *scores = D == 64 ? SfLayout<64>::bytes(nb_cap) : D == 32 ? SfLayout<32>::bytes(nb_cap) : SfLayout<16>::bytes(nb_cap);
-  *select = D == 64 ? SelLayout<64>::bytes(nb_cap) : D == 32 ? SelLayout<32>::bytes(nb_cap)
-                                                             : SelLayout<16>::bytes(nb_cap);
+  constexpr int W = kSelThreads / 32;
+  *select = 128 + W * (D == 64 ? sizeof(SelWarpMem<64>) : D == 32 ? sizeof(SelWarpMem<32>) : sizeof(SelWarpMem<16>));
   if (G > kSfCols || *scores > 220 * 1024 || *select > 220 * 1024) *scores = *select = 0;
 }
 
@@ -797,6 +876,7 @@ int launch_qblock_topk_fast(const lsrm_varlen* meta, const lsrm_attn_shape* shap
   p.nb_cap = nb_cap;
   p.nb_total = meta->num_blocks;
   p.nqb = num_query_blocks;
+  p.hkv = (int)hkv;
   p.ckn = static_cast<const float*>(workspace);
   p.bounds = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align_up(4 * hkv * nb_cap, 256));
   p.qk_scale = (float)qk_scale;
