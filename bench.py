@@ -49,6 +49,13 @@ CONFIGS = {
 }
 
 
+def _check_device_errors(ops):
+    """Raise if a kernel set a bit in the library's device error word."""
+    err = ops.read_errors()
+    if err:
+        raise RuntimeError(f"device error word 0x{err:x} (LSRM_ERR_* bits of include/lsrm_sparse.h)")
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -780,7 +787,7 @@ def run_volume_output(args):
     call = lambda v, i: V.prepare_volume_output(v, i, prior, c["channels"], c["upsample"], c["res"], batch_size=1)
     for _ in range(args.warmup):
         call(vol, vidx)
-    assert ops.read_errors() == 0
+    _check_device_errors(ops)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = _lib.launch_count()
@@ -901,7 +908,7 @@ def run_volume_geo(args):
     call = lambda: blocks.volume_block_topk(coords, cu_sb, cu_blk, c["batch"], c["res"], c["bbox_radius"], c["topk"])
     for _ in range(args.warmup):
         call()
-    assert ops.read_errors() == 0
+    _check_device_errors(ops)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = _lib.launch_count()
@@ -1182,7 +1189,7 @@ def run_view_maps(args):
 
     for _ in range(args.warmup):
         out = call()
-    assert ops.read_errors() == 0
+    _check_device_errors(ops)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = _lib.launch_count()
@@ -1311,6 +1318,9 @@ def run_decoder(args):
     ws, rank, local = dist_env()
     if args.impl == "reference" and rank != 0:
         return
+    if args.decoder_heads:  # other head geometries (hidden size unchanged, so head_dim = dim / Q)
+        hq, hkv = (int(x) for x in args.decoder_heads.split(","))
+        DEC_CFG.update(q_heads=hq, kv_heads=hkv)
     c = DEC_CFG
     n_req = args.decoder_tokens or c["n_vol"]
     base = {"metric": "sparse decoder training step (voxel tokens/s)", "unit": "tokens/s", "higher_is_better": True}
@@ -1372,7 +1382,7 @@ def run_decoder(args):
     for _ in range(args.warmup):
         step(x_in, y_in)
     torch.cuda.synchronize()
-    assert ops.read_errors() == 0
+    _check_device_errors(ops)
     mem_gb = torch.cuda.max_memory_allocated(dev) / 2 ** 30
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1477,6 +1487,8 @@ def main():
                          "training step (decoder tokens/s)")
     ap.add_argument("--decoder-tokens", type=int, default=0, help="voxel tokens of --path decoder (default cfg4's)")
     ap.add_argument("--decoder-layers", type=int, default=0, help="layers of --path decoder (default 24)")
+    ap.add_argument("--decoder-heads", default="", help="Q,KV heads of --path decoder (default 16,16; the "
+                    "reference's production model uses 32,2 at hidden 1024, i.e. head_dim 32)")
     ap.add_argument("--torch-profile", action="store_true",
                     help="--path decoder: print torch.profiler's per-kernel table of one extra step on stderr")
     args = ap.parse_args()

@@ -156,7 +156,10 @@ int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_attn_shape*
 /* Dense-range branches                                                     */
 /* ---------------------------------------------------------------------- */
 
-/* Workspace for the compressed / window / sliding-window entries. */
+/* Workspace for the compressed / window / sliding-window entries.  With more
+ * than one query head per kv head the dense kernels run over kv heads
+ * repeated num_q_heads / num_kv_heads times (one query head each); the
+ * workspace then also holds the repeated k / v and their gradients. */
 size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode);
 
 #define LSRM_DENSE_COMPRESSED 0 /* q vs all compressed blocks of its sequence */

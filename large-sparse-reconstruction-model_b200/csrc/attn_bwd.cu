@@ -206,6 +206,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.tiles_ub = plan.tiles_ub;
     p.union_cap = plan.union_cap;
     p.cu_block_include_tokens = meta->cu_block_include_tokens;
+    p.num_blocks = meta->num_blocks;
     p.out = out;
     p.dout = dout;
     p.lse = lse_log2;
@@ -249,6 +250,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.item_nch = plan.item_nch;
     p.kv_tok_stride = shape->kv_token_stride;
     p.total_q = meta->total_q;
+    p.total_k = meta->total_k;
     p.G = G;
     p.hkv = hkv;
     p.scale_log2 = scale * 1.44269504f;
@@ -275,33 +277,56 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
                           shape->kv_token_stride, row_elems, s);
 }
 
-extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode,
-                                   int32_t window, const void* q, const void* k, const void* v, const void* out,
-                                   const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
-                                   void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
+namespace lsrm {
+
+// dk / dv [n, hkv, D] (row stride `stride`) = sum over the R copies of each
+// kv head in src [n, hkv * R, D], in copy order, fp32.
+template <typename T>
+__global__ void sum_kv_head_copies_kernel(const T* __restrict__ src, T* __restrict__ dst, long long stride,
+                                          long long n, int hkv, int R, int D) {
+  const long long total = n * hkv * D;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % D);
+    const int h = (int)((i / D) % hkv);
+    const long long t = i / ((long long)D * hkv);
+    const T* row = src + ((t * hkv + h) * R) * (long long)D + d;
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc += (float)row[(long long)r * D];
+    dst[t * stride + (long long)h * D + d] = (T)acc;
+  }
+}
+
+static int sum_kv_head_copies(const void* src, void* dst, long long stride, long long n, int hkv, int R, int D,
+                              bool bf16, cudaStream_t s) {
+  if (n <= 0) return LSRM_OK;
+  const long long total = n * hkv * D;
+  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  ProfScope ps("dense_regroup", s);
+  if (bf16)
+    sum_kv_head_copies_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(src),
+                                                                  static_cast<__nv_bfloat16*>(dst), stride, n, hkv, R,
+                                                                  D);
+  else
+    sum_kv_head_copies_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(src), static_cast<__half*>(dst),
+                                                           stride, n, hkv, R, D);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
+
+// The dense backward with at most kDenseMaxG query heads per kv head; the
+// workspace holds `need` bytes (dense_ws_direct).
+static int dense_bwd_direct(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int mode, int window,
+                            const void* q, const void* k, const void* v, const void* out, const float* lse,
+                            const void* dout, void* dq, void* dk, void* dv, float* delta, void* workspace,
+                            size_t need, int* err_flags, cudaStream_t s) {
   int G = 1, rc;
   if ((rc = check_shape(meta, shape, G))) return rc;
-  LSRM_CHECK_ARG(G <= 64, "the backward supports up to 64 query heads per kv head (got %d)", G);
-  LSRM_CHECK_ARG(mode >= 0 && mode <= 2, "unknown dense mode %d", mode);
-  LSRM_CHECK_ARG(mode == LSRM_DENSE_COMPRESSED || meta->total_q == meta->total_k,
-                 "window branches attend inside one token sequence (total_q == total_k)");
-  const size_t need = lsrm_dense_workspace_bytes(meta, shape, mode);
-  if (workspace_bytes < need || !workspace) {
-    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
-    return LSRM_ERR_WORKSPACE;
-  }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LSRM_CHECK_ARG(G <= kDenseMaxG, "dense kernels take at most %d query heads per kv head (got %d)", kDenseMaxG, G);
   const int D = shape->head_dim, hkv = shape->num_kv_heads;
   const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
   const long long nk = (mode == LSRM_DENSE_COMPRESSED) ? meta->num_blocks : meta->total_k;
   const int row_elems = hkv * D;
-  if (meta->total_q == 0) {
-    if (nk > 0) {
-      LSRM_CUDA_TRY(cudaMemsetAsync(dk, 0, (size_t)nk * shape->kv_token_stride * 2, s));
-      LSRM_CUDA_TRY(cudaMemsetAsync(dv, 0, (size_t)nk * shape->kv_token_stride * 2, s));
-    }
-    return LSRM_OK;
-  }
   DensePlan plan = make_dense_plan(meta, G, mode, workspace);
   uint8_t* extra = static_cast<uint8_t*>(workspace) + plan.bytes;
   int* err = err_flags ? err_flags : reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + need - 256);
@@ -366,6 +391,7 @@ extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shap
     p.partial = p.n_split > 1 ? reinterpret_cast<float*>(extra) : nullptr;
     p.kv_tok_stride = shape->kv_token_stride;
     p.total_q = meta->total_q;
+    p.total_k = (int)nk;
     p.G = G;
     p.hkv = hkv;
     p.scale_log2 = scale * 1.44269504f;
@@ -386,4 +412,52 @@ extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shap
                          : mode == LSRM_DENSE_INTRA_BLOCK ? meta->cu_block_include_tokens + meta->num_blocks
                                                           : meta->cu_seqlens_k + meta->num_seqs;
   return launch_zero_tail(dk, dv, start, nk, shape->kv_token_stride, row_elems, s);
+}
+
+}  // namespace lsrm
+
+extern "C" int lsrm_dense_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode,
+                                   int32_t window, const void* q, const void* k, const void* v, const void* out,
+                                   const float* lse, const void* dout, void* dq, void* dk, void* dv, float* delta,
+                                   void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
+  int G = 1, rc;
+  if ((rc = check_shape(meta, shape, G))) return rc;
+  LSRM_CHECK_ARG(G <= 64, "the backward supports up to 64 query heads per kv head (got %d)", G);
+  LSRM_CHECK_ARG(mode >= 0 && mode <= 2, "unknown dense mode %d", mode);
+  LSRM_CHECK_ARG(mode == LSRM_DENSE_COMPRESSED || meta->total_q == meta->total_k,
+                 "window branches attend inside one token sequence (total_q == total_k)");
+  const size_t need = lsrm_dense_workspace_bytes(meta, shape, mode);
+  if (workspace_bytes < need || !workspace) {
+    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    return LSRM_ERR_WORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long nk = (mode == LSRM_DENSE_COMPRESSED) ? meta->num_blocks : meta->total_k;
+  if (meta->total_q == 0) {
+    if (nk > 0) {
+      LSRM_CUDA_TRY(cudaMemsetAsync(dk, 0, (size_t)nk * shape->kv_token_stride * 2, s));
+      LSRM_CUDA_TRY(cudaMemsetAsync(dv, 0, (size_t)nk * shape->kv_token_stride * 2, s));
+    }
+    return LSRM_OK;
+  }
+  if (G <= kDenseMaxG)
+    return dense_bwd_direct(meta, shape, mode, window, q, k, v, out, lse, dout, dq, dk, dv, delta, workspace, need,
+                            err_flags, s);
+  // regrouped as in the forward: repeated kv heads in, their gradients summed
+  // back per kv head afterwards
+  const DenseRegroup r = dense_regroup(meta, shape, mode);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  void* k2 = base + r.inner;
+  void* v2 = base + r.inner + r.buf;
+  void* dk2 = base + r.inner + 2 * r.buf;
+  void* dv2 = base + r.inner + 3 * r.buf;
+  const int hkv = shape->num_kv_heads, D = shape->head_dim;
+  const bool bf16 = shape->dtype == LSRM_DTYPE_BF16;
+  if ((rc = repeat_kv_heads(k, shape->kv_token_stride, k2, r.nk, hkv, r.R, D, s))) return rc;
+  if ((rc = repeat_kv_heads(v, shape->kv_token_stride, v2, r.nk, hkv, r.R, D, s))) return rc;
+  if ((rc = dense_bwd_direct(meta, &r.shape, mode, window, q, k2, v2, out, lse, dout, dq, dk2, dv2, delta, workspace,
+                             r.inner, err_flags, s)))
+    return rc;
+  if ((rc = sum_kv_head_copies(dk2, dk, shape->kv_token_stride, r.nk, hkv, r.R, D, bf16, s))) return rc;
+  return sum_kv_head_copies(dv2, dv, shape->kv_token_stride, r.nk, hkv, r.R, D, bf16, s);
 }

@@ -38,6 +38,7 @@ struct DqParams {
   int tiles_ub;
   int union_cap;
   const int32_t* cu_block_include_tokens;
+  int num_blocks;
   const void* out;
   const void* dout;
   const float* lse;
@@ -89,7 +90,7 @@ template <int NG>
 __device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, int U, const int* union_blk,
                                                   const uint4* union_mask, size_t ubase, const int32_t* cu_blk,
                                                   int kv_lo, int kv_hi, int* row0, uint32_t (*qmask)[4],
-                                                  uint32_t* colmask) {
+                                                  uint32_t* colmask, int num_blocks, int* err) {
   uint32_t cm[NG / 4];
 #pragma unroll
   for (int w = 0; w < NG / 4; ++w) cm[w] = 0u;
@@ -97,6 +98,7 @@ __device__ __forceinline__ void walk_union_groups(int& u, int& tcur, int& tend, 
     while (tcur >= tend && u + 1 < U) {
       ++u;
       const int gb = union_blk[ubase + u];
+      if (!dcheck((unsigned)gb < (unsigned)num_blocks, kDcUnion, err)) continue;  // tcur == tend: next entry
       tcur = max(cu_blk[gb], kv_lo);
       tend = min(cu_blk[gb + 1], kv_hi);
     }
@@ -182,9 +184,14 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       it.ubase = th * prm.union_cap;
       it.U = prm.union_cnt[th];
       it.n_chunks = (prm.union_ngroups[th] + kDqGroups - 1) / kDqGroups;
+      if (!dcheck((unsigned)it.U <= (unsigned)prm.union_cap, kDcUnion, prm.err)) it.U = it.n_chunks = 0;
     } else {
       it.n_chunks = it.tile.kv_hi > it.tile.kv_lo ? (it.tile.kv_hi - it.tile.kv_lo + kDqChunk - 1) / kDqChunk : 0;
     }
+    if (!dcheck(it.tile.q_start >= 0 && it.tile.n_q >= 0 && it.tile.q_start + it.tile.n_q <= prm.total_q &&
+                    it.n_chunks >= 0,
+                kDcQTile, prm.err))
+      it.tile.n_q = it.n_chunks = 0;
     return it;
   };
 
@@ -272,7 +279,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         if (pw == 0) {
           if (!warp_wait(uc_empty, par, abort_flag, prm.err)) { ok = false; break; }
           union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens, tile.kv_lo,
-                           tile.kv_hi);
+                           tile.kv_hi, prm.num_blocks, prm.err);
           __syncwarp();
           if (lane == 0) mbar_arrive(uc_full);
         } else {
@@ -315,7 +322,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
             DqMeta& mt = meta[s];
             walk_union_groups<kDqGroups>(u, tcur, tend, w.U, prm.union_blk, prm.union_mask, w.ubase,
                                          prm.cu_block_include_tokens, tile.kv_lo, tile.kv_hi, mt.row0, mt.qmask,
-                                         mt.colmask);
+                                         mt.colmask, prm.num_blocks, prm.err);
             mbar_arrive_expect_tx(&kv_full[s], 2 * L::KTILE);
             load_group_runs<kDqGroups, RB>(mt.row0, sK + s * L::KTILE, sV + s * L::KTILE, kv.k, kv.v, h, prm.total_k,
                                            &kv_full[s]);
@@ -573,6 +580,7 @@ struct DkvParams {
   const int* item_nch;  // select mode: query chunks of each work item
   long long kv_tok_stride;
   int total_q;
+  int total_k;
   int G;
   int hkv;
   float scale_log2;
@@ -671,8 +679,11 @@ __device__ __forceinline__ void rev_cache_fill(RevCache& rc, const DkvParams& pr
     int cnt = 0, gcnt = 0;
     if (i < n) {
       const int2 x = ent[e0 + i];
-      const uint4 m = prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y];
-      rc.tq0[i] = prm.qtiles[x.x].q_start;
+      const bool good = dcheck((unsigned)x.x < (unsigned)prm.tiles_ub && (unsigned)x.y < (unsigned)prm.union_cap,
+                               kDcRevEntry, prm.err);
+      const uint4 m = good ? prm.union_mask[((size_t)h * prm.tiles_ub + x.x) * prm.union_cap + x.y]
+                           : make_uint4(0u, 0u, 0u, 0u);
+      rc.tq0[i] = good ? prm.qtiles[x.x].q_start : 0;
       rc.mask[i] = m;
       cnt = __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
       if (prm.G <= 8) {
@@ -833,8 +844,15 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
     it.kt = prm.kvtiles[it.kt_idx];  // rows = keys [q_start, q_start + n_q)
     it.q_lo = it.kt.kv_lo;
     it.q_hi = it.kt.kv_hi;
+    if (!dcheck(it.kt.q_start >= 0 && it.kt.n_q >= 0 && it.kt.n_q <= 128 && it.kt.q_start + it.kt.n_q <= prm.total_k &&
+                    (MODE != kSelect || (unsigned)it.kt.seg < (unsigned)prm.num_blocks),
+                kDcKvTile, prm.err)) {
+      it.skip = true;
+      return it;
+    }
     if constexpr (MODE == kSelect) {
       it.n_chunks = prm.item_nch[(size_t)it.h * prm.kvtiles_ub + it.kt_idx];
+      if (!dcheck(it.n_chunks >= 0, kDcChunks, prm.err)) it.n_chunks = 0;
     } else {
       const int nq = max(it.q_hi - it.q_lo, 0);
       const int per = ((nq + prm.n_split - 1) / prm.n_split + qpc - 1) / qpc * qpc;
@@ -928,6 +946,10 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
         e_first = off[kt.seg];
         e_count = off[kt.seg + 1] - e_first;
+        if (!dcheck(e_first >= 0 && e_count >= 0 &&
+                        (long long)e_first + e_count <= (long long)prm.tiles_ub * prm.union_cap,
+                    kDcRevRange, prm.err))
+          e_first = e_count = 0;
       }
       const int n_seg = MODE == kSelect ? (e_count + kRevCacheCap - 1) / kRevCacheCap : 1;
       const bool have_rc = MODE == kSelect && n_seg > 0;
@@ -1016,7 +1038,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
               const int t = __shfl_sync(0xffffffffu, tok, grp);
               const uint32_t bb = __shfl_sync(0xffffffffu, bits, grp);
               const int qq = rr >> lg_g, g = rr & (G - 1);
-              const bool valid = t >= 0 && ((bb >> qq) & 1u);
+              const bool valid = t >= 0 && ((bb >> qq) & 1u) && dcheck(t + qq < prm.total_q, kDcQRow, prm.err);
               mt.qidx[row] = valid ? t + qq : -1;
               if (valid) {
                 const size_t si = (size_t)(h * G + g) * prm.total_q + (t + qq);
@@ -1050,7 +1072,9 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
             if (lane == 0) mt.n_rows = n * G;
             __syncwarp();
             for (int row = lane; row < kKvQRows; row += 32) {
-              const int q = mt.qlist[row >> lg_g], g = row & (G - 1);
+              int q = mt.qlist[row >> lg_g];
+              const int g = row & (G - 1);
+              if (q >= 0 && !dcheck(q < prm.total_q, kDcQRow, prm.err)) q = -1;
               mt.qidx[row] = q;
               if (q >= 0) {
                 const size_t si = (size_t)(h * G + g) * prm.total_q + q;
@@ -1301,7 +1325,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
 #pragma unroll
         for (int cc = 0; cc < D; ++cc) v[cc] = 0.f;
       }
-      if (row_valid) {
+      if (row_valid && dcheck(kidx < prm.total_k, kDcKvOut, prm.err)) {
         if (prm.n_split > 1) {
           float* dst_p = prm.partial +
                          ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +

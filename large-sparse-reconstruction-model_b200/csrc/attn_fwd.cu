@@ -51,11 +51,6 @@ int check_shape(const lsrm_varlen* m, const lsrm_attn_shape* sh, int& G) {
                  "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", sh->num_q_heads, sh->num_kv_heads);
   G = sh->num_q_heads / sh->num_kv_heads;
   LSRM_CHECK_ARG(G <= 128 && (G & (G - 1)) == 0, "query heads per kv head (%d) must be a power of two <= 128", G);
-  // 8 query heads per kv head with several kv heads faulted once in a 24-layer decoder at 131k tokens
-  // (16 query / 2 kv heads); the cause is not found yet, so the combination is refused until it is
-  LSRM_CHECK_ARG(G != 8 || sh->num_kv_heads == 1,
-                 "8 query heads per kv head with %d kv heads is disabled (an open fault); use 1 or 16 kv heads "
-                 "for 16 query heads", sh->num_kv_heads);
   LSRM_CHECK_ARG(m->num_seqs >= 1 && m->total_q >= 0 && m->total_k >= 0 && m->num_blocks >= 0, "bad varlen sizes");
   LSRM_CHECK_ARG(sh->q_token_stride >= (int64_t)sh->num_q_heads * sh->head_dim, "q token stride too small");
   LSRM_CHECK_ARG(sh->kv_token_stride >= (int64_t)sh->num_kv_heads * sh->head_dim, "kv token stride too small");
@@ -119,6 +114,7 @@ extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_sha
   p.tiles_ub = plan.tiles_ub;
   p.union_cap = plan.union_cap;
   p.cu_block_include_tokens = meta->cu_block_include_tokens;
+  p.num_blocks = meta->num_blocks;
   p.out = out;
   p.lse = lse_log2;
   p.q_tok_stride = shape->q_token_stride;
@@ -133,14 +129,58 @@ extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_sha
   return launch_fwd<kSelect>(D, shape->dtype == LSRM_DTYPE_BF16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
 }
 
-extern "C" size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode) {
+namespace lsrm {
+
+// Workspace of the dense kernels run directly (G <= kDenseMaxG).
+size_t dense_ws_direct(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int mode) {
   int G = 1;
   if (check_shape(meta, shape, G) != LSRM_OK) return 0;
   DensePlan p = make_dense_plan(meta, G, mode, nullptr);
   return p.bytes + dense_bwd_extra_bytes(meta, shape, mode) + 256;
 }
 
-namespace lsrm {
+DenseRegroup dense_regroup(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int mode) {
+  DenseRegroup r{};
+  r.shape = *shape;
+  const int G = shape->num_q_heads / shape->num_kv_heads;
+  r.R = G > kDenseMaxG ? G / kDenseMaxG : 1;
+  r.nk = (mode == LSRM_DENSE_COMPRESSED) ? meta->num_blocks : meta->total_k;
+  if (r.R > 1) {
+    r.shape.num_kv_heads = shape->num_kv_heads * r.R;
+    r.shape.kv_token_stride = (int64_t)r.shape.num_kv_heads * shape->head_dim;
+  }
+  r.inner = align_up(dense_ws_direct(meta, &r.shape, mode), 256);
+  r.buf = align_up((size_t)std::max<long long>(r.nk, 1) * r.shape.num_kv_heads * shape->head_dim * 2, 256);
+  return r;
+}
+
+// k / v [n, hkv, D] (row stride `stride` elements) -> [n, hkv * R, D] with
+// head h copied to heads h*R .. h*R+R-1; 16-byte moves.
+__global__ void repeat_kv_heads_kernel(const uint4* __restrict__ src, long long stride_v, uint4* __restrict__ dst,
+                                       long long n, int hkv, int R, int vpr) {
+  const long long total = n * hkv * R * vpr;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % vpr);
+    const long long hr = i / vpr;
+    const int h = (int)((hr / R) % hkv);
+    const long long t = hr / ((long long)R * hkv);
+    dst[i] = src[t * stride_v + (long long)h * vpr + c];
+  }
+}
+
+int repeat_kv_heads(const void* src, long long stride, void* dst, long long n, int hkv, int R, int D,
+                    cudaStream_t s) {
+  if (n <= 0) return LSRM_OK;
+  const int vpr = D * 2 / 16;  // 16-byte vectors per head row
+  const long long total = n * hkv * R * vpr;
+  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  ProfScope ps("dense_regroup", s);
+  repeat_kv_heads_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(src), stride * 2 / 16,
+                                              static_cast<uint4*>(dst), n, hkv, R, vpr);
+  LSRM_LAUNCH_CHECK();
+  return LSRM_OK;
+}
 
 int dense_fwd_tiles(const lsrm_varlen* meta, int G, int mode, int window, DensePlan& plan, int* err, cudaStream_t s) {
   const int qpt = kRows / G;
@@ -154,24 +194,14 @@ int dense_fwd_tiles(const lsrm_varlen* meta, int G, int mode, int window, DenseP
                             window, err, s);
 }
 
-}  // namespace lsrm
-
-extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode,
-                                   int32_t window, const void* q, const void* k, const void* v, void* out, float* lse,
-                                   void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
+// The dense forward with at most kDenseMaxG query heads per kv head; the
+// workspace holds `need` bytes (dense_ws_direct).
+static int dense_fwd_direct(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int mode, int window,
+                            const void* q, const void* k, const void* v, void* out, float* lse, void* workspace,
+                            size_t need, int* err_flags, cudaStream_t s) {
   int G = 1, rc;
   if ((rc = check_shape(meta, shape, G))) return rc;
-  LSRM_CHECK_ARG(mode >= 0 && mode <= 2, "unknown dense mode %d", mode);
-  LSRM_CHECK_ARG(mode != LSRM_DENSE_SLIDING || window >= 0, "window must be >= 0");
-  LSRM_CHECK_ARG(mode == LSRM_DENSE_COMPRESSED || meta->total_q == meta->total_k,
-                 "window branches attend inside one token sequence (total_q == total_k)");
-  const size_t need = lsrm_dense_workspace_bytes(meta, shape, mode);
-  if (workspace_bytes < need || !workspace) {
-    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
-    return LSRM_ERR_WORKSPACE;
-  }
-  if (meta->total_q == 0) return LSRM_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LSRM_CHECK_ARG(G <= kDenseMaxG, "dense kernels take at most %d query heads per kv head (got %d)", kDenseMaxG, G);
   DensePlan plan = make_dense_plan(meta, G, mode, workspace);
   int* err = err_flags ? err_flags : reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + need - 256);
   if ((rc = dense_fwd_tiles(meta, G, mode, window, plan, err, s))) return rc;
@@ -199,6 +229,47 @@ extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shap
   if (mode == LSRM_DENSE_SLIDING)
     return launch_fwd<kBand>(D, bf16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
   return launch_fwd<kRange>(D, bf16, mq, kv, p, plan.tiles_ub, shape->num_kv_heads, s);
+}
+
+}  // namespace lsrm
+
+extern "C" size_t lsrm_dense_workspace_bytes(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode) {
+  int G = 1;
+  if (check_shape(meta, shape, G) != LSRM_OK) return 0;
+  if (G <= kDenseMaxG) return dense_ws_direct(meta, shape, mode);
+  const DenseRegroup r = dense_regroup(meta, shape, mode);
+  return r.inner + 4 * r.buf;  // inner workspace, repeated k / v, their gradients
+}
+
+extern "C" int lsrm_dense_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, int32_t mode,
+                                   int32_t window, const void* q, const void* k, const void* v, void* out, float* lse,
+                                   void* workspace, size_t workspace_bytes, int* err_flags, void* stream) {
+  int G = 1, rc;
+  if ((rc = check_shape(meta, shape, G))) return rc;
+  LSRM_CHECK_ARG(mode >= 0 && mode <= 2, "unknown dense mode %d", mode);
+  LSRM_CHECK_ARG(mode != LSRM_DENSE_SLIDING || window >= 0, "window must be >= 0");
+  LSRM_CHECK_ARG(mode == LSRM_DENSE_COMPRESSED || meta->total_q == meta->total_k,
+                 "window branches attend inside one token sequence (total_q == total_k)");
+  const size_t need = lsrm_dense_workspace_bytes(meta, shape, mode);
+  if (workspace_bytes < need || !workspace) {
+    set_error("workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    return LSRM_ERR_WORKSPACE;
+  }
+  if (meta->total_q == 0) return LSRM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (G <= kDenseMaxG)
+    return dense_fwd_direct(meta, shape, mode, window, q, k, v, out, lse, workspace, need, err_flags, s);
+  // more query heads per kv head than the dense kernels take: repeat every kv
+  // head R times and run with kDenseMaxG (the query heads, the output and the
+  // LSE are the same; only the grouping changes)
+  const DenseRegroup r = dense_regroup(meta, shape, mode);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  void* k2 = base + r.inner;
+  void* v2 = base + r.inner + r.buf;
+  const int hkv = shape->num_kv_heads, D = shape->head_dim;
+  if ((rc = repeat_kv_heads(k, shape->kv_token_stride, k2, r.nk, hkv, r.R, D, s))) return rc;
+  if ((rc = repeat_kv_heads(v, shape->kv_token_stride, v2, r.nk, hkv, r.R, D, s))) return rc;
+  return dense_fwd_direct(meta, &r.shape, mode, window, q, k2, v2, out, lse, workspace, r.inner, err_flags, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -361,6 +432,7 @@ extern "C" int lsrm_select_attn_fwd_noalloc(const lsrm_varlen* meta, const lsrm_
   p.tiles_ub = plan.tiles_ub;
   p.union_cap = plan.union_cap;
   p.cu_block_include_tokens = meta->cu_block_include_tokens;
+  p.num_blocks = meta->num_blocks;
   p.out = out;
   p.lse = lse_log2;
   p.q_tok_stride = shape->q_token_stride;

@@ -41,6 +41,7 @@ struct FwdParams {
   int tiles_ub;
   int union_cap;
   const int32_t* cu_block_include_tokens;
+  int num_blocks;
   // outputs
   void* out;
   float* lse;
@@ -153,9 +154,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       it.ubase = th * prm.union_cap;
       it.U = prm.union_cnt[th];
       it.n_chunks = (prm.union_ngroups[th] + kGroupsPerChunk - 1) / kGroupsPerChunk;
+      if (!dcheck((unsigned)it.U <= (unsigned)prm.union_cap, kDcUnion, prm.err)) it.U = it.n_chunks = 0;
     } else {
       it.n_chunks = it.tile.kv_hi > it.tile.kv_lo ? (it.tile.kv_hi - it.tile.kv_lo + kKVChunk - 1) / kKVChunk : 0;
     }
+    if (!dcheck(it.tile.q_start >= 0 && it.tile.n_q >= 0 && it.tile.q_start + it.tile.n_q <= prm.total_q &&
+                    it.n_chunks >= 0,
+                kDcQTile, prm.err))
+      it.tile.n_q = it.n_chunks = 0;
     return it;
   };
 
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       bool cached = false;
       if constexpr (MODE == kSelect)
         cached = union_cache_fill(uc, w.U, prm.union_blk, prm.union_mask, w.ubase, prm.cu_block_include_tokens,
-                                  tile.kv_lo, tile.kv_hi);
+                                  tile.kv_lo, tile.kv_hi, prm.num_blocks, prm.err);
       if (cached) {
         // the whole warp lays out each chunk (one lane per group) and issues its boxes
         int ucur = 0;
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 while (tcur >= tend && u + 1 < w.U) {
                   ++u;
                   const int gb = prm.union_blk[w.ubase + u];
+                  if (!dcheck((unsigned)gb < (unsigned)prm.num_blocks, kDcUnion, prm.err)) continue;
                   tcur = max(prm.cu_block_include_tokens[gb], tile.kv_lo);
                   tend = min(prm.cu_block_include_tokens[gb + 1], tile.kv_hi);
                 }

@@ -22,6 +22,35 @@ namespace lsrm {
 // error word and makes the CTA tear down cleanly.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Device-side index checks, compiled in with -DLSRM_DEVICE_CHECKS (build.py
+// --device-checks): a data-dependent index is tested before use; a failed
+// test sets LSRM_ERR_BAD_INDEX plus the site's bit (1 << (8 + site)) in the
+// error word and the access is skipped.  Release builds compile every check
+// to `true`.
+enum DcheckSite : int {
+  kDcUnion = 0,     // union size above its capacity, or a union block id out of range
+  kDcQTile = 1,     // a query tile outside the query tensor
+  kDcKvRow = 2,     // a key group row outside the key tensor
+  kDcOutRow = 3,    // an output / dQ row outside the query tensor
+  kDcRevRange = 4,  // a reverse-list range outside the entry array
+  kDcRevEntry = 5,  // a reverse entry (tile, union slot) out of range
+  kDcQRow = 6,      // a dK/dV query row outside the query tensor
+  kDcKvOut = 7,     // a dK/dV key row outside the key tensor
+  kDcSelRow = 8,    // a selection row out of range (union builder)
+  kDcRevFill = 9,   // a reverse-map fill position out of range
+  kDcKvTile = 10,   // a dK/dV tile whose block or rows are out of range
+  kDcChunks = 11,   // a work item's chunk count out of range
+};
+
+#ifdef LSRM_DEVICE_CHECKS
+__device__ __forceinline__ bool dcheck(bool ok, int site, int* err) {
+  if (!ok && err) atomicOr(err, LSRM_ERR_BAD_INDEX | (1 << (8 + site)));
+  return ok;
+}
+#else
+__device__ __forceinline__ bool dcheck(bool, int, int*) { return true; }
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -397,7 +426,8 @@ struct UnionCache {
 
 // Warp-wide fill (all 32 lanes).  Returns false when the union does not fit.
 __device__ __forceinline__ bool union_cache_fill(UnionCache& uc, int U, const int* union_blk, const uint4* union_mask,
-                                                 size_t ubase, const int32_t* cu_blk, int kv_lo, int kv_hi) {
+                                                 size_t ubase, const int32_t* cu_blk, int kv_lo, int kv_hi,
+                                                 int num_blocks, int* err) {
   const int lane = threadIdx.x & 31;
   if (U > kUnionCacheCap) return false;
   int carry = 0;
@@ -405,7 +435,7 @@ __device__ __forceinline__ bool union_cache_fill(UnionCache& uc, int U, const in
     const int e = b0 + lane;
     int t0 = 0, t1 = 0, g = 0;
     uint4 m = make_uint4(0u, 0u, 0u, 0u);
-    if (e < U) {
+    if (e < U && dcheck((unsigned)union_blk[ubase + e] < (unsigned)num_blocks, kDcUnion, err)) {
       const int gb = union_blk[ubase + e];
       t0 = max(cu_blk[gb], kv_lo);
       t1 = min(cu_blk[gb + 1], kv_hi);

@@ -2,6 +2,7 @@
 // All integer work; deterministic outputs (the reverse map is sorted).
 #include <cuda_runtime.h>
 
+#include "common.cuh"
 #include "host_util.h"
 #include "plan.cuh"
 
@@ -194,8 +195,10 @@ __global__ void __launch_bounds__(kUnionThreads)
     int v = INT32_MAX;
     if (i < E) {
       const int row = per_block ? tile.sel_row : tile.q_start + i / topk;
-      const int id = sel[(size_t)row * topk + (i % topk)];
-      if (id >= 0 && id < nb_seq) v = id;
+      if (dcheck(row >= 0 && row < sel_rows, kDcSelRow, err)) {
+        const int id = sel[(size_t)row * topk + (i % topk)];
+        if (id >= 0 && id < nb_seq) v = id;
+      }
     }
     keys[i] = v;
   }
@@ -255,6 +258,7 @@ __global__ void __launch_bounds__(kUnionThreads)
   } else {
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
       const int r = i / topk;
+      if (!dcheck(tile.q_start + r < sel_rows, kDcSelRow, err)) continue;
       const int id = sel[(size_t)(tile.q_start + r) * topk + (i % topk)];
       if (id < 0 || id >= nb_seq) continue;
       int lo = 0, hi = U;  // lower bound of id in ids[0..U)
@@ -321,7 +325,7 @@ __global__ void rev_scan_kernel(SelectPlan p) {
   if (threadIdx.x == 0) off[0] = 0;
 }
 
-__global__ void rev_fill_kernel(SelectPlan p) {
+__global__ void rev_fill_kernel(SelectPlan p, int* err) {
   const int t = blockIdx.x, h = blockIdx.y;
   if (t >= *p.n_tiles) return;
   const size_t base = ((size_t)h * p.tiles_ub + t) * p.union_cap;
@@ -329,30 +333,47 @@ __global__ void rev_fill_kernel(SelectPlan p) {
   for (int u = threadIdx.x; u < U; u += blockDim.x) {
     const int b = p.union_blk[base + u];
     const int pos = atomicAdd(&p.rev_cursor[(size_t)h * p.num_blocks + b], 1);
-    p.rev_entries[(size_t)h * p.tiles_ub * p.union_cap + pos] = make_int2(t, u);
+    if (dcheck(pos >= 0 && (long long)pos < (long long)p.tiles_ub * p.union_cap, kDcRevFill, err))
+      p.rev_entries[(size_t)h * p.tiles_ub * p.union_cap + pos] = make_int2(t, u);
   }
 }
 
-constexpr int kRevSortMax = 8192;
+// Per-block sort of the reverse lists (bitonic, in shared memory).  Keys are
+// (tile, union slot); a block appears at most once per tile, so a list holds
+// at most one entry per query tile.  When tile and slot fit in 19 + 13 bits
+// the key is 32-bit and a list may hold kRevSortMax32 entries, otherwise 64-bit
+// and kRevSortMax64; a longer list is left unsorted and flagged
+// (LSRM_ERR_CAPACITY).  Two launches: lists of up to kRevSortSmall entries in
+// small CTAs (many per SM), then the longer ones with the full capacity.
+constexpr int kRevSortMax32 = 32768;  // 128 KB of keys
+constexpr int kRevSortMax64 = 16384;  // 128 KB of keys
+constexpr int kRevSortSmall = 2048;
+constexpr int kRevSlotBits = 13;
 
+template <typename K, bool SMALL>
 __global__ void __launch_bounds__(256) rev_sort_kernel(SelectPlan p, int* err) {
-  extern __shared__ long long keys[];  // [kRevSortMax]
+  extern __shared__ __align__(16) unsigned char rs_smem[];
+  K* keys = reinterpret_cast<K*>(rs_smem);
+  constexpr bool k32 = sizeof(K) == 4;
+  constexpr int cap = SMALL ? kRevSortSmall : k32 ? kRevSortMax32 : kRevSortMax64;
   const int b = blockIdx.x, h = blockIdx.y;
   const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
   const int s = off[b], e = off[b + 1], n = e - s;
-  if (n <= 1) return;
-  if (n > kRevSortMax) {
+  if (n <= 1 || (SMALL ? n > kRevSortSmall : n <= kRevSortSmall)) return;  // the other launch's list
+  if (n > cap) {
     if (threadIdx.x == 0) atomicOr(err, LSRM_ERR_CAPACITY);
     return;
   }
   int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap + s;
   int P = 1;
   while (P < n) P <<= 1;
+  const K kmax = ~K(0);
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    long long k = LLONG_MAX;
+    K k = kmax;
     if (i < n) {
       const int2 x = ent[i];
-      k = ((long long)x.x << 32) | (unsigned)x.y;
+      k = k32 ? (K)(((uint32_t)x.x << kRevSlotBits) | (uint32_t)x.y)
+              : (K)(((unsigned long long)(uint32_t)x.x << 32) | (uint32_t)x.y);
     }
     keys[i] = k;
   }
@@ -362,7 +383,7 @@ __global__ void __launch_bounds__(256) rev_sort_kernel(SelectPlan p, int* err) {
       for (int i = threadIdx.x; i < P; i += blockDim.x) {
         const int ixj = i ^ j;
         if (ixj > i) {
-          const long long a = keys[i], c = keys[ixj];
+          const K a = keys[i], c = keys[ixj];
           const bool up = (i & k) == 0;
           if ((a > c) == up) {
             keys[i] = c;
@@ -373,8 +394,11 @@ __global__ void __launch_bounds__(256) rev_sort_kernel(SelectPlan p, int* err) {
       __syncthreads();
     }
   }
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    ent[i] = make_int2((int)(keys[i] >> 32), (int)(keys[i] & 0xffffffffll));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const K k = keys[i];
+    ent[i] = k32 ? make_int2((int)(k >> kRevSlotBits), (int)(k & ((1u << kRevSlotBits) - 1u)))
+                 : make_int2((int)((unsigned long long)k >> 32), (int)((unsigned long long)k & 0xffffffffull));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -588,11 +612,26 @@ int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s) {
   LSRM_LAUNCH_CHECK();
   rev_scan_kernel<<<p.hkv, 1024, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();
-  rev_fill_kernel<<<grid, 128, 0, s>>>(p);
+  rev_fill_kernel<<<grid, 128, 0, s>>>(p, err);
   LSRM_LAUNCH_CHECK();
-  const int sort_smem = kRevSortMax * (int)sizeof(long long);
-  LSRM_CUDA_TRY(cudaFuncSetAttribute(rev_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sort_smem));
-  rev_sort_kernel<<<dim3(std::max(p.num_blocks, 1), p.hkv), 256, sort_smem, s>>>(p, err);
+  const dim3 grid_sort(std::max(p.num_blocks, 1), p.hkv);
+  // 32-bit keys when tile < 2^19 - 1 and slot < 2^13 (no key equals the padding key ~0)
+  if (p.tiles_ub < (1 << (32 - kRevSlotBits)) && p.union_cap <= (1 << kRevSlotBits)) {
+    rev_sort_kernel<uint32_t, true><<<grid_sort, 256, kRevSortSmall * (int)sizeof(uint32_t), s>>>(p, err);
+    LSRM_LAUNCH_CHECK();
+    const int smem = kRevSortMax32 * (int)sizeof(uint32_t);
+    LSRM_CUDA_TRY(
+        cudaFuncSetAttribute(rev_sort_kernel<uint32_t, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    rev_sort_kernel<uint32_t, false><<<grid_sort, 256, smem, s>>>(p, err);
+  } else {
+    rev_sort_kernel<unsigned long long, true>
+        <<<grid_sort, 256, kRevSortSmall * (int)sizeof(unsigned long long), s>>>(p, err);
+    LSRM_LAUNCH_CHECK();
+    const int smem = kRevSortMax64 * (int)sizeof(unsigned long long);
+    LSRM_CUDA_TRY(cudaFuncSetAttribute(rev_sort_kernel<unsigned long long, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    rev_sort_kernel<unsigned long long, false><<<grid_sort, 256, smem, s>>>(p, err);
+  }
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }

@@ -92,6 +92,13 @@ def _shape(q: torch.Tensor, k: torch.Tensor, softmax_scale: Optional[float]) -> 
     )
 
 
+def _rows(*ts):
+    """The kernels address q, out, dout and dq with q's token stride and k, v,
+    dk and dv with k's: hand them dense [tokens, heads, head_dim] tensors (a
+    no-op for contiguous inputs; a copy for any other layout)."""
+    return tuple(t if t is None or t.is_contiguous() else t.contiguous() for t in ts)
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
@@ -114,7 +121,7 @@ def select_attn_fwd(q, k, v, block_topk, meta: Meta, softmax_scale=None, cu_quer
     """Returns (out [Nq,Hq,D], lse_log2 [Hq,Nq] fp32, workspace)."""
     L = _lib.lib()
     assert q.dtype == k.dtype == v.dtype
-    assert k.stride() == v.stride(), "k and v must share a layout"
+    q, k, v = _rows(q, k, v)
     block_topk = _i32(block_topk)
     topk = block_topk.shape[-1]
     nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
@@ -127,8 +134,7 @@ def select_attn_fwd(q, k, v, block_topk, meta: Meta, softmax_scale=None, cu_quer
         raise _lib.LsrmError("invalid selection problem: " + L.lsrm_last_error().decode())
     if workspace is None or workspace.numel() < need:
         workspace = _workspace(need, q.device)
-    out = torch.empty_like(q) if q.is_contiguous() else torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    assert out.stride(0) == q.stride(0)
+    out = torch.empty_like(q)
     lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
     rc = L.lsrm_select_attn_fwd(
         ctypes.byref(vl), ctypes.byref(sh), _ptr(q), _ptr(k), _ptr(v), _ptr(block_topk), topk, _ptr(cqb), nqb,
@@ -142,6 +148,7 @@ def select_attn_bwd(q, k, v, out, lse, dout, block_topk, meta: Meta, softmax_sca
                     workspace: Optional[torch.Tensor] = None):
     """Returns (dq, dk, dv)."""
     L = _lib.lib()
+    q, k, v, out, dout = _rows(q, k, v, out, dout)
     block_topk = _i32(block_topk)
     topk = block_topk.shape[-1]
     nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1
@@ -152,7 +159,6 @@ def select_attn_bwd(q, k, v, out, lse, dout, block_topk, meta: Meta, softmax_sca
     need = L.lsrm_select_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), topk, nqb)
     if workspace is None or workspace.numel() < need:
         workspace = _workspace(need, q.device)
-    dout = dout.contiguous() if dout.stride() != q.stride() else dout
     dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
@@ -179,6 +185,7 @@ def dense_attn_fwd(q, k, v, meta: Meta, mode: int, window: int = 0, softmax_scal
     """Returns (out, lse).  lse is natural-log for DENSE_COMPRESSED, log2
     otherwise; [Hq, Nq] fp32."""
     L = _lib.lib()
+    q, k, v = _rows(q, k, v)
     vl = meta.struct(q.shape[0], k.shape[0])
     sh = _shape(q, k, softmax_scale)
     need = L.lsrm_dense_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), mode)
@@ -195,11 +202,11 @@ def dense_attn_fwd(q, k, v, meta: Meta, mode: int, window: int = 0, softmax_scal
 
 def dense_attn_bwd(q, k, v, out, lse, dout, meta: Meta, mode: int, window: int = 0, softmax_scale=None):
     L = _lib.lib()
+    q, k, v, out, dout = _rows(q, k, v, out, dout)
     vl = meta.struct(q.shape[0], k.shape[0])
     sh = _shape(q, k, softmax_scale)
     need = L.lsrm_dense_workspace_bytes(ctypes.byref(vl), ctypes.byref(sh), mode)
     ws = _workspace(need, q.device)
-    dout = dout.contiguous() if dout.stride() != q.stride() else dout
     dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
@@ -231,6 +238,7 @@ def block_topk(q, ck, lse_ln, topk: int, meta: Meta, cu_query_blocks=None, force
                sm_scale: Optional[float] = None):
     """Deterministic block selection; returns int32 [Hkv, rows, topk]."""
     L = _lib.lib()
+    q, ck = _rows(q, ck)
     vl = meta.struct(q.shape[0], ck.shape[0])
     sh = _shape(q, ck, None)
     nqb = 0 if cu_query_blocks is None else cu_query_blocks.numel() - 1

@@ -90,7 +90,6 @@ def _fwd(lib, meta, shape, topk=4, ws=None, ws_bytes=0):
     (dict(dtype=7), "LSRM_ERR_INVALID_ARG", "dtype"),
     (dict(Hq=6, Hkv=2), "LSRM_ERR_INVALID_ARG", "power of two"),
     (dict(Hq=5, Hkv=2), "LSRM_ERR_INVALID_ARG", "multiple"),
-    (dict(Hq=16, Hkv=2), "LSRM_ERR_INVALID_ARG", "open fault"),  # 8 query heads per kv head, 2 kv heads
 ])
 def test_select_fwd_rejects_bad_shapes_on_host(lib, bad, code, msg):
     rc = _fwd(lib, _meta(), _shape(**bad))
@@ -115,6 +114,19 @@ def test_workspace_queries_are_host_only_and_grow_with_the_problem(lib):
     assert h.lsrm_select_workspace_bytes(ctypes.byref(_meta()), ctypes.byref(_shape(D=48)), 8, 0) == 0
     for mode in (0, 1, 2):
         assert h.lsrm_dense_workspace_bytes(ctypes.byref(_meta(4096, 32)), ctypes.byref(_shape()), mode) > 0
+
+
+def test_dense_workspace_covers_regrouped_heads(lib):
+    """Dense branches with several query heads per kv head run over kv heads
+    repeated to one query head each: the workspace adds the repeated k / v and
+    their gradients (4 x rows x Hq x D x 2 bytes at least)."""
+    h = lib.lib()
+    meta = _meta(4096, 64)
+    for mode in (0, 1, 2):
+        g1 = h.lsrm_dense_workspace_bytes(ctypes.byref(meta), ctypes.byref(_shape(Hq=4, Hkv=4)), mode)
+        g8 = h.lsrm_dense_workspace_bytes(ctypes.byref(meta), ctypes.byref(_shape(Hq=16, Hkv=2)), mode)
+        rows = 64 if mode == 0 else 4096
+        assert 0 < g1 < g8 and g8 >= 4 * rows * 16 * 64 * 2
 
 
 def test_noalloc_scratch_bound_is_the_header_constant(lib):

@@ -8,7 +8,10 @@ shared-memory caches:
   tiles (five segments, 8 query heads per kv head) and 1094 tiles of 128
   queries on two kv heads,
 * a KV block with more than 4096 8-row query windows (dK/dV window list) but
-  few enough reverse entries for one cache segment.
+  few enough reverse entries for one cache segment,
+* a KV block selected by 10000 query tiles (16 query heads per kv head: 8
+  queries per tile), beyond the 2048 entries of the reverse map's small sort
+  and the 8192 of its former capacity.
 
 Checked against a gather-based fp32 torch reference of the same op (each query
 attends the tokens of its selected blocks), forward and backward."""
@@ -82,6 +85,7 @@ CASES = [
     ("windows_over_4096", 40000, 4, 1, 1, 64, 4, True),     # block 0: 313 tiles, ~5000 8-query windows
     ("reverse_five_segments", 80000, 4, 8, 1, 64, 4, True),  # block 0 in all 5000 16-query tiles
     ("reverse_two_heads_g1", 140000, 4, 2, 2, 64, 4, True),  # block 0 in all 1094 128-query tiles, per head
+    ("reverse_over_8192_g16", 80000, 4, 16, 1, 32, 4, True),  # block 0 in all 10000 8-query tiles (wide sort)
 ]
 
 
