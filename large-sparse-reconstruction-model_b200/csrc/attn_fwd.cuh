@@ -73,12 +73,12 @@ struct FwdSmem {
   static constexpr int OFF_Q = 0;                 // two Q tiles (persistent CTAs prefetch the next)
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
-  static constexpr int OFF_XCH = OFF_V + STAGES * TILE;  // row max / row sum exchange [2][2][128]; P is in TMEM
-  static constexpr int OFF_META = OFF_XCH + 4 * 128 * 4;
+  static constexpr int OFF_XCH = OFF_V + STAGES * TILE;  // row max / sum exchange [item parity][max|sum][half][128]
+  static constexpr int OFF_META = OFF_XCH + 2 * 4 * 128 * 4;
   static constexpr int OFF_BAR = OFF_META + STAGES * (int)sizeof(ChunkMeta);
   // barriers: kv_full[S], kv_empty[S], q_full[2], q_empty[2], s_full[2], s_free[2],
-  // p_full[2], p_free[2], pv_full[2], pv_free[2], mma_done, pv_mma_done
-  static constexpr int NBAR = 2 * STAGES + 4 + 12 + 2;
+  // p_full[2], p_free[2], pv_full[2], pv_free[2], mma_done, pv_mma_done, pair[4]
+  static constexpr int NBAR = 2 * STAGES + 4 + 12 + 2 + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_UC = (OFF_MISC + 16 + 15) / 16 * 16;  // select mode: the tile's union
   static constexpr int BYTES = OFF_UC + (int)sizeof(UnionCache);
@@ -89,9 +89,6 @@ struct FwdSmem {
 
 constexpr int kFwdThreads = 352;
 
-__device__ __forceinline__ void pair_bar(int quarter) {
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-}
 
 template <int D, bool BF16, int MODE, int STAGES>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -130,6 +127,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* pv_free = pv_full + 2;
   uint64_t* mma_done = pv_free + 2;
   uint64_t* pv_mma_done = mma_done + 1;
+  uint64_t* pair_mb = pv_mma_done + 1;  // [4]: the two softmax warps of a row quarter met at the item's end
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -177,11 +175,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&s_free[i], 8);
       mbar_init(&p_full[i], 8);
       mbar_init(&p_free[i], 1);
-      mbar_init(&pv_full[i], 1);
+      mbar_init(&pv_full[i], i == 0 ? 8 : 1);  // pv_full[0]: o_free (the softmax warps read O)
       mbar_init(&pv_free[i], 8);
     }
     mbar_init(mma_done, 1);
     mbar_init(pv_mma_done, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_mb[i], 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -193,9 +192,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,128), S1 [128,256), PV0 [256,256+D), PV1 [256+D, 256+2D),
-  // P0 [384,448), P1 [448,512) (16-bit pairs: the A operand of P V)
-  const uint32_t tm_s0 = tmem, tm_pv0 = tmem + 256, tm_p0 = tmem + 384;
+  // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D) and O1 [256+D, 256+2D)
+  // (the output accumulated over keys 0-63 and 64-127 of every chunk, each
+  // half on its own running row max), P0 [384,448), P1 [448,512) (16-bit
+  // pairs: the A operand of P V)
+  const uint32_t tm_s0 = tmem, tm_o0 = tmem + 256, tm_p0 = tmem + 384;
+  uint64_t* o_free = &pv_full[0];  // the softmax warps have read O of the item
 
   if (warp == 8) {
     // ------------------------------ producer ------------------------------
@@ -331,27 +333,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     __syncwarp();
   } else if (warp == 10) {
-    // --------------------------- MMA issuer: O_j = P_j V_j ------------------
-    // S_j is complete once P_j is written (the softmax warps read it first),
-    // so this thread's commit alone releases the chunk's K / V stage.
+    // --------------------------- MMA issuer: O += P_j V_j ------------------
+    // Two accumulations per chunk, O0 += P[:, 0:64] V[0:64] and
+    // O1 += P[:, 64:128] V[64:128] (the two softmax warps of a row quarter
+    // scale their halves independently).  S_j is complete once P_j is written
+    // (the softmax warps read it first), so this thread's commit alone
+    // releases the chunk's K / V stage; its commit on p_free also tells the
+    // softmax warps that O holds chunk j.
     if (lane == 0) {
       const uint32_t idesc_pv = make_idesc(AB, 0, 1, 128, D);
       bool ok = true;
-      int J = 0;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+      int J = 0, it_n = 0;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++it_n) {
         const int n_chunks = item_of(i).n_chunks;
+        // the previous item's O must have been read out before chunk 0 overwrites it
+        if (!mbar_wait(o_free, (it_n & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
         for (int j = 0; j < n_chunks; ++j, ++J) {
           const int pb = J & 1, s = J % STAGES;
           if (!mbar_wait(&p_full[pb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
-          if (!mbar_wait(&pv_free[pb], ((J >> 1) & 1) ^ 1, abort_flag, prm.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t v_base = smem_u32(sV + s * L::TILE);
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint64_t db = make_sdesc(v_base + ks * 16 * RB, L::TILE, 8 * RB, SWZ);
-            umma_f16_ts(tm_pv0 + pb * D, tm_p0 + pb * 64 + ks * 8, db, idesc_pv, ks > 0);
-          }
-          umma_commit(&pv_full[pb]);
+          for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t db = make_sdesc(v_base + (hh * 4 + ks) * 16 * RB, L::TILE, 8 * RB, SWZ);
+              umma_f16_ts(tm_o0 + hh * D, tm_p0 + pb * 64 + hh * 32 + ks * 8, db, idesc_pv,
+                          (j > 0 || ks > 0) ? 1u : 0u);
+            }
           umma_commit(&p_free[pb]);
           umma_commit(&kv_empty[s]);
         }
@@ -362,36 +371,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------ softmax -------------------------------
-    constexpr int DH = D / 2;  // output columns folded by each warp of a pair
+    // Warps w and w+4 share the rows of TMEM lane quarter w & 3 and take key
+    // columns 0-63 and 64-127 of every chunk.  Each keeps its own running row
+    // max m and sum l over its columns and its own output half O_h in TMEM,
+    // so the pair never synchronises inside an item.  The max is lazy: P =
+    // exp2(s - m) may reach 2^8 before O_h and l are rescaled to a new max
+    // (fp32 accumulators, bf16 P keeps its relative precision), which skips
+    // nearly every rescale after the first chunks.  At the end of an item the
+    // pair combines (m, l) once and each warp writes half of the output
+    // columns from both O halves.
+    constexpr int DH = D / 2;         // output columns written by each warp of a pair
+    constexpr float kLazy = 8.f;      // log2 headroom before a rescale
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;  // MMA row
     const int qloc = r / G;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tm_oh = tm_o0 + half * D;  // this warp's output half
     const float sl2 = prm.scale_log2;
     float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);  // [max|sum][half][128]
-    float o[DH];
     bool ok = true;
-    float alpha_prev = 1.f;
 
-    auto fold_pv = [&](int i) -> bool {
-      const int pb = i & 1;
-      if (!warp_wait(&pv_full[pb], (i >> 1) & 1, abort_flag, prm.err)) return false;
-      tc_fence_after();
-      {
-        float pv[DH];
-        tmem_load_cols<DH>(tm_pv0 + pb * D + half * DH + lane_base, pv);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < DH; ++c) o[c] = fmaf(o[c], alpha_prev, pv[c]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pv_free[pb]);
-      return true;
-    };
-
-    int J = 0;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    int J = 0, it_n = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++it_n) {
     const Item w = item_of(it);
     const QTile& tile = w.tile;
     const int n_chunks = w.n_chunks;
@@ -399,9 +400,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int qi = tile.q_start + qloc;
     const bool row_valid = qloc < tile.n_q;
     float m = -INFINITY, l = 0.f;
-    alpha_prev = 1.f;
-#pragma unroll
-    for (int c = 0; c < DH; ++c) o[c] = 0.f;
     for (int j = 0; j < n_chunks; ++j, ++J) {
       const int s = J % STAGES, sb = J & 1;
       if (!warp_wait(&s_full[sb], (J >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
@@ -411,14 +409,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t vm[2];
       const ChunkMeta& mt = meta[s];
       if constexpr (MODE == kSelect) {
-        const int w = qloc >> 5, b = qloc & 31;
+        const int wq = qloc >> 5, b = qloc & 31;
 #pragma unroll
         for (int xx = 0; xx < 2; ++xx) {
           const int x = 2 * half + xx;
           uint32_t e = 0u;
 #pragma unroll
           for (int y = 0; y < 4; ++y)
-            if ((mt.qmask[x * 4 + y][w] >> b) & 1u) e |= 0xffu << (y * 8);
+            if ((mt.qmask[x * 4 + y][wq] >> b) & 1u) e |= 0xffu << (y * 8);
           vm[xx] = e & mt.colmask[x];
         }
       } else {
@@ -448,7 +446,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // every row of the warp attends all 64 columns (rows past the tile do
       // not matter): no per-element masking
       const bool full = __all_sync(0xffffffffu, !row_valid || (vm[0] & vm[1]) == 0xffffffffu);
-      // row max over this half, then over the pair
       float mx = -INFINITY;
       if (full) {
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -463,12 +460,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) mx = fmaxf(mx, ((vm[xx] >> c) & 1u) ? sv[xx][c] : -INFINITY);
       }
-      xch[half * 128 + r] = mx;
-      pair_bar(quarter);
-      mx = fmaxf(xch[r], xch[128 + r]);
-      const float m_new = fmaxf(m, mx * sl2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
+      const float cand = mx * sl2;
+      if (j == 0) {
+        m = cand;  // O_h is overwritten by this chunk's product, l starts at 0
+      } else {
+        const bool need = cand > m + kLazy;
+        if (__any_sync(0xffffffffu, need)) {
+          // rescale this warp's rows of O_h to the new max: the previous
+          // chunk's product into O_h must have landed first
+          const int pj = J - 1;
+          if (!warp_wait(&p_free[pj & 1], (pj >> 1) & 1, abort_flag, prm.err)) { ok = false; break; }
+          tc_fence_after();
+          const float m_new = need ? cand : m;
+          // unchanged rows keep their scale (also m == m_new == -inf: no key
+          // yet); m == -inf with a finite m_new scales zeros by 0
+          const float alpha = (m_new == m) ? 1.f : ex2(m - m_new);
+          l *= alpha;
+          m = m_new;
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 16) {
+            float ov[16];
+            tmem_load_cols<16>(tm_oh + c0 + lane_base, ov);
+            tmem_wait_ld();
+            uint32_t ou[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) ou[c] = __float_as_uint(ov[c] * alpha);
+            tmem_st16(tm_oh + c0 + lane_base, ou);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
       // probabilities -> P: this warp's 64 keys as 16-bit pairs into TMEM
       // columns [half*32, half*32+32) of the P buffer (operand A of P V)
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -502,38 +524,69 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
-      // each warp keeps the row sum of its own columns (same scale m in both);
-      // the halves are added once, after the last chunk
-      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      l = l * alpha + rs;
-      if (j >= 1 && !fold_pv(J - 1)) { ok = false; break; }
-      alpha_prev = alpha;
-      m = m_new;
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
     }
-    if (ok && n_chunks > 0) ok = fold_pv(J - 1);
-    if (ok) {  // both warps of a pair agree on ok: they fail on the same barriers
-      xch[256 + half * 128 + r] = l;
-      pair_bar(quarter);
-      l = xch[256 + r] + xch[256 + 128 + r];  // same order in both warps
-      pair_bar(quarter);                      // the slots are reused by the next item
+    // epilogue: wait for the item's last product, combine the pair's (m, l)
+    // once, and write this warp's output columns from both O halves
+    if (ok && n_chunks > 0) {
+      const int pj = J - 1;
+      ok = warp_wait(&p_free[pj & 1], (pj >> 1) & 1, abort_flag, prm.err);
     }
-    if (ok && row_valid) {
-      const float inv = (l > 0.f) ? 1.f / l : __int_as_float(0x7fc00000);
-      uint8_t* orow =
-          static_cast<uint8_t*>(prm.out) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D + half * DH) * 2;
+    if (ok) {
+      // the pair meets on an mbarrier (a bounded wait, so a partner that
+      // aborted cannot hold this warp); slots alternate by item, and a warp
+      // cannot reach item n+2 before its partner has read item n's values
+      float* xb = xch + (it_n & 1) * 512;
+      xb[half * 128 + r] = m;
+      xb[256 + half * 128 + r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pair_mb[quarter]);
+      ok = warp_wait(&pair_mb[quarter], it_n & 1, abort_flag, prm.err);
+    }
+    if (ok) {
+      const float* xb = xch + (it_n & 1) * 512;
+      const float m0 = xb[r], m1 = xb[128 + r];
+      const float l0 = xb[256 + r], l1 = xb[256 + 128 + r];
+      const float mm = fmaxf(m0, m1);
+      const float c0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mm);
+      const float c1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mm);
+      const float lt = l0 * c0 + l1 * c1;  // same order in both warps
+      float o[DH];
+      if (n_chunks > 0) {
+        float o1[DH];
+        tc_fence_after();
+        tmem_load_cols<DH>(tm_o0 + half * DH + lane_base, o);
+        tmem_load_cols<DH>(tm_o0 + D + half * DH + lane_base, o1);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < DH; c += 8) {
-        uint4 pk;
-        pk.x = pack2<BF16>(o[c] * inv, o[c + 1] * inv);
-        pk.y = pack2<BF16>(o[c + 2] * inv, o[c + 3] * inv);
-        pk.z = pack2<BF16>(o[c + 4] * inv, o[c + 5] * inv);
-        pk.w = pack2<BF16>(o[c + 6] * inv, o[c + 7] * inv);
-        *reinterpret_cast<uint4*>(orow + c * 2) = pk;
+        for (int c = 0; c < DH; ++c) o[c] = o[c] * c0 + o1[c] * c1;
+      } else {
+#pragma unroll
+        for (int c = 0; c < DH; ++c) o[c] = 0.f;
       }
-      if (half == 0) {
-        float lse = (l > 0.f) ? m + __log2f(l) : -INFINITY;
-        if (prm.lse_natural) lse *= 0.69314718055994531f;
-        prm.lse[(size_t)hq * prm.total_q + qi] = lse;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);  // O of this item is read
+      if (row_valid) {
+        const float inv = (lt > 0.f) ? 1.f / lt : __int_as_float(0x7fc00000);
+        uint8_t* orow =
+            static_cast<uint8_t*>(prm.out) + ((size_t)qi * prm.q_tok_stride + (size_t)hq * D + half * DH) * 2;
+        if (dcheck(qi < prm.total_q && hq < prm.num_q_heads, kDcOutRow, prm.err)) {
+#pragma unroll
+          for (int c = 0; c < DH; c += 8) {
+            uint4 pk;
+            pk.x = pack2<BF16>(o[c] * inv, o[c + 1] * inv);
+            pk.y = pack2<BF16>(o[c + 2] * inv, o[c + 3] * inv);
+            pk.z = pack2<BF16>(o[c + 4] * inv, o[c + 5] * inv);
+            pk.w = pack2<BF16>(o[c + 6] * inv, o[c + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 2) = pk;
+          }
+          if (half == 0) {
+            float lse = (lt > 0.f) ? mm + __log2f(lt) : -INFINITY;
+            if (prm.lse_natural) lse *= 0.69314718055994531f;
+            prm.lse[(size_t)hq * prm.total_q + qi] = lse;
+          }
+        }
       }
     }
     }  // items
