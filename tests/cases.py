@@ -70,3 +70,30 @@ def coherent_selection(seed, cu_seqlens, cu_seqblocks, Hkv, topk, jitter=2):
                 perm = torch.randperm(cand.numel(), generator=g)[:kk]
                 out[h, i, :kk] = cand[perm].sort().values.to(torch.int32)
     return out
+
+
+def by_value(obj):
+    """Tensors (nested in tuples, lists, dicts) as numpy arrays: a spawned
+    worker's results then travel through a multiprocessing queue by value,
+    not as shared-memory handles that break when the worker exits before the
+    parent has read them."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().cpu().numpy().copy()
+    if isinstance(obj, dict):
+        return {k: by_value(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(by_value(v) for v in obj)
+    return obj
+
+
+def as_tensors(obj):
+    """The inverse of by_value (numpy arrays back to tensors)."""
+    import numpy as np
+
+    if isinstance(obj, np.ndarray):
+        return torch.from_numpy(obj)
+    if isinstance(obj, dict):
+        return {k: as_tensors(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(as_tensors(v) for v in obj)
+    return obj

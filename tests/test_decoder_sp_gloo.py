@@ -13,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from tests.cases import cu
+from tests.cases import as_tensors, by_value, cu
 
 
 def _free_port():
@@ -48,7 +48,7 @@ def _worker(rank, world, port, vol_lens, img_lens, q):
         (full,), _, _, _, _ = ulysses.seq_parallel_token_blocks([xg], [], m, "collect")
         full.sum().backward()
         res["full"], res["grad"] = full.detach(), xg.grad
-        q.put((rank, res))
+        q.put((rank, by_value(res)))
     finally:
         dist.destroy_process_group()
 
@@ -60,7 +60,7 @@ def _run(world, vol_lens, img_lens):
     ps = [ctx.Process(target=_worker, args=(r, world, port, vol_lens, img_lens, q)) for r in range(world)]
     for p in ps:
         p.start()
-    out = dict(q.get(timeout=120) for _ in ps)
+    out = {r: as_tensors(res) for r, res in (q.get(timeout=120) for _ in ps)}
     for p in ps:
         p.join(60)
         assert p.exitcode == 0

@@ -16,7 +16,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from tests.cases import cu, expand_qblock_selection
+from tests.cases import as_tensors, by_value, cu, expand_qblock_selection
 
 
 def pack_ref(x, world):
@@ -92,7 +92,7 @@ def _worker(rank, world, port, Hq, Hkv, D, lens, topk, window, q_out):
         out = ulysses.three_branch_attention(ql, kl, vl, zl, plan, cu_blk, topk, window, branch_fn=oracle_branches,
                                              pack=pack_ref, unpack=unpack_ref)
         out.backward(dout[s:e])
-        q_out.put((rank, s, e, out.detach(), ql.grad, kl.grad, vl.grad, zl.grad))
+        q_out.put(by_value((rank, s, e, out.detach(), ql.grad, kl.grad, vl.grad, zl.grad)))
     finally:
         dist.destroy_process_group()
 
@@ -105,7 +105,7 @@ def _run(world, Hq, Hkv, D, lens, topk=3, window=16):
              for r in range(world)]
     for p in procs:
         p.start()
-    res = [qq.get(timeout=240) for _ in range(world)]
+    res = [as_tensors(qq.get(timeout=240)) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
