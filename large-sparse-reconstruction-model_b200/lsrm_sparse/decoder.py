@@ -186,29 +186,12 @@ class CrossAttention(nn.Module):
         q_x, k_x, ck_x2x = self._norm(q_x, Hq), self._norm(k_x, Hkv), self._norm(ck_x2x, Hkv)
         k_y, ck_x2y = self._norm(k_y, Hkv), self._norm(ck_x2y, Hkv)
 
-        def to_heads(plan, *ts):
-            """[n_local, H_i*D] tensors sharing a plan -> [N, H_i/W * D] each, in one
-            exchange: each rank's head slices of all of them travel together
-            (rank r receives [its slice of t_0, its slice of t_1, ...])."""
-            n = ts[0].shape[0]
-            parts = [t.reshape(n, W, -1, D) for t in ts]
-            widths = [p_.shape[2] for p_ in parts]
-            both = parts[0] if len(parts) == 1 else torch.cat(parts, 2)
-            h = ulysses.seq_to_head(both.reshape(n, -1, D), plan, group)  # [N, sum(widths), D]
-            return [x.reshape(x.shape[0], -1) for x in torch.split(h, widths, 1)]
+        def to_heads(t, plan, heads):  # [n_local, heads*D] -> [N, heads/W * D]
+            h = ulysses.seq_to_head(t.reshape(t.shape[0], heads, D), plan, group)
+            return h.reshape(h.shape[0], -1)
 
-        def to_tokens(plan, *ts):
-            """[N, hp*D] branch outputs sharing a plan -> [n_local, Hq*D] each, in one
-            exchange (the mirror of to_heads)."""
-            N_ = ts[0].shape[0]
-            both = torch.cat([t.reshape(N_, hp, D) for t in ts], 1)  # [N, k*hp, D]
-            y = ulysses.head_to_seq(both, plan, len(ts) * Hq, group)  # [n_local, W*k*hp, D]
-            y = y.reshape(y.shape[0], W, len(ts), hp, D)
-            return [y[:, :, i].reshape(y.shape[0], Hq * D) for i in range(len(ts))]
-
-        def outputs_to_tokens(o, plan):  # a Mid result dict, both branch outputs in one exchange
-            keys = list(o)
-            return dict(zip(keys, to_tokens(plan, *(o[k] for k in keys))))
+        def to_tokens(t, plan):  # [N, hp*D] -> [n_local, Hq*D]
+            return ulysses.head_to_seq(t.reshape(t.shape[0], hp, D), plan, Hq, group).reshape(-1, Hq * D)
 
         def heads_of(m):  # this rank's kv heads of a map, the whole sequence's block tables
             return {"block_topk": m["block_topk"][k0:k1], "cu_seqblocks": m["cu_seqblocks"],
@@ -218,29 +201,29 @@ class CrossAttention(nn.Module):
         Nx, Ny = sp.vol.total, sp.img.total
         cu_nx = torch.tensor([0, Nx], dtype=torch.int32, device=x.device)
         cu_ny = torch.tensor([0, Ny], dtype=torch.int32, device=x.device)
-        qh_x, kh_x, vh_x = to_heads(sp.vol, q_x, k_x, v_x)
-        kh_y, vh_y = to_heads(sp.img, k_y, v_y)
+        qh_x, kh_x, vh_x = to_heads(q_x, sp.vol, Hq), to_heads(k_x, sp.vol, Hkv), to_heads(v_x, sp.vol, Hkv)
+        kh_y, vh_y = to_heads(k_y, sp.img, Hkv), to_heads(v_y, sp.img, Hkv)
         sparse_info = {}
-        ckh, cvh = to_heads(sp.img_blocks, ck_x2y, cv_x2y)
-        o, sparse_info["v_2_i"] = mid(qh_x, cu_nx, kh_y, ckh, vh_y, cvh, self.topk_multiimage * im_num,
+        o, sparse_info["v_2_i"] = mid(qh_x, cu_nx, kh_y, to_heads(ck_x2y, sp.img_blocks, Hkv), vh_y,
+                                      to_heads(cv_x2y, sp.img_blocks, Hkv), self.topk_multiimage * im_num,
                                       heads_of(m_vi))
-        x_cross_out = outputs_to_tokens(o, sp.vol)
-        ckh, cvh = to_heads(sp.vol_blocks, ck_x2x, cv_x2x)
-        o, sparse_info["v_2_v"] = mid(qh_x, cu_nx, kh_x, ckh, vh_x, cvh, self.topk_volume, heads_of(m_vv))
-        x_self_out = outputs_to_tokens(o, sp.vol)
+        x_cross_out = {k: to_tokens(t, sp.vol) for k, t in o.items()}
+        o, sparse_info["v_2_v"] = mid(qh_x, cu_nx, kh_x, to_heads(ck_x2x, sp.vol_blocks, Hkv), vh_x,
+                                      to_heads(cv_x2x, sp.vol_blocks, Hkv), self.topk_volume, heads_of(m_vv))
+        x_self_out = {k: to_tokens(t, sp.vol) for k, t in o.items()}
         x_cross = self.x_2_y_attn_out(x, q_x, k_y, v_y, m_vi, x_cross_out)
         x_self = self.x_2_x_attn_out(x, q_x, k_x, v_x, m_vv, x_self_out)  # window: local blocks
         x_new = self.proj_x(self._gate(x, self.gate_x, x_cross, x_self))
         if self.oneside:
             return x_new, sparse_info
-        (qh_y,) = to_heads(sp.img, q_y)
-        ckh, cvh = to_heads(sp.vol_blocks, ck_y2x, cv_y2x)
-        o, sparse_info["i_2_v"] = mid(qh_y, cu_ny, kh_x, ckh, vh_x, cvh, self.topk_volume, heads_of(m_iv))
-        y_cross_out = outputs_to_tokens(o, sp.img)
-        ckh, cvh = to_heads(sp.img_blocks, ck_y2y, cv_y2y)
-        o, sparse_info["i_2_i"] = mid(qh_y, cu_ny, kh_y, ckh, vh_y, cvh, self.topk_multiimage * im_num,
+        qh_y = to_heads(q_y, sp.img, Hq)
+        o, sparse_info["i_2_v"] = mid(qh_y, cu_ny, kh_x, to_heads(ck_y2x, sp.vol_blocks, Hkv), vh_x,
+                                      to_heads(cv_y2x, sp.vol_blocks, Hkv), self.topk_volume, heads_of(m_iv))
+        y_cross_out = {k: to_tokens(t, sp.img) for k, t in o.items()}
+        o, sparse_info["i_2_i"] = mid(qh_y, cu_ny, kh_y, to_heads(ck_y2y, sp.img_blocks, Hkv), vh_y,
+                                      to_heads(cv_y2y, sp.img_blocks, Hkv), self.topk_multiimage * im_num,
                                       heads_of(m_ii))
-        y_self_out = outputs_to_tokens(o, sp.img)
+        y_self_out = {k: to_tokens(t, sp.img) for k, t in o.items()}
         y_cross = self.y_2_x_attn_out(y, q_y, k_x, v_x, m_iv, y_cross_out)
         y_self = self.y_2_y_attn_out(y, q_y, k_y, v_y, m_ii, y_self_out)
         y_new = self.proj_y(self._gate(y, self.gate_y, y_cross, y_self))
