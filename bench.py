@@ -241,6 +241,41 @@ def zero_grads(p: Problem):
         t.grad = None
 
 
+def capture_step(step, p, lib_launches):
+    """One whole step — forward, backward, every gradient — captured as a CUDA
+    graph, so replaying it costs one launch on the host instead of issuing
+    each kernel (and, under sequence parallelism, each NCCL exchange) from
+    Python.  The gradients are None when the capture starts, so the captured
+    backward writes them into buffers of the graph's pool and every replay
+    recomputes them there.  Returns (graph, launches of this library's kernels
+    per replay)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # the allocator and the libraries settle on the capture stream first
+        for _ in range(2):
+            step(p)
+            zero_grads(p)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = lib_launches()
+    # thread_local: NCCL's watchdog thread keeps polling its events during the capture
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        step(p)
+    return graph, lib_launches() - n0
+
+
+def grads_of(p):
+    return [t.grad for t in [p.q, p.k, p.v, p.x] + (p.params() if hasattr(p, "params") else [p.wg])]
+
+
+def _eager_grads(step, p):
+    zero_grads(p)
+    step(p)
+    torch.cuda.synchronize()
+    return grads_of(p)
+
+
 def count_pairs(p: Problem, bt: torch.Tensor):
     """Attended (query, key) pairs per head of the three branches."""
     lens = torch.tensor(p.lens, dtype=torch.int64)
@@ -493,6 +528,35 @@ def run_ours(args, cfg):
         if ws > 1:
             torch.distributed.barrier()
 
+    # ---- the step as a CUDA graph (checked against the eager step's gradients) ----
+    graph, graph_launches, graph_note = None, 0, "eager (--eager)"
+    if not args.eager:
+        ok = 1
+        try:
+            ref = [None if g is None else g.clone() for g in _eager_grads(step, p)]
+            graph, graph_launches = capture_step(step, p, lib_launches)
+            graph.replay()
+            torch.cuda.synchronize()
+            same = all((a is None and b is None) or (a is not None and b is not None and torch.equal(a, b))
+                       for a, b in zip(ref, grads_of(p)))
+            if not same:
+                raise RuntimeError("graph replay gradients differ from the eager step's")
+            del ref
+            graph_note = "CUDA graph of the whole step (forward + backward), replayed once per step; its " \
+                         "gradients equal the eager step's bit for bit"
+        except Exception as e:  # a call on the path refused the capture: time the eager step
+            print(f"CUDA graph capture not used ({e}); timing the eager step", file=sys.stderr, flush=True)
+            graph, ok, graph_note = None, 0, f"eager (graph capture failed: {str(e)[:120]})"
+        if ws > 1:  # every rank replays or none does
+            t = torch.tensor([ok], dtype=torch.int32, device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            if int(t.item()) == 0 and graph is not None:
+                graph, graph_note = None, "eager (graph capture failed on another rank)"
+        if graph is None:
+            zero_grads(p)
+        for _ in range(2 if graph is not None else 0):  # warm replays
+            graph.replay()
+
     # ---- timed pass (device time, CUDA events on the compute stream) ----
     stream = torch.cuda.current_stream()
     torch.cuda.synchronize()
@@ -502,12 +566,18 @@ def run_ours(args, cfg):
     with ClockSampler(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            step(p)
-            zero_grads(p)
+            if graph is not None:
+                graph.replay()
+            else:
+                step(p)
+                zero_grads(p)
         ev1.record(stream)
         torch.cuda.synchronize()
-    launches = lib_launches() - n0
+    launches = lib_launches() - n0 + graph_launches * (args.steps if graph is not None else 0)
+    _check_device_errors(ops)
     barrier()
+    if graph is not None:
+        zero_grads(p)  # the eager passes below allocate their own gradients
     if rank == 0:
         print(f"device memory: {torch.cuda.max_memory_allocated(dev) / 2**30:.2f} GiB allocated at peak",
               file=sys.stderr, flush=True)
@@ -660,6 +730,9 @@ def run_ours(args, cfg):
         cpu = cpu_sample(p, args.cpu_qblocks, args.seed)
         cpu.pop("seconds", None)
 
+    # a graph holding NCCL calls is released before the process group goes
+    graph = None
+    torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -681,6 +754,7 @@ def run_ours(args, cfg):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": int(launches),
+        "timed_step": graph_note,
         "clocks": clk.summary(),
         "exchange": exchange,
         "kernels": kernels,
@@ -1476,6 +1550,7 @@ def main():
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time the eager step instead of its CUDA graph")
     ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack",
                                        "view_block_topk", "decoder"],
                     default="attention",
