@@ -8,20 +8,75 @@
 namespace lsrm {
 
 // Sums the split partials of dK/dV in split order (deterministic) and casts.
+constexpr int kReduceRows = 16;
 template <bool BF16, int D>
 __global__ void dkdv_reduce_kernel_d(DkvParams p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  const int kt_idx = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
+  // grid (KV tile, kv head, 2 x row groups of kReduceRows): every thread sums
+  // 4 consecutive channels of one row over the splits, in split order
+  const int kt_idx = blockIdx.x, h = blockIdx.y, which = blockIdx.z & 1, rg = blockIdx.z >> 1;
   if (kt_idx >= *p.n_kvtiles) return;
   const QTile kt = p.kvtiles[kt_idx];
   T* out = static_cast<T*>(which == 0 ? p.dk : p.dv);
-  for (int i = threadIdx.x; i < kt.n_q * D; i += blockDim.x) {
-    const int r = i / D, d = i % D;
-    float acc = 0.f;
-    for (int sp = 0; sp < p.n_split; ++sp)
-      acc += p.partial[((((size_t)which * p.n_split + sp) * p.hkv + h) * p.kvtiles_ub + kt_idx) * 128 * D +
-                       (size_t)r * D + d];
-    out[(size_t)(kt.q_start + r) * p.kv_tok_stride + (size_t)h * D + d] = (T)acc;
+  const size_t split_stride = (size_t)p.hkv * p.kvtiles_ub * 128 * D;
+  const float* base = p.partial + ((((size_t)which * p.n_split) * p.hkv + h) * p.kvtiles_ub + kt_idx) * 128 * D;
+  const int r_end = min(kt.n_q, (rg + 1) * kReduceRows);
+  for (int i = threadIdx.x; i < kReduceRows * D / 4; i += blockDim.x) {
+    const int r = rg * kReduceRows + (i * 4) / D, d = (i * 4) % D;
+    if (r >= r_end) break;
+    const float* src = base + (size_t)r * D + d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < p.n_split; ++sp) {
+      const float4 x = *reinterpret_cast<const float4*>(src + sp * split_stride);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    T* o = out + (size_t)(kt.q_start + r) * p.kv_tok_stride + (size_t)h * D + d;
+    o[0] = (T)acc.x;
+    o[1] = (T)acc.y;
+    o[2] = (T)acc.z;
+    o[3] = (T)acc.w;
+  }
+}
+
+// Select mode: dK / dV of every item that was cut into pieces = the sum of
+// its pieces' fp32 slots in piece order (deterministic), cast.  grid (split
+// item, 2 x row groups of kReduceRows).
+template <bool BF16, int D>
+__global__ void dkdv_piece_reduce_kernel(DkvParams p) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int k = blockIdx.x;
+  if (k >= p.sched_ctr[2]) return;
+  const int4 si = p.split_items[k];
+  const int item = si.x, slot0 = si.y, pieces = si.z;
+  if (!dcheck(item >= 0 && item < p.hkv * p.kvtiles_ub && slot0 >= 0 && pieces >= 1 &&
+                  slot0 + pieces <= p.piece_slots,
+              kDcChunks, p.err))
+    return;
+  const int h = item / p.kvtiles_ub, kt_idx = item - h * p.kvtiles_ub;
+  const QTile kt = p.kvtiles[kt_idx];
+  const int which = blockIdx.y & 1, rg = blockIdx.y >> 1;
+  T* out = static_cast<T*>(which == 0 ? p.dk : p.dv);
+  const int r_end = min(kt.n_q, (rg + 1) * kReduceRows);
+  for (int i = threadIdx.x; i < kReduceRows * D / 4; i += blockDim.x) {
+    const int r = rg * kReduceRows + (i * 4) / D, d = (i * 4) % D;
+    if (r >= r_end) break;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int pc = 0; pc < pieces; ++pc) {
+      const float4 x = *reinterpret_cast<const float4*>(p.piece_partial +
+                                                        (((size_t)(slot0 + pc) * 2 + which) * 128 + r) * D + d);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    T* o = out + (size_t)(kt.q_start + r) * p.kv_tok_stride + (size_t)h * D + d;
+    o[0] = (T)acc.x;
+    o[1] = (T)acc.y;
+    o[2] = (T)acc.z;
+    o[3] = (T)acc.w;
   }
 }
 
@@ -75,19 +130,25 @@ static int launch_dkdv_t(const CUtensorMap& mk, const CUtensorMap& mv, const CUt
   using L = DkvSmem<D, STAGES>;
   auto kern = attn_dkdv_kernel<D, BF16, MODE, STAGES>;
   LSRM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC));
+  DkvParams pp = p;
+  pp.hkv = hkv;
   {
     ProfScope ps(MODE == kSelect ? "attn_dkdv_select" : (MODE == kBand ? "attn_dkdv_sliding" : "attn_dkdv_range"), s);
     // persistent: one CTA per SM walks the work items
-    DkvParams pp = p;
-    pp.hkv = hkv;
-    const long long items = (long long)grid_x * hkv * (p.kv_sched ? 1 : p.n_split);
+    const long long items = p.kv_sched ? (long long)grid_x * hkv + p.piece_slots : (long long)grid_x * hkv * p.n_split;
     const int grid = (int)std::min<long long>(items, num_sms());
     kern<<<dim3(grid, 1), kDkvThreads, L::ALLOC, s>>>(mk, mv, mq, mdo, qm, pp);
     LSRM_LAUNCH_CHECK();
   }
+  if (p.kv_sched && p.piece_slots > 0) {
+    ProfScope ps("dkdv_piece_reduce", s);
+    dkdv_piece_reduce_kernel<BF16, D>
+        <<<dim3(std::max(p.piece_slots / 2, 1), 2 * (128 / kReduceRows)), 256, 0, s>>>(pp);
+    LSRM_LAUNCH_CHECK();
+  }
   if (p.n_split > 1) {
     ProfScope ps("dkdv_split_reduce", s);
-    dkdv_reduce_kernel_d<BF16, D><<<dim3(grid_x, hkv, 2), 256, 0, s>>>(p);
+    dkdv_reduce_kernel_d<BF16, D><<<dim3(grid_x, hkv, 2 * (128 / kReduceRows)), 256, 0, s>>>(p);
     LSRM_LAUNCH_CHECK();
   }
   return LSRM_OK;
@@ -186,7 +247,7 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
   if ((rc = launch_build_tiles(plan.kvtiles, plan.n_kvtiles, plan.kvtiles_ub, kTilesKVBlock, kRows, meta, nullptr,
                                meta->num_blocks, 0, err, s)))
     return rc;
-  if ((rc = launch_build_kv_schedule(plan, G, s))) return rc;
+  if ((rc = launch_build_kv_schedule(plan, G, num_sms(), s))) return rc;
   const float scale = softmax_scale_of(shape);
   // dQ (+ delta)
   {
@@ -248,6 +309,12 @@ extern "C" int lsrm_select_attn_bwd(const lsrm_varlen* meta, const lsrm_attn_sha
     p.n_split = 1;
     p.kv_sched = plan.kv_sched;
     p.item_nch = plan.item_nch;
+    p.item_rng = plan.item_rng;
+    p.item_src = plan.item_src;
+    p.piece_partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.bytes + 256);
+    p.split_items = plan.split_items;
+    p.sched_ctr = plan.sched_ctr;
+    p.piece_slots = plan.piece_slots;
     p.kv_tok_stride = shape->kv_token_stride;
     p.total_q = meta->total_q;
     p.total_k = meta->total_k;

@@ -576,8 +576,14 @@ struct DkvParams {
   void* dv;
   float* partial;  // [split][hkv][kvtiles_ub][128][D] x 2 when n_split > 1
   int n_split;
-  const int* kv_sched;  // select mode: work items (h * kvtiles_ub + tile), heaviest first
-  const int* item_nch;  // select mode: query chunks of each work item
+  const int* kv_sched;  // select mode: work entries, heaviest first (items, then pieces of long items)
+  const int* item_nch;  // select mode: query chunks of each work entry
+  const int2* item_rng; // select mode: {first entry, entries} of the block's list; x < 0: item split
+  const int* item_src;  // select mode: the item of each piece
+  float* piece_partial; // select mode: [piece_slots][2][128][D] fp32 dK / dV of each piece
+  const int4* split_items;  // select mode: {item, first slot, pieces, 0}
+  const int* sched_ctr;     // select mode: [2] = number of split items
+  int piece_slots;
   long long kv_tok_stride;
   int total_q;
   int total_k;
@@ -788,7 +794,8 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   // the next item's loads overlap the current item's tail.
   const int G = prm.G;
   const int qpc = kKvQRows / G;  // queries per chunk (gather path)
-  const int n_items = prm.kv_sched ? prm.hkv * prm.kvtiles_ub : prm.hkv * prm.kvtiles_ub * prm.n_split;
+  const int n_items = prm.kv_sched ? prm.hkv * prm.kvtiles_ub + prm.piece_slots
+                                   : prm.hkv * prm.kvtiles_ub * prm.n_split;
   const int n_kv = *prm.n_kvtiles;
 
   extern __shared__ uint8_t smem_raw[];
@@ -821,15 +828,36 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
   struct KvItem {
     QTile kt;
     int kt_idx, h, split, n_chunks, q_lo, q_hi;
+    int slot, e_lo, e_cnt;  // select mode: piece slot (-1: the whole item) and its run of the list
     bool skip;
   };
   auto item_of = [&](int i) {
     KvItem it;
     it.split = 0;
+    it.slot = -1;
+    it.e_lo = it.e_cnt = 0;
+    int sched_e = 0;
     if (prm.kv_sched) {
-      const int e = prm.kv_sched[i];
-      it.h = e / prm.kvtiles_ub;
-      it.kt_idx = e - it.h * prm.kvtiles_ub;
+      const int n_whole = prm.hkv * prm.kvtiles_ub;
+      sched_e = prm.kv_sched[i];
+      int src = sched_e;
+      if (!dcheck((unsigned)sched_e < (unsigned)(n_whole + prm.piece_slots), kDcKvTile, prm.err)) {
+        it.skip = true;
+        return it;
+      }
+      if (sched_e >= n_whole) {
+        it.slot = sched_e - n_whole;
+        src = prm.item_src[it.slot];
+      }
+      const int2 rg = prm.item_rng[sched_e];
+      if (rg.x < 0 || !dcheck((unsigned)src < (unsigned)n_whole, kDcKvTile, prm.err)) {  // split, or unused
+        it.skip = true;
+        return it;
+      }
+      it.e_lo = rg.x;
+      it.e_cnt = rg.y;
+      it.h = src / prm.kvtiles_ub;
+      it.kt_idx = src - it.h * prm.kvtiles_ub;
     } else {
       const int per_h = prm.kvtiles_ub * prm.n_split;
       it.h = i / per_h;
@@ -851,7 +879,7 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
       return it;
     }
     if constexpr (MODE == kSelect) {
-      it.n_chunks = prm.item_nch[(size_t)it.h * prm.kvtiles_ub + it.kt_idx];
+      it.n_chunks = prm.item_nch[sched_e];
       if (!dcheck(it.n_chunks >= 0, kDcChunks, prm.err)) it.n_chunks = 0;
     } else {
       const int nq = max(it.q_hi - it.q_lo, 0);
@@ -946,6 +974,14 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         const int* off = prm.rev_off + (size_t)h * (prm.num_blocks + 1);
         e_first = off[kt.seg];
         e_count = off[kt.seg + 1] - e_first;
+        if (w.slot >= 0) {  // a piece: its run of the list
+          if (!dcheck(w.e_lo >= 0 && w.e_cnt >= 0 && w.e_lo + w.e_cnt <= e_count, kDcRevRange, prm.err))
+            e_count = 0;
+          else {
+            e_first += w.e_lo;
+            e_count = w.e_cnt;
+          }
+        }
         if (!dcheck(e_first >= 0 && e_count >= 0 &&
                         (long long)e_first + e_count <= (long long)prm.tiles_ub * prm.union_cap,
                     kDcRevRange, prm.err))
@@ -1326,7 +1362,12 @@ __global__ void __launch_bounds__(kDkvThreads, 1)
         for (int cc = 0; cc < D; ++cc) v[cc] = 0.f;
       }
       if (row_valid && dcheck(kidx < prm.total_k, kDcKvOut, prm.err)) {
-        if (prm.n_split > 1) {
+        if (MODE == kSelect && w.slot >= 0) {  // a piece: fp32 into its slot, summed after the launch
+          float* dst_p = prm.piece_partial + (((size_t)w.slot * 2 + which) * 128 + r) * D;
+#pragma unroll
+          for (int cc = 0; cc < D; cc += 4)
+            *reinterpret_cast<float4*>(dst_p + cc) = make_float4(v[cc], v[cc + 1], v[cc + 2], v[cc + 3]);
+        } else if (prm.n_split > 1) {
           float* dst_p = prm.partial +
                          ((((size_t)which * prm.n_split + split) * prm.hkv + h) * prm.kvtiles_ub + kt_idx) * 128 * D +
                          (size_t)r * D;

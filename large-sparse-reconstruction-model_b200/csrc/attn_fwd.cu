@@ -70,7 +70,7 @@ extern "C" size_t lsrm_select_workspace_bytes(const lsrm_varlen* meta, const lsr
   int G = 1;
   if (check_shape(meta, shape, G) != LSRM_OK || topk < 1) return 0;
   SelectPlan p = make_select_plan(meta, G, shape->num_kv_heads, topk, num_query_blocks, nullptr);
-  return p.bytes + 256;  // + internal error word
+  return p.bytes + 256 + piece_partial_bytes(p, shape->head_dim);  // + internal error word, dK/dV pieces
 }
 
 extern "C" int lsrm_select_attn_fwd(const lsrm_varlen* meta, const lsrm_attn_shape* shape, const void* q,

@@ -25,42 +25,66 @@ struct Vec8 {
 };
 
 // ----------------------------- block mean ----------------------------------
-// grid: blocks; threads cover the channels 8 at a time.
+// grid: blocks; 256 threads = kMeanCg channel groups of 8 x (256 / kMeanCg)
+// token slices (cg = tid % cgp, slice = tid / cgp, cgp a power of two >= the
+// channel groups, at most 256).  Slice s sums tokens t0 + s, t0 + s + slices,
+// ...; slice 0 then adds the slices' sums in slice order.
+constexpr int kMeanThreads = 256;
 template <typename T>
-__global__ void block_mean_fwd_kernel(const int32_t* __restrict__ cu, const T* __restrict__ x, long long x_stride,
-                                      T* __restrict__ out, int C, int nb) {
+__global__ void __launch_bounds__(kMeanThreads)
+    block_mean_fwd_kernel(const int32_t* __restrict__ cu, const T* __restrict__ x, long long x_stride,
+                          T* __restrict__ out, int C, int nb, int cgp) {
+  __shared__ float part[kMeanThreads * 8];
   const int b = blockIdx.x;
   if (b >= nb) return;
   const int t0 = cu[b], t1 = cu[b + 1];
   const float inv = t1 > t0 ? 1.f / (float)(t1 - t0) : __int_as_float(0x7fc00000);
-  for (int c = threadIdx.x * 8; c < C; c += blockDim.x * 8) {
+  const int cg = threadIdx.x % cgp, sl = threadIdx.x / cgp, slices = kMeanThreads / cgp;
+  for (int cb = 0; cb < C; cb += cgp * 8) {
+    const int c = cb + cg * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int t = t0;
-    for (; t + 4 <= t1; t += 4) {
-      Vec8<T> v[4];
+    if (c < C) {
+      int t = t0 + sl;
+      for (; t + 3 * slices < t1; t += 4 * slices) {
+        Vec8<T> v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u].raw = *reinterpret_cast<const uint4*>(x + (size_t)(t + u) * x_stride + c);
+        for (int u = 0; u < 4; ++u)
+          v[u].raw = *reinterpret_cast<const uint4*>(x + (size_t)(t + u * slices) * x_stride + c);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 4; ++u) {
+          float f[8];
+          v[u].to_float(f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += f[i];
+        }
+      }
+      for (; t < t1; t += slices) {
+        Vec8<T> v;
+        v.raw = *reinterpret_cast<const uint4*>(x + (size_t)t * x_stride + c);
         float f[8];
-        v[u].to_float(f);
+        v.to_float(f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] += f[i];
       }
     }
-    for (; t < t1; ++t) {
-      Vec8<T> v;
-      v.raw = *reinterpret_cast<const uint4*>(x + (size_t)t * x_stride + c);
-      float f[8];
-      v.to_float(f);
+    if (slices > 1) {
+      __syncthreads();  // the previous channel round's partial sums are consumed
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += f[i];
+      for (int i = 0; i < 8; ++i) part[threadIdx.x * 8 + i] = acc[i];
+      __syncthreads();
+      if (sl == 0) {
+        for (int s2 = 1; s2 < slices; ++s2)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += part[(s2 * cgp + cg) * 8 + i];
+      }
     }
+    if (sl == 0 && c < C) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] *= inv;
-    Vec8<T> o;
-    o.from_float(acc);
-    *reinterpret_cast<uint4*>(out + (size_t)b * C + c) = o.raw;
+      for (int i = 0; i < 8; ++i) acc[i] *= inv;
+      Vec8<T> o;
+      o.from_float(acc);
+      *reinterpret_cast<uint4*>(out + (size_t)b * C + c) = o.raw;
+    }
   }
 }
 
@@ -354,11 +378,12 @@ extern "C" int lsrm_block_mean_fwd(int32_t num_blocks, int32_t channels, int32_t
   LSRM_CHECK_ARG(x_stride % 8 == 0, "x row stride must be a multiple of 8 elements");
   if (num_blocks <= 0) return LSRM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int threads = std::min(256, std::max(32, (channels / 8 + 31) / 32 * 32));
+  int cgp = 1;  // channel groups of 8, rounded up to a power of two, at most the block's threads
+  while (cgp < channels / 8 && cgp < kMeanThreads) cgp *= 2;
   ProfScope ps("block_mean_fwd", s);
-  DISPATCH_T(dtype, (block_mean_fwd_kernel<T><<<num_blocks, threads, 0, s>>>(
+  DISPATCH_T(dtype, (block_mean_fwd_kernel<T><<<num_blocks, kMeanThreads, 0, s>>>(
                         cu_block_include_tokens, static_cast<const T*>(x), x_stride, static_cast<T*>(out), channels,
-                        num_blocks)));
+                        num_blocks, cgp)));
   LSRM_LAUNCH_CHECK();
   return LSRM_OK;
 }

@@ -439,10 +439,18 @@ SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int 
   p.rev_off = reinterpret_cast<int*>(take(sizeof(int) * hkv * ((size_t)m->num_blocks + 1)));
   p.rev_cursor = reinterpret_cast<int*>(take(sizeof(int) * hkv * (size_t)std::max(m->num_blocks, 1)));
   p.rev_entries = reinterpret_cast<int2*>(take(sizeof(int2) * ent));
-  p.kv_sched = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
-  p.sched_key = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
-  p.item_nch = reinterpret_cast<int*>(take(sizeof(int) * (size_t)hkv * p.kvtiles_ub));
+  const size_t items = (size_t)hkv * p.kvtiles_ub;
+  p.piece_slots = (int)std::min<size_t>(kMaxPieceSlots, items);
+  const size_t entries = items + p.piece_slots;
+  p.kv_sched = reinterpret_cast<int*>(take(sizeof(int) * entries));
+  p.sched_key = reinterpret_cast<int*>(take(sizeof(int) * entries));
+  p.item_nch = reinterpret_cast<int*>(take(sizeof(int) * entries));
+  p.item_rng = reinterpret_cast<int2*>(take(sizeof(int2) * entries));
+  p.item_src = reinterpret_cast<int*>(take(sizeof(int) * p.piece_slots));
+  p.item_slot = reinterpret_cast<int*>(take(sizeof(int) * items));
   p.sched_bins = reinterpret_cast<int*>(take(sizeof(int) * 2 * kSchedBins));
+  p.sched_ctr = reinterpret_cast<int*>(take(sizeof(int) * 4));
+  p.split_items = reinterpret_cast<int4*>(take(sizeof(int4) * p.piece_slots));
   p.bytes = (size_t)(cur - base);
   return p;
 }
@@ -503,56 +511,186 @@ int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t
   return LSRM_OK;
 }
 
-// dK/dV schedule: every (kv head, KV tile) item gets a bucket by its number
-// of 64-query chunks (the queries that selected the tile's block), and the
-// items are listed heaviest bucket first, so the longest CTAs start early
-// instead of trailing the launch.  Order inside a bucket is arbitrary; it
-// does not change any result.
-// The chunk count follows the dK/dV kernel's rule: the block's reverse list
-// runs in segments of kRevCacheCap entries (one shared-memory cache fill
-// each); within a segment, G <= 8 runs in 8-row query groups (chunks of 8
-// groups), G > 8 in chunks of 64/G gathered queries.  One warp per item: the
-// lanes stride over each segment's entries.
-__global__ void sched_key_kernel(SelectPlan p, int G) {
-  const int items = p.hkv * p.kvtiles_ub;
-  const int n_kv = *p.n_kvtiles;
+// dK/dV schedule.  Every (kv head, KV tile) item gets its number of 64-query
+// chunks (the queries that selected the tile's block); an item much longer
+// than the average load of one CTA is cut into pieces (runs of its reverse
+// list, each accumulated into its own fp32 slot and summed afterwards in
+// piece order), and the work entries are listed heaviest bucket first, so the
+// longest CTAs start early instead of trailing the launch.  Order inside a
+// bucket is arbitrary; it does not change any result.
+// The chunk count follows the dK/dV kernel's rule: a run of the block's
+// reverse list is read in segments of kRevCacheCap entries from its first
+// entry (one shared-memory cache fill each); within a segment, G <= 8 runs in
+// 8-row query groups (chunks of 8 groups), G > 8 in chunks of 64/G gathered
+// queries.  One warp per item: the lanes stride over each segment's entries.
+__device__ __forceinline__ int run_chunks(const SelectPlan& p, int h, int e0, int e1, int G) {
   const int qpc = 64 / G, W = G <= 8 ? 8 / G : 1;
   const int lane = threadIdx.x & 31;
+  const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
+  const bool grouped = G <= 8;
+  int chunks = 0;
+  for (int s0 = e0; s0 < e1; s0 += kRevCacheCap) {
+    const int s1 = min(e1, s0 + kRevCacheCap);
+    int nq = 0, ng = 0;
+    for (int e = s0 + lane; e < s1; e += 32) {
+      const int2 x = ent[e];
+      const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
+      nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+      if (grouped) ng += window_count(m, W);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      nq += __shfl_xor_sync(0xffffffffu, nq, o);
+      ng += __shfl_xor_sync(0xffffffffu, ng, o);
+    }
+    chunks += grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
+  }
+  return chunks;
+}
+
+__device__ __forceinline__ int sched_bin(int chunks) { return kSchedBins - 1 - min(chunks, kSchedBins - 1); }
+
+// Pass 1: chunks of every item (whole list), their total; the piece entries
+// start empty.
+__global__ void sched_count_kernel(SelectPlan p, int G) {
+  const int items = p.hkv * p.kvtiles_ub;
+  const int n_kv = *p.n_kvtiles;
+  const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < p.piece_slots; j += gridDim.x * blockDim.x) {
+    p.item_nch[items + j] = 0;
+    p.item_rng[items + j] = make_int2(-1, 0);
+    p.sched_key[items + j] = kSchedBins - 1;
+    p.item_src[j] = 0;
+  }
   for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < items; i += warps) {
     const int h = i / p.kvtiles_ub, kt = i - h * p.kvtiles_ub;
-    int bin = kSchedBins - 1;  // empty / unused items last
-    int chunks = 0;
+    int chunks = 0, e0 = 0, e1 = 0;
     if (kt < n_kv) {
       const int blk = p.kvtiles[kt].seg;
       const int* off = p.rev_off + (size_t)h * (p.num_blocks + 1);
-      const int2* ent = p.rev_entries + (size_t)h * p.tiles_ub * p.union_cap;
-      const int e0 = off[blk], e1 = off[blk + 1];
-      const bool grouped = G <= 8;
-      for (int s0 = e0; s0 < e1; s0 += kRevCacheCap) {
-        const int s1 = min(e1, s0 + kRevCacheCap);
-        int nq = 0, ng = 0;
-        for (int e = s0 + lane; e < s1; e += 32) {
-          const int2 x = ent[e];
-          const uint4 m = p.union_mask[((size_t)h * p.tiles_ub + x.x) * p.union_cap + x.y];
-          nq += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
-          if (grouped) ng += window_count(m, W);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          nq += __shfl_xor_sync(0xffffffffu, nq, o);
-          ng += __shfl_xor_sync(0xffffffffu, ng, o);
-        }
-        chunks += grouped ? (ng + 7) / 8 : (nq + qpc - 1) / qpc;
-      }
-      bin = kSchedBins - 1 - min(chunks, kSchedBins - 1);
+      e0 = off[blk];
+      e1 = off[blk + 1];
+      chunks = run_chunks(p, h, e0, e1, G);
     }
     if (lane == 0) {
-      p.sched_key[i] = bin;
       p.item_nch[i] = chunks;
-      atomicAdd(&p.sched_bins[bin], 1);
+      p.item_rng[i] = make_int2(0, e1 - e0);
+      if (chunks) atomicAdd(&p.sched_ctr[0], chunks);
     }
   }
+}
+
+// Pieces of one item: an item of more than half the average load of a CTA
+// (total / 2 ctas chunks, at least 2 * kMinPieceChunks) is cut into up to
+// kMaxPieces runs of equal entry counts, each about that long — the CTAs walk
+// the heaviest-first list in a fixed snake order, so no single entry may hold
+// much more than half a CTA's share.  1: the item stays whole.
+__device__ __forceinline__ int item_pieces(int nch, int n_ent, bool valid, int target, int* per) {
+  *per = n_ent;
+  if (!valid || nch <= target || nch < 2 * kMinPieceChunks) return 1;
+  const int want = min(min(kMaxPieces, (nch + target - 1) / target), min(n_ent, nch / kMinPieceChunks));
+  if (want <= 1) return 1;
+  *per = (n_ent + want - 1) / want;
+  return (n_ent + *per - 1) / *per;
+}
+
+__device__ __forceinline__ int piece_target(const SelectPlan& p, int ctas) {
+  return max((p.sched_ctr[0] + 2 * ctas - 1) / (2 * ctas), kMinPieceChunks);
+}
+
+// Pass 2 (one block): piece slots in item order — an exclusive scan of the
+// pieces of every item to be cut; an item whose pieces would pass the last
+// slot stays whole.  The choice depends on the item order alone, so the
+// schedule (and every sum) is the same from run to run.
+constexpr int kSlotThreads = 1024;
+__global__ void __launch_bounds__(kSlotThreads) sched_slots_kernel(SelectPlan p, int ctas) {
+  __shared__ int wsum[32];
+  const int items = p.hkv * p.kvtiles_ub;
+  const int n_kv = *p.n_kvtiles;
+  const int target = piece_target(p, ctas);
+  const int per_t = (items + kSlotThreads - 1) / kSlotThreads;
+  const int i0 = threadIdx.x * per_t, i1 = min(items, i0 + per_t);
+  auto pieces_of = [&](int i) {
+    const int kt = i % p.kvtiles_ub;
+    int per;
+    const int pc = item_pieces(p.item_nch[i], p.item_rng[i].y, kt < n_kv, target, &per);
+    return pc > 1 ? pc : 0;
+  };
+  int own = 0;
+  for (int i = i0; i < i1; ++i) own += pieces_of(i);
+  // block exclusive scan of `own`
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int incl = own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int x = wsum[lane];
+    int xi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += y;
+    }
+    wsum[lane] = xi - x;
+  }
+  __syncthreads();
+  int pre = wsum[w] + incl - own;
+  for (int i = i0; i < i1; ++i) {
+    const int pc = pieces_of(i);
+    p.item_slot[i] = pc > 0 && pre + pc <= p.piece_slots ? pre : -1;
+    pre += pc;
+  }
+}
+
+// Pass 3: the pieces of every item given slots (their runs, chunk counts and
+// buckets); every item gets its bucket.
+__global__ void sched_split_kernel(SelectPlan p, int G, int ctas) {
+  const int items = p.hkv * p.kvtiles_ub;
+  const int n_kv = *p.n_kvtiles;
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const int target = piece_target(p, ctas);
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < items; i += warps) {
+    const int h = i / p.kvtiles_ub, kt = i - h * p.kvtiles_ub;
+    const int nch = p.item_nch[i];
+    const int n_ent = p.item_rng[i].y;
+    const int slot0 = p.item_slot[i];
+    if (slot0 < 0) {
+      if (lane == 0) p.sched_key[i] = kt < n_kv ? sched_bin(nch) : kSchedBins - 1;
+      continue;
+    }
+    int per;
+    const int pieces = item_pieces(nch, n_ent, kt < n_kv, target, &per);
+    const int e0 = p.rev_off[(size_t)h * (p.num_blocks + 1) + p.kvtiles[kt].seg];
+    for (int k = 0; k < pieces; ++k) {
+      const int lo = k * per, cnt = min(per, n_ent - lo);
+      const int c = run_chunks(p, h, e0 + lo, e0 + lo + cnt, G);
+      if (lane == 0) {
+        const int j = items + slot0 + k;
+        p.item_nch[j] = c;
+        p.item_rng[j] = make_int2(lo, cnt);
+        p.item_src[slot0 + k] = i;
+        p.sched_key[j] = sched_bin(c);
+      }
+    }
+    if (lane == 0) {
+      p.item_rng[i] = make_int2(-1, 0);
+      p.sched_key[i] = kSchedBins - 1;
+      p.split_items[atomicAdd(&p.sched_ctr[2], 1)] = make_int4(i, slot0, pieces, 0);
+    }
+  }
+}
+
+__global__ void sched_bins_kernel(SelectPlan p) {
+  const int entries = p.hkv * p.kvtiles_ub + p.piece_slots;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < entries; j += gridDim.x * blockDim.x)
+    atomicAdd(&p.sched_bins[p.sched_key[j]], 1);
 }
 
 __global__ void sched_scan_kernel(SelectPlan p) {
@@ -583,19 +721,28 @@ __global__ void sched_scan_kernel(SelectPlan p) {
 }
 
 __global__ void sched_scatter_kernel(SelectPlan p) {
-  const int items = p.hkv * p.kvtiles_ub;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
+  const int entries = p.hkv * p.kvtiles_ub + p.piece_slots;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < entries; i += gridDim.x * blockDim.x) {
     const int pos = atomicAdd(&p.sched_bins[kSchedBins + p.sched_key[i]], 1);
     p.kv_sched[pos] = i;
   }
 }
 
-int launch_build_kv_schedule(const SelectPlan& p, int G, cudaStream_t s) {
+int launch_build_kv_schedule(const SelectPlan& p, int G, int ctas, cudaStream_t s) {
   ProfScope ps("plan_schedule", s);
   LSRM_CUDA_TRY(cudaMemsetAsync(p.sched_bins, 0, sizeof(int) * kSchedBins, s));
+  LSRM_CUDA_TRY(cudaMemsetAsync(p.sched_ctr, 0, sizeof(int) * 4, s));
   const int items = p.hkv * p.kvtiles_ub;
-  const int grid = std::min((items + 255) / 256, 148 * 8);
-  sched_key_kernel<<<std::min((items + 7) / 8, 148 * 16), 256, 0, s>>>(p, G);  // 8 items (warps) per block
+  const int entries = items + p.piece_slots;
+  const int grid = std::min((entries + 255) / 256, 148 * 8);
+  const int warp_grid = std::min((items + 7) / 8, 148 * 16);  // 8 items (warps) per block
+  sched_count_kernel<<<warp_grid, 256, 0, s>>>(p, G);
+  LSRM_LAUNCH_CHECK();
+  sched_slots_kernel<<<1, kSlotThreads, 0, s>>>(p, std::max(ctas, 1));
+  LSRM_LAUNCH_CHECK();
+  sched_split_kernel<<<warp_grid, 256, 0, s>>>(p, G, std::max(ctas, 1));
+  LSRM_LAUNCH_CHECK();
+  sched_bins_kernel<<<grid, 256, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();
   sched_scan_kernel<<<1, kSchedBins, 0, s>>>(p);
   LSRM_LAUNCH_CHECK();

@@ -57,6 +57,7 @@ struct SelectPlan {
   int kvtiles_ub;    // capacity of the KV tile list
   int hkv;
   int num_blocks;
+  int piece_slots;   // dK/dV work entries for the pieces of long items
   // device pointers into the workspace
   QTile* tiles;
   int* n_tiles;            // [1]
@@ -69,12 +70,25 @@ struct SelectPlan {
   int* rev_off;            // [hkv][num_blocks+1]
   int* rev_cursor;         // [hkv][num_blocks]
   int2* rev_entries;       // [hkv][tiles_ub*cap] (tile, union entry index)
-  int* kv_sched;           // [hkv*kvtiles_ub] dK/dV work items (h*kvtiles_ub + tile), heaviest first
-  int* item_nch;           // [hkv*kvtiles_ub] query chunks of each dK/dV work item
-  int* sched_key;          // [hkv*kvtiles_ub] bucket of each item
+  // dK/dV work entries: e < hkv*kvtiles_ub is the item (kv head, KV tile)
+  // e = h*kvtiles_ub + tile over the block's whole reverse list; e =
+  // hkv*kvtiles_ub + slot is a piece of a long item (a run of its list,
+  // accumulated into its own fp32 slot and summed afterwards)
+  int* kv_sched;           // [entries] work entries, heaviest first
+  int* item_nch;           // [entries] query chunks of each entry
+  int2* item_rng;          // [entries] {first entry, entries} of the block's list; x < 0: split into pieces
+  int* item_src;           // [piece_slots] the item each piece belongs to
+  int* item_slot;          // [hkv*kvtiles_ub] first piece slot of an item that is cut, else -1
+  int* sched_key;          // [entries] bucket of each entry
   int* sched_bins;         // [2*kSchedBins] bucket counts, then cursors
+  int* sched_ctr;          // [4] chunks of all items, 0, split items, 0
+  int4* split_items;       // [piece_slots] {item, first slot, pieces, 0} of every split item
   size_t bytes;
 };
+
+constexpr int kMaxPieceSlots = 256;  // pieces of long dK/dV items per launch
+constexpr int kMaxPieces = 8;        // pieces of one item
+constexpr int kMinPieceChunks = 8;   // no piece shorter than this many chunks
 
 constexpr int kSchedBins = 1024;  // dK/dV schedule buckets (query chunks, capped)
 
@@ -120,6 +134,11 @@ struct DensePlan {
   size_t bytes;
 };
 
+// fp32 dK and dV of every piece slot: [piece_slots][2][kRows][D].
+inline size_t piece_partial_bytes(const SelectPlan& p, int D) {
+  return (size_t)p.piece_slots * 2 * kRows * D * sizeof(float);
+}
+
 // Host helpers (plan.cu).
 SelectPlan make_select_plan(const lsrm_varlen* m, int G, int hkv, int topk, int num_qblocks, void* ws);
 DensePlan make_dense_plan(const lsrm_varlen* m, int G, int mode, void* ws);
@@ -130,6 +149,6 @@ int launch_build_tiles(QTile* tiles, int* n_tiles, int tiles_ub, int kind, int r
 int launch_build_unions(const SelectPlan& p, const lsrm_varlen* m, const int32_t* block_topk, int topk,
                         int sel_rows, int G, int* err, cudaStream_t s);
 int launch_build_reverse(const SelectPlan& p, int* err, cudaStream_t s);
-int launch_build_kv_schedule(const SelectPlan& p, int G, cudaStream_t s);
+int launch_build_kv_schedule(const SelectPlan& p, int G, int ctas, cudaStream_t s);
 
 }  // namespace lsrm
