@@ -674,9 +674,12 @@ def run_ours(args, cfg):
                 t.record_stream(stream)
             p.adopt(ts)
 
-        # one untimed round trip first: the allocator then holds the buffers of
-        # two steps' inputs (the prefetch keeps two alive)
-        for _ in range(2):
+        # untimed round trips first: the allocator then holds the buffers of
+        # two steps' inputs (the prefetch keeps two alive) next to the CUDA
+        # graph's private pool; the first eager steps after the capture run
+        # 3-5x slower while it grows (measured on one B200: 128, 87, 87, 118,
+        # 75 ms, then 26 ms per step)
+        for _ in range(max(6, args.warmup)):
             take(fetch())
             nxt_w = fetch()
             loss = step(p, want_loss=True)
