@@ -1388,6 +1388,7 @@ def decoder_problem(seed, n_vol, dev):
         m["block_topk"] = m["block_topk"][:1].expand(c["kv_heads"], -1, -1).contiguous()
     torch.cuda.synchronize()
     map_ms = (time.perf_counter() - t0) * 1e3
+    maps["_vol_index"], maps["_im_index"] = volc.contiguous(), imc.contiguous()  # the whole decoder's inputs
     return maps, volc.shape[0], imc.shape[0], shell, map_ms
 
 
@@ -1421,16 +1422,37 @@ def run_decoder(args):
     maps, nx, ny, shell, map_ms = decoder_problem(args.seed, n_req, dev)
     torch.manual_seed(args.seed)  # the same weights on every rank
     n_layers = args.decoder_layers or c["layers"]
-    layers = torch.nn.ModuleList(
-        BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
-                 topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1)
-        for _ in range(n_layers)
-    ).to(dev).to(torch.bfloat16)
+    full = args.decoder_model == "full"
+    if full:  # the whole decoder; its forward distributes and collects the tokens itself
+        from lsrm_sparse.decoder import VolTransformer
+
+        skips = tuple(i for i in (17, 11, 4) if i < n_layers)
+        layers = VolTransformer(vol_res=c["volume_res"], upsample_scale=2, embed_dim=c["dim"], output_dim=32,
+                                depth=n_layers, num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"],
+                                mlp_ratio=c["mlp_ratio"], skip_links=skips, topk_volume=c["topk_volume"],
+                                topk_multiimage=c["topk_multiimage"], use_decomposed_embed=True,
+                                use_sequence_parallel=ws > 1).to(dev).to(torch.bfloat16)
+    else:
+        layers = torch.nn.ModuleList(
+            BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
+                     topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1)
+            for _ in range(n_layers)
+        ).to(dev).to(torch.bfloat16)
     opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     x_in = torch.randn(nx, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
     y_in = torch.randn(ny, c["dim"], device=dev, dtype=torch.bfloat16, generator=gen)
-    if ws > 1:
+    if full:
+        # x_in stands for the prior volume features (only the fuse_all_layers variant reads them); the
+        # decoder embeds the voxel tokens itself
+        vol_index, im_index = maps.pop("_vol_index"), maps.pop("_im_index")
+        prior_volume = torch.zeros(1, 32, 4, 4, 4, device=dev)
+        params = list(layers.parameters())
+    else:
+        maps.pop("_vol_index"), maps.pop("_im_index")
+    if full:
+        pass
+    elif ws > 1:
         # sequence parallel: this rank's whole blocks of both token sets (the reference's distribute step)
         (x_in,), (y_in,), cu_x, cu_y, maps = ulysses.seq_parallel_token_blocks([x_in], [y_in], maps, "distribute")
         x_in, y_in = x_in.contiguous(), y_in.contiguous()
@@ -1442,10 +1464,14 @@ def run_decoder(args):
 
     def step(x, y):
         opt.zero_grad(set_to_none=True)
-        for blk in layers:  # one checkpoint per block (the reference's cp_freq = 1)
-            x, y, _ = cp.checkpoint(blk, x, cu_x, y, cu_y, maps, c["views"], use_reentrant=False)
-        # the loss of the whole token set: every rank's share over the global counts
-        loss = x.float().square().sum() / nx + y.float().square().sum() / ny
+        if full:  # embedding, layers (one checkpoint each, cp_freq = 1), upsampler, output formatting
+            out, _ = layers(y, [y], im_index, x, None, vol_index, prior_volume, None, maps, c["views"])
+            loss = out["sparse_feat"].float().square().mean()  # the same collected volume on every rank
+        else:
+            for blk in layers:  # one checkpoint per block (the reference's cp_freq = 1)
+                x, y, _ = cp.checkpoint(blk, x, cu_x, y, cu_y, maps, c["views"], use_reentrant=False)
+            # the loss of the whole token set: every rank's share over the global counts
+            loss = x.float().square().sum() / nx + y.float().square().sum() / ny
         loss.backward()
         if ws > 1:  # weights are replicated: sum the ranks' gradients in one flat exchange
             grads = [p.grad for p in params]
@@ -1525,6 +1551,8 @@ def run_decoder(args):
         scaling="strong", vs_baseline=None, dtype="bf16", exchange=exchange,
         config={"parallelism": f"Ulysses sequence parallel over {ws} GPUs (whole blocks per rank, all-to-all "
                                "around the attention cores, gradients all-reduced)" if ws > 1 else "single GPU",
+                "model": "VolTransformer: decomposed position embedding, the layers and 3 one-sided skip blocks, "
+                         "LayerNorm, upsampler (x2, 32 channels), output formatting" if full else "BlockMix stack",
                 "workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
                             f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
                             f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
@@ -1569,6 +1597,9 @@ def main():
                     "reference's production model uses 32,2 at hidden 1024, i.e. head_dim 32)")
     ap.add_argument("--torch-profile", action="store_true",
                     help="--path decoder: print torch.profiler's per-kernel table of one extra step on stderr")
+    ap.add_argument("--decoder-model", choices=["blocks", "full"], default="blocks",
+                    help="--path decoder: the BlockMix stack alone, or the whole VolTransformer (position "
+                         "embedding, layers + skip blocks, norm, upsampler, output formatting)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]

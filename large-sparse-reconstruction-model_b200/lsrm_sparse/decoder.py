@@ -6,6 +6,10 @@ path):
 * ``CrossAttention``  — :108-574: volume tokens x and image tokens y, each
   attending to both sets through SpatialSparseAttentionIn / Mid / Out
 * ``BlockMix``        — :575-640, ``BlockMixOneside`` — :643-705
+* ``VolUpsampler``    — models_sparse/voldecoder.py:18-36
+* ``VolTransformer``  — models_sparse/voldecoder.py:39-424: position
+  embedding, the layer loop with skip links and one-sided skip blocks, the
+  final norm, the upsampler and the output formatting
 
 Constructor arguments, forward signatures, return values and parameter names
 are the reference's, so its state dicts load (weight-normed Linears keep the
@@ -268,3 +272,206 @@ class BlockMixOneside(BlockMix):
         super().__init__(dim, num_q_heads, num_kv_heads, mlp_ratio, qkv_bias, act_layer, norm_layer, use_weight_norm,
                          topk_volume, topk_multiimage, use_sequence_parallel, no_checkpoint_all_gather,
                          oneside=True)
+
+
+# ---------------------------------------------------------------------------
+# The whole volume decoder: embedding, layer loop with skip blocks, upsampler,
+# output formatting (models_sparse/voldecoder.py)
+# ---------------------------------------------------------------------------
+
+
+class VolUpsampler(nn.Module):
+    """models_sparse/voldecoder.py:18-36: one Linear from the token width to
+    ``output_dim * upsample_scale**3`` sub-voxel features (channel-major per
+    token, the layout ``prepare_volume_output`` reads)."""
+
+    def __init__(self, upsample_scale, embed_dim=1024, output_dim=32, use_weight_norm=False):
+        super().__init__()
+        self.output_dim = output_dim
+        self.upsample_scale = upsample_scale
+        self.dconv3d = nn.Linear(embed_dim, output_dim * (upsample_scale ** 3))
+        if use_weight_norm:
+            self.dconv3d = nn.utils.parametrizations.weight_norm(self.dconv3d)
+
+    def forward(self, volume):
+        return self.dconv3d(volume)
+
+
+def batch_cu_seqlens(batch_ids: torch.Tensor, batch_size: int) -> torch.Tensor:
+    """int32 [batch_size + 1] offsets of the runs of equal ids in ``batch_ids``
+    (grouped by ascending batch id, as the reference assumes), found on the
+    device; the reference walks the id gaps with one ``.item()`` per batch
+    element (models_sparse/voldecoder.py:318-337)."""
+    b = batch_ids.to(torch.int64).contiguous()
+    probe = torch.arange(batch_size + 1, device=b.device, dtype=torch.int64)
+    return torch.searchsorted(b, probe).to(torch.int32)
+
+
+class VolTransformer(nn.Module):
+    """models_sparse/voldecoder.py:39-424 over this package's decoder blocks.
+
+    Same constructor arguments, parameter names (``pos_embed`` or
+    ``pos_embed_{x,y,z}``, ``cross_blocks``, ``skip_blocks``,
+    ``skip_fuse_prior_imfeats``, ``fuse_prior_*``, ``fuse_pred_volfeat``,
+    ``norm``, ``upsampler.dconv3d``), initialisation rule and forward
+    signature, so the reference's checkpoints load and its callers run
+    unchanged.  Differences inside: the batch offsets are found on the device
+    (``batch_cu_seqlens``) instead of one host read per batch element; the
+    ``fuse_all_layers`` output gate ``x * g[:, :C] + prior * g[:, C:]`` is the
+    fused two-branch ``gate_merge``; ``prepare_volume_output`` is the one-call
+    ``lsrm_prepare_volume_output``; under ``use_sequence_parallel`` the token
+    distribution and the final collect are ``ulysses.seq_parallel_token_blocks``
+    and the blocks exchange heads (Ulysses) instead of all-gathering K/V."""
+
+    def __init__(self, vol_res=64, upsample_scale=4, embed_dim=1024, output_dim=32, depth=24, num_q_heads=32,
+                 num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, cp_freq=1, use_weight_norm=False,
+                 skip_links=(17, 11, 4), topk_volume=8, topk_multiimage=2, use_decomposed_embed=False,
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, fuse_all_layers=False):
+        super().__init__()
+        import math
+
+        self.topk_multiimage = topk_multiimage
+        self.topk_volume = topk_volume
+        self.depth = depth
+        self.embed_dim = embed_dim
+        self.vol_res = vol_res
+        self.upsample_scale = upsample_scale
+        self.output_dim = output_dim
+        self.num_token = vol_res * vol_res * vol_res
+        self.fuse_all_layers = fuse_all_layers
+        self.use_decomposed_embed = use_decomposed_embed
+        self.use_sequence_parallel = use_sequence_parallel
+        self.no_checkpoint_all_gather = no_checkpoint_all_gather
+        scale = 1.0 / math.sqrt(float(embed_dim))
+        if use_decomposed_embed:  # one table per axis, concatenated z | y | x
+            self.embed_dim_z = embed_dim // 3
+            self.embed_dim_x = (embed_dim - self.embed_dim_z) // 2
+            self.embed_dim_y = embed_dim - self.embed_dim_z - self.embed_dim_x
+            self.pos_embed_x = nn.Parameter(torch.randn(1, vol_res, self.embed_dim_x) * scale)
+            self.pos_embed_y = nn.Parameter(torch.randn(1, vol_res, self.embed_dim_y) * scale)
+            self.pos_embed_z = nn.Parameter(torch.randn(1, vol_res, self.embed_dim_z) * scale)
+        else:
+            self.pos_embed = nn.Parameter(torch.randn(1, self.num_token, embed_dim) * scale)
+        blk_kw = dict(num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, mlp_ratio=mlp_ratio, qkv_bias=qkv_bias,
+                      norm_layer=LayerNorm32, use_weight_norm=use_weight_norm, topk_volume=topk_volume,
+                      topk_multiimage=topk_multiimage, use_sequence_parallel=use_sequence_parallel,
+                      no_checkpoint_all_gather=no_checkpoint_all_gather)
+        fuse_imfeat_ratio = len(skip_links) + 1
+        self.fuse_prior_volfeats = nn.ModuleList(
+            [nn.Linear(embed_dim, embed_dim, bias=False) for _ in range(depth)] if fuse_all_layers else [])
+        self.fuse_prior_imfeats = nn.ModuleList(
+            [nn.Linear(embed_dim * fuse_imfeat_ratio, embed_dim, bias=False) for _ in range(depth)]
+            if fuse_all_layers else [])
+        self.cross_blocks = nn.ModuleList([BlockMix(dim=embed_dim, **blk_kw) for _ in range(depth)])
+        self.skip_links = skip_links
+        skip_vol, skip_im = [], []
+        for n in range(len(skip_links)):
+            if fuse_all_layers:
+                skip_vol.append(nn.Linear(embed_dim, embed_dim, bias=False))
+                skip_im.append(nn.Linear(embed_dim * (fuse_imfeat_ratio + 1), embed_dim, bias=False))
+            elif n == 0:
+                skip_im.append(nn.Linear(embed_dim, embed_dim, bias=False))
+        self.skip_fuse_prior_volfeats = nn.ModuleList(skip_vol)
+        self.skip_fuse_prior_imfeats = nn.ModuleList(skip_im)
+        self.skip_blocks = nn.ModuleList([BlockMixOneside(dim=embed_dim, **blk_kw) for _ in skip_links])
+        if fuse_all_layers:
+            self.fuse_pred_volfeat = nn.Linear(embed_dim, 2 * embed_dim, bias=False)
+        self.norm = LayerNorm32(embed_dim)
+        self.upsampler = VolUpsampler(upsample_scale=upsample_scale, embed_dim=embed_dim, output_dim=output_dim,
+                                      use_weight_norm=use_weight_norm)
+        self.apply(self._init_weights)
+        self.cp_freq = int(cp_freq)
+
+    @staticmethod
+    def _init_weights(m):
+        """The reference's rule (voldecoder.py:183-193): Linear weights from a
+        normal of std 0.02 truncated to [-2, 2], biases 0; LayerNorm weight 1,
+        bias 0."""
+        if isinstance(m, nn.Linear):
+            nn.init.trunc_normal_(m.weight, std=0.02, a=-2.0, b=2.0)
+            if m.bias is not None:
+                nn.init.constant_(m.bias, 0)
+        elif isinstance(m, nn.LayerNorm):
+            if m.bias is not None:
+                nn.init.constant_(m.bias, 0)
+            if m.weight is not None:
+                nn.init.constant_(m.weight, 1.0)
+
+    def prepare_volume_output(self, volume, volume_index, prior_volume):
+        from .volume import prepare_volume_output
+
+        return prepare_volume_output(volume, volume_index, prior_volume, self.output_dim, self.upsample_scale,
+                                     self.vol_res)
+
+    def embed(self, volume_index, mask_volume, volume_coords_idx, batch_size, dtype):
+        """Position embedding of the voxel tokens (voldecoder.py:285-299):
+        three per-axis tables gathered by the (z, y, x) columns of
+        ``volume_index`` and concatenated, or the full table's rows of the
+        voxels ``mask_volume`` keeps (a flat mask over ``batch_size`` copies
+        of the volume), reordered by ``volume_coords_idx``."""
+        if self.use_decomposed_embed:
+            vi = volume_index.long()
+            return torch.cat([self.pos_embed_z[0].index_select(0, vi[:, 1]),
+                              self.pos_embed_y[0].index_select(0, vi[:, 2]),
+                              self.pos_embed_x[0].index_select(0, vi[:, 3])], dim=-1)
+        rows = torch.nonzero(mask_volume.reshape(-1)).squeeze(1)
+        rows = rows.index_select(0, volume_coords_idx.reshape(-1).long()) % self.num_token
+        return self.pos_embed[0].to(dtype=dtype).index_select(0, rows)
+
+    def _run(self, blk, *args):
+        import torch.utils.checkpoint as cp
+
+        return cp.checkpoint(blk, *args, use_reentrant=False)
+
+    def forward(self, y, prior_imfeat_list, image_index, prior_volfeat, mask_volume, volume_index, prior_volume,
+                volume_coords_idx, attn_map, im_num):
+        batch_size = int(image_index[:, 0].max().item()) + 1
+        x = self.embed(volume_index, mask_volume, volume_coords_idx, batch_size, y.dtype)
+        prior_imfeat = torch.cat(prior_imfeat_list, dim=1)
+        if self.use_sequence_parallel:
+            from .ulysses import seq_parallel_token_blocks
+
+            vol = [x] if prior_volfeat is None else [x, prior_volfeat]
+            vol, (y, prior_imfeat), cu_vol, cu_img, attn_map = seq_parallel_token_blocks(
+                vol, [y, prior_imfeat], attn_map, mode="distribute")
+            x, prior_volfeat = vol[0], (vol[1] if len(vol) > 1 else None)
+        else:
+            cu_vol = batch_cu_seqlens(volume_index[:, 0], batch_size)
+            cu_img = batch_cu_seqlens(image_index[:, 0], batch_size)
+        y_list, sparse_info_arr = [], []
+        for idx, blk in enumerate(self.cross_blocks):
+            if self.fuse_all_layers:
+                x = x + self.fuse_prior_volfeats[idx](prior_volfeat)
+                y = y + self.fuse_prior_imfeats[idx](prior_imfeat)
+            args = (x, cu_vol, y, cu_img, attn_map, im_num)
+            if self.cp_freq > 0 and idx % self.cp_freq == 0:
+                x, y, sparse_info = self._run(blk, *args)
+            else:
+                x, y, sparse_info = blk(*args)
+            if idx in self.skip_links:
+                y_list.insert(0, y)
+            sparse_info_arr.append(sparse_info)
+        y_list.insert(0, y)
+        for n, blk in enumerate(self.skip_blocks):
+            if self.fuse_all_layers:
+                x = x + self.skip_fuse_prior_volfeats[n](prior_volfeat)
+                y = y_list[n + 1] + self.skip_fuse_prior_imfeats[n](torch.cat([y_list[0], prior_imfeat], dim=1))
+            elif n == 0:
+                y = y_list[n + 1] + self.skip_fuse_prior_imfeats[n](y_list[0])
+            else:
+                y = y_list[n + 1]
+            args = (x, cu_vol, y, cu_img, attn_map, im_num)
+            if self.cp_freq > 0 and n % self.cp_freq == 0:
+                x, sparse_info = self._run(blk, *args)
+            else:
+                x, sparse_info = blk(*args)
+            sparse_info_arr.append(sparse_info)
+        if self.fuse_all_layers:  # x * g[:, :C] + prior * g[:, C:], g = sigmoid(fuse_pred_volfeat(x)), fused
+            x = F.gate_merge(self.fuse_pred_volfeat(x), [x, prior_volfeat.to(x.dtype)])
+        x = self.norm(x)
+        volume = self.upsampler(x)
+        if self.use_sequence_parallel:
+            from .ulysses import seq_parallel_token_blocks
+
+            (volume,), _, _, _, _ = seq_parallel_token_blocks([volume], [], attn_map, mode="collect")
+        return self.prepare_volume_output(volume, volume_index, prior_volume), sparse_info_arr

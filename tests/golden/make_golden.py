@@ -21,8 +21,9 @@ What runs, all unmodified reference code:
   (misc/sparse_utils.py:653-1200) on posed views of a sphere scene from
   ``lsrm_sparse.synth.view_scene`` (``--only image``).
 * the state-dict layout of ``BlockMix`` / ``BlockMixOneside``
-  (models_sparse/utils.py:575-705) with and without weight norm
-  (``--only modules``, ``module_keys.json``).
+  (models_sparse/utils.py:575-705) with and without weight norm, and of
+  ``VolTransformer`` (models_sparse/voldecoder.py:39-194) with the decomposed
+  and the full position embedding (``--only modules``, ``module_keys.json``).
 * ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
   without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
   for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
@@ -371,16 +372,30 @@ MODULE_CASES = [  # (name, BlockMix kwargs): small dims, the reference's layer l
 ]
 
 
-def make_module_keys(utils):
+VOLT_CASES = [  # (name, VolTransformer kwargs): small dims, the reference's decoder layout
+    ("voltransformer_decomposed", dict(vol_res=8, upsample_scale=2, embed_dim=64, output_dim=8, depth=3,
+                                       num_q_heads=4, num_kv_heads=2, skip_links=(1,), use_decomposed_embed=True)),
+    ("voltransformer_fuse_all_weight_norm", dict(vol_res=4, upsample_scale=2, embed_dim=64, output_dim=4, depth=3,
+                                                 num_q_heads=4, num_kv_heads=4, skip_links=(2, 0),
+                                                 fuse_all_layers=True, use_weight_norm=True, qkv_bias=True)),
+]
+
+
+def make_module_keys(utils, voldecoder=None):
     """State-dict layout (parameter name -> shape) of the reference's
     ``BlockMix`` / ``BlockMixOneside`` (models_sparse/utils.py:575-705), which
-    holds ``CrossAttention`` (:80-240, weight norm at :228-236) and ``Mlp``."""
+    holds ``CrossAttention`` (:80-240, weight norm at :228-236) and ``Mlp``,
+    and of ``VolTransformer`` (models_sparse/voldecoder.py:39-194)."""
     out = {}
     for name, kw in MODULE_CASES:
         kw = dict(kw)
         cls = utils.BlockMixOneside if kw.pop("oneside", False) else utils.BlockMix
         m = cls(**kw)
         out[name] = {k: list(v.shape) for k, v in m.state_dict().items()}
+    if voldecoder is not None:
+        for name, kw in VOLT_CASES:
+            m = voldecoder.VolTransformer(**kw)
+            out[name] = {k: list(v.shape) for k, v in m.state_dict().items()}
     return out
 
 
@@ -398,10 +413,10 @@ def main():
     if args.only == "modules":
         import json
 
-        from models_sparse import utils
+        from models_sparse import utils, voldecoder
 
         with open(os.path.join(HERE, "module_keys.json"), "w") as f:
-            json.dump(make_module_keys(utils), f, indent=1, sort_keys=True)
+            json.dump(make_module_keys(utils, voldecoder), f, indent=1, sort_keys=True)
         print("wrote module_keys.json")
         return
     if args.only == "imsort":

@@ -22,19 +22,28 @@ def _cos(a, b):
     return float((a @ b) / (a.norm() * b.norm() + 1e-30))
 
 
-def _scene():
+def _scene_coords():
+    """Voxel tokens (batch, z, y, x) of a two-sphere shell in a 32^3 volume,
+    Morton-block order, and the image tokens (batch, view, row, column) of 4
+    posed 64^2 views; returns (volc, imc, view scene)."""
     from lsrm_sparse import blocks, synth
 
     spheres = ((2, 3), (0.2, 0.3))
     centres, radii = synth.scene_spheres(5, *spheres)
-    M, H, S, ps, bs = 4, 64, 32, 4, 4
-    sc = synth.view_scene(centres, radii, 1, M, H, S, 6)
-    im = synth.image_tokens(sc["mask_input"], ps, bs)
+    sc = synth.view_scene(centres, radii, 1, 4, 64, 32, 6)
+    im = synth.image_tokens(sc["mask_input"], 4, 4)
     vox, _ = synth.sdf_shell_voxels(32, 1800, 5, *spheres)
     vol = np.stack([np.zeros(len(vox)), vox[:, 2], vox[:, 1], vox[:, 0]], 1).astype(np.int32)
     volc = torch.from_numpy(vol).to(DEV)
-    volc = volc[torch.argsort(blocks.volume_sort_keys(volc, 32, bs), stable=True)].contiguous()
-    imc = torch.from_numpy(im).to(DEV)
+    volc = volc[torch.argsort(blocks.volume_sort_keys(volc, 32, 4), stable=True)].contiguous()
+    return volc, torch.from_numpy(im).to(DEV), sc
+
+
+def _scene():
+    from lsrm_sparse import blocks
+
+    M, H, ps, bs = 4, 64, 4, 4
+    volc, imc, sc = _scene_coords()
     args = types.SimpleNamespace(block_size=bs, volume_res=32, use_3d_aware_attn=True, topk_volume=8,
                                  bbox_radius=0.5, attn_winsize=2, topk_multiimage=2, image_num_per_batch=M,
                                  input_image_res=[H // 2, H], patch_size=ps)
