@@ -26,10 +26,16 @@ from . import functional as F
 
 
 class LayerNorm32(nn.LayerNorm):
-    """residual_block.py:11-13: LayerNorm evaluated in fp32, cast back."""
+    """residual_block.py:11-13: LayerNorm evaluated in fp32, cast back.  An
+    affine one also evaluates its weight and bias in fp32, so a module cast to
+    bf16 as a whole (``.to(torch.bfloat16)``) still runs (the reference's
+    fp32 LayerNorm rejects bf16 parameters); with fp32 parameters the result
+    is the reference's."""
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return super().forward(x.float()).type(x.dtype)
+        w = None if self.weight is None else self.weight.float()
+        b = None if self.bias is None else self.bias.float()
+        return nn.functional.layer_norm(x.float(), self.normalized_shape, w, b, self.eps).type(x.dtype)
 
 
 class SparseResBlock(nn.Module):

@@ -117,14 +117,30 @@ def time_exchanges(on: bool = True) -> Optional[ExchangeTimer]:
     return _timer
 
 
+def _host_staged(t: torch.Tensor, group) -> bool:
+    """Device tensors exchanged over a gloo group go through host memory
+    (gloo's all-to-all and all-gather take host tensors only): ranks that share
+    one GPU, or a machine without NCCL, still run the sequence-parallel path."""
+    return t.is_cuda and dist.get_backend(group) == "gloo"
+
+
+def _all_to_all(recv, send, out_splits, in_splits, group):
+    if _host_staged(recv, group):
+        r = torch.empty(recv.shape, dtype=recv.dtype)
+        dist.all_to_all_single(r, send.cpu(), out_splits, in_splits, group=group)
+        recv.copy_(r)
+        return
+    dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+
+
 def _a2a(recv: torch.Tensor, send: torch.Tensor, out_splits, in_splits, group, rank: int):
     t = _timer
     if t is None or not recv.is_cuda:
-        dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+        _all_to_all(recv, send, out_splits, in_splits, group)
         return
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+    _all_to_all(recv, send, out_splits, in_splits, group)
     e1.record()
     el = recv.element_size()
     t.records.append((e0, e1, (sum(in_splits) - in_splits[rank]) * el, (sum(out_splits) - out_splits[rank]) * el))
@@ -364,7 +380,12 @@ class _Collect(torch.autograd.Function):
         pad = x.new_zeros((n_max,) + tuple(x.shape[1:]))
         pad[: x.shape[0]] = x
         full = x.new_empty((plan.world * n_max,) + tuple(x.shape[1:]))
-        dist.all_gather_into_tensor(full, pad.contiguous(), group=group)
+        if _host_staged(x, group):
+            f = torch.empty(full.shape, dtype=full.dtype)
+            dist.all_gather_into_tensor(f, pad.cpu(), group=group)
+            full.copy_(f)
+        else:
+            dist.all_gather_into_tensor(full, pad.contiguous(), group=group)
         ctx.plan = plan
         return torch.cat([full[r * n_max: r * n_max + c] for r, c in enumerate(plan.counts)])
 

@@ -4,7 +4,9 @@
 cores), against the same block run on one GPU over all tokens: every rank's
 outputs, its tokens' input gradients and the rank-summed weight gradients
 within 2e-2 (relative to the tensor's scale) and >= 0.9995 cosine.  Runs the
-ranks as child processes; skipped with fewer than 2 GPUs."""
+ranks as child processes: over NCCL on 2 GPUs (skipped with fewer), and over
+gloo with both ranks on one GPU (the exchanges staged through host memory),
+so a one-GPU machine checks the per-rank path as well."""
 
 import os
 import subprocess
@@ -21,9 +23,13 @@ CHILD = r'''
 import os, sys, datetime, copy, torch, torch.distributed as dist
 sys.path[:0] = [ROOT, os.path.join(ROOT, "large-sparse-reconstruction-model_b200")]
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-torch.cuda.set_device(rank)
-dev = torch.device("cuda", rank)
-dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+BACKEND = "BK"  # nccl: one GPU per rank; gloo: every rank on GPU 0, exchanges through host memory
+dev = torch.device("cuda", rank if BACKEND == "nccl" else 0)
+torch.cuda.set_device(dev)
+if BACKEND == "nccl":
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+else:
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 from tests.test_gpu_decoder import _scene
 from lsrm_sparse import decoder, ulysses, ops
 dim, Hq, Hkv = 128, 4, HKV
@@ -52,7 +58,12 @@ sx, sy, _ = sp_blk(xl, cxl, yl, cyl, smaps, M)
 torch.cuda.synchronize()
 assert ops.read_errors() == 0
 for p in sp_blk.parameters():
-    dist.all_reduce(p.grad)
+    if BACKEND == "nccl":
+        dist.all_reduce(p.grad)
+    else:
+        c = p.grad.float().cpu()
+        dist.all_reduce(c)
+        p.grad.copy_(c)
 ok = True
 def close(name, a, b):
     global ok
@@ -71,19 +82,24 @@ for (n, a), (_, b) in zip(sp_blk.named_parameters(), ref_blk.named_parameters())
 (full,), _, _, _, _ = ulysses.seq_parallel_token_blocks([sx.detach()], [], smaps, "collect")
 close("collect", full[vs:ve], sx)
 ok = ok and full.shape[0] == nx
-flag = torch.tensor([int(ok)], device=dev)
+flag = torch.tensor([int(ok)], device=dev if BACKEND == "nccl" else "cpu")
 dist.all_reduce(flag, op=dist.ReduceOp.MIN)
 dist.destroy_process_group()
 sys.exit(0 if flag.item() == 1 else 3)
 '''
 
 
+@pytest.mark.parametrize("backend", ["nccl", "gloo_one_gpu"])
 @pytest.mark.parametrize("hkv", [4, 2])
-def test_sequence_parallel_blockmix_matches_single_gpu(hkv, tmp_path):
-    if torch.cuda.device_count() < 2:
+def test_sequence_parallel_blockmix_matches_single_gpu(hkv, backend, tmp_path):
+    """``nccl``: two GPUs; ``gloo_one_gpu``: both ranks on one GPU with the
+    exchanges staged through host memory (the same per-rank code path, so a
+    one-GPU machine checks it too)."""
+    if backend == "nccl" and torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     script = tmp_path / "child.py"
-    script.write_text(CHILD.replace("ROOT", repr(ROOT)).replace("HKV", str(hkv)))
+    script.write_text(CHILD.replace("ROOT", repr(ROOT)).replace("HKV", str(hkv))
+                      .replace('"BK"', repr(backend.split("_")[0])))
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29534", str(script)]

@@ -2,7 +2,9 @@
 the single-GPU whole-sequence op bit for bit (heads are computed by the same
 kernels), and its gradients agree within the bf16 tolerance (the compressed
 branch's dK/dV split count depends on how many heads one launch holds).  Runs
-the ranks as child processes; skipped with fewer than 2 GPUs."""
+the ranks as child processes: over NCCL on 2 GPUs (skipped with fewer), and
+over gloo with both ranks on one GPU (the exchanges staged through host
+memory), so a one-GPU machine checks the per-rank path as well."""
 
 import os
 import subprocess
@@ -20,9 +22,13 @@ import os, sys, datetime, torch, torch.distributed as dist
 sys.path[:0] = [ROOT, os.path.join(ROOT, "large-sparse-reconstruction-model_b200")]
 from lsrm_sparse import ulysses, synth, ops
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-torch.cuda.set_device(rank)
-dev = torch.device("cuda", rank)
-dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+BACKEND = "BK"  # nccl: one GPU per rank; gloo: every rank on GPU 0, exchanges through host memory
+dev = torch.device("cuda", rank if BACKEND == "nccl" else 0)
+torch.cuda.set_device(dev)
+if BACKEND == "nccl":
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+else:
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 lens = synth.uniform_blocks(6000, 40, 64, 256, 5)
 cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32)
 N, H, Hkv, D = int(cu[-1]), 8, HKV, 64
@@ -54,19 +60,24 @@ for name, a, b in zip("qkvz", ls, ts):
     if not (err <= 2e-2 and cos >= 0.9995):
         print("rank", rank, "d" + name, err, cos, flush=True)
         ok = False
-flag = torch.tensor([int(ok)], device=dev)
+flag = torch.tensor([int(ok)], device=dev if BACKEND == "nccl" else "cpu")
 dist.all_reduce(flag, op=dist.ReduceOp.MIN)
 dist.destroy_process_group()
 sys.exit(0 if flag.item() == 1 else 3)
 '''
 
 
+@pytest.mark.parametrize("backend", ["nccl", "gloo_one_gpu"])
 @pytest.mark.parametrize("hkv", [8, 2])
-def test_ulysses_two_gpus_bit_identical_to_single_gpu(hkv, tmp_path):
-    if torch.cuda.device_count() < 2:
+def test_ulysses_two_gpus_bit_identical_to_single_gpu(hkv, backend, tmp_path):
+    """``nccl``: two GPUs; ``gloo_one_gpu``: both ranks on one GPU with the
+    exchanges staged through host memory (the same per-rank code path, so a
+    one-GPU machine checks it too)."""
+    if backend == "nccl" and torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     script = tmp_path / "child.py"
-    script.write_text(CHILD.replace("ROOT", repr(ROOT)).replace("HKV", str(hkv)))
+    script.write_text(CHILD.replace("ROOT", repr(ROOT)).replace("HKV", str(hkv))
+                      .replace('"BK"', repr(backend.split("_")[0])))
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", str(script)]
