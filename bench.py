@@ -1516,6 +1516,15 @@ def run_decoder(args):
                     "bytes_out_per_step": xs["bytes_out"], "share_of_step": float(t.item()) / ms,
                     "a2a_gbs": xs["bytes_out"] / (float(t.item()) * 1e-3) / 1e9 if t.item() > 0 else None,
                     "link_gbs": 900.0}
+    # per-kernel device time of this library's launches in one more step (CUDA events on the launching
+    # stream); the rest of the step is library GEMMs, elementwise glue and (N > 1) the exchanges
+    _lib.profile_enable(True)
+    step(x_in, y_in)
+    torch.cuda.synchronize()
+    prof = _lib.profile_collect()
+    _lib.profile_enable(False)
+    kernels = {k: {"ms_per_step": v[0], "launches_per_step": v[1], "share_of_step": v[0] / ms}
+               for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}
     if args.torch_profile:  # per-kernel device time of one more step, as a table on stderr
         from torch.profiler import ProfilerActivity, profile
 
@@ -1563,7 +1572,8 @@ def run_decoder(args):
         data=f"synthetic: seeded random-sphere shell ({shell} voxels before subsampling), N(0,1) token features, "
              f"random-init weights",
         attn_map_ms=map_ms, peak_mem_gib=mem_gb, cpu_baseline=None, e2e=e2e, gpu_launches=int(launches),
-        clocks=clk.summary())), flush=True)
+        clocks=clk.summary(), kernels=kernels,
+        kernels_ms_per_step=sum(v["ms_per_step"] for v in kernels.values()))), flush=True)
 
 
 def F_layer_norm(x, D):
@@ -1578,6 +1588,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--seed", type=int, default=0)
+    # overrides of the chosen attention config (the BASELINE scaling sweep's axes)
+    ap.add_argument("--tokens", type=int, default=0, help="voxel tokens N (with --grid-res: the shell's grid)")
+    ap.add_argument("--grid-res", type=int, default=0, help="resolution of the random-sphere SDF grid")
+    ap.add_argument("--blk-range", default="", help="octree block sizes MIN,MAX")
+    ap.add_argument("--topk", type=int, default=0, help="selected blocks per query block")
+    ap.add_argument("--window", type=int, default=0, help="sliding window")
     ap.add_argument("--cpu-qblocks", type=int, default=24)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -1602,7 +1618,12 @@ def main():
                          "embedding, layers + skip blocks, norm, upsampler, output formatting)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    for key, val in (("n", args.tokens), ("res", args.grid_res), ("topk", args.topk), ("window", args.window)):
+        if val:
+            cfg[key] = val
+    if args.blk_range:
+        cfg["blk_min"], cfg["blk_max"] = (int(x) for x in args.blk_range.split(","))
     if args.path == "volume_output":
         run_volume_output(args)
     elif args.path == "volume_geo_topk":

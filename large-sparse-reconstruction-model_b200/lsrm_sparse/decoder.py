@@ -408,15 +408,18 @@ class VolTransformer(nn.Module):
         three per-axis tables gathered by the (z, y, x) columns of
         ``volume_index`` and concatenated, or the full table's rows of the
         voxels ``mask_volume`` keeps (a flat mask over ``batch_size`` copies
-        of the volume), reordered by ``volume_coords_idx``."""
+        of the volume), reordered by ``volume_coords_idx``.  The gathers read
+        fp32 copies of the tables, so the backward's scatter-add (many tokens
+        per table row) accumulates in fp32 whatever the parameters' dtype; the
+        values are the tables' own."""
         if self.use_decomposed_embed:
             vi = volume_index.long()
-            return torch.cat([self.pos_embed_z[0].index_select(0, vi[:, 1]),
-                              self.pos_embed_y[0].index_select(0, vi[:, 2]),
-                              self.pos_embed_x[0].index_select(0, vi[:, 3])], dim=-1)
+            return torch.cat([self.pos_embed_z[0].float().index_select(0, vi[:, 1]),
+                              self.pos_embed_y[0].float().index_select(0, vi[:, 2]),
+                              self.pos_embed_x[0].float().index_select(0, vi[:, 3])], dim=-1).to(dtype)
         rows = torch.nonzero(mask_volume.reshape(-1)).squeeze(1)
         rows = rows.index_select(0, volume_coords_idx.reshape(-1).long()) % self.num_token
-        return self.pos_embed[0].to(dtype=dtype).index_select(0, rows)
+        return self.pos_embed[0].float().index_select(0, rows).to(dtype)
 
     def _run(self, blk, *args):
         import torch.utils.checkpoint as cp

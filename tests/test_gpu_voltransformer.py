@@ -44,17 +44,21 @@ def _reference_prepare(m, volume, volume_index, prior_volume):
 
 def _reference_forward(m, y, prior_imfeat_list, image_index, prior_volfeat, mask_volume, volume_index,
                        prior_volume, volume_coords_idx, maps, im_num):
-    """VolTransformer.forward (voldecoder.py:270-424), one GPU, no checkpoints."""
+    """VolTransformer.forward (voldecoder.py:270-424), one GPU, no checkpoints.
+    The position tables are indexed as fp32 copies (the same values): in
+    bf16 the gradient's scatter-add over ~60 tokens per table row rounds
+    differently for every summation order, by up to a few percent."""
     B = int(image_index[:, 0].max()) + 1
     C = m.embed_dim
     if m.use_decomposed_embed:
-        x = torch.cat([m.pos_embed_z.reshape(-1, m.embed_dim_z)[volume_index[:, 1].long()],
-                       m.pos_embed_y.reshape(-1, m.embed_dim_y)[volume_index[:, 2].long()],
-                       m.pos_embed_x.reshape(-1, m.embed_dim_x)[volume_index[:, 3].long()]], dim=-1)
+        x = torch.cat([m.pos_embed_z.float().reshape(-1, m.embed_dim_z)[volume_index[:, 1].long()],
+                       m.pos_embed_y.float().reshape(-1, m.embed_dim_y)[volume_index[:, 2].long()],
+                       m.pos_embed_x.float().reshape(-1, m.embed_dim_x)[volume_index[:, 3].long()]],
+                      dim=-1).to(y.dtype)
     else:
-        x = m.pos_embed.repeat(B, 1, 1).to(dtype=y.dtype).reshape(-1, C)
+        x = m.pos_embed.float().repeat(B, 1, 1).reshape(-1, C)
         x = x[mask_volume, :]
-        x = x[volume_coords_idx, :]
+        x = x[volume_coords_idx, :].to(y.dtype)
     prior_imfeat = torch.cat(prior_imfeat_list, dim=1)
 
     def cu_of(ids):
@@ -137,7 +141,7 @@ def test_voltransformer_matches_reference_forward(variant):
     for a, b in [(outs[0]["sparse_feat"], outs[1]["sparse_feat"])] + list(zip(grads[0], grads[1])):
         assert a.shape == b.shape
         assert torch.isfinite(a).all()
-        scale = max(1.0, float(b.float().abs().max()))
+        scale = max(1.0, float(b.detach().float().abs().max()))
         assert float((a.float() - b.float()).abs().max()) <= 2e-2 * scale
         assert _cos(a, b) >= 0.9995
 

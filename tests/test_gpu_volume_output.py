@@ -89,3 +89,19 @@ def test_volume_output_flags_bad_index():
     vidx[10, 1] = 8  # outside the 8^3 token grid
     _run(volume, vidx, 4, 2, 8)
     assert ops.read_errors() & 0x8  # LSRM_ERR_BAD_INDEX
+
+
+def test_volume_output_gradient_is_the_inverse_transpose():
+    """``sparse_feat`` is differentiable with respect to ``volume``: its
+    gradient is the reference's reshape / permute (voldecoder.py:200-207)
+    taken backward, bit for bit."""
+    volume, vidx = _case(7, [300, 200], 16, 2, 8, torch.float32)
+    a = volume.cuda().requires_grad_()
+    out = _run(a, vidx, 8, 2, 16)
+    g = torch.randn(out["sparse_feat"].shape, device="cuda")
+    out["sparse_feat"].backward(g)
+    b = volume.cuda().requires_grad_()
+    ref = b.reshape(-1, 8, 2, 2, 2).permute(0, 2, 3, 4, 1).reshape(-1, 8)
+    assert torch.equal(ref.detach(), out["sparse_feat"].detach())
+    ref.backward(g)
+    assert torch.equal(a.grad, b.grad)
