@@ -629,7 +629,7 @@ def run_ours(args, cfg):
         achieved = fl / (avg_ms * 1e-3) / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": traffic_for(dom),
+                    "frac": achieved / peak, "traffic": traffic_for(dom, cfg.get("name") if ws == 1 else None),
                     "peak_source": f"bf16_tflops_sustained of {peak_kind} (kernel timed inside a long step)",
                     "scope": "one GPU (rank 0): its own pairs and launch time" if ws > 1 else "one GPU"}
     slowest = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
@@ -637,7 +637,7 @@ def run_ours(args, cfg):
     # ---- end to end through the public API: H2D inputs, D2H loss ----
     e2e = None
     if not args.no_e2e:
-        e_steps = max(3, min(args.steps, 10))
+        e_steps = max(3, min(args.steps, 20))
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -772,13 +772,15 @@ def _json_default(o):
     return str(o)
 
 
-def traffic_for(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if
-    one exists (profiles/traffic.json: {kernel: bytes_per_launch})."""
+def traffic_for(kernel, workload):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary of
+    this very workload on one GPU, if one exists (profiles/traffic.json:
+    {config name: {kernel: bytes_per_launch}}); None for any other workload
+    (another config, overridden sizes, or one rank's share under N > 1)."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(path):
+    if workload and os.path.exists(path):
         with open(path) as f:
-            return json.load(f).get(kernel)
+            return json.load(f).get(workload, {}).get(kernel)
     return None
 
 
@@ -1618,12 +1620,14 @@ def main():
                          "embedding, layers + skip blocks, norm, upsampler, output formatting)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = dict(CONFIGS[args.config])
+    cfg = dict(CONFIGS[args.config], name=args.config)
     for key, val in (("n", args.tokens), ("res", args.grid_res), ("topk", args.topk), ("window", args.window)):
         if val:
             cfg[key] = val
+            cfg["name"] = None  # no longer the named workload
     if args.blk_range:
         cfg["blk_min"], cfg["blk_max"] = (int(x) for x in args.blk_range.split(","))
+        cfg["name"] = None
     if args.path == "volume_output":
         run_volume_output(args)
     elif args.path == "volume_geo_topk":
