@@ -1433,11 +1433,12 @@ def run_decoder(args):
                                 depth=n_layers, num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"],
                                 mlp_ratio=c["mlp_ratio"], skip_links=skips, topk_volume=c["topk_volume"],
                                 topk_multiimage=c["topk_multiimage"], use_decomposed_embed=True,
-                                use_sequence_parallel=ws > 1).to(dev).to(torch.bfloat16)
+                                use_sequence_parallel=ws > 1, fused_qkv=args.fused_qkv).to(dev).to(torch.bfloat16)
     else:
         layers = torch.nn.ModuleList(
             BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
-                     topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1)
+                     topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1,
+                     fused_qkv=args.fused_qkv)
             for _ in range(n_layers)
         ).to(dev).to(torch.bfloat16)
     opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
@@ -1564,6 +1565,8 @@ def run_decoder(args):
                                "around the attention cores, gradients all-reduced)" if ws > 1 else "single GPU",
                 "model": "VolTransformer: decomposed position embedding, the layers and 3 one-sided skip blocks, "
                          "LayerNorm, upsampler (x2, 32 channels), output formatting" if full else "BlockMix stack",
+                "qkv": "one GEMM per token set with the per-head LayerNorm in its epilogue" if args.fused_qkv
+                       else "three Linears (library GEMMs), then the fused per-head LayerNorm",
                 "workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
                             f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
                             f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
@@ -1576,6 +1579,91 @@ def run_decoder(args):
         attn_map_ms=map_ms, peak_mem_gib=mem_gb, cpu_baseline=None, e2e=e2e, gpu_launches=int(launches),
         clocks=clk.summary(), kernels=kernels,
         kernels_ms_per_step=sum(v["ms_per_step"] for v in kernels.values()))), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# --path qkv_norm: CrossAttention's q / k / v projections with the per-head
+# LayerNorm32 of q and k (models_sparse/utils.py:114-127, 239-270) at the
+# decoder's token count: one fused GEMM against three Linears + the fused norm
+# ---------------------------------------------------------------------------
+
+
+def run_qkv_norm(args):
+    ws, rank, local = dist_env()
+    n, C, Hq, Hkv = 131072, 1024, 16, 16
+    D = C // Hq
+    base = {"metric": "q/k/v projection + per-head LayerNorm forward+backward (TFLOP/s of the GEMMs)",
+            "unit": "TFLOP/s", "higher_is_better": True}
+    if args.impl == "reference" or rank != 0:
+        if rank == 0:
+            print(json.dumps(dict(base, impl="reference", unavailable="the reference runs these as torch "
+                                  "Linears + LayerNorm32; this path's baseline is the library-GEMM leg below")))
+        return
+    from lsrm_sparse import _lib, ops
+    from lsrm_sparse import functional as F
+    from lsrm_sparse.ulysses import head_layernorm
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(args.seed)
+    lins = [torch.nn.Linear(C, n_, bias=False).to(dev).bfloat16() for n_ in (C, Hkv * D, Hkv * D)]
+    x = torch.randn(n, C, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    gs = [torch.randn(n, m, device=dev, dtype=torch.bfloat16) for m in (C, Hkv * D, Hkv * D, Hkv * D)]
+    N = C + 2 * Hkv * D
+    flops_fwd = 2.0 * n * C * N
+    flops = 3 * flops_fwd  # forward + input and weight gradients
+
+    def fused():
+        (_, q), (k, kn), (v, _) = F.qkv_norm(x, lins, [(False, True), (True, True), (True, False)], D)
+        torch.autograd.backward([q, k, kn, v], gs)
+
+    def unfused():
+        q, k, v = (lin(x) for lin in lins)
+        qn = head_layernorm(q.view(n, Hq, D)).view(n, -1)
+        kn = head_layernorm(k.view(n, Hkv, D)).view(n, -1)
+        torch.autograd.backward([qn, k, kn, v], gs)
+
+    res = {}
+    stream = torch.cuda.current_stream()
+    with ClockSampler(local) as clk:
+        for name, fn in (("fused", fused), ("library_gemms", unfused)):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            res[name] = {"ms_per_step": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+    _check_device_errors(ops)
+    # the fused forward kernel alone (CUDA events on the launching stream, this library's profiler)
+    _lib.profile_enable(True)
+    for _ in range(args.steps):
+        F.qkv_norm(x.detach(), lins, [(False, True), (True, True), (True, False)], D)
+    torch.cuda.synchronize()
+    prof = _lib.profile_collect()
+    _lib.profile_enable(False)
+    ms_k, cnt = prof.get("qkv_norm_gemm", (0.0, 1))
+    k_ms = ms_k / max(cnt, 1)
+    peaks, peak_kind = load_peaks()
+    peak = peaks.get("bf16_tflops", 0)
+    achieved = flops_fwd / (k_ms * 1e-3) / 1e12 if k_ms else None
+    print(json.dumps(dict(
+        base, value=res["fused"]["tflops"], n_gpus=1, steps=args.steps, warmup=args.warmup,
+        ms_per_step=res["fused"]["ms_per_step"], scaling="weak", vs_baseline=None, dtype="bf16",
+        data="synthetic: N(0,1) tokens, random-init Linears",
+        config={"workload": f"{n} tokens, hidden {C}, {Hq} q / {Hkv} kv heads of {D}: q, k, v projections "
+                            f"(N = {N}), LayerNorm32 of q and k per head, forward + backward",
+                "l2": "inputs larger than L2"},
+        library_gemms=res["library_gemms"], fused=res["fused"],
+        roofline={"kernel": "qkv_norm_gemm", "bound": "tensor", "achieved": achieved, "peak": peak,
+                  "unit": "TFLOP/s", "frac": achieved / peak if achieved and peak else None, "traffic": None,
+                  "peak_source": f"bf16_tflops (burst) of {peak_kind}: the forward kernel timed alone",
+                  "ms_per_launch": k_ms},
+        cpu_baseline=None, e2e=None, gpu_launches=None, clocks=clk.summary())), flush=True)
 
 
 def F_layer_norm(x, D):
@@ -1601,7 +1689,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--eager", action="store_true", help="time the eager step instead of its CUDA graph")
     ap.add_argument("--path", choices=["attention", "volume_output", "volume_geo_topk", "head_layernorm_pack",
-                                       "view_block_topk", "decoder"],
+                                       "view_block_topk", "decoder", "qkv_norm"],
                     default="attention",
                     help="attention: the three-branch sparse-attention step (the headline); volume_output: the "
                          "decoder's output formatting (prepare_volume_output); volume_geo_topk: the geometric "
@@ -1615,6 +1703,8 @@ def main():
                     "reference's production model uses 32,2 at hidden 1024, i.e. head_dim 32)")
     ap.add_argument("--torch-profile", action="store_true",
                     help="--path decoder: print torch.profiler's per-kernel table of one extra step on stderr")
+    ap.add_argument("--fused-qkv", action="store_true",
+                    help="--path decoder: q / k / v projections as one GEMM with the per-head LayerNorm fused")
     ap.add_argument("--decoder-model", choices=["blocks", "full"], default="blocks",
                     help="--path decoder: the BlockMix stack alone, or the whole VolTransformer (position "
                          "embedding, layers + skip blocks, norm, upsampler, output formatting)")
@@ -1638,6 +1728,8 @@ def main():
         run_view_maps(args)
     elif args.path == "decoder":
         run_decoder(args)
+    elif args.path == "qkv_norm":
+        run_qkv_norm(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

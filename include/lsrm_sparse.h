@@ -425,6 +425,45 @@ int lsrm_head_layernorm_pack_bwd(int32_t n_tokens, int32_t num_heads, int32_t he
                                  int64_t src_token_stride, float eps, const void* src, const void* grad_packed,
                                  void* grad_src, void* stream);
 
+/* Projection GEMM with the per-head LayerNorm in its epilogue: replaces
+ * CrossAttention's q / k / v projections (models_sparse/utils.py:114-127,
+ * q_proj_x / k_proj_x / v_proj_x, and the y side) followed by
+ * _normalize_qkv's LayerNorm32 of q and k (:239-270).
+ * fwd: Y = x W^T (+ bias) for x [M, K] (token stride x_token_stride
+ *   elements) and W [N, K] bf16 (the Linears' weights stacked), fp32
+ *   accumulation on the tensor cores.  The N columns are the segments in
+ *   order; segment s writes its columns of bf16(Y) to `out` and/or the
+ *   per-head LayerNorm of bf16(Y) (non-affine over head_dim columns, fp32
+ *   statistics, biased variance, eps) to `out_norm`, each [M, cols]
+ *   contiguous and 16-byte aligned, and 1/std of each normalised head to
+ *   rstd [M, N / head_dim].  K a multiple of 64, head_dim 32 or 64, up to 4
+ *   segments.  err_flags required (a bounded wait that ran out sets
+ *   LSRM_ERR_TIMEOUT).
+ * bwd: grad_pre [M, N] bf16 = the gradient of Y given, per segment, the
+ *   gradient of `out` (grad_out) and/or of `out_norm` (grad_norm, with the
+ *   forward's out_norm and rstd); any of them may be NULL.  The input and
+ *   weight gradients are then grad_pre W and grad_pre^T x. */
+typedef struct {
+  int32_t cols;     /* GEMM columns of this segment, a multiple of head_dim */
+  int32_t reserved;
+  void* out;        /* [M, cols] bf16 result, or NULL */
+  void* out_norm;   /* [M, cols] bf16 per-head LayerNorm of the result, or NULL */
+} lsrm_qkv_segment;
+
+typedef struct {
+  int32_t cols;
+  int32_t reserved;
+  const void* out_norm;   /* the forward's normalised output (needed with grad_norm) */
+  const void* grad_out;   /* gradient of the raw output, or NULL */
+  const void* grad_norm;  /* gradient of the normalised output, or NULL */
+} lsrm_qkv_grad_segment;
+
+int lsrm_qkv_norm_fwd(int64_t M, int32_t K, int32_t N, int32_t head_dim, const void* x, int64_t x_token_stride,
+                      const void* w, const void* bias, const lsrm_qkv_segment* segs, int32_t n_segs, float eps,
+                      float* rstd, int* err_flags, void* stream);
+int lsrm_qkv_norm_bwd(int64_t M, int32_t N, int32_t head_dim, const lsrm_qkv_grad_segment* segs, int32_t n_segs,
+                      const float* rstd, void* grad_pre, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Self-test of the tcgen05 / TMA building blocks (used by the GPU tests)   */
 /* ---------------------------------------------------------------------- */

@@ -54,6 +54,15 @@ class AttnShape(ctypes.Structure):
     ]
 
 
+class QkvSegment(ctypes.Structure):
+    _fields_ = [("cols", c_int32), ("reserved", c_int32), ("out", c_void_p), ("out_norm", c_void_p)]
+
+
+class QkvGradSegment(ctypes.Structure):
+    _fields_ = [("cols", c_int32), ("reserved", c_int32), ("out_norm", c_void_p), ("grad_out", c_void_p),
+                ("grad_norm", c_void_p)]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "lsrm_abi_version": (c_int, []),
@@ -160,6 +169,11 @@ _SIGS = {
         c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
                 c_void_p, c_void_p, c_void_p, c_void_p]
     ),
+    "lsrm_qkv_norm_fwd": (
+        c_int, [c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32,
+                ctypes.c_float, c_void_p, c_void_p, c_void_p]
+    ),
+    "lsrm_qkv_norm_bwd": (c_int, [c_int64, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "lsrm_umma_selftest": (
         c_int, [c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     ),

@@ -60,8 +60,12 @@ def _attn_triple(dim, num_q_heads, num_kv_heads, window):
 
 class CrossAttention(nn.Module):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, qkv_bias=False, use_weight_norm=False, oneside=False,
-                 topk_volume=8, topk_multiimage=2, use_sequence_parallel=False, no_checkpoint_all_gather=False):
+                 topk_volume=8, topk_multiimage=2, use_sequence_parallel=False, no_checkpoint_all_gather=False, *,
+                 fused_qkv=False):
         super().__init__()
+        # fused_qkv: each token set's q / k / v projections run as one GEMM with the per-head LayerNorm32 of
+        # q and k in its epilogue (lsrm_qkv_norm_fwd); head_dim 32 or 64, bf16
+        self.fused_qkv = fused_qkv
         self.num_q_heads = num_q_heads
         self.num_kv_heads = num_kv_heads
         self.dim = dim
@@ -101,6 +105,31 @@ class CrossAttention(nn.Module):
             if not oneside:
                 self.q_proj_y, self.proj_y = wn(self.q_proj_y), wn(self.proj_y)
 
+    def _projections(self, x, y):
+        """q (normalised), k (raw and normalised) and v of both token sets:
+        q_x, k_x, kn_x, v_x, q_y (None one-sided), k_y, kn_y, v_y.  With
+        ``fused_qkv`` every set is one GEMM with the norms in its epilogue;
+        otherwise the Linears, then the fused per-head LayerNorm32
+        (models_sparse/utils.py:114-127, 239-270)."""
+        Hq, Hkv = self.num_q_heads, self.num_kv_heads
+        if self.fused_qkv:
+            D, eps = self.head_dim, self.norm_layer_q.eps
+            (_, q_x), (k_x, kn_x), (v_x, _) = F.qkv_norm(
+                x, [self.q_proj_x, self.k_proj_x, self.v_proj_x], [(False, True), (True, True), (True, False)], D, eps)
+            if self.oneside:
+                (k_y, kn_y), (v_y, _) = F.qkv_norm(y, [self.k_proj_y, self.v_proj_y], [(True, True), (True, False)],
+                                                  D, eps)
+                q_y = None
+            else:
+                (_, q_y), (k_y, kn_y), (v_y, _) = F.qkv_norm(
+                    y, [self.q_proj_y, self.k_proj_y, self.v_proj_y], [(False, True), (True, True), (True, False)],
+                    D, eps)
+            return q_x, k_x, kn_x, v_x, q_y, k_y, kn_y, v_y
+        q_x, k_x, v_x = self.q_proj_x(x), self.k_proj_x(x), self.v_proj_x(x)
+        k_y, v_y = self.k_proj_y(y), self.v_proj_y(y)
+        q_y = None if self.oneside else self._norm(self.q_proj_y(y), Hq)
+        return self._norm(q_x, Hq), k_x, self._norm(k_x, Hkv), v_x, q_y, k_y, self._norm(k_y, Hkv), v_y
+
     def _norm(self, t, heads):
         """LayerNorm32 over head_dim of [n, heads * head_dim] (norm_layer_q /
         norm_layer_kv, models_sparse/utils.py:239-270), fused."""
@@ -115,20 +144,17 @@ class CrossAttention(nn.Module):
     def forward(self, x, cu_seqlens_x, y, cu_seqlens_y, im_num, attn_map):
         if self.use_sequence_parallel:
             return self._forward_sequence_parallel(x, y, im_num, attn_map)
-        q_x, k_x, v_x = self.q_proj_x(x), self.k_proj_x(x), self.v_proj_x(x)
-        k_y, v_y = self.k_proj_y(y), self.v_proj_y(y)
+        q_x, k_x_raw, k_x, v_x, q_y, k_y_raw, k_y, v_y = self._projections(x, y)
+        # the compression reads the raw keys / values (the In modules run before the norms)
+        ck_x2x, cv_x2x = self.x_2_x_attn_in(k_x_raw, v_x, attn_map["vol_to_vol_attn"])
+        ck_x2y, cv_x2y = self.x_2_y_attn_in(k_y_raw, v_y, attn_map["vol_to_img_attn"])
         if not self.oneside:
-            q_y = self.q_proj_y(y)
-        ck_x2x, cv_x2x = self.x_2_x_attn_in(k_x, v_x, attn_map["vol_to_vol_attn"])
-        ck_x2y, cv_x2y = self.x_2_y_attn_in(k_y, v_y, attn_map["vol_to_img_attn"])
+            ck_y2y, cv_y2y = self.y_2_y_attn_in(k_y_raw, v_y, attn_map["img_to_img_attn"])
+            ck_y2x, cv_y2x = self.y_2_x_attn_in(k_x_raw, v_x, attn_map["img_to_vol_attn"])
+        Hkv = self.num_kv_heads
+        ck_x2x, ck_x2y = self._norm(ck_x2x, Hkv), self._norm(ck_x2y, Hkv)
         if not self.oneside:
-            ck_y2y, cv_y2y = self.y_2_y_attn_in(k_y, v_y, attn_map["img_to_img_attn"])
-            ck_y2x, cv_y2x = self.y_2_x_attn_in(k_x, v_x, attn_map["img_to_vol_attn"])
-        Hq, Hkv = self.num_q_heads, self.num_kv_heads
-        q_x, k_x, ck_x2x = self._norm(q_x, Hq), self._norm(k_x, Hkv), self._norm(ck_x2x, Hkv)
-        k_y, ck_x2y = self._norm(k_y, Hkv), self._norm(ck_x2y, Hkv)
-        if not self.oneside:
-            q_y, ck_y2y, ck_y2x = self._norm(q_y, Hq), self._norm(ck_y2y, Hkv), self._norm(ck_y2x, Hkv)
+            ck_y2y, ck_y2x = self._norm(ck_y2y, Hkv), self._norm(ck_y2x, Hkv)
 
         sparse_info = {}
         x_cross_out, sparse_info["v_2_i"] = self.x_2_y_attn_mid(
@@ -175,20 +201,17 @@ class CrossAttention(nn.Module):
         hp, hkp = Hq // W, Hkv // W
         k0, k1 = rank * hkp, (rank + 1) * hkp
         m_vv, m_vi = attn_map["vol_to_vol_attn"], attn_map["vol_to_img_attn"]
-        q_x, k_x, v_x = self.q_proj_x(x), self.k_proj_x(x), self.v_proj_x(x)
-        k_y, v_y = self.k_proj_y(y), self.v_proj_y(y)
+        q_x, k_x_raw, k_x, v_x, q_y, k_y_raw, k_y, v_y = self._projections(x, y)
         # compression of the raw keys / values on local whole blocks, then the per-head norms (the
         # reference's order: In modules first, _normalize_qkv after)
-        ck_x2x, cv_x2x = self.x_2_x_attn_in(k_x, v_x, m_vv)
-        ck_x2y, cv_x2y = self.x_2_y_attn_in(k_y, v_y, m_vi)
+        ck_x2x, cv_x2x = self.x_2_x_attn_in(k_x_raw, v_x, m_vv)
+        ck_x2y, cv_x2y = self.x_2_y_attn_in(k_y_raw, v_y, m_vi)
         if not self.oneside:
             m_ii, m_iv = attn_map["img_to_img_attn"], attn_map["img_to_vol_attn"]
-            ck_y2y, cv_y2y = self.y_2_y_attn_in(k_y, v_y, m_ii)
-            ck_y2x, cv_y2x = self.y_2_x_attn_in(k_x, v_x, m_iv)
-            q_y = self._norm(self.q_proj_y(y), Hq)
+            ck_y2y, cv_y2y = self.y_2_y_attn_in(k_y_raw, v_y, m_ii)
+            ck_y2x, cv_y2x = self.y_2_x_attn_in(k_x_raw, v_x, m_iv)
             ck_y2y, ck_y2x = self._norm(ck_y2y, Hkv), self._norm(ck_y2x, Hkv)
-        q_x, k_x, ck_x2x = self._norm(q_x, Hq), self._norm(k_x, Hkv), self._norm(ck_x2x, Hkv)
-        k_y, ck_x2y = self._norm(k_y, Hkv), self._norm(ck_x2y, Hkv)
+        ck_x2x, ck_x2y = self._norm(ck_x2x, Hkv), self._norm(ck_x2y, Hkv)
 
         def to_heads(t, plan, heads):  # [n_local, heads*D] -> [N, heads/W * D]
             h = ulysses.seq_to_head(t.reshape(t.shape[0], heads, D), plan, group)
@@ -237,7 +260,7 @@ class CrossAttention(nn.Module):
 class BlockMix(nn.Module):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, act_layer=nn.GELU,
                  norm_layer=LayerNorm32, use_weight_norm=False, topk_volume=8, topk_multiimage=2,
-                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, oneside=False):
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, oneside=False, fused_qkv=False):
         super().__init__()
         hidden = int(dim * mlp_ratio)
         self.oneside = oneside
@@ -245,7 +268,7 @@ class BlockMix(nn.Module):
         self.crs_attn = CrossAttention(dim, num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, qkv_bias=qkv_bias,
                                        use_weight_norm=use_weight_norm, oneside=oneside, topk_volume=topk_volume,
                                        topk_multiimage=topk_multiimage, use_sequence_parallel=use_sequence_parallel,
-                                       no_checkpoint_all_gather=no_checkpoint_all_gather)
+                                       no_checkpoint_all_gather=no_checkpoint_all_gather, fused_qkv=fused_qkv)
         self.mlp_x_1 = Mlp(in_features=dim, hidden_features=hidden, act_layer=act_layer,
                            use_weight_norm=use_weight_norm)
         if not oneside:
@@ -268,10 +291,10 @@ class BlockMix(nn.Module):
 class BlockMixOneside(BlockMix):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, act_layer=nn.GELU,
                  norm_layer=LayerNorm32, use_weight_norm=False, topk_volume=8, topk_multiimage=2,
-                 use_sequence_parallel=False, no_checkpoint_all_gather=False):
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, fused_qkv=False):
         super().__init__(dim, num_q_heads, num_kv_heads, mlp_ratio, qkv_bias, act_layer, norm_layer, use_weight_norm,
                          topk_volume, topk_multiimage, use_sequence_parallel, no_checkpoint_all_gather,
-                         oneside=True)
+                         oneside=True, fused_qkv=fused_qkv)
 
 
 # ---------------------------------------------------------------------------
@@ -326,7 +349,8 @@ class VolTransformer(nn.Module):
     def __init__(self, vol_res=64, upsample_scale=4, embed_dim=1024, output_dim=32, depth=24, num_q_heads=32,
                  num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, cp_freq=1, use_weight_norm=False,
                  skip_links=(17, 11, 4), topk_volume=8, topk_multiimage=2, use_decomposed_embed=False,
-                 use_sequence_parallel=False, no_checkpoint_all_gather=False, fuse_all_layers=False):
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, fuse_all_layers=False, *,
+                 fused_qkv=False):
         super().__init__()
         import math
 
@@ -355,7 +379,7 @@ class VolTransformer(nn.Module):
         blk_kw = dict(num_q_heads=num_q_heads, num_kv_heads=num_kv_heads, mlp_ratio=mlp_ratio, qkv_bias=qkv_bias,
                       norm_layer=LayerNorm32, use_weight_norm=use_weight_norm, topk_volume=topk_volume,
                       topk_multiimage=topk_multiimage, use_sequence_parallel=use_sequence_parallel,
-                      no_checkpoint_all_gather=no_checkpoint_all_gather)
+                      no_checkpoint_all_gather=no_checkpoint_all_gather, fused_qkv=fused_qkv)
         fuse_imfeat_ratio = len(skip_links) + 1
         self.fuse_prior_volfeats = nn.ModuleList(
             [nn.Linear(embed_dim, embed_dim, bias=False) for _ in range(depth)] if fuse_all_layers else [])

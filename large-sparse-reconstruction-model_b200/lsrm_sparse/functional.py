@@ -170,3 +170,61 @@ def three_branch_attention(q, k, v, cu_blk, topk: int, window: int, gate_logits,
     if capture is not None:
         capture.update(block_topk=bt, ck=ck.detach(), cv=cv.detach(), lse=lse, out=out.detach())
     return out
+
+
+class QkvNormFn(torch.autograd.Function):
+    """Stacked projections with the per-head LayerNorm32 in the GEMM's
+    epilogue (lsrm_qkv_norm_fwd); the backward turns the outputs' gradients
+    into the pre-norm gradient (lsrm_qkv_norm_bwd), then two GEMMs give the
+    input and weight gradients."""
+
+    @staticmethod
+    def forward(ctx, x2, w, b, spec, head_dim, eps):
+        ctx.set_materialize_grads(False)
+        outs, rstd = ops.qkv_norm_fwd(x2, w, b, spec, head_dim, eps)
+        norms = [on for _, on in outs if on is not None]
+        ctx.spec, ctx.head_dim, ctx.has_b = spec, head_dim, b is not None
+        ctx.save_for_backward(x2, w, rstd, *norms)
+        return tuple(t for pair in outs for t in pair if t is not None)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        x2, w, rstd, *norms = ctx.saved_tensors
+        g_it, n_it = iter(grads), iter(norms)
+        segs = []
+        for cols, raw, norm in ctx.spec:
+            go = next(g_it) if raw else None
+            gn = next(g_it) if norm else None
+            on = next(n_it) if norm else None
+            segs.append((cols, on, go, gn))
+        dpre = ops.qkv_norm_bwd(x2.shape[0], w.shape[0], ctx.head_dim, segs, rstd, x2.device, x2.dtype)
+        dx = dpre @ w if ctx.needs_input_grad[0] else None
+        dw = dpre.t() @ x2 if ctx.needs_input_grad[1] else None
+        db = dpre.float().sum(0).to(w.dtype) if ctx.has_b and ctx.needs_input_grad[2] else None
+        return dx, dw, db, None, None, None
+
+
+def qkv_norm(x, linears, outputs, head_dim: int, eps: float = 1e-5):
+    """The Linears of ``linears`` (all over x's last dim, bf16) as one GEMM
+    with the per-head LayerNorm32 of their outputs fused in its epilogue.
+    ``outputs`` gives per Linear (raw, norm): whether its plain output and /
+    or its per-head LayerNorm (non-affine over ``head_dim``) is wanted.
+    Returns per Linear a (raw, norm) pair with None for what was not asked.
+    The Linears must all have biases or none."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    w = torch.cat([lin.weight for lin in linears], 0)
+    biases = [lin.bias for lin in linears]
+    if any(b is not None for b in biases) and not all(b is not None for b in biases):
+        raise ValueError("qkv_norm: the Linears must all have biases or none")
+    b = torch.cat(biases) if biases[0] is not None else None
+    spec = tuple((lin.weight.shape[0], bool(raw), bool(norm)) for lin, (raw, norm) in zip(linears, outputs))
+    flat = iter(QkvNormFn.apply(x2, w, b, spec, int(head_dim), float(eps)))
+    res = []
+    for cols, raw, norm in spec:
+        r = next(flat).reshape(*lead, cols) if raw else None
+        n = next(flat).reshape(*lead, cols) if norm else None
+        res.append((r, n))
+    return res

@@ -391,3 +391,58 @@ def head_layernorm_pack_bwd(x: torch.Tensor, grad_packed: torch.Tensor, eps: flo
                                         _ptr(out), _stream())
     check(rc, "lsrm_head_layernorm_pack_bwd")
     return out
+
+
+# ---------------------------------------------------------------------------
+# Projection GEMM with the per-head LayerNorm in its epilogue
+# ---------------------------------------------------------------------------
+
+
+def _addr(t: Optional[torch.Tensor]):
+    return t.data_ptr() if t is not None else None
+
+
+def qkv_norm_fwd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], segments, head_dim: int,
+                 eps: float = 1e-5):
+    """x [M, K] bf16 (row stride >= K), w [N, K] bf16 (stacked Linear
+    weights), ``segments`` a list of (cols, raw, norm) in column order.
+    Returns (outputs, rstd): per segment the bf16 result [M, cols] if ``raw``
+    and its per-head LayerNorm [M, cols] if ``norm`` (None otherwise), and
+    rstd [M, N / head_dim] fp32."""
+    L = _lib.lib()
+    assert x.dim() == 2 and x.stride(1) == 1 and x.dtype == torch.bfloat16, "x must be [M, K] bf16, unit column stride"
+    w = w.contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    dev = x.device
+    segs = (_lib.QkvSegment * len(segments))()
+    outs = []
+    for i, (cols, raw, norm) in enumerate(segments):
+        o = torch.empty(M, cols, dtype=x.dtype, device=dev) if raw else None
+        on = torch.empty(M, cols, dtype=x.dtype, device=dev) if norm else None
+        segs[i] = _lib.QkvSegment(int(cols), 0, _addr(o), _addr(on))
+        outs.append((o, on))
+    rstd = torch.empty(M, N // head_dim, dtype=torch.float32, device=dev)
+    b = bias.contiguous() if bias is not None else None
+    rc = L.lsrm_qkv_norm_fwd(M, K, N, int(head_dim), _ptr(x), x.stride(0), _ptr(w), _ptr(b), segs, len(segments),
+                             float(eps), _ptr(rstd), _ptr(_err_word(dev)), _stream())
+    check(rc, "lsrm_qkv_norm_fwd")
+    return outs, rstd
+
+
+def qkv_norm_bwd(M: int, N: int, head_dim: int, segments, rstd: torch.Tensor, device, dtype=torch.bfloat16):
+    """``segments``: per segment (cols, out_norm, grad_out, grad_norm) with
+    None for absent tensors.  Returns the gradient of the pre-norm result
+    [M, N]."""
+    L = _lib.lib()
+    segs = (_lib.QkvGradSegment * len(segments))()
+    keep = []
+    for i, (cols, on, go, gn) in enumerate(segments):
+        go = go.contiguous() if go is not None else None
+        gn = gn.contiguous() if gn is not None else None
+        keep += [go, gn]
+        segs[i] = _lib.QkvGradSegment(int(cols), 0, _addr(on), _addr(go), _addr(gn))
+    out = torch.empty(M, N, dtype=dtype, device=device)
+    rc = L.lsrm_qkv_norm_bwd(M, N, int(head_dim), segs, len(segments), _ptr(rstd), _ptr(out), _stream())
+    check(rc, "lsrm_qkv_norm_bwd")
+    return out

@@ -217,3 +217,26 @@ def test_block_topk_workspace_query_and_host_rejection(lib):
     rc = h.lsrm_block_topk(ctypes.byref(meta), ctypes.byref(shape), p, p, p, 8, p, 64, 1, 0.0, p, p, 1024, p, None)
     assert rc == _header_define("LSRM_ERR_WORKSPACE")
     assert "workspace" in h.lsrm_last_error().decode()
+
+
+def test_qkv_norm_host_checks():
+    """lsrm_qkv_norm_fwd / _bwd reject bad shapes and segment tables on the
+    host, before any CUDA call, with a message naming the problem."""
+    from lsrm_sparse import _lib as lib
+
+    h = lib.lib()
+    one = (lib.QkvSegment * 1)(lib.QkvSegment(128, 0, 16, None))
+    assert h.lsrm_qkv_norm_fwd(10, 100, 128, 64, 16, 100, 16, None, one, 1, 1e-5, None, 16, None) == -1
+    assert "multiple of 64" in h.lsrm_last_error().decode()
+    assert h.lsrm_qkv_norm_fwd(10, 128, 128, 48, 16, 128, 16, None, one, 1, 1e-5, None, 16, None) == -1
+    assert "head_dim" in h.lsrm_last_error().decode()
+    short = (lib.QkvSegment * 1)(lib.QkvSegment(64, 0, 16, None))
+    assert h.lsrm_qkv_norm_fwd(10, 128, 128, 64, 16, 128, 16, None, short, 1, 1e-5, None, 16, None) == -1
+    assert "segments cover 64 columns" in h.lsrm_last_error().decode()
+    norm_no_rstd = (lib.QkvSegment * 1)(lib.QkvSegment(128, 0, None, 16))
+    assert h.lsrm_qkv_norm_fwd(10, 128, 128, 64, 16, 128, 16, None, norm_no_rstd, 1, 1e-5, None, 16, None) == -1
+    assert "rstd is required" in h.lsrm_last_error().decode()
+    assert h.lsrm_qkv_norm_fwd(0, 128, 128, 64, 16, 128, 16, None, one, 1, 1e-5, None, 16, None) == 0
+    g = (lib.QkvGradSegment * 1)(lib.QkvGradSegment(128, 0, None, None, 16))
+    assert h.lsrm_qkv_norm_bwd(10, 128, 64, g, 1, None, 16, None) == -1
+    assert "needs out_norm and rstd" in h.lsrm_last_error().decode()
