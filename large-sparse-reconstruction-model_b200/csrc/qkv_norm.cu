@@ -1,13 +1,15 @@
 // Projection GEMM with the per-head LayerNorm32 in its epilogue (sm_100a).
 //
 // Y = X W^T (+ b) for X [M, K] and W [N, K] (nn.Linear layout), bf16 in, fp32
-// accumulation on the tensor cores.  Persistent CTAs walk 128 x 128 output
+// accumulation on the tensor cores.  Persistent CTAs walk 128 x 256 output
 // tiles (row tiles outer, so the CTAs working at one time share X rows in
 // L2; W is small enough to stay there): warp 0 streams 64-wide K chunks of X
 // and W by TMA into a 4-stage ring, warp 1 issues tcgen05.mma (M = 128,
-// N = 128, K = 16, both operands K-major from shared memory) into one of two
-// TMEM accumulators, and warps 2-5 (one output row per thread) empty a
-// finished accumulator while the next tile accumulates in the other.
+// N = 256, K = 16, both operands K-major from shared memory; at N = 256 the
+// products are bound by the tensor pipe rather than by shared-memory operand
+// reads) into one of two TMEM accumulators (2 x 256 columns), and warps 2-5
+// (one output row per thread) empty a finished accumulator while the next
+// tile accumulates in the other.
 //
 // The N columns are cut into segments (CrossAttention's q, k and v
 // projections).  Per segment the epilogue writes the bf16 result, its
@@ -27,9 +29,10 @@
 namespace lsrm {
 namespace {
 
-constexpr int kQnBM = 128, kQnBN = 128, kQnBK = 64, kQnStages = 4;
+constexpr int kQnBM = 128, kQnBN = 256, kQnBK = 64, kQnStages = 4;
 constexpr int kQnThreads = 192;                  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kQnTile = kQnBM * kQnBK * 2;       // bytes of one 128 x 64 bf16 operand tile (A and B alike)
+constexpr int kQnTileA = kQnBM * kQnBK * 2;      // bytes of one 128 x 64 bf16 tile of X
+constexpr int kQnTileB = kQnBN * kQnBK * 2;      // bytes of one 256 x 64 bf16 tile of W
 constexpr int kQnMaxSeg = 4;
 constexpr int kQnTmemCols = 2 * kQnBN;          // two accumulators
 
@@ -52,13 +55,14 @@ struct QnParams {
 
 struct QnSmem {
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = kQnStages * kQnTile;
-  static constexpr int OFF_BAR = 2 * kQnStages * kQnTile;
+  static constexpr int OFF_B = kQnStages * kQnTileA;
+  static constexpr int OFF_BAR = OFF_B + kQnStages * kQnTileB;
   // full[S], empty[S], acc_full[2], acc_empty[2], mma_done
   static constexpr int NBAR = 2 * kQnStages + 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;  // + alignment of the swizzled tiles
+  static_assert(ALLOC <= 227 * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ int qn_segment(const QnParams& p, int col) {
@@ -152,9 +156,9 @@ __global__ void __launch_bounds__(kQnThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], 2 * kQnTile);
-          tma_load_3d(sA + s * kQnTile, &tm_x, 0, kc, m0, &full[s]);
-          tma_load_3d(sB + s * kQnTile, &tm_w, 0, kc, n0, &full[s]);
+          mbar_arrive_expect_tx(&full[s], kQnTileA + kQnTileB);
+          tma_load_3d(sA + s * kQnTileA, &tm_x, 0, kc, m0, &full[s]);
+          tma_load_3d(sB + s * kQnTileB, &tm_w, 0, kc, n0, &full[s]);
           last = J;
         }
       }
@@ -181,7 +185,7 @@ __global__ void __launch_bounds__(kQnThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + s * kQnTile), b_base = smem_u32(sB + s * kQnTile);
+          const uint32_t a_base = smem_u32(sA + s * kQnTileA), b_base = smem_u32(sB + s * kQnTileB);
 #pragma unroll
           for (int ks = 0; ks < kQnBK / 16; ++ks)
             umma_f16(acc, make_sdesc(a_base + ks * 32, 16, 8 * 128, kSw128),
