@@ -1433,12 +1433,13 @@ def run_decoder(args):
                                 depth=n_layers, num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"],
                                 mlp_ratio=c["mlp_ratio"], skip_links=skips, topk_volume=c["topk_volume"],
                                 topk_multiimage=c["topk_multiimage"], use_decomposed_embed=True,
-                                use_sequence_parallel=ws > 1, fused_qkv=args.fused_qkv).to(dev).to(torch.bfloat16)
+                                use_sequence_parallel=ws > 1,
+                                fused_qkv=False if args.unfused_qkv else None).to(dev).to(torch.bfloat16)
     else:
         layers = torch.nn.ModuleList(
             BlockMix(c["dim"], num_q_heads=c["q_heads"], num_kv_heads=c["kv_heads"], mlp_ratio=c["mlp_ratio"],
                      topk_volume=c["topk_volume"], topk_multiimage=c["topk_multiimage"], use_sequence_parallel=ws > 1,
-                     fused_qkv=args.fused_qkv)
+                     fused_qkv=False if args.unfused_qkv else None)
             for _ in range(n_layers)
         ).to(dev).to(torch.bfloat16)
     opt = torch.optim.AdamW(layers.parameters(), lr=1e-5, fused=True)
@@ -1565,8 +1566,8 @@ def run_decoder(args):
                                "around the attention cores, gradients all-reduced)" if ws > 1 else "single GPU",
                 "model": "VolTransformer: decomposed position embedding, the layers and 3 one-sided skip blocks, "
                          "LayerNorm, upsampler (x2, 32 channels), output formatting" if full else "BlockMix stack",
-                "qkv": "one GEMM per token set with the per-head LayerNorm in its epilogue" if args.fused_qkv
-                       else "three Linears (library GEMMs), then the fused per-head LayerNorm",
+                "qkv": "three Linears (library GEMMs), then the fused per-head LayerNorm" if args.unfused_qkv
+                       else "one GEMM per token set with the per-head LayerNorm in its epilogue",
                 "workload": f"{n_layers} BlockMix layers, hidden {c['dim']}, {c['q_heads']} query / "
                             f"{c['kv_heads']} key-value heads, MLP {c['mlp_ratio']}x; {nx} voxel tokens "
                             f"({c['volume_res']}^3 shell, {c['block_size']}^3 blocks) + {ny} image tokens "
@@ -1703,8 +1704,9 @@ def main():
                     "reference's production model uses 32,2 at hidden 1024, i.e. head_dim 32)")
     ap.add_argument("--torch-profile", action="store_true",
                     help="--path decoder: print torch.profiler's per-kernel table of one extra step on stderr")
-    ap.add_argument("--fused-qkv", action="store_true",
-                    help="--path decoder: q / k / v projections as one GEMM with the per-head LayerNorm fused")
+    ap.add_argument("--unfused-qkv", action="store_true",
+                    help="--path decoder: q / k / v projections as three Linears (library GEMMs) and the fused "
+                         "per-head LayerNorm, instead of one GEMM with the norm in its epilogue")
     ap.add_argument("--decoder-model", choices=["blocks", "full"], default="blocks",
                     help="--path decoder: the BlockMix stack alone, or the whole VolTransformer (position "
                          "embedding, layers + skip blocks, norm, upsampler, output formatting)")

@@ -61,10 +61,11 @@ def _attn_triple(dim, num_q_heads, num_kv_heads, window):
 class CrossAttention(nn.Module):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, qkv_bias=False, use_weight_norm=False, oneside=False,
                  topk_volume=8, topk_multiimage=2, use_sequence_parallel=False, no_checkpoint_all_gather=False, *,
-                 fused_qkv=False):
+                 fused_qkv=None):
         super().__init__()
         # fused_qkv: each token set's q / k / v projections run as one GEMM with the per-head LayerNorm32 of
-        # q and k in its epilogue (lsrm_qkv_norm_fwd); head_dim 32 or 64, bf16
+        # q and k in its epilogue (lsrm_qkv_norm_fwd; bf16 on the GPU, head_dim 32 or 64, width a multiple
+        # of 64); None: wherever those hold; False: the Linears, then the fused per-head LayerNorm
         self.fused_qkv = fused_qkv
         self.num_q_heads = num_q_heads
         self.num_kv_heads = num_kv_heads
@@ -112,7 +113,10 @@ class CrossAttention(nn.Module):
         otherwise the Linears, then the fused per-head LayerNorm32
         (models_sparse/utils.py:114-127, 239-270)."""
         Hq, Hkv = self.num_q_heads, self.num_kv_heads
-        if self.fused_qkv:
+        fused = self.fused_qkv
+        if fused is None:
+            fused = x.is_cuda and x.dtype == torch.bfloat16 and self.head_dim in (32, 64) and self.dim % 64 == 0
+        if fused:
             D, eps = self.head_dim, self.norm_layer_q.eps
             (_, q_x), (k_x, kn_x), (v_x, _) = F.qkv_norm(
                 x, [self.q_proj_x, self.k_proj_x, self.v_proj_x], [(False, True), (True, True), (True, False)], D, eps)
@@ -260,7 +264,7 @@ class CrossAttention(nn.Module):
 class BlockMix(nn.Module):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, act_layer=nn.GELU,
                  norm_layer=LayerNorm32, use_weight_norm=False, topk_volume=8, topk_multiimage=2,
-                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, oneside=False, fused_qkv=False):
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, oneside=False, fused_qkv=None):
         super().__init__()
         hidden = int(dim * mlp_ratio)
         self.oneside = oneside
@@ -291,7 +295,7 @@ class BlockMix(nn.Module):
 class BlockMixOneside(BlockMix):
     def __init__(self, dim, num_q_heads=32, num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, act_layer=nn.GELU,
                  norm_layer=LayerNorm32, use_weight_norm=False, topk_volume=8, topk_multiimage=2,
-                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, fused_qkv=False):
+                 use_sequence_parallel=False, no_checkpoint_all_gather=False, *, fused_qkv=None):
         super().__init__(dim, num_q_heads, num_kv_heads, mlp_ratio, qkv_bias, act_layer, norm_layer, use_weight_norm,
                          topk_volume, topk_multiimage, use_sequence_parallel, no_checkpoint_all_gather,
                          oneside=True, fused_qkv=fused_qkv)
@@ -350,7 +354,7 @@ class VolTransformer(nn.Module):
                  num_kv_heads=2, mlp_ratio=4.0, qkv_bias=False, cp_freq=1, use_weight_norm=False,
                  skip_links=(17, 11, 4), topk_volume=8, topk_multiimage=2, use_decomposed_embed=False,
                  use_sequence_parallel=False, no_checkpoint_all_gather=False, fuse_all_layers=False, *,
-                 fused_qkv=False):
+                 fused_qkv=None):
         super().__init__()
         import math
 
