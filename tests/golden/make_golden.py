@@ -24,6 +24,10 @@ What runs, all unmodified reference code:
   (models_sparse/utils.py:575-705) with and without weight norm, and of
   ``VolTransformer`` (models_sparse/voldecoder.py:39-194) with the decomposed
   and the full position embedding (``--only modules``, ``module_keys.json``).
+* ``VolTransformer.forward`` with its decoder blocks replaced by seeded stubs
+  (``StubDecoderBlock``; the real blocks need the GPU): embedding, skip links,
+  final norm, upsampler and ``prepare_volume_output``, outputs and gradients
+  (``--only voltransformer``).
 * ``SpatialSparseAttentionOut`` (sigmoid-gated merge, :196-270) with and
   without the window branch.  ``flash_attn_varlen_func`` has no CPU kernel, so
   for the window branch it is replaced by ``_cpu_varlen_attention`` below (a
@@ -399,10 +403,97 @@ def make_module_keys(utils, voldecoder=None):
     return out
 
 
+class StubDecoderBlock(torch.nn.Module):
+    """A deterministic stand-in for BlockMix / BlockMixOneside with their call
+    signature (x, cu_seqlens_x, y, cu_seqlens_y, attn_map, im_num) and return
+    shape: x gains tanh(x Wx) and a share of the image tokens' mean, so the y
+    that the skip links route reaches the output.  It lets the reference's
+    VolTransformer run on the CPU (its attention needs the GPU) and pins the
+    orchestration around the blocks: embedding, skip links, final norm,
+    upsampler, output formatting."""
+
+    def __init__(self, dim, seed, oneside):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.wx = torch.nn.Parameter(torch.randn(dim, dim, generator=g) / math.sqrt(dim))
+        self.wy = torch.nn.Parameter(torch.randn(dim, dim, generator=g) / math.sqrt(dim))
+        self.oneside = oneside
+
+    def forward(self, x, cu_seqlens_x, y, cu_seqlens_y, attn_map, im_num):
+        x = x + torch.tanh(x @ self.wx) + 0.1 * y.mean(0, keepdim=True)
+        if self.oneside:
+            return x, {}
+        return x, y + torch.tanh(y @ self.wy), {}
+
+
+def stub_blocks(model, dim):
+    """Replaces a VolTransformer's decoder blocks by StubDecoderBlocks (seeded
+    by position)."""
+    model.cross_blocks = torch.nn.ModuleList(StubDecoderBlock(dim, 1000 + i, False)
+                                             for i in range(len(model.cross_blocks)))
+    model.skip_blocks = torch.nn.ModuleList(StubDecoderBlock(dim, 2000 + i, True)
+                                            for i in range(len(model.skip_blocks)))
+    return model
+
+
+VOLT_FWD_CASES = [  # (name, VolTransformer kwargs) for the orchestration fixtures
+    ("voltransformer_fwd_decomposed", dict(vol_res=8, upsample_scale=2, embed_dim=32, output_dim=4, depth=3,
+                                           num_q_heads=2, num_kv_heads=2, skip_links=(1, 0),
+                                           use_decomposed_embed=True)),
+    ("voltransformer_fwd_full_embed", dict(vol_res=4, upsample_scale=2, embed_dim=32, output_dim=4, depth=2,
+                                           num_q_heads=2, num_kv_heads=2, skip_links=(0,))),
+]
+
+
+def volt_inputs(kw, seed):
+    """Two batch elements of voxels (unique coordinates, grouped by batch) and
+    image tokens, the flat voxel mask and its token order, random features."""
+    g = torch.Generator().manual_seed(seed)
+    R, C = kw["vol_res"], kw["embed_dim"]
+    parts, flats = [], []
+    for b, n in enumerate((37, 29)):
+        flat = torch.randperm(R ** 3, generator=g)[:n]
+        parts.append(torch.stack([torch.full_like(flat, b), flat // (R * R), (flat // R) % R, flat % R], 1))
+        flats.append(flat + b * R ** 3)
+    volume_index = torch.cat(parts).long()
+    flat = torch.cat(flats)
+    mask = torch.zeros(2 * R ** 3, dtype=torch.bool)
+    mask[flat] = True
+    coords_idx = torch.searchsorted(torch.nonzero(mask).squeeze(1), flat)
+    image_index = torch.cat([torch.zeros(10, 4), torch.ones(8, 4)]).long()
+    ny, n = image_index.shape[0], volume_index.shape[0]
+    return dict(y=torch.randn(ny, C, generator=g), prior_imfeat=torch.randn(ny, C, generator=g),
+                image_index=image_index, prior_volfeat=torch.randn(n, C, generator=g), mask_volume=mask,
+                volume_index=volume_index, volume_coords_idx=coords_idx,
+                grad_w=torch.randn(n * kw["upsample_scale"] ** 3, kw["output_dim"], generator=g))
+
+
+def make_volt_forward(voldecoder, name, kw, seed):
+    """The reference's VolTransformer.forward (models_sparse/voldecoder.py:
+    270-424, prepare_volume_output :196-268) with stub blocks, fp32 on the
+    CPU: inputs, the state dict, the output dict and the gradients of a
+    seeded weighted sum of sparse_feat with respect to y and the model's
+    parameters."""
+    torch.manual_seed(seed)
+    m = stub_blocks(voldecoder.VolTransformer(**kw), kw["embed_dim"])
+    inp = volt_inputs(kw, seed + 1)
+    y = inp["y"].clone().requires_grad_()
+    out, _ = m(y, [inp["prior_imfeat"]], inp["image_index"], inp["prior_volfeat"], inp["mask_volume"],
+               inp["volume_index"], torch.zeros(1), inp["volume_coords_idx"], {}, 4)
+    (out["sparse_feat"] * inp["grad_w"]).sum().backward()
+    res = {"in_" + k: v.numpy() for k, v in inp.items()}
+    res.update({"sd_" + k: v.detach().numpy() for k, v in m.state_dict().items()})
+    res.update({"grad_" + k: p.grad.numpy() for k, p in m.named_parameters() if p.grad is not None})
+    res.update(out_sparse_feat=out["sparse_feat"].detach().numpy(), out_cu_seqlens=out["cu_seqlens"].numpy(),
+               out_index_volume=out["index_volume"].numpy(), grad_y=y.grad.numpy())
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image", "imsort", "modules"], default=None,
+    ap.add_argument("--only", choices=["blocks", "volume", "geo", "image", "imsort", "modules", "voltransformer"],
+                    default=None,
                     help="regenerate one group of fixtures")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
@@ -418,6 +509,13 @@ def main():
         with open(os.path.join(HERE, "module_keys.json"), "w") as f:
             json.dump(make_module_keys(utils, voldecoder), f, indent=1, sort_keys=True)
         print("wrote module_keys.json")
+        return
+    if args.only == "voltransformer":
+        from models_sparse import voldecoder
+
+        for i, (name, kw) in enumerate(VOLT_FWD_CASES):
+            np.savez_compressed(os.path.join(HERE, name + ".npz"), **make_volt_forward(voldecoder, name, kw, 300 + i))
+            print("wrote", name)
         return
     if args.only == "imsort":
         np.savez_compressed(os.path.join(HERE, "image_sort.npz"), **make_image_sort(sparse_utils, 81))
